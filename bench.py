@@ -1,0 +1,331 @@
+#!/usr/bin/env python
+"""bench.py: Trochilus's OLMoE MoE layer on B200, tokens/s through one MoE layer.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--tokens T]
+                    [--gate q4_k|q8_0] [--down q6_k|q4_k|q8_0]
+
+Default workload: BASELINE.json configs[1]'s MoE layer: OLMoE-1B-7B shape (64 experts, top-8, hidden
+2048, expert FFN 1024), Q4_K_M (gate/up Q4_K, down Q6_K), BF16 router, batch-1 decode (T = 1 token a
+call). A step is one MoE-layer call (router -> top-8 -> dispatch -> gate/up/SwiGLU -> down -> id-ordered
+combine -> residual add) on T tokens. 16 layers are resident in HBM (4.2 GB) and step i runs layer i % 16
+on a fresh input row, so every step's 8 experts come from HBM, not from L2 (126 MB).
+
+Arms:
+  ours       libtrmoe.so through its C ABI. `value` = T * N / (device time per step); `e2e` = the same
+             through tr_gpu_moe_layer with pinned host buffers (copies in and out inside the timed region);
+             `roofline` = the dominant zone's algorithmic bytes / its CUDA-event time; `cpu_baseline` =
+             Trochilus's own code (oracle/_ref, best SIMD tier, all host cores) on a bounded sample.
+  reference  Trochilus's own CPU code on this box's host cores, same config (rank 0 only under torchrun).
+N > 1: one process per GPU (torchrun); each rank runs its own replica of the workload (the layer has no
+data-path exchange at batch 1), time = max over ranks, `value` = all ranks' tokens / that time.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+from trochilus_b200 import gguf_blocks as gb  # noqa: E402
+
+METRIC = "MoE-layer tokens/s (decode & prefill) OLMoE shape Q4_K/Q8_0; % of HBM/TC peak"
+TYPES = {"q4_k": gb.Q4_K, "q8_0": gb.Q8_0, "q6_k": gb.Q6_K}
+E, K_USED, H, F = 64, 8, 2048, 1024
+
+
+def args_parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=2000)
+    p.add_argument("--warmup", type=int, default=50)
+    p.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    p.add_argument("--tokens", type=int, default=1)
+    p.add_argument("--gate", default="q4_k", choices=["q4_k", "q8_0"])
+    p.add_argument("--down", default="q6_k", choices=["q6_k", "q4_k", "q8_0"])
+    p.add_argument("--layers", type=int, default=16)
+    p.add_argument("--cpu-seconds", type=float, default=8.0)
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    return p.parse_args()
+
+
+def bytes_per_expert(gate, down):
+    return 2 * F * gb.row_bytes(gate, H) + H * gb.row_bytes(down, F)
+
+
+def host_layers(gate, down, n_host=2, n_routers=16):
+    """n_host distinct layers of host GGUF bytes (random quant blocks with bounded scales) and n_routers
+    BF16-rounded N(0, 0.02) routers."""
+    lays = [gb.make_layer(1000 + i, E, H, F, gate, down, gb.BF16, mode="random") for i in range(n_host)]
+    rng = np.random.Generator(np.random.PCG64(77))
+    routers = [gb.quantize(gb.BF16, gb.round_to_bf16(rng.normal(0, 0.02, size=(E, H)).astype(np.float32)))
+               for _ in range(n_routers)]
+    return lays, routers
+
+
+class Clocks:
+    """nvidia-smi samples during the timed region (SM clock, max, throttle reasons)."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index, self.rows, self.proc = index, [], None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([v.strip() for v in line.split(",")])
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in self.rows if len(r) > 8 and r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if len(r) > 8 and r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in self.rows if len(r) > 8 for i in range(4) if r[5 + i] == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.rows)}
+
+
+def cpu_reference(args, gate, down, seconds, steps=None, warmup=0):
+    """Trochilus's own code (oracle/_ref) on all host cores: tokens/s of one MoE layer on T tokens. Either a
+    bounded time (seconds) or exactly `steps` layer calls after `warmup`."""
+    from oracle.oracle import RefLib, make_desc
+    ref = RefLib()
+    lays, routers = host_layers(gate, down, n_host=1, n_routers=1)
+    lay = dict(lays[0])
+    lay["router"] = routers[0]
+    d, keep = make_desc(lay, H, F, K_USED, 0, gb.BF16, gate, down)
+    pool = ref.pool(0)
+    st = ref.state(pool, d, args.tokens)
+    rng = np.random.default_rng(5)
+    xs = [rng.normal(size=(args.tokens, H)).astype(np.float32) for _ in range(16)]
+    res = np.zeros((args.tokens, H), np.float32)
+    for i in range(warmup):
+        ref.moe_layer(d, xs[i % 16], res, pool=pool, state=st)
+    n, t0 = 0, time.perf_counter()
+    while True:
+        ref.moe_layer(d, xs[n % 16], res, pool=pool, state=st)
+        n += 1
+        el = time.perf_counter() - t0
+        if (steps is not None and n >= steps) or (steps is None and el >= seconds):
+            break
+    cores = ref.pool_size(pool)
+    tier = ref.tier()
+    ref.state_free(st)
+    ref.pool_destroy(pool)
+    return {"value": args.tokens * n / el, "unit": "tokens/s", "cores": cores, "kind": "reference",
+            "sample": f"{n} MoE-layer calls of {args.tokens} token(s), {args.gate}/{args.down}, BF16 router, "
+                      f"{el:.1f} s, Trochilus tier {tier}, tr_pool of {cores} threads"}
+
+
+def run_reference(args, rank, world):
+    gate, down = TYPES[args.gate], TYPES[args.down]
+    if rank != 0:
+        return
+    steps = max(args.steps // 20, 20)
+    warm = max(args.warmup, 3)
+    r = cpu_reference(args, gate, down, None, steps=steps, warmup=warm)
+    line = {"impl": "reference", "metric": METRIC, "value": r["value"], "unit": "tokens/s", "n_gpus": world,
+            "steps": steps, "warmup": warm, "ms_per_step": 1000.0 * args.tokens / r["value"],
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32 lane contract / int64+f64",
+            "data": "synthetic", "config": workload_config(args),
+            "cpu_baseline": {"kind": "reference", "cores": r["cores"], "sample": r["sample"], "value": r["value"],
+                             "unit": "tokens/s"},
+            "e2e": {"value": r["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def workload_config(args):
+    return {"workload": f"configs[1] MoE layer: OLMoE-1B-7B shape (E=64, top-8, H=2048, F=1024), gate/up "
+                        f"{args.gate.upper()}, down {args.down.upper()}, BF16 router, {args.tokens}-token decode "
+                        f"call", "tokens_per_step": args.tokens, "layers_resident": args.layers,
+            "l2": "inputs larger than L2: each step runs the next of the resident layers (~261 MB each)",
+            "weights": "random quant blocks with bounded f16 scales (synthetic), inputs N(0,1)"}
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return p["hbm_gbs"], "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback"
+
+
+def run_ours(args, rank, world, dist):
+    import torch
+    from trochilus_b200.moe import GpuMoe
+
+    dev = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(dev)
+    gate, down = TYPES[args.gate], TYPES[args.down]
+    T, NL = args.tokens, args.layers
+    m = GpuMoe(NL, E, K_USED, H, F, gb.BF16, gate, down, max_tokens=T, device=dev)
+    lays, routers = host_layers(gate, down, n_host=2, n_routers=NL)
+    for l in range(NL):
+        lay = dict(lays[l % len(lays)])
+        lay["router"] = routers[l]
+        m.set_layer(l, lay)
+    del lays
+    n_in = 64
+    g = torch.Generator(device="cuda")
+    g.manual_seed(1234 + rank)
+    normed = torch.randn((n_in, T, H), device="cuda", generator=g)
+    x = torch.randn((T, H), device="cuda", generator=g)
+    stream = torch.cuda.current_stream()
+    sp = stream.cuda_stream
+
+    def step(i):
+        m.layer_dev(i % NL, normed[i % n_in].data_ptr(), T, x.data_ptr(), None, stream=sp)
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(dev) as clk:
+        torch.cuda.synchronize()
+        start.record(stream)
+        for i in range(args.steps):
+            step(i)
+        end.record(stream)
+        torch.cuda.synchronize()
+    ms = start.elapsed_time(end)
+    if dist:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        dist.barrier()
+    ms_step = ms / args.steps
+    value = world * T / (ms_step / 1000.0)
+
+    # roofline pass: zone times with CUDA events on the launching stream, and the experts actually used
+    m.profile(True)
+    for i in range(args.steps):
+        step(i)
+    zones = m.profile_read()
+    m.profile(False)
+    # distinct experts per call (computed from the routing each call makes)
+    sel = torch.zeros((args.steps, T * K_USED), dtype=torch.int64, device="cuda")
+    sel_w = torch.zeros((T * K_USED,), device="cuda")
+    for i in range(min(args.steps, 256)):
+        m.layer_dev(i % NL, normed[i % n_in].data_ptr(), T, x.data_ptr(),
+                    {"sel_id": sel[i].data_ptr(), "sel_w": sel_w.data_ptr()}, stream=sp)
+    torch.cuda.synchronize()
+    sel_h = sel[:min(args.steps, 256)].cpu().numpy()
+    used = [len(np.unique(r)) for r in sel_h]
+    U = float(np.mean(used))
+    bpe = bytes_per_expert(gate, down)
+    router_bytes = E * gb.row_bytes(gb.BF16, H)
+    layer_bytes = U * bpe + router_bytes + 2 * T * H * 4
+    gate_bytes = U * 2 * F * gb.row_bytes(gate, H) + T * H * 4 + T * K_USED * F * 4
+    down_bytes = U * H * gb.row_bytes(down, F) + T * K_USED * F * 4 + 2 * T * H * 4
+    zone_bytes = {"router": router_bytes + T * H * 4, "gate_up": gate_bytes,
+                  "act_prep": 2 * T * K_USED * F * 4, "down": down_bytes}
+    zone_ms = {z: (v[0] / v[1] if v[1] else 0.0) for z, v in zones.items()}
+    dom = max(zone_ms, key=lambda z: zone_ms[z])
+    peak, peak_kind = peaks()
+    achieved = zone_bytes[dom] / (zone_ms[dom] / 1000.0) / 1e9
+    traffic = None
+    try:
+        with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
+            traffic = json.load(f).get(f"{args.gate}/{args.down}/T{T}/{dom}")
+    except (OSError, ValueError):
+        pass
+    layer_ms = sum(zone_ms.values())
+
+    # e2e through the public host-pointer call, pinned buffers, copies inside the timed region
+    hn = torch.randn((n_in, T, H), generator=torch.Generator().manual_seed(99)).pin_memory()
+    hx = torch.randn((T, H)).pin_memory()
+    e2e_steps = max(min(args.steps, 2000), 10)
+    for i in range(5):
+        m.layer_ptrs(i % NL, hn[i % n_in].data_ptr(), T, hx.data_ptr(), host=True)
+    if dist:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for i in range(e2e_steps):
+        m.layer_ptrs(i % NL, hn[i % n_in].data_ptr(), T, hx.data_ptr(), host=True)
+    e2e_s = time.perf_counter() - t0
+    if dist:
+        t = torch.tensor([e2e_s], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    e2e = {"value": world * T * e2e_steps / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": 2 * T * H * 4,
+           "d2h_bytes_per_step": T * H * 4, "steps": e2e_steps}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        try:
+            cpu = cpu_reference(args, gate, down, args.cpu_seconds)
+        except Exception as exc:  # the prebuilt reference is missing on this box
+            cpu = {"value": None, "unit": "tokens/s", "cores": 0, "kind": "reference", "sample": f"unavailable: {exc}"}
+    launches = m.launches(T)
+    m.close()
+    if rank != 0:
+        return
+    line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int32/int64+f64 (Q4_K), f32 (Q6_K/Q8_0 lane contract)",
+            "data": "synthetic", "config": workload_config(args),
+            "roofline": {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "peak_kind": peak_kind, "traffic": traffic,
+                         "algorithmic_bytes": zone_bytes[dom], "avg_ms": zone_ms[dom]},
+            "layer_roofline": {"achieved": layer_bytes / (ms_step / 1000.0) / 1e9, "unit": "GB/s",
+                               "frac": layer_bytes / (ms_step / 1000.0) / 1e9 / peak, "bytes": layer_bytes,
+                               "distinct_experts": U, "zone_ms": zone_ms, "zone_sum_ms": layer_ms},
+            "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches * args.steps, "clocks": clk.summary()}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = args_parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    dist = None
+    if world > 1 and args.impl == "ours":
+        import datetime
+
+        import torch
+        import torch.distributed as dist_
+        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+        dist_.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+        dist = dist_
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+    else:
+        run_ours(args, rank, world, dist)
+    if dist:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,156 @@
+/* trmoe.h: the C ABI of libtrmoe.so, Trochilus's OLMoE Mixture-of-Experts layer on an NVIDIA B200.
+ *
+ * Two levels, both plain C (pointers and sizes; no CUDA or torch types in the signatures):
+ *
+ *  1. The layer hook, modelled on Trochilus's GPU attention backend (src/backend/gpu_attn.h:32-74): a
+ *     tr_gpu_moe holds every layer's router and experts resident in HBM, uploaded once from the host
+ *     GGUF bytes, and runs one MoE layer per call from the normed FFN input to the residual add. It
+ *     replaces forward_layer's block from the router matmul to the mix (src/models/olmoe.c:1845-1933).
+ *
+ *  2. The kernel level, the same names and arguments as Trochilus's quantized-matmul API
+ *     (src/kernels/kernels.h:239-300, 342-350): tr_matmul, tr_matmul_grouped(_s), tr_softmax,
+ *     tr_swiglu. Pointers are the caller's host memory as in the reference; a weight is uploaded the
+ *     first time its data pointer is seen and then read from HBM (the pointer must stay valid and its
+ *     bytes unchanged, as the reference's expert store slots are). The pool argument is ignored.
+ *
+ * Numerics: every result is bit for bit Trochilus's scalar definition (the 16-lane contract for F32,
+ * BF16, Q8_0 and Q6_K rows; Q4_K's exact-integer definition; the correctly rounded exp; the id-ordered
+ * combine), for every token count.
+ *
+ * Conventions kept from gpu_attn.h: int results are 0 on success and -1 on failure; creation returns
+ * NULL with a message in (err, err_len); one context, one thread at a time. There is no CPU fallback:
+ * a failure is an error. The void kernel-level calls have no return code in the reference; on a
+ * failure they print the reason to stderr, leave the output untouched and record the message that
+ * trmoe_last_error() returns. */
+#ifndef TRMOE_H
+#define TRMOE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define TRMOE_API __attribute__((visibility("default")))
+#else
+#define TRMOE_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ggml tensor type numbers (Trochilus src/format/gguf.h:16-27); the supported subset */
+enum { TRMOE_F32 = 0, TRMOE_F16 = 1, TRMOE_Q8_0 = 8, TRMOE_Q4_K = 12, TRMOE_Q6_K = 14, TRMOE_BF16 = 30 };
+
+/* ---------------------------------------------------------------------------------------------
+ * 1. The layer hook */
+
+typedef struct tr_gpu_moe tr_gpu_moe;
+
+typedef struct {
+    int64_t n_layers;   /* layers held */
+    int64_t n_expert;   /* experts per layer (<= 64) */
+    int64_t n_used;     /* experts per token (<= 32, <= n_expert) */
+    int64_t n_embd;     /* hidden size H: a multiple of 256 (OLMoE: 2048) */
+    int64_t n_ff;       /* expert intermediate size F: a multiple of 256 (OLMoE: 1024) */
+    int32_t norm_topk;  /* 1: the k weights renormalised to sum 1 (OLMoE: 0) */
+    int32_t router_type; /* F32 or BF16 */
+    int32_t gate_type;   /* Q8_0 or Q4_K (gate and up share it) */
+    int32_t down_type;   /* Q8_0, Q4_K or Q6_K */
+    int64_t max_tokens;  /* the most tokens one call passes */
+} tr_gpu_moe_config;
+
+/* Replaces: tr_gpu_attn_create (src/backend/gpu_attn.h:46-47) as the model's GPU context for the MoE
+ * layer. Device `device` (CUDA ordinal); the layers are set by tr_gpu_moe_set_layer. NULL with a
+ * message when the shape or a type is not supported, or HBM is short. */
+TRMOE_API tr_gpu_moe *tr_gpu_moe_create(const tr_gpu_moe_config *cfg, int device, char *err, size_t err_len);
+/* Replaces: tr_gpu_attn_free (src/backend/gpu_attn.h:48). NULL: nothing. */
+TRMOE_API void tr_gpu_moe_free(tr_gpu_moe *m);
+/* Replaces: tr_gpu_attn_bytes (src/backend/gpu_attn.h:50): bytes of HBM a context of cfg holds. */
+TRMOE_API uint64_t tr_gpu_moe_bytes(const tr_gpu_moe_config *cfg);
+
+/* Uploads layer `layer`'s weights from host GGUF bytes, replacing the reference's expert-store slots
+ * (src/models/olmoe.c:2146-2186; the tr_mat views of olmoe.c:466-472): router = n_expert rows of
+ * n_embd (ffn_gate_inp); router_bias = NULL or n_expert floats added to every logit (a benchmark
+ * extension, not in the reference); gate[e], up[e] = n_ff rows of n_embd; down[e] = n_embd rows of
+ * n_ff. Returns when the bytes are in HBM. 0, or -1 with a message. */
+TRMOE_API int tr_gpu_moe_set_layer(tr_gpu_moe *m, int64_t layer, const void *router, const float *router_bias,
+                         const void *const *gate, const void *const *up, const void *const *down, char *err,
+                         size_t err_len);
+
+/* Replaces: forward_layer's MoE block from the router to the mix (src/models/olmoe.c:1845-1933), the
+ * hook sitting where tr_gpu_attn_decode sits for the attention (olmoe.c:1790-1797).
+ * normed: n_tok rows of n_embd (the ffn_norm output); x_inout: the residual stream, n_tok rows of
+ * n_embd, to which the layer's output is added. sel_id_out, sel_w_out (optional): the n_tok * n_used
+ * experts (increasing id per token) and their weights. Host memory (pinned or not). Returns when x
+ * holds the result. 0, or -1 on a CUDA error or a bad argument. */
+TRMOE_API int tr_gpu_moe_layer(tr_gpu_moe *m, int64_t layer, const float *normed, int64_t n_tok, float *x_inout,
+                     int64_t *sel_id_out, float *sel_w_out);
+
+/* Optional device outputs of tr_gpu_moe_layer_dev (any field NULL: not written) */
+typedef struct {
+    float *logits;      /* [n_tok][n_expert] router logits (after the bias) */
+    int64_t *sel_id;    /* [n_tok * n_used] */
+    float *sel_w;       /* [n_tok * n_used] */
+    int64_t *offsets;   /* [n_expert + 1] segment starts of the grouped order */
+    int64_t *place;     /* [n_tok * n_used] grouped position of each (token, slot) row */
+    float *ffn_out;     /* [n_tok][n_embd] the layer's output before the residual add */
+} tr_gpu_moe_outputs;
+
+/* tr_gpu_moe_layer on device memory, enqueued on `stream` (a cudaStream_t; NULL: the context's own
+ * stream) and returning without waiting. d_normed and d_x_inout are device pointers. 0, or -1. */
+TRMOE_API int tr_gpu_moe_layer_dev(tr_gpu_moe *m, int64_t layer, const float *d_normed, int64_t n_tok, float *d_x_inout,
+                         const tr_gpu_moe_outputs *out, void *stream);
+
+/* Zone timing, the GPU counterpart of Trochilus's profiler zones (src/base/prof.h:42-47: ROUTER,
+ * EXPERT_GATE_UP, EXPERT_ACT, EXPERT_DOWN with EXPERT_MIX): when on, every layer call records CUDA events
+ * around its kernels on the stream it runs on. tr_gpu_moe_profile_read waits for the last call and
+ * returns, per zone, the summed milliseconds and the calls counted since profiling was switched on:
+ * zone 0 router + top-k + dispatch, 1 gate/up + SwiGLU, 2 the down input's Q4_K preparation (0 calls when
+ * the down is not Q4_K), 3 down + combine + residual. 0, or -1. */
+#define TRMOE_ZONES 4
+TRMOE_API int tr_gpu_moe_profile(tr_gpu_moe *m, int on);
+TRMOE_API int tr_gpu_moe_profile_read(tr_gpu_moe *m, double *ms, int64_t *calls, int n_zones);
+
+/* How many kernels one tr_gpu_moe_layer_dev call launches for n_tok tokens. */
+TRMOE_API int tr_gpu_moe_launches(const tr_gpu_moe *m, int64_t n_tok);
+
+/* The message of this thread's last failure ("" if none). */
+TRMOE_API const char *trmoe_last_error(void);
+
+/* ---------------------------------------------------------------------------------------------
+ * 2. The kernel level (Trochilus src/kernels/kernels.h) */
+
+typedef struct tr_pool tr_pool; /* the reference's thread pool: accepted and ignored */
+
+/* Trochilus's tr_mat (src/kernels/kernels.h:69-76): `rows` rows of `cols` elements of `type`, ggml
+ * layout. The type is a ggml type number (an enum in the reference, an int here: same size). */
+typedef struct {
+    int32_t type;
+    int64_t rows;
+    int64_t cols;
+    const void *data;
+} tr_mat;
+
+/* Replaces: tr_matmul (src/kernels/kernels.h:239). y[t*rows + r] = row r of w . x[t*cols ..]. */
+TRMOE_API void tr_matmul(tr_pool *pool, const tr_mat *w, const float *x, int64_t n_tokens, float *y);
+/* Replaces: tr_matmul_grouped (src/kernels/kernels.h:244-245). Group g holds input rows
+ * [offsets[g], offsets[g+1]) and multiplies them by w[g]; empty groups skipped. */
+TRMOE_API void tr_matmul_grouped(tr_pool *pool, const tr_mat *w, const int64_t *offsets, int64_t n_groups, const float *x,
+                       float *y);
+/* Replaces: tr_matmul_grouped_s (src/kernels/kernels.h:277-278); the scratch argument is ignored (the
+ * GPU keeps its own), the result is tr_matmul_grouped's. */
+TRMOE_API void tr_matmul_grouped_s(tr_pool *pool, const tr_mat *w, const int64_t *offsets, int64_t n_groups, const float *x,
+                         float *y, const void *s);
+/* Replaces: tr_softmax (src/kernels/kernels.h:342): in place over n logits. */
+TRMOE_API void tr_softmax(float *x, int64_t n);
+/* Replaces: tr_swiglu (src/kernels/kernels.h:345): x[i] = silu(x[i]) * y[i]. */
+TRMOE_API void tr_swiglu(tr_pool *pool, float *x, const float *y, int64_t n);
+
+/* Drops every weight the kernel level uploaded (the next call uploads again). */
+TRMOE_API void trmoe_kernel_cache_clear(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif

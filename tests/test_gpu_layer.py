@@ -1,0 +1,109 @@
+"""The MoE layer on the GPU through the C ABI (tr_gpu_moe_*), compared bit for bit with Trochilus's own
+outputs (golden vectors) and with the CPU oracle (fresh seeds): logits, top-k ids and weights, the
+dispatch permutation, the layer output and the residual."""
+import os
+
+import numpy as np
+import pytest
+
+from oracle.oracle import make_desc
+from tests.golden.cases import CASES, build_case, digest, same_bits
+from trochilus_b200 import gguf_blocks as gb
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+pytestmark = pytest.mark.gpu
+
+
+def _ctx(c, n_layers=1, max_tokens=None):
+    from trochilus_b200.moe import GpuMoe
+    return GpuMoe(n_layers, c["E"], c["k"], c["H"], c["F"], c["router"], c["gate"], c["down"],
+                  max_tokens or c["T"], norm_topk=c["norm_topk"])
+
+
+def _dev_outputs(torch, m, layer, normed, x, E, k):
+    T, H = normed.shape
+    dn = torch.from_numpy(normed).cuda()
+    dx = torch.from_numpy(x.copy()).cuda()
+    o = {"logits": torch.full((T, E), float("nan"), device="cuda"),
+         "sel_id": torch.full((T * k,), -1, dtype=torch.int64, device="cuda"),
+         "sel_w": torch.full((T * k,), float("nan"), device="cuda"),
+         "offsets": torch.full((E + 1,), -1, dtype=torch.int64, device="cuda"),
+         "place": torch.full((T * k,), -1, dtype=torch.int64, device="cuda"),
+         "ffn_out": torch.full((T, H), float("nan"), device="cuda")}
+    m.layer_dev(layer, dn.data_ptr(), T, dx.data_ptr(), {kk: v.data_ptr() for kk, v in o.items()},
+                stream=torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    res = {kk: v.cpu().numpy() for kk, v in o.items()}
+    res["x"] = dx.cpu().numpy()
+    res["sel_id"] = res["sel_id"].reshape(T, k)
+    res["sel_w"] = res["sel_w"].reshape(T, k)
+    res["place"] = res["place"].reshape(T, k)
+    return res
+
+
+@pytest.mark.parametrize("case", CASES, ids=[c["name"] for c in CASES])
+def test_layer_matches_reference_golden(cuda, case):
+    g = np.load(os.path.join(GOLDEN, case["name"] + ".npz"))
+    lay, bias, normed, x = build_case(case)
+    assert digest(lay, bias, normed, x) == str(g["digest"]), "the synthetic generator changed"
+    m = _ctx(case)
+    m.set_layer(0, lay, bias)
+    for rep in range(2):  # a second call: counters and scratch left clean by the first
+        xo = x.copy()
+        sid, sw = m.layer(0, normed, xo)
+        assert same_bits(sid, g["sel_id"]), rep
+        assert same_bits(sw, g["sel_w"]), rep
+        assert same_bits(xo, g["x"]), rep
+    r = _dev_outputs(cuda, m, 0, normed, x, case["E"], case["k"])
+    for key in ("logits", "sel_id", "sel_w", "offsets", "place", "ffn_out", "x"):
+        assert same_bits(r[key], g[key]), key
+    m.close()
+
+
+@pytest.mark.parametrize("gt,dt,rt", [(gb.Q8_0, gb.Q8_0, gb.F32), (gb.Q4_K, gb.Q6_K, gb.BF16),
+                                      (gb.Q4_K, gb.Q4_K, gb.BF16), (gb.Q8_0, gb.Q4_K, gb.F32),
+                                      (gb.Q4_K, gb.Q8_0, gb.F32), (gb.Q8_0, gb.Q6_K, gb.BF16)])
+def test_layer_matches_oracle_fresh_seeds(cuda, oracle, gt, dt, rt):
+    rng = np.random.default_rng(gt * 100 + dt)
+    lay = gb.make_layer(int(rng.integers(1 << 30)), 64, 2048, 1024, gt, dt, rt, mode="random")
+    bias = gb.zipf_bias(3, 64)
+    d, keep = make_desc(lay, 2048, 1024, 8, 0, rt, gt, dt, bias)
+    m = _ctx(dict(E=64, k=8, H=2048, F=1024, router=rt, gate=gt, down=dt, norm_topk=0, T=16))
+    m.set_layer(0, lay, bias)
+    for T in (1, 2, 7, 16):
+        normed = rng.normal(size=(T, 2048)).astype(np.float32)
+        x = rng.normal(size=(T, 2048)).astype(np.float32)
+        want = oracle.moe_layer(d, normed, x)
+        got = _dev_outputs(cuda, m, 0, normed, x, 64, 8)
+        for key in ("logits", "sel_id", "sel_w", "offsets", "place", "ffn_out", "x"):
+            assert same_bits(got[key], want[key]), (T, key)
+    m.close()
+
+
+def test_many_layers_one_context(cuda, oracle):
+    """layers set independently, called in any order, each its own weights"""
+    c = dict(E=64, k=8, H=2048, F=1024, router=gb.BF16, gate=gb.Q4_K, down=gb.Q6_K, norm_topk=0, T=3)
+    m = _ctx(c, n_layers=3)
+    lays = [gb.make_layer(900 + i, 64, 2048, 1024, gb.Q4_K, gb.Q6_K, gb.BF16, mode="random") for i in range(3)]
+    for i in (2, 0, 1):
+        m.set_layer(i, lays[i])
+    rng = np.random.default_rng(1)
+    for L in (1, 2, 0, 1):
+        normed = rng.normal(size=(3, 2048)).astype(np.float32)
+        x = rng.normal(size=(3, 2048)).astype(np.float32)
+        d, keep = make_desc(lays[L], 2048, 1024, 8, 0, gb.BF16, gb.Q4_K, gb.Q6_K)
+        want = oracle.moe_layer(d, normed, x)
+        xo = x.copy()
+        sid, sw = m.layer(L, normed, xo)
+        assert same_bits(xo, want["x"]) and same_bits(sid, want["sel_id"]), L
+    with pytest.raises(RuntimeError):
+        m.layer(0, np.zeros((4, 2048), np.float32), np.zeros((4, 2048), np.float32))  # past max_tokens
+    m.close()
+
+
+def test_unset_layer_is_an_error(cuda):
+    c = dict(E=64, k=8, H=2048, F=1024, router=gb.F32, gate=gb.Q8_0, down=gb.Q8_0, norm_topk=0, T=1)
+    m = _ctx(c, n_layers=2)
+    with pytest.raises(RuntimeError, match="not set"):
+        m.layer(1, np.zeros((1, 2048), np.float32), np.zeros((1, 2048), np.float32))
+    m.close()

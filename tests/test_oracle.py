@@ -1,0 +1,140 @@
+"""The CPU oracle (oracle/moe_oracle.c) pinned against Trochilus's own code (oracle/_ref) and against the
+golden vectors that code produced (tests/golden). CPU only."""
+import os
+
+import numpy as np
+import pytest
+
+from oracle.oracle import make_desc
+from tests.golden.cases import CASES, build_case, digest, same_bits
+from trochilus_b200 import gguf_blocks as gb
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+
+def _special_floats():
+    u = np.array([0x00000000, 0x80000000, 0x00000001, 0x007fffff, 0x00800000, 0x3f800000, 0xbf800000, 0x7f7fffff,
+                  0xff7fffff, 0x7f800000, 0xff800000, 0x7fc00000, 0x42b17218, 0x42b17217, 0x42b17219, 0xc2d00000,
+                  0xc2cff1b5, 0xc2cff1b4, 0xc2ce8ed0], dtype=np.uint32)
+    return u.view(np.float32)
+
+
+def test_expf_pinned_to_reference_sampled(oracle, reflib):
+    rng = np.random.default_rng(5)
+    x = rng.integers(0, 2 ** 32, size=1 << 22, dtype=np.uint64).astype(np.uint32).view(np.float32)
+    x = np.concatenate([x, _special_floats(), np.linspace(-110, 90, 200001, dtype=np.float32)])
+    assert same_bits(oracle.expf(x), reflib.expf(x))
+
+
+def test_expf_exception_table(oracle):
+    from trochilus_b200.csrc_consts import exceptions
+    for xb, yb in exceptions():
+        y = oracle.expf(np.array([xb], np.uint32).view(np.float32))
+        assert y.view(np.uint32)[0] == yb
+
+
+@pytest.mark.skipif(os.environ.get("TRX_EXHAUSTIVE") != "1", reason="all 2^32 floats: set TRX_EXHAUSTIVE=1")
+def test_expf_exhaustive(oracle, reflib):
+    for hi in range(1 << 8):
+        u = (np.arange(1 << 24, dtype=np.uint64) + (hi << 24)).astype(np.uint32)
+        x = u.view(np.float32)
+        assert same_bits(oracle.expf(x), reflib.expf(x)), hex(hi)
+
+
+@pytest.mark.parametrize("type_,n", [(gb.F32, 2048), (gb.BF16, 2048), (gb.Q8_0, 2048), (gb.Q8_0, 1024),
+                                     (gb.Q4_K, 2048), (gb.Q4_K, 512), (gb.Q6_K, 1024), (gb.Q6_K, 256)])
+@pytest.mark.parametrize("special", [False, True])
+def test_dot_row_pinned_to_reference(oracle, reflib, type_, n, special):
+    from tests.golden.cases import witness_inputs
+    rng = np.random.default_rng(n + type_ + special)
+    if type_ in (gb.F32, gb.BF16):
+        rows = gb.quantize(type_, gb.round_to_bf16(rng.normal(0, 0.02, size=(8, n)).astype(np.float32)))
+    else:
+        rows = gb.random_blocks(type_, 8, n, rng, special=special)
+    xs = witness_inputs(rng, 6, n) if special else rng.normal(size=(6, n)).astype(np.float32)
+    for r in range(rows.shape[0]):
+        for x in xs:
+            a, b = oracle.dot_row(type_, rows[r], x), reflib.dot_row(type_, rows[r], x)
+            assert same_bits(np.float32(a), np.float32(b)), (r, a, b)
+
+
+def test_dot_row_not_blind(oracle):
+    """one ulp of one block's d changes the result (the comparison can see a wrong bit)"""
+    rng = np.random.default_rng(3)
+    for t in (gb.Q8_0, gb.Q4_K, gb.Q6_K):
+        row = gb.random_blocks(t, 1, 512, rng)[0]
+        x = rng.normal(size=512).astype(np.float32)
+        good = oracle.dot_row(t, row, x)
+        off = {gb.Q8_0: 34, gb.Q4_K: 144, gb.Q6_K: 210 + 208}[t]
+        bad = row.copy()
+        bad[off] ^= 1
+        assert not same_bits(np.float32(good), np.float32(oracle.dot_row(t, bad, x)))
+
+
+@pytest.mark.parametrize("case", CASES, ids=[c["name"] for c in CASES])
+def test_oracle_matches_golden(oracle, case):
+    g = np.load(os.path.join(GOLDEN, case["name"] + ".npz"))
+    lay, bias, normed, x = build_case(case)
+    assert digest(lay, bias, normed, x) == str(g["digest"]), "the synthetic generator changed: regenerate fixtures"
+    if case["T"] > 16:
+        pytest.skip("long case: covered on the GPU against the reference fixture")
+    d, keep = make_desc(lay, case["H"], case["F"], case["k"], case["norm_topk"], case["router"], case["gate"],
+                        case["down"], bias)
+    r = oracle.moe_layer(d, normed, x)
+    for key in ("logits", "sel_id", "sel_w", "offsets", "place", "ffn_out", "x"):
+        assert same_bits(r[key], g[key]), key
+
+
+def test_oracle_matches_reference_live(oracle, reflib):
+    """fresh seeds, every type pair, T from 1 to 9, routing with and without renormalisation"""
+    rng = np.random.default_rng(77)
+    pool = reflib.pool(0)
+    for i, (gt, dt, rt) in enumerate([(gb.Q8_0, gb.Q8_0, gb.F32), (gb.Q4_K, gb.Q6_K, gb.BF16),
+                                      (gb.Q4_K, gb.Q4_K, gb.F32), (gb.Q8_0, gb.Q4_K, gb.BF16)]):
+        E, k, H, F = (64, 8, 2048, 1024) if i % 2 == 0 else (32, 6, 2048, 512)
+        lay = gb.make_layer(500 + i, E, H, F, gt, dt, rt, mode="random", special=(i == 2))
+        T = int(rng.integers(1, 10))
+        normed = rng.normal(size=(T, H)).astype(np.float32)
+        x = rng.normal(size=(T, H)).astype(np.float32)
+        d, keep = make_desc(lay, H, F, k, i % 2, rt, gt, dt, None)
+        a = oracle.moe_layer(d, normed, x)
+        b = reflib.moe_layer(d, normed, x, pool=pool)
+        for key in ("logits", "sel_id", "sel_w", "offsets", "place", "h1", "h3", "ffn_out", "x"):
+            assert same_bits(a[key], b[key]), (i, key)
+    reflib.pool_destroy(pool)
+
+
+def test_grouped_layout_edges(oracle, reflib):
+    """the reference's grouped-matmul layouts (tests/test_kernels.c:1785-1888): empty groups first, middle
+    and last, one-row groups, odd row counts"""
+    rng = np.random.default_rng(9)
+    for t, rows, cols in ((gb.Q8_0, 48, 512), (gb.Q4_K, 32, 512), (gb.Q6_K, 16, 256), (gb.F32, 24, 64)):
+        mats = [gb.random_blocks(t, rows, cols, rng) if t != gb.F32 else
+                gb.quantize(gb.F32, rng.normal(size=(rows, cols)).astype(np.float32)) for _ in range(6)]
+        offsets = np.array([0, 0, 1, 1, 4, 9, 9])
+        x = rng.normal(size=(9, cols)).astype(np.float32)
+        assert same_bits(oracle.matmul_grouped(t, rows, cols, mats, offsets, x),
+                         reflib.matmul_grouped(t, rows, cols, mats, offsets, x))
+
+
+def test_softmax_swiglu_pinned(oracle, reflib):
+    rng = np.random.default_rng(4)
+    for n in (1, 7, 16, 64, 100, 1000):
+        x = (rng.normal(size=n) * 5).astype(np.float32)
+        assert same_bits(oracle.softmax(x), reflib.softmax(x))
+    x = (rng.normal(size=5000) * 8).astype(np.float32)
+    y = rng.normal(size=5000).astype(np.float32)
+    x[:6] = [0.0, -0.0, np.inf, -np.inf, np.nan, 100.0]
+    assert same_bits(oracle.swiglu(x, y), reflib.swiglu(x, y))
+
+
+@pytest.mark.parametrize("t", [gb.Q8_0, gb.Q4_K, gb.Q6_K])
+def test_encoders_decode_close(reflib, t):
+    """this project's encoders give blocks the reference decodes back to the inputs (within the format's step)"""
+    rng = np.random.default_rng(t)
+    w = rng.normal(0, 0.02, size=(4, 512)).astype(np.float32)
+    q = gb.quantize(t, w)
+    for r in range(4):
+        back = reflib.dequant_row(t, q[r], 512)
+        tol = {gb.Q8_0: 0.02 * 4 / 127, gb.Q4_K: 0.02 * 8 / 15 * 1.2, gb.Q6_K: 0.02 * 4 / 31}[t]
+        assert np.max(np.abs(back - w[r])) < tol

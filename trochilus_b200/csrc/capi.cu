@@ -1,0 +1,681 @@
+// capi.cu: the extern "C" entry points of libtrmoe.so (declared in include/trmoe.h).
+//
+// Host side of the layer hook (tr_gpu_moe_*) and of the kernel-level API (tr_matmul*, tr_softmax,
+// tr_swiglu). Plain CUDA runtime; no torch. Every host wait on the GPU polls with a deadline and
+// reports a timeout as an error instead of blocking forever.
+#include <cuda_runtime.h>
+
+#include <chrono>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <thread>
+#include <unordered_map>
+#include <vector>
+
+#include "../../include/trmoe.h"
+#include "common.cuh"
+#include "expf.cuh"
+#include "layouts.cuh"
+#include "moe_kernels.cuh"
+#include "kernel_api.cuh"
+
+namespace {
+
+thread_local std::string g_err;
+
+void set_err(const char *fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    g_err = buf;
+}
+
+void put_err(char *err, size_t err_len) {
+    if (err != nullptr && err_len > 0) snprintf(err, err_len, "%s", g_err.c_str());
+}
+
+bool ck(cudaError_t e, const char *what) {
+    if (e == cudaSuccess) return true;
+    set_err("%s: %s", what, cudaGetErrorString(e));
+    return false;
+}
+
+// waits for the stream, polling; a GPU that does not finish within timeout_s is an error, not a hang
+bool stream_wait(cudaStream_t s, double timeout_s = 60.0) {
+    const auto t0 = std::chrono::steady_clock::now();
+    for (unsigned spins = 0;; spins++) {
+        const cudaError_t e = cudaStreamQuery(s);
+        if (e == cudaSuccess) return true;
+        if (e != cudaErrorNotReady) return ck(e, "cudaStreamQuery");
+        const double dt = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+        if (dt > timeout_s) {
+            set_err("the GPU did not finish within %.0f s", timeout_s);
+            return false;
+        }
+        if (spins > 64) std::this_thread::sleep_for(std::chrono::microseconds(20));
+    }
+}
+
+int64_t align_up(int64_t v, int64_t a) { return (v + a - 1) / a * a; }
+
+
+// Copies one GGUF matrix (rows x cols of type) from the host into dst in its device layout;
+// tmp: a device staging buffer of at least the matrix's bytes (for the repacked types).
+bool upload_matrix(int type, int64_t rows, int64_t cols, const void *host, uint8_t *dst, uint8_t *tmp,
+                   cudaStream_t st) {
+    const int64_t bytes = trx_row_bytes(type, cols) * rows;
+    if (bytes <= 0) {
+        set_err("type %d with %lld columns has no whole rows", type, (long long)cols);
+        return false;
+    }
+    if (type == TRX_Q8_0 || type == TRX_Q6_K) {
+        if (cols % 256 != 0) {
+            set_err("type %d needs a multiple of 256 columns, got %lld", type, (long long)cols);
+            return false;
+        }
+        if (!ck(cudaMemcpyAsync(tmp, host, (size_t)bytes, cudaMemcpyHostToDevice, st), "upload")) return false;
+        if (type == TRX_Q8_0) trx_repack_q8l<<<(unsigned)rows, 256, 0, st>>>(tmp, dst, rows, cols);
+        else trx_repack_q6l<<<(unsigned)rows, 128, 0, st>>>(tmp, dst, rows, cols);
+        if (!ck(cudaGetLastError(), "repack")) return false;
+    } else {
+        if (!ck(cudaMemcpyAsync(dst, host, (size_t)bytes, cudaMemcpyHostToDevice, st), "upload")) return false;
+    }
+    return stream_wait(st, 300.0);
+}
+
+struct WorkLayout {
+    int64_t off[24];
+    int64_t total;
+};
+
+// carve the workspace of one context (every piece 256-byte aligned)
+WorkLayout work_layout(const tr_gpu_moe_config &c) {
+    const int64_t T = c.max_tokens, E = c.n_expert, k = c.n_used, H = c.n_embd, F = c.n_ff, R = T * k;
+    const int64_t sizes[] = {
+        T * E * 4,          // 0 logits
+        R * 4,              // 1 sel_id
+        R * 4,              // 2 sel_w
+        (E + 1) * 4,        // 3 offsets
+        R * 4,              // 4 place
+        R * 4,              // 5 xmap
+        E * 4,              // 6 active
+        4,                  // 7 n_active
+        4,                  // 8 route_cnt
+        (H / TRX_DN_ROWS) * 4, // 9 comb_cnt
+        T * H * 4,          // 10 x_lc
+        T * H * 4,          // 11 xq
+        T * (H / 32) * 8,   // 12 xq_bf
+        T * (H / 256) * 8,  // 13 xq_sc
+        R * F * 4,          // 14 h
+        R * F * 4,          // 15 hq
+        R * (F / 32) * 8,   // 16 hq_bf
+        R * (F / 256) * 8,  // 17 hq_sc
+        R * H * 4,          // 18 h3
+        T * H * 4,          // 19 host-call normed
+        T * H * 4,          // 20 host-call x
+        R * 8,              // 21 host-call sel_id
+        R * 4,              // 22 host-call sel_w
+    };
+    WorkLayout w{};
+    int64_t o = 0;
+    for (int i = 0; i < 23; i++) {
+        w.off[i] = o;
+        o += align_up(sizes[i], 256);
+    }
+    w.total = o;
+    return w;
+}
+
+int64_t mat_stride(int type, int64_t rows, int64_t cols) { return align_up(trx_row_bytes(type, cols) * rows, 256); }
+
+int64_t layer_bytes(const tr_gpu_moe_config &c) {
+    const int64_t E = c.n_expert, H = c.n_embd, F = c.n_ff;
+    return align_up(trx_row_bytes(c.router_type, H) * E, 256) + align_up(E * 4, 256) +
+           2 * E * mat_stride(c.gate_type, F, H) + E * mat_stride(c.down_type, H, F);
+}
+
+} // namespace
+
+struct tr_gpu_moe {
+    tr_gpu_moe_config cfg;
+    int device = 0, sm_count = 148;
+    cudaStream_t stream = nullptr;
+    std::vector<uint8_t *> layer_mem;
+    std::vector<TrxLayer> layers;
+    std::vector<int> layer_set;
+    uint8_t *work_mem = nullptr;
+    uint8_t *tmp = nullptr;
+    TrxWork work{};
+    float *d_normed = nullptr, *d_x = nullptr;
+    int64_t *d_sel_id = nullptr;
+    float *d_sel_w = nullptr;
+    // zone timing (tr_gpu_moe_profile)
+    bool prof = false, prof_pending = false;
+    cudaEvent_t ev[TRMOE_ZONES + 1] = {};
+    bool ev_used[TRMOE_ZONES] = {};
+    double prof_ms[TRMOE_ZONES] = {};
+    int64_t prof_calls[TRMOE_ZONES] = {};
+};
+
+// adds the last call's zone times to the sums (waits for its events)
+static bool prof_collect(tr_gpu_moe *m) {
+    if (!m->prof_pending) return true;
+    if (!ck(cudaEventSynchronize(m->ev[TRMOE_ZONES]), "cudaEventSynchronize")) return false;
+    for (int z = 0; z < TRMOE_ZONES; z++) {
+        if (!m->ev_used[z]) continue;
+        float ms = 0.0f;
+        if (!ck(cudaEventElapsedTime(&ms, m->ev[z], m->ev[z + 1]), "cudaEventElapsedTime")) return false;
+        m->prof_ms[z] += ms;
+        m->prof_calls[z] += 1;
+    }
+    m->prof_pending = false;
+    return true;
+}
+
+extern "C" const char *trmoe_last_error(void) { return g_err.c_str(); }
+
+extern "C" uint64_t tr_gpu_moe_bytes(const tr_gpu_moe_config *cfg) {
+    if (cfg == nullptr) return 0;
+    return (uint64_t)(layer_bytes(*cfg) * cfg->n_layers + work_layout(*cfg).total);
+}
+
+static bool check_config(const tr_gpu_moe_config *c) {
+    if (c == nullptr) {
+        set_err("no config");
+        return false;
+    }
+    if (c->n_layers < 1 || c->n_expert < 1 || c->n_expert > TRX_MAX_EXPERTS || c->n_used < 1 ||
+        c->n_used > TRX_MAX_USED || c->n_used > c->n_expert || c->max_tokens < 1) {
+        set_err("unsupported counts (layers %lld, experts %lld, used %lld, max tokens %lld)", (long long)c->n_layers,
+                (long long)c->n_expert, (long long)c->n_used, (long long)c->max_tokens);
+        return false;
+    }
+    if (c->n_embd % 256 || c->n_ff % 256 || c->n_embd < 256 || c->n_ff < 256 || c->n_embd > 8192) {
+        set_err("n_embd and n_ff must be multiples of 256 (n_embd <= 8192), got %lld and %lld", (long long)c->n_embd,
+                (long long)c->n_ff);
+        return false;
+    }
+    if (c->router_type != TRX_F32 && c->router_type != TRX_BF16) {
+        set_err("router type %d not supported (F32, BF16)", c->router_type);
+        return false;
+    }
+    if (c->gate_type != TRX_Q8_0 && c->gate_type != TRX_Q4_K) {
+        set_err("gate/up type %d not supported (Q8_0, Q4_K)", c->gate_type);
+        return false;
+    }
+    if (c->down_type != TRX_Q8_0 && c->down_type != TRX_Q4_K && c->down_type != TRX_Q6_K) {
+        set_err("down type %d not supported (Q8_0, Q4_K, Q6_K)", c->down_type);
+        return false;
+    }
+    if (c->gate_type == TRX_Q4_K && c->n_embd != 2048) {
+        set_err("Q4_K gate/up needs n_embd 2048 (8 blocks a row), got %lld", (long long)c->n_embd);
+        return false;
+    }
+    if (c->down_type == TRX_Q4_K && c->n_ff != 1024) {
+        set_err("Q4_K down needs n_ff 1024 (4 blocks a row), got %lld", (long long)c->n_ff);
+        return false;
+    }
+    return true;
+}
+
+extern "C" tr_gpu_moe *tr_gpu_moe_create(const tr_gpu_moe_config *cfg, int device, char *err, size_t err_len) {
+    g_err.clear();
+    if (!check_config(cfg)) {
+        put_err(err, err_len);
+        return nullptr;
+    }
+    tr_gpu_moe *m = new tr_gpu_moe();
+    m->cfg = *cfg;
+    m->device = device;
+    const WorkLayout wl = work_layout(*cfg);
+    const int64_t lb = layer_bytes(*cfg);
+    const int64_t tmp_bytes = std::max(trx_row_bytes(cfg->gate_type, cfg->n_embd) * cfg->n_ff,
+                                       trx_row_bytes(cfg->down_type, cfg->n_ff) * cfg->n_embd);
+    bool ok = ck(cudaSetDevice(device), "cudaSetDevice") &&
+              ck(cudaDeviceGetAttribute(&m->sm_count, cudaDevAttrMultiProcessorCount, device), "attribute") &&
+              ck(cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking), "cudaStreamCreate") &&
+              ck(cudaMalloc(&m->work_mem, (size_t)wl.total), "cudaMalloc(workspace)") &&
+              ck(cudaMemset(m->work_mem, 0, (size_t)wl.total), "cudaMemset") &&
+              ck(cudaMalloc(&m->tmp, (size_t)tmp_bytes), "cudaMalloc(staging)");
+    if (ok) {
+        m->layer_mem.assign((size_t)cfg->n_layers, nullptr);
+        m->layers.assign((size_t)cfg->n_layers, TrxLayer{});
+        m->layer_set.assign((size_t)cfg->n_layers, 0);
+        for (int64_t l = 0; l < cfg->n_layers && ok; l++)
+            ok = ck(cudaMalloc(&m->layer_mem[(size_t)l], (size_t)lb), "cudaMalloc(layer)");
+    }
+    if (!ok) {
+        put_err(err, err_len);
+        tr_gpu_moe_free(m);
+        return nullptr;
+    }
+    uint8_t *b = m->work_mem;
+    TrxWork &w = m->work;
+    w.logits = (float *)(b + wl.off[0]);
+    w.sel_id = (int32_t *)(b + wl.off[1]);
+    w.sel_w = (float *)(b + wl.off[2]);
+    w.offsets = (int32_t *)(b + wl.off[3]);
+    w.place = (int32_t *)(b + wl.off[4]);
+    w.xmap = (int32_t *)(b + wl.off[5]);
+    w.active = (int32_t *)(b + wl.off[6]);
+    w.n_active = (int32_t *)(b + wl.off[7]);
+    w.route_cnt = (uint32_t *)(b + wl.off[8]);
+    w.comb_cnt = (uint32_t *)(b + wl.off[9]);
+    w.x_lc = (float *)(b + wl.off[10]);
+    w.xq = (uint32_t *)(b + wl.off[11]);
+    w.xq_bf = (double *)(b + wl.off[12]);
+    w.xq_sc = (double *)(b + wl.off[13]);
+    w.h = (float *)(b + wl.off[14]);
+    w.hq = (uint32_t *)(b + wl.off[15]);
+    w.hq_bf = (double *)(b + wl.off[16]);
+    w.hq_sc = (double *)(b + wl.off[17]);
+    w.h3 = (float *)(b + wl.off[18]);
+    m->d_normed = (float *)(b + wl.off[19]);
+    m->d_x = (float *)(b + wl.off[20]);
+    m->d_sel_id = (int64_t *)(b + wl.off[21]);
+    m->d_sel_w = (float *)(b + wl.off[22]);
+    return m;
+}
+
+extern "C" void tr_gpu_moe_free(tr_gpu_moe *m) {
+    if (m == nullptr) return;
+    cudaSetDevice(m->device);
+    if (m->stream) stream_wait(m->stream, 60.0);
+    for (uint8_t *p : m->layer_mem)
+        if (p) cudaFree(p);
+    if (m->work_mem) cudaFree(m->work_mem);
+    if (m->tmp) cudaFree(m->tmp);
+    for (cudaEvent_t e : m->ev)
+        if (e) cudaEventDestroy(e);
+    if (m->stream) cudaStreamDestroy(m->stream);
+    delete m;
+}
+
+extern "C" int tr_gpu_moe_set_layer(tr_gpu_moe *m, int64_t layer, const void *router, const float *router_bias,
+                                    const void *const *gate, const void *const *up, const void *const *down,
+                                    char *err, size_t err_len) {
+    g_err.clear();
+    if (m == nullptr || layer < 0 || layer >= m->cfg.n_layers || router == nullptr || gate == nullptr ||
+        up == nullptr || down == nullptr) {
+        set_err("bad arguments to tr_gpu_moe_set_layer");
+        put_err(err, err_len);
+        return -1;
+    }
+    const tr_gpu_moe_config &c = m->cfg;
+    const int64_t E = c.n_expert, H = c.n_embd, F = c.n_ff;
+    if (!ck(cudaSetDevice(m->device), "cudaSetDevice")) {
+        put_err(err, err_len);
+        return -1;
+    }
+    uint8_t *b = m->layer_mem[(size_t)layer];
+    TrxLayer L{};
+    L.router_type = c.router_type;
+    L.gate_type = L.up_type = c.gate_type;
+    L.down_type = c.down_type;
+    const int64_t router_bytes = trx_row_bytes(c.router_type, H) * E;
+    int64_t o = 0;
+    L.router = b + o;
+    o += align_up(router_bytes, 256);
+    float *bias = (float *)(b + o);
+    o += align_up(E * 4, 256);
+    L.router_bias = router_bias ? bias : nullptr;
+    L.gate_mb = mat_stride(c.gate_type, F, H);
+    L.up_mb = L.gate_mb;
+    L.down_mb = mat_stride(c.down_type, H, F);
+    L.gate = b + o;
+    o += E * L.gate_mb;
+    L.up = b + o;
+    o += E * L.up_mb;
+    L.down = b + o;
+    bool ok = ck(cudaMemcpyAsync((void *)L.router, router, (size_t)router_bytes, cudaMemcpyHostToDevice, m->stream),
+                 "upload router");
+    if (ok && router_bias)
+        ok = ck(cudaMemcpyAsync(bias, router_bias, (size_t)E * 4, cudaMemcpyHostToDevice, m->stream), "upload bias");
+    for (int64_t e = 0; e < E && ok; e++) {
+        ok = upload_matrix(c.gate_type, F, H, gate[e], (uint8_t *)L.gate + e * L.gate_mb, m->tmp, m->stream) &&
+             upload_matrix(c.gate_type, F, H, up[e], (uint8_t *)L.up + e * L.up_mb, m->tmp, m->stream) &&
+             upload_matrix(c.down_type, H, F, down[e], (uint8_t *)L.down + e * L.down_mb, m->tmp, m->stream);
+    }
+    if (ok) ok = stream_wait(m->stream, 300.0);
+    if (!ok) {
+        put_err(err, err_len);
+        return -1;
+    }
+    m->layers[(size_t)layer] = L;
+    m->layer_set[(size_t)layer] = 1;
+    return 0;
+}
+
+extern "C" int tr_gpu_moe_profile(tr_gpu_moe *m, int on) {
+    g_err.clear();
+    if (m == nullptr || !ck(cudaSetDevice(m->device), "cudaSetDevice")) return -1;
+    if (on && m->ev[0] == nullptr)
+        for (cudaEvent_t &e : m->ev)
+            if (!ck(cudaEventCreate(&e), "cudaEventCreate")) return -1;
+    if (!prof_collect(m)) return -1;
+    m->prof = on != 0;
+    for (int z = 0; z < TRMOE_ZONES; z++) {
+        m->prof_ms[z] = 0.0;
+        m->prof_calls[z] = 0;
+    }
+    return 0;
+}
+
+extern "C" int tr_gpu_moe_profile_read(tr_gpu_moe *m, double *ms, int64_t *calls, int n_zones) {
+    g_err.clear();
+    if (m == nullptr || !ck(cudaSetDevice(m->device), "cudaSetDevice") || !prof_collect(m)) return -1;
+    for (int z = 0; z < n_zones && z < TRMOE_ZONES; z++) {
+        if (ms) ms[z] = m->prof_ms[z];
+        if (calls) calls[z] = m->prof_calls[z];
+    }
+    return 0;
+}
+
+extern "C" int tr_gpu_moe_launches(const tr_gpu_moe *m, int64_t n_tok) {
+    (void)n_tok;
+    if (m == nullptr) return 0;
+    return m->cfg.down_type == TRX_Q4_K ? 4 : 3;
+}
+
+static int launch_layer(tr_gpu_moe *m, int64_t layer, const float *d_normed, int64_t n_tok, float *d_x,
+                        const tr_gpu_moe_outputs *out, cudaStream_t st) {
+    const tr_gpu_moe_config &c = m->cfg;
+    if (layer < 0 || layer >= c.n_layers || !m->layer_set[(size_t)layer]) {
+        set_err("layer %lld is not set", (long long)layer);
+        return -1;
+    }
+    if (n_tok < 1 || n_tok > c.max_tokens || d_normed == nullptr || d_x == nullptr) {
+        set_err("bad token count %lld (max %lld) or input", (long long)n_tok, (long long)c.max_tokens);
+        return -1;
+    }
+    const TrxLayer &L = m->layers[(size_t)layer];
+    TrxShape S{(int)c.n_expert, (int)c.n_used, (int)c.n_embd, (int)c.n_ff, (int)c.norm_topk};
+    TrxWork w = m->work;
+    if (out) {
+        w.out_logits = out->logits;
+        w.out_sel_id = out->sel_id;
+        w.out_sel_w = out->sel_w;
+        w.out_offsets = out->offsets;
+        w.out_place = out->place;
+    }
+    if ((w.out_sel_id == nullptr) != (w.out_sel_w == nullptr)) {
+        set_err("sel_id and sel_w outputs go together");
+        return -1;
+    }
+    const int T = (int)n_tok, E = S.E, R = T * S.k;
+    const int act_max = std::min(E, R);
+    if (m->prof && !prof_collect(m)) return -1;
+    // zone z's kernels run between events z and z + 1; an unused zone's two events coincide
+    auto mark = [&](int z) {
+        if (m->prof) cudaEventRecord(m->ev[z], st);
+    };
+    for (int z = 0; z < TRMOE_ZONES; z++) m->ev_used[z] = true;
+    m->ev_used[2] = c.down_type == TRX_Q4_K;
+    mark(0);
+    trx_k_router<<<(unsigned)(E + T), 256, (size_t)S.H * 4, st>>>(L, S, d_normed, T, w);
+    mark(1);
+    const int gu_items = act_max * (S.F / TRX_GU_ROWS);
+    const unsigned gu_grid = (unsigned)std::min(gu_items, 2 * m->sm_count);
+    const bool down_lc = c.down_type != TRX_Q4_K;
+    if (c.gate_type == TRX_Q4_K) {
+        if (down_lc) trx_k_gateup<TRX_Q4_K, true><<<gu_grid, 256, 0, st>>>(L, S, w);
+        else trx_k_gateup<TRX_Q4_K, false><<<gu_grid, 256, 0, st>>>(L, S, w);
+    } else {
+        if (down_lc) trx_k_gateup<TRX_Q8_0, true><<<gu_grid, 256, 0, st>>>(L, S, w);
+        else trx_k_gateup<TRX_Q8_0, false><<<gu_grid, 256, 0, st>>>(L, S, w);
+    }
+    mark(2);
+    if (!down_lc) {
+        const int warps = R * (S.F / 256);
+        trx_k_prep<<<(unsigned)((warps + 7) / 8), 256, 0, st>>>(S, nullptr, R, w);
+    }
+    mark(3);
+    const int dn_items = act_max * (S.H / TRX_DN_ROWS);
+    const unsigned dn_grid = (unsigned)std::min(dn_items, 2 * m->sm_count);
+    float *ffn = out ? out->ffn_out : nullptr;
+    if (c.down_type == TRX_Q4_K) trx_k_down<TRX_Q4_K><<<dn_grid, 256, 0, st>>>(L, S, w, d_x, T, ffn);
+    else if (c.down_type == TRX_Q8_0) trx_k_down<TRX_Q8_0><<<dn_grid, 256, 0, st>>>(L, S, w, d_x, T, ffn);
+    else trx_k_down<TRX_Q6_K><<<dn_grid, 256, 0, st>>>(L, S, w, d_x, T, ffn);
+    mark(4);
+    if (m->prof) m->prof_pending = true;
+    return ck(cudaGetLastError(), "launch") ? 0 : -1;
+}
+
+extern "C" int tr_gpu_moe_layer_dev(tr_gpu_moe *m, int64_t layer, const float *d_normed, int64_t n_tok,
+                                    float *d_x_inout, const tr_gpu_moe_outputs *out, void *stream) {
+    g_err.clear();
+    if (m == nullptr) {
+        set_err("no context");
+        return -1;
+    }
+    if (!ck(cudaSetDevice(m->device), "cudaSetDevice")) return -1;
+    cudaStream_t st = stream ? (cudaStream_t)stream : m->stream;
+    return launch_layer(m, layer, d_normed, n_tok, d_x_inout, out, st);
+}
+
+extern "C" int tr_gpu_moe_layer(tr_gpu_moe *m, int64_t layer, const float *normed, int64_t n_tok, float *x_inout,
+                                int64_t *sel_id_out, float *sel_w_out) {
+    g_err.clear();
+    if (m == nullptr || normed == nullptr || x_inout == nullptr) {
+        set_err("bad arguments to tr_gpu_moe_layer");
+        return -1;
+    }
+    if (n_tok < 1 || n_tok > m->cfg.max_tokens) {
+        set_err("bad token count %lld (max %lld)", (long long)n_tok, (long long)m->cfg.max_tokens);
+        return -1;
+    }
+    if (!ck(cudaSetDevice(m->device), "cudaSetDevice")) return -1;
+    const size_t xb = (size_t)(n_tok * m->cfg.n_embd) * 4;
+    const int64_t R = n_tok * m->cfg.n_used;
+    cudaStream_t st = m->stream;
+    tr_gpu_moe_outputs out{};
+    const bool sel = sel_id_out != nullptr || sel_w_out != nullptr;
+    if (sel) {
+        out.sel_id = m->d_sel_id;
+        out.sel_w = m->d_sel_w;
+    }
+    bool ok = ck(cudaMemcpyAsync(m->d_normed, normed, xb, cudaMemcpyHostToDevice, st), "copy normed") &&
+              ck(cudaMemcpyAsync(m->d_x, x_inout, xb, cudaMemcpyHostToDevice, st), "copy x") &&
+              launch_layer(m, layer, m->d_normed, n_tok, m->d_x, sel ? &out : nullptr, st) == 0 &&
+              ck(cudaMemcpyAsync(x_inout, m->d_x, xb, cudaMemcpyDeviceToHost, st), "copy x back");
+    if (ok && sel_id_out)
+        ok = ck(cudaMemcpyAsync(sel_id_out, m->d_sel_id, (size_t)R * 8, cudaMemcpyDeviceToHost, st), "copy sel_id");
+    if (ok && sel_w_out)
+        ok = ck(cudaMemcpyAsync(sel_w_out, m->d_sel_w, (size_t)R * 4, cudaMemcpyDeviceToHost, st), "copy sel_w");
+    if (ok) ok = stream_wait(st);
+    return ok ? 0 : -1;
+}
+
+// ---------------------------------------------------------------------------------------------
+// the kernel level
+
+namespace {
+
+struct KMat {
+    uint8_t *dev;
+    int64_t bytes;
+};
+
+struct KCtx {
+    std::mutex mu;
+    bool init = false;
+    int device = 0;
+    cudaStream_t st = nullptr;
+    std::unordered_map<std::string, KMat> mats;
+    uint8_t *buf = nullptr; // x, prepared x, y
+    int64_t buf_bytes = 0;
+    uint8_t *tmp = nullptr;
+    int64_t tmp_bytes = 0;
+};
+
+KCtx &kctx() {
+    static KCtx c;
+    return c;
+}
+
+bool kinit(KCtx &c) {
+    if (c.init) return true;
+    if (!ck(cudaGetDevice(&c.device), "cudaGetDevice") ||
+        !ck(cudaStreamCreateWithFlags(&c.st, cudaStreamNonBlocking), "cudaStreamCreate"))
+        return false;
+    c.init = true;
+    return true;
+}
+
+bool kreserve(uint8_t **p, int64_t *have, int64_t need) {
+    if (*have >= need) return true;
+    if (*p) cudaFree(*p);
+    *p = nullptr;
+    *have = 0;
+    if (!ck(cudaMalloc(p, (size_t)need), "cudaMalloc")) return false;
+    *have = need;
+    return true;
+}
+
+// the device copy of a host matrix, uploaded on first sight
+uint8_t *kmat(KCtx &c, const tr_mat &w) {
+    char key[96];
+    snprintf(key, sizeof key, "%p/%d/%lld/%lld", w.data, (int)w.type, (long long)w.rows, (long long)w.cols);
+    auto it = c.mats.find(key);
+    if (it != c.mats.end()) return it->second.dev;
+    const int64_t bytes = trx_row_bytes(w.type, w.cols) * w.rows;
+    uint8_t *d = nullptr;
+    if (!ck(cudaMalloc(&d, (size_t)align_up(bytes, 256)), "cudaMalloc(weight)")) return nullptr;
+    if (!kreserve(&c.tmp, &c.tmp_bytes, bytes) || !upload_matrix(w.type, w.rows, w.cols, w.data, d, c.tmp, c.st)) {
+        cudaFree(d);
+        return nullptr;
+    }
+    c.mats[key] = KMat{d, bytes};
+    return d;
+}
+
+bool ktype_ok(const tr_mat &w) {
+    switch (w.type) {
+    case TRX_F32:
+    case TRX_F16:
+    case TRX_BF16: return w.cols % 16 == 0;
+    case TRX_Q8_0:
+    case TRX_Q6_K:
+    case TRX_Q4_K: return w.cols % 256 == 0;
+    default: return false;
+    }
+}
+
+bool kgrouped(const tr_mat *w, const int64_t *offsets, int64_t n_groups, const float *x, float *y) {
+    if (n_groups <= 0 || offsets[n_groups] <= 0 || w[0].rows <= 0) return true;
+    const int type = w[0].type;
+    const int64_t rows = w[0].rows, cols = w[0].cols, n_in = offsets[n_groups];
+    for (int64_t g = 0; g < n_groups; g++)
+        if (w[g].type != type || w[g].rows != rows || w[g].cols != cols || !ktype_ok(w[g])) {
+            set_err("tr_matmul_grouped: group %lld has type %d %lldx%lld, not supported or not the first's", (long long)g,
+                    (int)w[g].type, (long long)w[g].rows, (long long)w[g].cols);
+            return false;
+        }
+    if (n_in > INT32_MAX / 2 || rows > INT32_MAX / 2) {
+        set_err("tr_matmul_grouped: too large");
+        return false;
+    }
+    KCtx &c = kctx();
+    std::lock_guard<std::mutex> lock(c.mu);
+    if (!kinit(c) || !ck(cudaSetDevice(c.device), "cudaSetDevice")) return false;
+    std::vector<const uint8_t *> ptrs((size_t)n_groups, nullptr);
+    for (int64_t g = 0; g < n_groups; g++)
+        if (offsets[g + 1] > offsets[g]) {
+            ptrs[(size_t)g] = kmat(c, w[g]);
+            if (ptrs[(size_t)g] == nullptr) return false;
+        }
+    // device buffer: x, prepared x (planes + bf + scale), y, group table, offsets
+    const int64_t xb = align_up(n_in * cols * 4, 256), pb = align_up(n_in * cols * 4, 256),
+                  bfb = align_up(n_in * (cols / 32) * 8, 256), scb = align_up(n_in * (cols / 256 + 1) * 8, 256),
+                  yb = align_up(n_in * rows * 4, 256), gb = align_up(n_groups * 8, 256),
+                  ob = align_up((n_groups + 1) * 4, 256);
+    if (!kreserve(&c.buf, &c.buf_bytes, xb + pb + bfb + scb + yb + gb + ob)) return false;
+    uint8_t *b = c.buf;
+    float *dx = (float *)b;
+    uint32_t *dq = (uint32_t *)(b + xb);
+    double *dbf = (double *)(b + xb + pb);
+    double *dsc = (double *)(b + xb + pb + bfb);
+    float *dy = (float *)(b + xb + pb + bfb + scb);
+    const uint8_t **dg = (const uint8_t **)(b + xb + pb + bfb + scb + yb);
+    int32_t *doff = (int32_t *)(b + xb + pb + bfb + scb + yb + gb);
+    std::vector<int32_t> off32((size_t)n_groups + 1);
+    for (int64_t g = 0; g <= n_groups; g++) off32[(size_t)g] = (int32_t)offsets[g];
+    bool ok = ck(cudaMemcpyAsync(dx, x, (size_t)(n_in * cols * 4), cudaMemcpyHostToDevice, c.st), "copy x") &&
+              ck(cudaMemcpyAsync(dg, ptrs.data(), (size_t)n_groups * 8, cudaMemcpyHostToDevice, c.st), "copy table") &&
+              ck(cudaMemcpyAsync(doff, off32.data(), (size_t)(n_groups + 1) * 4, cudaMemcpyHostToDevice, c.st),
+                 "copy offsets");
+    if (!ok) return false;
+    ok = trx_kapi_grouped(type, rows, cols, dg, doff, (int)n_groups, (int)n_in, dx, dq, dbf, dsc, dy, c.st) &&
+         ck(cudaGetLastError(), "grouped kernel") &&
+         ck(cudaMemcpyAsync(y, dy, (size_t)(n_in * rows * 4), cudaMemcpyDeviceToHost, c.st), "copy y") &&
+         stream_wait(c.st);
+    return ok;
+}
+
+void kfail(const char *fn) { fprintf(stderr, "trmoe: %s failed: %s\n", fn, g_err.c_str()); }
+
+} // namespace
+
+extern "C" void tr_matmul_grouped(tr_pool *pool, const tr_mat *w, const int64_t *offsets, int64_t n_groups,
+                                  const float *x, float *y) {
+    (void)pool;
+    g_err.clear();
+    if (!kgrouped(w, offsets, n_groups, x, y)) kfail("tr_matmul_grouped");
+}
+
+extern "C" void tr_matmul_grouped_s(tr_pool *pool, const tr_mat *w, const int64_t *offsets, int64_t n_groups,
+                                    const float *x, float *y, const void *s) {
+    (void)s;
+    tr_matmul_grouped(pool, w, offsets, n_groups, x, y);
+}
+
+extern "C" void tr_matmul(tr_pool *pool, const tr_mat *w, const float *x, int64_t n_tokens, float *y) {
+    const int64_t offsets[2] = {0, n_tokens};
+    tr_matmul_grouped(pool, w, offsets, 1, x, y);
+}
+
+extern "C" void tr_softmax(float *x, int64_t n) {
+    g_err.clear();
+    if (n <= 0) return;
+    KCtx &c = kctx();
+    std::lock_guard<std::mutex> lock(c.mu);
+    bool ok = kinit(c) && ck(cudaSetDevice(c.device), "cudaSetDevice") &&
+              kreserve(&c.buf, &c.buf_bytes, align_up(n * 4, 256));
+    if (ok) {
+        float *d = (float *)c.buf;
+        ok = ck(cudaMemcpyAsync(d, x, (size_t)n * 4, cudaMemcpyHostToDevice, c.st), "copy") &&
+             trx_kapi_softmax(d, n, c.st) && ck(cudaGetLastError(), "softmax kernel") &&
+             ck(cudaMemcpyAsync(x, d, (size_t)n * 4, cudaMemcpyDeviceToHost, c.st), "copy back") && stream_wait(c.st);
+    }
+    if (!ok) kfail("tr_softmax");
+}
+
+extern "C" void tr_swiglu(tr_pool *pool, float *x, const float *y, int64_t n) {
+    (void)pool;
+    g_err.clear();
+    if (n <= 0) return;
+    KCtx &c = kctx();
+    std::lock_guard<std::mutex> lock(c.mu);
+    bool ok = kinit(c) && ck(cudaSetDevice(c.device), "cudaSetDevice") &&
+              kreserve(&c.buf, &c.buf_bytes, 2 * align_up(n * 4, 256));
+    if (ok) {
+        float *dx = (float *)c.buf, *dy = (float *)(c.buf + align_up(n * 4, 256));
+        ok = ck(cudaMemcpyAsync(dx, x, (size_t)n * 4, cudaMemcpyHostToDevice, c.st), "copy x") &&
+             ck(cudaMemcpyAsync(dy, y, (size_t)n * 4, cudaMemcpyHostToDevice, c.st), "copy y") &&
+             trx_kapi_swiglu(dx, dy, n, c.st) && ck(cudaGetLastError(), "swiglu kernel") &&
+             ck(cudaMemcpyAsync(x, dx, (size_t)n * 4, cudaMemcpyDeviceToHost, c.st), "copy back") && stream_wait(c.st);
+    }
+    if (!ok) kfail("tr_swiglu");
+}
+
+extern "C" void trmoe_kernel_cache_clear(void) {
+    KCtx &c = kctx();
+    std::lock_guard<std::mutex> lock(c.mu);
+    for (auto &kv : c.mats) cudaFree(kv.second.dev);
+    c.mats.clear();
+}

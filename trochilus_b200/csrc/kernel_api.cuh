@@ -1,0 +1,180 @@
+// kernel_api.cuh: device side of the kernel-level entry points (tr_matmul_grouped, tr_softmax,
+// tr_swiglu), for any shape the reference's API takes with these types: a grouped GEMV where each
+// warp or half-warp owns a weight row and every input row of its group, plus element-wise kernels.
+// Numerics as the layer kernels (layouts.cuh): Trochilus's scalar definitions, bit for bit.
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+#include "common.cuh"
+#include "expf.cuh"
+#include "layouts.cuh"
+
+// one warp per 256-block of an input row: Q4_K's prepared rows
+__global__ void trx_kapi_prep_q4x(const float *__restrict__ x, int n_in, int cols, uint32_t *__restrict__ q,
+                                  double *__restrict__ bf, double *__restrict__ sc) {
+    const int nsb = cols / 256;
+    const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int p = gw / nsb, s = gw % nsb;
+    if (p >= n_in) return;
+    trx_prep_q4x_block(x + (int64_t)p * cols + 256 * s, q + (int64_t)p * cols + 256 * s,
+                       bf + (int64_t)p * (cols / 32) + 8 * s, sc + (int64_t)p * nsb + s, threadIdx.x & 31);
+}
+
+__global__ void trx_kapi_lc(const float *__restrict__ x, int64_t total, int cols, float *__restrict__ y) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t p = i / cols;
+        const int k = (int)(i % cols);
+        y[p * cols + trx_lc_pos(k)] = x[i];
+    }
+}
+
+// a Q4_K row of any number of blocks by one warp, 8 blocks a pass
+__device__ __forceinline__ float trx_q4k_row_any(const uint8_t *__restrict__ row, int nsb,
+                                                 const uint32_t *__restrict__ planes, const double *__restrict__ bf,
+                                                 const double *__restrict__ sc, int lane) {
+    double y = 0.0;
+    const int c = lane & 3;
+    for (int s0 = 0; s0 < nsb; s0 += 8) {
+        const int s = s0 + (lane >> 2);
+        const bool valid = s < nsb;
+        int64_t T = 0;
+        uint4 hdr = make_uint4(0, 0, 0, 0);
+        if (valid) {
+            TrxQ4X X;
+            trx_q4x_load(planes + 256 * s, c, X);
+            const uint8_t *blk = row + 144 * s;
+            hdr = __ldg(reinterpret_cast<const uint4 *>(blk));
+            const uint4 q0 = __ldg(reinterpret_cast<const uint4 *>(blk + 16 + 32 * c));
+            const uint4 q1 = __ldg(reinterpret_cast<const uint4 *>(blk + 32 + 32 * c));
+            T = trx_q4k_chunk_T(hdr, q0, q1, c, X);
+        }
+        T += trx_shfl_xor64(T, 1);
+        T += trx_shfl_xor64(T, 2);
+        double v = 0.0;
+        if (valid && c == 0) v = trx_q4k_finish(hdr, T, bf + 8 * s, sc[s]);
+        for (int i = 0; i < 8 && s0 + i < nsb; i++) y = __dadd_rn(y, trx_shfl_d(v, 4 * i));
+    }
+    return __double2float_rn(y);
+}
+
+template <int TYPE>
+__global__ void __launch_bounds__(256) trx_kapi_grouped_k(const uint8_t *const *__restrict__ mats,
+                                                          const int32_t *__restrict__ offsets, int rows, int cols,
+                                                          const float *__restrict__ x, const uint32_t *__restrict__ xq,
+                                                          const double *__restrict__ bf, const double *__restrict__ sc,
+                                                          float *__restrict__ y) {
+    const int g = blockIdx.y;
+    const int p0 = offsets[g], p1 = offsets[g + 1];
+    if (p1 <= p0) return;
+    const uint8_t *W = mats[g];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int64_t rb = trx_row_bytes(TYPE, cols);
+    if (TYPE == TRX_Q4_K) { // one row per warp, 8 rows a block
+        const int r = blockIdx.x * 8 + warp;
+        if (r >= rows) return;
+        const int nsb = cols / 256;
+        for (int p = p0; p < p1; p++) {
+            const float v = trx_q4k_row_any(W + (int64_t)r * rb, nsb, xq + (int64_t)p * cols, bf + (int64_t)p * (cols / 32),
+                                            sc + (int64_t)p * nsb, lane);
+            if (lane == 0) y[(int64_t)p * rows + r] = v;
+        }
+    } else { // a half-warp per row, 16 rows a block
+        const int r0 = blockIdx.x * 16 + 2 * warp + (lane >> 4);
+        const bool valid = r0 < rows;
+        const int r = valid ? r0 : rows - 1; // every lane takes part in the shuffles
+        for (int p = p0; p < p1; p++) {
+            float v;
+            if (TYPE == TRX_Q8_0)
+                v = trx_q8l_dot(W + (int64_t)r * rb, reinterpret_cast<const float *>(xq) + (int64_t)p * cols, cols / 256,
+                                lane & 15);
+            else if (TYPE == TRX_Q6_K)
+                v = trx_q6l_dot(W + (int64_t)r * (cols / 256) * 208,
+                                W + (int64_t)rows * (cols / 256) * 208 + (int64_t)r * (cols / 256) * 2,
+                                reinterpret_cast<const float *>(xq) + (int64_t)p * cols, cols / 256, lane & 15);
+            else
+                v = trx_plain_dot<TYPE>(W + (int64_t)r * rb, x + (int64_t)p * cols, cols, lane & 15);
+            if (valid && (lane & 15) == 0) y[(int64_t)p * rows + r] = v;
+        }
+    }
+}
+
+inline bool trx_kapi_grouped(int type, int64_t rows, int64_t cols, const uint8_t *const *dg, const int32_t *doff,
+                             int n_groups, int n_in, const float *dx, uint32_t *dq, double *dbf, double *dsc, float *dy,
+                             cudaStream_t st) {
+    if (type == TRX_Q4_K) {
+        const int64_t warps = (int64_t)n_in * (cols / 256);
+        trx_kapi_prep_q4x<<<(unsigned)((warps + 7) / 8), 256, 0, st>>>(dx, n_in, (int)cols, dq, dbf, dsc);
+        dim3 grid((unsigned)((rows + 7) / 8), (unsigned)n_groups);
+        trx_kapi_grouped_k<TRX_Q4_K><<<grid, 256, 0, st>>>(dg, doff, (int)rows, (int)cols, dx, dq, dbf, dsc, dy);
+        return true;
+    }
+    dim3 grid((unsigned)((rows + 15) / 16), (unsigned)n_groups);
+    if (type == TRX_Q8_0 || type == TRX_Q6_K) {
+        const int64_t total = (int64_t)n_in * cols;
+        trx_kapi_lc<<<(unsigned)std::min<int64_t>((total + 255) / 256, 4096), 256, 0, st>>>(dx, total, (int)cols,
+                                                                                           reinterpret_cast<float *>(dq));
+        if (type == TRX_Q8_0)
+            trx_kapi_grouped_k<TRX_Q8_0><<<grid, 256, 0, st>>>(dg, doff, (int)rows, (int)cols, dx, dq, dbf, dsc, dy);
+        else
+            trx_kapi_grouped_k<TRX_Q6_K><<<grid, 256, 0, st>>>(dg, doff, (int)rows, (int)cols, dx, dq, dbf, dsc, dy);
+        return true;
+    }
+    if (type == TRX_F32)
+        trx_kapi_grouped_k<TRX_F32><<<grid, 256, 0, st>>>(dg, doff, (int)rows, (int)cols, dx, dq, dbf, dsc, dy);
+    else if (type == TRX_BF16)
+        trx_kapi_grouped_k<TRX_BF16><<<grid, 256, 0, st>>>(dg, doff, (int)rows, (int)cols, dx, dq, dbf, dsc, dy);
+    else
+        trx_kapi_grouped_k<TRX_F16><<<grid, 256, 0, st>>>(dg, doff, (int)rows, (int)cols, dx, dq, dbf, dsc, dy);
+    return true;
+}
+
+// tr_softmax over n values, one block: the max as the reference's serial scan from x[0], the exp of each
+// difference, the 16-lane sum (lane l adds elements l, l + 16, ... in order), the divisions
+__global__ void __launch_bounds__(256) trx_kapi_softmax_k(float *__restrict__ x, int64_t n) {
+    __shared__ float red[8];
+    __shared__ float s_m, s_sum;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    float m = -__int_as_float(0x7f800000);
+    for (int64_t i = tid; i < n; i += blockDim.x)
+        if (x[i] == x[i]) m = fmaxf(m, x[i]);
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (lane == 0) red[warp] = m;
+    __syncthreads();
+    if (tid == 0) {
+        float mm = red[0];
+        for (int i = 1; i < 8; i++) mm = fmaxf(mm, red[i]);
+        s_m = x[0] != x[0] ? x[0] : mm;
+    }
+    __syncthreads();
+    const float mx = s_m;
+    for (int64_t i = tid; i < n; i += blockDim.x) x[i] = trx_expf(__fsub_rn(x[i], mx));
+    __syncthreads();
+    if (warp == 0) {
+        float acc = 0.0f;
+        if (lane < 16)
+            for (int64_t i = lane; i < n; i += 16) acc = __fadd_rn(acc, x[i]);
+        acc = trx_lane_tree16(acc);
+        if (lane == 0) s_sum = acc;
+    }
+    __syncthreads();
+    const float sum = s_sum;
+    for (int64_t i = tid; i < n; i += blockDim.x) x[i] = __fdiv_rn(x[i], sum);
+}
+
+inline bool trx_kapi_softmax(float *d, int64_t n, cudaStream_t st) {
+    trx_kapi_softmax_k<<<1, 256, 0, st>>>(d, n);
+    return true;
+}
+
+__global__ void trx_kapi_swiglu_k(float *__restrict__ x, const float *__restrict__ y, int64_t n) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const float v = x[i];
+        const float e = trx_expf(-v);
+        x[i] = __fmul_rn(__fdiv_rn(v, __fadd_rn(1.0f, e)), y[i]);
+    }
+}
+
+inline bool trx_kapi_swiglu(float *dx, const float *dy, int64_t n, cudaStream_t st) {
+    trx_kapi_swiglu_k<<<(unsigned)std::min<int64_t>((n + 255) / 256, 8192), 256, 0, st>>>(dx, dy, n);
+    return true;
+}

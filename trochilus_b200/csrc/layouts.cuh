@@ -1,0 +1,320 @@
+// layouts.cuh: the weight layouts in HBM, the upload-time repack kernels, and the per-warp dot
+// products of one weight row against one input row under Trochilus's numerics.
+//
+// A GGUF row is read from the host once (tr_gpu_moe_create, or the first kernel-level call that
+// names it) and kept in HBM in one of these layouts. Each layout has exactly the GGUF row's bytes;
+// only their order changes, so the HBM traffic per weight is the format's own.
+//
+//  Q4_K  kept as GGUF blocks (144 B = 16 B header + 128 B quants): 16-byte aligned already.
+//        Dot: Q4_K's exact-integer definition (Trochilus src/kernels/kernels.h:186-205,
+//        src/kernels/kernels.c:196-253). The input row is prepared once (trx_prep_q4x below: per
+//        256-block shift, X = nearest-even(x 2^sh), its four bytes as planes); a thread takes one
+//        32-byte quant chunk (64 weights of sub-blocks 2c and 2c+1) and forms sum q X exactly with
+//        dp4a over the byte planes, the 4 threads of a block add their int64 T exactly (any order),
+//        and one thread finishes v = (d T - dmin M) 2^-sh in f64; the row sums v in increasing
+//        block order from +0, then rounds to float once.
+//  Q8L   from Q8_0 (34 B per 32 weights): per 256 weights (8 blocks), 16 B of the 8 f16 scales, then
+//        256 B where byte 16 l + m is q[l + 16 m] (lane l's m-th weight of the chunk). A 16-byte
+//        load of a thread of the 16-lane contract is then 16 consecutive terms of its own lane.
+//  Q6L   from Q6_K (210 B per 256 weights): per row, for each block s: 128 B low nibbles
+//        (lane l: 8 bytes, weight m in nibble m & 1 of byte m >> 1), then 64 B high bit-pairs
+//        (lane l: 4 bytes, weight m in bits 2 (m & 3) of byte m >> 2), then the 16 int8 scales;
+//        the f16 d of every (row, block) after all the rows of the matrix.
+//  F32, BF16 (router): as in the file.
+// The lane-contract dots (Q8_0, Q6_K, F32, BF16) take their input row in the "LC order": inside
+// every 256 floats, x[l + 16 m] sits at 64 (m >> 2) + 4 l + (m & 3), so that a thread's four
+// 16-byte loads hold its lane's 16 inputs and a half-warp's loads are one contiguous 256 B.
+#pragma once
+#include <cstdint>
+#include "common.cuh"
+
+// ---- sizes ----
+__host__ __device__ inline int64_t trx_row_bytes(int type, int64_t n) {
+    switch (type) {
+    case TRX_F32: return n * 4;
+    case TRX_F16:
+    case TRX_BF16: return n * 2;
+    case TRX_Q8_0: return n % 32 ? 0 : n / 32 * 34;
+    case TRX_Q4_K: return n % 256 ? 0 : n / 256 * 144;
+    case TRX_Q6_K: return n % 256 ? 0 : n / 256 * 210;
+    default: return 0;
+    }
+}
+
+// LC position of natural index k (inside its 256-chunk)
+__host__ __device__ inline int trx_lc_pos(int k) {
+    const int i = k >> 8, r = k & 255, l = r & 15, m = r >> 4;
+    return (i << 8) + ((m >> 2) << 6) + (l << 2) + (m & 3);
+}
+
+// ---- repack kernels (one thread block per row) ----
+
+// Q8_0 rows (GGUF) -> Q8L rows; n % 256 == 0
+__global__ void trx_repack_q8l(const uint8_t *__restrict__ src, uint8_t *__restrict__ dst, int64_t rows, int64_t n) {
+    const int64_t r = blockIdx.x;
+    if (r >= rows) return;
+    const int64_t rb = n / 32 * 34;
+    const uint8_t *s = src + r * rb;
+    uint8_t *d = dst + r * rb;
+    for (int64_t k = threadIdx.x; k < n; k += blockDim.x) {
+        const int64_t i = k >> 8, rr = k & 255, l = rr & 15, m = rr >> 4, b = k >> 5;
+        d[i * 272 + 16 + 16 * l + m] = s[b * 34 + 2 + (k & 31)];
+        if ((k & 31) == 0) { // the block's scale
+            d[i * 272 + 2 * (b & 7)] = s[b * 34];
+            d[i * 272 + 2 * (b & 7) + 1] = s[b * 34 + 1];
+        }
+    }
+}
+
+// Q6_K rows (GGUF) -> Q6L matrix (rows consecutive, then the d's); n % 256 == 0
+__global__ void trx_repack_q6l(const uint8_t *__restrict__ src, uint8_t *__restrict__ dst, int64_t rows, int64_t n) {
+    const int64_t r = blockIdx.x;
+    if (r >= rows) return;
+    const int64_t nsb = n / 256;
+    const uint8_t *srow = src + r * nsb * 210;
+    uint8_t *drow = dst + r * nsb * 208;
+    uint8_t *dd = dst + rows * nsb * 208 + r * nsb * 2;
+    for (int64_t s = 0; s < nsb; s++) {
+        const uint8_t *blk = srow + s * 210;
+        // lane l, pair b: low nibbles of weights m = 2b, 2b + 1 (element l + 16 m)
+        for (int t = threadIdx.x; t < 128; t += blockDim.x) {
+            const int l = t >> 3, b = t & 7;
+            uint8_t v = 0;
+            for (int h = 0; h < 2; h++) {
+                const int i = l + 16 * (2 * b + h); // element in the block
+                const int hh = i >> 7, c = (i >> 5) & 3, ll = i & 31;
+                unsigned lo = blk[64 * hh + 32 * (c & 1) + ll];
+                lo = (c & 2) ? lo >> 4 : lo & 15u;
+                v |= (uint8_t)(lo << (4 * h));
+            }
+            drow[s * 128 + t] = v;
+        }
+        for (int t = threadIdx.x; t < 64; t += blockDim.x) {
+            const int l = t >> 2, b = t & 3;
+            uint8_t v = 0;
+            for (int u = 0; u < 4; u++) {
+                const int i = l + 16 * (4 * b + u);
+                const int hh = i >> 7, c = (i >> 5) & 3, ll = i & 31;
+                const unsigned hi = (blk[128 + 32 * hh + ll] >> (2 * c)) & 3u;
+                v |= (uint8_t)(hi << (2 * u));
+            }
+            drow[nsb * 128 + s * 64 + t] = v;
+        }
+        for (int t = threadIdx.x; t < 16; t += blockDim.x) drow[nsb * 192 + s * 16 + t] = blk[192 + t];
+        if (threadIdx.x == 0) {
+            dd[2 * s] = blk[208];
+            dd[2 * s + 1] = blk[209];
+        }
+    }
+}
+
+// ---- input-row preparation ----
+
+// Q4_K's prepared input row of n floats (n % 256 == 0), per 256-block s:
+//   planes: word ((s*4 + c)*4 + p)*16 + g = byte p of X at elements 256 s + 64 c + 4 g .. +3
+//   bf[8 s + j] = sum of X over sub-block j (exact, as a double); scale[s] = 2^-sh, NaN for a block
+//   holding a NaN or an infinity (its X then 0). Restated from Trochilus k_q4x_prep
+//   (src/kernels/kernels.c:200-239) and tr_q4x_shift (src/kernels/kernels_internal.h:150-166).
+// One warp per 256-block; lane L takes elements 8 L .. 8 L + 7.
+__device__ __forceinline__ void trx_prep_q4x_block(const float *__restrict__ x, uint32_t *__restrict__ planes,
+                                                   double *__restrict__ bf, double *__restrict__ scale, int lane) {
+    float v[8];
+    const float4 a = *reinterpret_cast<const float4 *>(x + 8 * lane);
+    const float4 b = *reinterpret_cast<const float4 *>(x + 8 * lane + 4);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+    float m = 0.0f;
+    int bad = 0;
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        const float av = fabsf(v[i]);
+        if (!(av <= 3.40282347e38f)) bad = 1;
+        else m = fmaxf(m, av);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        bad |= __shfl_xor_sync(0xffffffffu, bad, o);
+    }
+    int sh = 0;
+    if (!bad && m != 0.0f) {
+        const uint32_t mb = __float_as_uint(m);
+        const int field = (int)((mb >> 23) & 255u);
+        const int e = field ? field - 126 : (32 - __clz((int)(mb & 0x7fffffu))) - 149;
+        sh = 31 - e;
+        // m 2^sh is exact in double (a power of two times a float)
+        if (__dmul_rn((double)m, ldexp(1.0, sh)) > 2085998640.0) sh--;
+    }
+    const double f = bad ? 0.0 : ldexp(1.0, sh);
+    int32_t X[8];
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        const double t = __dmul_rn((double)v[i], f); // exact
+        X[i] = bad ? 0 : (int32_t)__double2ll_rn(t);   // nearest, ties to even
+    }
+    // sub-block sums: sub-block j holds lanes 4 j .. 4 j + 3
+    int64_t s = 0;
+#pragma unroll
+    for (int i = 0; i < 8; i++) s += X[i];
+    s += trx_shfl_xor64(s, 1);
+    s += trx_shfl_xor64(s, 2);
+    if ((lane & 3) == 0) bf[lane >> 2] = (double)s;
+    if (lane == 0) scale[0] = bad ? __longlong_as_double(0x7ff8000000000000ll) : ldexp(1.0, -sh);
+    // planes: chunk c = lane / 8, groups g = 2 (lane % 8), 2 (lane % 8) + 1
+    const int c = lane >> 3, g = 2 * (lane & 7);
+#pragma unroll
+    for (int p = 0; p < 4; p++) {
+        uint32_t w0 = 0, w1 = 0;
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            w0 |= (((uint32_t)X[i] >> (8 * p)) & 255u) << (8 * i);
+            w1 |= (((uint32_t)X[4 + i] >> (8 * p)) & 255u) << (8 * i);
+        }
+        uint32_t *dst = planes + ((c * 4 + p) * 16 + g);
+        dst[0] = w0;
+        dst[1] = w1;
+    }
+}
+
+// ---- dot products ----
+
+// Q4_K: the 4 * G lanes of a row group hold G blocks (lane: block s = lane/4 % G, chunk c = lane % 4)
+// X registers: the thread's 64 inputs as 4 byte planes x 16 words
+struct TrxQ4X {
+    uint32_t w[4][16];
+};
+
+__device__ __forceinline__ void trx_q4x_load(const uint32_t *__restrict__ planes_blk, int c, TrxQ4X &X) {
+    const uint4 *src = reinterpret_cast<const uint4 *>(planes_blk + c * 64);
+#pragma unroll
+    for (int p = 0; p < 4; p++)
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            const uint4 v = src[p * 4 + q];
+            X.w[p][4 * q + 0] = v.x;
+            X.w[p][4 * q + 1] = v.y;
+            X.w[p][4 * q + 2] = v.z;
+            X.w[p][4 * q + 3] = v.w;
+        }
+}
+
+// One thread's part of T for its 32-byte chunk c of a block whose header is hdr and quants q0, q1.
+__device__ __forceinline__ int64_t trx_q4k_chunk_T(uint4 hdr, uint4 q0, uint4 q1, int c, const TrxQ4X &X) {
+    const uint32_t words[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+    uint32_t alo[3] = {0, 0, 0}, ahi[3] = {0, 0, 0};
+    int slo = 0, shi = 0;
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        const uint32_t lo = words[i] & 0x0f0f0f0fu, hi = (words[i] >> 4) & 0x0f0f0f0fu;
+#pragma unroll
+        for (int p = 0; p < 3; p++) {
+            alo[p] = __dp4a(lo, X.w[p][i], alo[p]);
+            ahi[p] = __dp4a(hi, X.w[p][8 + i], ahi[p]);
+        }
+        slo = __dp4a((int)lo, (int)X.w[3][i], slo);
+        shi = __dp4a((int)hi, (int)X.w[3][8 + i], shi);
+    }
+    // 6-bit scales of sub-blocks 2c and 2c+1 from the 12 packed bytes (header bytes 4..15)
+    const uint32_t sw[3] = {hdr.y, hdr.z, hdr.w};
+    auto sbyte = [&](int i) -> int { return (int)((sw[i >> 2] >> (8 * (i & 3))) & 255u); };
+    int sc_lo, sc_hi;
+    {
+        const int j0 = 2 * c, j1 = 2 * c + 1;
+        sc_lo = j0 < 4 ? (sbyte(j0) & 63) : ((sbyte(j0 + 4) & 15) | ((sbyte(j0 - 4) >> 6) << 4));
+        sc_hi = j1 < 4 ? (sbyte(j1) & 63) : ((sbyte(j1 + 4) & 15) | ((sbyte(j1 - 4) >> 6) << 4));
+    }
+    const int64_t b0 = (int64_t)sc_lo * alo[0] + (int64_t)sc_hi * ahi[0];
+    const int64_t b1 = (int64_t)sc_lo * alo[1] + (int64_t)sc_hi * ahi[1];
+    const int64_t b2 = (int64_t)sc_lo * alo[2] + (int64_t)sc_hi * ahi[2];
+    const int64_t b3 = (int64_t)sc_lo * slo + (int64_t)sc_hi * shi;
+    return b0 + (b1 << 8) + (b2 << 16) + b3 * 16777216ll;
+}
+
+// M of a block: sum_j m_j bf_j (exact: |bf| < 2^37, m < 64), then v = (d T - dmin M) scale in f64
+__device__ __forceinline__ double trx_q4k_finish(uint4 hdr, int64_t T, const double *__restrict__ bf, double scale) {
+    const uint32_t sw[3] = {hdr.y, hdr.z, hdr.w};
+    auto sbyte = [&](int i) -> int { return (int)((sw[i >> 2] >> (8 * (i & 3))) & 255u); };
+    int64_t M = 0;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        const int mj = j < 4 ? (sbyte(j + 4) & 63) : ((sbyte(j + 4) >> 4) | ((sbyte(j) >> 6) << 4));
+        M += (int64_t)mj * (int64_t)bf[j];
+    }
+    const double d = (double)trx_half((uint16_t)(hdr.x & 0xffffu));
+    const double dmin = (double)trx_half((uint16_t)(hdr.x >> 16));
+    const double val = __dsub_rn(__dmul_rn(d, (double)T), __dmul_rn(dmin, (double)M));
+    return __dmul_rn(val, scale);
+}
+
+// Q8L lane-contract dot of one row (n = 256 * nch) against an LC-ordered input row; thread l of the
+// half-warp. Returns the tree sum (same in all 16 threads).
+__device__ __forceinline__ float trx_q8l_dot(const uint8_t *__restrict__ row, const float *__restrict__ xlc, int nch,
+                                             int l) {
+    float acc = 0.0f;
+    for (int i = 0; i < nch; i++) {
+        const uint4 sc = __ldg(reinterpret_cast<const uint4 *>(row + 272 * i));
+        const uint4 q = __ldg(reinterpret_cast<const uint4 *>(row + 272 * i + 16 + 16 * l));
+        const float *xs = xlc + 256 * i + 4 * l;
+        const float4 x0 = *reinterpret_cast<const float4 *>(xs);
+        const float4 x1 = *reinterpret_cast<const float4 *>(xs + 64);
+        const float4 x2 = *reinterpret_cast<const float4 *>(xs + 128);
+        const float4 x3 = *reinterpret_cast<const float4 *>(xs + 192);
+        const float xv[16] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w,
+                              x2.x, x2.y, x2.z, x2.w, x3.x, x3.y, x3.z, x3.w};
+        const uint32_t qw[4] = {q.x ^ 0x80808080u, q.y ^ 0x80808080u, q.z ^ 0x80808080u, q.w ^ 0x80808080u};
+        const uint32_t sw[4] = {sc.x, sc.y, sc.z, sc.w};
+#pragma unroll
+        for (int m = 0; m < 16; m++) {
+            const float d = trx_half((uint16_t)(sw[m >> 2] >> (16 * ((m >> 1) & 1))));
+            const float w = __fmul_rn(d, trx_s8_to_f32(qw[m >> 2], m & 3));
+            acc = __fadd_rn(acc, __fmul_rn(w, xv[m]));
+        }
+    }
+    return trx_lane_tree16(acc);
+}
+
+// Q6L lane-contract dot (n = 256 * nsb); dptr: this row's nsb f16 d values
+__device__ __forceinline__ float trx_q6l_dot(const uint8_t *__restrict__ row, const uint8_t *__restrict__ dptr,
+                                             const float *__restrict__ xlc, int nsb, int l) {
+    float acc = 0.0f;
+    for (int s = 0; s < nsb; s++) {
+        const uint2 ql = __ldg(reinterpret_cast<const uint2 *>(row + 128 * s + 8 * l));
+        const uint32_t qh = __ldg(reinterpret_cast<const uint32_t *>(row + 128 * nsb + 64 * s + 4 * l));
+        const uint4 scv = __ldg(reinterpret_cast<const uint4 *>(row + 192 * nsb + 16 * s));
+        const float d = trx_half(__ldg(reinterpret_cast<const uint16_t *>(dptr) + s));
+        const float *xs = xlc + 256 * s + 4 * l;
+        const float4 x0 = *reinterpret_cast<const float4 *>(xs);
+        const float4 x1 = *reinterpret_cast<const float4 *>(xs + 64);
+        const float4 x2 = *reinterpret_cast<const float4 *>(xs + 128);
+        const float4 x3 = *reinterpret_cast<const float4 *>(xs + 192);
+        const float xv[16] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w,
+                              x2.x, x2.y, x2.z, x2.w, x3.x, x3.y, x3.z, x3.w};
+        const uint32_t scw[4] = {scv.x, scv.y, scv.z, scv.w};
+        const uint32_t qlw[2] = {ql.x, ql.y};
+#pragma unroll
+        for (int m = 0; m < 16; m++) {
+            const int sc = (int)(int8_t)(uint8_t)(scw[m >> 2] >> (8 * (m & 3)));
+            const float scale = __fmul_rn(d, (float)sc);
+            const uint32_t lo = (qlw[m >> 3] >> (4 * (m & 7))) & 15u;
+            const uint32_t hi = (qh >> (2 * m)) & 3u;
+            const int q = (int)(lo | (hi << 4)) - 32;
+            const float w = __fmul_rn(scale, (float)q);
+            acc = __fadd_rn(acc, __fmul_rn(w, xv[m]));
+        }
+    }
+    return trx_lane_tree16(acc);
+}
+
+// F32 / F16 / BF16 row, natural-order input, thread l of the half-warp (n % 16 == 0)
+template <int TYPE>
+__device__ __forceinline__ float trx_plain_dot(const uint8_t *__restrict__ row, const float *__restrict__ x, int n,
+                                               int l) {
+    float acc = 0.0f;
+    for (int k = l; k < n; k += 16) {
+        float w;
+        if (TYPE == TRX_F32) w = __ldg(reinterpret_cast<const float *>(row) + k);
+        else if (TYPE == TRX_F16) w = trx_half(__ldg(reinterpret_cast<const uint16_t *>(row) + k));
+        else w = trx_bf16(__ldg(reinterpret_cast<const uint16_t *>(row) + k));
+        acc = __fadd_rn(acc, __fmul_rn(w, x[k]));
+    }
+    return trx_lane_tree16(acc);
+}

@@ -1,0 +1,224 @@
+"""Python mirror of libtrmoe.so's C ABI (include/trmoe.h), through ctypes.
+
+The C library is the product; this module only binds it, the way a Python host of Trochilus's
+kernels would. It raises when the library is missing: there is no fallback of any kind.
+
+  GpuMoe          the layer hook (tr_gpu_moe_*): Trochilus's forward_layer MoE block
+                  (src/models/olmoe.c:1845-1933) on the GPU, weights resident in HBM
+  matmul_grouped  tr_matmul_grouped (src/kernels/kernels.h:244-245) on host arrays
+  matmul, softmax, swiglu   tr_matmul, tr_softmax, tr_swiglu
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libtrmoe.so")
+
+F32, F16, Q8_0, Q4_K, Q6_K, BF16 = 0, 1, 8, 12, 14, 30
+
+# every function include/trmoe.h declares
+EXPORTS = ["tr_gpu_moe_create", "tr_gpu_moe_free", "tr_gpu_moe_bytes", "tr_gpu_moe_set_layer", "tr_gpu_moe_layer",
+           "tr_gpu_moe_layer_dev", "tr_gpu_moe_launches", "tr_gpu_moe_profile", "tr_gpu_moe_profile_read", "trmoe_last_error", "tr_matmul", "tr_matmul_grouped",
+           "tr_matmul_grouped_s", "tr_softmax", "tr_swiglu", "trmoe_kernel_cache_clear"]
+
+
+class Config(C.Structure):
+    _fields_ = [("n_layers", C.c_int64), ("n_expert", C.c_int64), ("n_used", C.c_int64), ("n_embd", C.c_int64),
+                ("n_ff", C.c_int64), ("norm_topk", C.c_int32), ("router_type", C.c_int32),
+                ("gate_type", C.c_int32), ("down_type", C.c_int32), ("max_tokens", C.c_int64)]
+
+
+class Outputs(C.Structure):
+    _fields_ = [("logits", C.c_void_p), ("sel_id", C.c_void_p), ("sel_w", C.c_void_p), ("offsets", C.c_void_p),
+                ("place", C.c_void_p), ("ffn_out", C.c_void_p)]
+
+
+class TrMat(C.Structure):
+    _fields_ = [("type", C.c_int32), ("rows", C.c_int64), ("cols", C.c_int64), ("data", C.c_void_p)]
+
+
+_lib = None
+
+
+def lib():
+    """The loaded libtrmoe.so (built in-tree by trochilus_b200.build); raises if it is missing."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise RuntimeError(f"{LIB_PATH} is missing: build it with `python -m trochilus_b200.build`")
+    L = C.CDLL(LIB_PATH)
+    L.tr_gpu_moe_create.restype = C.c_void_p
+    L.tr_gpu_moe_create.argtypes = [C.POINTER(Config), C.c_int, C.c_char_p, C.c_size_t]
+    L.tr_gpu_moe_free.argtypes = [C.c_void_p]
+    L.tr_gpu_moe_bytes.restype = C.c_uint64
+    L.tr_gpu_moe_bytes.argtypes = [C.POINTER(Config)]
+    L.tr_gpu_moe_set_layer.argtypes = [C.c_void_p, C.c_int64, C.c_void_p, C.c_void_p, C.POINTER(C.c_void_p),
+                                       C.POINTER(C.c_void_p), C.POINTER(C.c_void_p), C.c_char_p, C.c_size_t]
+    L.tr_gpu_moe_layer.argtypes = [C.c_void_p, C.c_int64, C.c_void_p, C.c_int64, C.c_void_p, C.c_void_p, C.c_void_p]
+    L.tr_gpu_moe_layer_dev.argtypes = [C.c_void_p, C.c_int64, C.c_void_p, C.c_int64, C.c_void_p,
+                                       C.POINTER(Outputs), C.c_void_p]
+    L.tr_gpu_moe_launches.argtypes = [C.c_void_p, C.c_int64]
+    L.tr_gpu_moe_profile.argtypes = [C.c_void_p, C.c_int]
+    L.tr_gpu_moe_profile_read.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int]
+    L.trmoe_last_error.restype = C.c_char_p
+    L.tr_matmul.argtypes = [C.c_void_p, C.POINTER(TrMat), C.c_void_p, C.c_int64, C.c_void_p]
+    L.tr_matmul_grouped.argtypes = [C.c_void_p, C.POINTER(TrMat), C.c_void_p, C.c_int64, C.c_void_p, C.c_void_p]
+    L.tr_matmul_grouped_s.argtypes = [C.c_void_p, C.POINTER(TrMat), C.c_void_p, C.c_int64, C.c_void_p, C.c_void_p,
+                                      C.c_void_p]
+    L.tr_softmax.argtypes = [C.c_void_p, C.c_int64]
+    L.tr_swiglu.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64]
+    _lib = L
+    return L
+
+
+def last_error() -> str:
+    return lib().trmoe_last_error().decode()
+
+
+def _p(a):
+    return None if a is None else a.ctypes.data_as(C.c_void_p)
+
+
+class GpuMoe:
+    """A tr_gpu_moe context: n_layers MoE layers resident on one GPU."""
+
+    def __init__(self, n_layers, n_expert, n_used, n_embd, n_ff, router_type, gate_type, down_type, max_tokens,
+                 norm_topk=0, device=0):
+        L = lib()
+        self.cfg = Config(n_layers, n_expert, n_used, n_embd, n_ff, norm_topk, router_type, gate_type, down_type,
+                          max_tokens)
+        err = C.create_string_buffer(512)
+        self.h = L.tr_gpu_moe_create(C.byref(self.cfg), device, err, 512)
+        if not self.h:
+            raise RuntimeError(f"tr_gpu_moe_create: {err.value.decode()}")
+        self._keep = {}
+
+    @staticmethod
+    def bytes_needed(**kw) -> int:
+        cfg = Config(kw["n_layers"], kw["n_expert"], kw["n_used"], kw["n_embd"], kw["n_ff"], kw.get("norm_topk", 0),
+                     kw["router_type"], kw["gate_type"], kw["down_type"], kw["max_tokens"])
+        return int(lib().tr_gpu_moe_bytes(C.byref(cfg)))
+
+    def set_layer(self, layer: int, lay: dict, bias: np.ndarray | None = None):
+        E = self.cfg.n_expert
+        arr = {n: (C.c_void_p * E)(*[m.ctypes.data for m in lay[n]]) for n in ("gate", "up", "down")}
+        b = None if bias is None else np.ascontiguousarray(bias, dtype=np.float32)
+        err = C.create_string_buffer(512)
+        rc = lib().tr_gpu_moe_set_layer(self.h, layer, lay["router"].ctypes.data, _p(b),
+                                        C.cast(arr["gate"], C.POINTER(C.c_void_p)),
+                                        C.cast(arr["up"], C.POINTER(C.c_void_p)),
+                                        C.cast(arr["down"], C.POINTER(C.c_void_p)), err, 512)
+        if rc != 0:
+            raise RuntimeError(f"tr_gpu_moe_set_layer: {err.value.decode()}")
+
+    def layer(self, layer: int, normed: np.ndarray, x: np.ndarray, want_sel: bool = True):
+        """Host arrays: x is updated in place; returns (sel_id, sel_w) or None."""
+        normed = np.ascontiguousarray(normed, dtype=np.float32)
+        assert x.dtype == np.float32 and x.flags.c_contiguous
+        T = normed.shape[0]
+        sid = np.zeros((T, self.cfg.n_used), np.int64) if want_sel else None
+        sw = np.zeros((T, self.cfg.n_used), np.float32) if want_sel else None
+        rc = lib().tr_gpu_moe_layer(self.h, layer, _p(normed), T, _p(x), _p(sid), _p(sw))
+        if rc != 0:
+            raise RuntimeError(f"tr_gpu_moe_layer: {last_error()}")
+        return (sid, sw) if want_sel else None
+
+    def layer_ptrs(self, layer: int, normed_ptr: int, n_tok: int, x_ptr: int, host: bool):
+        """Raw-pointer form of layer() for pinned host buffers (host=True) or device buffers (host=False, on the
+        context's stream, not waited for)."""
+        if host:
+            rc = lib().tr_gpu_moe_layer(self.h, layer, normed_ptr, n_tok, x_ptr, None, None)
+        else:
+            rc = lib().tr_gpu_moe_layer_dev(self.h, layer, normed_ptr, n_tok, x_ptr, None, None)
+        if rc != 0:
+            raise RuntimeError(f"tr_gpu_moe_layer: {last_error()}")
+
+    def layer_dev(self, layer: int, normed_ptr: int, n_tok: int, x_ptr: int, outs: dict | None = None,
+                  stream: int = 0):
+        """Device pointers (e.g. torch tensors' data_ptr()); enqueued on `stream` (0: the context's own)."""
+        o = None
+        if outs:
+            o = Outputs(*(outs.get(k) for k in ("logits", "sel_id", "sel_w", "offsets", "place", "ffn_out")))
+        rc = lib().tr_gpu_moe_layer_dev(self.h, layer, normed_ptr, n_tok, x_ptr, C.byref(o) if o else None,
+                                        stream or None)
+        if rc != 0:
+            raise RuntimeError(f"tr_gpu_moe_layer_dev: {last_error()}")
+
+    ZONES = ("router", "gate_up", "act_prep", "down")
+
+    def profile(self, on: bool):
+        if lib().tr_gpu_moe_profile(self.h, 1 if on else 0) != 0:
+            raise RuntimeError(f"tr_gpu_moe_profile: {last_error()}")
+
+    def profile_read(self) -> dict:
+        ms = np.zeros(4, np.float64)
+        calls = np.zeros(4, np.int64)
+        if lib().tr_gpu_moe_profile_read(self.h, _p(ms), _p(calls), 4) != 0:
+            raise RuntimeError(f"tr_gpu_moe_profile_read: {last_error()}")
+        return {z: (float(ms[i]), int(calls[i])) for i, z in enumerate(self.ZONES)}
+
+    def launches(self, n_tok: int) -> int:
+        return int(lib().tr_gpu_moe_launches(self.h, n_tok))
+
+    def close(self):
+        if self.h:
+            lib().tr_gpu_moe_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def matmul_grouped(type_: int, rows: int, cols: int, mats, offsets, x: np.ndarray, use_s: bool = False):
+    """tr_matmul_grouped on host arrays: mats[g] = rows x row_bytes uint8 (GGUF), x = offsets[-1] x cols."""
+    n = len(mats)
+    ws = (TrMat * n)(*[TrMat(type_, rows, cols, m.ctypes.data) for m in mats])
+    off = np.ascontiguousarray(offsets, dtype=np.int64)
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    y = np.full((int(off[-1]), rows), np.nan, dtype=np.float32)
+    if use_s:
+        lib().tr_matmul_grouped_s(None, ws, _p(off), n, _p(x), _p(y), None)
+    else:
+        lib().tr_matmul_grouped(None, ws, _p(off), n, _p(x), _p(y))
+    err = last_error()
+    if err:
+        raise RuntimeError(f"tr_matmul_grouped: {err}")
+    return y
+
+
+def matmul(type_: int, rows: int, cols: int, w: np.ndarray, x: np.ndarray):
+    m = TrMat(type_, rows, cols, w.ctypes.data)
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    y = np.full((x.shape[0], rows), np.nan, dtype=np.float32)
+    lib().tr_matmul(None, C.byref(m), _p(x), x.shape[0], _p(y))
+    err = last_error()
+    if err:
+        raise RuntimeError(f"tr_matmul: {err}")
+    return y
+
+
+def softmax(x: np.ndarray) -> np.ndarray:
+    y = np.array(x, dtype=np.float32, copy=True)
+    lib().tr_softmax(_p(y), y.size)
+    err = last_error()
+    if err:
+        raise RuntimeError(f"tr_softmax: {err}")
+    return y
+
+
+def swiglu(x: np.ndarray, y: np.ndarray) -> np.ndarray:
+    out = np.array(x, dtype=np.float32, copy=True)
+    y = np.ascontiguousarray(y, dtype=np.float32)
+    lib().tr_swiglu(None, _p(out), _p(y), out.size)
+    err = last_error()
+    if err:
+        raise RuntimeError(f"tr_swiglu: {err}")
+    return out
