@@ -45,7 +45,7 @@ E, K_USED, H, F = 64, 8, 2048, 1024
 def args_parse():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=2000)
+    p.add_argument("--steps", type=int, default=32000)
     p.add_argument("--warmup", type=int, default=50)
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--tokens", type=int, default=1)
@@ -90,6 +90,11 @@ class Clocks:
         except OSError:
             self.proc = None
         return self
+
+    def wait_first(self, limit_s=3.0):
+        t0 = time.time()
+        while self.proc and not self.rows and time.time() - t0 < limit_s:
+            time.sleep(0.02)
 
     def _read(self):
         for line in self.proc.stdout:
@@ -195,28 +200,47 @@ def run_ours(args, rank, world, dist):
         lay["router"] = routers[l]
         m.set_layer(l, lay)
     del lays
-    n_in = 64
     g = torch.Generator(device="cuda")
     g.manual_seed(1234 + rank)
-    normed = torch.randn((n_in, T, H), device="cuda", generator=g)
+    normed = torch.randn((NL, T, H), device="cuda", generator=g)
     x = torch.randn((T, H), device="cuda", generator=g)
-    stream = torch.cuda.current_stream()
-    sp = stream.cuda_stream
+    side = torch.cuda.Stream()
 
-    def step(i):
-        m.layer_dev(i % NL, normed[i % n_in].data_ptr(), T, x.data_ptr(), None, stream=sp)
+    def capture(parts, n=NL):
+        """a CUDA graph of n layer calls (call l: layer l on input row l), the given parts only"""
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=side):
+            sp = torch.cuda.current_stream().cuda_stream
+            for l in range(n):
+                for part in parts:
+                    m.layer_part(l, part, normed[l].data_ptr(), T, x.data_ptr(), stream=sp)
+        return graph
 
-    for i in range(args.warmup):
-        step(i)
+    # warm-up outside graphs (first touches), then the graphs
+    for i in range(max(args.warmup, 3)):
+        m.layer_dev(i % NL, normed[i % NL].data_ptr(), T, x.data_ptr(), None,
+                    stream=torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    parts_of = {"route": [0], "gate_up": [0, 1], "act_prep": [0, 1, 2], "full": [0, 1, 2, 3]}
+    graphs = {k: capture(v) for k, v in parts_of.items()}
+    steps = args.steps
+    reps, tail_n = steps // NL, steps % NL
+    tail = capture(parts_of["full"], tail_n) if tail_n else None
+    for _ in range(max(args.warmup // NL, 3)):
+        graphs["full"].replay()
     torch.cuda.synchronize()
     if dist:
         dist.barrier()
+    stream = torch.cuda.current_stream()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with Clocks(dev) as clk:
+        clk.wait_first()
         torch.cuda.synchronize()
         start.record(stream)
-        for i in range(args.steps):
-            step(i)
+        for _ in range(reps):
+            graphs["full"].replay()
+        if tail is not None:
+            tail.replay()
         end.record(stream)
         torch.cuda.synchronize()
     ms = start.elapsed_time(end)
@@ -225,24 +249,34 @@ def run_ours(args, rank, world, dist):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
         dist.barrier()
-    ms_step = ms / args.steps
+    ms_step = ms / steps
     value = world * T / (ms_step / 1000.0)
 
-    # roofline pass: zone times with CUDA events on the launching stream, and the experts actually used
-    m.profile(True)
-    for i in range(args.steps):
-        step(i)
-    zones = m.profile_read()
-    m.profile(False)
+    # zones: each part's marginal device time per layer call, from graphs of parts 0..z (CUDA events on the
+    # replaying stream), warm replays first
+    cum = {}
+    for k in ("route", "gate_up", "act_prep", "full"):
+        for _ in range(3):
+            graphs[k].replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(max(reps, 1)):
+            graphs[k].replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        cum[k] = e0.elapsed_time(e1) / (max(reps, 1) * NL)
+    zone_ms = {"router": cum["route"], "gate_up": cum["gate_up"] - cum["route"],
+               "act_prep": cum["act_prep"] - cum["gate_up"], "down": cum["full"] - cum["act_prep"]}
+    del graphs, tail
     # distinct experts per call (computed from the routing each call makes)
-    sel = torch.zeros((args.steps, T * K_USED), dtype=torch.int64, device="cuda")
+    sel = torch.zeros((NL, T * K_USED), dtype=torch.int64, device="cuda")
     sel_w = torch.zeros((T * K_USED,), device="cuda")
-    for i in range(min(args.steps, 256)):
-        m.layer_dev(i % NL, normed[i % n_in].data_ptr(), T, x.data_ptr(),
-                    {"sel_id": sel[i].data_ptr(), "sel_w": sel_w.data_ptr()}, stream=sp)
+    for l in range(NL):
+        m.layer_dev(l, normed[l].data_ptr(), T, x.data_ptr(), {"sel_id": sel[l].data_ptr(), "sel_w": sel_w.data_ptr()},
+                    stream=torch.cuda.current_stream().cuda_stream)
     torch.cuda.synchronize()
-    sel_h = sel[:min(args.steps, 256)].cpu().numpy()
-    used = [len(np.unique(r)) for r in sel_h]
+    used = [len(np.unique(r)) for r in sel.cpu().numpy()]
     U = float(np.mean(used))
     bpe = bytes_per_expert(gate, down)
     router_bytes = E * gb.row_bytes(gb.BF16, H)
@@ -251,7 +285,6 @@ def run_ours(args, rank, world, dist):
     down_bytes = U * H * gb.row_bytes(down, F) + T * K_USED * F * 4 + 2 * T * H * 4
     zone_bytes = {"router": router_bytes + T * H * 4, "gate_up": gate_bytes,
                   "act_prep": 2 * T * K_USED * F * 4, "down": down_bytes}
-    zone_ms = {z: (v[0] / v[1] if v[1] else 0.0) for z, v in zones.items()}
     dom = max(zone_ms, key=lambda z: zone_ms[z])
     peak, peak_kind = peaks()
     achieved = zone_bytes[dom] / (zone_ms[dom] / 1000.0) / 1e9
@@ -264,9 +297,10 @@ def run_ours(args, rank, world, dist):
     layer_ms = sum(zone_ms.values())
 
     # e2e through the public host-pointer call, pinned buffers, copies inside the timed region
+    n_in = 16
     hn = torch.randn((n_in, T, H), generator=torch.Generator().manual_seed(99)).pin_memory()
     hx = torch.randn((T, H)).pin_memory()
-    e2e_steps = max(min(args.steps, 2000), 10)
+    e2e_steps = max(min(args.steps, 4000), 10)
     for i in range(5):
         m.layer_ptrs(i % NL, hn[i % n_in].data_ptr(), T, hx.data_ptr(), host=True)
     if dist:
@@ -292,7 +326,7 @@ def run_ours(args, rank, world, dist):
     m.close()
     if rank != 0:
         return
-    line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+    line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": steps,
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "int32/int64+f64 (Q4_K), f32 (Q6_K/Q8_0 lane contract)",
             "data": "synthetic", "config": workload_config(args),
@@ -302,7 +336,9 @@ def run_ours(args, rank, world, dist):
             "layer_roofline": {"achieved": layer_bytes / (ms_step / 1000.0) / 1e9, "unit": "GB/s",
                                "frac": layer_bytes / (ms_step / 1000.0) / 1e9 / peak, "bytes": layer_bytes,
                                "distinct_experts": U, "zone_ms": zone_ms, "zone_sum_ms": layer_ms},
-            "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches * args.steps, "clocks": clk.summary()}
+            "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches * steps, "clocks": clk.summary(),
+            "timing": f"CUDA graphs of {NL} layer calls replayed (+ a graph of the last {tail_n}); zones from graphs "
+                      f"of parts 0..z"}
     print(json.dumps(line), flush=True)
 
 

@@ -101,6 +101,15 @@ typedef struct {
 TRMOE_API int tr_gpu_moe_layer_dev(tr_gpu_moe *m, int64_t layer, const float *d_normed, int64_t n_tok, float *d_x_inout,
                          const tr_gpu_moe_outputs *out, void *stream);
 
+/* One part of tr_gpu_moe_layer_dev: 0 route (router, top-k, dispatch, input preparation), 1 gate/up and
+ * SwiGLU, 2 the down input's Q4_K preparation (nothing for another down type), 3 down, combine and residual
+ * add: Trochilus's profiler zones ROUTER, EXPERT_GATE_UP, EXPERT_ACT, EXPERT_DOWN + EXPERT_MIX
+ * (src/base/prof.h:42-47). Parts 0..3 enqueued in order on one stream with the same arguments are one layer
+ * call; `out` is read by the parts that write it (0: logits, sel_id, sel_w, offsets, place; 3: ffn_out).
+ * Enqueues only, like tr_gpu_moe_layer_dev; it can be captured in a CUDA graph. 0, or -1. */
+TRMOE_API int tr_gpu_moe_layer_part(tr_gpu_moe *m, int64_t layer, int part, const float *d_normed, int64_t n_tok,
+                                    float *d_x_inout, const tr_gpu_moe_outputs *out, void *stream);
+
 /* Zone timing, the GPU counterpart of Trochilus's profiler zones (src/base/prof.h:42-47: ROUTER,
  * EXPERT_GATE_UP, EXPERT_ACT, EXPERT_DOWN with EXPERT_MIX): when on, every layer call records CUDA events
  * around its kernels on the stream it runs on. tr_gpu_moe_profile_read waits for the last call and
@@ -110,6 +119,10 @@ TRMOE_API int tr_gpu_moe_layer_dev(tr_gpu_moe *m, int64_t layer, const float *d_
 #define TRMOE_ZONES 4
 TRMOE_API int tr_gpu_moe_profile(tr_gpu_moe *m, int on);
 TRMOE_API int tr_gpu_moe_profile_read(tr_gpu_moe *m, double *ms, int64_t *calls, int n_zones);
+
+/* Waits for the context's stream and reports whether a kernel gave up on a bounded wait since the last
+ * check (the device error flag, then cleared). 0, or -1 with a message. tr_gpu_moe_layer checks it itself. */
+TRMOE_API int tr_gpu_moe_check(tr_gpu_moe *m);
 
 /* How many kernels one tr_gpu_moe_layer_dev call launches for n_tok tokens. */
 TRMOE_API int tr_gpu_moe_launches(const tr_gpu_moe *m, int64_t n_tok);

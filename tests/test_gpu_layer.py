@@ -107,3 +107,71 @@ def test_unset_layer_is_an_error(cuda):
     with pytest.raises(RuntimeError, match="not set"):
         m.layer(1, np.zeros((1, 2048), np.float32), np.zeros((1, 2048), np.float32))
     m.close()
+
+
+def test_zone_profile_counts_calls(cuda):
+    """the zone timer sees every call and gives positive times without changing results"""
+    c = dict(E=64, k=8, H=2048, F=1024, router=gb.BF16, gate=gb.Q4_K, down=gb.Q4_K, norm_topk=0, T=2)
+    m = _ctx(c)
+    m.set_layer(0, gb.make_layer(31, 64, 2048, 1024, gb.Q4_K, gb.Q4_K, gb.BF16, mode="random"))
+    rng = np.random.default_rng(0)
+    normed = rng.normal(size=(2, 2048)).astype(np.float32)
+    x = rng.normal(size=(2, 2048)).astype(np.float32)
+    x0 = x.copy()
+    m.layer(0, normed, x0)
+    m.profile(True)
+    for _ in range(5):
+        x1 = x.copy()
+        m.layer(0, normed, x1)
+        assert same_bits(x1, x0)
+    z = m.profile_read()
+    assert all(z[k][1] == 5 and z[k][0] > 0 for k in ("router", "gate_up", "act_prep", "down")), z
+    m.profile(False)
+    m.close()
+
+
+@pytest.mark.parametrize("T", [1, 7, 70])
+def test_parts_path_matches_oracle(cuda, oracle, T):
+    """tr_gpu_moe_layer_part 0..3 (the multi-kernel road, also the one of passes longer than the fused kernel
+    takes) against the oracle, and against the single-call road"""
+    gt, dt, rt = gb.Q8_0, gb.Q6_K, gb.F32
+    lay = gb.make_layer(600 + T, 16, 512, 256, gt, dt, rt, mode="random")
+    d, keep = make_desc(lay, 512, 256, 4, 0, rt, gt, dt)
+    from trochilus_b200.moe import GpuMoe
+    m = GpuMoe(1, 16, 4, 512, 256, rt, gt, dt, max_tokens=T)
+    m.set_layer(0, lay)
+    rng = np.random.default_rng(T)
+    normed = rng.normal(size=(T, 512)).astype(np.float32)
+    x = rng.normal(size=(T, 512)).astype(np.float32)
+    want = oracle.moe_layer(d, normed, x)
+    dn = cuda.from_numpy(normed).cuda()
+    dx = cuda.from_numpy(x.copy()).cuda()
+    st = cuda.cuda.current_stream().cuda_stream
+    for part in range(4):
+        m.layer_part(0, part, dn.data_ptr(), T, dx.data_ptr(), stream=st)
+    cuda.cuda.synchronize()
+    assert same_bits(dx.cpu().numpy(), want["x"])
+    xo = x.copy()
+    sid, sw = m.layer(0, normed, xo)
+    assert same_bits(xo, want["x"]) and same_bits(sid, want["sel_id"]) and same_bits(sw, want["sel_w"])
+    m.check()
+    m.close()
+
+
+def test_q4k_long_pass_multikernel(cuda, oracle):
+    """a pass longer than the fused kernel serves (T > 64) on the OLMoE shape, Q4_K experts"""
+    T = 72
+    lay = gb.make_layer(777, 64, 2048, 1024, gb.Q4_K, gb.Q4_K, gb.BF16, mode="random")
+    d, keep = make_desc(lay, 2048, 1024, 8, 0, gb.BF16, gb.Q4_K, gb.Q4_K)
+    from trochilus_b200.moe import GpuMoe
+    m = GpuMoe(1, 64, 8, 2048, 1024, gb.BF16, gb.Q4_K, gb.Q4_K, max_tokens=T)
+    m.set_layer(0, lay)
+    rng = np.random.default_rng(5)
+    normed = rng.normal(size=(T, 2048)).astype(np.float32)
+    x = rng.normal(size=(T, 2048)).astype(np.float32)
+    want = oracle.moe_layer(d, normed, x)
+    xo = x.copy()
+    sid, sw = m.layer(0, normed, xo)
+    assert same_bits(sid, want["sel_id"]) and same_bits(sw, want["sel_w"])
+    assert same_bits(xo, want["x"])
+    m.close()

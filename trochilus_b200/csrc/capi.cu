@@ -21,6 +21,7 @@
 #include "layouts.cuh"
 #include "moe_kernels.cuh"
 #include "kernel_api.cuh"
+#include "fused_layer.cuh"
 
 namespace {
 
@@ -89,7 +90,7 @@ bool upload_matrix(int type, int64_t rows, int64_t cols, const void *host, uint8
 }
 
 struct WorkLayout {
-    int64_t off[24];
+    int64_t off[25];
     int64_t total;
 };
 
@@ -106,7 +107,7 @@ WorkLayout work_layout(const tr_gpu_moe_config &c) {
         E * 4,              // 6 active
         4,                  // 7 n_active
         4,                  // 8 route_cnt
-        (H / TRX_DN_ROWS) * 4, // 9 comb_cnt
+        (H / TRX_DN_CHUNK) * 4 + 256, // 9 comb_cnt, then the error flag
         T * H * 4,          // 10 x_lc
         T * H * 4,          // 11 xq
         T * (H / 32) * 8,   // 12 xq_bf
@@ -120,10 +121,11 @@ WorkLayout work_layout(const tr_gpu_moe_config &c) {
         T * H * 4,          // 20 host-call x
         R * 8,              // 21 host-call sel_id
         R * 4,              // 22 host-call sel_w
+        (int64_t)sizeof(TrxSync), // 23 the fused kernel's counters
     };
     WorkLayout w{};
     int64_t o = 0;
-    for (int i = 0; i < 23; i++) {
+    for (int i = 0; i < 24; i++) {
         w.off[i] = o;
         o += align_up(sizes[i], 256);
     }
@@ -151,30 +153,128 @@ struct tr_gpu_moe {
     uint8_t *work_mem = nullptr;
     uint8_t *tmp = nullptr;
     TrxWork work{};
+    int grid_gu = 0, grid_dn = 0, grid_fused = 0;
+    size_t smem_gu = 0, smem_dn = 0, smem_fused = 0;
+    TrxSync *sync = nullptr;
+    uint32_t epoch = 0;
+    bool fused_ok = false;
     float *d_normed = nullptr, *d_x = nullptr;
     int64_t *d_sel_id = nullptr;
     float *d_sel_w = nullptr;
-    // zone timing (tr_gpu_moe_profile)
-    bool prof = false, prof_pending = false;
-    cudaEvent_t ev[TRMOE_ZONES + 1] = {};
-    bool ev_used[TRMOE_ZONES] = {};
+    // zone timing (tr_gpu_moe_profile): one set of events per profiled call, read when asked, so that
+    // profiling never makes a call wait for the one before it
+    struct EvSet {
+        cudaEvent_t ev[TRMOE_ZONES + 1];
+        bool used[TRMOE_ZONES];
+    };
+    bool prof = false;
+    std::vector<EvSet> evs;   // every set created so far
+    size_t ev_next = 0;       // sets [0, ev_next) hold calls not yet added to the sums
     double prof_ms[TRMOE_ZONES] = {};
     int64_t prof_calls[TRMOE_ZONES] = {};
 };
 
-// adds the last call's zone times to the sums (waits for its events)
+#define TRMOE_PROF_SETS 4096
+
+// adds the recorded calls' zone times to the sums (waits for their events)
 static bool prof_collect(tr_gpu_moe *m) {
-    if (!m->prof_pending) return true;
-    if (!ck(cudaEventSynchronize(m->ev[TRMOE_ZONES]), "cudaEventSynchronize")) return false;
-    for (int z = 0; z < TRMOE_ZONES; z++) {
-        if (!m->ev_used[z]) continue;
-        float ms = 0.0f;
-        if (!ck(cudaEventElapsedTime(&ms, m->ev[z], m->ev[z + 1]), "cudaEventElapsedTime")) return false;
-        m->prof_ms[z] += ms;
-        m->prof_calls[z] += 1;
+    for (size_t i = 0; i < m->ev_next; i++) {
+        auto &e = m->evs[i];
+        if (!ck(cudaEventSynchronize(e.ev[TRMOE_ZONES]), "cudaEventSynchronize")) return false;
+        for (int z = 0; z < TRMOE_ZONES; z++) {
+            if (!e.used[z]) continue;
+            float ms = 0.0f;
+            if (!ck(cudaEventElapsedTime(&ms, e.ev[z], e.ev[z + 1]), "cudaEventElapsedTime")) return false;
+            m->prof_ms[z] += ms;
+            m->prof_calls[z] += 1;
+        }
     }
-    m->prof_pending = false;
+    m->ev_next = 0;
     return true;
+}
+
+// the event set of the next profiled call (collecting the recorded ones when the ring is full)
+static tr_gpu_moe::EvSet *prof_slot(tr_gpu_moe *m) {
+    if (m->ev_next == TRMOE_PROF_SETS && !prof_collect(m)) return nullptr;
+    if (m->ev_next == m->evs.size()) {
+        tr_gpu_moe::EvSet e{};
+        for (auto &v : e.ev)
+            if (!ck(cudaEventCreate(&v), "cudaEventCreate")) return nullptr;
+        m->evs.push_back(e);
+    }
+    return &m->evs[m->ev_next++];
+}
+
+using GateUpFn = void (*)(TrxLayer, TrxShape, TrxWork);
+using DownFn = void (*)(TrxLayer, TrxShape, TrxWork, float *, int, float *);
+
+static GateUpFn gateup_fn(int gate_type, int down_type) {
+    const bool lc = down_type != TRX_Q4_K;
+    if (gate_type == TRX_Q4_K) return lc ? trx_k_gateup<TRX_Q4_K, true> : trx_k_gateup<TRX_Q4_K, false>;
+    return lc ? trx_k_gateup<TRX_Q8_0, true> : trx_k_gateup<TRX_Q8_0, false>;
+}
+
+static DownFn down_fn(int down_type) {
+    if (down_type == TRX_Q4_K) return trx_k_down<TRX_Q4_K>;
+    if (down_type == TRX_Q8_0) return trx_k_down<TRX_Q8_0>;
+    return trx_k_down<TRX_Q6_K>;
+}
+
+using LayerFn = void (*)(TrxLayer, TrxShape, const float *, int, TrxWork, TrxSync *, float *, float *, uint32_t);
+
+static LayerFn layer_fn(int gate_type, int down_type) {
+    if (gate_type == TRX_Q4_K) {
+        if (down_type == TRX_Q4_K) return trx_k_layer<TRX_Q4_K, TRX_Q4_K>;
+        if (down_type == TRX_Q6_K) return trx_k_layer<TRX_Q4_K, TRX_Q6_K>;
+        return trx_k_layer<TRX_Q4_K, TRX_Q8_0>;
+    }
+    if (down_type == TRX_Q4_K) return trx_k_layer<TRX_Q8_0, TRX_Q4_K>;
+    if (down_type == TRX_Q6_K) return trx_k_layer<TRX_Q8_0, TRX_Q6_K>;
+    return trx_k_layer<TRX_Q8_0, TRX_Q8_0>;
+}
+
+// the fused kernel: its shared memory at the largest pass it serves and a cooperative grid (every CTA resident)
+static bool plan_fused(tr_gpu_moe *m) {
+    const tr_gpu_moe_config &c = m->cfg;
+    const int tmax = (int)std::min<int64_t>(c.max_tokens, TRX_ROUTE_FUSED_MAX);
+    m->smem_fused = trx_fused_smem(c.gate_type, c.down_type, (int)c.n_embd, (int)c.n_ff, tmax);
+    int coop = 0, occ = 0;
+    LayerFn fn = layer_fn(c.gate_type, c.down_type);
+    if (!ck(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, m->device), "attribute")) return false;
+    if (!coop || m->smem_fused > 227 * 1024) return true; // the multi-kernel road serves every pass
+    if (!ck(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)m->smem_fused), "smem fused") ||
+        !ck(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fn, 256, m->smem_fused), "occupancy"))
+        return false;
+    m->grid_fused = occ * m->sm_count;
+    m->fused_ok = occ >= 1 && m->grid_fused >= (int)(c.n_expert + tmax);
+    return true;
+}
+
+// shared memory of the streaming kernels and their persistent grids (every CTA resident at once)
+static bool plan_kernels(tr_gpu_moe *m) {
+    const tr_gpu_moe_config &c = m->cfg;
+    const int64_t rb_gu = trx_row_bytes(c.gate_type, c.n_embd);
+    const int64_t rb_dn = c.down_type == TRX_Q6_K ? c.n_ff / 256 * 208 : trx_row_bytes(c.down_type, c.n_ff);
+    m->smem_gu = (size_t)(TRX_STAGES * 2 * TRX_GU_CHUNK * rb_gu + TRX_STAGES * 8);
+    m->smem_dn = (size_t)(TRX_STAGES * TRX_DN_CHUNK * rb_dn + TRX_STAGES * 8);
+    const size_t smem_router = (size_t)(1 + TRX_TOK_STAGE) * c.n_embd * 4;
+    GateUpFn gu = gateup_fn(c.gate_type, c.down_type);
+    DownFn dn = down_fn(c.down_type);
+    int occ_gu = 0, occ_dn = 0;
+    bool ok = ck(cudaFuncSetAttribute(gu, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)m->smem_gu), "smem gate/up") &&
+              ck(cudaFuncSetAttribute(dn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)m->smem_dn), "smem down") &&
+              ck(cudaFuncSetAttribute(trx_k_router, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_router),
+                 "smem router") &&
+              ck(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ_gu, gu, 256, m->smem_gu), "occupancy") &&
+              ck(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ_dn, dn, 256, m->smem_dn), "occupancy");
+    if (!ok) return false;
+    if (occ_gu < 1 || occ_dn < 1) {
+        set_err("the expert kernels do not fit on an SM (occupancy %d, %d)", occ_gu, occ_dn);
+        return false;
+    }
+    m->grid_gu = occ_gu * m->sm_count;
+    m->grid_dn = occ_dn * m->sm_count;
+    return plan_fused(m);
 }
 
 extern "C" const char *trmoe_last_error(void) { return g_err.c_str(); }
@@ -249,6 +349,7 @@ extern "C" tr_gpu_moe *tr_gpu_moe_create(const tr_gpu_moe_config *cfg, int devic
         for (int64_t l = 0; l < cfg->n_layers && ok; l++)
             ok = ck(cudaMalloc(&m->layer_mem[(size_t)l], (size_t)lb), "cudaMalloc(layer)");
     }
+    if (ok) ok = plan_kernels(m);
     if (!ok) {
         put_err(err, err_len);
         tr_gpu_moe_free(m);
@@ -266,6 +367,7 @@ extern "C" tr_gpu_moe *tr_gpu_moe_create(const tr_gpu_moe_config *cfg, int devic
     w.n_active = (int32_t *)(b + wl.off[7]);
     w.route_cnt = (uint32_t *)(b + wl.off[8]);
     w.comb_cnt = (uint32_t *)(b + wl.off[9]);
+    w.err = (int32_t *)(b + wl.off[9] + (cfg->n_embd / TRX_DN_CHUNK) * 4);
     w.x_lc = (float *)(b + wl.off[10]);
     w.xq = (uint32_t *)(b + wl.off[11]);
     w.xq_bf = (double *)(b + wl.off[12]);
@@ -279,6 +381,7 @@ extern "C" tr_gpu_moe *tr_gpu_moe_create(const tr_gpu_moe_config *cfg, int devic
     m->d_x = (float *)(b + wl.off[20]);
     m->d_sel_id = (int64_t *)(b + wl.off[21]);
     m->d_sel_w = (float *)(b + wl.off[22]);
+    m->sync = (TrxSync *)(b + wl.off[23]);
     return m;
 }
 
@@ -290,8 +393,8 @@ extern "C" void tr_gpu_moe_free(tr_gpu_moe *m) {
         if (p) cudaFree(p);
     if (m->work_mem) cudaFree(m->work_mem);
     if (m->tmp) cudaFree(m->tmp);
-    for (cudaEvent_t e : m->ev)
-        if (e) cudaEventDestroy(e);
+    for (auto &es : m->evs)
+        for (cudaEvent_t e : es.ev) cudaEventDestroy(e);
     if (m->stream) cudaStreamDestroy(m->stream);
     delete m;
 }
@@ -354,9 +457,6 @@ extern "C" int tr_gpu_moe_set_layer(tr_gpu_moe *m, int64_t layer, const void *ro
 extern "C" int tr_gpu_moe_profile(tr_gpu_moe *m, int on) {
     g_err.clear();
     if (m == nullptr || !ck(cudaSetDevice(m->device), "cudaSetDevice")) return -1;
-    if (on && m->ev[0] == nullptr)
-        for (cudaEvent_t &e : m->ev)
-            if (!ck(cudaEventCreate(&e), "cudaEventCreate")) return -1;
     if (!prof_collect(m)) return -1;
     m->prof = on != 0;
     for (int z = 0; z < TRMOE_ZONES; z++) {
@@ -376,14 +476,39 @@ extern "C" int tr_gpu_moe_profile_read(tr_gpu_moe *m, double *ms, int64_t *calls
     return 0;
 }
 
-extern "C" int tr_gpu_moe_launches(const tr_gpu_moe *m, int64_t n_tok) {
-    (void)n_tok;
-    if (m == nullptr) return 0;
-    return m->cfg.down_type == TRX_Q4_K ? 4 : 3;
+// after a kernel gave up: every counter and flag back to zero (the next call starts clean)
+static void reset_counters(tr_gpu_moe *m, cudaStream_t st) {
+    cudaMemsetAsync(m->work.err, 0, 4, st);
+    cudaMemsetAsync(m->work.route_cnt, 0, 4, st);
+    cudaMemsetAsync(m->work.comb_cnt, 0, (size_t)(m->cfg.n_embd / TRX_DN_CHUNK) * 4, st);
+    cudaMemsetAsync(m->sync, 0, sizeof(TrxSync), st);
+    m->epoch = 0;
+    stream_wait(st);
 }
 
+extern "C" int tr_gpu_moe_launches(const tr_gpu_moe *m, int64_t n_tok) {
+    if (m == nullptr) return 0;
+    if (m->fused_ok && n_tok <= TRX_ROUTE_FUSED_MAX && !m->prof) return 1;
+    return (n_tok <= TRX_ROUTE_FUSED_MAX ? 1 : 4) + 2 + (m->cfg.down_type == TRX_Q4_K ? 1 : 0);
+}
+
+extern "C" int tr_gpu_moe_check(tr_gpu_moe *m) {
+    g_err.clear();
+    if (m == nullptr || !ck(cudaSetDevice(m->device), "cudaSetDevice") || !stream_wait(m->stream)) return -1;
+    int32_t flag = 0;
+    if (!ck(cudaMemcpy(&flag, m->work.err, 4, cudaMemcpyDeviceToHost), "read error flag")) return -1;
+    if (flag != 0) {
+        reset_counters(m, m->stream);
+        set_err("a kernel gave up on a bounded wait (device error flag %d)", flag);
+        return -1;
+    }
+    return 0;
+}
+
+// Enqueues parts [first, last] of one layer call on st: 0 route (router, top-k, dispatch, input preparation),
+// 1 gate/up + SwiGLU, 2 the down input's Q4_K preparation, 3 down + combine + residual.
 static int launch_layer(tr_gpu_moe *m, int64_t layer, const float *d_normed, int64_t n_tok, float *d_x,
-                        const tr_gpu_moe_outputs *out, cudaStream_t st) {
+                        const tr_gpu_moe_outputs *out, cudaStream_t st, int first = 0, int last = 3) {
     const tr_gpu_moe_config &c = m->cfg;
     if (layer < 0 || layer >= c.n_layers || !m->layer_set[(size_t)layer]) {
         set_err("layer %lld is not set", (long long)layer);
@@ -391,6 +516,10 @@ static int launch_layer(tr_gpu_moe *m, int64_t layer, const float *d_normed, int
     }
     if (n_tok < 1 || n_tok > c.max_tokens || d_normed == nullptr || d_x == nullptr) {
         set_err("bad token count %lld (max %lld) or input", (long long)n_tok, (long long)c.max_tokens);
+        return -1;
+    }
+    if (first < 0 || last > 3 || first > last) {
+        set_err("bad part range %d..%d", first, last);
         return -1;
     }
     const TrxLayer &L = m->layers[(size_t)layer];
@@ -408,41 +537,62 @@ static int launch_layer(tr_gpu_moe *m, int64_t layer, const float *d_normed, int
         return -1;
     }
     const int T = (int)n_tok, E = S.E, R = T * S.k;
-    const int act_max = std::min(E, R);
-    if (m->prof && !prof_collect(m)) return -1;
+    tr_gpu_moe::EvSet *es = nullptr;
+    if (m->prof && first == 0 && last == 3 && (es = prof_slot(m)) == nullptr) return -1;
     // zone z's kernels run between events z and z + 1; an unused zone's two events coincide
     auto mark = [&](int z) {
-        if (m->prof) cudaEventRecord(m->ev[z], st);
+        if (es) cudaEventRecord(es->ev[z], st);
     };
-    for (int z = 0; z < TRMOE_ZONES; z++) m->ev_used[z] = true;
-    m->ev_used[2] = c.down_type == TRX_Q4_K;
-    mark(0);
-    trx_k_router<<<(unsigned)(E + T), 256, (size_t)S.H * 4, st>>>(L, S, d_normed, T, w);
-    mark(1);
-    const int gu_items = act_max * (S.F / TRX_GU_ROWS);
-    const unsigned gu_grid = (unsigned)std::min(gu_items, 2 * m->sm_count);
-    const bool down_lc = c.down_type != TRX_Q4_K;
-    if (c.gate_type == TRX_Q4_K) {
-        if (down_lc) trx_k_gateup<TRX_Q4_K, true><<<gu_grid, 256, 0, st>>>(L, S, w);
-        else trx_k_gateup<TRX_Q4_K, false><<<gu_grid, 256, 0, st>>>(L, S, w);
-    } else {
-        if (down_lc) trx_k_gateup<TRX_Q8_0, true><<<gu_grid, 256, 0, st>>>(L, S, w);
-        else trx_k_gateup<TRX_Q8_0, false><<<gu_grid, 256, 0, st>>>(L, S, w);
+    if (es) {
+        for (int z = 0; z < TRMOE_ZONES; z++) es->used[z] = true;
+        es->used[2] = c.down_type == TRX_Q4_K;
     }
+    if (first == 0 && last == 3 && m->fused_ok && T <= TRX_ROUTE_FUSED_MAX && !es) {
+        float *ffn = out ? out->ffn_out : nullptr;
+        const uint32_t epoch = ++m->epoch;
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)m->grid_fused);
+        cfg.blockDim = dim3(256);
+        cfg.dynamicSmemBytes = m->smem_fused;
+        cfg.stream = st;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeCooperative;
+        attr[0].val.cooperative = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        return ck(cudaLaunchKernelEx(&cfg, layer_fn(c.gate_type, c.down_type), L, S, d_normed, T, w, m->sync, d_x, ffn,
+                                     epoch),
+                  "fused layer launch")
+                   ? 0
+                   : -1;
+    }
+    mark(0);
+    if (first <= 0 && 0 <= last) {
+        const bool fused = T <= TRX_ROUTE_FUSED_MAX;
+        const size_t smem_router = (size_t)(1 + std::min(T, TRX_TOK_STAGE)) * S.H * 4;
+        if (fused) {
+            trx_k_router<<<(unsigned)(E + T), 256, smem_router, st>>>(L, S, d_normed, T, w, 1);
+        } else {
+            trx_k_router<<<dim3((unsigned)E, (unsigned)((T + TRX_TOK_STAGE - 1) / TRX_TOK_STAGE)), 256, smem_router,
+                           st>>>(L, S, d_normed, T, w, 0);
+            trx_k_prep_tokens<<<(unsigned)T, 256, 0, st>>>(L, S, d_normed, w);
+            trx_k_route<<<(unsigned)((T + 7) / 8), 256, 0, st>>>(S, T, w);
+            trx_k_sort<<<1, 1024, 0, st>>>(S, T, w);
+        }
+    }
+    mark(1);
+    if (first <= 1 && 1 <= last) gateup_fn(c.gate_type, c.down_type)<<<(unsigned)m->grid_gu, 256, m->smem_gu, st>>>(L, S, w);
     mark(2);
-    if (!down_lc) {
+    if (first <= 2 && 2 <= last && c.down_type == TRX_Q4_K) {
         const int warps = R * (S.F / 256);
-        trx_k_prep<<<(unsigned)((warps + 7) / 8), 256, 0, st>>>(S, nullptr, R, w);
+        trx_k_prep<<<(unsigned)((warps + 7) / 8), 256, 0, st>>>(S, R, w);
     }
     mark(3);
-    const int dn_items = act_max * (S.H / TRX_DN_ROWS);
-    const unsigned dn_grid = (unsigned)std::min(dn_items, 2 * m->sm_count);
-    float *ffn = out ? out->ffn_out : nullptr;
-    if (c.down_type == TRX_Q4_K) trx_k_down<TRX_Q4_K><<<dn_grid, 256, 0, st>>>(L, S, w, d_x, T, ffn);
-    else if (c.down_type == TRX_Q8_0) trx_k_down<TRX_Q8_0><<<dn_grid, 256, 0, st>>>(L, S, w, d_x, T, ffn);
-    else trx_k_down<TRX_Q6_K><<<dn_grid, 256, 0, st>>>(L, S, w, d_x, T, ffn);
+    if (first <= 3 && 3 <= last) {
+        float *ffn = out ? out->ffn_out : nullptr;
+        down_fn(c.down_type)<<<(unsigned)m->grid_dn, 256, m->smem_dn, st>>>(L, S, w, d_x, T, ffn);
+    }
     mark(4);
-    if (m->prof) m->prof_pending = true;
     return ck(cudaGetLastError(), "launch") ? 0 : -1;
 }
 
@@ -456,6 +606,18 @@ extern "C" int tr_gpu_moe_layer_dev(tr_gpu_moe *m, int64_t layer, const float *d
     if (!ck(cudaSetDevice(m->device), "cudaSetDevice")) return -1;
     cudaStream_t st = stream ? (cudaStream_t)stream : m->stream;
     return launch_layer(m, layer, d_normed, n_tok, d_x_inout, out, st);
+}
+
+extern "C" int tr_gpu_moe_layer_part(tr_gpu_moe *m, int64_t layer, int part, const float *d_normed, int64_t n_tok,
+                                     float *d_x_inout, const tr_gpu_moe_outputs *out, void *stream) {
+    g_err.clear();
+    if (m == nullptr) {
+        set_err("no context");
+        return -1;
+    }
+    if (!ck(cudaSetDevice(m->device), "cudaSetDevice")) return -1;
+    cudaStream_t st = stream ? (cudaStream_t)stream : m->stream;
+    return launch_layer(m, layer, d_normed, n_tok, d_x_inout, out, st, part, part);
 }
 
 extern "C" int tr_gpu_moe_layer(tr_gpu_moe *m, int64_t layer, const float *normed, int64_t n_tok, float *x_inout,
@@ -487,7 +649,14 @@ extern "C" int tr_gpu_moe_layer(tr_gpu_moe *m, int64_t layer, const float *norme
         ok = ck(cudaMemcpyAsync(sel_id_out, m->d_sel_id, (size_t)R * 8, cudaMemcpyDeviceToHost, st), "copy sel_id");
     if (ok && sel_w_out)
         ok = ck(cudaMemcpyAsync(sel_w_out, m->d_sel_w, (size_t)R * 4, cudaMemcpyDeviceToHost, st), "copy sel_w");
+    int32_t flag = 0;
+    if (ok) ok = ck(cudaMemcpyAsync(&flag, m->work.err, 4, cudaMemcpyDeviceToHost, st), "copy error flag");
     if (ok) ok = stream_wait(st);
+    if (ok && flag != 0) {
+        reset_counters(m, st);
+        set_err("a kernel gave up on a bounded wait (device error flag %d)", flag);
+        ok = false;
+    }
     return ok ? 0 : -1;
 }
 

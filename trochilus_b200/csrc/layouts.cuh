@@ -47,6 +47,13 @@ __host__ __device__ inline int trx_lc_pos(int k) {
     return (i << 8) + ((m >> 2) << 6) + (l << 2) + (m & 3);
 }
 
+// a float4 load, through L2 only when CG (data another CTA of the same kernel wrote)
+template <bool CG>
+__device__ __forceinline__ float4 trx_ldx(const float *p) {
+    if (CG) return __ldcg(reinterpret_cast<const float4 *>(p));
+    return *reinterpret_cast<const float4 *>(p);
+}
+
 // ---- repack kernels (one thread block per row) ----
 
 // Q8_0 rows (GGUF) -> Q8L rows; n % 256 == 0
@@ -116,11 +123,13 @@ __global__ void trx_repack_q6l(const uint8_t *__restrict__ src, uint8_t *__restr
 //   holding a NaN or an infinity (its X then 0). Restated from Trochilus k_q4x_prep
 //   (src/kernels/kernels.c:200-239) and tr_q4x_shift (src/kernels/kernels_internal.h:150-166).
 // One warp per 256-block; lane L takes elements 8 L .. 8 L + 7.
+// CG: read x through L2 only (rows another CTA of the same kernel wrote)
+template <bool CG = false>
 __device__ __forceinline__ void trx_prep_q4x_block(const float *__restrict__ x, uint32_t *__restrict__ planes,
                                                    double *__restrict__ bf, double *__restrict__ scale, int lane) {
     float v[8];
-    const float4 a = *reinterpret_cast<const float4 *>(x + 8 * lane);
-    const float4 b = *reinterpret_cast<const float4 *>(x + 8 * lane + 4);
+    const float4 a = trx_ldx<CG>(x + 8 * lane);
+    const float4 b = trx_ldx<CG>(x + 8 * lane + 4);
     v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
     float m = 0.0f;
     int bad = 0;
@@ -177,19 +186,29 @@ __device__ __forceinline__ void trx_prep_q4x_block(const float *__restrict__ x, 
 
 // ---- dot products ----
 
+// a 16-byte (8-, 4-, 2-byte) load from global memory through the read-only path, or a plain load
+// (shared memory: SM = true)
+template <bool SM, typename V>
+__device__ __forceinline__ V trx_ld(const void *p) {
+    if (SM) return *reinterpret_cast<const V *>(p);
+    return __ldg(reinterpret_cast<const V *>(p));
+}
+
 // Q4_K: the 4 * G lanes of a row group hold G blocks (lane: block s = lane/4 % G, chunk c = lane % 4)
 // X registers: the thread's 64 inputs as 4 byte planes x 16 words
 struct TrxQ4X {
     uint32_t w[4][16];
 };
 
+// CG: through L2 only (__ldcg), for rows another CTA of the same kernel wrote
+template <bool CG = false>
 __device__ __forceinline__ void trx_q4x_load(const uint32_t *__restrict__ planes_blk, int c, TrxQ4X &X) {
     const uint4 *src = reinterpret_cast<const uint4 *>(planes_blk + c * 64);
 #pragma unroll
     for (int p = 0; p < 4; p++)
 #pragma unroll
         for (int q = 0; q < 4; q++) {
-            const uint4 v = src[p * 4 + q];
+            const uint4 v = CG ? __ldcg(src + p * 4 + q) : src[p * 4 + q];
             X.w[p][4 * q + 0] = v.x;
             X.w[p][4 * q + 1] = v.y;
             X.w[p][4 * q + 2] = v.z;
@@ -230,6 +249,7 @@ __device__ __forceinline__ int64_t trx_q4k_chunk_T(uint4 hdr, uint4 q0, uint4 q1
 }
 
 // M of a block: sum_j m_j bf_j (exact: |bf| < 2^37, m < 64), then v = (d T - dmin M) scale in f64
+template <bool CG = false>
 __device__ __forceinline__ double trx_q4k_finish(uint4 hdr, int64_t T, const double *__restrict__ bf, double scale) {
     const uint32_t sw[3] = {hdr.y, hdr.z, hdr.w};
     auto sbyte = [&](int i) -> int { return (int)((sw[i >> 2] >> (8 * (i & 3))) & 255u); };
@@ -237,7 +257,7 @@ __device__ __forceinline__ double trx_q4k_finish(uint4 hdr, int64_t T, const dou
 #pragma unroll
     for (int j = 0; j < 8; j++) {
         const int mj = j < 4 ? (sbyte(j + 4) & 63) : ((sbyte(j + 4) >> 4) | ((sbyte(j) >> 6) << 4));
-        M += (int64_t)mj * (int64_t)bf[j];
+        M += (int64_t)mj * (int64_t)(CG ? __ldcg(bf + j) : bf[j]);
     }
     const double d = (double)trx_half((uint16_t)(hdr.x & 0xffffu));
     const double dmin = (double)trx_half((uint16_t)(hdr.x >> 16));
@@ -247,17 +267,18 @@ __device__ __forceinline__ double trx_q4k_finish(uint4 hdr, int64_t T, const dou
 
 // Q8L lane-contract dot of one row (n = 256 * nch) against an LC-ordered input row; thread l of the
 // half-warp. Returns the tree sum (same in all 16 threads).
+template <bool SM = false, bool CG = false>
 __device__ __forceinline__ float trx_q8l_dot(const uint8_t *__restrict__ row, const float *__restrict__ xlc, int nch,
                                              int l) {
     float acc = 0.0f;
     for (int i = 0; i < nch; i++) {
-        const uint4 sc = __ldg(reinterpret_cast<const uint4 *>(row + 272 * i));
-        const uint4 q = __ldg(reinterpret_cast<const uint4 *>(row + 272 * i + 16 + 16 * l));
+        const uint4 sc = trx_ld<SM, uint4>(row + 272 * i);
+        const uint4 q = trx_ld<SM, uint4>(row + 272 * i + 16 + 16 * l);
         const float *xs = xlc + 256 * i + 4 * l;
-        const float4 x0 = *reinterpret_cast<const float4 *>(xs);
-        const float4 x1 = *reinterpret_cast<const float4 *>(xs + 64);
-        const float4 x2 = *reinterpret_cast<const float4 *>(xs + 128);
-        const float4 x3 = *reinterpret_cast<const float4 *>(xs + 192);
+        const float4 x0 = trx_ldx<CG>(xs);
+        const float4 x1 = trx_ldx<CG>(xs + 64);
+        const float4 x2 = trx_ldx<CG>(xs + 128);
+        const float4 x3 = trx_ldx<CG>(xs + 192);
         const float xv[16] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w,
                               x2.x, x2.y, x2.z, x2.w, x3.x, x3.y, x3.z, x3.w};
         const uint32_t qw[4] = {q.x ^ 0x80808080u, q.y ^ 0x80808080u, q.z ^ 0x80808080u, q.w ^ 0x80808080u};
@@ -273,19 +294,20 @@ __device__ __forceinline__ float trx_q8l_dot(const uint8_t *__restrict__ row, co
 }
 
 // Q6L lane-contract dot (n = 256 * nsb); dptr: this row's nsb f16 d values
+template <bool SM = false, bool CG = false>
 __device__ __forceinline__ float trx_q6l_dot(const uint8_t *__restrict__ row, const uint8_t *__restrict__ dptr,
                                              const float *__restrict__ xlc, int nsb, int l) {
     float acc = 0.0f;
     for (int s = 0; s < nsb; s++) {
-        const uint2 ql = __ldg(reinterpret_cast<const uint2 *>(row + 128 * s + 8 * l));
-        const uint32_t qh = __ldg(reinterpret_cast<const uint32_t *>(row + 128 * nsb + 64 * s + 4 * l));
-        const uint4 scv = __ldg(reinterpret_cast<const uint4 *>(row + 192 * nsb + 16 * s));
+        const uint2 ql = trx_ld<SM, uint2>(row + 128 * s + 8 * l);
+        const uint32_t qh = trx_ld<SM, uint32_t>(row + 128 * nsb + 64 * s + 4 * l);
+        const uint4 scv = trx_ld<SM, uint4>(row + 192 * nsb + 16 * s);
         const float d = trx_half(__ldg(reinterpret_cast<const uint16_t *>(dptr) + s));
         const float *xs = xlc + 256 * s + 4 * l;
-        const float4 x0 = *reinterpret_cast<const float4 *>(xs);
-        const float4 x1 = *reinterpret_cast<const float4 *>(xs + 64);
-        const float4 x2 = *reinterpret_cast<const float4 *>(xs + 128);
-        const float4 x3 = *reinterpret_cast<const float4 *>(xs + 192);
+        const float4 x0 = trx_ldx<CG>(xs);
+        const float4 x1 = trx_ldx<CG>(xs + 64);
+        const float4 x2 = trx_ldx<CG>(xs + 128);
+        const float4 x3 = trx_ldx<CG>(xs + 192);
         const float xv[16] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w,
                               x2.x, x2.y, x2.z, x2.w, x3.x, x3.y, x3.z, x3.w};
         const uint32_t scw[4] = {scv.x, scv.y, scv.z, scv.w};

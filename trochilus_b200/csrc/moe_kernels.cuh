@@ -1,34 +1,47 @@
-// moe_kernels.cuh: the decode-regime MoE layer as four kernels on one stream.
+// moe_kernels.cuh: Trochilus's OLMoE MoE layer on the GPU, exact, as a few kernels on one stream.
 //
-//   trx_k_router   router logits (16-lane contract), then in the last block to finish: the softmax
-//                  (correctly rounded exp), top-k by repeated argmax (ties to the lower id), sort of the
-//                  k by id, and the stable counting sort of the (token, slot) rows by expert; extra
+//   trx_k_router   router logits under the 16-lane contract (the expert row and the inputs staged in shared
+//                  memory, the lane chains fed from registers); for up to TRX_ROUTE_FUSED_MAX tokens the last
+//                  router block to finish also routes every token (softmax with the correctly rounded exp,
+//                  top-k, ids sorted) and runs the stable counting sort of the (token, slot) rows; extra
 //                  blocks prepare each token's input row for the expert products
-//   trx_k_gateup   per (expert, block of rows): gate and up dots of every row of the expert's segment,
-//                  SwiGLU fused, h written (natural order, or the LC order the lane-contract down reads)
+//   trx_k_route / trx_k_sort / trx_k_prep_tokens   the same steps as separate kernels for longer passes
+//   trx_k_gateup   gate and up rows of the routed experts streamed through shared memory by 1-D TMA bulk
+//                  copies; SwiGLU fused; h written in the order the down kernel reads
 //   trx_k_prep     Q4_K down only: h rows prepared for Q4_K's integer definition
-//   trx_k_down     per (expert, block of output rows): down dots into h3; the last block to finish a
-//                  block of output rows adds the k expert outputs of every token in increasing expert
-//                  id and adds the sum to the residual, exactly Trochilus's mix_body
+//   trx_k_down     down rows streamed the same way into h3; the last CTA to finish a block of 16 output rows
+//                  adds every token's k expert outputs in increasing expert id and adds the sum to the
+//                  residual (Trochilus's mix_body)
 //
-// Trochilus references: forward_layer's MoE block src/models/olmoe.c:1845-1933; route_token /
-// top_experts olmoe.c:1455-1502; the counting sort olmoe.c:1850-1861; tr_softmax
-// src/kernels/kernels.c:1377-1388; SwiGLU kernels.c:1397-1421; mix_body olmoe.c:1432-1446.
+// Work split of the streaming kernels: the routed experts' rows form one virtual row space (slot i of the
+// active experts owns rows [i R, (i + 1) R)); CTA c takes the contiguous range [c V / G, (c + 1) V / G), so
+// every CTA streams the same number of rows (+-1) whatever the routing, and cuts it into chunks that do not
+// cross an expert (nor, for the down, a 16-row combine block). A CTA arms up to TRX_STAGES chunks at once.
+//
+// Trochilus references: forward_layer's MoE block src/models/olmoe.c:1845-1933; route_token / top_experts
+// olmoe.c:1455-1502; the counting sort olmoe.c:1850-1861; tr_softmax src/kernels/kernels.c:1377-1388;
+// SwiGLU kernels.c:1397-1421; mix_body olmoe.c:1432-1446.
 #pragma once
 #include <cstdint>
+#include "bulk.cuh"
 #include "common.cuh"
 #include "expf.cuh"
 #include "layouts.cuh"
 
 #define TRX_MAX_EXPERTS 64
 #define TRX_MAX_USED 32
-#define TRX_GU_ROWS 32   // gate/up rows per work item (8 warps x 4)
-#define TRX_DN_ROWS 64   // down output rows per work item
+#define TRX_GU_CHUNK 8          // gate/up rows a chunk (a warp per row: its gate and up rows)
+#define TRX_DN_CHUNK 16         // down output rows a chunk (a half-warp per row); the combine block
+#define TRX_STAGES 4            // chunks a CTA has in flight
+#define TRX_TOK_GROUP 8         // a segment's rows per epilogue pass
+#define TRX_ROUTE_FUSED_MAX 64  // tokens up to which the router kernel routes in its last block
+#define TRX_TOK_STAGE 16        // tokens whose inputs a router block stages at once
+#define TRX_WAIT_NS 2000000000ull
 
 struct TrxLayer {
     int router_type, gate_type, up_type, down_type;
     const uint8_t *router;
-    const float *router_bias; // NULL: none
+    const float *router_bias;        // NULL: none
     const uint8_t *gate, *up, *down; // n_expert matrices each
     int64_t gate_mb, up_mb, down_mb; // bytes per expert matrix
 };
@@ -38,43 +51,47 @@ struct TrxShape {
 };
 
 struct TrxWork {
-    float *logits;      // [T][E]
-    int32_t *sel_id;    // [R]
-    float *sel_w;       // [R]
-    int32_t *offsets;   // [E + 1]
-    int32_t *place;     // [R]
-    int32_t *xmap;      // [R] token of grouped row p
-    int32_t *active;    // [E]
-    int32_t *n_active;  // [1]
-    uint32_t *route_cnt;  // [1]
-    uint32_t *comb_cnt;   // [H / TRX_DN_ROWS]
-    float *x_lc;        // [T][H]
-    uint32_t *xq;       // [T][H]
-    double *xq_bf;      // [T][H / 32]
-    double *xq_sc;      // [T][H / 256]
-    float *h;           // [R][F]
-    uint32_t *hq;       // [R][F]
-    double *hq_bf;      // [R][F / 32]
-    double *hq_sc;      // [R][F / 256]
-    float *h3;          // [R][H]
-    int64_t *out_sel_id;  // optional outputs (NULL: not written)
+    float *logits;       // [T][E]
+    int32_t *sel_id;     // [R]
+    float *sel_w;        // [R]
+    int32_t *offsets;    // [E + 1]
+    int32_t *place;      // [R]
+    int32_t *xmap;       // [R] token of grouped row p
+    int32_t *active;     // [E]
+    int32_t *n_active;   // [1]
+    uint32_t *route_cnt; // [1]
+    uint32_t *comb_cnt;  // [H / TRX_DN_CHUNK]
+    int32_t *err;        // [1] nonzero: a kernel gave up waiting for its copies
+    float *x_lc;         // [T][H]
+    uint32_t *xq;        // [T][H]
+    double *xq_bf;       // [T][H / 32]
+    double *xq_sc;       // [T][H / 256]
+    float *h;            // [R][F]
+    uint32_t *hq;        // [R][F]
+    double *hq_bf;       // [R][F / 32]
+    double *hq_sc;       // [R][F / 256]
+    float *h3;           // [R][H]
+    int64_t *out_sel_id; // optional outputs (NULL: not written)
     float *out_sel_w;
     int64_t *out_offsets;
     int64_t *out_place;
     float *out_logits;
 };
 
-__device__ __forceinline__ bool trx_lc_type(int t) { return t == TRX_Q8_0 || t == TRX_Q6_K; }
-
 // ---------------------------------------------------------------------------------------------
-// router + route + dispatch
+// routing
 
+// One token's routing by one warp: softmax over E <= 64 logits (lane i holds i and i + 32), the k experts,
+// their weights, written sorted by id. After the softmax the probabilities are either all NaN (a NaN or an
+// infinite logit, or every logit -inf) or none is; the reference's repeated argmax (first untaken id when it
+// is NaN, else the largest, ties to the lower id) then picks ids 0..k-1 in the first case and the k largest
+// by (value, -id) in the second. The rank of each value among all E gives the latter directly.
 __device__ void trx_route_token(const float *__restrict__ logits, int E, int k, int norm_topk, int lane,
-                                int32_t *ids_out, float *w_out) {
+                                float *__restrict__ sp, int32_t *ids_out, float *w_out) {
     const bool ok0 = lane < E, ok1 = lane + 32 < E;
     const float v0 = ok0 ? __ldcg(logits + lane) : 0.0f, v1 = ok1 ? __ldcg(logits + lane + 32) : 0.0f;
-    // max: the reference's serial scan from x[0] with strict > keeps x[0] when it is a NaN, else it is the
-    // largest non-NaN value (which x[0] is one of)
+    // max: the serial scan from x[0] with strict > keeps x[0] when it is a NaN, else it is the largest
+    // non-NaN value (x[0] among them)
     float m = -__int_as_float(0x7f800000);
     if (ok0 && v0 == v0) m = fmaxf(m, v0);
     if (ok1 && v1 == v1) m = fmaxf(m, v1);
@@ -84,79 +101,65 @@ __device__ void trx_route_token(const float *__restrict__ logits, int E, int k, 
     if (x0 != x0) m = x0;
     const float e0 = ok0 ? trx_expf(__fsub_rn(v0, m)) : 0.0f;
     const float e1 = ok1 ? trx_expf(__fsub_rn(v1, m)) : 0.0f;
-    // lane sum: lane l (< 16) adds elements l, l+16, l+32, l+48 in order from +0
+    // 16-lane sum: lane l (< 16) adds elements l, l+16, l+32, l+48 in order from +0 (absent ones are +0)
     const float b = __shfl_sync(0xffffffffu, e0, (lane & 15) + 16);
     const float d = __shfl_sync(0xffffffffu, e1, (lane & 15) + 16);
     float acc = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(0.0f, e0), b), e1), d);
     acc = trx_lane_tree16(acc);
     const float sum = __shfl_sync(0xffffffffu, acc, 0);
     const float p0 = __fdiv_rn(e0, sum), p1 = __fdiv_rn(e1, sum);
-    bool t0 = !ok0, t1 = !ok1; // taken (or absent)
-    int ids[TRX_MAX_USED];
-    float ws[TRX_MAX_USED];
-    for (int s = 0; s < k; s++) {
-        const unsigned u0 = __ballot_sync(0xffffffffu, !t0), u1 = __ballot_sync(0xffffffffu, !t1);
-        const int f = u0 ? __ffs(u0) - 1 : 32 + __ffs(u1) - 1; // first untaken id
-        const float pf = __shfl_sync(0xffffffffu, f < 32 ? p0 : p1, f & 31);
-        int best;
-        if (pf != pf) {
-            best = f;
-        } else {
-            // largest non-NaN untaken, lowest id among equals
-            float bv = 0.0f;
-            int bi = 1 << 30;
-            if (!t0 && p0 == p0) { bv = p0; bi = lane; }
-            if (!t1 && p1 == p1 && (bi == (1 << 30) || p1 > bv)) { bv = p1; bi = lane + 32; }
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-                const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-                const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-                const bool take = oi != (1 << 30) && (bi == (1 << 30) || ov > bv || (ov == bv && oi < bi));
-                if (take) { bv = ov; bi = oi; }
-            }
-            best = bi;
+    const bool any_nan = __any_sync(0xffffffffu, (ok0 && p0 != p0) || (ok1 && p1 != p1));
+    int r0 = lane, r1 = lane + 32; // selection rank of elements lane and lane + 32
+    if (!any_nan) {
+        sp[lane] = p0;
+        sp[lane + 32] = p1;
+        __syncwarp();
+        r0 = 0;
+        r1 = 0;
+        for (int j = 0; j < E; j++) {
+            const float q = sp[j];
+            r0 += (q > p0) || (q == p0 && j < lane);
+            r1 += (q > p1) || (q == p1 && j < lane + 32);
         }
-        const float pb = __shfl_sync(0xffffffffu, best < 32 ? p0 : p1, best & 31);
-        if (best == lane) t0 = true;
-        if (best == lane + 32) t1 = true;
-        ids[s] = best;
-        ws[s] = pb;
+        __syncwarp();
     }
-    if (lane == 0) {
-        if (norm_topk) {
-            float sm = 0.0f;
-            for (int s = 0; s < k; s++) sm = __fadd_rn(sm, ws[s]);
-            for (int s = 0; s < k; s++) ws[s] = __fdiv_rn(ws[s], sm);
-        }
-        for (int i = 1; i < k; i++) { // insertion sort by id
-            const int id = ids[i];
-            const float w = ws[i];
-            int j = i - 1;
-            while (j >= 0 && ids[j] > id) {
-                ids[j + 1] = ids[j];
-                ws[j + 1] = ws[j];
-                j--;
-            }
-            ids[j + 1] = id;
-            ws[j + 1] = w;
-        }
-        for (int s = 0; s < k; s++) {
-            ids_out[s] = ids[s];
-            w_out[s] = ws[s];
-        }
+    const bool s0 = ok0 && r0 < k, s1 = ok1 && r1 < k;
+    float w0 = p0, w1 = p1;
+    if (norm_topk) { // the weights summed in selection order, then each divided by the sum
+        if (s0) sp[64 + r0] = p0;
+        if (s1) sp[64 + r1] = p1;
+        __syncwarp();
+        float sm = 0.0f;
+        for (int i = 0; i < k; i++) sm = __fadd_rn(sm, sp[64 + i]);
+        __syncwarp();
+        w0 = __fdiv_rn(p0, sm);
+        w1 = __fdiv_rn(p1, sm);
+    }
+    const unsigned b0 = __ballot_sync(0xffffffffu, s0), b1 = __ballot_sync(0xffffffffu, s1);
+    const unsigned lt = (1u << lane) - 1u;
+    if (s0) {
+        const int slot = __popc(b0 & lt);
+        ids_out[slot] = lane;
+        w_out[slot] = w0;
+    }
+    if (s1) {
+        const int slot = __popc(b0) + __popc(b1 & lt);
+        ids_out[slot] = lane + 32;
+        w_out[slot] = w1;
     }
 }
 
-// Stable counting sort of R rows by expert, by one block of 256 threads (8 warps). place[j] = the
-// row's position in the grouped order: its expert's start plus the rows of that expert before j.
+// Stable counting sort of R rows by expert, by one block of WARPS warps. place[j] = the row's position in
+// the grouped order: its expert's start plus the rows of that expert before j.
+template <int WARPS>
 __device__ void trx_block_counting_sort(const int32_t *__restrict__ sel_id, int R, int E, int k, TrxWork w) {
     __shared__ int cnt[TRX_MAX_EXPERTS + 1];
     __shared__ int run[TRX_MAX_EXPERTS];
-    __shared__ int wc[8][TRX_MAX_EXPERTS];
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    for (int e = tid; e <= E; e += blockDim.x) cnt[e] = 0;
+    __shared__ int wc[WARPS][TRX_MAX_EXPERTS];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nt = WARPS * 32;
+    for (int e = tid; e <= E; e += nt) cnt[e] = 0;
     __syncthreads();
-    for (int j = tid; j < R; j += blockDim.x) atomicAdd(&cnt[sel_id[j]], 1);
+    for (int j = tid; j < R; j += nt) atomicAdd(&cnt[sel_id[j]], 1);
     __syncthreads();
     if (tid == 0) {
         int acc = 0, na = 0;
@@ -173,10 +176,10 @@ __device__ void trx_block_counting_sort(const int32_t *__restrict__ sel_id, int 
         *w.n_active = na;
     }
     __syncthreads();
-    for (int base = 0; base < R; base += blockDim.x) {
+    for (int base = 0; base < R; base += nt) {
         const int j = base + tid;
         const int e = j < R ? sel_id[j] : -1;
-        for (int i = tid; i < 8 * TRX_MAX_EXPERTS; i += blockDim.x) (&wc[0][0])[i] = 0;
+        for (int i = tid; i < WARPS * TRX_MAX_EXPERTS; i += nt) (&wc[0][0])[i] = 0;
         __syncthreads();
         const unsigned peers = __match_any_sync(0xffffffffu, e);
         const int rank = __popc(peers & ((1u << lane) - 1u));
@@ -190,68 +193,108 @@ __device__ void trx_block_counting_sort(const int32_t *__restrict__ sel_id, int 
             if (w.out_place) w.out_place[j] = pos;
         }
         __syncthreads();
-        for (int ee = tid; ee < E; ee += blockDim.x) {
+        for (int ee = tid; ee < E; ee += nt) {
             int s = 0;
-            for (int v = 0; v < 8; v++) s += wc[v][ee];
+            for (int v = 0; v < WARPS; v++) s += wc[v][ee];
             run[ee] += s;
         }
         __syncthreads();
     }
 }
 
-// grid: E router blocks + T prep blocks; 256 threads
-__global__ void __launch_bounds__(256) trx_k_router(TrxLayer L, TrxShape S, const float *__restrict__ normed, int T,
-                                                    TrxWork w) {
-    extern __shared__ float srow[]; // H floats
-    const int tid = threadIdx.x, lane = tid & 31;
-    const int E = S.E, H = S.H;
-    if ((int)blockIdx.x >= E) { // input preparation for the gate/up products
-        const int t = blockIdx.x - E;
-        const float *x = normed + (int64_t)t * H;
-        if (L.gate_type == TRX_Q4_K) {
-            const int nsb = H / 256;
-            for (int s = tid >> 5; s < nsb; s += blockDim.x >> 5)
-                trx_prep_q4x_block(x + 256 * s, w.xq + (int64_t)t * H + 256 * s, w.xq_bf + (int64_t)t * (H / 32) + 8 * s,
-                                   w.xq_sc + (int64_t)t * (H / 256) + s, lane);
-        } else {
-            for (int kk = tid; kk < H; kk += blockDim.x) w.x_lc[(int64_t)t * H + trx_lc_pos(kk)] = x[kk];
-        }
-        return;
+// one token's input row prepared for the gate/up products (one block)
+__device__ void trx_prep_token(const TrxLayer &L, const TrxShape &S, const float *__restrict__ normed, int t,
+                               TrxWork &w) {
+    const int tid = threadIdx.x, lane = tid & 31, H = S.H;
+    const float *x = normed + (int64_t)t * H;
+    if (L.gate_type == TRX_Q4_K) {
+        const int nsb = H / 256;
+        for (int s = tid >> 5; s < nsb; s += blockDim.x >> 5)
+            trx_prep_q4x_block(x + 256 * s, w.xq + (int64_t)t * H + 256 * s, w.xq_bf + (int64_t)t * (H / 32) + 8 * s,
+                               w.xq_sc + (int64_t)t * (H / 256) + s, lane);
+    } else {
+        for (int kk = tid; kk < H; kk += blockDim.x) w.x_lc[(int64_t)t * H + trx_lc_pos(kk)] = x[kk];
     }
-    const int e = blockIdx.x;
+}
+
+// Router logits of expert e for tokens [g_begin, g_end) by one block of 256 threads; sdyn: (1 +
+// min(tokens, TRX_TOK_STAGE)) * H floats of shared memory.
+__device__ void trx_router_block(const TrxLayer &L, const TrxShape &S, const float *__restrict__ normed, int e,
+                                 int g_begin, int g_end, TrxWork &w, float *sdyn) {
+    const int tid = threadIdx.x;
+    const int E = S.E, H = S.H;
+    float *srow = sdyn, *sx = sdyn + H;
     const int64_t rb = trx_row_bytes(L.router_type, H);
     const uint8_t *row = L.router + e * rb;
     for (int kk = tid; kk < H; kk += blockDim.x)
-        srow[kk] = L.router_type == TRX_F32 ? __ldg(reinterpret_cast<const float *>(row) + kk)
-                                            : trx_bf16(__ldg(reinterpret_cast<const uint16_t *>(row) + kk));
-    __syncthreads();
+        srow[trx_lc_pos(kk)] = L.router_type == TRX_F32 ? __ldg(reinterpret_cast<const float *>(row) + kk)
+                                                        : trx_bf16(__ldg(reinterpret_cast<const uint16_t *>(row) + kk));
     const int tg = tid >> 4, l = tid & 15;
     const float bias = L.router_bias ? L.router_bias[e] : 0.0f;
-    for (int t0 = 0; t0 < T; t0 += 16) {
-        const int t = t0 + tg < T ? t0 + tg : T - 1;
-        const float *x = normed + (int64_t)t * H;
+    const int nch = H / 256;
+    for (int g0 = g_begin; g0 < g_end; g0 += TRX_TOK_STAGE) {
+        const int ng = min(TRX_TOK_STAGE, g_end - g0);
+        __syncthreads();
+        for (int i = tid; i < ng * H / 4; i += blockDim.x) { // inputs of the group, LC order
+            const int tk = (4 * i) / H, kk = (4 * i) % H;
+            const float4 v = *reinterpret_cast<const float4 *>(normed + (int64_t)(g0 + tk) * H + kk);
+            float *dst = sx + tk * H;
+            dst[trx_lc_pos(kk)] = v.x;
+            dst[trx_lc_pos(kk + 1)] = v.y;
+            dst[trx_lc_pos(kk + 2)] = v.z;
+            dst[trx_lc_pos(kk + 3)] = v.w;
+        }
+        __syncthreads();
+        const int tk = tg < ng ? tg : 0;
+        const float *xs = sx + tk * H + 4 * l, *ws = srow + 4 * l;
         float acc = 0.0f;
-        for (int kk = l; kk < H; kk += 16) acc = __fadd_rn(acc, __fmul_rn(srow[kk], x[kk]));
+        for (int i = 0; i < nch; i++) {
+            float wv[16], xv[16];
+#pragma unroll
+            for (int q = 0; q < 4; q++) {
+                const float4 a = *reinterpret_cast<const float4 *>(ws + 256 * i + 64 * q);
+                const float4 c = *reinterpret_cast<const float4 *>(xs + 256 * i + 64 * q);
+                wv[4 * q] = a.x; wv[4 * q + 1] = a.y; wv[4 * q + 2] = a.z; wv[4 * q + 3] = a.w;
+                xv[4 * q] = c.x; xv[4 * q + 1] = c.y; xv[4 * q + 2] = c.z; xv[4 * q + 3] = c.w;
+            }
+#pragma unroll
+            for (int m = 0; m < 16; m++) acc = __fadd_rn(acc, __fmul_rn(wv[m], xv[m]));
+        }
         acc = trx_lane_tree16(acc);
-        if (l == 0 && t0 + tg < T) {
+        if (l == 0 && tg < ng) {
             const float v = L.router_bias ? __fadd_rn(acc, bias) : acc;
-            w.logits[(int64_t)t * E + e] = v;
-            if (w.out_logits) w.out_logits[(int64_t)t * E + e] = v;
+            w.logits[(int64_t)(g0 + tg) * E + e] = v;
+            if (w.out_logits) w.out_logits[(int64_t)(g0 + tg) * E + e] = v;
         }
     }
-    // the last router block to finish routes every token
-    __shared__ int s_last;
-    __syncthreads();
-    if (tid == 0) {
-        __threadfence();
-        s_last = atomicAdd(w.route_cnt, 1u) == (unsigned)(E - 1);
+}
+
+// grid.x: E router blocks (+ T prep blocks when fused); grid.y: token groups of TRX_TOK_STAGE (unfused).
+// Dynamic shared memory: (1 + min(T, TRX_TOK_STAGE)) * H floats.
+__global__ void __launch_bounds__(256) trx_k_router(TrxLayer L, TrxShape S, const float *__restrict__ normed, int T,
+                                                    TrxWork w, int fused) {
+    extern __shared__ __align__(16) float sdyn[];
+    const int tid = threadIdx.x, lane = tid & 31;
+    const int E = S.E;
+    if ((int)blockIdx.x >= E) {
+        trx_prep_token(L, S, normed, blockIdx.x - E, w);
+        return;
     }
+    const int g_begin = fused ? 0 : blockIdx.y * TRX_TOK_STAGE, g_end = fused ? T : min(T, g_begin + TRX_TOK_STAGE);
+    trx_router_block(L, S, normed, blockIdx.x, g_begin, g_end, w, sdyn);
+    if (!fused) return;
+    // the last router block to finish routes every token and sorts the rows
+    __shared__ int s_last;
+    __shared__ float sp[8][96];
+    __threadfence(); // every writer's logits visible device-wide before the block is counted
+    __syncthreads();
+    if (tid == 0) s_last = atomicAdd(w.route_cnt, 1u) == (unsigned)(E - 1);
     __syncthreads();
     if (!s_last) return;
     __threadfence();
     const int warp = tid >> 5, k = S.k;
     for (int t = warp; t < T; t += blockDim.x >> 5)
-        trx_route_token(w.logits + (int64_t)t * E, E, k, S.norm_topk, lane, w.sel_id + (int64_t)t * k,
+        trx_route_token(w.logits + (int64_t)t * E, E, k, S.norm_topk, lane, sp[warp], w.sel_id + (int64_t)t * k,
                         w.sel_w + (int64_t)t * k);
     __syncthreads();
     const int R = T * k;
@@ -260,8 +303,31 @@ __global__ void __launch_bounds__(256) trx_k_router(TrxLayer L, TrxShape S, cons
             w.out_sel_id[j] = w.sel_id[j];
             w.out_sel_w[j] = w.sel_w[j];
         }
-    trx_block_counting_sort(w.sel_id, R, E, k, w);
+    trx_block_counting_sort<8>(w.sel_id, R, E, k, w);
     if (tid == 0) *w.route_cnt = 0u;
+}
+
+// longer passes: a warp per token
+__global__ void __launch_bounds__(256) trx_k_route(TrxShape S, int T, TrxWork w) {
+    __shared__ float sp[8][96];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, t = blockIdx.x * 8 + warp;
+    if (t >= T) return;
+    trx_route_token(w.logits + (int64_t)t * S.E, S.E, S.k, S.norm_topk, lane, sp[warp], w.sel_id + (int64_t)t * S.k,
+                    w.sel_w + (int64_t)t * S.k);
+    __syncwarp();
+    if (w.out_sel_id && lane < S.k) {
+        w.out_sel_id[(int64_t)t * S.k + lane] = w.sel_id[(int64_t)t * S.k + lane];
+        w.out_sel_w[(int64_t)t * S.k + lane] = w.sel_w[(int64_t)t * S.k + lane];
+    }
+}
+
+__global__ void __launch_bounds__(1024) trx_k_sort(TrxShape S, int T, TrxWork w) {
+    trx_block_counting_sort<32>(w.sel_id, T * S.k, S.E, S.k, w);
+}
+
+__global__ void __launch_bounds__(256) trx_k_prep_tokens(TrxLayer L, TrxShape S, const float *__restrict__ normed,
+                                                         TrxWork w) {
+    trx_prep_token(L, S, normed, blockIdx.x, w);
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -273,33 +339,35 @@ __device__ __forceinline__ float trx_silu_mul(float g, float u) {
     return __fmul_rn(silu, u);
 }
 
-// Q4_K row of 8 blocks (2048 columns) by one warp: returns float(sum_s v_s) in every lane
+// Q4_K row of 8 blocks (2048 columns) by one warp: float(sum_s v_s) in every lane
+template <bool SM, bool CG = false>
 __device__ __forceinline__ float trx_q4k_row8(const uint8_t *__restrict__ row, const TrxQ4X &X,
                                               const double *__restrict__ bf, const double *__restrict__ sc, int lane) {
     const int s = lane >> 2, c = lane & 3;
     const uint8_t *blk = row + 144 * s;
-    const uint4 hdr = __ldg(reinterpret_cast<const uint4 *>(blk));
-    const uint4 q0 = __ldg(reinterpret_cast<const uint4 *>(blk + 16 + 32 * c));
-    const uint4 q1 = __ldg(reinterpret_cast<const uint4 *>(blk + 32 + 32 * c));
+    const uint4 hdr = trx_ld<SM, uint4>(blk);
+    const uint4 q0 = trx_ld<SM, uint4>(blk + 16 + 32 * c);
+    const uint4 q1 = trx_ld<SM, uint4>(blk + 32 + 32 * c);
     int64_t T = trx_q4k_chunk_T(hdr, q0, q1, c, X);
     T += trx_shfl_xor64(T, 1);
     T += trx_shfl_xor64(T, 2);
     double v = 0.0;
-    if (c == 0) v = trx_q4k_finish(hdr, T, bf + 8 * s, sc[s]);
+    if (c == 0) v = trx_q4k_finish<CG>(hdr, T, bf + 8 * s, CG ? __ldcg(sc + s) : sc[s]);
     double y = 0.0;
 #pragma unroll
     for (int i = 0; i < 8; i++) y = __dadd_rn(y, trx_shfl_d(v, 4 * i));
     return __double2float_rn(y);
 }
 
-// Q4_K rows of 4 blocks (1024 columns), two per warp (half-warp each): returns the half's row value
+// Q4_K rows of 4 blocks (1024 columns), a half-warp each: the half's row value
+template <bool SM>
 __device__ __forceinline__ float trx_q4k_row4(const uint8_t *__restrict__ row, const TrxQ4X &X,
                                               const double *__restrict__ bf, const double *__restrict__ sc, int lane) {
     const int s = (lane >> 2) & 3, c = lane & 3;
     const uint8_t *blk = row + 144 * s;
-    const uint4 hdr = __ldg(reinterpret_cast<const uint4 *>(blk));
-    const uint4 q0 = __ldg(reinterpret_cast<const uint4 *>(blk + 16 + 32 * c));
-    const uint4 q1 = __ldg(reinterpret_cast<const uint4 *>(blk + 32 + 32 * c));
+    const uint4 hdr = trx_ld<SM, uint4>(blk);
+    const uint4 q0 = trx_ld<SM, uint4>(blk + 16 + 32 * c);
+    const uint4 q1 = trx_ld<SM, uint4>(blk + 32 + 32 * c);
     int64_t T = trx_q4k_chunk_T(hdr, q0, q1, c, X);
     T += trx_shfl_xor64(T, 1);
     T += trx_shfl_xor64(T, 2);
@@ -312,51 +380,118 @@ __device__ __forceinline__ float trx_q4k_row4(const uint8_t *__restrict__ row, c
     return __double2float_rn(y);
 }
 
+// the CTA's range of the virtual row space [a, b), V = n_active * rows_per_expert
+__device__ __forceinline__ void trx_cta_range(int64_t V, int64_t &a, int64_t &b) {
+    a = V * blockIdx.x / gridDim.x;
+    b = V * (blockIdx.x + 1) / gridDim.x;
+}
+
+// on a timed-out wait: record it, wait (bounded) for this CTA's other copies in flight, leave
+__device__ __forceinline__ void trx_bail(TrxWork &w, uint64_t *bar, int from, int issued) {
+    if (threadIdx.x == 0) {
+        atomicExch(w.err, 1);
+        for (int q = from; q < issued; q++) trx_mbar_wait(&bar[q % TRX_STAGES], (q / TRX_STAGES) & 1, TRX_WAIT_NS);
+    }
+    __syncthreads();
+}
+
+// GT: Q4_K or Q8_0 (gate and up share it). Dynamic shared memory: TRX_STAGES * 2 * TRX_GU_CHUNK rows + barriers.
 template <int GT, bool DOWN_LC>
 __global__ void __launch_bounds__(256) trx_k_gateup(TrxLayer L, TrxShape S, TrxWork w) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ float res[2][TRX_TOK_GROUP][TRX_GU_CHUNK];
+    constexpr int CH = TRX_GU_CHUNK;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int H = S.H, F = S.F;
-    const int nrb = F / TRX_GU_ROWS;
-    const int n_items = *w.n_active * nrb;
+    const int rb = GT == TRX_Q4_K ? H / 256 * 144 : H / 32 * 34;
+    const int half = CH * rb;
+    uint64_t *bar = reinterpret_cast<uint64_t *>(smem + TRX_STAGES * 2 * half);
+    const int n_act = *w.n_active;
+    int64_t a, b;
+    trx_cta_range((int64_t)n_act * F, a, b);
+    if (tid == 0) {
+        for (int s = 0; s < TRX_STAGES; s++) trx_mbar_init(&bar[s], 1);
+        trx_fence_barrier_init();
+    }
+    __syncthreads();
+    auto chunk_end = [&](int64_t v) { return min(min(v + CH, b), (v / F + 1) * F); };
+    int64_t issue_v = a;
+    int issued = 0;
+    auto issue = [&]() { // thread 0
+        const int64_t ve = chunk_end(issue_v);
+        const int e = w.active[issue_v / F], r0 = (int)(issue_v % F), n = (int)(ve - issue_v);
+        const int s = issued % TRX_STAGES;
+        uint8_t *dst = smem + s * 2 * half;
+        trx_mbar_expect_tx(&bar[s], 2u * n * rb);
+        trx_bulk_g2s(dst, L.gate + e * L.gate_mb + (int64_t)r0 * rb, n * rb, &bar[s]);
+        trx_bulk_g2s(dst + half, L.up + e * L.up_mb + (int64_t)r0 * rb, n * rb, &bar[s]);
+        issue_v = ve;
+        issued++;
+    };
+    if (tid == 0)
+        for (int q = 0; q < TRX_STAGES && issue_v < b; q++) issue();
     int cur_t = -1;
     TrxQ4X X;
-    for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
-        const int e = w.active[item / nrb], rb = item % nrb;
+    int j = 0;
+    for (int64_t v = a; v < b; j++) {
+        const int64_t ve = chunk_end(v);
+        const int e = w.active[v / F], r0 = (int)(v % F), n = (int)(ve - v);
         const int p0 = w.offsets[e], p1 = w.offsets[e + 1];
-        const uint8_t *G = L.gate + (int64_t)e * L.gate_mb, *U = L.up + (int64_t)e * L.up_mb;
-        for (int rr = warp; rr < TRX_GU_ROWS; rr += 8) {
-            const int r = rb * TRX_GU_ROWS + rr;
-            for (int p = p0; p < p1; p++) {
-                const int t = w.xmap[p];
-                float hv;
-                if (GT == TRX_Q4_K) {
-                    // H == 2048: one row per warp
-                    if (t != cur_t) trx_q4x_load(w.xq + (int64_t)t * H + 256 * (lane >> 2), lane & 3, X);
-                    cur_t = t;
-                    const float g = trx_q4k_row8(G + (int64_t)r * (H / 256) * 144, X, w.xq_bf + (int64_t)t * (H / 32),
-                                                 w.xq_sc + (int64_t)t * (H / 256), lane);
-                    const float u = trx_q4k_row8(U + (int64_t)r * (H / 256) * 144, X, w.xq_bf + (int64_t)t * (H / 32),
-                                                 w.xq_sc + (int64_t)t * (H / 256), lane);
-                    hv = trx_silu_mul(g, u);
-                } else {
-                    // half 0: gate row r, half 1: up row r
-                    const uint8_t *M = lane < 16 ? G : U;
-                    const float v = trx_q8l_dot(M + (int64_t)r * (H / 256) * 272, w.x_lc + (int64_t)t * H, H / 256,
-                                                lane & 15);
-                    const float u = __shfl_sync(0xffffffffu, v, 16);
-                    hv = trx_silu_mul(v, u);
-                }
-                if (lane == 0) w.h[(int64_t)p * F + (DOWN_LC ? trx_lc_pos(r) : r)] = hv;
-            }
+        const int s = j % TRX_STAGES;
+        if (GT == TRX_Q4_K && warp < n && w.xmap[p0] != cur_t) { // the first row's input, while the copy lands
+            cur_t = w.xmap[p0];
+            trx_q4x_load(w.xq + (int64_t)cur_t * H + 256 * (lane >> 2), lane & 3, X);
         }
+        const bool ok = trx_mbar_wait(&bar[s], (j / TRX_STAGES) & 1, TRX_WAIT_NS);
+        if (__syncthreads_or(!ok)) {
+            trx_bail(w, bar, j, issued);
+            return;
+        }
+        const uint8_t *gs = smem + s * 2 * half, *us = gs + half;
+        for (int pg = p0; pg < p1; pg += TRX_TOK_GROUP) {
+            const int ng = min(TRX_TOK_GROUP, p1 - pg);
+            for (int q = 0; q < ng; q++) {
+                const int t = w.xmap[pg + q];
+                if (GT == TRX_Q4_K) {
+                    if (warp < n) {
+                        if (t != cur_t) {
+                            cur_t = t;
+                            trx_q4x_load(w.xq + (int64_t)t * H + 256 * (lane >> 2), lane & 3, X);
+                        }
+                        const double *bf = w.xq_bf + (int64_t)t * (H / 32), *sc = w.xq_sc + (int64_t)t * (H / 256);
+                        const float g = trx_q4k_row8<true>(gs + warp * rb, X, bf, sc, lane);
+                        const float u = trx_q4k_row8<true>(us + warp * rb, X, bf, sc, lane);
+                        if (lane == 0) {
+                            res[0][q][warp] = g;
+                            res[1][q][warp] = u;
+                        }
+                    }
+                } else { // half-warp hw: row hw & 7 of matrix hw >> 3
+                    const int hw = tid >> 4, row = hw & 7, mat = hw >> 3;
+                    const float vv = trx_q8l_dot<true>((mat ? us : gs) + (row < n ? row : 0) * rb,
+                                                       w.x_lc + (int64_t)t * H, H / 256, lane & 15);
+                    if (row < n && (lane & 15) == 0) res[mat][q][row] = vv;
+                }
+            }
+            __syncthreads();
+            for (int i = tid; i < ng * n; i += blockDim.x) {
+                const int q = i / n, row = i % n, r = r0 + row;
+                w.h[(int64_t)(pg + q) * F + (DOWN_LC ? trx_lc_pos(r) : r)] = trx_silu_mul(res[0][q][row], res[1][q][row]);
+            }
+            __syncthreads();
+        }
+        if (tid == 0 && issue_v < b) { // stage s is free again
+            trx_fence_proxy_async();
+            issue();
+        }
+        v = ve;
     }
 }
 
 // ---------------------------------------------------------------------------------------------
 // Q4_K down input: every h row prepared (one warp per (row, 256-block))
-__global__ void __launch_bounds__(256) trx_k_prep(TrxShape S, const int *__restrict__ n_rows_dev, int R_max, TrxWork w) {
+__global__ void __launch_bounds__(256) trx_k_prep(TrxShape S, int R, TrxWork w) {
     const int F = S.F, nsb = F / 256;
-    const int R = n_rows_dev ? *n_rows_dev : R_max;
     const int lane = threadIdx.x & 31;
     const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int p = gw / nsb, s = gw % nsb;
@@ -366,69 +501,104 @@ __global__ void __launch_bounds__(256) trx_k_prep(TrxShape S, const int *__restr
 }
 
 // ---------------------------------------------------------------------------------------------
-// down + combine + residual
-
+// down + combine + residual. DT: Q4_K (F == 1024), Q8_0 or Q6_K. Dynamic shared memory: TRX_STAGES *
+// TRX_DN_CHUNK rows + barriers.
 template <int DT>
 __global__ void __launch_bounds__(256) trx_k_down(TrxLayer L, TrxShape S, TrxWork w, float *__restrict__ x_io, int T,
                                                   float *__restrict__ ffn_out) {
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int H = S.H, F = S.F, k = S.k;
-    const int nrb = H / TRX_DN_ROWS;
-    const int n_act = *w.n_active;
-    const int n_items = n_act * nrb;
+    extern __shared__ __align__(128) uint8_t smem[];
+    constexpr int CH = TRX_DN_CHUNK;
+    const int tid = threadIdx.x, lane = tid & 31, hw = tid >> 4;
+    const int H = S.H, F = S.F, k = S.k, nsb = F / 256;
+    const int rb = DT == TRX_Q4_K ? nsb * 144 : DT == TRX_Q6_K ? nsb * 208 : F / 32 * 34;
+    const int stage = CH * rb;
+    uint64_t *bar = reinterpret_cast<uint64_t *>(smem + TRX_STAGES * stage);
     __shared__ int s_last;
-    for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
-        const int e = w.active[item / nrb], rb = item % nrb;
+    const int n_act = *w.n_active;
+    int64_t a, b;
+    trx_cta_range((int64_t)n_act * H, a, b);
+    if (tid == 0) {
+        for (int s = 0; s < TRX_STAGES; s++) trx_mbar_init(&bar[s], 1);
+        trx_fence_barrier_init();
+    }
+    __syncthreads();
+    auto chunk_end = [&](int64_t v) { return min(b, (v / CH + 1) * CH); }; // H % CH == 0: never crosses an expert
+    int64_t issue_v = a;
+    int issued = 0;
+    auto issue = [&]() {
+        const int64_t ve = chunk_end(issue_v);
+        const int e = w.active[issue_v / H], d0 = (int)(issue_v % H), n = (int)(ve - issue_v);
+        const int s = issued % TRX_STAGES;
+        trx_mbar_expect_tx(&bar[s], (uint32_t)(n * rb));
+        trx_bulk_g2s(smem + s * stage, L.down + e * L.down_mb + (int64_t)d0 * rb, n * rb, &bar[s]);
+        issue_v = ve;
+        issued++;
+    };
+    if (tid == 0)
+        for (int q = 0; q < TRX_STAGES && issue_v < b; q++) issue();
+    int cur_p = -1;
+    TrxQ4X X;
+    int j = 0;
+    for (int64_t v = a; v < b; j++) {
+        const int64_t ve = chunk_end(v);
+        const int e = w.active[v / H], d0 = (int)(v % H), n = (int)(ve - v);
         const int p0 = w.offsets[e], p1 = w.offsets[e + 1];
-        const uint8_t *D = L.down + (int64_t)e * L.down_mb;
-        // two output rows per warp (a half-warp each): d = rb * 64 + 16 j + 2 warp + half
-        for (int p = p0; p < p1; p++) {
-            if (DT == TRX_Q4_K) { // F == 1024: 4 blocks a row
-                TrxQ4X X;
-                trx_q4x_load(w.hq + (int64_t)p * F + 256 * ((lane >> 2) & 3), lane & 3, X);
-#pragma unroll 1
-                for (int j = 0; j < TRX_DN_ROWS / 16; j++) {
-                    const int d = rb * TRX_DN_ROWS + 16 * j + 2 * warp + (lane >> 4);
-                    const float v = trx_q4k_row4(D + (int64_t)d * (F / 256) * 144, X, w.hq_bf + (int64_t)p * (F / 32),
-                                                 w.hq_sc + (int64_t)p * (F / 256), lane);
-                    if ((lane & 15) == 0) w.h3[(int64_t)p * H + d] = v;
-                }
-            } else {
-#pragma unroll 1
-                for (int j = 0; j < TRX_DN_ROWS / 16; j++) {
-                    const int d = rb * TRX_DN_ROWS + 16 * j + 2 * warp + (lane >> 4);
-                    float v;
-                    if (DT == TRX_Q8_0)
-                        v = trx_q8l_dot(D + (int64_t)d * (F / 256) * 272, w.h + (int64_t)p * F, F / 256, lane & 15);
-                    else
-                        v = trx_q6l_dot(D + (int64_t)d * (F / 256) * 208,
-                                        D + (int64_t)H * (F / 256) * 208 + (int64_t)d * (F / 256) * 2,
-                                        w.h + (int64_t)p * F, F / 256, lane & 15);
-                    if ((lane & 15) == 0) w.h3[(int64_t)p * H + d] = v;
-                }
-            }
+        const int s = j % TRX_STAGES;
+        if (DT == TRX_Q4_K && hw < n && p0 != cur_p) {
+            cur_p = p0;
+            trx_q4x_load(w.hq + (int64_t)p0 * F + 256 * ((lane >> 2) & 3), lane & 3, X);
         }
-        // the last block to finish this block of output rows (over all active experts) combines it
+        const bool ok = trx_mbar_wait(&bar[s], (j / TRX_STAGES) & 1, TRX_WAIT_NS);
+        if (__syncthreads_or(!ok)) {
+            trx_bail(w, bar, j, issued);
+            return;
+        }
+        const uint8_t *st = smem + s * stage;
+        const int row = hw < n ? hw : 0, d = d0 + row;
+        for (int p = p0; p < p1; p++) {
+            float vv;
+            if (DT == TRX_Q4_K) {
+                if (p != cur_p) {
+                    cur_p = p;
+                    trx_q4x_load(w.hq + (int64_t)p * F + 256 * ((lane >> 2) & 3), lane & 3, X);
+                }
+                vv = trx_q4k_row4<true>(st + row * rb, X, w.hq_bf + (int64_t)p * (F / 32), w.hq_sc + (int64_t)p * nsb,
+                                        lane);
+            } else if (DT == TRX_Q8_0) {
+                vv = trx_q8l_dot<true>(st + row * rb, w.h + (int64_t)p * F, nsb, lane & 15);
+            } else {
+                const uint8_t *dptr = L.down + e * L.down_mb + (int64_t)H * rb + (int64_t)d * nsb * 2;
+                vv = trx_q6l_dot<true>(st + row * rb, dptr, w.h + (int64_t)p * F, nsb, lane & 15);
+            }
+            if (hw < n && (lane & 15) == 0) w.h3[(int64_t)p * H + d] = vv;
+        }
+        // count this chunk's rows into its combine block; the CTA completing the block combines it
+        __threadfence();
         __syncthreads();
+        const int blk = d0 / CH;
         if (tid == 0) {
-            __threadfence();
-            s_last = atomicAdd(&w.comb_cnt[rb], 1u) == (unsigned)(n_act - 1);
+            const unsigned old = atomicAdd(&w.comb_cnt[blk], (unsigned)n);
+            s_last = old + (unsigned)n == (unsigned)(n_act * CH);
+            if (issue_v < b) { // stage s is free again
+                trx_fence_proxy_async();
+                issue();
+            }
         }
         __syncthreads();
         if (s_last) {
             __threadfence();
-            for (int i = tid; i < T * TRX_DN_ROWS; i += blockDim.x) {
-                const int t = i / TRX_DN_ROWS, d = rb * TRX_DN_ROWS + i % TRX_DN_ROWS;
+            for (int i = tid; i < T * CH; i += blockDim.x) {
+                const int t = i / CH, dd = blk * CH + i % CH;
                 float out = 0.0f;
-                for (int s = 0; s < k; s++) {
-                    const int j = t * k + s;
-                    out = __fadd_rn(out, __fmul_rn(w.sel_w[j], __ldcg(w.h3 + (int64_t)w.place[j] * H + d)));
+                for (int sl = 0; sl < k; sl++) {
+                    const int jj = t * k + sl;
+                    out = __fadd_rn(out, __fmul_rn(w.sel_w[jj], __ldcg(w.h3 + (int64_t)w.place[jj] * H + dd)));
                 }
-                if (ffn_out) ffn_out[(int64_t)t * H + d] = out;
-                x_io[(int64_t)t * H + d] = __fadd_rn(x_io[(int64_t)t * H + d], out);
+                if (ffn_out) ffn_out[(int64_t)t * H + dd] = out;
+                x_io[(int64_t)t * H + dd] = __fadd_rn(x_io[(int64_t)t * H + dd], out);
             }
-            if (tid == 0) w.comb_cnt[rb] = 0u;
+            if (tid == 0) w.comb_cnt[blk] = 0u;
         }
-        __syncthreads();
+        v = ve;
     }
 }

@@ -22,7 +22,8 @@ F32, F16, Q8_0, Q4_K, Q6_K, BF16 = 0, 1, 8, 12, 14, 30
 
 # every function include/trmoe.h declares
 EXPORTS = ["tr_gpu_moe_create", "tr_gpu_moe_free", "tr_gpu_moe_bytes", "tr_gpu_moe_set_layer", "tr_gpu_moe_layer",
-           "tr_gpu_moe_layer_dev", "tr_gpu_moe_launches", "tr_gpu_moe_profile", "tr_gpu_moe_profile_read", "trmoe_last_error", "tr_matmul", "tr_matmul_grouped",
+           "tr_gpu_moe_layer_dev", "tr_gpu_moe_launches", "tr_gpu_moe_profile", "tr_gpu_moe_profile_read",
+           "tr_gpu_moe_check", "tr_gpu_moe_layer_part", "trmoe_last_error", "tr_matmul", "tr_matmul_grouped",
            "tr_matmul_grouped_s", "tr_softmax", "tr_swiglu", "trmoe_kernel_cache_clear"]
 
 
@@ -64,6 +65,9 @@ def lib():
                                        C.POINTER(Outputs), C.c_void_p]
     L.tr_gpu_moe_launches.argtypes = [C.c_void_p, C.c_int64]
     L.tr_gpu_moe_profile.argtypes = [C.c_void_p, C.c_int]
+    L.tr_gpu_moe_check.argtypes = [C.c_void_p]
+    L.tr_gpu_moe_layer_part.argtypes = [C.c_void_p, C.c_int64, C.c_int, C.c_void_p, C.c_int64, C.c_void_p,
+                                        C.POINTER(Outputs), C.c_void_p]
     L.tr_gpu_moe_profile_read.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int]
     L.trmoe_last_error.restype = C.c_char_p
     L.tr_matmul.argtypes = [C.c_void_p, C.POINTER(TrMat), C.c_void_p, C.c_int64, C.c_void_p]
@@ -149,6 +153,12 @@ class GpuMoe:
         if rc != 0:
             raise RuntimeError(f"tr_gpu_moe_layer_dev: {last_error()}")
 
+    def layer_part(self, layer: int, part: int, normed_ptr: int, n_tok: int, x_ptr: int, stream: int = 0):
+        """tr_gpu_moe_layer_part: one of the four parts of a layer call (device pointers, enqueued only)."""
+        rc = lib().tr_gpu_moe_layer_part(self.h, layer, part, normed_ptr, n_tok, x_ptr, None, stream or None)
+        if rc != 0:
+            raise RuntimeError(f"tr_gpu_moe_layer_part: {last_error()}")
+
     ZONES = ("router", "gate_up", "act_prep", "down")
 
     def profile(self, on: bool):
@@ -161,6 +171,11 @@ class GpuMoe:
         if lib().tr_gpu_moe_profile_read(self.h, _p(ms), _p(calls), 4) != 0:
             raise RuntimeError(f"tr_gpu_moe_profile_read: {last_error()}")
         return {z: (float(ms[i]), int(calls[i])) for i, z in enumerate(self.ZONES)}
+
+    def check(self):
+        """tr_gpu_moe_check: wait for the stream; raise if a kernel gave up on a bounded wait."""
+        if lib().tr_gpu_moe_check(self.h) != 0:
+            raise RuntimeError(f"tr_gpu_moe_check: {last_error()}")
 
     def launches(self, n_tok: int) -> int:
         return int(lib().tr_gpu_moe_launches(self.h, n_tok))
@@ -203,6 +218,11 @@ def matmul(type_: int, rows: int, cols: int, w: np.ndarray, x: np.ndarray):
     if err:
         raise RuntimeError(f"tr_matmul: {err}")
     return y
+
+
+def kernel_cache_clear():
+    """trmoe_kernel_cache_clear: forget every weight the kernel-level calls uploaded."""
+    lib().trmoe_kernel_cache_clear()
 
 
 def softmax(x: np.ndarray) -> np.ndarray:
