@@ -124,6 +124,14 @@ TRMOE_API int tr_gpu_moe_profile_read(tr_gpu_moe *m, double *ms, int64_t *calls,
  * check (the device error flag, then cleared). 0, or -1 with a message. tr_gpu_moe_layer checks it itself. */
 TRMOE_API int tr_gpu_moe_check(tr_gpu_moe *m);
 
+/* Timeline of the fused kernel (the counterpart of Trochilus's TR_POOL_TRACE, src/base/threads.h:98-108): when
+ * on, every CTA of the fused kernel writes %globaltimer (ns) at its events into 64 slots: 0 start, 1 router or
+ * preparation work done, 2 routing seen, 3 copies armed, 4+j gate/up chunk j done (j < 16), 20+j down chunk j's
+ * inputs ready, 36+j down chunk j done, 52 end (0: no such event). tr_gpu_moe_trace_read waits for the stream and
+ * copies the last call's slots (ctas * 64 values, at most n) to host memory; returns the number of CTAs, or -1. */
+TRMOE_API int tr_gpu_moe_trace(tr_gpu_moe *m, int on);
+TRMOE_API int tr_gpu_moe_trace_read(tr_gpu_moe *m, uint64_t *slots, int64_t n);
+
 /* How many kernels one tr_gpu_moe_layer_dev call launches for n_tok tokens. */
 TRMOE_API int tr_gpu_moe_launches(const tr_gpu_moe *m, int64_t n_tok);
 

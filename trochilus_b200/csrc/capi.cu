@@ -156,6 +156,7 @@ struct tr_gpu_moe {
     int grid_gu = 0, grid_dn = 0, grid_fused = 0;
     size_t smem_gu = 0, smem_dn = 0, smem_fused = 0;
     TrxSync *sync = nullptr;
+    uint64_t *trace = nullptr;
     uint32_t epoch = 0;
     bool fused_ok = false;
     float *d_normed = nullptr, *d_x = nullptr;
@@ -220,7 +221,8 @@ static DownFn down_fn(int down_type) {
     return trx_k_down<TRX_Q6_K>;
 }
 
-using LayerFn = void (*)(TrxLayer, TrxShape, const float *, int, TrxWork, TrxSync *, float *, float *, uint32_t);
+using LayerFn = void (*)(TrxLayer, TrxShape, const float *, int, TrxWork, TrxSync *, float *, float *, uint32_t, int,
+                         int);
 
 static LayerFn layer_fn(int gate_type, int down_type) {
     if (gate_type == TRX_Q4_K) {
@@ -233,20 +235,46 @@ static LayerFn layer_fn(int gate_type, int down_type) {
     return trx_k_layer<TRX_Q8_0, TRX_Q8_0>;
 }
 
-// the fused kernel: its shared memory at the largest pass it serves and a cooperative grid (every CTA resident)
+// the fused kernel: the most shared memory a CTA may take, and a cooperative grid of one CTA per SM
 static bool plan_fused(tr_gpu_moe *m) {
     const tr_gpu_moe_config &c = m->cfg;
-    const int tmax = (int)std::min<int64_t>(c.max_tokens, TRX_ROUTE_FUSED_MAX);
-    m->smem_fused = trx_fused_smem(c.gate_type, c.down_type, (int)c.n_embd, (int)c.n_ff, tmax);
     int coop = 0, occ = 0;
     LayerFn fn = layer_fn(c.gate_type, c.down_type);
-    if (!ck(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, m->device), "attribute")) return false;
-    if (!coop || m->smem_fused > 227 * 1024) return true; // the multi-kernel road serves every pass
-    if (!ck(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)m->smem_fused), "smem fused") ||
-        !ck(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fn, 256, m->smem_fused), "occupancy"))
+    cudaFuncAttributes fa{};
+    if (!ck(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, m->device), "attribute") ||
+        !ck(cudaFuncGetAttributes(&fa, fn), "cudaFuncGetAttributes"))
         return false;
-    m->grid_fused = occ * m->sm_count;
-    m->fused_ok = occ >= 1 && m->grid_fused >= (int)(c.n_expert + tmax);
+    if (!coop) return true; // the multi-kernel road serves every pass
+    const size_t limit = 232448; // bytes of shared memory a block may use on sm_100 (static + dynamic)
+    m->smem_fused = limit - fa.sharedSizeBytes - 1024;
+    if (!ck(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)m->smem_fused), "smem fused") ||
+        !ck(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fn, TRX_FU_THREADS, m->smem_fused), "occupancy"))
+        return false;
+    m->grid_fused = m->sm_count; // one CTA per SM (occupancy is at least one: checked)
+    m->fused_ok = occ >= 1;
+    return true;
+}
+
+// the stages of a fused call of T tokens: as many as this CTA's share of the routed rows can use, within the
+// shared memory; false when even two of each do not fit (the multi-kernel road then takes the call)
+static bool fused_stages(const tr_gpu_moe *m, int T, int *sg, int *sd) {
+    const tr_gpu_moe_config &c = m->cfg;
+    const int H = (int)c.n_embd, F = (int)c.n_ff, k = (int)c.n_used;
+    const int64_t act = std::min<int64_t>(c.n_expert, (int64_t)T * k);
+    const int64_t rows_g = (act * F + m->grid_fused - 1) / m->grid_fused, rows_d = (act * H + m->grid_fused - 1) / m->grid_fused;
+    int g = (int)std::min<int64_t>(TRX_FU_MAXST, std::max<int64_t>(2, (rows_g + TRX_GU_CHUNK - 1) / TRX_GU_CHUNK + 1));
+    int d = (int)std::min<int64_t>(TRX_FU_MAXST, std::max<int64_t>(2, (rows_d + TRX_DN_CHUNK - 1) / TRX_DN_CHUNK + 1));
+    auto fits = [&](int a, int b) {
+        return trx_fused_layout(c.gate_type, c.down_type, H, F, T, k, a, b).total <= m->smem_fused;
+    };
+    while (!fits(g, d)) {
+        const TrxFusedSmem l = trx_fused_layout(c.gate_type, c.down_type, H, F, T, k, g, d);
+        if (g > 2 && (g * l.gu_stage >= d * l.dn_stage || d <= 2)) g--;
+        else if (d > 2) d--;
+        else return false;
+    }
+    *sg = g;
+    *sd = d;
     return true;
 }
 
@@ -334,8 +362,9 @@ extern "C" tr_gpu_moe *tr_gpu_moe_create(const tr_gpu_moe_config *cfg, int devic
     m->device = device;
     const WorkLayout wl = work_layout(*cfg);
     const int64_t lb = layer_bytes(*cfg);
-    const int64_t tmp_bytes = std::max(trx_row_bytes(cfg->gate_type, cfg->n_embd) * cfg->n_ff,
-                                       trx_row_bytes(cfg->down_type, cfg->n_ff) * cfg->n_embd);
+    const int64_t tmp_bytes = std::max(std::max(trx_row_bytes(cfg->gate_type, cfg->n_embd) * cfg->n_ff,
+                                                trx_row_bytes(cfg->down_type, cfg->n_ff) * cfg->n_embd),
+                                       trx_row_bytes(cfg->router_type, cfg->n_embd) * cfg->n_expert);
     bool ok = ck(cudaSetDevice(device), "cudaSetDevice") &&
               ck(cudaDeviceGetAttribute(&m->sm_count, cudaDevAttrMultiProcessorCount, device), "attribute") &&
               ck(cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking), "cudaStreamCreate") &&
@@ -393,6 +422,7 @@ extern "C" void tr_gpu_moe_free(tr_gpu_moe *m) {
         if (p) cudaFree(p);
     if (m->work_mem) cudaFree(m->work_mem);
     if (m->tmp) cudaFree(m->tmp);
+    if (m->trace) cudaFree(m->trace);
     for (auto &es : m->evs)
         for (cudaEvent_t e : es.ev) cudaEventDestroy(e);
     if (m->stream) cudaStreamDestroy(m->stream);
@@ -435,8 +465,13 @@ extern "C" int tr_gpu_moe_set_layer(tr_gpu_moe *m, int64_t layer, const void *ro
     L.up = b + o;
     o += E * L.up_mb;
     L.down = b + o;
-    bool ok = ck(cudaMemcpyAsync((void *)L.router, router, (size_t)router_bytes, cudaMemcpyHostToDevice, m->stream),
-                 "upload router");
+    // the router in lane-row order (trx_repack_lanerows), staged through the matrix buffer
+    bool ok = ck(cudaMemcpyAsync(m->tmp, router, (size_t)router_bytes, cudaMemcpyHostToDevice, m->stream), "upload router");
+    if (ok) {
+        trx_repack_lanerows<<<(unsigned)E, 256, 0, m->stream>>>(m->tmp, (uint8_t *)L.router, E, H,
+                                                                  c.router_type == TRX_F32 ? 4 : 2);
+        ok = ck(cudaGetLastError(), "repack router") && stream_wait(m->stream, 300.0);
+    }
     if (ok && router_bias)
         ok = ck(cudaMemcpyAsync(bias, router_bias, (size_t)E * 4, cudaMemcpyHostToDevice, m->stream), "upload bias");
     for (int64_t e = 0; e < E && ok; e++) {
@@ -466,6 +501,32 @@ extern "C" int tr_gpu_moe_profile(tr_gpu_moe *m, int on) {
     return 0;
 }
 
+extern "C" int tr_gpu_moe_trace(tr_gpu_moe *m, int on) {
+    g_err.clear();
+    if (m == nullptr || !ck(cudaSetDevice(m->device), "cudaSetDevice") || !stream_wait(m->stream)) return -1;
+    if (!on) {
+        if (m->trace) cudaFree(m->trace);
+        m->trace = nullptr;
+        return 0;
+    }
+    const size_t bytes = (size_t)std::max(m->grid_fused, 1) * 64 * 8;
+    if (m->trace == nullptr && !ck(cudaMalloc(&m->trace, bytes), "cudaMalloc(trace)")) return -1;
+    return ck(cudaMemset(m->trace, 0, bytes), "cudaMemset(trace)") ? 0 : -1;
+}
+
+extern "C" int tr_gpu_moe_trace_read(tr_gpu_moe *m, uint64_t *slots, int64_t n) {
+    g_err.clear();
+    if (m == nullptr || m->trace == nullptr || slots == nullptr) {
+        set_err("tracing is off");
+        return -1;
+    }
+    if (!ck(cudaSetDevice(m->device), "cudaSetDevice") || !ck(cudaDeviceSynchronize(), "cudaDeviceSynchronize"))
+        return -1;
+    const int64_t have = (int64_t)m->grid_fused * 64;
+    if (!ck(cudaMemcpy(slots, m->trace, (size_t)std::min(n, have) * 8, cudaMemcpyDeviceToHost), "copy trace")) return -1;
+    return m->grid_fused;
+}
+
 extern "C" int tr_gpu_moe_profile_read(tr_gpu_moe *m, double *ms, int64_t *calls, int n_zones) {
     g_err.clear();
     if (m == nullptr || !ck(cudaSetDevice(m->device), "cudaSetDevice") || !prof_collect(m)) return -1;
@@ -488,7 +549,10 @@ static void reset_counters(tr_gpu_moe *m, cudaStream_t st) {
 
 extern "C" int tr_gpu_moe_launches(const tr_gpu_moe *m, int64_t n_tok) {
     if (m == nullptr) return 0;
-    if (m->fused_ok && n_tok <= TRX_ROUTE_FUSED_MAX && !m->prof) return 1;
+    int sg, sd;
+    if (m->fused_ok && n_tok <= TRX_ROUTE_FUSED_MAX && m->cfg.n_expert + n_tok <= m->grid_fused && !m->prof &&
+        fused_stages(m, (int)n_tok, &sg, &sd))
+        return 1;
     return (n_tok <= TRX_ROUTE_FUSED_MAX ? 1 : 4) + 2 + (m->cfg.down_type == TRX_Q4_K ? 1 : 0);
 }
 
@@ -525,6 +589,7 @@ static int launch_layer(tr_gpu_moe *m, int64_t layer, const float *d_normed, int
     const TrxLayer &L = m->layers[(size_t)layer];
     TrxShape S{(int)c.n_expert, (int)c.n_used, (int)c.n_embd, (int)c.n_ff, (int)c.norm_topk};
     TrxWork w = m->work;
+    w.trace = m->trace;
     if (out) {
         w.out_logits = out->logits;
         w.out_sel_id = out->sel_id;
@@ -547,13 +612,15 @@ static int launch_layer(tr_gpu_moe *m, int64_t layer, const float *d_normed, int
         for (int z = 0; z < TRMOE_ZONES; z++) es->used[z] = true;
         es->used[2] = c.down_type == TRX_Q4_K;
     }
-    if (first == 0 && last == 3 && m->fused_ok && T <= TRX_ROUTE_FUSED_MAX && !es) {
+    int sg = 0, sd = 0;
+    if (first == 0 && last == 3 && m->fused_ok && T <= TRX_ROUTE_FUSED_MAX && E + T <= m->grid_fused && !es &&
+        fused_stages(m, T, &sg, &sd)) {
         float *ffn = out ? out->ffn_out : nullptr;
         const uint32_t epoch = ++m->epoch;
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3((unsigned)m->grid_fused);
-        cfg.blockDim = dim3(256);
-        cfg.dynamicSmemBytes = m->smem_fused;
+        cfg.blockDim = dim3(TRX_FU_THREADS);
+        cfg.dynamicSmemBytes = trx_fused_layout(c.gate_type, c.down_type, S.H, S.F, T, S.k, sg, sd).total;
         cfg.stream = st;
         cudaLaunchAttribute attr[1];
         attr[0].id = cudaLaunchAttributeCooperative;
@@ -561,7 +628,7 @@ static int launch_layer(tr_gpu_moe *m, int64_t layer, const float *d_normed, int
         cfg.attrs = attr;
         cfg.numAttrs = 1;
         return ck(cudaLaunchKernelEx(&cfg, layer_fn(c.gate_type, c.down_type), L, S, d_normed, T, w, m->sync, d_x, ffn,
-                                     epoch),
+                                     epoch, sg, sd),
                   "fused layer launch")
                    ? 0
                    : -1;

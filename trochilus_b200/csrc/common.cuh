@@ -14,7 +14,37 @@
 // ggml type numbers (Trochilus src/format/gguf.h:16-27)
 enum : int { TRX_F32 = 0, TRX_F16 = 1, TRX_Q8_0 = 8, TRX_Q4_K = 12, TRX_Q6_K = 14, TRX_BF16 = 30 };
 
+// IEEE half to float and to double, exact (every half is a float): the conversion instruction, which takes no
+// branch for the rare classes (subnormals, infinities, NaNs)
 __device__ __forceinline__ float trx_half(uint16_t h) { return __half2float(__ushort_as_half(h)); }
+__device__ __forceinline__ double trx_half_d(uint16_t h) { return (double)__half2float(__ushort_as_half(h)); }
+
+// Two floats in one 64-bit register and the sm_100 paired operations on them: each half rounded to nearest even
+// on its own, exactly as the scalar __fadd_rn / __fsub_rn / __fmul_rn would (no contraction, subnormals kept)
+typedef unsigned long long trx_f2;
+__device__ __forceinline__ trx_f2 trx_pack2(float lo, float hi) {
+    return (trx_f2)__float_as_uint(lo) | ((trx_f2)__float_as_uint(hi) << 32);
+}
+__device__ __forceinline__ float trx_lo(trx_f2 v) { return __uint_as_float((uint32_t)v); }
+__device__ __forceinline__ float trx_hi(trx_f2 v) { return __uint_as_float((uint32_t)(v >> 32)); }
+__device__ __forceinline__ trx_f2 trx_mul2(trx_f2 a, trx_f2 b) {
+    trx_f2 d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ trx_f2 trx_sub2(trx_f2 a, trx_f2 b) {
+    trx_f2 d;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+
+// an integer |v| < 2^51 to double and back, exactly, through the 1.5 * 2^52 bias (integer and double adds only)
+__device__ __forceinline__ double trx_i2d(int64_t v) {
+    return __dsub_rn(__longlong_as_double(v + 0x4338000000000000ll), 6755399441055744.0);
+}
+__device__ __forceinline__ int64_t trx_d2i(double x) {
+    return __double_as_longlong(__dadd_rn(x, 6755399441055744.0)) - 0x4338000000000000ll;
+}
 __device__ __forceinline__ float trx_bf16(uint16_t b) { return __uint_as_float((uint32_t)b << 16); }
 
 // The 16-lane tree ((l0+l1)+(l2+l3))+((l4+l5)+(l6+l7)), same for 8..15, halves last

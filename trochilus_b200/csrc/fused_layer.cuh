@@ -1,36 +1,47 @@
-// fused_layer.cuh: one MoE layer call for a short pass (decode, up to TRX_ROUTE_FUSED_MAX tokens) as ONE
-// persistent kernel, launched cooperatively so that every CTA is resident and may wait for another.
+// fused_layer.cuh: one MoE layer call for a short pass (decode) as ONE persistent kernel, launched
+// cooperatively so that every CTA is resident and may wait for another.
 //
 //  phase A  CTAs 0..E-1 compute the router logits of one expert each (trx_router_block); CTAs E..E+T-1
-//           prepare one token's input row each; the last of them to finish routes every token and sorts the
-//           (token, slot) rows by expert, then publishes the routing (a release store of the call's epoch).
-//  phase B  every CTA waits for the routing, takes its share of the routed gate/up rows and of the routed
-//           down rows (trx_cta_range over each virtual row space) and arms 1-D TMA bulk copies for BOTH at
-//           once: the down weights do not depend on the activations, so they stream from HBM while the
-//           gate/up rows are multiplied.
-//  gate/up  as trx_k_gateup; each finished chunk adds its rows to its expert's counter (release).
-//  down     before a chunk of expert i: wait (acquire) until expert i's F gate/up rows are counted; Q4_K
-//           prepares the expert's h rows in shared memory; then the dots into h3 and the id-ordered combine
-//           by the last CTA to finish each 16-row block (as trx_k_down).
+//           prepare one token's input row each; the last of them to finish routes every token, sorts the
+//           (token, slot) rows by expert and publishes the routing (a release store of the call's epoch).
+//  phase B  every CTA waits for the routing, copies the call's routing and the tokens' prepared input rows
+//           into shared memory, and takes its share of the routed gate/up rows and of the routed down rows
+//           (trx_cta_range over each virtual row space).
+//  then     warp-specialised: a producer warp streams this CTA's gate/up chunks (8 rows of gate and of up)
+//           and down chunks (16 rows) from HBM into shared-memory stages with 1-D TMA bulk copies, refilling a
+//           stage when its "empty" barrier says the 8 consumer warps are done with it; the down weights do not
+//           depend on the activations, so they stream while the gate/up rows are multiplied. Each consumer
+//           warp works on its own rows with no block-wide barrier: gate/up row w of every chunk (both matrices,
+//           SwiGLU fused, h written, the row counted into its expert with release semantics; the warp that
+//           counts an expert's last row prepares that expert's down inputs for Q4_K), then rows 2w, 2w + 1 of
+//           every down chunk once its expert's rows are all counted (acquire); the warp completing a 16-row
+//           block combines it: every token's k expert outputs added in increasing expert id, the sum added to
+//           the residual (Trochilus's mix_body).
 //  end      the last CTA resets the per-expert counters for the next call.
 //
-// Every wait is bounded (TRX_SPIN_NS); a CTA that gives up sets the error flag, waits (bounded) for its own
-// copies in flight and leaves. The counters a kernel leaves non-zero after an error are reset by
-// tr_gpu_moe_check.
+// Every wait is bounded (TRX_SPIN_NS, TRX_WAIT_NS); a warp that gives up marks the CTA failed, the producer
+// waits (bounded) for every copy it armed, the error flag is set and the CTA leaves. The counters a failed call
+// leaves behind are reset by the host (tr_gpu_moe_check, and the host-pointer call on an error).
+//
+// Trochilus references: forward_layer's MoE block src/models/olmoe.c:1845-1933 (route_token :1455-1502, the
+// counting sort :1850-1861, expert_stages :1642-1689, mix_body :1432-1446).
 #pragma once
 #include <cstdint>
 #include "bulk.cuh"
 #include "moe_kernels.cuh"
 
 #define TRX_SPIN_NS 1000000000ull
-#define TRX_FU_SD 4 // down stages
+#define TRX_FU_CWARPS 8                           // consumer warps
+#define TRX_FU_THREADS (32 * (TRX_FU_CWARPS + 1)) // + the producer warp
+#define TRX_FU_MAXST 8                            // most stages of either kind
+#define TRX_LOCAL_ROUTE_MAX 2                     // tokens up to which every CTA routes the call itself
 
 struct TrxSync {
-    uint32_t route_cnt;            // router and prep CTAs done in this call
-    uint32_t routed;               // the epoch of the last call whose routing is published
-    uint32_t finish;               // CTAs done in this call
+    uint32_t route_cnt;                // router and prep CTAs done in this call
+    uint32_t routed;                   // the epoch of the last call whose routing is published
+    uint32_t finish;                   // CTAs done in this call
     uint32_t pad;
-    uint32_t gu_done[TRX_MAX_EXPERTS]; // gate/up rows done per active slot
+    uint32_t gu_done[TRX_MAX_EXPERTS]; // gate/up rows done per active slot (+1 once Q4_K's down inputs are ready)
 };
 
 __device__ __forceinline__ uint32_t trx_ld_acquire(const uint32_t *p) {
@@ -43,6 +54,10 @@ __device__ __forceinline__ void trx_st_release(uint32_t *p, uint32_t v) {
     asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
+__device__ __forceinline__ void trx_mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(trx_smem(bar)) : "memory");
+}
+
 // thread-level bounded wait: *p == target (eq) or *p >= target
 __device__ __forceinline__ bool trx_spin(const uint32_t *p, uint32_t target, bool eq) {
     uint64_t t0 = 0;
@@ -51,279 +66,532 @@ __device__ __forceinline__ bool trx_spin(const uint32_t *p, uint32_t target, boo
         if (eq ? v == target : v >= target) return true;
         if (it == 0) t0 = trx_globaltimer();
         else if (trx_globaltimer() - t0 > TRX_SPIN_NS) return false;
-        __nanosleep(32);
+        __nanosleep(20);
     }
 }
 
-template <int GT>
-__host__ __device__ constexpr int trx_fu_sg() { return GT == TRX_Q4_K ? 4 : 3; }
+// A CTA's walk over its range [v, end) of a virtual row space of n_active experts x per rows, in chunks of at most
+// `most` rows that stay inside one expert (and, when aligned, inside one `most`-row block). int32: the spaces hold at
+// most 64 x 2048 rows.
+struct TrxWalk {
+    int v, end, slot, r, per, most;
+    bool aligned;
+    __device__ void init(int V, int per_, int most_, bool aligned_) {
+        int64_t a, b;
+        trx_cta_range(V, a, b);
+        v = (int)a;
+        end = (int)b;
+        per = per_;
+        most = most_;
+        aligned = aligned_;
+        slot = v / per;
+        r = v - slot * per;
+    }
+    __device__ bool more() const { return v < end; }
+    __device__ int n() const { return min(min(aligned ? most - r % most : most, end - v), per - r); }
+    __device__ void next() {
+        const int k = n();
+        v += k;
+        r += k;
+        if (r == per) {
+            r = 0;
+            slot++;
+        }
+    }
+};
 
-// dynamic shared memory of the fused kernel (the router phase reuses the stage buffers)
-__host__ __device__ inline size_t trx_fused_smem(int gate_type, int down_type, int H, int F, int T) {
+// The fused kernel's dynamic shared memory: the stage buffers (the router phase reuses them), the barriers,
+// the call's routing (xmap, sel_w, place, sel_id: R = T k entries each), then the tokens' prepared input rows
+// (Q4_K: planes, sums, scales; Q8_0: the LC-ordered row), each region 128-byte aligned.
+struct TrxFusedSmem {
+    size_t gu_stage, dn_stage, bars, meta, tok, tok_bytes, total;
+};
+
+__host__ __device__ inline size_t trx_align128(size_t v) { return (v + 127) / 128 * 128; }
+
+__host__ __device__ inline TrxFusedSmem trx_fused_layout(int gate_type, int down_type, int H, int F, int T, int k, int sg,
+                                                         int sd) {
     const int rbg = gate_type == TRX_Q4_K ? H / 256 * 144 : H / 32 * 34;
     const int rbd = down_type == TRX_Q4_K ? F / 256 * 144 : down_type == TRX_Q6_K ? F / 256 * 208 : F / 32 * 34;
-    const int sg = gate_type == TRX_Q4_K ? 4 : 3;
-    size_t stages = (size_t)sg * 2 * TRX_GU_CHUNK * rbg + (size_t)TRX_FU_SD * TRX_DN_CHUNK * rbd;
+    TrxFusedSmem l;
+    l.gu_stage = (size_t)2 * TRX_GU_CHUNK * rbg;
+    l.dn_stage = (size_t)TRX_DN_CHUNK * rbd;
+    size_t stages = sg * l.gu_stage + sd * l.dn_stage;
     const size_t router = (size_t)(1 + (T < TRX_TOK_STAGE ? T : TRX_TOK_STAGE)) * H * 4;
     if (router > stages) stages = router;
-    const size_t prep = down_type == TRX_Q4_K ? (size_t)F * 4 + (size_t)(F / 32 + F / 256) * 8 : 0;
-    return (stages + 8 * (sg + TRX_FU_SD) + 127) / 128 * 128 + prep;
+    l.bars = trx_align128(stages);
+    l.meta = trx_align128(l.bars + 8 * 4 * TRX_FU_MAXST);
+    l.tok = trx_align128(l.meta + (size_t)T * k * 16);
+    l.tok_bytes = gate_type == TRX_Q4_K ? trx_align128((size_t)H * 4 + (size_t)(H / 32 + H / 256) * 8) : (size_t)H * 4;
+    l.total = l.tok + (size_t)T * l.tok_bytes;
+    return l;
 }
 
+#define TRX_TRACE(slot)                                                                                                \
+    do {                                                                                                               \
+        if (w.trace != nullptr && threadIdx.x == 0) w.trace[(size_t)blockIdx.x * 64 + (slot)] = trx_globaltimer();     \
+    } while (0)
+
 template <int GT, int DT>
-__global__ void __launch_bounds__(256, 1) trx_k_layer(TrxLayer L, TrxShape S, const float *__restrict__ normed, int T,
-                                                      TrxWork w, TrxSync *sync, float *__restrict__ x_io,
-                                                      float *__restrict__ ffn_out, uint32_t epoch) {
+__global__ void __launch_bounds__(TRX_FU_THREADS, 1)
+    trx_k_layer(TrxLayer L, TrxShape S, const float *__restrict__ normed, int T, TrxWork w, TrxSync *sync,
+                float *__restrict__ x_io, float *__restrict__ ffn_out, uint32_t epoch, int SG, int SD) {
     extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ float res[2][TRX_TOK_GROUP][TRX_GU_CHUNK];
     __shared__ int s_active[TRX_MAX_EXPERTS], s_off[TRX_MAX_EXPERTS + 1], s_nact, s_flag;
-    __shared__ float sp[8][96];
-    constexpr int CHG = TRX_GU_CHUNK, CHD = TRX_DN_CHUNK, SG = trx_fu_sg<GT>(), SD = TRX_FU_SD;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, hw = tid >> 4;
-    const int E = S.E, H = S.H, F = S.F, k = S.k, nsb_d = F / 256;
+    __shared__ float sp[TRX_FU_CWARPS + 1][96];
+    __shared__ int scnt[64];
+    __shared__ float s_logit[TRX_LOCAL_ROUTE_MAX * TRX_MAX_EXPERTS];
+    __shared__ uint32_t s_gcnt[TRX_FU_MAXST], s_dcnt[TRX_FU_MAXST];
+    constexpr int CHG = TRX_GU_CHUNK, CHD = TRX_DN_CHUNK;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int E = S.E, H = S.H, F = S.F, k = S.k, nsb_d = F / 256, R = T * k;
+    TRX_TRACE(0);
     const int rbg = GT == TRX_Q4_K ? H / 256 * 144 : H / 32 * 34;
     const int rbd = DT == TRX_Q4_K ? nsb_d * 144 : DT == TRX_Q6_K ? nsb_d * 208 : F / 32 * 34;
-    const int gu_half = CHG * rbg, gu_stage = 2 * gu_half, dn_stage = CHD * rbd;
-    uint8_t *gu_buf = smem, *dn_buf = smem + SG * gu_stage;
-    size_t stage_bytes = (size_t)SG * gu_stage + (size_t)SD * dn_stage;
-    const size_t router_bytes = (size_t)(1 + min(T, TRX_TOK_STAGE)) * H * 4;
-    if (router_bytes > stage_bytes) stage_bytes = router_bytes;
-    uint64_t *bar = reinterpret_cast<uint64_t *>(smem + stage_bytes); // SG gate/up, then SD down
-    // Q4_K down: one prepared h row, 128-byte aligned (its planes are read 16 bytes at a time)
-    uint32_t *s_planes = reinterpret_cast<uint32_t *>(smem + ((stage_bytes + 8 * (SG + SD) + 127) / 128) * 128);
-    double *s_bf = reinterpret_cast<double *>(s_planes + F), *s_sc = s_bf + F / 32;
+    const TrxFusedSmem lay = trx_fused_layout(GT, DT, H, F, T, k, SG, SD);
+    const int gu_half = CHG * rbg;
+    uint8_t *gu_buf = smem, *dn_buf = smem + SG * lay.gu_stage;
+    uint64_t *full_g = reinterpret_cast<uint64_t *>(smem + lay.bars), *empty_g = full_g + TRX_FU_MAXST;
+    uint64_t *full_d = empty_g + TRX_FU_MAXST, *empty_d = full_d + TRX_FU_MAXST;
+    int *s_xmap = reinterpret_cast<int *>(smem + lay.meta);
+    float *s_selw = reinterpret_cast<float *>(s_xmap + R);
+    int *s_place = reinterpret_cast<int *>(s_selw + R);
+    int *s_selid = s_place + R;
+    uint8_t *s_tok = smem + lay.tok;
+    if (tid < TRX_FU_MAXST) s_gcnt[tid] = s_dcnt[tid] = 0u;
+    const int nsb_g = H / 256;
 
-    // ---------------- phase A: router logits, token preparation, routing
-    if ((int)blockIdx.x < E + T) {
-        if ((int)blockIdx.x < E) trx_router_block(L, S, normed, blockIdx.x, 0, T, w, reinterpret_cast<float *>(smem));
-        else trx_prep_token(L, S, normed, blockIdx.x - E, w);
-        __syncthreads();
-        if (tid == 0) {
-            __threadfence();
-            s_flag = atomicAdd(&sync->route_cnt, 1u) == (uint32_t)(E + T - 1);
-        }
-        __syncthreads();
-        if (s_flag) {
-            __threadfence();
-            for (int t = warp; t < T; t += 8)
-                trx_route_token(w.logits + (int64_t)t * E, E, k, S.norm_topk, lane, sp[warp], w.sel_id + (int64_t)t * k,
-                                w.sel_w + (int64_t)t * k);
-            __syncthreads();
-            const int R = T * k;
-            if (w.out_sel_id)
-                for (int j = tid; j < R; j += blockDim.x) {
-                    w.out_sel_id[j] = w.sel_id[j];
-                    w.out_sel_w[j] = w.sel_w[j];
+    // Local routing (a decode call with a BF16 router of 2048 columns): every CTA computes all of the call's
+    // logits from L2, routes and sorts them in shared memory, and prepares the tokens itself; no CTA waits for
+    // another before the weights stream. Otherwise phase A / B below route once and publish.
+    const bool local = T <= TRX_LOCAL_ROUTE_MAX && H == 2048 && L.router_type == TRX_BF16;
+    if (local) {
+        // logits: a chain per (expert, lane l), lane l's 16 elements of each 256-block in lane-row order (2 x 16
+        // bytes), every token of the call against the same weights; the next round's weights load while a round
+        // is multiplied
+        constexpr int NB = 8;
+        const int nchain = E * 16, nth = blockDim.x;
+        auto load_chain = [&](int c, uint4(&r)[2 * NB]) {
+            const uint4 *p = reinterpret_cast<const uint4 *>(L.router + (int64_t)min(c >> 4, E - 1) * (NB * 512)) + 2 * (c & 15);
+#pragma unroll
+            for (int i = 0; i < NB; i++) {
+                r[2 * i] = __ldg(p + 32 * i);
+                r[2 * i + 1] = __ldg(p + 32 * i + 1);
+            }
+        };
+        float *sx = reinterpret_cast<float *>(GT == TRX_Q8_0 ? s_tok : smem); // the inputs, LC order, H apart
+        auto chains = [&](int c, const uint4(&r)[2 * NB]) {
+            const int e = min(c >> 4, E - 1), l = c & 15;
+            float acc[TRX_LOCAL_ROUTE_MAX];
+#pragma unroll
+            for (int t = 0; t < TRX_LOCAL_ROUTE_MAX; t++) acc[t] = 0.0f;
+#pragma unroll
+            for (int i = 0; i < NB; i++) {
+                float wv[16];
+#pragma unroll
+                for (int q = 0; q < 2; q++) {
+                    const uint32_t u[4] = {r[2 * i + q].x, r[2 * i + q].y, r[2 * i + q].z, r[2 * i + q].w};
+#pragma unroll
+                    for (int j = 0; j < 4; j++) {
+                        wv[8 * q + 2 * j] = __uint_as_float(u[j] << 16);
+                        wv[8 * q + 2 * j + 1] = __uint_as_float(u[j] & 0xffff0000u);
+                    }
                 }
-            trx_block_counting_sort<8>(w.sel_id, R, E, k, w);
-            __syncthreads();
-            if (tid == 0) {
-                sync->route_cnt = 0u;
-                __threadfence();
-                trx_st_release(&sync->routed, epoch);
+#pragma unroll
+                for (int t = 0; t < TRX_LOCAL_ROUTE_MAX; t++) {
+                    if (t < T) {
+                        const float *xs = sx + t * H + 256 * i + 4 * l;
+                        float xv[16];
+#pragma unroll
+                        for (int q = 0; q < 4; q++) {
+                            const float4 v = *reinterpret_cast<const float4 *>(xs + 64 * q);
+                            xv[4 * q] = v.x; xv[4 * q + 1] = v.y; xv[4 * q + 2] = v.z; xv[4 * q + 3] = v.w;
+                        }
+#pragma unroll
+                        for (int m = 0; m < 16; m++) acc[t] = __fadd_rn(acc[t], __fmul_rn(wv[m], xv[m]));
+                    }
+                }
+            }
+#pragma unroll
+            for (int t = 0; t < TRX_LOCAL_ROUTE_MAX; t++) {
+                if (t < T) {
+                    const float v = trx_lane_tree16(acc[t]);
+                    if (l == 0 && c < nchain)
+                        s_logit[t * E + e] = L.router_bias ? __fadd_rn(v, L.router_bias[e]) : v;
+                }
+            }
+        };
+        uint4 wa[2 * NB], wb[2 * NB];
+        load_chain(tid, wa);
+        for (int i = tid; i < T * H / 4; i += blockDim.x) {
+            const int t = (4 * i) / H, kk = (4 * i) % H;
+            const float4 v = *reinterpret_cast<const float4 *>(normed + (int64_t)t * H + kk);
+            float *dst = sx + t * H;
+            dst[trx_lc_pos(kk)] = v.x;
+            dst[trx_lc_pos(kk + 1)] = v.y;
+            dst[trx_lc_pos(kk + 2)] = v.z;
+            dst[trx_lc_pos(kk + 3)] = v.w;
+        }
+        if (GT == TRX_Q4_K) // the tokens prepared for the gate/up products, one warp per 256-block
+            for (int q = warp; q < T * nsb_g; q += TRX_FU_CWARPS + 1) {
+                const int t = q / nsb_g, s4 = q % nsb_g;
+                uint8_t *tok = s_tok + t * lay.tok_bytes;
+                double *bfd = reinterpret_cast<double *>(tok + (size_t)H * 4);
+                trx_prep_q4x_block(normed + (int64_t)t * H + 256 * s4, reinterpret_cast<uint32_t *>(tok), s4, nsb_g,
+                                   bfd + 8 * s4, bfd + H / 32 + s4, lane);
+            }
+        __syncthreads();
+        TRX_TRACE(62);
+        for (int base = 0; base < nchain; base += 2 * nth) {
+            if (base + nth < nchain) load_chain(base + nth + tid, wb);
+            chains(base + tid, wa);
+            if (base + nth < nchain) {
+                if (base + 2 * nth < nchain) load_chain(base + 2 * nth + tid, wa);
+                chains(base + nth + tid, wb);
             }
         }
+        __syncthreads();
+        TRX_TRACE(59);
+        if (warp < T)
+            trx_route_token<true>(s_logit + warp * E, E, k, S.norm_topk, lane, sp[warp], s_selid + warp * k,
+                                  s_selw + warp * k);
+        __syncthreads();
+        TRX_TRACE(60);
+        if (warp == 0) {
+            const bool out = blockIdx.x == 0;
+            const TrxSortOut so{s_off, s_active, &s_nact, s_place, s_xmap, out ? w.out_offsets : nullptr,
+                                out ? w.out_place : nullptr};
+            trx_warp_counting_sort(s_selid, R, E, k, so, scnt, lane);
+        }
+        if (blockIdx.x == 0) {
+            if (w.out_logits)
+                for (int j = tid; j < T * E; j += blockDim.x) w.out_logits[j] = s_logit[j];
+            if (w.out_sel_id)
+                for (int j = tid; j < R; j += blockDim.x) {
+                    w.out_sel_id[j] = s_selid[j];
+                    w.out_sel_w[j] = s_selw[j];
+                }
+        }
+        __syncthreads();
+        TRX_TRACE(2);
+    } else {
+        // ---------------- phase A: router logits, token preparation, routing by the last CTA of them
+        if ((int)blockIdx.x < E + T) {
+            if ((int)blockIdx.x < E) trx_router_block(L, S, normed, blockIdx.x, 0, T, w, reinterpret_cast<float *>(smem));
+            else trx_prep_token(L, S, normed, blockIdx.x - E, w);
+            __syncthreads();
+            TRX_TRACE(62);
+            if (tid == 0) {
+                __threadfence();
+                s_flag = atomicAdd(&sync->route_cnt, 1u) == (uint32_t)(E + T - 1);
+            }
+            __syncthreads();
+            if (s_flag) {
+                __threadfence();
+                TRX_TRACE(59);
+                for (int t = warp; t < T; t += TRX_FU_CWARPS + 1)
+                    trx_route_token(w.logits + (int64_t)t * E, E, k, S.norm_topk, lane, sp[warp], w.sel_id + (int64_t)t * k,
+                                    w.sel_w + (int64_t)t * k);
+                __syncthreads();
+                TRX_TRACE(60);
+                if (w.out_sel_id)
+                    for (int j = tid; j < R; j += blockDim.x) {
+                        w.out_sel_id[j] = w.sel_id[j];
+                        w.out_sel_w[j] = w.sel_w[j];
+                    }
+                if (R <= 32) {
+                    const TrxSortOut so{w.offsets, w.active, w.n_active, w.place, w.xmap, w.out_offsets, w.out_place};
+                    if (warp == 0) trx_warp_counting_sort(w.sel_id, R, E, k, so, scnt, lane);
+                } else {
+                    trx_block_counting_sort<TRX_FU_CWARPS + 1>(w.sel_id, R, E, k, w);
+                }
+                __syncthreads();
+                TRX_TRACE(61);
+                if (tid == 0) {
+                    sync->route_cnt = 0u;
+                    __threadfence();
+                    trx_st_release(&sync->routed, epoch);
+                }
+            }
+            TRX_TRACE(1);
+        }
+        // ---------------- phase B: the routing and the tokens' inputs into shared memory
+        if (tid == 0) s_flag = trx_spin(&sync->routed, epoch, true);
+        __syncthreads();
+        if (!s_flag) {
+            if (tid == 0) atomicExch(w.err, 2);
+            return;
+        }
+        TRX_TRACE(2);
+        if (tid == 0) s_nact = __ldcg(w.n_active);
+        if (tid <= E) s_off[tid] = __ldcg(w.offsets + tid);
+        if (tid < E) s_active[tid] = __ldcg(w.active + tid);
+        for (int j = tid; j < R; j += blockDim.x) {
+            s_xmap[j] = __ldcg(w.xmap + j);
+            s_selw[j] = __ldcg(w.sel_w + j);
+            s_place[j] = __ldcg(w.place + j);
+        }
+        for (int t = 0; t < T; t++) {
+            uint8_t *dst = s_tok + t * lay.tok_bytes;
+            if (GT == TRX_Q4_K) {
+                for (int i = tid; i < H / 4; i += blockDim.x)
+                    reinterpret_cast<uint4 *>(dst)[i] = __ldcg(reinterpret_cast<const uint4 *>(w.xq + (int64_t)t * H) + i);
+                double *bfd = reinterpret_cast<double *>(dst + (size_t)H * 4);
+                for (int i = tid; i < H / 32; i += blockDim.x) bfd[i] = __ldcg(w.xq_bf + (int64_t)t * (H / 32) + i);
+                for (int i = tid; i < H / 256; i += blockDim.x)
+                    bfd[H / 32 + i] = __ldcg(w.xq_sc + (int64_t)t * (H / 256) + i);
+            } else {
+                for (int i = tid; i < H / 4; i += blockDim.x)
+                    reinterpret_cast<float4 *>(dst)[i] =
+                        __ldcg(reinterpret_cast<const float4 *>(w.x_lc + (int64_t)t * H) + i);
+            }
+        }
+        __syncthreads();
     }
-
-    // ---------------- phase B: the routing, this CTA's rows, every copy armed
-    if (tid == 0) s_flag = trx_spin(&sync->routed, epoch, true);
-    __syncthreads();
-    if (!s_flag) {
-        if (tid == 0) atomicExch(w.err, 2);
-        return;
-    }
-    if (tid == 0) s_nact = __ldcg(w.n_active);
-    if (tid <= E) s_off[tid] = __ldcg(w.offsets + tid);
-    if (tid < E) s_active[tid] = __ldcg(w.active + tid);
-    __syncthreads();
-    const int n_act = s_nact;
-    int64_t ag, bg, ad, bd;
-    trx_cta_range((int64_t)n_act * F, ag, bg);
-    trx_cta_range((int64_t)n_act * H, ad, bd);
-    if (tid == 0) {
-        for (int s = 0; s < SG + SD; s++) trx_mbar_init(&bar[s], 1);
+    if (tid == 0) { // the stage buffers' scratch use is over: the pipelines' barriers
+        for (int s = 0; s < SG; s++) {
+            trx_mbar_init(&full_g[s], 1);
+            trx_mbar_init(&empty_g[s], TRX_FU_CWARPS);
+        }
+        for (int s = 0; s < SD; s++) {
+            trx_mbar_init(&full_d[s], 1);
+            trx_mbar_init(&empty_d[s], TRX_FU_CWARPS);
+        }
         trx_fence_barrier_init();
     }
     __syncthreads();
-    auto gu_end = [&](int64_t v) { return min(min(v + CHG, bg), (v / F + 1) * F); };
-    auto dn_end = [&](int64_t v) { return min(bd, (v / CHD + 1) * CHD); };
-    int64_t gu_iv = ag, dn_iv = ad;
-    int gu_issued = 0, dn_issued = 0;
-    auto issue_gu = [&]() {
-        const int64_t ve = gu_end(gu_iv);
-        const int e = s_active[gu_iv / F], r0 = (int)(gu_iv % F), n = (int)(ve - gu_iv);
-        const int s = gu_issued % SG;
-        uint8_t *dst = gu_buf + s * gu_stage;
-        trx_mbar_expect_tx(&bar[s], 2u * n * rbg);
-        trx_bulk_g2s(dst, L.gate + e * L.gate_mb + (int64_t)r0 * rbg, n * rbg, &bar[s]);
-        trx_bulk_g2s(dst + gu_half, L.up + e * L.up_mb + (int64_t)r0 * rbg, n * rbg, &bar[s]);
-        gu_iv = ve;
-        gu_issued++;
-    };
-    auto issue_dn = [&]() {
-        const int64_t ve = dn_end(dn_iv);
-        const int e = s_active[dn_iv / H], d0 = (int)(dn_iv % H), n = (int)(ve - dn_iv);
-        const int s = dn_issued % SD;
-        trx_mbar_expect_tx(&bar[SG + s], (uint32_t)(n * rbd));
-        trx_bulk_g2s(dn_buf + s * dn_stage, L.down + e * L.down_mb + (int64_t)d0 * rbd, n * rbd, &bar[SG + s]);
-        dn_iv = ve;
-        dn_issued++;
-    };
-    if (tid == 0) {
-        for (int q = 0; q < SG && gu_iv < bg; q++) issue_gu();
-        for (int q = 0; q < SD && dn_iv < bd; q++) issue_dn();
-    }
+    TRX_TRACE(3);
+    const int n_act = s_nact;
     bool failed = false;
+    int issued_g = 0, issued_d = 0; // the producer's counts, for the drain after a failure
 
-    // ---------------- gate / up / SwiGLU
-    int cur_t = -1;
-    TrxQ4X X;
-    int j = 0;
-    for (int64_t v = ag; v < bg && !failed; j++) {
-        const int64_t ve = gu_end(v);
-        const int slot = (int)(v / F), e = s_active[slot], r0 = (int)(v % F), n = (int)(ve - v);
-        const int p0 = s_off[e], p1 = s_off[e + 1];
-        const int s = j % SG;
-        if (GT == TRX_Q4_K && warp < n) {
-            const int t0 = __ldcg(w.xmap + p0);
-            if (t0 != cur_t) {
-                cur_t = t0;
-                trx_q4x_load<true>(w.xq + (int64_t)t0 * H + 256 * (lane >> 2), lane & 3, X);
+    if (warp == TRX_FU_CWARPS) {
+        // ---------------- the producer: every chunk of this CTA, in consumption order
+        if (lane == 0) {
+            TrxWalk gw, dw;
+            gw.init(n_act * F, F, CHG, false);
+            dw.init(n_act * H, H, CHD, true);
+            auto issue_g = [&](int s) {
+                const int e = s_active[gw.slot], n = gw.n();
+                uint8_t *dst = gu_buf + s * lay.gu_stage;
+                trx_mbar_expect_tx(&full_g[s], 2u * n * rbg);
+                trx_bulk_g2s(dst, L.gate + e * L.gate_mb + (int64_t)gw.r * rbg, n * rbg, &full_g[s]);
+                trx_bulk_g2s(dst + gu_half, L.up + e * L.up_mb + (int64_t)gw.r * rbg, n * rbg, &full_g[s]);
+            };
+            auto issue_d = [&](int s) {
+                const int e = s_active[dw.slot], n = dw.n();
+                trx_mbar_expect_tx(&full_d[s], (uint32_t)(n * rbd));
+                trx_bulk_g2s(dn_buf + s * lay.dn_stage, L.down + e * L.down_mb + (int64_t)dw.r * rbd, n * rbd, &full_d[s]);
+            };
+            for (; issued_g < SG && gw.more(); issued_g++, gw.next()) issue_g(issued_g);
+            for (; issued_d < SD && dw.more(); issued_d++, dw.next()) issue_d(issued_d);
+            for (; gw.more(); issued_g++, gw.next()) {
+                const int s = issued_g % SG;
+                if (!trx_mbar_wait(&empty_g[s], ((issued_g / SG) - 1) & 1, TRX_WAIT_NS)) {
+                    failed = true;
+                    break;
+                }
+                trx_fence_proxy_async();
+                issue_g(s);
+            }
+            for (; !failed && dw.more(); issued_d++, dw.next()) {
+                const int s = issued_d % SD;
+                if (!trx_mbar_wait(&empty_d[s], ((issued_d / SD) - 1) & 1, TRX_WAIT_NS)) {
+                    failed = true;
+                    break;
+                }
+                trx_fence_proxy_async();
+                issue_d(s);
             }
         }
-        const bool ok = trx_mbar_wait(&bar[s], (j / SG) & 1, TRX_WAIT_NS);
-        if (__syncthreads_or(!ok)) {
-            failed = true;
-            break;
-        }
-        const uint8_t *gs = gu_buf + s * gu_stage, *us = gs + gu_half;
-        for (int pg = p0; pg < p1; pg += TRX_TOK_GROUP) {
-            const int ng = min(TRX_TOK_GROUP, p1 - pg);
-            for (int q = 0; q < ng; q++) {
-                const int t = __ldcg(w.xmap + pg + q);
-                if (GT == TRX_Q4_K) {
-                    if (warp < n) {
-                        if (t != cur_t) {
-                            cur_t = t;
-                            trx_q4x_load<true>(w.xq + (int64_t)t * H + 256 * (lane >> 2), lane & 3, X);
+    } else {
+        // ---------------- a consumer warp: gate / up / SwiGLU, row `warp` of every chunk
+        int cur = -1; // the token (gate/up) or grouped row (down) whose input this warp holds
+        TrxQ4X X;
+        int jg = 0;
+        TrxWalk gw;
+        gw.init(n_act * F, F, CHG, false);
+        for (; gw.more(); jg++, gw.next()) {
+            const int slot = gw.slot, e = s_active[slot], r0 = gw.r, n = gw.n();
+            const int p0 = s_off[e], p1 = s_off[e + 1];
+            const int s = jg % SG;
+            if (!__all_sync(0xffffffffu, trx_mbar_wait(&full_g[s], (jg / SG) & 1, TRX_WAIT_NS))) {
+                failed = true;
+                break;
+            }
+            if (warp == 0 && jg < 8) TRX_TRACE(8 + jg);
+            if (warp < n) {
+                const uint8_t *gs = gu_buf + s * lay.gu_stage + warp * rbg, *us = gs + gu_half;
+                for (int p = p0; p < p1; p++) {
+                    const int t = s_xmap[p];
+                    const uint8_t *tok = s_tok + t * lay.tok_bytes;
+                    float g, u;
+                    if (GT == TRX_Q4_K) {
+                        if (t != cur) {
+                            const double *bfd = reinterpret_cast<const double *>(tok + (size_t)H * 4);
+                            trx_q4x_load(reinterpret_cast<const uint32_t *>(tok), 32, lane, bfd + 8 * (lane >> 2),
+                                         bfd + H / 32 + (lane >> 2), X);
+                            cur = t;
                         }
-                        const double *bf = w.xq_bf + (int64_t)t * (H / 32), *sc = w.xq_sc + (int64_t)t * (H / 256);
-                        const float g = trx_q4k_row8<true, true>(gs + warp * rbg, X, bf, sc, lane);
-                        const float u = trx_q4k_row8<true, true>(us + warp * rbg, X, bf, sc, lane);
-                        if (lane == 0) {
-                            res[0][q][warp] = g;
-                            res[1][q][warp] = u;
-                        }
+                        trx_q4k_row8x2<true>(gs, us, X, lane, g, u);
+                    } else { // half 0 the gate row, half 1 the up row
+                        g = trx_q8l_dot<true, false>(lane < 16 ? gs : us, reinterpret_cast<const float *>(tok), H / 256,
+                                                     lane & 15);
+                        u = __shfl_sync(0xffffffffu, g, 16);
                     }
-                } else {
-                    const int row = hw & 7, mat = hw >> 3;
-                    const float vv = trx_q8l_dot<true, true>((mat ? us : gs) + (row < n ? row : 0) * rbg,
-                                                             w.x_lc + (int64_t)t * H, H / 256, lane & 15);
-                    if (row < n && (lane & 15) == 0) res[mat][q][row] = vv;
+                    if (lane == 0) {
+                        const int r = r0 + warp;
+                        w.h[(int64_t)p * F + (DT != TRX_Q4_K ? trx_lc_pos(r) : r)] = trx_silu_mul(g, u);
+                    }
                 }
             }
-            __syncthreads();
-            for (int i = tid; i < ng * n; i += blockDim.x) {
-                const int q = i / n, row = i % n, r = r0 + row;
-                w.h[(int64_t)(pg + q) * F + (DT != TRX_Q4_K ? trx_lc_pos(r) : r)] =
-                    trx_silu_mul(res[0][q][row], res[1][q][row]);
+            if (warp == 0 && jg < 8) TRX_TRACE(40 + jg);
+            // Every consumer warp counts itself into the stage once per chunk (block scope, after its h stores); the
+            // last one publishes the chunk's n rows to the expert's count with one device-scope fence and atomic.
+            // A stage's uses are TRX_FU_CWARPS counts apart (a warp reaches its next use only after every warp's
+            // empty arrive), so the count's residue tells the last warp without a reset.
+            __syncwarp();
+            uint32_t last = 0;
+            if (lane == 0) {
+                __threadfence_block();
+                last = atomicAdd_block(&s_gcnt[s], 1u) % TRX_FU_CWARPS == TRX_FU_CWARPS - 1;
             }
-            __syncthreads();
-        }
-        if (tid == 0) {
-            __threadfence(); // this chunk's h rows before its count
-            atomicAdd(&sync->gu_done[slot], (uint32_t)n);
-            if (gu_iv < bg) { // stage s is free again
-                trx_fence_proxy_async();
-                issue_gu();
+            if (__shfl_sync(0xffffffffu, last, 0)) {
+                uint32_t old = 0;
+                if (lane == 0) {
+                    __threadfence(); // the chunk's h rows (this CTA's warps', observed above) before the count
+                    old = atomicAdd(&sync->gu_done[slot], (uint32_t)n);
+                }
+                old = __shfl_sync(0xffffffffu, old, 0);
+                if (DT == TRX_Q4_K && old + (uint32_t)n == (uint32_t)F) {
+                    // the expert's last chunk: every other row of it is counted, so its h rows are complete; prepare
+                    // them for the down's integer definition, then count once more
+                    __threadfence();
+                    for (int p = p0; p < p1; p++)
+                        for (int s4 = 0; s4 < nsb_d; s4++)
+                            trx_prep_q4x_block<true>(w.h + (int64_t)p * F + 256 * s4, w.hq + (int64_t)p * F, s4, nsb_d,
+                                                     w.hq_bf + (int64_t)p * (F / 32) + 8 * s4, w.hq_sc + (int64_t)p * nsb_d + s4,
+                                                     lane);
+                    __syncwarp();
+                    if (lane == 0) {
+                        __threadfence();
+                        atomicAdd(&sync->gu_done[slot], 1u);
+                    }
+                }
             }
+            __syncwarp();
+            if (lane == 0) trx_mbar_arrive(&empty_g[s]);
+            if (warp == 0 && jg < 8) TRX_TRACE(16 + jg);
         }
-        v = ve;
-    }
+        if (warp == 0) TRX_TRACE(4);
 
-    // ---------------- down + combine + residual
-    int prepped_p = -1;
-    j = 0;
-    for (int64_t v = ad; v < bd && !failed; j++) {
-        const int64_t ve = dn_end(v);
-        const int slot = (int)(v / H), e = s_active[slot], d0 = (int)(v % H), n = (int)(ve - v);
-        const int p0 = s_off[e], p1 = s_off[e + 1];
-        const int s = j % SD;
-        if (tid == 0) s_flag = trx_spin(&sync->gu_done[slot], (uint32_t)F, false);
-        __syncthreads();
-        if (!s_flag) {
-            failed = true;
-            break;
-        }
-        const bool ok = trx_mbar_wait(&bar[SG + s], (j / SD) & 1, TRX_WAIT_NS);
-        if (__syncthreads_or(!ok)) {
-            failed = true;
-            break;
-        }
-        const uint8_t *st = dn_buf + s * dn_stage;
-        const int row = hw < n ? hw : 0, d = d0 + row;
-        for (int p = p0; p < p1; p++) {
-            float vv;
-            if (DT == TRX_Q4_K) {
-                if (p != prepped_p) { // the h row prepared in shared memory (one warp per 256-block)
-                    __syncthreads();
-                    if (warp < nsb_d)
-                        trx_prep_q4x_block<true>(w.h + (int64_t)p * F + 256 * warp, s_planes + 256 * warp, s_bf + 8 * warp,
-                                                 s_sc + warp, lane);
-                    __syncthreads();
-                    prepped_p = p;
+        // ---------------- down + combine + residual, rows 2 warp and 2 warp + 1 of every chunk
+        cur = -1;
+        constexpr int NSB4 = 4; // the register road for F == 1024 (OLMoE)
+        float xr[NSB4 * 16];
+        const uint32_t need = (uint32_t)F + (DT == TRX_Q4_K ? 1u : 0u);
+        int jd = 0, ready = -1; // ready: the last slot whose gate/up rows this warp saw complete
+        TrxWalk dw;
+        dw.init(n_act * H, H, CHD, true);
+        for (; dw.more() && !failed; jd++, dw.next()) {
+            const int slot = dw.slot, e = s_active[slot], d0 = dw.r, n = dw.n();
+            const int p0 = s_off[e], p1 = s_off[e + 1];
+            const int s = jd % SD;
+            if (slot != ready) {
+                bool ok = true;
+                if (lane == 0) ok = trx_spin(&sync->gu_done[slot], need, false);
+                if (!__shfl_sync(0xffffffffu, ok, 0)) {
+                    failed = true;
+                    break;
                 }
-                trx_q4x_load(s_planes + 256 * ((lane >> 2) & 3), lane & 3, X);
-                vv = trx_q4k_row4<true>(st + row * rbd, X, s_bf, s_sc, lane);
-            } else if (DT == TRX_Q8_0) {
-                vv = trx_q8l_dot<true, true>(st + row * rbd, w.h + (int64_t)p * F, nsb_d, lane & 15);
-            } else {
-                const uint8_t *dptr = L.down + e * L.down_mb + (int64_t)H * rbd + (int64_t)d * nsb_d * 2;
-                vv = trx_q6l_dot<true, true>(st + row * rbd, dptr, w.h + (int64_t)p * F, nsb_d, lane & 15);
+                ready = slot;
             }
-            if (hw < n && (lane & 15) == 0) w.h3[(int64_t)p * H + d] = vv;
-        }
-        __syncthreads();
-        const int blk = d0 / CHD;
-        if (tid == 0) {
-            __threadfence();
-            const uint32_t old = atomicAdd(&w.comb_cnt[blk], (uint32_t)n);
-            s_flag = old + (uint32_t)n == (uint32_t)(n_act * CHD);
-            if (dn_iv < bd) {
-                trx_fence_proxy_async();
-                issue_dn();
+            if (!__all_sync(0xffffffffu, trx_mbar_wait(&full_d[s], (jd / SD) & 1, TRX_WAIT_NS))) {
+                failed = true;
+                break;
             }
-        }
-        __syncthreads();
-        if (s_flag) {
-            __threadfence();
-            for (int i = tid; i < T * CHD; i += blockDim.x) {
-                const int t = i / CHD, dd = blk * CHD + i % CHD;
-                float out = 0.0f;
-                for (int sl = 0; sl < k; sl++) {
-                    const int jj = t * k + sl;
-                    out = __fadd_rn(out, __fmul_rn(__ldcg(w.sel_w + jj), __ldcg(w.h3 + (int64_t)__ldcg(w.place + jj) * H + dd)));
+            if (warp == 0 && jd == 0) TRX_TRACE(5);
+            if (warp == 0 && jd < 8) TRX_TRACE(24 + jd);
+            const int row = 2 * warp + (lane >> 4), rowc = row < n ? row : 2 * warp, d = d0 + rowc;
+            if (2 * warp < n) {
+                const uint8_t *st = dn_buf + s * lay.dn_stage + rowc * rbd;
+                for (int p = p0; p < p1; p++) {
+                    float vv;
+                    if (DT == TRX_Q4_K) {
+                        if (p != cur) {
+                            trx_q4x_load<true>(w.hq + (int64_t)p * F, 16, lane & 15,
+                                               w.hq_bf + (int64_t)p * (F / 32) + 8 * ((lane >> 2) & 3),
+                                               w.hq_sc + (int64_t)p * nsb_d + ((lane >> 2) & 3), X);
+                            cur = p;
+                        }
+                        vv = trx_q4k_row4<true>(st, X, lane);
+                    } else if (nsb_d == NSB4) {
+                        if (p != cur) {
+                            trx_lc_load<NSB4, true>(w.h + (int64_t)p * F, lane & 15, xr);
+                            cur = p;
+                        }
+                        if (DT == TRX_Q8_0) {
+                            vv = trx_q8l_dot_reg<NSB4>(st, xr, lane & 15);
+                        } else {
+                            const uint8_t *dptr = L.down + e * L.down_mb + (int64_t)H * rbd + (int64_t)d * NSB4 * 2;
+                            vv = trx_q6l_dot_reg<NSB4>(st, dptr, xr, lane & 15);
+                        }
+                    } else if (DT == TRX_Q8_0) {
+                        vv = trx_q8l_dot<true, true>(st, w.h + (int64_t)p * F, nsb_d, lane & 15);
+                    } else {
+                        const uint8_t *dptr = L.down + e * L.down_mb + (int64_t)H * rbd + (int64_t)d * nsb_d * 2;
+                        vv = trx_q6l_dot<true, true>(st, dptr, w.h + (int64_t)p * F, nsb_d, lane & 15);
+                    }
+                    if (row < n && (lane & 15) == 0) w.h3[(int64_t)p * H + d] = vv;
                 }
-                if (ffn_out) ffn_out[(int64_t)t * H + dd] = out;
-                x_io[(int64_t)t * H + dd] = __fadd_rn(x_io[(int64_t)t * H + dd], out);
             }
-            if (tid == 0) w.comb_cnt[blk] = 0u;
+            __syncwarp();
+            if (warp == 0 && jd < 6) TRX_TRACE(53 + jd);
+            // count the chunk's rows into their 16-row block: the stage's last warp (as for gate/up) adds the chunk's
+            // n rows; the warp completing the block combines it
+            const int blk = d0 / CHD;
+            bool last = false;
+            if (lane == 0) {
+                __threadfence_block();
+                if (atomicAdd_block(&s_dcnt[s], 1u) % TRX_FU_CWARPS == TRX_FU_CWARPS - 1) {
+                    __threadfence();
+                    const uint32_t old = atomicAdd(&w.comb_cnt[blk], (uint32_t)n);
+                    last = old + (uint32_t)n == (uint32_t)(n_act * CHD);
+                }
+            }
+            if (__shfl_sync(0xffffffffu, last, 0)) {
+                __threadfence();
+                for (int i = lane; i < T * CHD; i += 32) {
+                    const int t = i / CHD, dd = blk * CHD + i % CHD;
+                    float out = 0.0f;
+                    for (int sl = 0; sl < k; sl++) {
+                        const int jj = t * k + sl;
+                        out = __fadd_rn(out, __fmul_rn(s_selw[jj], __ldcg(w.h3 + (int64_t)s_place[jj] * H + dd)));
+                    }
+                    if (ffn_out) ffn_out[(int64_t)t * H + dd] = out;
+                    x_io[(int64_t)t * H + dd] = __fadd_rn(x_io[(int64_t)t * H + dd], out);
+                }
+                if (lane == 0) w.comb_cnt[blk] = 0u;
+            }
+            __syncwarp();
+            if (lane == 0) trx_mbar_arrive(&empty_d[s]);
+            if (warp == 0 && jd < 8) TRX_TRACE(32 + jd);
         }
-        v = ve;
+        if (warp == 0) TRX_TRACE(6);
     }
 
     // ---------------- end
-    if (failed) {
-        if (tid == 0) {
+    if (__syncthreads_or(failed)) {
+        if (warp == TRX_FU_CWARPS && lane == 0) {
             atomicExch(w.err, 3);
             // every copy still in flight lands before the CTA's shared memory goes away
-            for (int q = 0; q < gu_issued; q++) trx_mbar_wait(&bar[q % SG], (q / SG) & 1, TRX_WAIT_NS);
-            for (int q = 0; q < dn_issued; q++) trx_mbar_wait(&bar[SG + q % SD], (q / SD) & 1, TRX_WAIT_NS);
+            for (int q = 0; q < issued_g; q++) trx_mbar_wait(&full_g[q % SG], (q / SG) & 1, TRX_WAIT_NS);
+            for (int q = 0; q < issued_d; q++) trx_mbar_wait(&full_d[q % SD], (q / SD) & 1, TRX_WAIT_NS);
         }
         __syncthreads();
         return;
     }
-    __syncthreads();
+    TRX_TRACE(52);
     if (tid == 0) {
         __threadfence();
         if (atomicAdd(&sync->finish, 1u) == gridDim.x - 1) { // every CTA is past its waits

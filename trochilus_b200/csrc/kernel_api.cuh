@@ -16,8 +16,8 @@ __global__ void trx_kapi_prep_q4x(const float *__restrict__ x, int n_in, int col
     const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int p = gw / nsb, s = gw % nsb;
     if (p >= n_in) return;
-    trx_prep_q4x_block(x + (int64_t)p * cols + 256 * s, q + (int64_t)p * cols + 256 * s,
-                       bf + (int64_t)p * (cols / 32) + 8 * s, sc + (int64_t)p * nsb + s, threadIdx.x & 31);
+    trx_prep_q4x_block(x + (int64_t)p * cols + 256 * s, q + (int64_t)p * cols, s, nsb, bf + (int64_t)p * (cols / 32) + 8 * s,
+                       sc + (int64_t)p * nsb + s, threadIdx.x & 31);
 }
 
 __global__ void trx_kapi_lc(const float *__restrict__ x, int64_t total, int cols, float *__restrict__ y) {
@@ -37,21 +37,19 @@ __device__ __forceinline__ float trx_q4k_row_any(const uint8_t *__restrict__ row
     for (int s0 = 0; s0 < nsb; s0 += 8) {
         const int s = s0 + (lane >> 2);
         const bool valid = s < nsb;
-        int64_t T = 0;
+        int64_t T = 0, M = 0;
         uint4 hdr = make_uint4(0, 0, 0, 0);
+        TrxQ4X X;
+        X.sc = 0.0;
         if (valid) {
-            TrxQ4X X;
-            trx_q4x_load(planes + 256 * s, c, X);
+            trx_q4x_load(planes + 2048 * (s >> 3), trx_q4x_lanes(s, nsb), lane, bf + 8 * s, sc + s, X);
             const uint8_t *blk = row + 144 * s;
             hdr = __ldg(reinterpret_cast<const uint4 *>(blk));
             const uint4 q0 = __ldg(reinterpret_cast<const uint4 *>(blk + 16 + 32 * c));
             const uint4 q1 = __ldg(reinterpret_cast<const uint4 *>(blk + 32 + 32 * c));
-            T = trx_q4k_chunk_T(hdr, q0, q1, c, X);
+            trx_q4k_chunk(hdr, q0, q1, c, X, T, M);
         }
-        T += trx_shfl_xor64(T, 1);
-        T += trx_shfl_xor64(T, 2);
-        double v = 0.0;
-        if (valid && c == 0) v = trx_q4k_finish(hdr, T, bf + 8 * s, sc[s]);
+        const double v = trx_q4k_value(hdr, T, M, X.sc); // every lane takes part in the shuffles
         for (int i = 0; i < 8 && s0 + i < nsb; i++) y = __dadd_rn(y, trx_shfl_d(v, 4 * i));
     }
     return __double2float_rn(y);

@@ -115,18 +115,40 @@ __global__ void trx_repack_q6l(const uint8_t *__restrict__ src, uint8_t *__restr
     }
 }
 
+// Router rows (F32 or BF16, n % 256 == 0) -> "lane rows": inside every 256 elements, lane l's 16 elements
+// (l + 16 m, m = 0..15) contiguous at 16 l + m, so one thread of a 16-lane chain reads its lane with 16-byte loads
+__global__ void trx_repack_lanerows(const uint8_t *__restrict__ src, uint8_t *__restrict__ dst, int64_t rows, int64_t n,
+                                    int elem) {
+    const int64_t r = blockIdx.x;
+    if (r >= rows) return;
+    for (int64_t k = threadIdx.x; k < n; k += blockDim.x) {
+        const int64_t i = k >> 8, l = k & 15, m = (k >> 4) & 15;
+        const int64_t q = (i << 8) + 16 * l + m;
+        for (int b = 0; b < elem; b++) dst[(r * n + q) * elem + b] = src[(r * n + k) * elem + b];
+    }
+}
+
 // ---- input-row preparation ----
 
-// Q4_K's prepared input row of n floats (n % 256 == 0), per 256-block s:
-//   planes: word ((s*4 + c)*4 + p)*16 + g = byte p of X at elements 256 s + 64 c + 4 g .. +3
-//   bf[8 s + j] = sum of X over sub-block j (exact, as a double); scale[s] = 2^-sh, NaN for a block
-//   holding a NaN or an infinity (its X then 0). Restated from Trochilus k_q4x_prep
-//   (src/kernels/kernels.c:200-239) and tr_q4x_shift (src/kernels/kernels_internal.h:150-166).
-// One warp per 256-block; lane L takes elements 8 L .. 8 L + 7.
-// CG: read x through L2 only (rows another CTA of the same kernel wrote)
+// Q4_K's prepared input row of n floats (n % 256 == 0). Per 256-block s: X = nearest-even(x 2^sh_s) as 4 byte
+// planes; bf[8 s + j] = the exact sum of X over sub-block j (a double); scale[s] = 2^-sh_s, NaN for a block
+// holding a NaN or an infinity (its X then 0). Restated from Trochilus k_q4x_prep (src/kernels/kernels.c:200-239)
+// and tr_q4x_shift (src/kernels/kernels_internal.h:150-166).
+// The planes are laid out for the warps that read them: a row's blocks go in passes of up to 8 (pass P: blocks
+// 8P .. 8P + NB - 1), read by NL = 4 NB lanes, lane L = 4 (s mod 8) + c taking chunk c (64 inputs) of block s as
+// 16 words-of-4: its q-th 16 bytes sit at words 2048 P + 4 (q NL + L), so that every 16-byte load of a warp is
+// one contiguous NL x 16 bytes. Word j = 16 p + g of a lane holds byte p of X at elements 256 s + 64 c + 4 g .. +3.
+__host__ __device__ inline int trx_q4x_lanes(int s, int nsb) {
+    const int nb = nsb - (s & ~7);
+    return 4 * (nb < 8 ? nb : 8);
+}
+
+// One warp per 256-block; lane L takes elements 8 L .. 8 L + 7. CG: read x through L2 only (a row another CTA of
+// the same kernel wrote). planes_row, bf_blk, sc_blk: the row's planes, the block's sums and scale.
 template <bool CG = false>
-__device__ __forceinline__ void trx_prep_q4x_block(const float *__restrict__ x, uint32_t *__restrict__ planes,
-                                                   double *__restrict__ bf, double *__restrict__ scale, int lane) {
+__device__ __forceinline__ void trx_prep_q4x_block(const float *__restrict__ x, uint32_t *__restrict__ planes_row, int s,
+                                                   int nsb, double *__restrict__ bf_blk, double *__restrict__ sc_blk,
+                                                   int lane) {
     float v[8];
     const float4 a = trx_ldx<CG>(x + 8 * lane);
     const float4 b = trx_ldx<CG>(x + 8 * lane + 4);
@@ -161,15 +183,16 @@ __device__ __forceinline__ void trx_prep_q4x_block(const float *__restrict__ x, 
         X[i] = bad ? 0 : (int32_t)__double2ll_rn(t);   // nearest, ties to even
     }
     // sub-block sums: sub-block j holds lanes 4 j .. 4 j + 3
-    int64_t s = 0;
+    int64_t sum = 0;
 #pragma unroll
-    for (int i = 0; i < 8; i++) s += X[i];
-    s += trx_shfl_xor64(s, 1);
-    s += trx_shfl_xor64(s, 2);
-    if ((lane & 3) == 0) bf[lane >> 2] = (double)s;
-    if (lane == 0) scale[0] = bad ? __longlong_as_double(0x7ff8000000000000ll) : ldexp(1.0, -sh);
-    // planes: chunk c = lane / 8, groups g = 2 (lane % 8), 2 (lane % 8) + 1
-    const int c = lane >> 3, g = 2 * (lane & 7);
+    for (int i = 0; i < 8; i++) sum += X[i];
+    sum += trx_shfl_xor64(sum, 1);
+    sum += trx_shfl_xor64(sum, 2);
+    if ((lane & 3) == 0) bf_blk[lane >> 2] = (double)sum;
+    if (lane == 0) sc_blk[0] = bad ? __longlong_as_double(0x7ff8000000000000ll) : ldexp(1.0, -sh);
+    // this lane's 8 elements: chunk c = lane / 8, groups g, g + 1 (g = 2 (lane % 8)) of consumer lane 4 (s % 8) + c
+    const int c = lane >> 3, g = 2 * (lane & 7), NL = trx_q4x_lanes(s, nsb), L = 4 * (s & 7) + c;
+    uint32_t *pass = planes_row + 2048 * (s >> 3);
 #pragma unroll
     for (int p = 0; p < 4; p++) {
         uint32_t w0 = 0, w1 = 0;
@@ -178,9 +201,8 @@ __device__ __forceinline__ void trx_prep_q4x_block(const float *__restrict__ x, 
             w0 |= (((uint32_t)X[i] >> (8 * p)) & 255u) << (8 * i);
             w1 |= (((uint32_t)X[4 + i] >> (8 * p)) & 255u) << (8 * i);
         }
-        uint32_t *dst = planes + ((c * 4 + p) * 16 + g);
-        dst[0] = w0;
-        dst[1] = w1;
+        const int j = 16 * p + g; // g even: words j and j + 1 share a 16-byte group
+        *reinterpret_cast<uint2 *>(pass + 4 * ((j >> 2) * NL + L) + (j & 3)) = make_uint2(w0, w1);
     }
 }
 
@@ -195,29 +217,39 @@ __device__ __forceinline__ V trx_ld(const void *p) {
 }
 
 // Q4_K: the 4 * G lanes of a row group hold G blocks (lane: block s = lane/4 % G, chunk c = lane % 4)
-// X registers: the thread's 64 inputs as 4 byte planes x 16 words
 struct TrxQ4X {
-    uint32_t w[4][16];
+    uint32_t w[4][16]; // the thread's 64 inputs as 4 byte planes x 16 words
+    int64_t b[2];      // the sums of X over its chunk's sub-blocks 2c and 2c + 1 (exact integers)
+    double sc;         // its block's 2^-sh (NaN for a block holding a NaN or an infinity)
 };
 
-// CG: through L2 only (__ldcg), for rows another CTA of the same kernel wrote
+// The thread's share of a prepared row (trx_prep_q4x_block's layout): lane L of NL reading the pass whose planes
+// start at pass_planes, and its block's sub-block sums (bf_blk[0..7]) and scale (*sc_blk). CG: through L2 only
+// (__ldcg), for a row another CTA of the same kernel wrote.
 template <bool CG = false>
-__device__ __forceinline__ void trx_q4x_load(const uint32_t *__restrict__ planes_blk, int c, TrxQ4X &X) {
-    const uint4 *src = reinterpret_cast<const uint4 *>(planes_blk + c * 64);
+__device__ __forceinline__ void trx_q4x_load(const uint32_t *__restrict__ pass_planes, int NL, int L,
+                                             const double *__restrict__ bf_blk, const double *__restrict__ sc_blk,
+                                             TrxQ4X &X) {
+    const int c = L & 3;
+    X.b[0] = trx_d2i(CG ? __ldcg(bf_blk + 2 * c) : bf_blk[2 * c]);
+    X.b[1] = trx_d2i(CG ? __ldcg(bf_blk + 2 * c + 1) : bf_blk[2 * c + 1]);
+    X.sc = CG ? __ldcg(sc_blk) : *sc_blk;
+    const uint4 *src = reinterpret_cast<const uint4 *>(pass_planes) + L;
 #pragma unroll
-    for (int p = 0; p < 4; p++)
-#pragma unroll
-        for (int q = 0; q < 4; q++) {
-            const uint4 v = CG ? __ldcg(src + p * 4 + q) : src[p * 4 + q];
-            X.w[p][4 * q + 0] = v.x;
-            X.w[p][4 * q + 1] = v.y;
-            X.w[p][4 * q + 2] = v.z;
-            X.w[p][4 * q + 3] = v.w;
-        }
+    for (int q = 0; q < 16; q++) {
+        const uint4 v = CG ? __ldcg(src + q * NL) : src[q * NL];
+        X.w[q >> 2][4 * (q & 3) + 0] = v.x;
+        X.w[q >> 2][4 * (q & 3) + 1] = v.y;
+        X.w[q >> 2][4 * (q & 3) + 2] = v.z;
+        X.w[q >> 2][4 * (q & 3) + 3] = v.w;
+    }
 }
 
-// One thread's part of T for its 32-byte chunk c of a block whose header is hdr and quants q0, q1.
-__device__ __forceinline__ int64_t trx_q4k_chunk_T(uint4 hdr, uint4 q0, uint4 q1, int c, const TrxQ4X &X) {
+// One thread's part of a block's T = sum_j sc_j sum q X and M = sum_j m_j sum X, for its 32-byte chunk c (sub-blocks
+// 2c: the low nibbles, 2c + 1: the high nibbles) of a block whose header is hdr and quants q0, q1. Both are exact
+// integers, so the four chunks' parts add in any order.
+__device__ __forceinline__ void trx_q4k_chunk(uint4 hdr, uint4 q0, uint4 q1, int c, const TrxQ4X &X, int64_t &T,
+                                              int64_t &M) {
     const uint32_t words[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
     uint32_t alo[3] = {0, 0, 0}, ahi[3] = {0, 0, 0};
     int slo = 0, shi = 0;
@@ -232,37 +264,101 @@ __device__ __forceinline__ int64_t trx_q4k_chunk_T(uint4 hdr, uint4 q0, uint4 q1
         slo = __dp4a((int)lo, (int)X.w[3][i], slo);
         shi = __dp4a((int)hi, (int)X.w[3][8 + i], shi);
     }
-    // 6-bit scales of sub-blocks 2c and 2c+1 from the 12 packed bytes (header bytes 4..15)
-    const uint32_t sw[3] = {hdr.y, hdr.z, hdr.w};
-    auto sbyte = [&](int i) -> int { return (int)((sw[i >> 2] >> (8 * (i & 3))) & 255u); };
-    int sc_lo, sc_hi;
-    {
-        const int j0 = 2 * c, j1 = 2 * c + 1;
-        sc_lo = j0 < 4 ? (sbyte(j0) & 63) : ((sbyte(j0 + 4) & 15) | ((sbyte(j0 - 4) >> 6) << 4));
-        sc_hi = j1 < 4 ? (sbyte(j1) & 63) : ((sbyte(j1 + 4) & 15) | ((sbyte(j1 - 4) >> 6) << 4));
+    // the 6-bit scales and mins of sub-blocks 2c, 2c + 1 from the 12 packed bytes (header words y, z, w):
+    // j < 4: sc = byte j & 63, m = byte j + 4 & 63; j >= 4: the low (sc) or high (m) nibble of byte j + 4 and the top
+    // two bits of byte j - 4 (sc) or byte j (m)
+    const int sh = 16 * (c & 1);
+    const uint32_t y2 = hdr.y >> sh, z2 = hdr.z >> sh, w2 = hdr.w >> sh;
+    int sc0, sc1, m0, m1;
+    if (c < 2) {
+        sc0 = (int)(y2 & 63u);
+        sc1 = (int)((y2 >> 8) & 63u);
+        m0 = (int)(z2 & 63u);
+        m1 = (int)((z2 >> 8) & 63u);
+    } else {
+        sc0 = (int)((w2 & 15u) | (((y2 >> 6) & 3u) << 4));
+        sc1 = (int)(((w2 >> 8) & 15u) | (((y2 >> 14) & 3u) << 4));
+        m0 = (int)(((w2 >> 4) & 15u) | (((z2 >> 6) & 3u) << 4));
+        m1 = (int)(((w2 >> 12) & 15u) | (((z2 >> 14) & 3u) << 4));
     }
-    const int64_t b0 = (int64_t)sc_lo * alo[0] + (int64_t)sc_hi * ahi[0];
-    const int64_t b1 = (int64_t)sc_lo * alo[1] + (int64_t)sc_hi * ahi[1];
-    const int64_t b2 = (int64_t)sc_lo * alo[2] + (int64_t)sc_hi * ahi[2];
-    const int64_t b3 = (int64_t)sc_lo * slo + (int64_t)sc_hi * shi;
-    return b0 + (b1 << 8) + (b2 << 16) + b3 * 16777216ll;
+    const int64_t b0 = (int64_t)sc0 * alo[0] + (int64_t)sc1 * ahi[0];
+    const int64_t b1 = (int64_t)sc0 * alo[1] + (int64_t)sc1 * ahi[1];
+    const int64_t b2 = (int64_t)sc0 * alo[2] + (int64_t)sc1 * ahi[2];
+    const int64_t b3 = (int64_t)sc0 * slo + (int64_t)sc1 * shi;
+    T = b0 + (b1 << 8) + (b2 << 16) + b3 * 16777216ll;
+    M = (int64_t)m0 * X.b[0] + (int64_t)m1 * X.b[1];
 }
 
-// M of a block: sum_j m_j bf_j (exact: |bf| < 2^37, m < 64), then v = (d T - dmin M) scale in f64
-template <bool CG = false>
-__device__ __forceinline__ double trx_q4k_finish(uint4 hdr, int64_t T, const double *__restrict__ bf, double scale) {
-    const uint32_t sw[3] = {hdr.y, hdr.z, hdr.w};
-    auto sbyte = [&](int i) -> int { return (int)((sw[i >> 2] >> (8 * (i & 3))) & 255u); };
-    int64_t M = 0;
+// T and M summed over the 4 threads of a block (xor 1, 2), then v = (d T - dmin M) 2^-sh in f64, in every thread
+// of the group (|T| < 2^49, |M| < 2^45: exact as doubles)
+__device__ __forceinline__ double trx_q4k_value(uint4 hdr, int64_t T, int64_t M, double sc) {
+    T += trx_shfl_xor64(T, 1);
+    M += trx_shfl_xor64(M, 1);
+    T += trx_shfl_xor64(T, 2);
+    M += trx_shfl_xor64(M, 2);
+    const double d = trx_half_d((uint16_t)(hdr.x & 0xffffu));
+    const double dmin = trx_half_d((uint16_t)(hdr.x >> 16));
+    const double val = __dsub_rn(__dmul_rn(d, trx_i2d(T)), __dmul_rn(dmin, trx_i2d(M)));
+    return __dmul_rn(val, sc);
+}
+
+// One 256-block of the lane contract for thread l of a half-warp: its 16 elements k = 256 i + l + 16 m, m = 0..15,
+// dequantised and multiplied two at a time with the paired operations (each product rounded on its own), then added
+// to the thread's running sum one at a time in order of m.
+
+// Q8L: sc = the block's 8 f16 scales (element m has scale m / 2), q = the thread's 16 quants (byte m = element m)
+__device__ __forceinline__ float trx_q8l_block(float acc, uint4 sc, uint4 q, const float (&xv)[16]) {
+    const uint32_t qw[4] = {q.x ^ 0x80808080u, q.y ^ 0x80808080u, q.z ^ 0x80808080u, q.w ^ 0x80808080u};
+    const uint32_t sw[4] = {sc.x, sc.y, sc.z, sc.w};
+    const trx_f2 bias = trx_pack2(8388736.0f, 8388736.0f); // 2^23 + 128
 #pragma unroll
-    for (int j = 0; j < 8; j++) {
-        const int mj = j < 4 ? (sbyte(j + 4) & 63) : ((sbyte(j + 4) >> 4) | ((sbyte(j) >> 6) << 4));
-        M += (int64_t)mj * (int64_t)(CG ? __ldcg(bf + j) : bf[j]);
+    for (int m = 0; m < 16; m += 2) {
+        const float d = trx_half((uint16_t)(sw[m >> 2] >> (16 * ((m >> 1) & 1))));
+        // the int8 quants as floats from their bits: 2^23 + (q + 128), less 2^23 + 128 (exact)
+        const trx_f2 qf = trx_sub2(trx_pack2(__uint_as_float(__byte_perm(qw[m >> 2], 0x4b000000u, 0x7440u | (m & 3))),
+                                             __uint_as_float(__byte_perm(qw[m >> 2], 0x4b000000u, 0x7440u | ((m + 1) & 3)))),
+                                   bias);
+        const trx_f2 p = trx_mul2(trx_mul2(trx_pack2(d, d), qf), trx_pack2(xv[m], xv[m + 1]));
+        acc = __fadd_rn(acc, trx_lo(p));
+        acc = __fadd_rn(acc, trx_hi(p));
     }
-    const double d = (double)trx_half((uint16_t)(hdr.x & 0xffffu));
-    const double dmin = (double)trx_half((uint16_t)(hdr.x >> 16));
-    const double val = __dsub_rn(__dmul_rn(d, (double)T), __dmul_rn(dmin, (double)M));
-    return __dmul_rn(val, scale);
+    return acc;
+}
+
+// Q6L: ql = the thread's 16 low nibbles (element m: bits 4 (m % 8) of word m / 8), qh = its 16 high bit pairs
+// (bits 2 m), scv = the block's 16 int8 sub-block scales (element m has scale m), d = the block's f16 d
+__device__ __forceinline__ float trx_q6l_block(float acc, uint2 ql, uint32_t qh, uint4 scv, float d, const float (&xv)[16]) {
+    const uint32_t scw[4] = {scv.x ^ 0x80808080u, scv.y ^ 0x80808080u, scv.z ^ 0x80808080u, scv.w ^ 0x80808080u};
+    const uint32_t qlw[2] = {ql.x, ql.y};
+    const trx_f2 d2 = trx_pack2(d, d), bias8 = trx_pack2(8388736.0f, 8388736.0f), bias6 = trx_pack2(8388640.0f, 8388640.0f);
+    auto qbits = [&](int m) { // 2^23 + the 6-bit quant, as float bits
+        return 0x4b000000u | ((qlw[m >> 3] >> (4 * (m & 7))) & 15u) | (((qh >> (2 * m)) & 3u) << 4);
+    };
+#pragma unroll
+    for (int m = 0; m < 16; m += 2) {
+        const trx_f2 scf = trx_sub2(trx_pack2(__uint_as_float(__byte_perm(scw[m >> 2], 0x4b000000u, 0x7440u | (m & 3))),
+                                              __uint_as_float(__byte_perm(scw[m >> 2], 0x4b000000u, 0x7440u | ((m + 1) & 3)))),
+                                    bias8);
+        const trx_f2 scale = trx_mul2(d2, scf);                                                  // d * sc
+        const trx_f2 qv = trx_sub2(trx_pack2(__uint_as_float(qbits(m)), __uint_as_float(qbits(m + 1))), bias6); // q - 32
+        const trx_f2 p = trx_mul2(trx_mul2(scale, qv), trx_pack2(xv[m], xv[m + 1]));
+        acc = __fadd_rn(acc, trx_lo(p));
+        acc = __fadd_rn(acc, trx_hi(p));
+    }
+    return acc;
+}
+
+// the thread's 16 inputs of block i of an LC-ordered row
+template <bool CG>
+__device__ __forceinline__ void trx_lc_block(const float *__restrict__ xlc, int i, int l, float (&xv)[16]) {
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+        const float4 v = trx_ldx<CG>(xlc + 256 * i + 64 * q + 4 * l);
+        xv[4 * q] = v.x;
+        xv[4 * q + 1] = v.y;
+        xv[4 * q + 2] = v.z;
+        xv[4 * q + 3] = v.w;
+    }
 }
 
 // Q8L lane-contract dot of one row (n = 256 * nch) against an LC-ordered input row; thread l of the
@@ -272,23 +368,9 @@ __device__ __forceinline__ float trx_q8l_dot(const uint8_t *__restrict__ row, co
                                              int l) {
     float acc = 0.0f;
     for (int i = 0; i < nch; i++) {
-        const uint4 sc = trx_ld<SM, uint4>(row + 272 * i);
-        const uint4 q = trx_ld<SM, uint4>(row + 272 * i + 16 + 16 * l);
-        const float *xs = xlc + 256 * i + 4 * l;
-        const float4 x0 = trx_ldx<CG>(xs);
-        const float4 x1 = trx_ldx<CG>(xs + 64);
-        const float4 x2 = trx_ldx<CG>(xs + 128);
-        const float4 x3 = trx_ldx<CG>(xs + 192);
-        const float xv[16] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w,
-                              x2.x, x2.y, x2.z, x2.w, x3.x, x3.y, x3.z, x3.w};
-        const uint32_t qw[4] = {q.x ^ 0x80808080u, q.y ^ 0x80808080u, q.z ^ 0x80808080u, q.w ^ 0x80808080u};
-        const uint32_t sw[4] = {sc.x, sc.y, sc.z, sc.w};
-#pragma unroll
-        for (int m = 0; m < 16; m++) {
-            const float d = trx_half((uint16_t)(sw[m >> 2] >> (16 * ((m >> 1) & 1))));
-            const float w = __fmul_rn(d, trx_s8_to_f32(qw[m >> 2], m & 3));
-            acc = __fadd_rn(acc, __fmul_rn(w, xv[m]));
-        }
+        float xv[16];
+        trx_lc_block<CG>(xlc, i, l, xv);
+        acc = trx_q8l_block(acc, trx_ld<SM, uint4>(row + 272 * i), trx_ld<SM, uint4>(row + 272 * i + 16 + 16 * l), xv);
     }
     return trx_lane_tree16(acc);
 }
@@ -299,29 +381,58 @@ __device__ __forceinline__ float trx_q6l_dot(const uint8_t *__restrict__ row, co
                                              const float *__restrict__ xlc, int nsb, int l) {
     float acc = 0.0f;
     for (int s = 0; s < nsb; s++) {
-        const uint2 ql = trx_ld<SM, uint2>(row + 128 * s + 8 * l);
-        const uint32_t qh = trx_ld<SM, uint32_t>(row + 128 * nsb + 64 * s + 4 * l);
-        const uint4 scv = trx_ld<SM, uint4>(row + 192 * nsb + 16 * s);
-        const float d = trx_half(__ldg(reinterpret_cast<const uint16_t *>(dptr) + s));
-        const float *xs = xlc + 256 * s + 4 * l;
-        const float4 x0 = trx_ldx<CG>(xs);
-        const float4 x1 = trx_ldx<CG>(xs + 64);
-        const float4 x2 = trx_ldx<CG>(xs + 128);
-        const float4 x3 = trx_ldx<CG>(xs + 192);
-        const float xv[16] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w,
-                              x2.x, x2.y, x2.z, x2.w, x3.x, x3.y, x3.z, x3.w};
-        const uint32_t scw[4] = {scv.x, scv.y, scv.z, scv.w};
-        const uint32_t qlw[2] = {ql.x, ql.y};
+        float xv[16];
+        trx_lc_block<CG>(xlc, s, l, xv);
+        acc = trx_q6l_block(acc, trx_ld<SM, uint2>(row + 128 * s + 8 * l), trx_ld<SM, uint32_t>(row + 128 * nsb + 64 * s + 4 * l),
+                            trx_ld<SM, uint4>(row + 192 * nsb + 16 * s),
+                            trx_half(__ldg(reinterpret_cast<const uint16_t *>(dptr) + s)), xv);
+    }
+    return trx_lane_tree16(acc);
+}
+
+// The thread's 16 inputs of each of NCH 256-chunks of an LC-ordered row, in registers (CG: through L2)
+template <int NCH, bool CG>
+__device__ __forceinline__ void trx_lc_load(const float *__restrict__ xlc, int l, float (&xr)[NCH * 16]) {
 #pragma unroll
-        for (int m = 0; m < 16; m++) {
-            const int sc = (int)(int8_t)(uint8_t)(scw[m >> 2] >> (8 * (m & 3)));
-            const float scale = __fmul_rn(d, (float)sc);
-            const uint32_t lo = (qlw[m >> 3] >> (4 * (m & 7))) & 15u;
-            const uint32_t hi = (qh >> (2 * m)) & 3u;
-            const int q = (int)(lo | (hi << 4)) - 32;
-            const float w = __fmul_rn(scale, (float)q);
-            acc = __fadd_rn(acc, __fmul_rn(w, xv[m]));
+    for (int i = 0; i < NCH; i++)
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            const float4 v = trx_ldx<CG>(xlc + 256 * i + 64 * q + 4 * l);
+            xr[16 * i + 4 * q] = v.x;
+            xr[16 * i + 4 * q + 1] = v.y;
+            xr[16 * i + 4 * q + 2] = v.z;
+            xr[16 * i + 4 * q + 3] = v.w;
         }
+}
+
+// trx_q8l_dot / trx_q6l_dot of a row in shared memory against inputs already in registers
+template <int NCH>
+__device__ __forceinline__ float trx_q8l_dot_reg(const uint8_t *__restrict__ row, const float (&xr)[NCH * 16], int l) {
+    float acc = 0.0f;
+#pragma unroll
+    for (int i = 0; i < NCH; i++) {
+        float xv[16];
+#pragma unroll
+        for (int m = 0; m < 16; m++) xv[m] = xr[16 * i + m];
+        acc = trx_q8l_block(acc, *reinterpret_cast<const uint4 *>(row + 272 * i),
+                            *reinterpret_cast<const uint4 *>(row + 272 * i + 16 + 16 * l), xv);
+    }
+    return trx_lane_tree16(acc);
+}
+
+template <int NSB>
+__device__ __forceinline__ float trx_q6l_dot_reg(const uint8_t *__restrict__ row, const uint8_t *__restrict__ dptr,
+                                                 const float (&xr)[NSB * 16], int l) {
+    float acc = 0.0f;
+#pragma unroll
+    for (int s = 0; s < NSB; s++) {
+        float xv[16];
+#pragma unroll
+        for (int m = 0; m < 16; m++) xv[m] = xr[16 * s + m];
+        acc = trx_q6l_block(acc, *reinterpret_cast<const uint2 *>(row + 128 * s + 8 * l),
+                            *reinterpret_cast<const uint32_t *>(row + 128 * NSB + 64 * s + 4 * l),
+                            *reinterpret_cast<const uint4 *>(row + 192 * NSB + 16 * s),
+                            trx_half(__ldg(reinterpret_cast<const uint16_t *>(dptr) + s)), xv);
     }
     return trx_lane_tree16(acc);
 }

@@ -76,6 +76,7 @@ struct TrxWork {
     int64_t *out_offsets;
     int64_t *out_place;
     float *out_logits;
+    uint64_t *trace;     // NULL, or 64 %globaltimer slots per CTA of the fused kernel (tr_gpu_moe_trace)
 };
 
 // ---------------------------------------------------------------------------------------------
@@ -86,10 +87,12 @@ struct TrxWork {
 // infinite logit, or every logit -inf) or none is; the reference's repeated argmax (first untaken id when it
 // is NaN, else the largest, ties to the lower id) then picks ids 0..k-1 in the first case and the k largest
 // by (value, -id) in the second. The rank of each value among all E gives the latter directly.
+template <bool SM = false>
 __device__ void trx_route_token(const float *__restrict__ logits, int E, int k, int norm_topk, int lane,
                                 float *__restrict__ sp, int32_t *ids_out, float *w_out) {
     const bool ok0 = lane < E, ok1 = lane + 32 < E;
-    const float v0 = ok0 ? __ldcg(logits + lane) : 0.0f, v1 = ok1 ? __ldcg(logits + lane + 32) : 0.0f;
+    const float v0 = ok0 ? (SM ? logits[lane] : __ldcg(logits + lane)) : 0.0f;
+    const float v1 = ok1 ? (SM ? logits[lane + 32] : __ldcg(logits + lane + 32)) : 0.0f;
     // max: the serial scan from x[0] with strict > keeps x[0] when it is a NaN, else it is the largest
     // non-NaN value (x[0] among them)
     float m = -__int_as_float(0x7f800000);
@@ -111,17 +114,24 @@ __device__ void trx_route_token(const float *__restrict__ logits, int E, int k, 
     const bool any_nan = __any_sync(0xffffffffu, (ok0 && p0 != p0) || (ok1 && p1 != p1));
     int r0 = lane, r1 = lane + 32; // selection rank of elements lane and lane + 32
     if (!any_nan) {
-        sp[lane] = p0;
-        sp[lane + 32] = p1;
-        __syncwarp();
-        r0 = 0;
-        r1 = 0;
-        for (int j = 0; j < E; j++) {
-            const float q = sp[j];
-            r0 += (q > p0) || (q == p0 && j < lane);
-            r1 += (q > p1) || (q == p1 && j < lane + 32);
+        // k rounds of argmax: probabilities are in [0, 1], so their bits order them as unsigned integers;
+        // key = bits + 1 for an untaken element, 0 for a taken (or absent) one
+        r0 = r1 = 1 << 20;
+        bool t0 = !ok0, t1 = !ok1;
+        for (int s = 0; s < k; s++) {
+            const uint32_t k0 = t0 ? 0u : __float_as_uint(p0) + 1u, k1 = t1 ? 0u : __float_as_uint(p1) + 1u;
+            const uint32_t mx = __reduce_max_sync(0xffffffffu, k0 > k1 ? k0 : k1);
+            const unsigned b0 = __ballot_sync(0xffffffffu, k0 == mx);
+            const int best = b0 ? __ffs(b0) - 1 : 32 + __ffs(__ballot_sync(0xffffffffu, k1 == mx)) - 1;
+            if (best == lane) {
+                t0 = true;
+                r0 = s;
+            }
+            if (best == lane + 32) {
+                t1 = true;
+                r1 = s;
+            }
         }
-        __syncwarp();
     }
     const bool s0 = ok0 && r0 < k, s1 = ok1 && r1 < k;
     float w0 = p0, w1 = p1;
@@ -202,6 +212,62 @@ __device__ void trx_block_counting_sort(const int32_t *__restrict__ sel_id, int 
     }
 }
 
+// Where a warp counting sort writes: offsets [E + 1], active [E], n_active [1], place [R], xmap [R] (shared or global
+// memory), and the optional int64 copies of offsets and place
+struct TrxSortOut {
+    int32_t *offsets, *active, *n_active, *place, *xmap;
+    int64_t *out_offsets, *out_place;
+};
+
+// The same by one warp for R <= 32 rows (a decode token's k rows); scnt: 64 ints of shared memory
+__device__ void trx_warp_counting_sort(const int32_t *__restrict__ sel_id, int R, int E, int k, TrxSortOut w, int *scnt,
+                                       int lane) {
+    const int e = lane < R ? sel_id[lane] : -1;
+    scnt[lane] = 0;
+    scnt[lane + 32] = 0;
+    __syncwarp();
+    const unsigned peers = __match_any_sync(0xffffffffu, e);
+    const int rank = __popc(peers & ((1u << lane) - 1u));
+    if (e >= 0 && rank == 0) scnt[e] = __popc(peers);
+    __syncwarp();
+    const int c0 = lane < E ? scnt[lane] : 0, c1 = lane + 32 < E ? scnt[lane + 32] : 0;
+    int i0 = c0, i1 = c1; // inclusive scans
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int a = __shfl_up_sync(0xffffffffu, i0, o), b = __shfl_up_sync(0xffffffffu, i1, o);
+        if (lane >= o) {
+            i0 += a;
+            i1 += b;
+        }
+    }
+    const int total0 = __shfl_sync(0xffffffffu, i0, 31);
+    const int off0 = i0 - c0, off1 = total0 + i1 - c1;
+    if (lane < E) {
+        w.offsets[lane] = off0;
+        if (w.out_offsets) w.out_offsets[lane] = off0;
+    }
+    if (lane + 32 < E) {
+        w.offsets[lane + 32] = off1;
+        if (w.out_offsets) w.out_offsets[lane + 32] = off1;
+    }
+    if (lane == 0) {
+        w.offsets[E] = R;
+        if (w.out_offsets) w.out_offsets[E] = R;
+    }
+    const unsigned a0 = __ballot_sync(0xffffffffu, c0 > 0), a1 = __ballot_sync(0xffffffffu, c1 > 0);
+    const unsigned lt = (1u << lane) - 1u;
+    if (c0 > 0) w.active[__popc(a0 & lt)] = lane;
+    if (c1 > 0) w.active[__popc(a0) + __popc(a1 & lt)] = lane + 32;
+    if (lane == 0) *w.n_active = __popc(a0) + __popc(a1);
+    const int base0 = __shfl_sync(0xffffffffu, off0, e & 31), base1 = __shfl_sync(0xffffffffu, off1, e & 31);
+    if (e >= 0) {
+        const int pos = (e < 32 ? base0 : base1) + rank;
+        w.place[lane] = pos;
+        w.xmap[pos] = lane / k;
+        if (w.out_place) w.out_place[lane] = pos;
+    }
+}
+
 // one token's input row prepared for the gate/up products (one block)
 __device__ void trx_prep_token(const TrxLayer &L, const TrxShape &S, const float *__restrict__ normed, int t,
                                TrxWork &w) {
@@ -210,7 +276,7 @@ __device__ void trx_prep_token(const TrxLayer &L, const TrxShape &S, const float
     if (L.gate_type == TRX_Q4_K) {
         const int nsb = H / 256;
         for (int s = tid >> 5; s < nsb; s += blockDim.x >> 5)
-            trx_prep_q4x_block(x + 256 * s, w.xq + (int64_t)t * H + 256 * s, w.xq_bf + (int64_t)t * (H / 32) + 8 * s,
+            trx_prep_q4x_block(x + 256 * s, w.xq + (int64_t)t * H, s, nsb, w.xq_bf + (int64_t)t * (H / 32) + 8 * s,
                                w.xq_sc + (int64_t)t * (H / 256) + s, lane);
     } else {
         for (int kk = tid; kk < H; kk += blockDim.x) w.x_lc[(int64_t)t * H + trx_lc_pos(kk)] = x[kk];
@@ -225,10 +291,27 @@ __device__ void trx_router_block(const TrxLayer &L, const TrxShape &S, const flo
     const int E = S.E, H = S.H;
     float *srow = sdyn, *sx = sdyn + H;
     const int64_t rb = trx_row_bytes(L.router_type, H);
-    const uint8_t *row = L.router + e * rb;
-    for (int kk = tid; kk < H; kk += blockDim.x)
-        srow[trx_lc_pos(kk)] = L.router_type == TRX_F32 ? __ldg(reinterpret_cast<const float *>(row) + kk)
-                                                        : trx_bf16(__ldg(reinterpret_cast<const uint16_t *>(row) + kk));
+    const uint8_t *row = L.router + e * rb; // lane-row order (trx_repack_lanerows): packed q holds element k below
+    auto k_of = [](int q) { return (q & ~255) + ((q >> 4) & 15) + 16 * (q & 15); };
+    if (L.router_type == TRX_F32) {
+        for (int i = tid; i < H / 4; i += blockDim.x) {
+            const float4 v = __ldg(reinterpret_cast<const float4 *>(row) + i);
+            srow[trx_lc_pos(k_of(4 * i))] = v.x;
+            srow[trx_lc_pos(k_of(4 * i + 1))] = v.y;
+            srow[trx_lc_pos(k_of(4 * i + 2))] = v.z;
+            srow[trx_lc_pos(k_of(4 * i + 3))] = v.w;
+        }
+    } else { // 8 bfloat16 a load, widened exactly
+        for (int i = tid; i < H / 8; i += blockDim.x) {
+            const uint4 v = __ldg(reinterpret_cast<const uint4 *>(row) + i);
+            const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int q = 0; q < 4; q++) {
+                srow[trx_lc_pos(k_of(8 * i + 2 * q))] = __uint_as_float(u[q] << 16);
+                srow[trx_lc_pos(k_of(8 * i + 2 * q + 1))] = __uint_as_float(u[q] & 0xffff0000u);
+            }
+        }
+    }
     const int tg = tid >> 4, l = tid & 15;
     const float bias = L.router_bias ? L.router_bias[e] : 0.0f;
     const int nch = H / 256;
@@ -303,7 +386,13 @@ __global__ void __launch_bounds__(256) trx_k_router(TrxLayer L, TrxShape S, cons
             w.out_sel_id[j] = w.sel_id[j];
             w.out_sel_w[j] = w.sel_w[j];
         }
-    trx_block_counting_sort<8>(w.sel_id, R, E, k, w);
+    if (R <= 32) {
+        __shared__ int scnt[64];
+        const TrxSortOut so{w.offsets, w.active, w.n_active, w.place, w.xmap, w.out_offsets, w.out_place};
+        if (warp == 0) trx_warp_counting_sort(w.sel_id, R, E, k, so, scnt, lane);
+    } else {
+        trx_block_counting_sort<8>(w.sel_id, R, E, k, w);
+    }
     if (tid == 0) *w.route_cnt = 0u;
 }
 
@@ -340,39 +429,56 @@ __device__ __forceinline__ float trx_silu_mul(float g, float u) {
 }
 
 // Q4_K row of 8 blocks (2048 columns) by one warp: float(sum_s v_s) in every lane
-template <bool SM, bool CG = false>
-__device__ __forceinline__ float trx_q4k_row8(const uint8_t *__restrict__ row, const TrxQ4X &X,
-                                              const double *__restrict__ bf, const double *__restrict__ sc, int lane) {
+template <bool SM>
+__device__ __forceinline__ float trx_q4k_row8(const uint8_t *__restrict__ row, const TrxQ4X &X, int lane) {
     const int s = lane >> 2, c = lane & 3;
     const uint8_t *blk = row + 144 * s;
     const uint4 hdr = trx_ld<SM, uint4>(blk);
     const uint4 q0 = trx_ld<SM, uint4>(blk + 16 + 32 * c);
     const uint4 q1 = trx_ld<SM, uint4>(blk + 32 + 32 * c);
-    int64_t T = trx_q4k_chunk_T(hdr, q0, q1, c, X);
-    T += trx_shfl_xor64(T, 1);
-    T += trx_shfl_xor64(T, 2);
-    double v = 0.0;
-    if (c == 0) v = trx_q4k_finish<CG>(hdr, T, bf + 8 * s, CG ? __ldcg(sc + s) : sc[s]);
+    int64_t T, M;
+    trx_q4k_chunk(hdr, q0, q1, c, X, T, M);
+    const double v = trx_q4k_value(hdr, T, M, X.sc);
     double y = 0.0;
 #pragma unroll
     for (int i = 0; i < 8; i++) y = __dadd_rn(y, trx_shfl_d(v, 4 * i));
     return __double2float_rn(y);
 }
 
+// Two Q4_K rows of 8 blocks against the same input (a gate row and its up row), interleaved for ILP
+template <bool SM>
+__device__ __forceinline__ void trx_q4k_row8x2(const uint8_t *__restrict__ ra, const uint8_t *__restrict__ rb_,
+                                               const TrxQ4X &X, int lane, float &ya, float &yb) {
+    const int s = lane >> 2, c = lane & 3;
+    const uint8_t *ba = ra + 144 * s, *bb = rb_ + 144 * s;
+    const uint4 ha = trx_ld<SM, uint4>(ba), hb = trx_ld<SM, uint4>(bb);
+    const uint4 a0 = trx_ld<SM, uint4>(ba + 16 + 32 * c), b0 = trx_ld<SM, uint4>(bb + 16 + 32 * c);
+    const uint4 a1 = trx_ld<SM, uint4>(ba + 32 + 32 * c), b1 = trx_ld<SM, uint4>(bb + 32 + 32 * c);
+    int64_t Ta, Ma, Tb, Mb;
+    trx_q4k_chunk(ha, a0, a1, c, X, Ta, Ma);
+    trx_q4k_chunk(hb, b0, b1, c, X, Tb, Mb);
+    const double va = trx_q4k_value(ha, Ta, Ma, X.sc), vb = trx_q4k_value(hb, Tb, Mb, X.sc);
+    double sa = 0.0, sb = 0.0;
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        sa = __dadd_rn(sa, trx_shfl_d(va, 4 * i));
+        sb = __dadd_rn(sb, trx_shfl_d(vb, 4 * i));
+    }
+    ya = __double2float_rn(sa);
+    yb = __double2float_rn(sb);
+}
+
 // Q4_K rows of 4 blocks (1024 columns), a half-warp each: the half's row value
 template <bool SM>
-__device__ __forceinline__ float trx_q4k_row4(const uint8_t *__restrict__ row, const TrxQ4X &X,
-                                              const double *__restrict__ bf, const double *__restrict__ sc, int lane) {
+__device__ __forceinline__ float trx_q4k_row4(const uint8_t *__restrict__ row, const TrxQ4X &X, int lane) {
     const int s = (lane >> 2) & 3, c = lane & 3;
     const uint8_t *blk = row + 144 * s;
     const uint4 hdr = trx_ld<SM, uint4>(blk);
     const uint4 q0 = trx_ld<SM, uint4>(blk + 16 + 32 * c);
     const uint4 q1 = trx_ld<SM, uint4>(blk + 32 + 32 * c);
-    int64_t T = trx_q4k_chunk_T(hdr, q0, q1, c, X);
-    T += trx_shfl_xor64(T, 1);
-    T += trx_shfl_xor64(T, 2);
-    double v = 0.0;
-    if (c == 0) v = trx_q4k_finish(hdr, T, bf + 8 * s, sc[s]);
+    int64_t T, M;
+    trx_q4k_chunk(hdr, q0, q1, c, X, T, M);
+    const double v = trx_q4k_value(hdr, T, M, X.sc);
     double y = 0.0;
     const int base = lane & 16;
 #pragma unroll
@@ -440,7 +546,8 @@ __global__ void __launch_bounds__(256) trx_k_gateup(TrxLayer L, TrxShape S, TrxW
         const int s = j % TRX_STAGES;
         if (GT == TRX_Q4_K && warp < n && w.xmap[p0] != cur_t) { // the first row's input, while the copy lands
             cur_t = w.xmap[p0];
-            trx_q4x_load(w.xq + (int64_t)cur_t * H + 256 * (lane >> 2), lane & 3, X);
+            trx_q4x_load(w.xq + (int64_t)cur_t * H, 32, lane, w.xq_bf + (int64_t)cur_t * (H / 32) + 8 * (lane >> 2),
+                         w.xq_sc + (int64_t)cur_t * (H / 256) + (lane >> 2), X);
         }
         const bool ok = trx_mbar_wait(&bar[s], (j / TRX_STAGES) & 1, TRX_WAIT_NS);
         if (__syncthreads_or(!ok)) {
@@ -456,11 +563,11 @@ __global__ void __launch_bounds__(256) trx_k_gateup(TrxLayer L, TrxShape S, TrxW
                     if (warp < n) {
                         if (t != cur_t) {
                             cur_t = t;
-                            trx_q4x_load(w.xq + (int64_t)t * H + 256 * (lane >> 2), lane & 3, X);
+                            trx_q4x_load(w.xq + (int64_t)t * H, 32, lane, w.xq_bf + (int64_t)t * (H / 32) + 8 * (lane >> 2),
+                                         w.xq_sc + (int64_t)t * (H / 256) + (lane >> 2), X);
                         }
-                        const double *bf = w.xq_bf + (int64_t)t * (H / 32), *sc = w.xq_sc + (int64_t)t * (H / 256);
-                        const float g = trx_q4k_row8<true>(gs + warp * rb, X, bf, sc, lane);
-                        const float u = trx_q4k_row8<true>(us + warp * rb, X, bf, sc, lane);
+                        const float g = trx_q4k_row8<true>(gs + warp * rb, X, lane);
+                        const float u = trx_q4k_row8<true>(us + warp * rb, X, lane);
                         if (lane == 0) {
                             res[0][q][warp] = g;
                             res[1][q][warp] = u;
@@ -496,7 +603,7 @@ __global__ void __launch_bounds__(256) trx_k_prep(TrxShape S, int R, TrxWork w) 
     const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int p = gw / nsb, s = gw % nsb;
     if (p >= R) return;
-    trx_prep_q4x_block(w.h + (int64_t)p * F + 256 * s, w.hq + (int64_t)p * F + 256 * s, w.hq_bf + (int64_t)p * (F / 32) + 8 * s,
+    trx_prep_q4x_block(w.h + (int64_t)p * F + 256 * s, w.hq + (int64_t)p * F, s, nsb, w.hq_bf + (int64_t)p * (F / 32) + 8 * s,
                        w.hq_sc + (int64_t)p * (F / 256) + s, lane);
 }
 
@@ -546,7 +653,8 @@ __global__ void __launch_bounds__(256) trx_k_down(TrxLayer L, TrxShape S, TrxWor
         const int s = j % TRX_STAGES;
         if (DT == TRX_Q4_K && hw < n && p0 != cur_p) {
             cur_p = p0;
-            trx_q4x_load(w.hq + (int64_t)p0 * F + 256 * ((lane >> 2) & 3), lane & 3, X);
+            trx_q4x_load(w.hq + (int64_t)p0 * F, 16, lane & 15, w.hq_bf + (int64_t)p0 * (F / 32) + 8 * ((lane >> 2) & 3),
+                         w.hq_sc + (int64_t)p0 * nsb + ((lane >> 2) & 3), X);
         }
         const bool ok = trx_mbar_wait(&bar[s], (j / TRX_STAGES) & 1, TRX_WAIT_NS);
         if (__syncthreads_or(!ok)) {
@@ -560,10 +668,10 @@ __global__ void __launch_bounds__(256) trx_k_down(TrxLayer L, TrxShape S, TrxWor
             if (DT == TRX_Q4_K) {
                 if (p != cur_p) {
                     cur_p = p;
-                    trx_q4x_load(w.hq + (int64_t)p * F + 256 * ((lane >> 2) & 3), lane & 3, X);
+                    trx_q4x_load(w.hq + (int64_t)p * F, 16, lane & 15, w.hq_bf + (int64_t)p * (F / 32) + 8 * ((lane >> 2) & 3),
+                                 w.hq_sc + (int64_t)p * nsb + ((lane >> 2) & 3), X);
                 }
-                vv = trx_q4k_row4<true>(st + row * rb, X, w.hq_bf + (int64_t)p * (F / 32), w.hq_sc + (int64_t)p * nsb,
-                                        lane);
+                vv = trx_q4k_row4<true>(st + row * rb, X, lane);
             } else if (DT == TRX_Q8_0) {
                 vv = trx_q8l_dot<true>(st + row * rb, w.h + (int64_t)p * F, nsb, lane & 15);
             } else {

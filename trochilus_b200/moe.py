@@ -23,7 +23,8 @@ F32, F16, Q8_0, Q4_K, Q6_K, BF16 = 0, 1, 8, 12, 14, 30
 # every function include/trmoe.h declares
 EXPORTS = ["tr_gpu_moe_create", "tr_gpu_moe_free", "tr_gpu_moe_bytes", "tr_gpu_moe_set_layer", "tr_gpu_moe_layer",
            "tr_gpu_moe_layer_dev", "tr_gpu_moe_launches", "tr_gpu_moe_profile", "tr_gpu_moe_profile_read",
-           "tr_gpu_moe_check", "tr_gpu_moe_layer_part", "trmoe_last_error", "tr_matmul", "tr_matmul_grouped",
+           "tr_gpu_moe_check", "tr_gpu_moe_layer_part", "tr_gpu_moe_trace",
+           "tr_gpu_moe_trace_read", "trmoe_last_error", "tr_matmul", "tr_matmul_grouped",
            "tr_matmul_grouped_s", "tr_softmax", "tr_swiglu", "trmoe_kernel_cache_clear"]
 
 
@@ -66,6 +67,8 @@ def lib():
     L.tr_gpu_moe_launches.argtypes = [C.c_void_p, C.c_int64]
     L.tr_gpu_moe_profile.argtypes = [C.c_void_p, C.c_int]
     L.tr_gpu_moe_check.argtypes = [C.c_void_p]
+    L.tr_gpu_moe_trace.argtypes = [C.c_void_p, C.c_int]
+    L.tr_gpu_moe_trace_read.argtypes = [C.c_void_p, C.c_void_p, C.c_int64]
     L.tr_gpu_moe_layer_part.argtypes = [C.c_void_p, C.c_int64, C.c_int, C.c_void_p, C.c_int64, C.c_void_p,
                                         C.POINTER(Outputs), C.c_void_p]
     L.tr_gpu_moe_profile_read.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int]
@@ -176,6 +179,18 @@ class GpuMoe:
         """tr_gpu_moe_check: wait for the stream; raise if a kernel gave up on a bounded wait."""
         if lib().tr_gpu_moe_check(self.h) != 0:
             raise RuntimeError(f"tr_gpu_moe_check: {last_error()}")
+
+    def trace(self, on: bool):
+        if lib().tr_gpu_moe_trace(self.h, 1 if on else 0) != 0:
+            raise RuntimeError(f"tr_gpu_moe_trace: {last_error()}")
+
+    def trace_read(self) -> np.ndarray:
+        """the fused kernel's last timeline: ctas x 64 %globaltimer slots (ns, 0: no event)"""
+        buf = np.zeros(148 * 8 * 64, np.uint64)
+        n = lib().tr_gpu_moe_trace_read(self.h, _p(buf), buf.size)
+        if n < 0:
+            raise RuntimeError(f"tr_gpu_moe_trace_read: {last_error()}")
+        return buf[:n * 64].reshape(n, 64)
 
     def launches(self, n_tok: int) -> int:
         return int(lib().tr_gpu_moe_launches(self.h, n_tok))
