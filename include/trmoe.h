@@ -167,6 +167,25 @@ TRMOE_API void tr_softmax(float *x, int64_t n);
 /* Replaces: tr_swiglu (src/kernels/kernels.h:345): x[i] = silu(x[i]) * y[i]. */
 TRMOE_API void tr_swiglu(tr_pool *pool, float *x, const float *y, int64_t n);
 
+/* No counterpart in the reference (it has no GPU matmul API). y[t*rows + r] = row r of a Q4_K matrix . x[t*cols ..],
+ * bit for bit tr_matmul's result, for callers that cannot allocate device memory: a process whose HBM is all held
+ * by another allocator (a serving engine that reserves it at start-up), or code that must not call cudaMalloc /
+ * cudaFree because they can synchronise the device behind other streams' backs.
+ * Every pointer is caller-owned DEVICE memory on the calling thread's current device: d_w = rows GGUF Q4_K rows
+ * (144 B per 256 columns), d_x = n_tokens x cols f32, d_y = n_tokens x rows f32; cols a multiple of 256; d_w and
+ * d_x 16-byte aligned. The prepared inputs go to a fixed scratch array inside the library, of
+ * TRMOE_NOALLOC_SCRATCH_BYTES on every GPU that loads it, held until the process exits. A call needs 256 bytes of
+ * it plus, per token, cols * 4 + cols / 4 + cols / 32 bytes (each part rounded up to 256), so 2048 columns fit
+ * 478 tokens; a larger call is rejected with an error. A successful call allocates nothing, host or device.
+ * The first call on a device looks up the scratch's device address (cudaGetSymbolAddress) and keeps it: make
+ * that first call before any stream capture. Every call shares the one scratch array and leaves its contents
+ * there: calls that may overlap on the GPU (different streams, or different host threads on one device) race,
+ * and the caller must serialise them. Asynchronous on `stream` (NULL: the default stream); returns 0, or -1 with
+ * trmoe_last_error() set. */
+#define TRMOE_NOALLOC_SCRATCH_BYTES 4194304
+TRMOE_API int tr_matmul_q4k_noalloc(const void *d_w, int64_t rows, int64_t cols, const float *d_x, int64_t n_tokens,
+                                    float *d_y, void *stream);
+
 /* Drops every weight the kernel level uploaded (the next call uploads again). */
 TRMOE_API void trmoe_kernel_cache_clear(void);
 

@@ -915,3 +915,75 @@ extern "C" void trmoe_kernel_cache_clear(void) {
     for (auto &kv : c.mats) cudaFree(kv.second.dev);
     c.mats.clear();
 }
+
+// ---------------------------------------------------------------------------------------------
+// tr_matmul_q4k_noalloc: the Q4_K kernel-level product on caller-owned device memory, allocating nothing
+
+// Its scratch, one per GPU that loads the library: bytes 0..7 the group table's one matrix pointer, 8..15 the
+// group offsets {0, n_tokens}, then from byte 256 the tokens' prepared rows (planes, sub-block sums, scales).
+// Host code never dereferences this name: on the host it only stands for the symbol, whose device address
+// cudaGetSymbolAddress gives.
+static __device__ __align__(256) uint8_t g_noalloc_scratch[TRMOE_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+
+constexpr int kNoallocDevices = 64;
+std::mutex g_noalloc_mu;
+uint8_t *g_noalloc_ptr[kNoallocDevices]; // per device: the scratch's device address, found on its first call
+
+// the scratch's address on the current device `dev`, looked up once with that device current
+uint8_t *noalloc_scratch(int dev) {
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (g_noalloc_ptr[dev] == nullptr) {
+        void *p = nullptr;
+        if (!ck(cudaGetSymbolAddress(&p, g_noalloc_scratch), "cudaGetSymbolAddress")) return nullptr;
+        g_noalloc_ptr[dev] = static_cast<uint8_t *>(p);
+    }
+    return g_noalloc_ptr[dev];
+}
+
+// writes the scratch's group table: one group of n_tok rows multiplied by w
+__global__ void trx_noalloc_table(uint8_t *scratch, const uint8_t *w, int32_t n_tok) {
+    *reinterpret_cast<const uint8_t **>(scratch) = w;
+    reinterpret_cast<int32_t *>(scratch + 8)[0] = 0;
+    reinterpret_cast<int32_t *>(scratch + 8)[1] = n_tok;
+}
+
+} // namespace
+
+extern "C" int tr_matmul_q4k_noalloc(const void *d_w, int64_t rows, int64_t cols, const float *d_x, int64_t n_tokens,
+                                     float *d_y, void *stream) {
+    g_err.clear();
+    if (d_w == nullptr || d_x == nullptr || d_y == nullptr || rows < 1 || rows > (1 << 24) || cols < 256 ||
+        cols % 256 != 0 || cols > (1 << 20) || n_tokens < 1 || ((uintptr_t)d_w & 15u) != 0 || ((uintptr_t)d_x & 15u) != 0) {
+        set_err("tr_matmul_q4k_noalloc: bad arguments (rows %lld, cols %lld: a multiple of 256, n_tokens %lld, "
+                "d_w and d_x 16-byte aligned)",
+                (long long)rows, (long long)cols, (long long)n_tokens);
+        return -1;
+    }
+    // the scratch's parts, each rounded up to 256 bytes: table, planes, sub-block sums, scales
+    const int64_t pb = align_up(n_tokens * cols * 4, 256), bfb = align_up(n_tokens * (cols / 32) * 8, 256),
+                  scb = align_up(n_tokens * (cols / 256) * 8, 256), need = 256 + pb + bfb + scb;
+    if (need > (int64_t)TRMOE_NOALLOC_SCRATCH_BYTES) {
+        set_err("tr_matmul_q4k_noalloc: %lld tokens of %lld columns need %lld bytes of scratch, more than its %lld",
+                (long long)n_tokens, (long long)cols, (long long)need, (long long)TRMOE_NOALLOC_SCRATCH_BYTES);
+        return -1;
+    }
+    int dev = 0;
+    if (!ck(cudaGetDevice(&dev), "cudaGetDevice")) return -1;
+    if (dev < 0 || dev >= kNoallocDevices) {
+        set_err("tr_matmul_q4k_noalloc: device %d is beyond the %d it serves", dev, kNoallocDevices);
+        return -1;
+    }
+    uint8_t *scratch = noalloc_scratch(dev);
+    if (scratch == nullptr) return -1;
+    cudaStream_t st = (cudaStream_t)stream;
+    // nothing in the scratch has to start at zero: this call writes the table and every prepared row it reads
+    trx_noalloc_table<<<1, 1, 0, st>>>(scratch, static_cast<const uint8_t *>(d_w), (int32_t)n_tokens);
+    uint32_t *dq = reinterpret_cast<uint32_t *>(scratch + 256);
+    double *dbf = reinterpret_cast<double *>(scratch + 256 + pb);
+    double *dsc = reinterpret_cast<double *>(scratch + 256 + pb + bfb);
+    trx_kapi_grouped(TRX_Q4_K, rows, cols, reinterpret_cast<const uint8_t *const *>(scratch),
+                     reinterpret_cast<const int32_t *>(scratch + 8), 1, (int)n_tokens, d_x, dq, dbf, dsc, d_y, st);
+    return ck(cudaGetLastError(), "tr_matmul_q4k_noalloc launch") ? 0 : -1;
+}

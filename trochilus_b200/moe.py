@@ -25,7 +25,7 @@ EXPORTS = ["tr_gpu_moe_create", "tr_gpu_moe_free", "tr_gpu_moe_bytes", "tr_gpu_m
            "tr_gpu_moe_layer_dev", "tr_gpu_moe_launches", "tr_gpu_moe_profile", "tr_gpu_moe_profile_read",
            "tr_gpu_moe_check", "tr_gpu_moe_layer_part", "tr_gpu_moe_trace",
            "tr_gpu_moe_trace_read", "trmoe_last_error", "tr_matmul", "tr_matmul_grouped",
-           "tr_matmul_grouped_s", "tr_softmax", "tr_swiglu", "trmoe_kernel_cache_clear"]
+           "tr_matmul_grouped_s", "tr_softmax", "tr_swiglu", "trmoe_kernel_cache_clear", "tr_matmul_q4k_noalloc"]
 
 
 class Config(C.Structure):
@@ -79,6 +79,8 @@ def lib():
                                       C.c_void_p]
     L.tr_softmax.argtypes = [C.c_void_p, C.c_int64]
     L.tr_swiglu.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64]
+    L.tr_matmul_q4k_noalloc.argtypes = [C.c_void_p, C.c_int64, C.c_int64, C.c_void_p, C.c_int64, C.c_void_p,
+                                        C.c_void_p]
     _lib = L
     return L
 
