@@ -96,6 +96,13 @@ typedef struct {
     float *ffn_out;     /* [n_tok][n_embd] the layer's output before the residual add */
 } tr_gpu_moe_outputs;
 
+/* No counterpart in the reference (its long passes run the same scalar definition): calls of at least min_tokens
+ * tokens take the tensor-core road of a context with Q8_0 gate/up and down weights (router, top-k and dispatch
+ * exact as always; expert products as 3xTF32 tcgen05 GEMMs, within 1e-5 relative of the exact result; combine
+ * exact). 0 keeps every call on the exact road. Default 256. Returns 0, or -1 (a non-zero min_tokens on a context
+ * without the road). */
+TRMOE_API int tr_gpu_moe_set_prefill(tr_gpu_moe *m, int64_t min_tokens);
+
 /* tr_gpu_moe_layer on device memory, enqueued on `stream` (a cudaStream_t; NULL: the context's own
  * stream) and returning without waiting. d_normed and d_x_inout are device pointers. 0, or -1. */
 TRMOE_API int tr_gpu_moe_layer_dev(tr_gpu_moe *m, int64_t layer, const float *d_normed, int64_t n_tok, float *d_x_inout,

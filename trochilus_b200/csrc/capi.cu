@@ -3,7 +3,9 @@
 // Host side of the layer hook (tr_gpu_moe_*) and of the kernel-level API (tr_matmul*, tr_softmax,
 // tr_swiglu). Plain CUDA runtime; no torch. Every host wait on the GPU polls with a deadline and
 // reports a timeout as an error instead of blocking forever.
+#include <cuda.h>
 #include <cuda_runtime.h>
+#include <cudaTypedefs.h>
 
 #include <chrono>
 #include <cstdarg>
@@ -22,6 +24,7 @@
 #include "moe_kernels.cuh"
 #include "kernel_api.cuh"
 #include "fused_layer.cuh"
+#include "prefill.cuh"
 
 namespace {
 
@@ -90,13 +93,17 @@ bool upload_matrix(int type, int64_t rows, int64_t cols, const void *host, uint8
 }
 
 struct WorkLayout {
-    int64_t off[25];
+    int64_t off[26];
     int64_t total;
 };
 
 // carve the workspace of one context (every piece 256-byte aligned)
+// whether a context can take the tensor-core road for long passes (Q8_0 gate/up and down)
+bool prefill_capable(const tr_gpu_moe_config &c) { return c.gate_type == TRX_Q8_0 && c.down_type == TRX_Q8_0; }
+
 WorkLayout work_layout(const tr_gpu_moe_config &c) {
     const int64_t T = c.max_tokens, E = c.n_expert, k = c.n_used, H = c.n_embd, F = c.n_ff, R = T * k;
+    const bool pf = prefill_capable(c);
     const int64_t sizes[] = {
         T * E * 4,          // 0 logits
         R * 4,              // 1 sel_id
@@ -122,10 +129,12 @@ WorkLayout work_layout(const tr_gpu_moe_config &c) {
         R * 8,              // 21 host-call sel_id
         R * 4,              // 22 host-call sel_w
         (int64_t)sizeof(TrxSync), // 23 the fused kernel's counters
+        pf ? R * H * 4 : 0, // 24 the tensor-core road: the grouped inputs' hi plane
+        pf ? R * H * 4 : 0, // 25 and lo plane
     };
     WorkLayout w{};
     int64_t o = 0;
-    for (int i = 0; i < 24; i++) {
+    for (int i = 0; i < 26; i++) {
         w.off[i] = o;
         o += align_up(sizes[i], 256);
     }
@@ -162,6 +171,11 @@ struct tr_gpu_moe {
     float *d_normed = nullptr, *d_x = nullptr;
     int64_t *d_sel_id = nullptr;
     float *d_sel_w = nullptr;
+    // the tensor-core road (prefill.cuh): calls of at least pf_min tokens take it (0: never)
+    bool pf_ok = false;
+    int64_t pf_min = 0;
+    float *pf_xhi = nullptr, *pf_xlo = nullptr;
+    CUtensorMap pf_map_x[2], pf_map_h[2]; // A operands of the gate/up and of the down GEMM: hi, lo planes
     // zone timing (tr_gpu_moe_profile): one set of events per profiled call, read when asked, so that
     // profiling never makes a call wait for the one before it
     struct EvSet {
@@ -351,6 +365,50 @@ static bool check_config(const tr_gpu_moe_config *c) {
     return true;
 }
 
+// a 2-D fp32 tensor map over rows x cols (row-major), boxes of 32 columns x 128 rows, 128-byte swizzle
+static bool encode_map(CUtensorMap *map, float *base, int64_t rows, int64_t cols) {
+    static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+    if (encode == nullptr) {
+        cudaDriverEntryPointQueryResult q{};
+        void *fn = nullptr;
+        if (!ck(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q), "driver entry point") ||
+            q != cudaDriverEntryPointSuccess || fn == nullptr) {
+            if (g_err.empty()) set_err("cuTensorMapEncodeTiled is not available");
+            return false;
+        }
+        encode = (PFN_cuTensorMapEncodeTiled_v12000)fn;
+    }
+    const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows}, strides[1] = {(cuuint64_t)cols * 4};
+    const cuuint32_t box[2] = {TRX_PF_BK, TRX_PF_BM}, es[2] = {1, 1};
+    const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, base, dims, strides, box, es,
+                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        set_err("cuTensorMapEncodeTiled failed (%d)", (int)r);
+        return false;
+    }
+    return true;
+}
+
+// the tensor-core road: its kernels' shared memory and the A operands' tensor maps (the h planes reuse the h and
+// hq regions, which the Q8_0 roads of the other kernels leave free during a prefill call)
+static bool plan_prefill(tr_gpu_moe *m) {
+    const tr_gpu_moe_config &c = m->cfg;
+    const int64_t R = c.max_tokens * c.n_used;
+    if (!ck(cudaFuncSetAttribute(trx_k_pf_gemm<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, TRX_PF_SMEM),
+            "smem prefill") ||
+        !ck(cudaFuncSetAttribute(trx_k_pf_gemm<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, TRX_PF_SMEM),
+            "smem prefill"))
+        return false;
+    if (!encode_map(&m->pf_map_x[0], m->pf_xhi, R, c.n_embd) || !encode_map(&m->pf_map_x[1], m->pf_xlo, R, c.n_embd) ||
+        !encode_map(&m->pf_map_h[0], m->work.h, R, c.n_ff) ||
+        !encode_map(&m->pf_map_h[1], reinterpret_cast<float *>(m->work.hq), R, c.n_ff))
+        return false;
+    m->pf_ok = true;
+    m->pf_min = 256;
+    return true;
+}
+
 extern "C" tr_gpu_moe *tr_gpu_moe_create(const tr_gpu_moe_config *cfg, int device, char *err, size_t err_len) {
     g_err.clear();
     if (!check_config(cfg)) {
@@ -411,6 +469,15 @@ extern "C" tr_gpu_moe *tr_gpu_moe_create(const tr_gpu_moe_config *cfg, int devic
     m->d_sel_id = (int64_t *)(b + wl.off[21]);
     m->d_sel_w = (float *)(b + wl.off[22]);
     m->sync = (TrxSync *)(b + wl.off[23]);
+    if (prefill_capable(*cfg)) {
+        m->pf_xhi = (float *)(b + wl.off[24]);
+        m->pf_xlo = (float *)(b + wl.off[25]);
+        if (!plan_prefill(m)) {
+            put_err(err, err_len);
+            tr_gpu_moe_free(m);
+            return nullptr;
+        }
+    }
     return m;
 }
 
@@ -549,6 +616,7 @@ static void reset_counters(tr_gpu_moe *m, cudaStream_t st) {
 
 extern "C" int tr_gpu_moe_launches(const tr_gpu_moe *m, int64_t n_tok) {
     if (m == nullptr) return 0;
+    if (m->pf_ok && m->pf_min > 0 && n_tok >= m->pf_min && !m->prof) return 7; // route 3, gather, 2 GEMMs, combine
     int sg, sd;
     if (m->fused_ok && n_tok <= TRX_ROUTE_FUSED_MAX && m->cfg.n_expert + n_tok <= m->grid_fused && !m->prof &&
         fused_stages(m, (int)n_tok, &sg, &sd))
@@ -567,6 +635,48 @@ extern "C" int tr_gpu_moe_check(tr_gpu_moe *m) {
         return -1;
     }
     return 0;
+}
+
+// A long pass on the tensor-core road: the exact routing (router, top-k, sort), the inputs gathered as hi/lo planes,
+// the gate/up and down GEMMs (3xTF32 on tcgen05), the exact combine.
+static int launch_prefill(tr_gpu_moe *m, const TrxLayer &L, const TrxShape &S, const TrxWork &w, const float *d_normed,
+                          int T, float *d_x, float *ffn_out, cudaStream_t st) {
+    const int E = S.E, H = S.H, F = S.F, R = T * S.k;
+    const size_t smem_router = (size_t)(1 + std::min(T, TRX_TOK_STAGE)) * H * 4;
+    trx_k_router<<<dim3((unsigned)E, (unsigned)((T + TRX_TOK_STAGE - 1) / TRX_TOK_STAGE)), 256, smem_router, st>>>(
+        L, S, d_normed, T, w, 0);
+    trx_k_route<<<(unsigned)((T + 7) / 8), 256, 0, st>>>(S, T, w);
+    trx_k_sort<<<1, 1024, 0, st>>>(S, T, w);
+    trx_k_pf_gather<<<(unsigned)R, 256, 0, st>>>(d_normed, w.xmap, w.offsets, E, H, m->pf_xhi, m->pf_xlo);
+    const unsigned mtiles = (unsigned)((R + TRX_PF_BM - 1) / TRX_PF_BM + std::min(E, R));
+    TrxPfArgs a{};
+    a.offsets = w.offsets;
+    a.active = w.active;
+    a.n_active = w.n_active;
+    a.err = w.err;
+    a.wa = L.gate;
+    a.wb = L.up;
+    a.wa_mb = L.gate_mb;
+    a.wb_mb = L.up_mb;
+    a.K = H;
+    a.N = F;
+    a.out_hi = w.h;
+    a.out_lo = reinterpret_cast<float *>(w.hq);
+    trx_k_pf_gemm<true><<<dim3((unsigned)(F / 128), mtiles), TRX_PF_THREADS, TRX_PF_SMEM, st>>>(m->pf_map_x[0],
+                                                                                               m->pf_map_x[1], a);
+    a.wa = L.down;
+    a.wb = nullptr;
+    a.wa_mb = L.down_mb;
+    a.wb_mb = 0;
+    a.K = F;
+    a.N = H;
+    a.out_hi = w.h3;
+    a.out_lo = nullptr;
+    trx_k_pf_gemm<false><<<dim3((unsigned)(H / TRX_PF_BN), mtiles), TRX_PF_THREADS, TRX_PF_SMEM, st>>>(m->pf_map_h[0],
+                                                                                                      m->pf_map_h[1], a);
+    const int64_t n = (int64_t)T * H;
+    trx_k_pf_combine<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(w.sel_w, w.place, w.h3, T, S.k, H, d_x, ffn_out);
+    return ck(cudaGetLastError(), "prefill launch") ? 0 : -1;
 }
 
 // Enqueues parts [first, last] of one layer call on st: 0 route (router, top-k, dispatch, input preparation),
@@ -612,6 +722,8 @@ static int launch_layer(tr_gpu_moe *m, int64_t layer, const float *d_normed, int
         for (int z = 0; z < TRMOE_ZONES; z++) es->used[z] = true;
         es->used[2] = c.down_type == TRX_Q4_K;
     }
+    if (first == 0 && last == 3 && m->pf_ok && m->pf_min > 0 && T >= m->pf_min && !es)
+        return launch_prefill(m, L, S, w, d_normed, T, d_x, out ? out->ffn_out : nullptr, st);
     int sg = 0, sd = 0;
     if (first == 0 && last == 3 && m->fused_ok && T <= TRX_ROUTE_FUSED_MAX && E + T <= m->grid_fused && !es &&
         fused_stages(m, T, &sg, &sd)) {
@@ -661,6 +773,21 @@ static int launch_layer(tr_gpu_moe *m, int64_t layer, const float *d_normed, int
     }
     mark(4);
     return ck(cudaGetLastError(), "launch") ? 0 : -1;
+}
+
+extern "C" int tr_gpu_moe_set_prefill(tr_gpu_moe *m, int64_t min_tokens) {
+    g_err.clear();
+    if (m == nullptr || min_tokens < 0) {
+        set_err("bad arguments to tr_gpu_moe_set_prefill");
+        return -1;
+    }
+    if (!m->pf_ok) {
+        if (min_tokens == 0) return 0;
+        set_err("this context has no tensor-core road (it needs Q8_0 gate/up and down weights)");
+        return -1;
+    }
+    m->pf_min = min_tokens;
+    return 0;
 }
 
 extern "C" int tr_gpu_moe_layer_dev(tr_gpu_moe *m, int64_t layer, const float *d_normed, int64_t n_tok,

@@ -25,7 +25,8 @@ EXPORTS = ["tr_gpu_moe_create", "tr_gpu_moe_free", "tr_gpu_moe_bytes", "tr_gpu_m
            "tr_gpu_moe_layer_dev", "tr_gpu_moe_launches", "tr_gpu_moe_profile", "tr_gpu_moe_profile_read",
            "tr_gpu_moe_check", "tr_gpu_moe_layer_part", "tr_gpu_moe_trace",
            "tr_gpu_moe_trace_read", "trmoe_last_error", "tr_matmul", "tr_matmul_grouped",
-           "tr_matmul_grouped_s", "tr_softmax", "tr_swiglu", "trmoe_kernel_cache_clear", "tr_matmul_q4k_noalloc"]
+           "tr_matmul_grouped_s", "tr_softmax", "tr_swiglu", "trmoe_kernel_cache_clear", "tr_matmul_q4k_noalloc",
+           "tr_gpu_moe_set_prefill"]
 
 
 class Config(C.Structure):
@@ -65,6 +66,7 @@ def lib():
     L.tr_gpu_moe_layer_dev.argtypes = [C.c_void_p, C.c_int64, C.c_void_p, C.c_int64, C.c_void_p,
                                        C.POINTER(Outputs), C.c_void_p]
     L.tr_gpu_moe_launches.argtypes = [C.c_void_p, C.c_int64]
+    L.tr_gpu_moe_set_prefill.argtypes = [C.c_void_p, C.c_int64]
     L.tr_gpu_moe_profile.argtypes = [C.c_void_p, C.c_int]
     L.tr_gpu_moe_check.argtypes = [C.c_void_p]
     L.tr_gpu_moe_trace.argtypes = [C.c_void_p, C.c_int]
@@ -196,6 +198,11 @@ class GpuMoe:
 
     def launches(self, n_tok: int) -> int:
         return int(lib().tr_gpu_moe_launches(self.h, n_tok))
+
+    def set_prefill(self, min_tokens: int):
+        """tr_gpu_moe_set_prefill: calls of at least min_tokens tokens take the tensor-core road (0: never)."""
+        if lib().tr_gpu_moe_set_prefill(self.h, min_tokens) != 0:
+            raise RuntimeError(f"tr_gpu_moe_set_prefill: {last_error()}")
 
     def close(self):
         if self.h:
