@@ -15,6 +15,8 @@ Arms:
              through tr_gpu_moe_layer with pinned host buffers (copies in and out inside the timed region);
              `roofline` = the dominant zone's algorithmic bytes / its CUDA-event time; `cpu_baseline` =
              Trochilus's own code (oracle/_ref, best SIMD tier, all host cores) on a bounded sample.
+             `prefill` = configs[2]'s layer (2048 tokens, Q8_0) on the tensor-core road, same keys, its roofline
+             the useful TFLOP/s over the dense TF32 peak (--prefill-tokens 0 skips it; --only-prefill prints it alone).
   reference  Trochilus's own CPU code on this box's host cores, same config (rank 0 only under torchrun).
 N > 1: one process per GPU (torchrun); each rank runs its own replica of the workload (the layer has no
 data-path exchange at batch 1), time = max over ranks, `value` = all ranks' tokens / that time.
@@ -54,6 +56,10 @@ def args_parse():
     p.add_argument("--layers", type=int, default=16)
     p.add_argument("--cpu-seconds", type=float, default=8.0)
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--prefill-tokens", type=int, default=2048,
+                   help="tokens of the prefill measurement added to the line (configs[2]'s layer); 0: skip it")
+    p.add_argument("--prefill-steps", type=int, default=20)
+    p.add_argument("--only-prefill", action="store_true", help="run and print only the prefill measurement")
     return p.parse_args()
 
 
@@ -183,6 +189,84 @@ def peaks():
         return p["hbm_gbs"], "measured"
     except (OSError, KeyError, ValueError):
         return 6650.0, "fallback"
+
+
+def tf32_peak():
+    """dense TF32 tensor peak: half the measured dense bf16 (cuBLAS) rate, the ratio of the two dense rates"""
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return p["bf16_tflops"] / 2.0, "half of measured bf16"
+    except (OSError, KeyError, ValueError):
+        return 1590.0 / 2.0, "half of fallback bf16"
+
+
+def run_prefill(args, dev, cpu_seconds):
+    """configs[2]'s MoE layer: T = --prefill-tokens tokens, Q8_0 gate/up/down, BF16 router, on the tensor-core road
+    (3xTF32 tcgen05 GEMMs). Two resident layers alternate (428 MB of weights each, larger than L2)."""
+    import torch
+    from trochilus_b200.moe import GpuMoe
+    T, NL, steps = args.prefill_tokens, 2, max(args.prefill_steps, 1)
+    m = GpuMoe(NL, E, K_USED, H, F, gb.BF16, gb.Q8_0, gb.Q8_0, max_tokens=T, device=dev)
+    lays, routers = host_layers(gb.Q8_0, gb.Q8_0, n_host=NL, n_routers=NL)
+    for l in range(NL):
+        lay = dict(lays[l])
+        lay["router"] = routers[l]
+        m.set_layer(l, lay)
+    del lays
+    assert m.launches(T) == 7, "the prefill call did not take the tensor-core road"
+    g = torch.Generator(device="cuda")
+    g.manual_seed(4321)
+    normed = torch.randn((NL, T, H), device="cuda", generator=g)
+    x = torch.randn((T, H), device="cuda", generator=g)
+    sp = torch.cuda.Stream()  # a stream of its own (handle 0 would mean the context's stream to the C API)
+    torch.cuda.synchronize()
+    for i in range(3):
+        m.layer_dev(i % NL, normed[i % NL].data_ptr(), T, x.data_ptr(), None, stream=sp.cuda_stream)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(dev) as clk:
+        clk.wait_first()
+        torch.cuda.synchronize()
+        e0.record(sp)
+        for i in range(steps):
+            m.layer_dev(i % NL, normed[i % NL].data_ptr(), T, x.data_ptr(), None, stream=sp.cuda_stream)
+        e1.record(sp)
+        torch.cuda.synchronize()
+    m.check()
+    ms = e0.elapsed_time(e1) / steps
+    flops = 2.0 * T * K_USED * 3 * H * F + 2.0 * T * E * H
+    tflops = flops / (ms / 1000.0) / 1e12
+    peak, peak_kind = tf32_peak()
+    # e2e through the host-pointer call: normed and x in, x out, per call
+    hn = torch.randn((T, H)).pin_memory()
+    hx = torch.randn((T, H)).pin_memory()
+    m.layer_ptrs(0, hn.data_ptr(), T, hx.data_ptr(), host=True)
+    n_e2e = max(steps // 2, 2)
+    t0 = time.perf_counter()
+    for i in range(n_e2e):
+        m.layer_ptrs(i % NL, hn.data_ptr(), T, hx.data_ptr(), host=True)
+    e2e_s = (time.perf_counter() - t0) / n_e2e
+    m.close()
+    out = {"workload": f"configs[2] MoE layer: OLMoE shape, Q8_0 gate/up/down, BF16 router, {T}-token prefill call "
+                       f"(2 resident layers alternating, 428 MB each)",
+           "value": T / (ms / 1000.0), "unit": "tokens/s", "ms_per_step": ms, "steps": steps, "warmup": 3,
+           "dtype": "3xTF32 (fp32 semantics, 1e-5)",
+           "roofline": {"bound": "tensor", "kernel": "trx_k_pf_gemm (gate/up + down)", "achieved": tflops,
+                        "peak": peak, "unit": "TFLOP/s", "frac": tflops / peak, "peak_kind": peak_kind,
+                        "flops": flops, "note": "useful flops of the whole layer call over its time; the tensor "
+                                                "pipe issues 3x these (hi.hi, hi.lo, lo.hi)"},
+           "e2e": {"value": T / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": 2 * T * H * 4,
+                   "d2h_bytes_per_step": T * H * 4},
+           "clocks": clk.summary()}
+    if cpu_seconds > 0:
+        try:
+            a = argparse.Namespace(**vars(args))
+            a.tokens, a.gate, a.down = T, "q8_0", "q8_0"
+            out["cpu_baseline"] = cpu_reference(a, gb.Q8_0, gb.Q8_0, cpu_seconds)
+        except Exception as exc:
+            out["cpu_baseline"] = {"value": None, "sample": f"unavailable: {exc}"}
+    return out
 
 
 def run_ours(args, rank, world, dist):
@@ -326,6 +410,9 @@ def run_ours(args, rank, world, dist):
     e2e = {"value": world * T * e2e_steps / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": 2 * T * H * 4,
            "d2h_bytes_per_step": T * H * 4, "steps": e2e_steps}
 
+    prefill = None
+    if world == 1 and args.prefill_tokens > 0:
+        prefill = run_prefill(args, dev, 0 if args.no_cpu_baseline else args.cpu_seconds)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
@@ -348,6 +435,7 @@ def run_ours(args, rank, world, dist):
                                "multikernel_zone_ms": {z: zone_ms[z] for z in ("router", "gate_up", "act_prep", "down")},
                                "multikernel_ms": layer_ms},
             "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches * steps, "clocks": clk.summary(),
+            "prefill": prefill,
             "timing": f"CUDA graphs of {NL} layer calls replayed (+ a graph of the last {tail_n}); zones from graphs "
                       f"of parts 0..z"}
     print(json.dumps(line), flush=True)
@@ -366,7 +454,11 @@ def main():
         torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
         dist_.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
         dist = dist_
-    if args.impl == "reference":
+    if args.only_prefill:
+        import torch
+        torch.cuda.set_device(0)
+        print(json.dumps(run_prefill(args, 0, 0 if args.no_cpu_baseline else args.cpu_seconds)), flush=True)
+    elif args.impl == "reference":
         run_reference(args, rank, world)
     else:
         run_ours(args, rank, world, dist)
