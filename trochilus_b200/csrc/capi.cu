@@ -305,6 +305,12 @@ static bool plan_kernels(tr_gpu_moe *m) {
     int occ_gu = 0, occ_dn = 0;
     bool ok = ck(cudaFuncSetAttribute(gu, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)m->smem_gu), "smem gate/up") &&
               ck(cudaFuncSetAttribute(dn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)m->smem_dn), "smem down") &&
+              ck(cudaFuncSetAttribute(trx_k_router_many<TRX_F32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)trx_router_many_smem(TRX_F32, TRX_MAX_EXPERTS)),
+                 "smem router") &&
+              ck(cudaFuncSetAttribute(trx_k_router_many<TRX_BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)trx_router_many_smem(TRX_BF16, TRX_MAX_EXPERTS)),
+                 "smem router") &&
               ck(cudaFuncSetAttribute(trx_k_router, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_router),
                  "smem router") &&
               ck(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ_gu, gu, 256, m->smem_gu), "occupancy") &&
@@ -637,14 +643,21 @@ extern "C" int tr_gpu_moe_check(tr_gpu_moe *m) {
     return 0;
 }
 
+// router logits of a long pass: 16 tokens a block, every expert
+static void launch_router_many(const TrxLayer &L, const TrxShape &S, const float *d_normed, int T, const TrxWork &w,
+                               cudaStream_t st) {
+    const unsigned blocks = (unsigned)((T + TRX_TOK_STAGE - 1) / TRX_TOK_STAGE);
+    const size_t smem = trx_router_many_smem(L.router_type, S.E);
+    if (L.router_type == TRX_F32) trx_k_router_many<TRX_F32><<<blocks, 256, smem, st>>>(L, S, d_normed, T, w);
+    else trx_k_router_many<TRX_BF16><<<blocks, 256, smem, st>>>(L, S, d_normed, T, w);
+}
+
 // A long pass on the tensor-core road: the exact routing (router, top-k, sort), the inputs gathered as hi/lo planes,
 // the gate/up and down GEMMs (3xTF32 on tcgen05), the exact combine.
 static int launch_prefill(tr_gpu_moe *m, const TrxLayer &L, const TrxShape &S, const TrxWork &w, const float *d_normed,
                           int T, float *d_x, float *ffn_out, cudaStream_t st) {
     const int E = S.E, H = S.H, F = S.F, R = T * S.k;
-    const size_t smem_router = (size_t)(1 + std::min(T, TRX_TOK_STAGE)) * H * 4;
-    trx_k_router<<<dim3((unsigned)E, (unsigned)((T + TRX_TOK_STAGE - 1) / TRX_TOK_STAGE)), 256, smem_router, st>>>(
-        L, S, d_normed, T, w, 0);
+    launch_router_many(L, S, d_normed, T, w, st);
     trx_k_route<<<(unsigned)((T + 7) / 8), 256, 0, st>>>(S, T, w);
     trx_k_sort<<<1, 1024, 0, st>>>(S, T, w);
     trx_k_pf_gather<<<(unsigned)R, 256, 0, st>>>(d_normed, w.xmap, w.offsets, E, H, m->pf_xhi, m->pf_xlo);
@@ -752,8 +765,7 @@ static int launch_layer(tr_gpu_moe *m, int64_t layer, const float *d_normed, int
         if (fused) {
             trx_k_router<<<(unsigned)(E + T), 256, smem_router, st>>>(L, S, d_normed, T, w, 1);
         } else {
-            trx_k_router<<<dim3((unsigned)E, (unsigned)((T + TRX_TOK_STAGE - 1) / TRX_TOK_STAGE)), 256, smem_router,
-                           st>>>(L, S, d_normed, T, w, 0);
+            launch_router_many(L, S, d_normed, T, w, st);
             trx_k_prep_tokens<<<(unsigned)T, 256, 0, st>>>(L, S, d_normed, w);
             trx_k_route<<<(unsigned)((T + 7) / 8), 256, 0, st>>>(S, T, w);
             trx_k_sort<<<1, 1024, 0, st>>>(S, T, w);

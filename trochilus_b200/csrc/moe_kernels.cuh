@@ -396,6 +396,94 @@ __global__ void __launch_bounds__(256) trx_k_router(TrxLayer L, TrxShape S, cons
     if (tid == 0) *w.route_cnt = 0u;
 }
 
+// Router logits of a long pass, 16 tokens a block and every expert: thread (t = tid / 16, l = tid % 16) keeps lane l's
+// running sums of token t for all E experts in registers while the 256-blocks of H go by in order. For each block the
+// 16 tokens' inputs (LC order) and every expert's router columns (lane-row packing) are staged in shared memory with
+// coalesced loads, one memory latency a block. Same sums, same order as trx_router_block: the 16-lane contract.
+// Dynamic shared memory: TRX_TOK_STAGE * 1024 + E * 256 * sizeof(router element) bytes.
+template <int RT>
+__global__ void __launch_bounds__(256) trx_k_router_many(TrxLayer L, TrxShape S, const float *__restrict__ normed,
+                                                         int T, TrxWork w) {
+    extern __shared__ __align__(16) float sdyn[];
+    constexpr int WB = RT == TRX_F32 ? 1024 : 512; // bytes of one expert's 256-block
+    float *sx = sdyn;
+    uint8_t *sw = reinterpret_cast<uint8_t *>(sdyn + TRX_TOK_STAGE * 256);
+    const int tid = threadIdx.x, t = tid >> 4, l = tid & 15, t0 = blockIdx.x * TRX_TOK_STAGE;
+    const int E = S.E, H = S.H, nb = H / 256;
+    const int64_t rb = trx_row_bytes(RT, H);
+    float acc[TRX_MAX_EXPERTS];
+#pragma unroll
+    for (int e = 0; e < TRX_MAX_EXPERTS; e++) acc[e] = 0.0f;
+    for (int i = 0; i < nb; i++) {
+        __syncthreads();
+        for (int j = tid; j < E * (WB / 16); j += blockDim.x) { // every expert's block i, 16 bytes a thread
+            const int e = j / (WB / 16), q = j % (WB / 16);
+            reinterpret_cast<uint4 *>(sw + e * WB)[q] = __ldg(reinterpret_cast<const uint4 *>(L.router + e * rb + (int64_t)i * WB) + q);
+        }
+        for (int j = tid; j < TRX_TOK_STAGE * 64; j += blockDim.x) { // block i of the 16 tokens, LC order
+            const int tt = j >> 6, k = 4 * (j & 63);
+            const float4 v = t0 + tt < T ? __ldg(reinterpret_cast<const float4 *>(normed + (int64_t)(t0 + tt) * H + 256 * i + k))
+                                         : make_float4(0.f, 0.f, 0.f, 0.f);
+            float *dst = sx + tt * 256;
+            dst[trx_lc_pos(k)] = v.x;
+            dst[trx_lc_pos(k + 1)] = v.y;
+            dst[trx_lc_pos(k + 2)] = v.z;
+            dst[trx_lc_pos(k + 3)] = v.w;
+        }
+        __syncthreads();
+        float xv[16];
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            const float4 c = *reinterpret_cast<const float4 *>(sx + t * 256 + 64 * q + 4 * l);
+            xv[4 * q] = c.x; xv[4 * q + 1] = c.y; xv[4 * q + 2] = c.z; xv[4 * q + 3] = c.w;
+        }
+#pragma unroll
+        for (int e = 0; e < TRX_MAX_EXPERTS; e++) {
+            if (e < E) {
+                float wv[16];
+                if (RT == TRX_F32) {
+                    const float4 *wp = reinterpret_cast<const float4 *>(sw + e * WB + 64 * l);
+#pragma unroll
+                    for (int q = 0; q < 4; q++) {
+                        const float4 a = wp[q];
+                        wv[4 * q] = a.x; wv[4 * q + 1] = a.y; wv[4 * q + 2] = a.z; wv[4 * q + 3] = a.w;
+                    }
+                } else {
+                    const uint4 *wp = reinterpret_cast<const uint4 *>(sw + e * WB + 32 * l);
+#pragma unroll
+                    for (int q = 0; q < 2; q++) {
+                        const uint4 a = wp[q];
+                        const uint32_t u[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+                        for (int r = 0; r < 4; r++) {
+                            wv[8 * q + 2 * r] = __uint_as_float(u[r] << 16);
+                            wv[8 * q + 2 * r + 1] = __uint_as_float(u[r] & 0xffff0000u);
+                        }
+                    }
+                }
+#pragma unroll
+                for (int m = 0; m < 16; m++) acc[e] = __fadd_rn(acc[e], __fmul_rn(wv[m], xv[m]));
+            }
+        }
+    }
+    const bool valid = t0 + t < T;
+#pragma unroll
+    for (int e = 0; e < TRX_MAX_EXPERTS; e++) {
+        if (e < E) {
+            const float v0 = trx_lane_tree16(acc[e]);
+            if (l == 0 && valid) {
+                const float v = L.router_bias ? __fadd_rn(v0, L.router_bias[e]) : v0;
+                w.logits[(int64_t)(t0 + t) * E + e] = v;
+                if (w.out_logits) w.out_logits[(int64_t)(t0 + t) * E + e] = v;
+            }
+        }
+    }
+}
+
+__host__ __device__ constexpr size_t trx_router_many_smem(int router_type, int E) {
+    return (size_t)TRX_TOK_STAGE * 1024 + (size_t)E * (router_type == TRX_F32 ? 1024 : 512);
+}
+
 // longer passes: a warp per token
 __global__ void __launch_bounds__(256) trx_k_route(TrxShape S, int T, TrxWork w) {
     __shared__ float sp[8][96];

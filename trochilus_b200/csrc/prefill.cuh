@@ -80,7 +80,22 @@ __device__ __forceinline__ void trx_umma_commit(uint64_t *bar) {
                  : "memory");
 }
 
-// 32 consecutive accumulator columns of this warp's 32 lanes (one row per thread)
+// 32 consecutive accumulator columns of this warp's 32 lanes (one row per thread); _nw: without the wait (the
+// registers are valid after trx_tmem_wait_ld)
+__device__ __forceinline__ void trx_tmem_ld32_nw(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
+                 "%14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+                   "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+                   "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]),
+                   "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]),
+                   "=r"(r[30]), "=r"(r[31])
+                 : "r"(taddr)
+                 : "memory");
+}
+__device__ __forceinline__ void trx_tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void trx_tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
 __device__ __forceinline__ void trx_tmem_ld32(uint32_t taddr, float (&v)[32]) {
     uint32_t r[32];
     asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
@@ -105,7 +120,6 @@ __device__ __forceinline__ void trx_tmem_st32(uint32_t taddr, const float (&v)[3
                  "f"(v[16]), "f"(v[17]), "f"(v[18]), "f"(v[19]), "f"(v[20]), "f"(v[21]), "f"(v[22]), "f"(v[23]),
                  "f"(v[24]), "f"(v[25]), "f"(v[26]), "f"(v[27]), "f"(v[28]), "f"(v[29]), "f"(v[30]), "f"(v[31])
                  : "memory");
-    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
 // 2-D tiled TMA load (no multicast): box at element (x, y) of the tensor map into shared memory
@@ -339,15 +353,17 @@ __global__ void __launch_bounds__(TRX_PF_THREADS, 1)
             trx_tc_fence_after();
 #pragma unroll 1
             for (int c0 = 0; c0 < TRX_PF_BN; c0 += 32) {
-                float v[32], r[32];
-                trx_tmem_ld32(tl + c0, v);
-                if (c > 0) {
-                    trx_tmem_ld32(tl + TRX_PF_BN + c0, r);
+                uint32_t v[32], r[32];
+                trx_tmem_ld32_nw(tl + c0, v);
+                if (c > 0) trx_tmem_ld32_nw(tl + TRX_PF_BN + c0, r);
+                trx_tmem_wait_ld();
+                float o[32];
 #pragma unroll
-                    for (int i = 0; i < 32; i++) v[i] = __fadd_rn(r[i], v[i]);
-                }
-                trx_tmem_st32(tl + TRX_PF_BN + c0, v);
+                for (int i = 0; i < 32; i++)
+                    o[i] = c > 0 ? __fadd_rn(__uint_as_float(r[i]), __uint_as_float(v[i])) : __uint_as_float(v[i]);
+                trx_tmem_st32(tl + TRX_PF_BN + c0, o); // waited for once, below
             }
+            trx_tmem_wait_st();
             trx_tc_fence_before();
             __syncwarp();
             if (lane == 0) trx_mbar_arrive(cempty);
