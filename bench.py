@@ -254,8 +254,9 @@ def run_prefill(args, dev, cpu_seconds):
            "dtype": "3xTF32 (fp32 semantics, 1e-5)",
            "roofline": {"bound": "tensor", "kernel": "trx_k_pf_gemm (gate/up + down)", "achieved": tflops,
                         "peak": peak, "unit": "TFLOP/s", "frac": tflops / peak, "peak_kind": peak_kind,
-                        "flops": flops, "note": "useful flops of the whole layer call over its time; the tensor "
-                                                "pipe issues 3x these (hi.hi, hi.lo, lo.hi)"},
+                        "flops": flops, "issued_frac": 3.0 * tflops / peak,
+                        "note": "useful flops of the whole layer call over its time; the tensor pipe issues 3x these "
+                                "(hi.hi, hi.lo, lo.hi): issued_frac", "traffic": None},
            "e2e": {"value": T / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": 2 * T * H * 4,
                    "d2h_bytes_per_step": T * H * 4},
            "clocks": clk.summary()}
