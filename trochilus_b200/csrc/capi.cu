@@ -25,6 +25,7 @@
 #include "kernel_api.cuh"
 #include "fused_layer.cuh"
 #include "prefill.cuh"
+#include "ep.cuh"
 
 namespace {
 
@@ -176,6 +177,11 @@ struct tr_gpu_moe {
     int64_t pf_min = 0;
     float *pf_xhi = nullptr, *pf_xlo = nullptr;
     CUtensorMap pf_map_x[2], pf_map_h[2]; // A operands of the gate/up and of the down GEMM: hi, lo planes
+    // expert parallelism: per layer the device tables of the experts' gate, up and down matrices (E pointers each),
+    // and the scratch of tr_gpu_moe_experts_dev (grown to the largest call)
+    const uint8_t **ep_tab = nullptr;
+    uint8_t *ep_buf = nullptr;
+    int64_t ep_cap = 0;
     // zone timing (tr_gpu_moe_profile): one set of events per profiled call, read when asked, so that
     // profiling never makes a call wait for the one before it
     struct EvSet {
@@ -496,6 +502,8 @@ extern "C" void tr_gpu_moe_free(tr_gpu_moe *m) {
     if (m->work_mem) cudaFree(m->work_mem);
     if (m->tmp) cudaFree(m->tmp);
     if (m->trace) cudaFree(m->trace);
+    if (m->ep_tab) cudaFree(m->ep_tab);
+    if (m->ep_buf) cudaFree(m->ep_buf);
     for (auto &es : m->evs)
         for (cudaEvent_t e : es.ev) cudaEventDestroy(e);
     if (m->stream) cudaStreamDestroy(m->stream);
@@ -548,11 +556,26 @@ extern "C" int tr_gpu_moe_set_layer(tr_gpu_moe *m, int64_t layer, const void *ro
     if (ok && router_bias)
         ok = ck(cudaMemcpyAsync(bias, router_bias, (size_t)E * 4, cudaMemcpyHostToDevice, m->stream), "upload bias");
     for (int64_t e = 0; e < E && ok; e++) {
+        if (gate[e] == nullptr && up[e] == nullptr && down[e] == nullptr) continue; // held by another rank
         ok = upload_matrix(c.gate_type, F, H, gate[e], (uint8_t *)L.gate + e * L.gate_mb, m->tmp, m->stream) &&
              upload_matrix(c.gate_type, F, H, up[e], (uint8_t *)L.up + e * L.up_mb, m->tmp, m->stream) &&
              upload_matrix(c.down_type, H, F, down[e], (uint8_t *)L.down + e * L.down_mb, m->tmp, m->stream);
     }
     if (ok) ok = stream_wait(m->stream, 300.0);
+    // the layer's matrix tables for tr_gpu_moe_experts_dev
+    if (ok && m->ep_tab == nullptr)
+        ok = ck(cudaMalloc(&m->ep_tab, (size_t)c.n_layers * 3 * E * sizeof(void *)), "cudaMalloc(expert tables)");
+    if (ok) {
+        std::vector<const uint8_t *> tab((size_t)(3 * E));
+        for (int64_t e = 0; e < E; e++) {
+            tab[(size_t)e] = L.gate + e * L.gate_mb;
+            tab[(size_t)(E + e)] = L.up + e * L.up_mb;
+            tab[(size_t)(2 * E + e)] = L.down + e * L.down_mb;
+        }
+        ok = ck(cudaMemcpy(m->ep_tab + (size_t)layer * 3 * E, tab.data(), tab.size() * sizeof(void *),
+                           cudaMemcpyHostToDevice),
+                "upload expert tables");
+    }
     if (!ok) {
         put_err(err, err_len);
         return -1;
@@ -579,6 +602,8 @@ extern "C" int tr_gpu_moe_trace(tr_gpu_moe *m, int on) {
     if (m == nullptr || !ck(cudaSetDevice(m->device), "cudaSetDevice") || !stream_wait(m->stream)) return -1;
     if (!on) {
         if (m->trace) cudaFree(m->trace);
+    if (m->ep_tab) cudaFree(m->ep_tab);
+    if (m->ep_buf) cudaFree(m->ep_buf);
         m->trace = nullptr;
         return 0;
     }
@@ -864,6 +889,97 @@ extern "C" int tr_gpu_moe_layer(tr_gpu_moe *m, int64_t layer, const float *norme
         ok = false;
     }
     return ok ? 0 : -1;
+}
+
+// ---------------------------------------------------------------------------------------------
+// expert parallelism (ep.cuh): pack, the experts of arriving rows, combine
+
+extern "C" int tr_gpu_moe_ep_pack(tr_gpu_moe *m, const int64_t *d_sel_id, int64_t n_tok, int32_t n_ranks,
+                                  const float *d_normed, float *d_send_rows, int32_t *d_send_ids, int32_t *d_send_counts,
+                                  int32_t *d_place, int32_t *d_scratch, void *stream) {
+    g_err.clear();
+    if (m == nullptr || d_sel_id == nullptr || d_normed == nullptr || d_send_rows == nullptr || d_send_ids == nullptr ||
+        d_send_counts == nullptr || d_place == nullptr || d_scratch == nullptr || n_tok < 1 || n_ranks < 1 ||
+        n_ranks > 64 || m->cfg.n_expert % n_ranks != 0) {
+        set_err("bad arguments to tr_gpu_moe_ep_pack (ranks must divide the experts)");
+        return -1;
+    }
+    if (!ck(cudaSetDevice(m->device), "cudaSetDevice")) return -1;
+    cudaStream_t st = stream ? (cudaStream_t)stream : m->stream;
+    const int R = (int)(n_tok * m->cfg.n_used), H = (int)m->cfg.n_embd;
+    int32_t *offsets = d_scratch, *xmap = d_scratch + 72; // scratch: 72 + R int32
+    trx_k_stable_sort<<<1, 1024, 0, st>>>(d_sel_id, nullptr, m->cfg.n_expert / n_ranks, R, n_ranks, offsets, d_place, xmap,
+                                          d_send_counts);
+    trx_k_gather_rows<<<(unsigned)R, 256, 0, st>>>(d_normed, xmap, offsets + n_ranks, (int)m->cfg.n_used, H, d_send_rows,
+                                                   d_sel_id, d_send_ids);
+    return ck(cudaGetLastError(), "ep pack launch") ? 0 : -1;
+}
+
+extern "C" int tr_gpu_moe_experts_dev(tr_gpu_moe *m, int64_t layer, const float *d_rows, const int32_t *d_ids,
+                                      int64_t n_rows, float *d_out, void *stream) {
+    g_err.clear();
+    if (m == nullptr || layer < 0 || layer >= m->cfg.n_layers || !m->layer_set[(size_t)layer] || n_rows < 0 ||
+        (n_rows > 0 && (d_rows == nullptr || d_ids == nullptr || d_out == nullptr))) {
+        set_err("bad arguments to tr_gpu_moe_experts_dev (or the layer is not set)");
+        return -1;
+    }
+    if (n_rows == 0) return 0;
+    if (n_rows > (1 << 24)) {
+        set_err("tr_gpu_moe_experts_dev: %lld rows is more than it takes", (long long)n_rows);
+        return -1;
+    }
+    if (!ck(cudaSetDevice(m->device), "cudaSetDevice")) return -1;
+    cudaStream_t st = stream ? (cudaStream_t)stream : m->stream;
+    const tr_gpu_moe_config &c = m->cfg;
+    const int64_t E = c.n_expert, H = c.n_embd, F = c.n_ff, n = n_rows, mx = std::max(H, F);
+    // scratch: sort (offsets, place, xmap), grouped rows, gate and up outputs, down output, prepared inputs
+    const int64_t so = align_up((E + 8 + 2 * n) * 4, 256), xb = align_up(n * H * 4, 256), gb = align_up(n * F * 4, 256),
+                  qb = align_up(n * mx * 4, 256), bfb = align_up(n * (mx / 32) * 8, 256), scb = align_up(n * (mx / 256) * 8, 256),
+                  need = so + 2 * xb + 2 * gb + qb + bfb + scb;
+    if (need > m->ep_cap) {
+        if (m->ep_buf) {
+            if (!stream_wait(st)) return -1;
+            cudaFree(m->ep_buf);
+            m->ep_buf = nullptr;
+            m->ep_cap = 0;
+        }
+        if (!ck(cudaMalloc(&m->ep_buf, (size_t)need), "cudaMalloc(expert scratch)")) return -1;
+        m->ep_cap = need;
+    }
+    uint8_t *b = m->ep_buf;
+    int32_t *offsets = (int32_t *)b, *place = offsets + E + 8, *xmap = place + n;
+    float *xg = (float *)(b + so), *y = (float *)(b + so + xb), *g = (float *)(b + so + 2 * xb),
+          *u = (float *)(b + so + 2 * xb + gb);
+    uint32_t *dq = (uint32_t *)(b + so + 2 * xb + 2 * gb);
+    double *dbf = (double *)(b + so + 2 * xb + 2 * gb + qb), *dsc = (double *)(b + so + 2 * xb + 2 * gb + qb + bfb);
+    const uint8_t *const *tab = m->ep_tab + (size_t)layer * 3 * E;
+    trx_k_stable_sort<<<1, 1024, 0, st>>>(nullptr, d_ids, 1, (int)n, (int)E, offsets, place, xmap, nullptr);
+    trx_k_gather_rows<<<(unsigned)n, 256, 0, st>>>(d_rows, xmap, offsets + E, 1, (int)H, xg, nullptr, nullptr);
+    bool ok = trx_kapi_grouped(c.gate_type, F, H, tab, offsets, (int)E, (int)n, xg, dq, dbf, dsc, g, st) &&
+              trx_kapi_grouped(c.gate_type, F, H, tab + E, offsets, (int)E, (int)n, xg, dq, dbf, dsc, u, st) &&
+              trx_kapi_swiglu(g, u, n * F, st) &&
+              trx_kapi_grouped(c.down_type, H, F, tab + 2 * E, offsets, (int)E, (int)n, g, dq, dbf, dsc, y, st);
+    if (!ok) {
+        set_err("tr_gpu_moe_experts_dev: launch failed");
+        return -1;
+    }
+    trx_k_scatter_rows<<<(unsigned)n, 256, 0, st>>>(y, xmap, offsets + E, (int)H, d_out);
+    return ck(cudaGetLastError(), "experts launch") ? 0 : -1;
+}
+
+extern "C" int tr_gpu_moe_ep_combine(tr_gpu_moe *m, const float *d_sel_w, const int32_t *d_place, const float *d_back,
+                                     int64_t n_tok, float *d_x, float *d_ffn_out, void *stream) {
+    g_err.clear();
+    if (m == nullptr || d_sel_w == nullptr || d_place == nullptr || d_back == nullptr || d_x == nullptr || n_tok < 1) {
+        set_err("bad arguments to tr_gpu_moe_ep_combine");
+        return -1;
+    }
+    if (!ck(cudaSetDevice(m->device), "cudaSetDevice")) return -1;
+    cudaStream_t st = stream ? (cudaStream_t)stream : m->stream;
+    const int64_t total = n_tok * m->cfg.n_embd;
+    trx_k_pf_combine<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(d_sel_w, d_place, d_back, (int)n_tok,
+                                                                     (int)m->cfg.n_used, (int)m->cfg.n_embd, d_x, d_ffn_out);
+    return ck(cudaGetLastError(), "ep combine launch") ? 0 : -1;
 }
 
 // ---------------------------------------------------------------------------------------------

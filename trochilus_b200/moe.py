@@ -26,7 +26,7 @@ EXPORTS = ["tr_gpu_moe_create", "tr_gpu_moe_free", "tr_gpu_moe_bytes", "tr_gpu_m
            "tr_gpu_moe_check", "tr_gpu_moe_layer_part", "tr_gpu_moe_trace",
            "tr_gpu_moe_trace_read", "trmoe_last_error", "tr_matmul", "tr_matmul_grouped",
            "tr_matmul_grouped_s", "tr_softmax", "tr_swiglu", "trmoe_kernel_cache_clear", "tr_matmul_q4k_noalloc",
-           "tr_gpu_moe_set_prefill"]
+           "tr_gpu_moe_set_prefill", "tr_gpu_moe_ep_pack", "tr_gpu_moe_experts_dev", "tr_gpu_moe_ep_combine"]
 
 
 class Config(C.Structure):
@@ -67,6 +67,12 @@ def lib():
                                        C.POINTER(Outputs), C.c_void_p]
     L.tr_gpu_moe_launches.argtypes = [C.c_void_p, C.c_int64]
     L.tr_gpu_moe_set_prefill.argtypes = [C.c_void_p, C.c_int64]
+    L.tr_gpu_moe_ep_pack.argtypes = [C.c_void_p, C.c_void_p, C.c_int64, C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p,
+                                     C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]
+    L.tr_gpu_moe_experts_dev.argtypes = [C.c_void_p, C.c_int64, C.c_void_p, C.c_void_p, C.c_int64, C.c_void_p,
+                                         C.c_void_p]
+    L.tr_gpu_moe_ep_combine.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_void_p,
+                                        C.c_void_p, C.c_void_p]
     L.tr_gpu_moe_profile.argtypes = [C.c_void_p, C.c_int]
     L.tr_gpu_moe_check.argtypes = [C.c_void_p]
     L.tr_gpu_moe_trace.argtypes = [C.c_void_p, C.c_int]
@@ -117,7 +123,8 @@ class GpuMoe:
 
     def set_layer(self, layer: int, lay: dict, bias: np.ndarray | None = None):
         E = self.cfg.n_expert
-        arr = {n: (C.c_void_p * E)(*[m.ctypes.data for m in lay[n]]) for n in ("gate", "up", "down")}
+        # an expert whose matrices are None is held by another rank (expert parallelism): not uploaded
+        arr = {n: (C.c_void_p * E)(*[None if m is None else m.ctypes.data for m in lay[n]]) for n in ("gate", "up", "down")}
         b = None if bias is None else np.ascontiguousarray(bias, dtype=np.float32)
         err = C.create_string_buffer(512)
         rc = lib().tr_gpu_moe_set_layer(self.h, layer, lay["router"].ctypes.data, _p(b),
@@ -160,9 +167,15 @@ class GpuMoe:
         if rc != 0:
             raise RuntimeError(f"tr_gpu_moe_layer_dev: {last_error()}")
 
-    def layer_part(self, layer: int, part: int, normed_ptr: int, n_tok: int, x_ptr: int, stream: int = 0):
-        """tr_gpu_moe_layer_part: one of the four parts of a layer call (device pointers, enqueued only)."""
-        rc = lib().tr_gpu_moe_layer_part(self.h, layer, part, normed_ptr, n_tok, x_ptr, None, stream or None)
+    def layer_part(self, layer: int, part: int, normed_ptr: int, n_tok: int, x_ptr: int, outs: dict | None = None,
+                   stream: int = 0):
+        """tr_gpu_moe_layer_part: one of the four parts of a layer call (device pointers, enqueued only); outs as in
+        layer_dev (part 0 writes logits, sel_id, sel_w, offsets, place)."""
+        o = None
+        if outs:
+            o = Outputs(*(outs.get(k) for k in ("logits", "sel_id", "sel_w", "offsets", "place", "ffn_out")))
+        rc = lib().tr_gpu_moe_layer_part(self.h, layer, part, normed_ptr, n_tok, x_ptr, C.byref(o) if o else None,
+                                         stream or None)
         if rc != 0:
             raise RuntimeError(f"tr_gpu_moe_layer_part: {last_error()}")
 
@@ -198,6 +211,24 @@ class GpuMoe:
 
     def launches(self, n_tok: int) -> int:
         return int(lib().tr_gpu_moe_launches(self.h, n_tok))
+
+    def ep_pack(self, sel_id_ptr, n_tok, n_ranks, normed_ptr, send_rows_ptr, send_ids_ptr, send_counts_ptr, place_ptr,
+                scratch_ptr, stream=0):
+        """tr_gpu_moe_ep_pack (device pointers)."""
+        if lib().tr_gpu_moe_ep_pack(self.h, sel_id_ptr, n_tok, n_ranks, normed_ptr, send_rows_ptr, send_ids_ptr,
+                                    send_counts_ptr, place_ptr, scratch_ptr, stream or None) != 0:
+            raise RuntimeError(f"tr_gpu_moe_ep_pack: {last_error()}")
+
+    def experts_dev(self, layer, rows_ptr, ids_ptr, n_rows, out_ptr, stream=0):
+        """tr_gpu_moe_experts_dev (device pointers)."""
+        if lib().tr_gpu_moe_experts_dev(self.h, layer, rows_ptr, ids_ptr, n_rows, out_ptr, stream or None) != 0:
+            raise RuntimeError(f"tr_gpu_moe_experts_dev: {last_error()}")
+
+    def ep_combine(self, sel_w_ptr, place_ptr, back_ptr, n_tok, x_ptr, ffn_ptr=None, stream=0):
+        """tr_gpu_moe_ep_combine (device pointers)."""
+        if lib().tr_gpu_moe_ep_combine(self.h, sel_w_ptr, place_ptr, back_ptr, n_tok, x_ptr, ffn_ptr,
+                                       stream or None) != 0:
+            raise RuntimeError(f"tr_gpu_moe_ep_combine: {last_error()}")
 
     def set_prefill(self, min_tokens: int):
         """tr_gpu_moe_set_prefill: calls of at least min_tokens tokens take the tensor-core road (0: never)."""
