@@ -18,8 +18,10 @@ Arms:
              `prefill` = configs[2]'s layer (2048 tokens, Q8_0) on the tensor-core road, same keys, its roofline
              the useful TFLOP/s over the dense TF32 peak (--prefill-tokens 0 skips it; --only-prefill prints it alone).
   reference  Trochilus's own CPU code on this box's host cores, same config (rank 0 only under torchrun).
-N > 1: one process per GPU (torchrun); each rank runs its own replica of the workload (the layer has no
-data-path exchange at batch 1), time = max over ranks, `value` = all ranks' tokens / that time.
+N > 1: one process per GPU (torchrun), expert parallel (trochilus_b200/ep.py): rank r holds experts
+[64 r / N, 64 (r + 1) / N) and owns T tokens a step (weak scaling); each step routes them, sends their rows to the
+experts' ranks and back with NCCL all-to-alls (padded blocks: no host sync), and combines. time = max over ranks,
+`value` = all ranks' tokens / that time.
 """
 from __future__ import annotations
 
@@ -270,6 +272,128 @@ def run_prefill(args, dev, cpu_seconds):
     return out
 
 
+def ep_launches(gate, down):
+    """our kernels a step of the expert-parallel layer: route 1; pack 2; experts: sort, gather, gate and up 2 each,
+    SwiGLU, down 2, scatter; combine 1"""
+    return 1 + 2 + (2 + 2 + 2 + 1 + 2 + 2) + 1
+
+
+def run_ep(args, rank, world, dist):
+    import torch
+    from trochilus_b200 import ep
+    from trochilus_b200.moe import GpuMoe
+
+    dev = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(dev)
+    gate, down = TYPES[args.gate], TYPES[args.down]
+    T, NL = args.tokens, args.layers
+    m = GpuMoe(NL, E, K_USED, H, F, gb.BF16, gate, down, max_tokens=T * world, device=dev)
+    lays, routers = host_layers(gate, down, n_host=2, n_routers=NL)
+    for l in range(NL):
+        lay = dict(lays[l % len(lays)])
+        lay["router"] = routers[l]
+        m.set_layer(l, ep.local_layer(lay, E, rank, world))
+    del lays
+    st = torch.cuda.Stream()
+    be = ep.GpuEpBackend(m, st)
+    cap = T * K_USED
+    g = torch.Generator(device="cuda")
+    g.manual_seed(1234 + rank)
+    with torch.cuda.stream(st):
+        normed = torch.randn((NL, T, H), device="cuda", generator=g)
+        x = torch.randn((T, H), device="cuda", generator=g)
+        for i in range(max(args.warmup, 3)):
+            ep.ep_layer(dist, be, i % NL, normed[i % NL], x, cap=cap)
+    torch.cuda.synchronize()
+    dist.barrier()
+    steps = args.steps
+    reps = max(steps // NL, 1)
+    steps = reps * NL
+    # a CUDA graph of NL layer calls (kernels and NCCL all-to-alls; the padded exchange has no host sync)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=st):
+        for l in range(NL):
+            ep.ep_layer(dist, be, l, normed[l], x, cap=cap)
+    torch.cuda.synchronize()
+    dist.barrier()
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    dist.barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    cur = torch.cuda.current_stream()
+    with Clocks(dev) as clk:
+        clk.wait_first()
+        torch.cuda.synchronize()
+        start.record(cur)
+        for _ in range(reps):
+            graph.replay()
+        end.record(cur)
+        torch.cuda.synchronize()
+    del graph  # graphs holding NCCL calls go before the process group does
+    ms = start.elapsed_time(end)
+    t = torch.tensor([ms], device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    ms_step = ms / steps
+    value = world * T / (ms_step / 1000.0)
+    # bytes: each rank's distinct local experts hit per step (from the routing of every rank's tokens)
+    with torch.cuda.stream(st):
+        sel = be.route(0, normed[0], x)[0]
+    allsel = [torch.empty_like(sel) for _ in range(world)]
+    dist.all_gather(allsel, sel)
+    ids = torch.cat(allsel).cpu().numpy()
+    a, b = ep.expert_range(E, rank, world)
+    u_local = len(set(int(e) for e in ids if a <= e < b))
+    rank_bytes = u_local * bytes_per_expert(gate, down) + E * gb.row_bytes(gb.BF16, H) + 2 * T * H * 4
+    tb = torch.tensor([float(rank_bytes)], device="cuda")
+    dist.all_reduce(tb)
+    peak, peak_kind = peaks()
+    achieved = float(tb.item()) / world / (ms_step / 1000.0) / 1e9
+    link_bytes = 2 * world * cap * H * 4 + world * cap * 4  # rows there and back, ids (padded blocks)
+    # e2e: pinned host inputs in, the layer, x back, every step
+    hn = torch.randn((16, T, H), generator=torch.Generator().manual_seed(99 + rank)).pin_memory()
+    hx = torch.empty((T, H)).pin_memory()
+    e2e_steps = max(min(steps, 2000), 10)
+    dist.barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    with torch.cuda.stream(st):
+        dn = torch.empty((T, H), device="cuda")
+        for i in range(e2e_steps):
+            dn.copy_(hn[i % 16], non_blocking=True)
+            ep.ep_layer(dist, be, i % NL, dn, x, cap=cap)
+            hx.copy_(x, non_blocking=True)
+            st.synchronize()
+    e2e_s = time.perf_counter() - t0
+    te = torch.tensor([e2e_s], device="cuda")
+    dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_s = float(te.item())
+    m.close()
+    if rank != 0:
+        return
+    cfg = workload_config(args)
+    cfg["parallelism"] = f"ep{world}"
+    cfg["experts_per_gpu"] = E // world
+    line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": steps,
+            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int32/int64+f64 (Q4_K), f32 (Q6_K/Q8_0 lane contract)",
+            "data": "synthetic", "config": cfg,
+            "roofline": {"bound": "hbm", "kernel": "expert-parallel layer (route, pack, experts, combine + NCCL)",
+                         "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "peak_kind": peak_kind, "traffic": None,
+                         "algorithmic_bytes_per_gpu": float(tb.item()) / world,
+                         "nvlink_bytes_per_gpu": link_bytes,
+                         "nvlink_gbs_per_gpu": link_bytes / (ms_step / 1000.0) / 1e9},
+            "cpu_baseline": None,
+            "e2e": {"value": world * T * e2e_steps / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": T * H * 4,
+                    "d2h_bytes_per_step": T * H * 4, "steps": e2e_steps},
+            "gpu_launches": ep_launches(gate, down) * steps, "clocks": clk.summary(),
+            "timing": f"CUDA graph of {NL} expert-parallel layer calls (kernels + NCCL) replayed {reps} times; CUDA "
+                      f"events, max over ranks"}
+    print(json.dumps(line), flush=True)
+
+
 def run_ours(args, rank, world, dist):
     import torch
     from trochilus_b200.moe import GpuMoe
@@ -461,6 +585,8 @@ def main():
         print(json.dumps(run_prefill(args, 0, 0 if args.no_cpu_baseline else args.cpu_seconds)), flush=True)
     elif args.impl == "reference":
         run_reference(args, rank, world)
+    elif world > 1:
+        run_ep(args, rank, world, dist)
     else:
         run_ours(args, rank, world, dist)
     if dist:

@@ -100,17 +100,20 @@ typedef struct {
  * sort and mix, src/models/olmoe.c:1845-1933, split across GPUs that hold E / n_ranks experts each). A rank passes
  * NULL for the gate, up and down pointers of experts it does not hold to tr_gpu_moe_set_layer. Per layer call:
  *   1. tr_gpu_moe_layer_part(part 0) with sel_id / sel_w outputs routes the rank's own tokens;
- *   2. tr_gpu_moe_ep_pack groups the rank's n_tok * n_used (token, slot) rows by destination rank (expert / (E /
+ *   2. tr_gpu_moe_ep_pack groups the rank's R = n_tok * n_used (token, slot) rows by destination rank (expert / (E /
  *      n_ranks)), stably: d_send_rows (rows x n_embd f32), d_send_ids (int32 expert ids), d_send_counts[n_ranks],
- *      d_place[j] = row j's position in that order; d_scratch: 72 + n_tok * n_used int32;
+ *      d_place[j] = row j's position in that order; d_scratch: 72 + R int32. cap = 0: the rows packed (R of them);
+ *      cap >= R: destination d's rows at d cap .. (n_ranks x cap rows, unused ids -1), so that an all-to-all of equal
+ *      splits needs no counts on the host;
  *   3. the caller exchanges counts, rows and ids (NCCL all-to-all);
  *   4. tr_gpu_moe_experts_dev computes the expert FFN (gate/up, SwiGLU, down; the exact definitions) of n_rows rows
- *      that arrived in any order with their expert ids, into d_out (n_rows x n_embd), in arrival order;
+ *      that arrived in any order with their expert ids, into d_out (n_rows x n_embd), in arrival order (a row whose id
+ *      is out of range, the padding, is skipped and its output row left as it was);
  *   5. the caller sends the outputs back;
  *   6. tr_gpu_moe_ep_combine: x[t] += sum over slots in expert-id order of sel_w[t][slot] * d_back[place[t k + slot]]
  *      (and ffn_out, if not NULL).
  * The result is bit for bit the one-GPU layer's. Device pointers; `stream` NULL: the context's stream. 0 or -1. */
-TRMOE_API int tr_gpu_moe_ep_pack(tr_gpu_moe *m, const int64_t *d_sel_id, int64_t n_tok, int32_t n_ranks,
+TRMOE_API int tr_gpu_moe_ep_pack(tr_gpu_moe *m, const int64_t *d_sel_id, int64_t n_tok, int32_t n_ranks, int64_t cap,
                                  const float *d_normed, float *d_send_rows, int32_t *d_send_ids, int32_t *d_send_counts,
                                  int32_t *d_place, int32_t *d_scratch, void *stream);
 TRMOE_API int tr_gpu_moe_experts_dev(tr_gpu_moe *m, int64_t layer, const float *d_rows, const int32_t *d_ids,

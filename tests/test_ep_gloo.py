@@ -38,30 +38,40 @@ class OracleEpBackend:
         ids, ws = self.o.route(logits, K, 0)
         return torch.from_numpy(ids.ravel().copy()), torch.from_numpy(ws.ravel().copy())
 
-    def pack(self, sel_id, normed, world):
-        sid = sel_id.numpy()
+    def pack(self, sel_id, normed, world, cap=0):
+        sid = sid_all = sel_id.numpy()
         dest = sid // (E // world)
         order = np.argsort(dest, kind="stable")
+        counts = np.bincount(dest, minlength=world).astype(np.int32)
+        pos = np.arange(sid.size)
+        if cap:  # destination d's rows at d cap + their rank
+            starts = np.concatenate([[0], np.cumsum(counts)[:-1]])
+            pos = dest[order] * cap + (pos - starts[dest[order]])
         place = np.empty(sid.size, np.int32)
-        place[order] = np.arange(sid.size, dtype=np.int32)
-        rows = normed.numpy()[order // K]
-        return (torch.from_numpy(np.ascontiguousarray(rows)), torch.from_numpy(sid[order].astype(np.int32)),
-                torch.from_numpy(np.bincount(dest, minlength=world).astype(np.int32)), torch.from_numpy(place))
+        place[order] = pos
+        n = world * cap if cap else sid.size
+        rows = np.zeros((n, H), np.float32)
+        ids = np.full(n, -1, np.int32)
+        rows[pos] = normed.numpy()[order // K]
+        ids[pos] = sid_all[order]
+        return torch.from_numpy(rows), torch.from_numpy(ids), torch.from_numpy(counts), torch.from_numpy(place)
 
     def experts(self, layer, rows, ids):
-        ids = ids.numpy()
-        if ids.size == 0:
-            return torch.zeros((0, H), dtype=torch.float32)
+        ids_all = ids.numpy()
+        out = np.zeros((ids_all.size, H), np.float32)
+        sel = np.nonzero(ids_all >= 0)[0]  # the padding (-1) carries no row
+        if sel.size == 0:
+            return torch.from_numpy(out)
+        ids = ids_all[sel]
         assert ids.min() >= self.first and ids.max() < self.last, "a row reached a rank without its expert"
         order = np.argsort(ids, kind="stable")
         off = np.concatenate([[0], np.cumsum(np.bincount(ids, minlength=E))])
-        xg = rows.numpy()[order]
+        xg = rows.numpy()[sel][order]
         h1 = self.o.matmul_grouped(self.gt, F, H, self.mats["gate"], off, xg)
         h2 = self.o.matmul_grouped(self.gt, F, H, self.mats["up"], off, xg)
         h1 = self.o.swiglu(h1, h2)
         h3 = self.o.matmul_grouped(self.dt, H, F, self.mats["down"], off, h1)
-        out = np.empty_like(h3)
-        out[order] = h3
+        out[sel[order]] = h3
         return torch.from_numpy(out)
 
     def combine(self, sel_w, place, back, x, ffn_out=None):
@@ -82,7 +92,7 @@ def _case(rank):
     return (rng.normal(size=(T, H)).astype(np.float32), rng.normal(size=(T, H)).astype(np.float32))
 
 
-def _worker(rank, world, port, rt, gt, dt):
+def _worker(rank, world, port, rt, gt, dt, padded):
     import torch.distributed as dist
     from oracle.oracle import Oracle, make_desc
     os.environ["MASTER_ADDR"], os.environ["MASTER_PORT"] = "127.0.0.1", str(port)
@@ -96,7 +106,7 @@ def _worker(rank, world, port, rt, gt, dt):
         xt = torch.from_numpy(x.copy())
         for rep in range(2):  # two calls: nothing is left over from the first
             xr = xt.clone()
-            sid, sw = ep.ep_layer(dist, be, 0, torch.from_numpy(normed), xr)
+            sid, sw = ep.ep_layer(dist, be, 0, torch.from_numpy(normed), xr, cap=(3 + 2 * (world - 1)) * K if padded else None)
             d, keep = make_desc(lay, H, F, K, 0, rt, gt, dt, bias)
             want = oracle.moe_layer(d, normed, x)
             assert np.array_equal(sid.numpy().reshape(-1, K), want["sel_id"]), (rank, rep)
@@ -112,10 +122,10 @@ def _free_port():
         return s.getsockname()[1]
 
 
-@pytest.mark.parametrize("world", [2, 4])
-def test_ep_exchange_on_gloo_ranks_matches_one_process(world):
+@pytest.mark.parametrize("world,padded", [(2, False), (2, True), (4, False), (4, True)])
+def test_ep_exchange_on_gloo_ranks_matches_one_process(world, padded):
     import torch.multiprocessing as mp
-    mp.spawn(_worker, args=(world, _free_port(), gb.F32, gb.Q8_0, gb.Q6_K), nprocs=world, join=True)
+    mp.spawn(_worker, args=(world, _free_port(), gb.F32, gb.Q8_0, gb.Q6_K, padded), nprocs=world, join=True)
 
 
 def test_expert_range_and_local_layer():

@@ -29,9 +29,9 @@ def _contexts(torch, lay, bias, world, T, rt, gt, dt, device=0):
     return ms
 
 
-@pytest.mark.parametrize("world", [2, 4])
+@pytest.mark.parametrize("world,padded", [(2, False), (4, True)])
 @pytest.mark.parametrize("rt,gt,dt", [(gb.BF16, gb.Q4_K, gb.Q6_K), (gb.F32, gb.Q8_0, gb.Q8_0)])
-def test_ep_emulated_ranks_match_oracle(cuda, oracle, world, rt, gt, dt):
+def test_ep_emulated_ranks_match_oracle(cuda, oracle, world, padded, rt, gt, dt):
     torch = cuda
     lay = gb.make_layer(808 + world, E, H, F, gt, dt, rt, mode="random")
     bias = gb.zipf_bias(6, E)
@@ -49,7 +49,7 @@ def test_ep_emulated_ranks_match_oracle(cuda, oracle, world, rt, gt, dt):
             dn = [torch.from_numpy(n).cuda() for n in normeds]
             dx = [torch.from_numpy(x.copy()).cuda() for x in xs]
             ffn = [torch.full((T, H), float("nan"), device="cuda") for T in Ts]
-            routed = ep.ep_layer_emulated(bes, 0, dn, dx, ffn)
+            routed = ep.ep_layer_emulated(bes, 0, dn, dx, ffn, padded=padded)
         torch.cuda.synchronize()
         for r in range(world):
             want = oracle.moe_layer(d, normeds[r], xs[r])
@@ -113,13 +113,15 @@ def _nccl_worker(rank, world, port, out_dir):
         T = 1 + rank
         normed = rng.normal(size=(T, H)).astype(np.float32)
         x = rng.normal(size=(T, H)).astype(np.float32)
-        with torch.cuda.stream(st):
-            dx = torch.from_numpy(x.copy()).cuda()
-            ep.ep_layer(dist, be, 0, torch.from_numpy(normed).cuda(), dx)
-        torch.cuda.synchronize()
         d, keep = make_desc(lay, H, F, K, 0, rt, gt, dt)
         want = Oracle().moe_layer(d, normed, x)
-        ok = same_bits(dx.cpu().numpy(), want["x"])
+        ok = True
+        for padded in (True, False):
+            with torch.cuda.stream(st):
+                dx = torch.from_numpy(x.copy()).cuda()
+                ep.ep_layer(dist, be, 0, torch.from_numpy(normed).cuda(), dx, cap=world * K if padded else None)
+            torch.cuda.synchronize()
+            ok = ok and same_bits(dx.cpu().numpy(), want["x"])
         with open(os.path.join(out_dir, f"rank{rank}"), "w") as f:
             f.write("ok" if ok else "mismatch")
         m.close()

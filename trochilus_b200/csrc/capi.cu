@@ -894,24 +894,26 @@ extern "C" int tr_gpu_moe_layer(tr_gpu_moe *m, int64_t layer, const float *norme
 // ---------------------------------------------------------------------------------------------
 // expert parallelism (ep.cuh): pack, the experts of arriving rows, combine
 
-extern "C" int tr_gpu_moe_ep_pack(tr_gpu_moe *m, const int64_t *d_sel_id, int64_t n_tok, int32_t n_ranks,
+extern "C" int tr_gpu_moe_ep_pack(tr_gpu_moe *m, const int64_t *d_sel_id, int64_t n_tok, int32_t n_ranks, int64_t cap,
                                   const float *d_normed, float *d_send_rows, int32_t *d_send_ids, int32_t *d_send_counts,
                                   int32_t *d_place, int32_t *d_scratch, void *stream) {
     g_err.clear();
+    const int64_t R = n_tok * (m ? m->cfg.n_used : 0);
     if (m == nullptr || d_sel_id == nullptr || d_normed == nullptr || d_send_rows == nullptr || d_send_ids == nullptr ||
         d_send_counts == nullptr || d_place == nullptr || d_scratch == nullptr || n_tok < 1 || n_ranks < 1 ||
-        n_ranks > 64 || m->cfg.n_expert % n_ranks != 0) {
-        set_err("bad arguments to tr_gpu_moe_ep_pack (ranks must divide the experts)");
+        n_ranks > 64 || m->cfg.n_expert % n_ranks != 0 || (cap != 0 && cap < R) || R > (1 << 24)) {
+        set_err("bad arguments to tr_gpu_moe_ep_pack (ranks must divide the experts; cap 0 or at least n_tok x n_used)");
         return -1;
     }
     if (!ck(cudaSetDevice(m->device), "cudaSetDevice")) return -1;
     cudaStream_t st = stream ? (cudaStream_t)stream : m->stream;
-    const int R = (int)(n_tok * m->cfg.n_used), H = (int)m->cfg.n_embd;
+    const int H = (int)m->cfg.n_embd;
+    const int64_t div = m->cfg.n_expert / n_ranks;
     int32_t *offsets = d_scratch, *xmap = d_scratch + 72; // scratch: 72 + R int32
-    trx_k_stable_sort<<<1, 1024, 0, st>>>(d_sel_id, nullptr, m->cfg.n_expert / n_ranks, R, n_ranks, offsets, d_place, xmap,
-                                          d_send_counts);
+    if (cap > 0 && !ck(cudaMemsetAsync(d_send_ids, 0xff, (size_t)(n_ranks * cap) * 4, st), "clear ids")) return -1;
+    trx_k_stable_sort<<<1, 1024, 0, st>>>(d_sel_id, nullptr, div, (int)R, n_ranks, offsets, d_place, xmap, d_send_counts);
     trx_k_gather_rows<<<(unsigned)R, 256, 0, st>>>(d_normed, xmap, offsets + n_ranks, (int)m->cfg.n_used, H, d_send_rows,
-                                                   d_sel_id, d_send_ids);
+                                                   d_sel_id, d_send_ids, offsets, (int)cap, div, d_place);
     return ck(cudaGetLastError(), "ep pack launch") ? 0 : -1;
 }
 
@@ -954,7 +956,8 @@ extern "C" int tr_gpu_moe_experts_dev(tr_gpu_moe *m, int64_t layer, const float 
     double *dbf = (double *)(b + so + 2 * xb + 2 * gb + qb), *dsc = (double *)(b + so + 2 * xb + 2 * gb + qb + bfb);
     const uint8_t *const *tab = m->ep_tab + (size_t)layer * 3 * E;
     trx_k_stable_sort<<<1, 1024, 0, st>>>(nullptr, d_ids, 1, (int)n, (int)E, offsets, place, xmap, nullptr);
-    trx_k_gather_rows<<<(unsigned)n, 256, 0, st>>>(d_rows, xmap, offsets + E, 1, (int)H, xg, nullptr, nullptr);
+    trx_k_gather_rows<<<(unsigned)n, 256, 0, st>>>(d_rows, xmap, offsets + E, 1, (int)H, xg, nullptr, nullptr, nullptr,
+                                                   0, 1, nullptr);
     bool ok = trx_kapi_grouped(c.gate_type, F, H, tab, offsets, (int)E, (int)n, xg, dq, dbf, dsc, g, st) &&
               trx_kapi_grouped(c.gate_type, F, H, tab + E, offsets, (int)E, (int)n, xg, dq, dbf, dsc, u, st) &&
               trx_kapi_swiglu(g, u, n * F, st) &&

@@ -80,18 +80,26 @@ __global__ void __launch_bounds__(1024) trx_k_stable_sort(const int64_t *__restr
 }
 
 // dst row pos = src row xmap[pos] / div (cols floats, cols % 4 == 0); ids_out[pos] = ids_in[xmap[pos]] when given.
-// Rows past *n_sorted (the sort's total: rows with a dropped key) are not touched.
+// Rows past *n_sorted (the sort's total: rows with a dropped key) are not touched. cap > 0 (the pack's padded form):
+// the rows of bucket b = ids_in[j] / kdiv go to b cap + their rank in the bucket instead, and place[j] says so.
 __global__ void __launch_bounds__(256) trx_k_gather_rows(const float *__restrict__ src, const int32_t *__restrict__ xmap,
                                                          const int32_t *__restrict__ n_sorted, int div, int cols,
                                                          float *__restrict__ dst, const int64_t *__restrict__ ids_in,
-                                                         int32_t *__restrict__ ids_out) {
+                                                         int32_t *__restrict__ ids_out, const int32_t *__restrict__ offsets,
+                                                         int cap, int64_t kdiv, int32_t *__restrict__ place) {
     const int pos = blockIdx.x;
     if (pos >= *n_sorted) return;
     const int j = xmap[pos];
+    int dpos = pos;
+    if (cap > 0) {
+        const int b = (int)(ids_in[j] / kdiv);
+        dpos = b * cap + pos - offsets[b];
+        if (threadIdx.x == 0) place[j] = dpos;
+    }
     const float4 *s = reinterpret_cast<const float4 *>(src + (int64_t)(j / div) * cols);
-    float4 *d = reinterpret_cast<float4 *>(dst + (int64_t)pos * cols);
+    float4 *d = reinterpret_cast<float4 *>(dst + (int64_t)dpos * cols);
     for (int i = threadIdx.x; i < cols / 4; i += blockDim.x) d[i] = s[i];
-    if (ids_out && threadIdx.x == 0) ids_out[pos] = (int32_t)ids_in[j];
+    if (ids_out && threadIdx.x == 0) ids_out[dpos] = (int32_t)ids_in[j];
 }
 
 // out row xmap[pos] = src row pos, for pos < *n_sorted

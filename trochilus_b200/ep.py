@@ -6,7 +6,8 @@ One layer call on every rank (SPMD, `ep_layer`):
 2. pack    its (token, slot) rows grouped by destination rank (expert // (E / N)), stably, with their expert ids;
 3. a2a     counts, then rows and ids, over torch.distributed (NCCL between GPUs; gloo in the CPU tests);
 4. experts the expert FFN of the rows that arrived, each with its expert id;
-5. a2a     the outputs back, in the order they were sent;
+5. a2a     the outputs back, in the order they were sent (short passes: blocks of equal size per destination,
+           padded, so that no count has to reach the host);
 6. combine x[t] += sum over slots, in increasing expert id, of w * out (the reference's mix_body order,
            src/models/olmoe.c:1432-1446).
 
@@ -38,34 +39,56 @@ def local_layer(lay: dict, E: int, rank: int, world: int) -> dict:
     return out
 
 
-def ep_layer(dist, be, layer: int, normed: torch.Tensor, x: torch.Tensor, ffn_out: torch.Tensor | None = None):
+def ep_layer(dist, be, layer: int, normed: torch.Tensor, x: torch.Tensor, ffn_out: torch.Tensor | None = None,
+             cap: int | None = None):
     """One expert-parallel MoE layer call on this rank: x (T x H) += the layer's output for this rank's tokens.
-    Returns (sel_id, sel_w) of the rank's tokens."""
+    Returns (sel_id, sel_w) of the rank's tokens.
+
+    cap (the padded exchange, for short passes): every rank sends every destination a block of cap rows (unused ids
+    -1), so the all-to-alls have equal splits and no count reaches the host. Every rank must pass the same cap, at
+    least its T x k rows (e.g. the per-rank token limit x k). None: the counts go first and the rows follow packed."""
     world = dist.get_world_size()
-    sel_id, sel_w = be.route(layer, normed, x)
-    send_rows, send_ids, send_counts, place = be.pack(sel_id, normed, world)
-    recv_counts = torch.empty_like(send_counts)
-    dist.all_to_all_single(recv_counts, send_counts)
-    sc, rc = send_counts.tolist(), recv_counts.tolist()
     H = normed.shape[1]
-    recv_rows = be.empty((sum(rc), H), torch.float32)
-    recv_ids = be.empty((sum(rc),), torch.int32)
-    dist.all_to_all_single(recv_rows, send_rows, rc, sc)
-    dist.all_to_all_single(recv_ids, send_ids, rc, sc)
-    out = be.experts(layer, recv_rows, recv_ids)
-    back = be.empty((sum(sc), H), torch.float32)
-    dist.all_to_all_single(back, out, sc, rc)
+    sel_id, sel_w = be.route(layer, normed, x)
+    if cap:
+        if sel_id.numel() > cap:
+            raise ValueError(f"{sel_id.numel()} rows do not fit the padded blocks of {cap}")
+        send_rows, send_ids, _, place = be.pack(sel_id, normed, world, cap)
+        recv_rows = be.empty((world * cap, H), torch.float32)
+        recv_ids = be.empty((world * cap,), torch.int32)
+        dist.all_to_all_single(recv_rows, send_rows)
+        dist.all_to_all_single(recv_ids, send_ids)
+        out = be.experts(layer, recv_rows, recv_ids)
+        back = be.empty((world * cap, H), torch.float32)
+        dist.all_to_all_single(back, out)
+    else:
+        send_rows, send_ids, send_counts, place = be.pack(sel_id, normed, world, 0)
+        recv_counts = torch.empty_like(send_counts)
+        dist.all_to_all_single(recv_counts, send_counts)
+        sc, rc = send_counts.tolist(), recv_counts.tolist()
+        recv_rows = be.empty((sum(rc), H), torch.float32)
+        recv_ids = be.empty((sum(rc),), torch.int32)
+        dist.all_to_all_single(recv_rows, send_rows, rc, sc)
+        dist.all_to_all_single(recv_ids, send_ids, rc, sc)
+        out = be.experts(layer, recv_rows, recv_ids)
+        back = be.empty((sum(sc), H), torch.float32)
+        dist.all_to_all_single(back, out, sc, rc)
     be.combine(sel_w, place, back, x, ffn_out)
     return sel_id, sel_w
 
 
-def ep_layer_emulated(bes, layer: int, normeds, xs, ffn_outs=None):
+def ep_layer_emulated(bes, layer: int, normeds, xs, ffn_outs=None, padded: bool = False):
     """ep_layer for len(bes) ranks in one process: the same steps, the all-to-alls done by slicing."""
     world = len(bes)
     routed = [be.route(layer, n, x) for be, n, x in zip(bes, normeds, xs)]
-    packs = [be.pack(r[0], n, world) for be, r, n in zip(bes, routed, normeds)]
-    counts = [p[2].tolist() for p in packs]
-    starts = [[sum(c[:d]) for d in range(world)] for c in counts]
+    cap = max(r[0].numel() for r in routed) if padded else 0
+    packs = [be.pack(r[0], n, world, cap) for be, r, n in zip(bes, routed, normeds)]
+    if padded:
+        counts = [[cap] * world for _ in range(world)]
+        starts = [[d * cap for d in range(world)] for _ in range(world)]
+    else:
+        counts = [p[2].tolist() for p in packs]
+        starts = [[sum(c[:d]) for d in range(world)] for c in counts]
     outs = []
     for d, be in enumerate(bes):  # destination d receives from every source s, in source order
         rows = torch.cat([packs[s][0][starts[s][d]:starts[s][d] + counts[s][d]] for s in range(world)])
@@ -106,16 +129,16 @@ class GpuEpBackend:
                               {"sel_id": sel_id.data_ptr(), "sel_w": sel_w.data_ptr()}, stream=self._s())
         return sel_id, sel_w
 
-    def pack(self, sel_id, normed, world):
+    def pack(self, sel_id, normed, world, cap=0):
         R = sel_id.numel()
-        rows = self.empty((R, self.H), torch.float32)
-        ids = self.empty((R,), torch.int32)
+        rows = self.empty((world * cap if cap else R, self.H), torch.float32)
+        ids = self.empty((world * cap if cap else R,), torch.int32)
         counts = self.empty((world,), torch.int32)
         place = self.empty((R,), torch.int32)
         scratch = self.empty((72 + R,), torch.int32)
         with torch.cuda.stream(self.stream):
-            self.m.ep_pack(sel_id.data_ptr(), R // self.k, world, normed.data_ptr(), rows.data_ptr(), ids.data_ptr(),
-                           counts.data_ptr(), place.data_ptr(), scratch.data_ptr(), stream=self._s())
+            self.m.ep_pack(sel_id.data_ptr(), R // self.k, world, cap, normed.data_ptr(), rows.data_ptr(),
+                           ids.data_ptr(), counts.data_ptr(), place.data_ptr(), scratch.data_ptr(), stream=self._s())
         return rows, ids, counts, place
 
     def experts(self, layer, rows, ids):

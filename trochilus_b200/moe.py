@@ -67,8 +67,8 @@ def lib():
                                        C.POINTER(Outputs), C.c_void_p]
     L.tr_gpu_moe_launches.argtypes = [C.c_void_p, C.c_int64]
     L.tr_gpu_moe_set_prefill.argtypes = [C.c_void_p, C.c_int64]
-    L.tr_gpu_moe_ep_pack.argtypes = [C.c_void_p, C.c_void_p, C.c_int64, C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p,
-                                     C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]
+    L.tr_gpu_moe_ep_pack.argtypes = [C.c_void_p, C.c_void_p, C.c_int64, C.c_int32, C.c_int64, C.c_void_p, C.c_void_p,
+                                     C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]
     L.tr_gpu_moe_experts_dev.argtypes = [C.c_void_p, C.c_int64, C.c_void_p, C.c_void_p, C.c_int64, C.c_void_p,
                                          C.c_void_p]
     L.tr_gpu_moe_ep_combine.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_void_p,
@@ -212,10 +212,10 @@ class GpuMoe:
     def launches(self, n_tok: int) -> int:
         return int(lib().tr_gpu_moe_launches(self.h, n_tok))
 
-    def ep_pack(self, sel_id_ptr, n_tok, n_ranks, normed_ptr, send_rows_ptr, send_ids_ptr, send_counts_ptr, place_ptr,
-                scratch_ptr, stream=0):
-        """tr_gpu_moe_ep_pack (device pointers)."""
-        if lib().tr_gpu_moe_ep_pack(self.h, sel_id_ptr, n_tok, n_ranks, normed_ptr, send_rows_ptr, send_ids_ptr,
+    def ep_pack(self, sel_id_ptr, n_tok, n_ranks, cap, normed_ptr, send_rows_ptr, send_ids_ptr, send_counts_ptr,
+                place_ptr, scratch_ptr, stream=0):
+        """tr_gpu_moe_ep_pack (device pointers; cap 0: packed, cap >= rows: padded per destination)."""
+        if lib().tr_gpu_moe_ep_pack(self.h, sel_id_ptr, n_tok, n_ranks, cap, normed_ptr, send_rows_ptr, send_ids_ptr,
                                     send_counts_ptr, place_ptr, scratch_ptr, stream or None) != 0:
             raise RuntimeError(f"tr_gpu_moe_ep_pack: {last_error()}")
 
