@@ -1,12 +1,13 @@
 // fused_layer.cuh: one MoE layer call for a short pass (decode) as ONE persistent kernel, launched
 // cooperatively so that every CTA is resident and may wait for another.
 //
-//  phase A  CTAs 0..E-1 compute the router logits of one expert each (trx_router_block); CTAs E..E+T-1
-//           prepare one token's input row each; the last of them to finish routes every token, sorts the
-//           (token, slot) rows by expert and publishes the routing (a release store of the call's epoch).
-//  phase B  every CTA waits for the routing, copies the call's routing and the tokens' prepared input rows
-//           into shared memory, and takes its share of the routed gate/up rows and of the routed down rows
-//           (trx_cta_range over each virtual row space).
+//  routing  (a) local, for T <= 2 with a BF16 2048-column router when enabled: every CTA computes all logits
+//           itself from L2. (b) otherwise: CTAs 0..E-1 compute the router logits of one expert each
+//           (trx_router_block), CTAs E..E+T-1 prepare one token's input row each, and every CTA counts itself in;
+//           once all E + T are in, every CTA reads the logits, routes every token and sorts the (token, slot) rows
+//           by expert in its own shared memory (no CTA publishes a routing for the others), and stages the
+//           tokens' prepared input rows. Each CTA then takes its share of the routed gate/up rows and of the
+//           routed down rows (trx_cta_range over each virtual row space).
 //  then     warp-specialised: a producer warp streams this CTA's gate/up chunks (8 rows of gate and of up)
 //           and down chunks (16 rows) from HBM into shared-memory stages with 1-D TMA bulk copies, refilling a
 //           stage when its "empty" barrier says the 8 consumer warps are done with it; the down weights do not
@@ -34,11 +35,12 @@
 #define TRX_FU_CWARPS 8                           // consumer warps
 #define TRX_FU_THREADS (32 * (TRX_FU_CWARPS + 1)) // + the producer warp
 #define TRX_FU_MAXST 8                            // most stages of either kind
-#define TRX_LOCAL_ROUTE_MAX 2                     // tokens up to which every CTA routes the call itself
+#define TRX_LOCAL_ROUTE_MAX 2                     // tokens up to which every CTA may route the call itself
+#define TRX_FU_LOCAL_PREP 8                       // tokens up to which every CTA prepares the inputs itself
 
 struct TrxSync {
     uint32_t route_cnt;                // router and prep CTAs done in this call
-    uint32_t routed;                   // the epoch of the last call whose routing is published
+    uint32_t routed;                   // unused (kept for the layout)
     uint32_t finish;                   // CTAs done in this call
     uint32_t pad;
     uint32_t gu_done[TRX_MAX_EXPERTS]; // gate/up rows done per active slot (+1 once Q4_K's down inputs are ready)
@@ -71,14 +73,20 @@ __device__ __forceinline__ bool trx_spin(const uint32_t *p, uint32_t target, boo
 }
 
 // A CTA's walk over its range [v, end) of a virtual row space of n_active experts x per rows, in chunks of at most
-// `most` rows that stay inside one expert (and, when aligned, inside one `most`-row block). int32: the spaces hold at
-// most 64 x 2048 rows.
+// `most` rows that stay inside one expert (and, when aligned, inside one `most`-row block). When `most` divides
+// `per` the CTAs share whole chunks. int32: the spaces hold at most 64 x 2048 rows.
 struct TrxWalk {
     int v, end, slot, r, per, most;
     bool aligned;
     __device__ void init(int V, int per_, int most_, bool aligned_) {
         int64_t a, b;
-        trx_cta_range(V, a, b);
+        if (per_ % most_ == 0) { // whole chunks: the CTAs' shares differ by one chunk at most, none is partial
+            trx_cta_range(V / most_, a, b);
+            a *= most_;
+            b *= most_;
+        } else {
+            trx_cta_range(V, a, b);
+        }
         v = (int)a;
         end = (int)b;
         per = per_;
@@ -115,7 +123,8 @@ __host__ __device__ inline TrxFusedSmem trx_fused_layout(int gate_type, int down
     const int rbd = down_type == TRX_Q4_K ? F / 256 * 144 : down_type == TRX_Q6_K ? F / 256 * 208 : F / 32 * 34;
     TrxFusedSmem l;
     l.gu_stage = (size_t)2 * TRX_GU_CHUNK * rbg;
-    l.dn_stage = (size_t)TRX_DN_CHUNK * rbd;
+    // Q6_K: the rows' f16 d values (stored after all rows of the matrix) come with them, the 16-row block's
+    l.dn_stage = (size_t)TRX_DN_CHUNK * rbd + (down_type == TRX_Q6_K ? (size_t)TRX_DN_CHUNK * (F / 256) * 2 : 0);
     size_t stages = sg * l.gu_stage + sd * l.dn_stage;
     const size_t router = (size_t)(1 + (T < TRX_TOK_STAGE ? T : TRX_TOK_STAGE)) * H * 4;
     if (router > stages) stages = router;
@@ -138,6 +147,7 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
                 float *__restrict__ x_io, float *__restrict__ ffn_out, uint32_t epoch, int SG, int SD) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ int s_active[TRX_MAX_EXPERTS], s_off[TRX_MAX_EXPERTS + 1], s_nact, s_flag;
+    __shared__ int s_pact[TRX_MAX_EXPERTS]; // the producer's copy of the active experts
     __shared__ float sp[TRX_FU_CWARPS + 1][96];
     __shared__ int scnt[64];
     __shared__ float s_logit[TRX_LOCAL_ROUTE_MAX * TRX_MAX_EXPERTS];
@@ -160,11 +170,22 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
     uint8_t *s_tok = smem + lay.tok;
     if (tid < TRX_FU_MAXST) s_gcnt[tid] = s_dcnt[tid] = 0u;
     const int nsb_g = H / 256;
+    if (tid == 0) { // the pipelines' barriers (their region is not scratch for the routing phase)
+        for (int s = 0; s < SG; s++) {
+            trx_mbar_init(&full_g[s], 1);
+            trx_mbar_init(&empty_g[s], TRX_FU_CWARPS);
+        }
+        for (int s = 0; s < SD; s++) {
+            trx_mbar_init(&full_d[s], 1);
+            trx_mbar_init(&empty_d[s], TRX_FU_CWARPS);
+        }
+        trx_fence_barrier_init();
+    }
 
     // Local routing (a decode call with a BF16 router of 2048 columns): every CTA computes all of the call's
     // logits from L2, routes and sorts them in shared memory, and prepares the tokens itself; no CTA waits for
-    // another before the weights stream. Otherwise phase A / B below route once and publish.
-    const bool local = T <= TRX_LOCAL_ROUTE_MAX && H == 2048 && L.router_type == TRX_BF16;
+    // another before the weights stream. Otherwise the logits are computed once, expert by expert (below).
+    const bool local = S.local_route && T <= TRX_LOCAL_ROUTE_MAX && H == 2048 && L.router_type == TRX_BF16;
     if (local) {
         // logits: a chain per (expert, lane l), lane l's 16 elements of each 256-block in lane-row order (2 x 16
         // bytes), every token of the call against the same weights; the next round's weights load while a round
@@ -255,113 +276,152 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
         if (warp < T)
             trx_route_token<true>(s_logit + warp * E, E, k, S.norm_topk, lane, sp[warp], s_selid + warp * k,
                                   s_selw + warp * k);
+        if (blockIdx.x == 0 && w.out_logits)
+            for (int j = tid; j < T * E; j += blockDim.x) w.out_logits[j] = s_logit[j];
         __syncthreads();
-        TRX_TRACE(60);
-        if (warp == 0) {
-            const bool out = blockIdx.x == 0;
-            const TrxSortOut so{s_off, s_active, &s_nact, s_place, s_xmap, out ? w.out_offsets : nullptr,
-                                out ? w.out_place : nullptr};
-            trx_warp_counting_sort(s_selid, R, E, k, so, scnt, lane);
-        }
-        if (blockIdx.x == 0) {
-            if (w.out_logits)
-                for (int j = tid; j < T * E; j += blockDim.x) w.out_logits[j] = s_logit[j];
-            if (w.out_sel_id)
-                for (int j = tid; j < R; j += blockDim.x) {
-                    w.out_sel_id[j] = s_selid[j];
-                    w.out_sel_w[j] = s_selw[j];
-                }
-        }
-        __syncthreads();
-        TRX_TRACE(2);
     } else {
-        // ---------------- phase A: router logits, token preparation, routing by the last CTA of them
-        if ((int)blockIdx.x < E + T) {
+        // ---------------- phase A: CTAs 0..E-1 the logits of one expert each; the tokens' prepared inputs either
+        // by every CTA for itself into shared memory (T <= TRX_FU_LOCAL_PREP: from normed, while the logits are
+        // computed elsewhere) or by CTAs E..E+T-1 into global memory; every CTA that wrote counts itself in (release)
+        const bool lprep = T <= TRX_FU_LOCAL_PREP;
+        const int writers = E + (lprep ? 0 : T);
+        if ((int)blockIdx.x < writers) {
             if ((int)blockIdx.x < E) trx_router_block(L, S, normed, blockIdx.x, 0, T, w, reinterpret_cast<float *>(smem));
             else trx_prep_token(L, S, normed, blockIdx.x - E, w);
             __syncthreads();
             TRX_TRACE(62);
             if (tid == 0) {
                 __threadfence();
-                s_flag = atomicAdd(&sync->route_cnt, 1u) == (uint32_t)(E + T - 1);
+                atomicAdd(&sync->route_cnt, 1u);
             }
-            __syncthreads();
-            if (s_flag) {
-                __threadfence();
-                TRX_TRACE(59);
-                for (int t = warp; t < T; t += TRX_FU_CWARPS + 1)
-                    trx_route_token(w.logits + (int64_t)t * E, E, k, S.norm_topk, lane, sp[warp], w.sel_id + (int64_t)t * k,
-                                    w.sel_w + (int64_t)t * k);
-                __syncthreads();
-                TRX_TRACE(60);
-                if (w.out_sel_id)
-                    for (int j = tid; j < R; j += blockDim.x) {
-                        w.out_sel_id[j] = w.sel_id[j];
-                        w.out_sel_w[j] = w.sel_w[j];
-                    }
-                if (R <= 32) {
-                    const TrxSortOut so{w.offsets, w.active, w.n_active, w.place, w.xmap, w.out_offsets, w.out_place};
-                    if (warp == 0) trx_warp_counting_sort(w.sel_id, R, E, k, so, scnt, lane);
-                } else {
-                    trx_block_counting_sort<TRX_FU_CWARPS + 1>(w.sel_id, R, E, k, w);
-                }
-                __syncthreads();
-                TRX_TRACE(61);
-                if (tid == 0) {
-                    sync->route_cnt = 0u;
-                    __threadfence();
-                    trx_st_release(&sync->routed, epoch);
-                }
-            }
-            TRX_TRACE(1);
         }
-        // ---------------- phase B: the routing and the tokens' inputs into shared memory
-        if (tid == 0) s_flag = trx_spin(&sync->routed, epoch, true);
+        if (lprep) {
+            if (GT == TRX_Q4_K) {
+                for (int q = warp; q < T * nsb_g; q += TRX_FU_CWARPS + 1) {
+                    const int t = q / nsb_g, s4 = q % nsb_g;
+                    uint8_t *tok = s_tok + t * lay.tok_bytes;
+                    double *bfd = reinterpret_cast<double *>(tok + (size_t)H * 4);
+                    trx_prep_q4x_block(normed + (int64_t)t * H + 256 * s4, reinterpret_cast<uint32_t *>(tok), s4, nsb_g,
+                                       bfd + 8 * s4, bfd + H / 32 + s4, lane);
+                }
+            } else {
+                for (int i = tid; i < T * H / 4; i += blockDim.x) {
+                    const int t = (4 * i) / H, kk = (4 * i) % H;
+                    const float4 v = *reinterpret_cast<const float4 *>(normed + (int64_t)t * H + kk);
+                    float *dst = reinterpret_cast<float *>(s_tok + t * lay.tok_bytes);
+                    dst[trx_lc_pos(kk)] = v.x;
+                    dst[trx_lc_pos(kk + 1)] = v.y;
+                    dst[trx_lc_pos(kk + 2)] = v.z;
+                    dst[trx_lc_pos(kk + 3)] = v.w;
+                }
+            }
+        }
+        // While the logits come in, warp 4 (on warp 0's sub-partition) runs the routing steps once on dummy logits,
+        // so that the instructions warp 0 runs next are in the SM's instruction caches (run once per call, they
+        // would otherwise be fetched cold from L2 line by line)
+        if (warp == 4) {
+            float *dl = reinterpret_cast<float *>(smem) + T * E; // after the logits' slot; the stage area is idle
+            int32_t *di = reinterpret_cast<int32_t *>(dl + 64);
+            float *dw = dl + 128;
+            for (int j = lane; j < 64; j += 32) dl[j] = 0.0f;
+            __syncwarp();
+            trx_route_token<true>(dl, E, k, S.norm_topk, lane, sp[warp], di, dw);
+        }
+        // ---------------- phase B: every CTA, once all writers are in (acquire), routes and sorts the whole call
+        // itself from the logits in L2 (no CTA publishes for the others), and stages the tokens' inputs
+        if (tid == 0) s_flag = trx_spin(&sync->route_cnt, (uint32_t)writers, false);
         __syncthreads();
         if (!s_flag) {
             if (tid == 0) atomicExch(w.err, 2);
             return;
         }
-        TRX_TRACE(2);
-        if (tid == 0) s_nact = __ldcg(w.n_active);
-        if (tid <= E) s_off[tid] = __ldcg(w.offsets + tid);
-        if (tid < E) s_active[tid] = __ldcg(w.active + tid);
-        for (int j = tid; j < R; j += blockDim.x) {
-            s_xmap[j] = __ldcg(w.xmap + j);
-            s_selw[j] = __ldcg(w.sel_w + j);
-            s_place[j] = __ldcg(w.place + j);
+        TRX_TRACE(1);
+        float *slog = reinterpret_cast<float *>(smem); // T x E logits (the stage buffers are free until the barriers)
+        for (int j = tid; j < T * E; j += blockDim.x) slog[j] = __ldcg(w.logits + j);
+        __syncthreads();
+        const long long c1 = clock64();
+        for (int t = warp; t < T; t += TRX_FU_CWARPS + 1)
+            trx_route_token<true>(slog + t * E, E, k, S.norm_topk, lane, sp[warp], s_selid + t * k, s_selw + t * k);
+        if (w.trace != nullptr && tid == 0) w.trace[(size_t)blockIdx.x * 64 + 7] = (uint64_t)(clock64() - c1);
+        __syncthreads();
+    }
+    TRX_TRACE(60);
+    // Both roads: s_selid / s_selw hold the call's routing. The producer derives the active experts from the ids and
+    // starts streaming at once; the consumers sort the rows by expert, write the optional outputs and stage the
+    // tokens' prepared inputs meanwhile, then meet at a barrier of their own (bar 1, the 8 consumer warps).
+    const bool lprep = T <= TRX_FU_LOCAL_PREP || local;
+    int n_act;
+    if (warp == TRX_FU_CWARPS) {
+        uint32_t m0 = 0, m1 = 0; // the selected experts as a 64-bit set
+        for (int j = lane; j < R; j += 32) {
+            const int e = s_selid[j];
+            if (e < 32) m0 |= 1u << e;
+            else m1 |= 1u << (e - 32);
         }
-        for (int t = 0; t < T; t++) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            m0 |= __shfl_xor_sync(0xffffffffu, m0, o);
+            m1 |= __shfl_xor_sync(0xffffffffu, m1, o);
+        }
+        n_act = __popc(m0) + __popc(m1);
+        const unsigned lt = (1u << lane) - 1u;
+        if (m0 >> lane & 1u) s_pact[__popc(m0 & lt)] = lane;
+        if (m1 >> lane & 1u) s_pact[__popc(m0) + __popc(m1 & lt)] = lane + 32;
+        __syncwarp();
+    } else {
+        const int ctid = tid; // 0..255
+        if (warp == 0) {
+            const bool out = blockIdx.x == 0;
+            const TrxSortOut so{s_off, s_active, &s_nact, s_place, s_xmap, out ? w.out_offsets : nullptr,
+                                out ? w.out_place : nullptr};
+            const long long c0 = clock64();
+            if (T == 1) {
+                // one token: its k ids are distinct and already in increasing order, so expert s_selid[j] holds row j
+                // alone: offsets[e] = the number of selected ids below e, place[j] = j, every row is token 0
+                const int e0 = lane < k ? s_selid[lane] : TRX_MAX_EXPERTS;
+                for (int e = lane; e <= E; e += 32) {
+                    int c = 0;
+                    for (int j = 0; j < k; j++) c += s_selid[j] < e;
+                    s_off[e] = c;
+                    if (so.out_offsets) so.out_offsets[e] = c;
+                }
+                if (lane < k) {
+                    s_active[lane] = e0;
+                    s_place[lane] = lane;
+                    s_xmap[lane] = 0;
+                    if (so.out_place) so.out_place[lane] = lane;
+                }
+                if (lane == 0) s_nact = k;
+            } else {
+                trx_warp_counting_sort(s_selid, R, E, k, so, scnt, lane);
+            }
+            if (w.trace != nullptr && lane == 0) w.trace[(size_t)blockIdx.x * 64 + 63] = (uint64_t)(clock64() - c0);
+            TRX_TRACE(48);
+        } else if (blockIdx.x == 0 && w.out_sel_id) {
+            for (int j = ctid - 32; j < R; j += 32 * (TRX_FU_CWARPS - 1)) {
+                w.out_sel_id[j] = s_selid[j];
+                w.out_sel_w[j] = s_selw[j];
+            }
+        }
+        for (int t = 0; t < (lprep ? 0 : T); t++) {
             uint8_t *dst = s_tok + t * lay.tok_bytes;
             if (GT == TRX_Q4_K) {
-                for (int i = tid; i < H / 4; i += blockDim.x)
+                for (int i = ctid; i < H / 4; i += 32 * TRX_FU_CWARPS)
                     reinterpret_cast<uint4 *>(dst)[i] = __ldcg(reinterpret_cast<const uint4 *>(w.xq + (int64_t)t * H) + i);
                 double *bfd = reinterpret_cast<double *>(dst + (size_t)H * 4);
-                for (int i = tid; i < H / 32; i += blockDim.x) bfd[i] = __ldcg(w.xq_bf + (int64_t)t * (H / 32) + i);
-                for (int i = tid; i < H / 256; i += blockDim.x)
+                for (int i = ctid; i < H / 32; i += 32 * TRX_FU_CWARPS) bfd[i] = __ldcg(w.xq_bf + (int64_t)t * (H / 32) + i);
+                for (int i = ctid; i < H / 256; i += 32 * TRX_FU_CWARPS)
                     bfd[H / 32 + i] = __ldcg(w.xq_sc + (int64_t)t * (H / 256) + i);
             } else {
-                for (int i = tid; i < H / 4; i += blockDim.x)
+                for (int i = ctid; i < H / 4; i += 32 * TRX_FU_CWARPS)
                     reinterpret_cast<float4 *>(dst)[i] =
                         __ldcg(reinterpret_cast<const float4 *>(w.x_lc + (int64_t)t * H) + i);
             }
         }
-        __syncthreads();
+        asm volatile("bar.sync 1, %0;" ::"n"(32 * TRX_FU_CWARPS) : "memory");
+        n_act = s_nact;
+        TRX_TRACE(2);
     }
-    if (tid == 0) { // the stage buffers' scratch use is over: the pipelines' barriers
-        for (int s = 0; s < SG; s++) {
-            trx_mbar_init(&full_g[s], 1);
-            trx_mbar_init(&empty_g[s], TRX_FU_CWARPS);
-        }
-        for (int s = 0; s < SD; s++) {
-            trx_mbar_init(&full_d[s], 1);
-            trx_mbar_init(&empty_d[s], TRX_FU_CWARPS);
-        }
-        trx_fence_barrier_init();
-    }
-    __syncthreads();
-    TRX_TRACE(3);
-    const int n_act = s_nact;
     bool failed = false;
     int issued_g = 0, issued_d = 0; // the producer's counts, for the drain after a failure
 
@@ -372,16 +432,21 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
             gw.init(n_act * F, F, CHG, false);
             dw.init(n_act * H, H, CHD, true);
             auto issue_g = [&](int s) {
-                const int e = s_active[gw.slot], n = gw.n();
+                const int e = s_pact[gw.slot], n = gw.n();
                 uint8_t *dst = gu_buf + s * lay.gu_stage;
                 trx_mbar_expect_tx(&full_g[s], 2u * n * rbg);
                 trx_bulk_g2s(dst, L.gate + e * L.gate_mb + (int64_t)gw.r * rbg, n * rbg, &full_g[s]);
                 trx_bulk_g2s(dst + gu_half, L.up + e * L.up_mb + (int64_t)gw.r * rbg, n * rbg, &full_g[s]);
             };
             auto issue_d = [&](int s) {
-                const int e = s_active[dw.slot], n = dw.n();
-                trx_mbar_expect_tx(&full_d[s], (uint32_t)(n * rbd));
+                const int e = s_pact[dw.slot], n = dw.n();
+                const int dbytes = DT == TRX_Q6_K ? CHD * nsb_d * 2 : 0; // 16-byte multiple, 16-byte aligned
+                trx_mbar_expect_tx(&full_d[s], (uint32_t)(n * rbd + dbytes));
                 trx_bulk_g2s(dn_buf + s * lay.dn_stage, L.down + e * L.down_mb + (int64_t)dw.r * rbd, n * rbd, &full_d[s]);
+                if (DT == TRX_Q6_K)
+                    trx_bulk_g2s(dn_buf + s * lay.dn_stage + CHD * rbd,
+                                 L.down + e * L.down_mb + (int64_t)H * rbd + (int64_t)(dw.r / CHD) * CHD * nsb_d * 2, dbytes,
+                                 &full_d[s]);
             };
             for (; issued_g < SG && gw.more(); issued_g++, gw.next()) issue_g(issued_g);
             for (; issued_d < SD && dw.more(); issued_d++, dw.next()) issue_d(issued_d);
@@ -533,14 +598,14 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
                         if (DT == TRX_Q8_0) {
                             vv = trx_q8l_dot_reg<NSB4>(st, xr, lane & 15);
                         } else {
-                            const uint8_t *dptr = L.down + e * L.down_mb + (int64_t)H * rbd + (int64_t)d * NSB4 * 2;
-                            vv = trx_q6l_dot_reg<NSB4>(st, dptr, xr, lane & 15);
+                            const uint8_t *dptr = dn_buf + s * lay.dn_stage + CHD * rbd + (d % CHD) * NSB4 * 2;
+                            vv = trx_q6l_dot_reg<NSB4, true>(st, dptr, xr, lane & 15);
                         }
                     } else if (DT == TRX_Q8_0) {
                         vv = trx_q8l_dot<true, true>(st, w.h + (int64_t)p * F, nsb_d, lane & 15);
                     } else {
-                        const uint8_t *dptr = L.down + e * L.down_mb + (int64_t)H * rbd + (int64_t)d * nsb_d * 2;
-                        vv = trx_q6l_dot<true, true>(st, dptr, w.h + (int64_t)p * F, nsb_d, lane & 15);
+                        const uint8_t *dptr = dn_buf + s * lay.dn_stage + CHD * rbd + (d % CHD) * nsb_d * 2;
+                        vv = trx_q6l_dot<true, true, true>(st, dptr, w.h + (int64_t)p * F, nsb_d, lane & 15);
                     }
                     if (row < n && (lane & 15) == 0) w.h3[(int64_t)p * H + d] = vv;
                 }
@@ -596,6 +661,7 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
         __threadfence();
         if (atomicAdd(&sync->finish, 1u) == gridDim.x - 1) { // every CTA is past its waits
             for (int i = 0; i < E; i++) sync->gu_done[i] = 0u;
+            sync->route_cnt = 0u;
             sync->finish = 0u;
             __threadfence();
         }

@@ -375,8 +375,8 @@ __device__ __forceinline__ float trx_q8l_dot(const uint8_t *__restrict__ row, co
     return trx_lane_tree16(acc);
 }
 
-// Q6L lane-contract dot (n = 256 * nsb); dptr: this row's nsb f16 d values
-template <bool SM = false, bool CG = false>
+// Q6L lane-contract dot (n = 256 * nsb); dptr: this row's nsb f16 d values (in shared memory when DSM)
+template <bool SM = false, bool CG = false, bool DSM = false>
 __device__ __forceinline__ float trx_q6l_dot(const uint8_t *__restrict__ row, const uint8_t *__restrict__ dptr,
                                              const float *__restrict__ xlc, int nsb, int l) {
     float acc = 0.0f;
@@ -385,7 +385,8 @@ __device__ __forceinline__ float trx_q6l_dot(const uint8_t *__restrict__ row, co
         trx_lc_block<CG>(xlc, s, l, xv);
         acc = trx_q6l_block(acc, trx_ld<SM, uint2>(row + 128 * s + 8 * l), trx_ld<SM, uint32_t>(row + 128 * nsb + 64 * s + 4 * l),
                             trx_ld<SM, uint4>(row + 192 * nsb + 16 * s),
-                            trx_half(__ldg(reinterpret_cast<const uint16_t *>(dptr) + s)), xv);
+                            trx_half(DSM ? reinterpret_cast<const uint16_t *>(dptr)[s]
+                                         : __ldg(reinterpret_cast<const uint16_t *>(dptr) + s)), xv);
     }
     return trx_lane_tree16(acc);
 }
@@ -420,7 +421,7 @@ __device__ __forceinline__ float trx_q8l_dot_reg(const uint8_t *__restrict__ row
     return trx_lane_tree16(acc);
 }
 
-template <int NSB>
+template <int NSB, bool DSM = false>
 __device__ __forceinline__ float trx_q6l_dot_reg(const uint8_t *__restrict__ row, const uint8_t *__restrict__ dptr,
                                                  const float (&xr)[NSB * 16], int l) {
     float acc = 0.0f;
@@ -432,7 +433,8 @@ __device__ __forceinline__ float trx_q6l_dot_reg(const uint8_t *__restrict__ row
         acc = trx_q6l_block(acc, *reinterpret_cast<const uint2 *>(row + 128 * s + 8 * l),
                             *reinterpret_cast<const uint32_t *>(row + 128 * NSB + 64 * s + 4 * l),
                             *reinterpret_cast<const uint4 *>(row + 192 * NSB + 16 * s),
-                            trx_half(__ldg(reinterpret_cast<const uint16_t *>(dptr) + s)), xv);
+                            trx_half(DSM ? reinterpret_cast<const uint16_t *>(dptr)[s]
+                                         : __ldg(reinterpret_cast<const uint16_t *>(dptr) + s)), xv);
     }
     return trx_lane_tree16(acc);
 }

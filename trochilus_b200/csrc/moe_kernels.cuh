@@ -48,6 +48,7 @@ struct TrxLayer {
 
 struct TrxShape {
     int E, k, H, F, norm_topk;
+    int local_route; // the fused kernel: every CTA routes a short call itself (see fused_layer.cuh)
 };
 
 struct TrxWork {
@@ -114,24 +115,19 @@ __device__ void trx_route_token(const float *__restrict__ logits, int E, int k, 
     const bool any_nan = __any_sync(0xffffffffu, (ok0 && p0 != p0) || (ok1 && p1 != p1));
     int r0 = lane, r1 = lane + 32; // selection rank of elements lane and lane + 32
     if (!any_nan) {
-        // k rounds of argmax: probabilities are in [0, 1], so their bits order them as unsigned integers;
-        // key = bits + 1 for an untaken element, 0 for a taken (or absent) one
-        r0 = r1 = 1 << 20;
-        bool t0 = !ok0, t1 = !ok1;
-        for (int s = 0; s < k; s++) {
-            const uint32_t k0 = t0 ? 0u : __float_as_uint(p0) + 1u, k1 = t1 ? 0u : __float_as_uint(p1) + 1u;
-            const uint32_t mx = __reduce_max_sync(0xffffffffu, k0 > k1 ? k0 : k1);
-            const unsigned b0 = __ballot_sync(0xffffffffu, k0 == mx);
-            const int best = b0 ? __ffs(b0) - 1 : 32 + __ffs(__ballot_sync(0xffffffffu, k1 == mx)) - 1;
-            if (best == lane) {
-                t0 = true;
-                r0 = s;
-            }
-            if (best == lane + 32) {
-                t1 = true;
-                r1 = s;
-            }
+        // the rank of each element in the order the k rounds of argmax take them (larger probability first, ties
+        // to the lower id): probabilities are in [0, 1], so their bits order them as unsigned integers; key = bits
+        // + 1 for a present element, 0 for an absent one (E < 64), which no present element follows
+        const uint32_t q0 = ok0 ? __float_as_uint(p0) + 1u : 0u, q1 = ok1 ? __float_as_uint(p1) + 1u : 0u;
+        int c0 = 0, c1 = 0;
+#pragma unroll 4
+        for (int j = 0; j < 32; j++) {
+            const uint32_t a = __shfl_sync(0xffffffffu, q0, j), b = __shfl_sync(0xffffffffu, q1, j); // ids j, j + 32
+            c0 += (a > q0 || (a == q0 && j < lane)) + (b > q0);
+            c1 += (a >= q1) + (b > q1 || (b == q1 && j < lane));
         }
+        r0 = c0;
+        r1 = c1;
     }
     const bool s0 = ok0 && r0 < k, s1 = ok1 && r1 < k;
     float w0 = p0, w1 = p1;
@@ -219,17 +215,18 @@ struct TrxSortOut {
     int64_t *out_offsets, *out_place;
 };
 
-// The same by one warp for R <= 32 rows (a decode token's k rows); scnt: 64 ints of shared memory
+// The same by one warp, any R (32 rows a pass, stable by match_any ranks); scnt: 64 ints of shared memory
 __device__ void trx_warp_counting_sort(const int32_t *__restrict__ sel_id, int R, int E, int k, TrxSortOut w, int *scnt,
                                        int lane) {
-    const int e = lane < R ? sel_id[lane] : -1;
     scnt[lane] = 0;
     scnt[lane + 32] = 0;
     __syncwarp();
-    const unsigned peers = __match_any_sync(0xffffffffu, e);
-    const int rank = __popc(peers & ((1u << lane) - 1u));
-    if (e >= 0 && rank == 0) scnt[e] = __popc(peers);
-    __syncwarp();
+    for (int b = 0; b < R; b += 32) {
+        const int e = b + lane < R ? sel_id[b + lane] : -1;
+        const unsigned peers = __match_any_sync(0xffffffffu, e);
+        if (e >= 0 && lane == __ffs(peers) - 1) scnt[e] += __popc(peers);
+        __syncwarp();
+    }
     const int c0 = lane < E ? scnt[lane] : 0, c1 = lane + 32 < E ? scnt[lane + 32] : 0;
     int i0 = c0, i1 = c1; // inclusive scans
 #pragma unroll
@@ -259,12 +256,22 @@ __device__ void trx_warp_counting_sort(const int32_t *__restrict__ sel_id, int R
     if (c0 > 0) w.active[__popc(a0 & lt)] = lane;
     if (c1 > 0) w.active[__popc(a0) + __popc(a1 & lt)] = lane + 32;
     if (lane == 0) *w.n_active = __popc(a0) + __popc(a1);
-    const int base0 = __shfl_sync(0xffffffffu, off0, e & 31), base1 = __shfl_sync(0xffffffffu, off1, e & 31);
-    if (e >= 0) {
-        const int pos = (e < 32 ? base0 : base1) + rank;
-        w.place[lane] = pos;
-        w.xmap[pos] = lane / k;
-        if (w.out_place) w.out_place[lane] = pos;
+    __syncwarp();
+    scnt[lane] = off0; // the running start of each expert
+    scnt[lane + 32] = off1;
+    __syncwarp();
+    for (int b = 0; b < R; b += 32) {
+        const int j = b + lane, e = j < R ? sel_id[j] : -1;
+        const unsigned peers = __match_any_sync(0xffffffffu, e);
+        if (e >= 0) {
+            const int pos = scnt[e] + __popc(peers & lt);
+            w.place[j] = pos;
+            w.xmap[pos] = j / k;
+            if (w.out_place) w.out_place[j] = pos;
+        }
+        __syncwarp();
+        if (e >= 0 && lane == __ffs(peers) - 1) scnt[e] += __popc(peers);
+        __syncwarp();
     }
 }
 
@@ -317,7 +324,7 @@ __device__ void trx_router_block(const TrxLayer &L, const TrxShape &S, const flo
     const int nch = H / 256;
     for (int g0 = g_begin; g0 < g_end; g0 += TRX_TOK_STAGE) {
         const int ng = min(TRX_TOK_STAGE, g_end - g0);
-        __syncthreads();
+        if (g0 != g_begin) __syncthreads(); // the first group's loads go out with the router row's
         for (int i = tid; i < ng * H / 4; i += blockDim.x) { // inputs of the group, LC order
             const int tk = (4 * i) / H, kk = (4 * i) % H;
             const float4 v = *reinterpret_cast<const float4 *>(normed + (int64_t)(g0 + tk) * H + kk);

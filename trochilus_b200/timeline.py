@@ -25,11 +25,13 @@ def summarize(tr: np.ndarray) -> dict:
         return {"min": round(float(u.min()), 2), "median": round(float(np.median(u)), 2), "max": round(float(u.max()), 2)}
 
     names = (("start", 0), ("router_prep_work_done", 62), ("routing_begin", 59), ("route_done", 60), ("sort_done", 61),
-             ("phase_a_done", 1), ("routing_seen", 2), ("inputs_staged", 3), ("gate_up_done_w0", 4),
+             ("phase_a_done", 1), ("sorted_w0", 48), ("routing_seen", 2), ("inputs_staged", 3), ("gate_up_done_w0", 4),
              ("down_first_ready_w0", 5), ("down_done_w0", 6), ("end", 52))
     out = {"ctas": int(tr.shape[0]), **{n: stat(tr[:, slot]) for n, slot in names}}
     med = lambda slot: (stat(tr[:, slot]) or {}).get("median")
     # per chunk of consumer warp 0: (data ready, rows multiplied, counted and released)
+    out["cycles_route_token_w0"] = int(np.median(tr[:, 7]))
+    out["cycles_sort_w0"] = int(np.median(tr[:, 63]))
     out["w0_gate_up_chunks"] = [(med(8 + j), med(40 + j), med(16 + j)) for j in range(8)]
     out["w0_down_chunks"] = [(med(24 + j), med(53 + j) if j < 6 else None, med(32 + j)) for j in range(8)]
     return out
