@@ -48,6 +48,7 @@ def _check(got, want, tag):
     for key in ("ffn_out", "x"):
         assert np.all(np.isfinite(got[key])), (tag, key)
         err = _rel_err(got[key], want[key])
+        print(f"{tag} {key}: max normwise relative error {err.max():.3e} (bound {REL:.0e})")
         assert err.max() <= REL, (tag, key, float(err.max()), int(err.argmax()))
 
 

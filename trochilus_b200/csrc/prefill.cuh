@@ -15,9 +15,10 @@
 //  down      tile = 128 grouped rows x 256 down rows; epilogue stores h3 (fp32).
 //  combine   the exact mix: out = +0, out += w_slot h3[place] in increasing expert id, x += out (olmoe.c:1432-1446).
 //
-// A GEMM CTA: warps 0-3 dequantise the tile's Q8L weight rows (d q: exact in fp32) into hi/lo tiles in shared
-// memory, then run the epilogue (warp q reads accumulator lanes 32 q .. 32 q + 31); warp 4 brings the A planes
-// with 2-D TMA (128-byte swizzle, no multicast); warp 5 owns the tensor memory and issues the MMAs (one thread).
+// A GEMM CTA: warps 0-7 dequantise the tile's Q8L weight rows (d q: exact in fp32; a row per thread) into hi/lo
+// tiles in shared memory, then run the epilogue (warp w reads accumulator lanes 32 (w % 4) .. + 31, half the
+// columns each); warp 8 brings the A planes with 2-D TMA (128-byte swizzle, no multicast); warp 9 owns the tensor
+// memory and issues the MMAs (one thread).
 // Two stages of BK = 32 columns; every wait bounded (TRX_WAIT_NS), a failure sets the error flag.
 //
 // Accumulation: the tensor core's fp32 accumulator does not round each addition to nearest, and over the ~800
@@ -35,7 +36,7 @@
 #define TRX_PF_BN 256
 #define TRX_PF_BK 32
 #define TRX_PF_STAGES 2
-#define TRX_PF_THREADS 192
+#define TRX_PF_THREADS 320 // warps 0-7 converters + epilogue, warp 8 TMA, warp 9 MMA
 #define TRX_PF_A_BYTES (TRX_PF_BM * TRX_PF_BK * 4)                 // one plane of the A tile: 16 KB
 #define TRX_PF_B_BYTES (TRX_PF_BN * TRX_PF_BK * 4)                 // one plane of the B tile: 32 KB
 #define TRX_PF_STAGE_BYTES (2 * TRX_PF_A_BYTES + 2 * TRX_PF_B_BYTES) // 96 KB
@@ -93,6 +94,14 @@ __device__ __forceinline__ void trx_tmem_ld32_nw(uint32_t taddr, uint32_t (&r)[3
                  : "r"(taddr)
                  : "memory");
 }
+__device__ __forceinline__ void trx_tmem_ld16_nw(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
+                 "%14, %15}, [%16];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+                   "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+                 : "r"(taddr)
+                 : "memory");
+}
 __device__ __forceinline__ void trx_tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void trx_tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
@@ -120,6 +129,10 @@ __device__ __forceinline__ void trx_tmem_st32(uint32_t taddr, const float (&v)[3
                  "f"(v[16]), "f"(v[17]), "f"(v[18]), "f"(v[19]), "f"(v[20]), "f"(v[21]), "f"(v[22]), "f"(v[23]),
                  "f"(v[24]), "f"(v[25]), "f"(v[26]), "f"(v[27]), "f"(v[28]), "f"(v[29]), "f"(v[30]), "f"(v[31])
                  : "memory");
+}
+
+__device__ __forceinline__ void trx_tmem_st32(uint32_t taddr, const uint32_t (&v)[32]) {
+    trx_tmem_st32(taddr, reinterpret_cast<const float(&)[32]>(v));
 }
 
 // 2-D tiled TMA load (no multicast): box at element (x, y) of the tensor map into shared memory
@@ -230,14 +243,14 @@ __global__ void __launch_bounds__(TRX_PF_THREADS, 1)
     if (tid == 0) {
         for (int s = 0; s < TRX_PF_STAGES; s++) {
             trx_mbar_init(&full_a[s], 1);
-            trx_mbar_init(&full_b[s], 4);
+            trx_mbar_init(&full_b[s], 8);
             trx_mbar_init(&empty[s], 1);
         }
         trx_mbar_init(cfull, 1);
-        trx_mbar_init(cempty, 4);
+        trx_mbar_init(cempty, 8);
         trx_fence_barrier_init();
     }
-    if (warp == 5) {
+    if (warp == 9) {
         trx_tmem_alloc(&s_tmem, 2 * TRX_PF_BN);
         trx_tmem_relinquish();
     }
@@ -246,7 +259,7 @@ __global__ void __launch_bounds__(TRX_PF_THREADS, 1)
     trx_tc_fence_after();
     const uint32_t tmem = s_tmem;
 
-    if (warp == 4) {
+    if (warp == 8) {
         // ---- TMA: the A planes of every k-step
         if (lane == 0) {
             int issued = 0;
@@ -264,7 +277,7 @@ __global__ void __launch_bounds__(TRX_PF_THREADS, 1)
             for (int q = max(0, issued - TRX_PF_STAGES); q < issued; q++)
                 trx_mbar_wait(&full_a[q % TRX_PF_STAGES], (q / TRX_PF_STAGES) & 1, TRX_WAIT_NS);
         }
-    } else if (warp == 5) {
+    } else if (warp == 9) {
         // ---- MMA issue: 4 k-slices of 8 x 3 split products per k-step, chunk by chunk into columns 0..255
         if (lane == 0) {
             const uint32_t sa = trx_smem(smem);
@@ -296,72 +309,63 @@ __global__ void __launch_bounds__(TRX_PF_THREADS, 1)
             if (*(volatile int *)&s_fail) trx_umma_commit(cfull); // wakes the converters (they see the failure)
         }
     } else {
-        // ---- converters: this thread's two B rows (gate/up: gate and up row of output 128 n + tid; down: rows
-        // 256 n + tid and + 128), dequantised k-step by k-step into the swizzled hi/lo tiles
+        // ---- converters: this thread's B row r = tid (gate/up: r < 128 the gate row of output 128 n + r, r >= 128
+        // the up row of output 128 n + r - 128; down: row 256 n + r), dequantised k-step by k-step into the swizzled
+        // hi/lo tiles
         const int64_t rb = (int64_t)(K / 256) * 272;
-        const uint8_t *r0p, *r1p;
-        if (GATEUP) {
-            const int j = trx_q8l_col(128 * n + tid);
-            r0p = a.wa + e * a.wa_mb + j * rb;
-            r1p = a.wb + e * a.wb_mb + j * rb;
-        } else {
-            r0p = a.wa + e * a.wa_mb + (int64_t)(256 * n + tid) * rb;
-            r1p = r0p + 128 * rb;
-        }
-        float d0[8], d1[8];
-        uint4 q0a, q0b, q1a, q1b; // this k-step's 32 quants of each row
+        const int r = tid;
+        const uint8_t *rp = GATEUP ? (r < 128 ? a.wa + e * a.wa_mb : a.wb + e * a.wb_mb) + trx_q8l_col(128 * n + (r & 127)) * rb
+                                   : a.wa + e * a.wa_mb + (int64_t)(256 * n + r) * rb;
+        float d[8];
+        uint4 qa, qb; // this k-step's 32 quants
         auto load_q = [&](int ks) {
             const int64_t o = (int64_t)(ks >> 3) * 272 + 16 + 32 * (ks & 7);
-            q0a = __ldg(reinterpret_cast<const uint4 *>(r0p + o));
-            q0b = __ldg(reinterpret_cast<const uint4 *>(r0p + o + 16));
-            q1a = __ldg(reinterpret_cast<const uint4 *>(r1p + o));
-            q1b = __ldg(reinterpret_cast<const uint4 *>(r1p + o + 16));
+            qa = __ldg(reinterpret_cast<const uint4 *>(rp + o));
+            qb = __ldg(reinterpret_cast<const uint4 *>(rp + o + 16));
         };
         auto load_d = [&](int chunk) {
-            const uint4 u0 = __ldg(reinterpret_cast<const uint4 *>(r0p + (int64_t)chunk * 272));
-            const uint4 u1 = __ldg(reinterpret_cast<const uint4 *>(r1p + (int64_t)chunk * 272));
-            const uint32_t w0[4] = {u0.x, u0.y, u0.z, u0.w}, w1[4] = {u1.x, u1.y, u1.z, u1.w};
+            const uint4 u = __ldg(reinterpret_cast<const uint4 *>(rp + (int64_t)chunk * 272));
+            const uint32_t wd[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
-            for (int b = 0; b < 8; b++) {
-                d0[b] = trx_half((uint16_t)(w0[b >> 1] >> (16 * (b & 1))));
-                d1[b] = trx_half((uint16_t)(w1[b >> 1] >> (16 * (b & 1))));
-            }
+            for (int b = 0; b < 8; b++) d[b] = trx_half((uint16_t)(wd[b >> 1] >> (16 * (b & 1))));
         };
-        // one row's 32 weights into tile row r: position b of the k-step has scale (b % 16) / 2
-        auto put_row = [&](int s, int r, uint4 qa, uint4 qb, const float (&d)[8]) {
-            const uint32_t qw[8] = {qa.x ^ 0x80808080u, qa.y ^ 0x80808080u, qa.z ^ 0x80808080u, qa.w ^ 0x80808080u,
-                                    qb.x ^ 0x80808080u, qb.y ^ 0x80808080u, qb.z ^ 0x80808080u, qb.w ^ 0x80808080u};
-            uint8_t *th = b_hi(s) + (r >> 3) * 1024 + (r & 7) * 128, *tl = b_lo(s) + (r >> 3) * 1024 + (r & 7) * 128;
+        // the row's 32 weights into tile row r: position b of the k-step has scale (b % 16) / 2
+        auto put_row = [&](int s, uint4 ca, uint4 cb) {
+            const uint32_t qw[8] = {ca.x ^ 0x80808080u, ca.y ^ 0x80808080u, ca.z ^ 0x80808080u, ca.w ^ 0x80808080u,
+                                    cb.x ^ 0x80808080u, cb.y ^ 0x80808080u, cb.z ^ 0x80808080u, cb.w ^ 0x80808080u};
+            uint8_t *th = b_hi(s) + (r >> 3) * 1024 + (r & 7) * 128, *tlo = b_lo(s) + (r >> 3) * 1024 + (r & 7) * 128;
 #pragma unroll
             for (int c = 0; c < 8; c++) { // 16-byte chunk c holds positions 4 c .. 4 c + 3
                 float hv[4], lv[4];
 #pragma unroll
                 for (int i = 0; i < 4; i++) {
                     const int b = 4 * c + i;
-                    const float w = __fmul_rn(d[(b & 15) >> 1], trx_s8_to_f32(qw[c], i)); // exact: 19 bits at most
-                    trx_split(w, hv[i], lv[i]);
+                    const float wv = __fmul_rn(d[(b & 15) >> 1], trx_s8_to_f32(qw[c], i)); // exact: 19 bits at most
+                    trx_split(wv, hv[i], lv[i]);
                 }
                 const int sw = (c ^ (r & 7)) << 4;
                 *reinterpret_cast<float4 *>(th + sw) = make_float4(hv[0], hv[1], hv[2], hv[3]);
-                *reinterpret_cast<float4 *>(tl + sw) = make_float4(lv[0], lv[1], lv[2], lv[3]);
+                *reinterpret_cast<float4 *>(tlo + sw) = make_float4(lv[0], lv[1], lv[2], lv[3]);
             }
         };
-        // adds finished chunk c (columns 0..255) into the running sum (columns 256..511) of this warp's 32 rows
-        const uint32_t tl = tmem + ((uint32_t)(32 * warp) << 16);
+        // warp w's share of the accumulator: lanes 32 (w % 4) .., columns (w / 4) 128 .. + 127
+        const uint32_t tl = tmem + ((uint32_t)(32 * (warp & 3)) << 16);
+        const int cb = (warp >> 2) * 128;
+        // adds finished chunk c (columns 0..255) into the running sum (columns 256..511)
         auto drain = [&](int c) -> bool {
             if (!__all_sync(0xffffffffu, trx_mbar_wait(cfull, c & 1, TRX_WAIT_NS)) || *(volatile int *)&s_fail) return false;
             trx_tc_fence_after();
 #pragma unroll 1
-            for (int c0 = 0; c0 < TRX_PF_BN; c0 += 32) {
-                uint32_t v[32], r[32];
+            for (int c0 = cb; c0 < cb + 128; c0 += 32) {
+                uint32_t v[32], rr[32];
                 trx_tmem_ld32_nw(tl + c0, v);
-                if (c > 0) trx_tmem_ld32_nw(tl + TRX_PF_BN + c0, r);
+                if (c > 0) trx_tmem_ld32_nw(tl + TRX_PF_BN + c0, rr);
                 trx_tmem_wait_ld();
-                float o[32];
+                if (c > 0) {
 #pragma unroll
-                for (int i = 0; i < 32; i++)
-                    o[i] = c > 0 ? __fadd_rn(__uint_as_float(r[i]), __uint_as_float(v[i])) : __uint_as_float(v[i]);
-                trx_tmem_st32(tl + TRX_PF_BN + c0, o); // waited for once, below
+                    for (int i = 0; i < 32; i++) v[i] = __float_as_uint(__fadd_rn(__uint_as_float(rr[i]), __uint_as_float(v[i])));
+                }
+                trx_tmem_st32(tl + TRX_PF_BN + c0, v); // waited for once, below
             }
             trx_tmem_wait_st();
             trx_tc_fence_before();
@@ -374,7 +378,7 @@ __global__ void __launch_bounds__(TRX_PF_THREADS, 1)
         load_q(0);
         for (int ks = 0; ks < nk; ks++) {
             const int s = ks % TRX_PF_STAGES;
-            const uint4 c0a = q0a, c0b = q0b, c1a = q1a, c1b = q1b;
+            const uint4 ca = qa, cbq = qb;
             if (ks + 1 < nk) load_q(ks + 1); // the next k-step's quants in flight while this one is written
             if (ks >= TRX_PF_STAGES &&
                 !__all_sync(0xffffffffu, trx_mbar_wait(&empty[s], ((ks / TRX_PF_STAGES) - 1) & 1, TRX_WAIT_NS))) {
@@ -382,8 +386,7 @@ __global__ void __launch_bounds__(TRX_PF_THREADS, 1)
                 break;
             }
             if ((ks & 7) == 0 && ks > 0) load_d(ks >> 3);
-            put_row(s, tid, c0a, c0b, d0);
-            put_row(s, tid + 128, c1a, c1b, d1);
+            put_row(s, ca, cbq);
             trx_fence_proxy_async(); // these generic-proxy writes before the tensor core's reads
             __syncwarp();
             if (lane == 0) trx_mbar_arrive(&full_b[s]);
@@ -395,7 +398,7 @@ __global__ void __launch_bounds__(TRX_PF_THREADS, 1)
             }
         }
         if (failed) atomicExch(&s_fail, 1);
-        // ---- epilogue: the last chunk plus the running sum, this warp's 32 rows
+        // ---- epilogue: the last chunk plus the running sum, this warp's 32 rows and share of the columns
         const int last = (nk - 1) / TRX_PF_CK;
         const bool ok = !failed && __all_sync(0xffffffffu, trx_mbar_wait(cfull, last & 1, TRX_WAIT_NS)) &&
                         !*(volatile int *)&s_fail;
@@ -403,21 +406,21 @@ __global__ void __launch_bounds__(TRX_PF_THREADS, 1)
         if (!ok) {
             atomicExch(&s_fail, 1);
         } else {
-            const int m = 32 * warp + lane;
+            const int m = 32 * (warp & 3) + lane;
             const int64_t p = row0 + m;
             const bool valid = m < rows;
             auto col32 = [&](int c0, float (&v)[32]) { // accumulator column block c0: chunk + sum
-                trx_tmem_ld32(tl + c0, v);
-                if (last > 0) {
-                    float r[32];
-                    trx_tmem_ld32(tl + TRX_PF_BN + c0, r);
+                uint32_t u0[32], u1[32];
+                trx_tmem_ld32_nw(tl + c0, u0);
+                if (last > 0) trx_tmem_ld32_nw(tl + TRX_PF_BN + c0, u1);
+                trx_tmem_wait_ld();
 #pragma unroll
-                    for (int i = 0; i < 32; i++) v[i] = __fadd_rn(r[i], v[i]);
-                }
+                for (int i = 0; i < 32; i++)
+                    v[i] = last > 0 ? __fadd_rn(__uint_as_float(u1[i]), __uint_as_float(u0[i])) : __uint_as_float(u0[i]);
             };
-            if (GATEUP) {
+            if (GATEUP) { // h columns (w / 4) 64 .. + 63: gate at c, up at 128 + c
 #pragma unroll 1
-                for (int c0 = 0; c0 < 128; c0 += 32) {
+                for (int c0 = (warp >> 2) * 64; c0 < (warp >> 2) * 64 + 64; c0 += 32) {
                     float g[32], u[32];
                     col32(c0, g);
                     col32(128 + c0, u);
@@ -435,7 +438,7 @@ __global__ void __launch_bounds__(TRX_PF_THREADS, 1)
                 }
             } else {
 #pragma unroll 1
-                for (int c0 = 0; c0 < TRX_PF_BN; c0 += 32) {
+                for (int c0 = cb; c0 < cb + 128; c0 += 32) {
                     float v[32];
                     col32(c0, v);
                     if (valid) {
@@ -450,7 +453,7 @@ __global__ void __launch_bounds__(TRX_PF_THREADS, 1)
     }
     trx_tc_fence_before();
     __syncthreads();
-    if (warp == 5) {
+    if (warp == 9) {
         trx_tc_fence_after();
         trx_tmem_dealloc(tmem, 2 * TRX_PF_BN);
     }
