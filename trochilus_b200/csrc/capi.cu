@@ -287,10 +287,10 @@ static bool fused_stages(const tr_gpu_moe *m, int T, int *sg, int *sd) {
     int g = (int)std::min<int64_t>(TRX_FU_MAXST, std::max<int64_t>(2, (rows_g + TRX_GU_CHUNK - 1) / TRX_GU_CHUNK + 1));
     int d = (int)std::min<int64_t>(TRX_FU_MAXST, std::max<int64_t>(2, (rows_d + TRX_DN_CHUNK - 1) / TRX_DN_CHUNK + 1));
     auto fits = [&](int a, int b) {
-        return trx_fused_layout(c.gate_type, c.down_type, H, F, T, k, a, b).total <= m->smem_fused;
+        return trx_fused_layout(c.gate_type, c.down_type, H, F, T, k, a, b, (int)c.n_expert, m->grid_fused).total <= m->smem_fused;
     };
     while (!fits(g, d)) {
-        const TrxFusedSmem l = trx_fused_layout(c.gate_type, c.down_type, H, F, T, k, g, d);
+        const TrxFusedSmem l = trx_fused_layout(c.gate_type, c.down_type, H, F, T, k, g, d, (int)c.n_expert, m->grid_fused);
         if (g > 2 && (g * l.gu_stage >= d * l.dn_stage || d <= 2)) g--;
         else if (d > 2) d--;
         else return false;
@@ -773,7 +773,7 @@ static int launch_layer(tr_gpu_moe *m, int64_t layer, const float *d_normed, int
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3((unsigned)m->grid_fused);
         cfg.blockDim = dim3(TRX_FU_THREADS);
-        cfg.dynamicSmemBytes = trx_fused_layout(c.gate_type, c.down_type, S.H, S.F, T, S.k, sg, sd).total;
+        cfg.dynamicSmemBytes = trx_fused_layout(c.gate_type, c.down_type, S.H, S.F, T, S.k, sg, sd, E, m->grid_fused).total;
         cfg.stream = st;
         cudaLaunchAttribute attr[1];
         attr[0].id = cudaLaunchAttributeCooperative;

@@ -112,13 +112,22 @@ struct TrxWalk {
 // the call's routing (xmap, sel_w, place, sel_id: R = T k entries each), then the tokens' prepared input rows
 // (Q4_K: planes, sums, scales; Q8_0: the LC-ordered row), each region 128-byte aligned.
 struct TrxFusedSmem {
-    size_t gu_stage, dn_stage, bars, meta, tok, tok_bytes, total;
+    size_t gu_stage, dn_stage, bars, meta, seg, tok, tok_bytes, total;
 };
+
+#define TRX_FU_SEG_MAX 4 // tokens up to which a CTA keeps its h values in shared memory and publishes once an expert
+
+// the most gate/up rows one CTA of `grid` takes (whole chunks)
+__host__ __device__ inline int trx_fu_rows_g(int E, int k, int T, int F, int grid) {
+    const int act = E < T * k ? E : T * k, units = act * F / TRX_GU_CHUNK;
+    return (units + grid - 1) / grid * TRX_GU_CHUNK;
+}
+
 
 __host__ __device__ inline size_t trx_align128(size_t v) { return (v + 127) / 128 * 128; }
 
 __host__ __device__ inline TrxFusedSmem trx_fused_layout(int gate_type, int down_type, int H, int F, int T, int k, int sg,
-                                                         int sd) {
+                                                         int sd, int E, int grid) {
     const int rbg = gate_type == TRX_Q4_K ? H / 256 * 144 : H / 32 * 34;
     const int rbd = down_type == TRX_Q4_K ? F / 256 * 144 : down_type == TRX_Q6_K ? F / 256 * 208 : F / 32 * 34;
     TrxFusedSmem l;
@@ -130,7 +139,10 @@ __host__ __device__ inline TrxFusedSmem trx_fused_layout(int gate_type, int down
     if (router > stages) stages = router;
     l.bars = trx_align128(stages);
     l.meta = trx_align128(l.bars + 8 * 4 * TRX_FU_MAXST);
-    l.tok = trx_align128(l.meta + (size_t)T * k * 16);
+    l.seg = trx_align128(l.meta + (size_t)T * k * 16);
+    const size_t seg_bytes =
+        T <= TRX_FU_SEG_MAX ? ((size_t)trx_fu_rows_g(E, k, T, F, grid) + (size_t)sd * TRX_DN_CHUNK) * T * 4 : 0;
+    l.tok = trx_align128(l.seg + seg_bytes);
     l.tok_bytes = gate_type == TRX_Q4_K ? trx_align128((size_t)H * 4 + (size_t)(H / 32 + H / 256) * 8) : (size_t)H * 4;
     l.total = l.tok + (size_t)T * l.tok_bytes;
     return l;
@@ -158,7 +170,7 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
     TRX_TRACE(0);
     const int rbg = GT == TRX_Q4_K ? H / 256 * 144 : H / 32 * 34;
     const int rbd = DT == TRX_Q4_K ? nsb_d * 144 : DT == TRX_Q6_K ? nsb_d * 208 : F / 32 * 34;
-    const TrxFusedSmem lay = trx_fused_layout(GT, DT, H, F, T, k, SG, SD);
+    const TrxFusedSmem lay = trx_fused_layout(GT, DT, H, F, T, k, SG, SD, E, gridDim.x);
     const int gu_half = CHG * rbg;
     uint8_t *gu_buf = smem, *dn_buf = smem + SG * lay.gu_stage;
     uint64_t *full_g = reinterpret_cast<uint64_t *>(smem + lay.bars), *empty_g = full_g + TRX_FU_MAXST;
@@ -348,7 +360,7 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
     TRX_TRACE(60);
     // Both roads: s_selid / s_selw hold the call's routing. The producer derives the active experts from the ids and
     // starts streaming at once; the consumers sort the rows by expert, write the optional outputs and stage the
-    // tokens' prepared inputs meanwhile, then meet at a barrier of their own (bar 1, the 8 consumer warps).
+    // tokens' prepared inputs meanwhile; all meet at bar 1 once the producer's first copies are out.
     const bool lprep = T <= TRX_FU_LOCAL_PREP || local;
     int n_act;
     if (warp == TRX_FU_CWARPS) {
@@ -418,55 +430,150 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
                         __ldcg(reinterpret_cast<const float4 *>(w.x_lc + (int64_t)t * H) + i);
             }
         }
-        asm volatile("bar.sync 1, %0;" ::"n"(32 * TRX_FU_CWARPS) : "memory");
+        asm volatile("bar.sync 1, %0;" ::"n"(32 * (TRX_FU_CWARPS + 1)) : "memory"); // with the producer
         n_act = s_nact;
         TRX_TRACE(2);
     }
     bool failed = false;
     int issued_g = 0, issued_d = 0; // the producer's counts, for the drain after a failure
+    // Short calls (seg): the consumers leave h and h3 in shared memory and release the stage; the producer warp,
+    // idle while they multiply, publishes: h once per expert segment of this CTA, h3 once per chunk (each write-out
+    // followed by one device-scope fence and count), and mixes a 16-row block when its count completes. Longer
+    // calls: the consumers publish themselves, chunk by chunk.
+    const bool seg = T <= TRX_FU_SEG_MAX;
+    float *sh = reinterpret_cast<float *>(smem + lay.seg);               // [row of the CTA's gate/up range][token]
+    float *sh3 = sh + (size_t)trx_fu_rows_g(E, k, T, F, gridDim.x) * T; // [stage][row of the chunk][token]
+    // the mix of a completed 16-row block (one warp): every token's k outputs in increasing expert id, then the residual
+    auto combine = [&](int blk) {
+        __threadfence();
+        for (int i = lane; i < T * CHD; i += 32) {
+            const int t = i / CHD, dd = blk * CHD + i % CHD;
+            float out = 0.0f;
+            for (int sl = 0; sl < k; sl++) {
+                const int jj = t * k + sl;
+                out = __fadd_rn(out, __fmul_rn(s_selw[jj], __ldcg(w.h3 + (int64_t)s_place[jj] * H + dd)));
+            }
+            if (ffn_out) ffn_out[(int64_t)t * H + dd] = out;
+            x_io[(int64_t)t * H + dd] = __fadd_rn(x_io[(int64_t)t * H + dd], out);
+        }
+        if (lane == 0) w.comb_cnt[blk] = 0u;
+    };
 
     if (warp == TRX_FU_CWARPS) {
-        // ---------------- the producer: every chunk of this CTA, in consumption order
-        if (lane == 0) {
-            TrxWalk gw, dw;
-            gw.init(n_act * F, F, CHG, false);
-            dw.init(n_act * H, H, CHD, true);
-            auto issue_g = [&](int s) {
+        // ---------------- the producer: every chunk of this CTA, in consumption order (the copies by lane 0; the
+        // publication by the whole warp)
+        TrxWalk gw, dw; // the next chunk to copy
+        gw.init(n_act * F, F, CHG, false);
+        dw.init(n_act * H, H, CHD, true);
+        auto issue_g = [&](int s) {
+            if (lane == 0) {
                 const int e = s_pact[gw.slot], n = gw.n();
                 uint8_t *dst = gu_buf + s * lay.gu_stage;
+                trx_fence_proxy_async();
                 trx_mbar_expect_tx(&full_g[s], 2u * n * rbg);
                 trx_bulk_g2s(dst, L.gate + e * L.gate_mb + (int64_t)gw.r * rbg, n * rbg, &full_g[s]);
                 trx_bulk_g2s(dst + gu_half, L.up + e * L.up_mb + (int64_t)gw.r * rbg, n * rbg, &full_g[s]);
-            };
-            auto issue_d = [&](int s) {
+            }
+        };
+        auto issue_d = [&](int s) {
+            if (lane == 0) {
                 const int e = s_pact[dw.slot], n = dw.n();
                 const int dbytes = DT == TRX_Q6_K ? CHD * nsb_d * 2 : 0; // 16-byte multiple, 16-byte aligned
+                trx_fence_proxy_async();
                 trx_mbar_expect_tx(&full_d[s], (uint32_t)(n * rbd + dbytes));
                 trx_bulk_g2s(dn_buf + s * lay.dn_stage, L.down + e * L.down_mb + (int64_t)dw.r * rbd, n * rbd, &full_d[s]);
                 if (DT == TRX_Q6_K)
                     trx_bulk_g2s(dn_buf + s * lay.dn_stage + CHD * rbd,
                                  L.down + e * L.down_mb + (int64_t)H * rbd + (int64_t)(dw.r / CHD) * CHD * nsb_d * 2, dbytes,
                                  &full_d[s]);
-            };
-            for (; issued_g < SG && gw.more(); issued_g++, gw.next()) issue_g(issued_g);
-            for (; issued_d < SD && dw.more(); issued_d++, dw.next()) issue_d(issued_d);
-            for (; gw.more(); issued_g++, gw.next()) {
-                const int s = issued_g % SG;
-                if (!trx_mbar_wait(&empty_g[s], ((issued_g / SG) - 1) & 1, TRX_WAIT_NS)) {
-                    failed = true;
-                    break;
-                }
-                trx_fence_proxy_async();
-                issue_g(s);
             }
-            for (; !failed && dw.more(); issued_d++, dw.next()) {
-                const int s = issued_d % SD;
-                if (!trx_mbar_wait(&empty_d[s], ((issued_d / SD) - 1) & 1, TRX_WAIT_NS)) {
-                    failed = true;
-                    break;
+        };
+        auto wait_all = [&](uint64_t *bar, int parity) {
+            return __all_sync(0xffffffffu, trx_mbar_wait(bar, parity, TRX_WAIT_NS));
+        };
+        for (; issued_g < SG && gw.more(); issued_g++, gw.next()) issue_g(issued_g);
+        asm volatile("bar.sync 1, %0;" ::"n"(32 * (TRX_FU_CWARPS + 1)) : "memory"); // the routing is sorted
+        // the down weights only after this CTA's first gate/up stages have landed: every CTA's gate/up data then
+        // comes first out of HBM, and the down data streams while the gate/up rows are multiplied
+        for (int q = 0; q < issued_g && !failed; q++)
+            if (!wait_all(&full_g[q], 0)) failed = true;
+        for (; !failed && issued_d < SD && dw.more(); issued_d++, dw.next()) issue_d(issued_d);
+        // gate/up chunks in order: wait for the consumers, publish (seg), refill the stage
+        TrxWalk pw;
+        pw.init(n_act * F, F, CHG, false);
+        const int gv0 = pw.v;
+        int seg_v0 = pw.v, seg_slot = pw.slot;
+        for (int j = 0; !failed && pw.more(); j++, pw.next()) {
+            const int s = j % SG, slot = pw.slot, n = pw.n();
+            if (slot != seg_slot) {
+                seg_slot = slot;
+                seg_v0 = pw.v;
+            }
+            if (!wait_all(&empty_g[s], (j / SG) & 1)) {
+                failed = true;
+                break;
+            }
+            if (seg && (pw.r + n == F || pw.v + n == pw.end)) { // this chunk ends the CTA's segment of the expert
+                const int e = s_active[slot], p0 = s_off[e], np = s_off[e + 1] - p0, rows = pw.v + n - seg_v0,
+                          sr0 = pw.r + n - rows;
+                for (int i = lane; i < rows * np; i += 32) {
+                    const int rr = i / np, pp = i % np, r = sr0 + rr;
+                    w.h[(int64_t)(p0 + pp) * F + (DT != TRX_Q4_K ? trx_lc_pos(r) : r)] = sh[(seg_v0 - gv0 + rr) * T + pp];
                 }
-                trx_fence_proxy_async();
+                __syncwarp();
+                uint32_t old = 0;
+                if (lane == 0) {
+                    __threadfence(); // the segment's h before its count
+                    old = atomicAdd(&sync->gu_done[slot], (uint32_t)rows);
+                }
+                old = __shfl_sync(0xffffffffu, old, 0);
+                if (DT == TRX_Q4_K && old + (uint32_t)rows == (uint32_t)F) {
+                    // the expert's last rows: its h is complete; prepare it for the down's integer definition,
+                    // then count once more
+                    __threadfence();
+                    for (int p = p0; p < p0 + np; p++)
+                        for (int s4 = 0; s4 < nsb_d; s4++)
+                            trx_prep_q4x_block<true>(w.h + (int64_t)p * F + 256 * s4, w.hq + (int64_t)p * F, s4, nsb_d,
+                                                     w.hq_bf + (int64_t)p * (F / 32) + 8 * s4, w.hq_sc + (int64_t)p * nsb_d + s4,
+                                                     lane);
+                    __syncwarp();
+                    if (lane == 0) {
+                        __threadfence();
+                        atomicAdd(&sync->gu_done[slot], 1u);
+                    }
+                }
+            }
+            if (gw.more()) {
+                issue_g(s);
+                issued_g++;
+                gw.next();
+            }
+        }
+        // down chunks in order: wait for the consumers, publish and mix (seg), refill the stage
+        TrxWalk pd;
+        pd.init(n_act * H, H, CHD, true);
+        for (int j = 0; !failed && pd.more(); j++, pd.next()) {
+            const int s = j % SD, n = pd.n(), d0 = pd.r;
+            if (!wait_all(&empty_d[s], (j / SD) & 1)) {
+                failed = true;
+                break;
+            }
+            if (seg) {
+                const int e = s_active[pd.slot], p0 = s_off[e], np = s_off[e + 1] - p0;
+                for (int i = lane; i < n * np; i += 32)
+                    w.h3[(int64_t)(p0 + i % np) * H + d0 + i / np] = sh3[((size_t)s * CHD + i / np) * T + i % np];
+                __syncwarp();
+                bool last = false;
+                if (lane == 0) {
+                    __threadfence();
+                    last = atomicAdd(&w.comb_cnt[d0 / CHD], (uint32_t)n) + (uint32_t)n == (uint32_t)(n_act * CHD);
+                }
+                if (__shfl_sync(0xffffffffu, last, 0)) combine(d0 / CHD);
+            }
+            if (dw.more()) {
                 issue_d(s);
+                issued_d++;
+                dw.next();
             }
         }
     } else {
@@ -476,6 +583,7 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
         int jg = 0;
         TrxWalk gw;
         gw.init(n_act * F, F, CHG, false);
+        const int gv0 = gw.v;
         for (; gw.more(); jg++, gw.next()) {
             const int slot = gw.slot, e = s_active[slot], r0 = gw.r, n = gw.n();
             const int p0 = s_off[e], p1 = s_off[e + 1];
@@ -506,41 +614,45 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
                     }
                     if (lane == 0) {
                         const int r = r0 + warp;
-                        w.h[(int64_t)p * F + (DT != TRX_Q4_K ? trx_lc_pos(r) : r)] = trx_silu_mul(g, u);
+                        const float h = trx_silu_mul(g, u);
+                        if (seg) sh[(gw.v + warp - gv0) * T + (p - p0)] = h;
+                        else w.h[(int64_t)p * F + (DT != TRX_Q4_K ? trx_lc_pos(r) : r)] = h;
                     }
                 }
             }
             if (warp == 0 && jg < 8) TRX_TRACE(40 + jg);
-            // Every consumer warp counts itself into the stage once per chunk (block scope, after its h stores); the
-            // last one publishes the chunk's n rows to the expert's count with one device-scope fence and atomic.
-            // A stage's uses are TRX_FU_CWARPS counts apart (a warp reaches its next use only after every warp's
-            // empty arrive), so the count's residue tells the last warp without a reset.
+            // Longer calls: every consumer warp counts itself into the stage once per chunk (block scope, after its h
+            // stores); the last one publishes the chunk's n rows to the expert's count with one device-scope fence and
+            // atomic. A stage's uses are TRX_FU_CWARPS counts apart (a warp reaches its next use only after every
+            // warp's empty arrive), so the count's residue tells the last warp without a reset.
             __syncwarp();
-            uint32_t last = 0;
-            if (lane == 0) {
-                __threadfence_block();
-                last = atomicAdd_block(&s_gcnt[s], 1u) % TRX_FU_CWARPS == TRX_FU_CWARPS - 1;
-            }
-            if (__shfl_sync(0xffffffffu, last, 0)) {
-                uint32_t old = 0;
+            if (!seg) {
+                uint32_t last = 0;
                 if (lane == 0) {
-                    __threadfence(); // the chunk's h rows (this CTA's warps', observed above) before the count
-                    old = atomicAdd(&sync->gu_done[slot], (uint32_t)n);
+                    __threadfence_block();
+                    last = atomicAdd_block(&s_gcnt[s], 1u) % TRX_FU_CWARPS == TRX_FU_CWARPS - 1;
                 }
-                old = __shfl_sync(0xffffffffu, old, 0);
-                if (DT == TRX_Q4_K && old + (uint32_t)n == (uint32_t)F) {
-                    // the expert's last chunk: every other row of it is counted, so its h rows are complete; prepare
-                    // them for the down's integer definition, then count once more
-                    __threadfence();
-                    for (int p = p0; p < p1; p++)
-                        for (int s4 = 0; s4 < nsb_d; s4++)
-                            trx_prep_q4x_block<true>(w.h + (int64_t)p * F + 256 * s4, w.hq + (int64_t)p * F, s4, nsb_d,
-                                                     w.hq_bf + (int64_t)p * (F / 32) + 8 * s4, w.hq_sc + (int64_t)p * nsb_d + s4,
-                                                     lane);
-                    __syncwarp();
+                if (__shfl_sync(0xffffffffu, last, 0)) {
+                    uint32_t old = 0;
                     if (lane == 0) {
+                        __threadfence(); // the chunk's h rows (this CTA's warps', observed above) before the count
+                        old = atomicAdd(&sync->gu_done[slot], (uint32_t)n);
+                    }
+                    old = __shfl_sync(0xffffffffu, old, 0);
+                    if (DT == TRX_Q4_K && old + (uint32_t)n == (uint32_t)F) {
+                        // the expert's last chunk: every other row of it is counted, so its h rows are complete;
+                        // prepare them for the down's integer definition, then count once more
                         __threadfence();
-                        atomicAdd(&sync->gu_done[slot], 1u);
+                        for (int p = p0; p < p1; p++)
+                            for (int s4 = 0; s4 < nsb_d; s4++)
+                                trx_prep_q4x_block<true>(w.h + (int64_t)p * F + 256 * s4, w.hq + (int64_t)p * F, s4, nsb_d,
+                                                         w.hq_bf + (int64_t)p * (F / 32) + 8 * s4,
+                                                         w.hq_sc + (int64_t)p * nsb_d + s4, lane);
+                        __syncwarp();
+                        if (lane == 0) {
+                            __threadfence();
+                            atomicAdd(&sync->gu_done[slot], 1u);
+                        }
                     }
                 }
             }
@@ -607,36 +719,29 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
                         const uint8_t *dptr = dn_buf + s * lay.dn_stage + CHD * rbd + (d % CHD) * nsb_d * 2;
                         vv = trx_q6l_dot<true, true, true>(st, dptr, w.h + (int64_t)p * F, nsb_d, lane & 15);
                     }
-                    if (row < n && (lane & 15) == 0) w.h3[(int64_t)p * H + d] = vv;
+                    if (row < n && (lane & 15) == 0) {
+                        if (seg) sh3[((size_t)s * CHD + row) * T + (p - p0)] = vv;
+                        else w.h3[(int64_t)p * H + d] = vv;
+                    }
                 }
             }
             __syncwarp();
             if (warp == 0 && jd < 6) TRX_TRACE(53 + jd);
-            // count the chunk's rows into their 16-row block: the stage's last warp (as for gate/up) adds the chunk's
-            // n rows; the warp completing the block combines it
-            const int blk = d0 / CHD;
-            bool last = false;
-            if (lane == 0) {
-                __threadfence_block();
-                if (atomicAdd_block(&s_dcnt[s], 1u) % TRX_FU_CWARPS == TRX_FU_CWARPS - 1) {
+            // longer calls: count the chunk's rows into their 16-row block: the stage's last warp (as for gate/up)
+            // adds the chunk's n rows; the warp completing the block combines it (per chunk: the blocks' mixes spread
+            // over the phase)
+            if (!seg) {
+                uint32_t slast = 0;
+                if (lane == 0) {
+                    __threadfence_block();
+                    slast = atomicAdd_block(&s_dcnt[s], 1u) % TRX_FU_CWARPS == TRX_FU_CWARPS - 1;
+                }
+                bool last = false;
+                if (__shfl_sync(0xffffffffu, slast, 0) && lane == 0) {
                     __threadfence();
-                    const uint32_t old = atomicAdd(&w.comb_cnt[blk], (uint32_t)n);
-                    last = old + (uint32_t)n == (uint32_t)(n_act * CHD);
+                    last = atomicAdd(&w.comb_cnt[d0 / CHD], (uint32_t)n) + (uint32_t)n == (uint32_t)(n_act * CHD);
                 }
-            }
-            if (__shfl_sync(0xffffffffu, last, 0)) {
-                __threadfence();
-                for (int i = lane; i < T * CHD; i += 32) {
-                    const int t = i / CHD, dd = blk * CHD + i % CHD;
-                    float out = 0.0f;
-                    for (int sl = 0; sl < k; sl++) {
-                        const int jj = t * k + sl;
-                        out = __fadd_rn(out, __fmul_rn(s_selw[jj], __ldcg(w.h3 + (int64_t)s_place[jj] * H + dd)));
-                    }
-                    if (ffn_out) ffn_out[(int64_t)t * H + dd] = out;
-                    x_io[(int64_t)t * H + dd] = __fadd_rn(x_io[(int64_t)t * H + dd], out);
-                }
-                if (lane == 0) w.comb_cnt[blk] = 0u;
+                if (__shfl_sync(0xffffffffu, last, 0)) combine(d0 / CHD);
             }
             __syncwarp();
             if (lane == 0) trx_mbar_arrive(&empty_d[s]);

@@ -47,6 +47,7 @@ def main():
     ap.add_argument("--down", default="q6_k")
     ap.add_argument("--tokens", type=int, default=1)
     ap.add_argument("--calls", type=int, default=20)
+    ap.add_argument("--per-cta", action="store_true", help="also print each CTA's gate/up-done and end times")
     a = ap.parse_args()
     types = {"q4_k": gb.Q4_K, "q8_0": gb.Q8_0, "q6_k": gb.Q6_K}
     gt, dt, T = types[a.gate], types[a.down], a.tokens
@@ -61,6 +62,10 @@ def main():
     tr = m.trace_read()
     m.check()
     print(json.dumps({"gate": a.gate, "down": a.down, "tokens": T, **summarize(tr)}))
+    if a.per_cta:
+        t0 = tr[:, 0][tr[:, 0] > 0].min()
+        rel = lambda c: [round((float(v) - t0) / 1000.0, 2) if v > t0 else None for v in tr[:, c]]
+        print(json.dumps({"gate_up_done": rel(4), "down_first": rel(5), "end": rel(52), "start": rel(0)}))
     m.close()
 
 
