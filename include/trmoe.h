@@ -82,7 +82,10 @@ TRMOE_API int tr_gpu_moe_set_layer(tr_gpu_moe *m, int64_t layer, const void *rou
  * normed: n_tok rows of n_embd (the ffn_norm output); x_inout: the residual stream, n_tok rows of
  * n_embd, to which the layer's output is added. sel_id_out, sel_w_out (optional): the n_tok * n_used
  * experts (increasing id per token) and their weights. Host memory (pinned or not). Returns when x
- * holds the result. 0, or -1 on a CUDA error or a bad argument. */
+ * holds the result. 0, or -1 on a CUDA error or a bad argument.
+ * Pinned x (page-locked and mapped, as the reference's gpu_attn.h:11-14 in/out buffers) and calls of up to
+ * 16 tokens without sel outputs: the GPU reads and writes x in place and posts its completion to pinned
+ * memory the call polls (no copy of x, no stream synchronisation); otherwise x is copied in and out. */
 TRMOE_API int tr_gpu_moe_layer(tr_gpu_moe *m, int64_t layer, const float *normed, int64_t n_tok, float *x_inout,
                      int64_t *sel_id_out, float *sel_w_out);
 

@@ -175,3 +175,30 @@ def test_q4k_long_pass_multikernel(cuda, oracle):
     assert same_bits(sid, want["sel_id"]) and same_bits(sw, want["sel_w"])
     assert same_bits(xo, want["x"])
     m.close()
+
+
+@pytest.mark.parametrize("gt,dt,rt", [(gb.Q4_K, gb.Q6_K, gb.BF16), (gb.Q8_0, gb.Q8_0, gb.F32)])
+def test_host_call_on_pinned_x(cuda, oracle, gt, dt, rt):
+    """tr_gpu_moe_layer with x in pinned host memory: short calls take the zero-copy road (x read and written in
+    place through its mapping, completion posted to a pinned word), longer ones the copy road; both bit for bit the
+    oracle's, call after call on the same buffers"""
+    torch = cuda
+    rng = np.random.default_rng(77 + gt)
+    lay = gb.make_layer(int(rng.integers(1 << 30)), 64, 2048, 1024, gt, dt, rt, mode="random")
+    d, keep = make_desc(lay, 2048, 1024, 8, 0, rt, gt, dt)
+    m = _ctx(dict(E=64, k=8, H=2048, F=1024, router=rt, gate=gt, down=dt, norm_topk=0, T=24))
+    m.set_layer(0, lay)
+    for T in (1, 3, 16, 24, 1):
+        normed = rng.normal(size=(T, 2048)).astype(np.float32)
+        x = rng.normal(size=(T, 2048)).astype(np.float32)
+        want = oracle.moe_layer(d, normed, x)
+        hn = torch.from_numpy(normed).pin_memory()
+        hx = torch.from_numpy(x.copy()).pin_memory()
+        for rep in range(2):  # the second call adds the layer to the first call's output
+            m.layer_ptrs(0, hn.data_ptr(), T, hx.data_ptr(), host=True)
+            if rep == 0:
+                assert same_bits(hx.numpy(), want["x"]), (T, rep)
+        want2 = oracle.moe_layer(d, normed, want["x"])
+        assert same_bits(hx.numpy(), want2["x"]), T
+    m.check()
+    m.close()

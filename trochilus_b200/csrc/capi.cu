@@ -169,6 +169,8 @@ struct tr_gpu_moe {
     TrxSync *sync = nullptr;
     uint64_t *trace = nullptr;
     uint32_t epoch = 0;
+    // the host-pointer road's completion word: mapped pinned host memory the fused kernel writes its epoch to
+    uint32_t *h_done = nullptr, *d_done = nullptr;
     bool fused_ok = false;
     float *d_normed = nullptr, *d_x = nullptr;
     int64_t *d_sel_id = nullptr;
@@ -452,6 +454,15 @@ extern "C" tr_gpu_moe *tr_gpu_moe_create(const tr_gpu_moe_config *cfg, int devic
             ok = ck(cudaMalloc(&m->layer_mem[(size_t)l], (size_t)lb), "cudaMalloc(layer)");
     }
     if (ok) ok = plan_kernels(m);
+    // the completion word of the host-pointer road (without it that road copies x and polls the stream)
+    if (ok && cudaHostAlloc((void **)&m->h_done, 256, cudaHostAllocMapped) == cudaSuccess) {
+        *(volatile uint32_t *)m->h_done = 0;
+        if (cudaHostGetDevicePointer((void **)&m->d_done, m->h_done, 0) != cudaSuccess) {
+            cudaFreeHost(m->h_done);
+            m->h_done = m->d_done = nullptr;
+        }
+    }
+    cudaGetLastError();
     if (!ok) {
         put_err(err, err_len);
         tr_gpu_moe_free(m);
@@ -507,6 +518,7 @@ extern "C" void tr_gpu_moe_free(tr_gpu_moe *m) {
     if (m->trace) cudaFree(m->trace);
     if (m->ep_tab) cudaFree(m->ep_tab);
     if (m->ep_buf) cudaFree(m->ep_buf);
+    if (m->h_done) cudaFreeHost(m->h_done);
     for (auto &es : m->evs)
         for (cudaEvent_t e : es.ev) cudaEventDestroy(e);
     if (m->stream) cudaStreamDestroy(m->stream);
@@ -722,8 +734,20 @@ static int launch_prefill(tr_gpu_moe *m, const TrxLayer &L, const TrxShape &S, c
 
 // Enqueues parts [first, last] of one layer call on st: 0 route (router, top-k, dispatch, input preparation),
 // 1 gate/up + SwiGLU, 2 the down input's Q4_K preparation, 3 down + combine + residual.
+// whether a whole layer call of T tokens takes the fused kernel (launch_layer's choice)
+#define TRX_HOST_ZC_MAX 16 // calls up to this many tokens may take the zero-copy host-pointer road
+
+static bool takes_fused(const tr_gpu_moe *m, int T) {
+    int sg, sd;
+    return m->fused_ok && !m->prof && !(m->pf_ok && m->pf_min > 0 && T >= m->pf_min) && T <= TRX_ROUTE_FUSED_MAX &&
+           (int)m->cfg.n_expert + T <= m->grid_fused && fused_stages(m, T, &sg, &sd);
+}
+
+// done: when the fused kernel takes the call, the device address of the word it writes its epoch to when every
+// output is out (*epoch_out: that epoch)
 static int launch_layer(tr_gpu_moe *m, int64_t layer, const float *d_normed, int64_t n_tok, float *d_x,
-                        const tr_gpu_moe_outputs *out, cudaStream_t st, int first = 0, int last = 3) {
+                        const tr_gpu_moe_outputs *out, cudaStream_t st, int first = 0, int last = 3,
+                        uint32_t *done = nullptr, uint32_t *epoch_out = nullptr) {
     const tr_gpu_moe_config &c = m->cfg;
     if (layer < 0 || layer >= c.n_layers || !m->layer_set[(size_t)layer]) {
         set_err("layer %lld is not set", (long long)layer);
@@ -769,7 +793,10 @@ static int launch_layer(tr_gpu_moe *m, int64_t layer, const float *d_normed, int
     if (first == 0 && last == 3 && m->fused_ok && T <= TRX_ROUTE_FUSED_MAX && E + T <= m->grid_fused && !es &&
         fused_stages(m, T, &sg, &sd)) {
         float *ffn = out ? out->ffn_out : nullptr;
-        const uint32_t epoch = ++m->epoch;
+        uint32_t epoch = ++m->epoch & 0x7fffffffu;
+        if (epoch == 0) epoch = ++m->epoch & 0x7fffffffu; // 0 is the completion word's initial value
+        w.host_done = done;
+        if (epoch_out) *epoch_out = epoch;
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3((unsigned)m->grid_fused);
         cfg.blockDim = dim3(TRX_FU_THREADS);
@@ -869,6 +896,47 @@ extern "C" int tr_gpu_moe_layer(tr_gpu_moe *m, int64_t layer, const float *norme
     const size_t xb = (size_t)(n_tok * m->cfg.n_embd) * 4;
     const int64_t R = n_tok * m->cfg.n_used;
     cudaStream_t st = m->stream;
+    // Short calls on pinned x (page-locked, mapped: cudaHostAlloc, cudaHostRegister, torch pin_memory): the fused
+    // kernel reads and writes x in place through its device mapping and posts its epoch to a pinned word once
+    // every output is out; the host polls that word instead of copying x back and synchronising the stream.
+    cudaPointerAttributes pa{};
+    if (m->h_done && sel_id_out == nullptr && sel_w_out == nullptr && n_tok <= TRX_HOST_ZC_MAX &&
+        takes_fused(m, (int)n_tok) && cudaPointerGetAttributes(&pa, x_inout) == cudaSuccess &&
+        pa.type == cudaMemoryTypeHost && pa.devicePointer != nullptr) {
+        uint32_t epoch = 0;
+        if (!ck(cudaMemcpyAsync(m->d_normed, normed, xb, cudaMemcpyHostToDevice, st), "copy normed") ||
+            launch_layer(m, layer, m->d_normed, n_tok, (float *)pa.devicePointer, nullptr, st, 0, 3, m->d_done,
+                         &epoch) != 0)
+            return -1;
+        const volatile uint32_t *word = m->h_done;
+        const auto t0 = std::chrono::steady_clock::now();
+        for (unsigned spins = 1;; spins++) {
+            const uint32_t v = *word;
+            if (v == epoch) return 0;
+            if (v == (epoch | 0x80000000u)) break; // the kernel gave up on a bounded wait
+            if ((spins & 1023) == 0) {
+                const double dt = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+                if (dt > 60.0) {
+                    set_err("the GPU did not finish within 60 s");
+                    return -1;
+                }
+                if (dt > 0.002) std::this_thread::sleep_for(std::chrono::microseconds(20));
+                const cudaError_t e = cudaStreamQuery(st); // a launch or device error ends the wait too
+                if (e != cudaSuccess && e != cudaErrorNotReady) {
+                    ck(e, "cudaStreamQuery");
+                    return -1;
+                }
+                if (e == cudaSuccess && *word != epoch) break; // finished without posting: the error road
+            }
+        }
+        stream_wait(st);
+        reset_counters(m, st);
+        int32_t flag = 0;
+        cudaMemcpy(&flag, m->work.err, 4, cudaMemcpyDeviceToHost);
+        set_err("a kernel gave up on a bounded wait (device error flag %d)", flag);
+        return -1;
+    }
+    cudaGetLastError(); // a pointer the runtime does not know (pageable memory) is not an error here
     tr_gpu_moe_outputs out{};
     const bool sel = sel_id_out != nullptr || sel_w_out != nullptr;
     if (sel) {

@@ -33,6 +33,7 @@
 
 #define TRX_SPIN_NS 1000000000ull
 #define TRX_FU_CWARPS 8                           // consumer warps
+#define TRX_FU_GW (TRX_FU_CWARPS / 2)             // consumer warps a group (two groups take the chunks in turn)
 #define TRX_FU_THREADS (32 * (TRX_FU_CWARPS + 1)) // + the producer warp
 #define TRX_FU_MAXST 8                            // most stages of either kind
 #define TRX_LOCAL_ROUTE_MAX 2                     // tokens up to which every CTA may route the call itself
@@ -54,6 +55,12 @@ __device__ __forceinline__ uint32_t trx_ld_acquire(const uint32_t *p) {
 
 __device__ __forceinline__ void trx_st_release(uint32_t *p, uint32_t v) {
     asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// the call's completion word in host memory (after a system-scope fence, so that what came before is visible first)
+__device__ __forceinline__ void trx_post_done(uint32_t *word, uint32_t v) {
+    __threadfence_system();
+    asm volatile("st.volatile.global.u32 [%0], %1;" ::"l"(word), "r"(v) : "memory");
 }
 
 __device__ __forceinline__ void trx_mbar_arrive(uint64_t *bar) {
@@ -141,7 +148,7 @@ __host__ __device__ inline TrxFusedSmem trx_fused_layout(int gate_type, int down
     l.meta = trx_align128(l.bars + 8 * 4 * TRX_FU_MAXST);
     l.seg = trx_align128(l.meta + (size_t)T * k * 16);
     const size_t seg_bytes =
-        T <= TRX_FU_SEG_MAX ? ((size_t)trx_fu_rows_g(E, k, T, F, grid) + (size_t)sd * TRX_DN_CHUNK) * T * 4 : 0;
+        T <= TRX_FU_SEG_MAX ? ((size_t)2 * trx_fu_rows_g(E, k, T, F, grid) + (size_t)sd * TRX_DN_CHUNK) * T * 4 : 0;
     l.tok = trx_align128(l.seg + seg_bytes);
     l.tok_bytes = gate_type == TRX_Q4_K ? trx_align128((size_t)H * 4 + (size_t)(H / 32 + H / 256) * 8) : (size_t)H * 4;
     l.total = l.tok + (size_t)T * l.tok_bytes;
@@ -168,6 +175,11 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int E = S.E, H = S.H, F = S.F, k = S.k, nsb_d = F / 256, R = T * k;
     TRX_TRACE(0);
+    if (w.trace != nullptr && tid == 0) {
+        uint32_t smid;
+        asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+        w.trace[(size_t)blockIdx.x * 64 + 49] = smid; // the SM this CTA runs on (not a time)
+    }
     const int rbg = GT == TRX_Q4_K ? H / 256 * 144 : H / 32 * 34;
     const int rbd = DT == TRX_Q4_K ? nsb_d * 144 : DT == TRX_Q6_K ? nsb_d * 208 : F / 32 * 34;
     const TrxFusedSmem lay = trx_fused_layout(GT, DT, H, F, T, k, SG, SD, E, gridDim.x);
@@ -185,14 +197,21 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
     if (tid == 0) { // the pipelines' barriers (their region is not scratch for the routing phase)
         for (int s = 0; s < SG; s++) {
             trx_mbar_init(&full_g[s], 1);
-            trx_mbar_init(&empty_g[s], TRX_FU_CWARPS);
+            trx_mbar_init(&empty_g[s], TRX_FU_GW);
         }
         for (int s = 0; s < SD; s++) {
             trx_mbar_init(&full_d[s], 1);
-            trx_mbar_init(&empty_d[s], TRX_FU_CWARPS);
+            trx_mbar_init(&empty_d[s], TRX_FU_GW);
         }
         trx_fence_barrier_init();
     }
+    if (warp == 1) trx_expf_prefetch(lane); // the softmax's table, before the routing needs it
+    // The producer warp mixes 16-row block blockIdx.x (below); for short calls its residual values are read now,
+    // so that the read (from host memory, in the host-pointer road) is over long before the mix
+    const bool xpre_ok = T * CHD <= 32 && (int)blockIdx.x < H / CHD;
+    float xpre = 0.0f;
+    if (xpre_ok && warp == TRX_FU_CWARPS && lane < T * CHD)
+        xpre = x_io[(int64_t)(lane / CHD) * H + (int64_t)blockIdx.x * CHD + lane % CHD];
 
     // Local routing (a decode call with a BF16 router of 2048 columns): every CTA computes all of the call's
     // logits from L2, routes and sorts them in shared memory, and prepares the tokens itself; no CTA waits for
@@ -344,7 +363,10 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
         if (tid == 0) s_flag = trx_spin(&sync->route_cnt, (uint32_t)writers, false);
         __syncthreads();
         if (!s_flag) {
-            if (tid == 0) atomicExch(w.err, 2);
+            if (tid == 0) {
+                atomicExch(w.err, 2);
+                if (w.host_done) trx_post_done(w.host_done, epoch | 0x80000000u);
+            }
             return;
         }
         TRX_TRACE(1);
@@ -436,13 +458,14 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
     }
     bool failed = false;
     int issued_g = 0, issued_d = 0; // the producer's counts, for the drain after a failure
-    // Short calls (seg): the consumers leave h and h3 in shared memory and release the stage; the producer warp,
-    // idle while they multiply, publishes: h once per expert segment of this CTA, h3 once per chunk (each write-out
-    // followed by one device-scope fence and count), and mixes a 16-row block when its count completes. Longer
-    // calls: the consumers publish themselves, chunk by chunk.
+    // Short calls (seg): the consumers leave the gate and up values (g, u) and the down values h3 in shared memory
+    // and release the stage; the producer warp, idle while they multiply, finishes and publishes them: per gate/up
+    // chunk h = silu(g) u, one row a lane, written out, and one device-scope fence and count per expert segment of
+    // this CTA; per down chunk h3 written out, one fence and count, and the mix of a 16-row block when its count
+    // completes. Longer calls: the consumers finish and publish themselves, chunk by chunk.
     const bool seg = T <= TRX_FU_SEG_MAX;
-    float *sh = reinterpret_cast<float *>(smem + lay.seg);               // [row of the CTA's gate/up range][token]
-    float *sh3 = sh + (size_t)trx_fu_rows_g(E, k, T, F, gridDim.x) * T; // [stage][row of the chunk][token]
+    float2 *sgu = reinterpret_cast<float2 *>(smem + lay.seg); // [row of the CTA's gate/up range][token]: (g, u)
+    float *sh3 = reinterpret_cast<float *>(sgu + (size_t)trx_fu_rows_g(E, k, T, F, gridDim.x) * T); // [stage][row][token]
     // the mix of a completed 16-row block (one warp): every token's k outputs in increasing expert id, then the residual
     auto combine = [&](int blk) {
         __threadfence();
@@ -454,7 +477,8 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
                 out = __fadd_rn(out, __fmul_rn(s_selw[jj], __ldcg(w.h3 + (int64_t)s_place[jj] * H + dd)));
             }
             if (ffn_out) ffn_out[(int64_t)t * H + dd] = out;
-            x_io[(int64_t)t * H + dd] = __fadd_rn(x_io[(int64_t)t * H + dd], out);
+            const float xv = xpre_ok && blk == (int)blockIdx.x ? xpre : x_io[(int64_t)t * H + dd];
+            x_io[(int64_t)t * H + dd] = __fadd_rn(xv, out);
         }
         if (lane == 0) w.comb_cnt[blk] = 0u;
     };
@@ -513,13 +537,16 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
                 failed = true;
                 break;
             }
-            if (seg && (pw.r + n == F || pw.v + n == pw.end)) { // this chunk ends the CTA's segment of the expert
-                const int e = s_active[slot], p0 = s_off[e], np = s_off[e + 1] - p0, rows = pw.v + n - seg_v0,
-                          sr0 = pw.r + n - rows;
-                for (int i = lane; i < rows * np; i += 32) {
-                    const int rr = i / np, pp = i % np, r = sr0 + rr;
-                    w.h[(int64_t)(p0 + pp) * F + (DT != TRX_Q4_K ? trx_lc_pos(r) : r)] = sh[(seg_v0 - gv0 + rr) * T + pp];
+            if (seg) {
+                const int e = s_active[slot], p0 = s_off[e], np = s_off[e + 1] - p0;
+                for (int i = lane; i < n * np; i += 32) {
+                    const int rr = i / np, pp = i % np, r = pw.r + rr;
+                    const float2 gu = sgu[(pw.v - gv0 + rr) * T + pp];
+                    w.h[(int64_t)(p0 + pp) * F + (DT != TRX_Q4_K ? trx_lc_pos(r) : r)] = trx_silu_mul(gu.x, gu.y);
                 }
+            }
+            if (seg && (pw.r + n == F || pw.v + n == pw.end)) { // this chunk ends the CTA's segment of the expert
+                const int e = s_active[slot], p0 = s_off[e], np = s_off[e + 1] - p0, rows = pw.v + n - seg_v0;
                 __syncwarp();
                 uint32_t old = 0;
                 if (lane == 0) {
@@ -552,6 +579,7 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
         // down chunks in order: wait for the consumers, publish and mix (seg), refill the stage
         TrxWalk pd;
         pd.init(n_act * H, H, CHD, true);
+        int n_mix = 0; // the blocks this CTA mixed (for the timeline)
         for (int j = 0; !failed && pd.more(); j++, pd.next()) {
             const int s = j % SD, n = pd.n(), d0 = pd.r;
             if (!wait_all(&empty_d[s], (j / SD) & 1)) {
@@ -563,12 +591,10 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
                 for (int i = lane; i < n * np; i += 32)
                     w.h3[(int64_t)(p0 + i % np) * H + d0 + i / np] = sh3[((size_t)s * CHD + i / np) * T + i % np];
                 __syncwarp();
-                bool last = false;
                 if (lane == 0) {
                     __threadfence();
-                    last = atomicAdd(&w.comb_cnt[d0 / CHD], (uint32_t)n) + (uint32_t)n == (uint32_t)(n_act * CHD);
+                    atomicAdd(&w.comb_cnt[d0 / CHD], (uint32_t)n);
                 }
-                if (__shfl_sync(0xffffffffu, last, 0)) combine(d0 / CHD);
             }
             if (dw.more()) {
                 issue_d(s);
@@ -576,15 +602,36 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
                 dw.next();
             }
         }
+        // the mixes: 16-row block b is mixed by CTA b mod grid once all its rows are counted (the mixing spread over
+        // the CTAs, none of them waiting for a block before its own rows are out)
+        for (int blk = blockIdx.x; !failed && blk < H / CHD; blk += gridDim.x) {
+            bool ok = true;
+            if (lane == 0) ok = trx_spin(&w.comb_cnt[blk], (uint32_t)(n_act * CHD), false);
+            if (!__shfl_sync(0xffffffffu, ok, 0)) {
+                failed = true;
+                break;
+            }
+            combine(blk);
+            n_mix++;
+        }
+        if (w.trace != nullptr && lane == 0) {
+            w.trace[(size_t)blockIdx.x * 64 + 50] = trx_globaltimer(); // the producer's publication done
+            w.trace[(size_t)blockIdx.x * 64 + 51] = (uint64_t)n_mix;
+        }
     } else {
-        // ---------------- a consumer warp: gate / up / SwiGLU, row `warp` of every chunk
+        // ---------------- a consumer warp. The consumers form two groups of TRX_FU_GW warps that take the chunks in
+        // turn (group 0 the even ones, group 1 the odd ones), each warp two rows of its group's chunks: two
+        // independent chains a warp, two chunks in work at once.
+        const int grp = warp / TRX_FU_GW, wl = warp % TRX_FU_GW;
         int cur = -1; // the token (gate/up) or grouped row (down) whose input this warp holds
         TrxQ4X X;
         int jg = 0;
         TrxWalk gw;
         gw.init(n_act * F, F, CHG, false);
         const int gv0 = gw.v;
+        // gate / up / SwiGLU: rows wl and wl + TRX_FU_GW of the group's chunks
         for (; gw.more(); jg++, gw.next()) {
+            if ((jg & 1) != grp) continue;
             const int slot = gw.slot, e = s_active[slot], r0 = gw.r, n = gw.n();
             const int p0 = s_off[e], p1 = s_off[e + 1];
             const int s = jg % SG;
@@ -592,13 +639,14 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
                 failed = true;
                 break;
             }
-            if (warp == 0 && jg < 8) TRX_TRACE(8 + jg);
-            if (warp < n) {
-                const uint8_t *gs = gu_buf + s * lay.gu_stage + warp * rbg, *us = gs + gu_half;
+            if (warp == 0 && jg < 16) TRX_TRACE(8 + jg / 2);
+            if (wl < n) {
+                const int ra = wl, rb = wl + TRX_FU_GW < n ? wl + TRX_FU_GW : wl; // rb == ra: one row left
+                const uint8_t *ga = gu_buf + s * lay.gu_stage + ra * rbg, *gb = gu_buf + s * lay.gu_stage + rb * rbg;
                 for (int p = p0; p < p1; p++) {
                     const int t = s_xmap[p];
                     const uint8_t *tok = s_tok + t * lay.tok_bytes;
-                    float g, u;
+                    float y[4]; // gate a, up a, gate b, up b
                     if (GT == TRX_Q4_K) {
                         if (t != cur) {
                             const double *bfd = reinterpret_cast<const double *>(tok + (size_t)H * 4);
@@ -606,31 +654,36 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
                                          bfd + H / 32 + (lane >> 2), X);
                             cur = t;
                         }
-                        trx_q4k_row8x2<true>(gs, us, X, lane, g, u);
-                    } else { // half 0 the gate row, half 1 the up row
-                        g = trx_q8l_dot<true, false>(lane < 16 ? gs : us, reinterpret_cast<const float *>(tok), H / 256,
-                                                     lane & 15);
-                        u = __shfl_sync(0xffffffffu, g, 16);
+                        const uint8_t *const rows[4] = {ga, ga + gu_half, gb, gb + gu_half};
+                        trx_q4k_row8xn<true, 4>(rows, X, lane, y);
+                    } else { // half 0 the gate rows, half 1 the up rows
+                        const float *xt = reinterpret_cast<const float *>(tok);
+                        const float va = trx_q8l_dot<true, false>(lane < 16 ? ga : ga + gu_half, xt, H / 256, lane & 15);
+                        const float vb = trx_q8l_dot<true, false>(lane < 16 ? gb : gb + gu_half, xt, H / 256, lane & 15);
+                        y[0] = va;
+                        y[1] = __shfl_sync(0xffffffffu, va, 16);
+                        y[2] = vb;
+                        y[3] = __shfl_sync(0xffffffffu, vb, 16);
                     }
-                    if (lane == 0) {
-                        const int r = r0 + warp;
-                        const float h = trx_silu_mul(g, u);
-                        if (seg) sh[(gw.v + warp - gv0) * T + (p - p0)] = h;
-                        else w.h[(int64_t)p * F + (DT != TRX_Q4_K ? trx_lc_pos(r) : r)] = h;
+                    if (lane < 2 && (lane == 0 || rb != ra)) { // lane 0 row a, lane 1 row b
+                        const int rr = lane ? rb : ra, r = r0 + rr;
+                        const float g = lane ? y[2] : y[0], u = lane ? y[3] : y[1];
+                        if (seg) sgu[(gw.v + rr - gv0) * T + (p - p0)] = make_float2(g, u);
+                        else w.h[(int64_t)p * F + (DT != TRX_Q4_K ? trx_lc_pos(r) : r)] = trx_silu_mul(g, u);
                     }
                 }
             }
-            if (warp == 0 && jg < 8) TRX_TRACE(40 + jg);
-            // Longer calls: every consumer warp counts itself into the stage once per chunk (block scope, after its h
-            // stores); the last one publishes the chunk's n rows to the expert's count with one device-scope fence and
-            // atomic. A stage's uses are TRX_FU_CWARPS counts apart (a warp reaches its next use only after every
-            // warp's empty arrive), so the count's residue tells the last warp without a reset.
+            if (warp == 0 && jg < 16) TRX_TRACE(40 + jg / 2);
+            // Longer calls: every warp of the group counts itself into the stage once per chunk (block scope, after
+            // its h stores); the last one publishes the chunk's n rows to the expert's count with one device-scope
+            // fence and atomic. A stage's uses are TRX_FU_GW counts apart (a warp reaches its next use only after
+            // every arrive of the previous one), so the count's residue tells the last warp without a reset.
             __syncwarp();
             if (!seg) {
                 uint32_t last = 0;
                 if (lane == 0) {
                     __threadfence_block();
-                    last = atomicAdd_block(&s_gcnt[s], 1u) % TRX_FU_CWARPS == TRX_FU_CWARPS - 1;
+                    last = atomicAdd_block(&s_gcnt[s], 1u) % TRX_FU_GW == TRX_FU_GW - 1;
                 }
                 if (__shfl_sync(0xffffffffu, last, 0)) {
                     uint32_t old = 0;
@@ -658,11 +711,11 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
             }
             __syncwarp();
             if (lane == 0) trx_mbar_arrive(&empty_g[s]);
-            if (warp == 0 && jg < 8) TRX_TRACE(16 + jg);
+            if (warp == 0 && jg < 16) TRX_TRACE(16 + jg / 2);
         }
         if (warp == 0) TRX_TRACE(4);
 
-        // ---------------- down + combine + residual, rows 2 warp and 2 warp + 1 of every chunk
+        // ---------------- down: half-warp hw = 2 wl + lane / 16 of the group takes rows hw and hw + 8 of its chunks
         cur = -1;
         constexpr int NSB4 = 4; // the register road for F == 1024 (OLMoE)
         float xr[NSB4 * 16];
@@ -671,6 +724,7 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
         TrxWalk dw;
         dw.init(n_act * H, H, CHD, true);
         for (; dw.more() && !failed; jd++, dw.next()) {
+            if ((jd & 1) != grp) continue;
             const int slot = dw.slot, e = s_active[slot], d0 = dw.r, n = dw.n();
             const int p0 = s_off[e], p1 = s_off[e + 1];
             const int s = jd % SD;
@@ -688,12 +742,15 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
                 break;
             }
             if (warp == 0 && jd == 0) TRX_TRACE(5);
-            if (warp == 0 && jd < 8) TRX_TRACE(24 + jd);
-            const int row = 2 * warp + (lane >> 4), rowc = row < n ? row : 2 * warp, d = d0 + rowc;
-            if (2 * warp < n) {
-                const uint8_t *st = dn_buf + s * lay.dn_stage + rowc * rbd;
+            if (warp == 0 && jd < 16) TRX_TRACE(24 + jd / 2);
+            const int hw = 2 * wl + (lane >> 4), ra = hw, rb = hw + CHD / 2;
+            const int rac = ra < n ? ra : 0, rbc = rb < n ? rb : 0; // a row past the chunk computes row 0, unstored
+            if (2 * wl < n) {
+                const uint8_t *sta = dn_buf + s * lay.dn_stage + rac * rbd, *stb = dn_buf + s * lay.dn_stage + rbc * rbd;
+                const uint8_t *dps = dn_buf + s * lay.dn_stage + CHD * rbd; // the block's Q6_K d values
+                const int da = (d0 + rac) % CHD, db = (d0 + rbc) % CHD;
                 for (int p = p0; p < p1; p++) {
-                    float vv;
+                    float va, vb;
                     if (DT == TRX_Q4_K) {
                         if (p != cur) {
                             trx_q4x_load<true>(w.hq + (int64_t)p * F, 16, lane & 15,
@@ -701,51 +758,53 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
                                                w.hq_sc + (int64_t)p * nsb_d + ((lane >> 2) & 3), X);
                             cur = p;
                         }
-                        vv = trx_q4k_row4<true>(st, X, lane);
+                        va = trx_q4k_row4<true>(sta, X, lane);
+                        vb = trx_q4k_row4<true>(stb, X, lane);
                     } else if (nsb_d == NSB4) {
                         if (p != cur) {
                             trx_lc_load<NSB4, true>(w.h + (int64_t)p * F, lane & 15, xr);
                             cur = p;
                         }
                         if (DT == TRX_Q8_0) {
-                            vv = trx_q8l_dot_reg<NSB4>(st, xr, lane & 15);
+                            va = trx_q8l_dot_reg<NSB4>(sta, xr, lane & 15);
+                            vb = trx_q8l_dot_reg<NSB4>(stb, xr, lane & 15);
                         } else {
-                            const uint8_t *dptr = dn_buf + s * lay.dn_stage + CHD * rbd + (d % CHD) * NSB4 * 2;
-                            vv = trx_q6l_dot_reg<NSB4, true>(st, dptr, xr, lane & 15);
+                            va = trx_q6l_dot_reg<NSB4, true>(sta, dps + da * NSB4 * 2, xr, lane & 15);
+                            vb = trx_q6l_dot_reg<NSB4, true>(stb, dps + db * NSB4 * 2, xr, lane & 15);
                         }
                     } else if (DT == TRX_Q8_0) {
-                        vv = trx_q8l_dot<true, true>(st, w.h + (int64_t)p * F, nsb_d, lane & 15);
+                        va = trx_q8l_dot<true, true>(sta, w.h + (int64_t)p * F, nsb_d, lane & 15);
+                        vb = trx_q8l_dot<true, true>(stb, w.h + (int64_t)p * F, nsb_d, lane & 15);
                     } else {
-                        const uint8_t *dptr = dn_buf + s * lay.dn_stage + CHD * rbd + (d % CHD) * nsb_d * 2;
-                        vv = trx_q6l_dot<true, true, true>(st, dptr, w.h + (int64_t)p * F, nsb_d, lane & 15);
+                        va = trx_q6l_dot<true, true, true>(sta, dps + da * nsb_d * 2, w.h + (int64_t)p * F, nsb_d, lane & 15);
+                        vb = trx_q6l_dot<true, true, true>(stb, dps + db * nsb_d * 2, w.h + (int64_t)p * F, nsb_d, lane & 15);
                     }
-                    if (row < n && (lane & 15) == 0) {
-                        if (seg) sh3[((size_t)s * CHD + row) * T + (p - p0)] = vv;
-                        else w.h3[(int64_t)p * H + d] = vv;
+                    if ((lane & 15) == 0) {
+                        if (ra < n) {
+                            if (seg) sh3[((size_t)s * CHD + ra) * T + (p - p0)] = va;
+                            else w.h3[(int64_t)p * H + d0 + ra] = va;
+                        }
+                        if (rb < n) {
+                            if (seg) sh3[((size_t)s * CHD + rb) * T + (p - p0)] = vb;
+                            else w.h3[(int64_t)p * H + d0 + rb] = vb;
+                        }
                     }
                 }
             }
             __syncwarp();
-            if (warp == 0 && jd < 6) TRX_TRACE(53 + jd);
+            if (warp == 0 && jd < 12) TRX_TRACE(53 + jd / 2);
             // longer calls: count the chunk's rows into their 16-row block: the stage's last warp (as for gate/up)
-            // adds the chunk's n rows; the warp completing the block combines it (per chunk: the blocks' mixes spread
-            // over the phase)
-            if (!seg) {
-                uint32_t slast = 0;
-                if (lane == 0) {
-                    __threadfence_block();
-                    slast = atomicAdd_block(&s_dcnt[s], 1u) % TRX_FU_CWARPS == TRX_FU_CWARPS - 1;
-                }
-                bool last = false;
-                if (__shfl_sync(0xffffffffu, slast, 0) && lane == 0) {
+            // adds the chunk's n rows
+            if (!seg && lane == 0) {
+                __threadfence_block();
+                if (atomicAdd_block(&s_dcnt[s], 1u) % TRX_FU_GW == TRX_FU_GW - 1) {
                     __threadfence();
-                    last = atomicAdd(&w.comb_cnt[d0 / CHD], (uint32_t)n) + (uint32_t)n == (uint32_t)(n_act * CHD);
+                    atomicAdd(&w.comb_cnt[d0 / CHD], (uint32_t)n);
                 }
-                if (__shfl_sync(0xffffffffu, last, 0)) combine(d0 / CHD);
             }
             __syncwarp();
             if (lane == 0) trx_mbar_arrive(&empty_d[s]);
-            if (warp == 0 && jd < 8) TRX_TRACE(32 + jd);
+            if (warp == 0 && jd < 16) TRX_TRACE(32 + jd / 2);
         }
         if (warp == 0) TRX_TRACE(6);
     }
@@ -757,18 +816,23 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
             // every copy still in flight lands before the CTA's shared memory goes away
             for (int q = 0; q < issued_g; q++) trx_mbar_wait(&full_g[q % SG], (q / SG) & 1, TRX_WAIT_NS);
             for (int q = 0; q < issued_d; q++) trx_mbar_wait(&full_d[q % SD], (q / SD) & 1, TRX_WAIT_NS);
+            if (w.host_done) trx_post_done(w.host_done, epoch | 0x80000000u);
         }
         __syncthreads();
         return;
     }
     TRX_TRACE(52);
     if (tid == 0) {
-        __threadfence();
+        // the CTA's outputs (x may be host memory: system scope) before its count
+        if (w.host_done) __threadfence_system();
+        else __threadfence();
         if (atomicAdd(&sync->finish, 1u) == gridDim.x - 1) { // every CTA is past its waits
+            __threadfence();
             for (int i = 0; i < E; i++) sync->gu_done[i] = 0u;
             sync->route_cnt = 0u;
             sync->finish = 0u;
             __threadfence();
+            if (w.host_done) trx_post_done(w.host_done, epoch); // every CTA's outputs are out
         }
     }
 }

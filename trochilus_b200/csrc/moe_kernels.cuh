@@ -78,6 +78,8 @@ struct TrxWork {
     int64_t *out_place;
     float *out_logits;
     uint64_t *trace;     // NULL, or 64 %globaltimer slots per CTA of the fused kernel (tr_gpu_moe_trace)
+    uint32_t *host_done; // NULL, or a word of mapped pinned host memory: the fused kernel writes its epoch there
+                         // once every output is visible to the host (bit 31 set: it gave up)
 };
 
 // ---------------------------------------------------------------------------------------------
@@ -561,6 +563,35 @@ __device__ __forceinline__ void trx_q4k_row8x2(const uint8_t *__restrict__ ra, c
     }
     ya = __double2float_rn(sa);
     yb = __double2float_rn(sb);
+}
+
+// N Q4_K rows of 8 blocks against the same input (a gate row and its up row, of one or two chunk rows), interleaved
+// for ILP: y[i] = float(sum_s v_s) of row i in every lane
+template <bool SM, int N>
+__device__ __forceinline__ void trx_q4k_row8xn(const uint8_t *const (&rows)[N], const TrxQ4X &X, int lane, float (&y)[N]) {
+    const int s = lane >> 2, c = lane & 3;
+    uint4 hd[N], q0[N], q1[N];
+#pragma unroll
+    for (int i = 0; i < N; i++) {
+        const uint8_t *b = rows[i] + 144 * s;
+        hd[i] = trx_ld<SM, uint4>(b);
+        q0[i] = trx_ld<SM, uint4>(b + 16 + 32 * c);
+        q1[i] = trx_ld<SM, uint4>(b + 32 + 32 * c);
+    }
+    double v[N], acc[N];
+#pragma unroll
+    for (int i = 0; i < N; i++) {
+        int64_t T, M;
+        trx_q4k_chunk(hd[i], q0[i], q1[i], c, X, T, M);
+        v[i] = trx_q4k_value(hd[i], T, M, X.sc);
+        acc[i] = 0.0;
+    }
+#pragma unroll
+    for (int j = 0; j < 8; j++)
+#pragma unroll
+        for (int i = 0; i < N; i++) acc[i] = __dadd_rn(acc[i], trx_shfl_d(v[i], 4 * j));
+#pragma unroll
+    for (int i = 0; i < N; i++) y[i] = __double2float_rn(acc[i]);
 }
 
 // Q4_K rows of 4 blocks (1024 columns), a half-warp each: the half's row value

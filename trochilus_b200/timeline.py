@@ -1,6 +1,6 @@
 """Reads the fused MoE-layer kernel's timeline (tr_gpu_moe_trace) into per-phase statistics.
 
-    python -m trochilus_b200.timeline [--gate q4_k] [--down q6_k] [--tokens 1] [--calls 20]
+    python -m trochilus_b200.timeline [--gate q4_k] [--down q6_k] [--tokens 1] [--calls 20] [--layers 2]
 
 runs a few calls on synthetic weights and prints, over the CTAs of the last call, when each phase ended
 (microseconds after the earliest CTA start): router/preparation done, routing seen, copies armed, gate/up
@@ -47,21 +47,25 @@ def main():
     ap.add_argument("--down", default="q6_k")
     ap.add_argument("--tokens", type=int, default=1)
     ap.add_argument("--calls", type=int, default=20)
+    ap.add_argument("--layers", type=int, default=2, help="resident layers, called in turn (16: weights from HBM)")
     ap.add_argument("--per-cta", action="store_true", help="also print each CTA's gate/up-done and end times")
+    ap.add_argument("--dump", default=None, help="also save the raw trace (CTAs x 64 slots) to this .npy file")
     a = ap.parse_args()
     types = {"q4_k": gb.Q4_K, "q8_0": gb.Q8_0, "q6_k": gb.Q6_K}
     gt, dt, T = types[a.gate], types[a.down], a.tokens
-    m = GpuMoe(2, 64, 8, 2048, 1024, gb.BF16, gt, dt, max_tokens=T)
-    for l in range(2):
+    m = GpuMoe(a.layers, 64, 8, 2048, 1024, gb.BF16, gt, dt, max_tokens=T)
+    for l in range(a.layers):
         m.set_layer(l, gb.make_layer(50 + l, 64, 2048, 1024, gt, dt, gb.BF16, mode="random"))
     normed = torch.randn((a.calls, T, 2048), device="cuda")
     x = torch.randn((T, 2048), device="cuda")
     m.trace(True)
     for i in range(a.calls):
-        m.layer_dev(i % 2, normed[i].data_ptr(), T, x.data_ptr(), None, stream=torch.cuda.current_stream().cuda_stream)
+        m.layer_dev(i % a.layers, normed[i].data_ptr(), T, x.data_ptr(), None, stream=torch.cuda.current_stream().cuda_stream)
     tr = m.trace_read()
     m.check()
     print(json.dumps({"gate": a.gate, "down": a.down, "tokens": T, **summarize(tr)}))
+    if a.dump:
+        np.save(a.dump, tr)
     if a.per_cta:
         t0 = tr[:, 0][tr[:, 0] > 0].min()
         rel = lambda c: [round((float(v) - t0) / 1000.0, 2) if v > t0 else None for v in tr[:, c]]
