@@ -167,7 +167,7 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ int s_active[TRX_MAX_EXPERTS], s_off[TRX_MAX_EXPERTS + 1], s_nact, s_flag;
     __shared__ int s_pact[TRX_MAX_EXPERTS]; // the producer's copy of the active experts
-    __shared__ float sp[TRX_FU_CWARPS + 1][96];
+    __shared__ __align__(16) float sp[TRX_FU_CWARPS + 1][96]; // per-warp scratch (16-byte aligned rows)
     __shared__ int scnt[64];
     __shared__ float s_logit[TRX_LOCAL_ROUTE_MAX * TRX_MAX_EXPERTS];
     __shared__ uint32_t s_gcnt[TRX_FU_MAXST], s_dcnt[TRX_FU_MAXST];
@@ -175,6 +175,11 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int E = S.E, H = S.H, F = S.F, k = S.k, nsb_d = F / 256, R = T * k;
     TRX_TRACE(0);
+    const long long ck0 = clock64();
+#define TRX_CYC(slot)                                                                                                  \
+    do {                                                                                                               \
+        if (w.trace != nullptr && threadIdx.x == 0) w.trace[(size_t)blockIdx.x * 64 + (slot)] = clock64() - ck0;      \
+    } while (0)
     if (w.trace != nullptr && tid == 0) {
         uint32_t smid;
         asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
@@ -309,6 +314,7 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
                                   s_selw + warp * k);
         if (blockIdx.x == 0 && w.out_logits)
             for (int j = tid; j < T * E; j += blockDim.x) w.out_logits[j] = s_logit[j];
+        trx_fence_proxy_async(); // the routing's writes to the stage area, before the copies that land there
         __syncthreads();
     } else {
         // ---------------- phase A: CTAs 0..E-1 the logits of one expert each; the tokens' prepared inputs either
@@ -357,6 +363,12 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
             for (int j = lane; j < 64; j += 32) dl[j] = 0.0f;
             __syncwarp();
             trx_route_token<true>(dl, E, k, S.norm_topk, lane, sp[warp], di, dw);
+            __syncwarp();
+            if (T == 1) { // and the single-token sort, into dummy arrays after them
+                int32_t *dsort = di + 64;
+                trx_sort_single(di, E, k, TrxSortOut{dsort, dsort + 72, dsort + 144, dsort + 152, dsort + 224, nullptr, nullptr},
+                                lane);
+            }
         }
         // ---------------- phase B: every CTA, once all writers are in (acquire), routes and sorts the whole call
         // itself from the logits in L2 (no CTA publishes for the others), and stages the tokens' inputs
@@ -370,16 +382,20 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
             return;
         }
         TRX_TRACE(1);
+        TRX_CYC(53);
         float *slog = reinterpret_cast<float *>(smem); // T x E logits (the stage buffers are free until the barriers)
         for (int j = tid; j < T * E; j += blockDim.x) slog[j] = __ldcg(w.logits + j);
         __syncthreads();
+        TRX_CYC(54);
         const long long c1 = clock64();
         for (int t = warp; t < T; t += TRX_FU_CWARPS + 1)
             trx_route_token<true>(slog + t * E, E, k, S.norm_topk, lane, sp[warp], s_selid + t * k, s_selw + t * k);
         if (w.trace != nullptr && tid == 0) w.trace[(size_t)blockIdx.x * 64 + 7] = (uint64_t)(clock64() - c1);
+        trx_fence_proxy_async(); // the routing's writes to the stage area, before the copies that land there
         __syncthreads();
     }
     TRX_TRACE(60);
+    TRX_CYC(55);
     // Both roads: s_selid / s_selw hold the call's routing. The producer derives the active experts from the ids and
     // starts streaming at once; the consumers sort the rows by expert, write the optional outputs and stage the
     // tokens' prepared inputs meanwhile; all meet at bar 1 once the producer's first copies are out.
@@ -408,29 +424,16 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
             const bool out = blockIdx.x == 0;
             const TrxSortOut so{s_off, s_active, &s_nact, s_place, s_xmap, out ? w.out_offsets : nullptr,
                                 out ? w.out_place : nullptr};
+            TRX_CYC(56);
             const long long c0 = clock64();
             if (T == 1) {
-                // one token: its k ids are distinct and already in increasing order, so expert s_selid[j] holds row j
-                // alone: offsets[e] = the number of selected ids below e, place[j] = j, every row is token 0
-                const int e0 = lane < k ? s_selid[lane] : TRX_MAX_EXPERTS;
-                for (int e = lane; e <= E; e += 32) {
-                    int c = 0;
-                    for (int j = 0; j < k; j++) c += s_selid[j] < e;
-                    s_off[e] = c;
-                    if (so.out_offsets) so.out_offsets[e] = c;
-                }
-                if (lane < k) {
-                    s_active[lane] = e0;
-                    s_place[lane] = lane;
-                    s_xmap[lane] = 0;
-                    if (so.out_place) so.out_place[lane] = lane;
-                }
-                if (lane == 0) s_nact = k;
+                trx_sort_single(s_selid, E, k, so, lane);
             } else {
                 trx_warp_counting_sort(s_selid, R, E, k, so, scnt, lane);
             }
             if (w.trace != nullptr && lane == 0) w.trace[(size_t)blockIdx.x * 64 + 63] = (uint64_t)(clock64() - c0);
             TRX_TRACE(48);
+            TRX_CYC(57);
         } else if (blockIdx.x == 0 && w.out_sel_id) {
             for (int j = ctid - 32; j < R; j += 32 * (TRX_FU_CWARPS - 1)) {
                 w.out_sel_id[j] = s_selid[j];
@@ -452,9 +455,11 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
                         __ldcg(reinterpret_cast<const float4 *>(w.x_lc + (int64_t)t * H) + i);
             }
         }
-        asm volatile("bar.sync 1, %0;" ::"n"(32 * (TRX_FU_CWARPS + 1)) : "memory"); // with the producer
+        asm volatile("bar.sync 1, %0;" ::"n"(32 * TRX_FU_CWARPS) : "memory");        // the consumers: sorted
+        asm volatile("bar.arrive 2, %0;" ::"n"(32 * (TRX_FU_CWARPS + 1)) : "memory"); // tell the producer
         n_act = s_nact;
         TRX_TRACE(2);
+        TRX_CYC(58);
     }
     bool failed = false;
     int issued_g = 0, issued_d = 0; // the producer's counts, for the drain after a failure
@@ -493,7 +498,6 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
             if (lane == 0) {
                 const int e = s_pact[gw.slot], n = gw.n();
                 uint8_t *dst = gu_buf + s * lay.gu_stage;
-                trx_fence_proxy_async();
                 trx_mbar_expect_tx(&full_g[s], 2u * n * rbg);
                 trx_bulk_g2s(dst, L.gate + e * L.gate_mb + (int64_t)gw.r * rbg, n * rbg, &full_g[s]);
                 trx_bulk_g2s(dst + gu_half, L.up + e * L.up_mb + (int64_t)gw.r * rbg, n * rbg, &full_g[s]);
@@ -503,7 +507,6 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
             if (lane == 0) {
                 const int e = s_pact[dw.slot], n = dw.n();
                 const int dbytes = DT == TRX_Q6_K ? CHD * nsb_d * 2 : 0; // 16-byte multiple, 16-byte aligned
-                trx_fence_proxy_async();
                 trx_mbar_expect_tx(&full_d[s], (uint32_t)(n * rbd + dbytes));
                 trx_bulk_g2s(dn_buf + s * lay.dn_stage, L.down + e * L.down_mb + (int64_t)dw.r * rbd, n * rbd, &full_d[s]);
                 if (DT == TRX_Q6_K)
@@ -516,7 +519,7 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
             return __all_sync(0xffffffffu, trx_mbar_wait(bar, parity, TRX_WAIT_NS));
         };
         for (; issued_g < SG && gw.more(); issued_g++, gw.next()) issue_g(issued_g);
-        asm volatile("bar.sync 1, %0;" ::"n"(32 * (TRX_FU_CWARPS + 1)) : "memory"); // the routing is sorted
+        asm volatile("bar.sync 2, %0;" ::"n"(32 * (TRX_FU_CWARPS + 1)) : "memory"); // the routing is sorted
         // the down weights only after this CTA's first gate/up stages have landed: every CTA's gate/up data then
         // comes first out of HBM, and the down data streams while the gate/up rows are multiplied
         for (int q = 0; q < issued_g && !failed; q++)
@@ -792,7 +795,7 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
                 }
             }
             __syncwarp();
-            if (warp == 0 && jd < 12) TRX_TRACE(53 + jd / 2);
+
             // longer calls: count the chunk's rows into their 16-row block: the stage's last warp (as for gate/up)
             // adds the chunk's n rows
             if (!seg && lane == 0) {

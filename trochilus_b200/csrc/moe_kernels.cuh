@@ -90,8 +90,10 @@ struct TrxWork {
 // infinite logit, or every logit -inf) or none is; the reference's repeated argmax (first untaken id when it
 // is NaN, else the largest, ties to the lower id) then picks ids 0..k-1 in the first case and the k largest
 // by (value, -id) in the second. The rank of each value among all E gives the latter directly.
+// Not inlined: one copy of the code, so that a warp that runs it early (on dummy logits) leaves it in the SM's
+// instruction caches for the call's real routing.
 template <bool SM = false>
-__device__ void trx_route_token(const float *__restrict__ logits, int E, int k, int norm_topk, int lane,
+__device__ __noinline__ void trx_route_token(const float *__restrict__ logits, int E, int k, int norm_topk, int lane,
                                 float *__restrict__ sp, int32_t *ids_out, float *w_out) {
     const bool ok0 = lane < E, ok1 = lane + 32 < E;
     const float v0 = ok0 ? (SM ? logits[lane] : __ldcg(logits + lane)) : 0.0f;
@@ -216,6 +218,26 @@ struct TrxSortOut {
     int32_t *offsets, *active, *n_active, *place, *xmap;
     int64_t *out_offsets, *out_place;
 };
+
+// The sort of a single token's k rows by one warp: its k ids are distinct and already in increasing order, so
+// expert sel_id[j] holds row j alone: offsets[e] = the number of selected ids below e, place[j] = j, every row is
+// token 0. Not inlined (warmed up early, as trx_route_token).
+__device__ __noinline__ void trx_sort_single(const int32_t *__restrict__ sel_id, int E, int k, TrxSortOut w, int lane) {
+    const int e0 = lane < k ? sel_id[lane] : TRX_MAX_EXPERTS;
+    for (int e = lane; e <= E; e += 32) {
+        int c = 0;
+        for (int j = 0; j < k; j++) c += sel_id[j] < e;
+        w.offsets[e] = c;
+        if (w.out_offsets) w.out_offsets[e] = c;
+    }
+    if (lane < k) {
+        w.active[lane] = e0;
+        w.place[lane] = lane;
+        w.xmap[lane] = 0;
+        if (w.out_place) w.out_place[lane] = lane;
+    }
+    if (lane == 0) *w.n_active = k;
+}
 
 // The same by one warp, any R (32 rows a pass, stable by match_any ranks); scnt: 64 ints of shared memory
 __device__ void trx_warp_counting_sort(const int32_t *__restrict__ sel_id, int R, int E, int k, TrxSortOut w, int *scnt,

@@ -33,7 +33,11 @@ def summarize(tr: np.ndarray) -> dict:
     out["cycles_route_token_w0"] = int(np.median(tr[:, 7]))
     out["cycles_sort_w0"] = int(np.median(tr[:, 63]))
     out["w0_gate_up_chunks"] = [(med(8 + j), med(40 + j), med(16 + j)) for j in range(8)]
-    out["w0_down_chunks"] = [(med(24 + j), med(53 + j) if j < 6 else None, med(32 + j)) for j in range(8)]
+    out["w0_down_chunks"] = [(med(24 + j), None, med(32 + j)) for j in range(8)]
+    cyc = lambda slot: int(np.median(tr[:, slot]))
+    # cycles since the CTA's start (thread 0): route count seen, logits loaded, routed, sort begun / done, barrier
+    out["cycles_w0"] = {n: cyc(sl) for n, sl in (("route_cnt_seen", 53), ("logits_loaded", 54), ("routed", 55),
+                                                 ("sort_begin", 56), ("sorted", 57), ("bar1", 58))}
     return out
 
 
