@@ -176,7 +176,6 @@ struct tr_gpu_moe {
     int64_t *d_sel_id = nullptr;
     float *d_sel_w = nullptr;
     // the tensor-core road (prefill.cuh): calls of at least pf_min tokens take it (0: never)
-    int local_route = 0; // fused kernel: replicated per-CTA routing for T <= 2 (TRMOE_LOCAL_ROUTE=1), else shared logits
     bool pf_ok = false;
     int64_t pf_min = 0;
     float *pf_xhi = nullptr, *pf_xlo = nullptr;
@@ -433,7 +432,6 @@ extern "C" tr_gpu_moe *tr_gpu_moe_create(const tr_gpu_moe_config *cfg, int devic
     }
     tr_gpu_moe *m = new tr_gpu_moe();
     m->cfg = *cfg;
-    if (const char *lr = getenv("TRMOE_LOCAL_ROUTE")) m->local_route = atoi(lr) != 0;
     m->device = device;
     const WorkLayout wl = work_layout(*cfg);
     const int64_t lb = layer_bytes(*cfg);
@@ -762,7 +760,7 @@ static int launch_layer(tr_gpu_moe *m, int64_t layer, const float *d_normed, int
         return -1;
     }
     const TrxLayer &L = m->layers[(size_t)layer];
-    TrxShape S{(int)c.n_expert, (int)c.n_used, (int)c.n_embd, (int)c.n_ff, (int)c.norm_topk, m->local_route};
+    TrxShape S{(int)c.n_expert, (int)c.n_used, (int)c.n_embd, (int)c.n_ff, (int)c.norm_topk};
     TrxWork w = m->work;
     w.trace = m->trace;
     if (out) {

@@ -1,24 +1,28 @@
 // fused_layer.cuh: one MoE layer call for a short pass (decode) as ONE persistent kernel, launched
 // cooperatively so that every CTA is resident and may wait for another.
 //
-//  routing  (a) local, for T <= 2 with a BF16 2048-column router when enabled: every CTA computes all logits
-//           itself from L2. (b) otherwise: CTAs 0..E-1 compute the router logits of one expert each
-//           (trx_router_block), CTAs E..E+T-1 prepare one token's input row each, and every CTA counts itself in;
-//           once all E + T are in, every CTA reads the logits, routes every token and sorts the (token, slot) rows
-//           by expert in its own shared memory (no CTA publishes a routing for the others), and stages the
-//           tokens' prepared input rows. Each CTA then takes its share of the routed gate/up rows and of the
-//           routed down rows (trx_cta_range over each virtual row space).
-//  then     warp-specialised: a producer warp streams this CTA's gate/up chunks (8 rows of gate and of up)
-//           and down chunks (16 rows) from HBM into shared-memory stages with 1-D TMA bulk copies, refilling a
-//           stage when its "empty" barrier says the 8 consumer warps are done with it; the down weights do not
-//           depend on the activations, so they stream while the gate/up rows are multiplied. Each consumer
-//           warp works on its own rows with no block-wide barrier: gate/up row w of every chunk (both matrices,
-//           SwiGLU fused, h written, the row counted into its expert with release semantics; the warp that
-//           counts an expert's last row prepares that expert's down inputs for Q4_K), then rows 2w, 2w + 1 of
-//           every down chunk once its expert's rows are all counted (acquire); the warp completing a 16-row
-//           block combines it: every token's k expert outputs added in increasing expert id, the sum added to
-//           the residual (Trochilus's mix_body).
-//  end      the last CTA resets the per-expert counters for the next call.
+//  routing  CTAs 0..E-1 compute the router logits of one expert each (trx_router_block); for calls of more than
+//           TRX_FU_LOCAL_PREP tokens CTAs E..E+T-1 prepare one token's input row each, for shorter ones every CTA
+//           prepares the inputs itself meanwhile; every writer counts itself in. Once all are in, every CTA reads
+//           the logits, routes every token and sorts the (token, slot) rows by expert in its own shared memory (no
+//           CTA publishes a routing for the others). Each CTA then takes its share of the routed gate/up rows and of
+//           the routed down rows (whole chunks of each virtual row space).
+//  then     warp-specialised: a producer warp streams this CTA's gate/up chunks (8 rows of gate and of up) and
+//           down chunks (16 rows) from HBM into shared-memory stages with 1-D TMA bulk copies, refilling a stage
+//           when its "empty" barrier says its consumers are done with it; the down weights do not depend on the
+//           activations, so they stream while the gate/up rows are multiplied. The 8 consumer warps form two groups
+//           that take the chunks in turn, each warp two rows of a chunk (two independent chains a warp), with no
+//           block-wide barrier: gate/up rows (both matrices, SwiGLU), then the down rows of every chunk once its
+//           expert's gate/up rows are all counted (acquire). Short calls (T <= TRX_FU_SEG_MAX) leave their values
+//           in shared memory and the producer warp, idle while they multiply, finishes and publishes them: h =
+//           silu(g) u per chunk, one fence and count per expert segment of the CTA (the count that completes an
+//           expert prepares its Q4_K down inputs), h3 and one fence and count per down chunk. Longer calls publish
+//           from the consumers, chunk by chunk.
+//  mix      16-row block b is mixed by CTA b mod grid (its producer warp) once all its rows are counted: every
+//           token's k expert outputs added in increasing expert id, the sum added to the residual (Trochilus's
+//           mix_body).
+//  end      the last CTA resets the per-expert counters for the next call and, for the host-pointer road, posts
+//           the call's epoch to a pinned host word once every output is visible.
 //
 // Every wait is bounded (TRX_SPIN_NS, TRX_WAIT_NS); a warp that gives up marks the CTA failed, the producer
 // waits (bounded) for every copy it armed, the error flag is set and the CTA leaves. The counters a failed call
@@ -36,7 +40,6 @@
 #define TRX_FU_GW (TRX_FU_CWARPS / 2)             // consumer warps a group (two groups take the chunks in turn)
 #define TRX_FU_THREADS (32 * (TRX_FU_CWARPS + 1)) // + the producer warp
 #define TRX_FU_MAXST 8                            // most stages of either kind
-#define TRX_LOCAL_ROUTE_MAX 2                     // tokens up to which every CTA may route the call itself
 #define TRX_FU_LOCAL_PREP 8                       // tokens up to which every CTA prepares the inputs itself
 
 struct TrxSync {
@@ -169,7 +172,6 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
     __shared__ int s_pact[TRX_MAX_EXPERTS]; // the producer's copy of the active experts
     __shared__ __align__(16) float sp[TRX_FU_CWARPS + 1][96]; // per-warp scratch (16-byte aligned rows)
     __shared__ int scnt[64];
-    __shared__ float s_logit[TRX_LOCAL_ROUTE_MAX * TRX_MAX_EXPERTS];
     __shared__ uint32_t s_gcnt[TRX_FU_MAXST], s_dcnt[TRX_FU_MAXST];
     constexpr int CHG = TRX_GU_CHUNK, CHD = TRX_DN_CHUNK;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -218,105 +220,7 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
     if (xpre_ok && warp == TRX_FU_CWARPS && lane < T * CHD)
         xpre = x_io[(int64_t)(lane / CHD) * H + (int64_t)blockIdx.x * CHD + lane % CHD];
 
-    // Local routing (a decode call with a BF16 router of 2048 columns): every CTA computes all of the call's
-    // logits from L2, routes and sorts them in shared memory, and prepares the tokens itself; no CTA waits for
-    // another before the weights stream. Otherwise the logits are computed once, expert by expert (below).
-    const bool local = S.local_route && T <= TRX_LOCAL_ROUTE_MAX && H == 2048 && L.router_type == TRX_BF16;
-    if (local) {
-        // logits: a chain per (expert, lane l), lane l's 16 elements of each 256-block in lane-row order (2 x 16
-        // bytes), every token of the call against the same weights; the next round's weights load while a round
-        // is multiplied
-        constexpr int NB = 8;
-        const int nchain = E * 16, nth = blockDim.x;
-        auto load_chain = [&](int c, uint4(&r)[2 * NB]) {
-            const uint4 *p = reinterpret_cast<const uint4 *>(L.router + (int64_t)min(c >> 4, E - 1) * (NB * 512)) + 2 * (c & 15);
-#pragma unroll
-            for (int i = 0; i < NB; i++) {
-                r[2 * i] = __ldg(p + 32 * i);
-                r[2 * i + 1] = __ldg(p + 32 * i + 1);
-            }
-        };
-        float *sx = reinterpret_cast<float *>(GT == TRX_Q8_0 ? s_tok : smem); // the inputs, LC order, H apart
-        auto chains = [&](int c, const uint4(&r)[2 * NB]) {
-            const int e = min(c >> 4, E - 1), l = c & 15;
-            float acc[TRX_LOCAL_ROUTE_MAX];
-#pragma unroll
-            for (int t = 0; t < TRX_LOCAL_ROUTE_MAX; t++) acc[t] = 0.0f;
-#pragma unroll
-            for (int i = 0; i < NB; i++) {
-                float wv[16];
-#pragma unroll
-                for (int q = 0; q < 2; q++) {
-                    const uint32_t u[4] = {r[2 * i + q].x, r[2 * i + q].y, r[2 * i + q].z, r[2 * i + q].w};
-#pragma unroll
-                    for (int j = 0; j < 4; j++) {
-                        wv[8 * q + 2 * j] = __uint_as_float(u[j] << 16);
-                        wv[8 * q + 2 * j + 1] = __uint_as_float(u[j] & 0xffff0000u);
-                    }
-                }
-#pragma unroll
-                for (int t = 0; t < TRX_LOCAL_ROUTE_MAX; t++) {
-                    if (t < T) {
-                        const float *xs = sx + t * H + 256 * i + 4 * l;
-                        float xv[16];
-#pragma unroll
-                        for (int q = 0; q < 4; q++) {
-                            const float4 v = *reinterpret_cast<const float4 *>(xs + 64 * q);
-                            xv[4 * q] = v.x; xv[4 * q + 1] = v.y; xv[4 * q + 2] = v.z; xv[4 * q + 3] = v.w;
-                        }
-#pragma unroll
-                        for (int m = 0; m < 16; m++) acc[t] = __fadd_rn(acc[t], __fmul_rn(wv[m], xv[m]));
-                    }
-                }
-            }
-#pragma unroll
-            for (int t = 0; t < TRX_LOCAL_ROUTE_MAX; t++) {
-                if (t < T) {
-                    const float v = trx_lane_tree16(acc[t]);
-                    if (l == 0 && c < nchain)
-                        s_logit[t * E + e] = L.router_bias ? __fadd_rn(v, L.router_bias[e]) : v;
-                }
-            }
-        };
-        uint4 wa[2 * NB], wb[2 * NB];
-        load_chain(tid, wa);
-        for (int i = tid; i < T * H / 4; i += blockDim.x) {
-            const int t = (4 * i) / H, kk = (4 * i) % H;
-            const float4 v = *reinterpret_cast<const float4 *>(normed + (int64_t)t * H + kk);
-            float *dst = sx + t * H;
-            dst[trx_lc_pos(kk)] = v.x;
-            dst[trx_lc_pos(kk + 1)] = v.y;
-            dst[trx_lc_pos(kk + 2)] = v.z;
-            dst[trx_lc_pos(kk + 3)] = v.w;
-        }
-        if (GT == TRX_Q4_K) // the tokens prepared for the gate/up products, one warp per 256-block
-            for (int q = warp; q < T * nsb_g; q += TRX_FU_CWARPS + 1) {
-                const int t = q / nsb_g, s4 = q % nsb_g;
-                uint8_t *tok = s_tok + t * lay.tok_bytes;
-                double *bfd = reinterpret_cast<double *>(tok + (size_t)H * 4);
-                trx_prep_q4x_block(normed + (int64_t)t * H + 256 * s4, reinterpret_cast<uint32_t *>(tok), s4, nsb_g,
-                                   bfd + 8 * s4, bfd + H / 32 + s4, lane);
-            }
-        __syncthreads();
-        TRX_TRACE(62);
-        for (int base = 0; base < nchain; base += 2 * nth) {
-            if (base + nth < nchain) load_chain(base + nth + tid, wb);
-            chains(base + tid, wa);
-            if (base + nth < nchain) {
-                if (base + 2 * nth < nchain) load_chain(base + 2 * nth + tid, wa);
-                chains(base + nth + tid, wb);
-            }
-        }
-        __syncthreads();
-        TRX_TRACE(59);
-        if (warp < T)
-            trx_route_token<true>(s_logit + warp * E, E, k, S.norm_topk, lane, sp[warp], s_selid + warp * k,
-                                  s_selw + warp * k);
-        if (blockIdx.x == 0 && w.out_logits)
-            for (int j = tid; j < T * E; j += blockDim.x) w.out_logits[j] = s_logit[j];
-        trx_fence_proxy_async(); // the routing's writes to the stage area, before the copies that land there
-        __syncthreads();
-    } else {
+    {
         // ---------------- phase A: CTAs 0..E-1 the logits of one expert each; the tokens' prepared inputs either
         // by every CTA for itself into shared memory (T <= TRX_FU_LOCAL_PREP: from normed, while the logits are
         // computed elsewhere) or by CTAs E..E+T-1 into global memory; every CTA that wrote counts itself in (release)
@@ -399,7 +303,7 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
     // Both roads: s_selid / s_selw hold the call's routing. The producer derives the active experts from the ids and
     // starts streaming at once; the consumers sort the rows by expert, write the optional outputs and stage the
     // tokens' prepared inputs meanwhile; all meet at bar 1 once the producer's first copies are out.
-    const bool lprep = T <= TRX_FU_LOCAL_PREP || local;
+    const bool lprep = T <= TRX_FU_LOCAL_PREP;
     int n_act;
     if (warp == TRX_FU_CWARPS) {
         uint32_t m0 = 0, m1 = 0; // the selected experts as a 64-bit set
@@ -720,8 +624,6 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
 
         // ---------------- down: half-warp hw = 2 wl + lane / 16 of the group takes rows hw and hw + 8 of its chunks
         cur = -1;
-        constexpr int NSB4 = 4; // the register road for F == 1024 (OLMoE)
-        float xr[NSB4 * 16];
         const uint32_t need = (uint32_t)F + (DT == TRX_Q4_K ? 1u : 0u);
         int jd = 0, ready = -1; // ready: the last slot whose gate/up rows this warp saw complete
         TrxWalk dw;
@@ -763,24 +665,13 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
                         }
                         va = trx_q4k_row4<true>(sta, X, lane);
                         vb = trx_q4k_row4<true>(stb, X, lane);
-                    } else if (nsb_d == NSB4) {
-                        if (p != cur) {
-                            trx_lc_load<NSB4, true>(w.h + (int64_t)p * F, lane & 15, xr);
-                            cur = p;
-                        }
-                        if (DT == TRX_Q8_0) {
-                            va = trx_q8l_dot_reg<NSB4>(sta, xr, lane & 15);
-                            vb = trx_q8l_dot_reg<NSB4>(stb, xr, lane & 15);
-                        } else {
-                            va = trx_q6l_dot_reg<NSB4, true>(sta, dps + da * NSB4 * 2, xr, lane & 15);
-                            vb = trx_q6l_dot_reg<NSB4, true>(stb, dps + db * NSB4 * 2, xr, lane & 15);
-                        }
-                    } else if (DT == TRX_Q8_0) {
-                        va = trx_q8l_dot<true, true>(sta, w.h + (int64_t)p * F, nsb_d, lane & 15);
-                        vb = trx_q8l_dot<true, true>(stb, w.h + (int64_t)p * F, nsb_d, lane & 15);
-                    } else {
-                        va = trx_q6l_dot<true, true, true>(sta, dps + da * nsb_d * 2, w.h + (int64_t)p * F, nsb_d, lane & 15);
-                        vb = trx_q6l_dot<true, true, true>(stb, dps + db * nsb_d * 2, w.h + (int64_t)p * F, nsb_d, lane & 15);
+                    } else { // one 256-block an iteration, h through L1 (after the acquire above)
+                        const float2 v = DT == TRX_Q8_0
+                                             ? trx_q8l_dot2(sta, stb, w.h + (int64_t)p * F, nsb_d, lane & 15)
+                                             : trx_q6l_dot2(sta, stb, dps + da * nsb_d * 2, dps + db * nsb_d * 2,
+                                                            w.h + (int64_t)p * F, nsb_d, lane & 15);
+                        va = v.x;
+                        vb = v.y;
                     }
                     if ((lane & 15) == 0) {
                         if (ra < n) {

@@ -391,6 +391,44 @@ __device__ __forceinline__ float trx_q6l_dot(const uint8_t *__restrict__ row, co
     return trx_lane_tree16(acc);
 }
 
+// Two rows (a, b in shared memory) of the same width against one LC-ordered input row read through L1 (each
+// 256-block's inputs loaded once for both rows), one 256-block an iteration (a small loop body). Q6L: da, db the
+// rows' f16 d values in shared memory. Returns both tree sums (the same in all 16 threads of the half-warp).
+__device__ __forceinline__ float2 trx_q6l_dot2(const uint8_t *__restrict__ ra, const uint8_t *__restrict__ rb,
+                                               const uint8_t *__restrict__ da, const uint8_t *__restrict__ db,
+                                               const float *__restrict__ xlc, int nsb, int l) {
+    float aa = 0.0f, ab = 0.0f;
+#pragma unroll 1
+    for (int s = 0; s < nsb; s++) {
+        float xv[16];
+        trx_lc_block<false>(xlc, s, l, xv);
+        aa = trx_q6l_block(aa, *reinterpret_cast<const uint2 *>(ra + 128 * s + 8 * l),
+                           *reinterpret_cast<const uint32_t *>(ra + 128 * nsb + 64 * s + 4 * l),
+                           *reinterpret_cast<const uint4 *>(ra + 192 * nsb + 16 * s),
+                           trx_half(reinterpret_cast<const uint16_t *>(da)[s]), xv);
+        ab = trx_q6l_block(ab, *reinterpret_cast<const uint2 *>(rb + 128 * s + 8 * l),
+                           *reinterpret_cast<const uint32_t *>(rb + 128 * nsb + 64 * s + 4 * l),
+                           *reinterpret_cast<const uint4 *>(rb + 192 * nsb + 16 * s),
+                           trx_half(reinterpret_cast<const uint16_t *>(db)[s]), xv);
+    }
+    return make_float2(trx_lane_tree16(aa), trx_lane_tree16(ab));
+}
+
+__device__ __forceinline__ float2 trx_q8l_dot2(const uint8_t *__restrict__ ra, const uint8_t *__restrict__ rb,
+                                               const float *__restrict__ xlc, int nch, int l) {
+    float aa = 0.0f, ab = 0.0f;
+#pragma unroll 1
+    for (int i = 0; i < nch; i++) {
+        float xv[16];
+        trx_lc_block<false>(xlc, i, l, xv);
+        aa = trx_q8l_block(aa, *reinterpret_cast<const uint4 *>(ra + 272 * i),
+                           *reinterpret_cast<const uint4 *>(ra + 272 * i + 16 + 16 * l), xv);
+        ab = trx_q8l_block(ab, *reinterpret_cast<const uint4 *>(rb + 272 * i),
+                           *reinterpret_cast<const uint4 *>(rb + 272 * i + 16 + 16 * l), xv);
+    }
+    return make_float2(trx_lane_tree16(aa), trx_lane_tree16(ab));
+}
+
 // The thread's 16 inputs of each of NCH 256-chunks of an LC-ordered row, in registers (CG: through L2)
 template <int NCH, bool CG>
 __device__ __forceinline__ void trx_lc_load(const float *__restrict__ xlc, int l, float (&xr)[NCH * 16]) {

@@ -48,7 +48,6 @@ struct TrxLayer {
 
 struct TrxShape {
     int E, k, H, F, norm_topk;
-    int local_route; // the fused kernel: every CTA routes a short call itself (see fused_layer.cuh)
 };
 
 struct TrxWork {
