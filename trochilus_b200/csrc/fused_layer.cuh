@@ -226,19 +226,24 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
         // computed elsewhere) or by CTAs E..E+T-1 into global memory; every CTA that wrote counts itself in (release)
         const bool lprep = T <= TRX_FU_LOCAL_PREP;
         const int writers = E + (lprep ? 0 : T);
-        if ((int)blockIdx.x < writers) {
-            if ((int)blockIdx.x < E) trx_router_block(L, S, normed, blockIdx.x, 0, T, w, reinterpret_cast<float *>(smem));
+        // short calls: the router CTAs compute the logits with warps 0-3 only, while the others prepare the inputs
+        // and warm up the routing code (below)
+        const int rthr = lprep ? 128 : 0, w0 = (int)blockIdx.x < E && rthr ? rthr / 32 : 0;
+        if ((int)blockIdx.x < writers && (rthr == 0 || tid < rthr)) {
+            if ((int)blockIdx.x < E)
+                trx_router_block(L, S, normed, blockIdx.x, 0, T, w, reinterpret_cast<float *>(smem), rthr);
             else trx_prep_token(L, S, normed, blockIdx.x - E, w);
-            __syncthreads();
+            if (rthr) asm volatile("bar.sync 3, %0;" ::"r"(rthr) : "memory");
+            else __syncthreads();
             TRX_TRACE(62);
             if (tid == 0) {
                 __threadfence();
                 atomicAdd(&sync->route_cnt, 1u);
             }
         }
-        if (lprep) {
+        if (lprep && warp >= w0) {
             if (GT == TRX_Q4_K) {
-                for (int q = warp; q < T * nsb_g; q += TRX_FU_CWARPS + 1) {
+                for (int q = warp - w0; q < T * nsb_g; q += TRX_FU_CWARPS + 1 - w0) {
                     const int t = q / nsb_g, s4 = q % nsb_g;
                     uint8_t *tok = s_tok + t * lay.tok_bytes;
                     double *bfd = reinterpret_cast<double *>(tok + (size_t)H * 4);
@@ -246,7 +251,7 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
                                        bfd + 8 * s4, bfd + H / 32 + s4, lane);
                 }
             } else {
-                for (int i = tid; i < T * H / 4; i += blockDim.x) {
+                for (int i = tid - 32 * w0; i < T * H / 4; i += blockDim.x - 32 * w0) {
                     const int t = (4 * i) / H, kk = (4 * i) % H;
                     const float4 v = *reinterpret_cast<const float4 *>(normed + (int64_t)t * H + kk);
                     float *dst = reinterpret_cast<float *>(s_tok + t * lay.tok_bytes);
@@ -260,8 +265,10 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
         // While the logits come in, warp 4 (on warp 0's sub-partition) runs the routing steps once on dummy logits,
         // so that the instructions warp 0 runs next are in the SM's instruction caches (run once per call, they
         // would otherwise be fetched cold from L2 line by line)
-        if (warp == 4) {
-            float *dl = reinterpret_cast<float *>(smem) + T * E; // after the logits' slot; the stage area is idle
+        // the routing warm-up's scratch: past the router's staging (in use meanwhile) and the logits' slot
+        const size_t wscr = trx_align128((size_t)(1 + (T < TRX_TOK_STAGE ? T : TRX_TOK_STAGE)) * H * 4 + (size_t)T * E * 4);
+        if (warp == 4 && wscr + 4096 <= lay.bars) {
+            float *dl = reinterpret_cast<float *>(smem + wscr);
             int32_t *di = reinterpret_cast<int32_t *>(dl + 64);
             float *dw = dl + 128;
             for (int j = lane; j < 64; j += 32) dl[j] = 0.0f;

@@ -315,16 +315,22 @@ __device__ void trx_prep_token(const TrxLayer &L, const TrxShape &S, const float
 
 // Router logits of expert e for tokens [g_begin, g_end) by one block of 256 threads; sdyn: (1 +
 // min(tokens, TRX_TOK_STAGE)) * H floats of shared memory.
+// nthr: 0 = the whole block takes part; else threads 0 .. nthr - 1 only (a multiple of 32), which meet at named
+// barrier 3 instead of the block barrier, so that the others are free meanwhile.
 __device__ void trx_router_block(const TrxLayer &L, const TrxShape &S, const float *__restrict__ normed, int e,
-                                 int g_begin, int g_end, TrxWork &w, float *sdyn) {
-    const int tid = threadIdx.x;
+                                 int g_begin, int g_end, TrxWork &w, float *sdyn, int nthr = 0) {
+    const int tid = threadIdx.x, nt = nthr ? nthr : (int)blockDim.x;
+    auto sync = [&]() {
+        if (nthr) asm volatile("bar.sync 3, %0;" ::"r"(nthr) : "memory");
+        else __syncthreads();
+    };
     const int E = S.E, H = S.H;
     float *srow = sdyn, *sx = sdyn + H;
     const int64_t rb = trx_row_bytes(L.router_type, H);
     const uint8_t *row = L.router + e * rb; // lane-row order (trx_repack_lanerows): packed q holds element k below
     auto k_of = [](int q) { return (q & ~255) + ((q >> 4) & 15) + 16 * (q & 15); };
     if (L.router_type == TRX_F32) {
-        for (int i = tid; i < H / 4; i += blockDim.x) {
+        for (int i = tid; i < H / 4; i += nt) {
             const float4 v = __ldg(reinterpret_cast<const float4 *>(row) + i);
             srow[trx_lc_pos(k_of(4 * i))] = v.x;
             srow[trx_lc_pos(k_of(4 * i + 1))] = v.y;
@@ -332,7 +338,7 @@ __device__ void trx_router_block(const TrxLayer &L, const TrxShape &S, const flo
             srow[trx_lc_pos(k_of(4 * i + 3))] = v.w;
         }
     } else { // 8 bfloat16 a load, widened exactly
-        for (int i = tid; i < H / 8; i += blockDim.x) {
+        for (int i = tid; i < H / 8; i += nt) {
             const uint4 v = __ldg(reinterpret_cast<const uint4 *>(row) + i);
             const uint32_t u[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
@@ -347,8 +353,8 @@ __device__ void trx_router_block(const TrxLayer &L, const TrxShape &S, const flo
     const int nch = H / 256;
     for (int g0 = g_begin; g0 < g_end; g0 += TRX_TOK_STAGE) {
         const int ng = min(TRX_TOK_STAGE, g_end - g0);
-        if (g0 != g_begin) __syncthreads(); // the first group's loads go out with the router row's
-        for (int i = tid; i < ng * H / 4; i += blockDim.x) { // inputs of the group, LC order
+        if (g0 != g_begin) sync(); // the first group's loads go out with the router row's
+        for (int i = tid; i < ng * H / 4; i += nt) { // inputs of the group, LC order
             const int tk = (4 * i) / H, kk = (4 * i) % H;
             const float4 v = *reinterpret_cast<const float4 *>(normed + (int64_t)(g0 + tk) * H + kk);
             float *dst = sx + tk * H;
@@ -357,8 +363,9 @@ __device__ void trx_router_block(const TrxLayer &L, const TrxShape &S, const flo
             dst[trx_lc_pos(kk + 2)] = v.z;
             dst[trx_lc_pos(kk + 3)] = v.w;
         }
-        __syncthreads();
-        const int tk = tg < ng ? tg : 0;
+        sync();
+        for (int tb = 0; tb < ng; tb += nt / 16) { // a half-warp a token (uniform trip count: the tree's shuffles)
+        const int tk = tb + tg < ng ? tb + tg : 0;
         const float *xs = sx + tk * H + 4 * l, *ws = srow + 4 * l;
         float acc = 0.0f;
         for (int i = 0; i < nch; i++) {
@@ -374,10 +381,11 @@ __device__ void trx_router_block(const TrxLayer &L, const TrxShape &S, const flo
             for (int m = 0; m < 16; m++) acc = __fadd_rn(acc, __fmul_rn(wv[m], xv[m]));
         }
         acc = trx_lane_tree16(acc);
-        if (l == 0 && tg < ng) {
+        if (l == 0 && tb + tg < ng) {
             const float v = L.router_bias ? __fadd_rn(acc, bias) : acc;
-            w.logits[(int64_t)(g0 + tg) * E + e] = v;
-            if (w.out_logits) w.out_logits[(int64_t)(g0 + tg) * E + e] = v;
+            w.logits[(int64_t)(g0 + tb + tg) * E + e] = v;
+            if (w.out_logits) w.out_logits[(int64_t)(g0 + tb + tg) * E + e] = v;
+        }
         }
     }
 }
