@@ -490,6 +490,7 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
                 gw.next();
             }
         }
+        if (w.trace != nullptr && lane == 0) w.trace[(size_t)blockIdx.x * 64 + 59] = trx_globaltimer(); // h published
         // down chunks in order: wait for the consumers, publish and mix (seg), refill the stage
         TrxWalk pd;
         pd.init(n_act * H, H, CHD, true);
@@ -647,6 +648,7 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
                     failed = true;
                     break;
                 }
+                if (warp == 0 && ready < 0) TRX_TRACE(61); // the first expert's gate/up rows seen complete
                 ready = slot;
             }
             if (!__all_sync(0xffffffffu, trx_mbar_wait(&full_d[s], (jd / SD) & 1, TRX_WAIT_NS))) {
