@@ -38,7 +38,8 @@
 #define TRX_SPIN_NS 1000000000ull
 #define TRX_FU_CWARPS 8                           // consumer warps
 #define TRX_FU_GW (TRX_FU_CWARPS / 2)             // consumer warps a group (two groups take the chunks in turn)
-#define TRX_FU_THREADS (32 * (TRX_FU_CWARPS + 1)) // + the producer warp
+#define TRX_FU_HWARP (TRX_FU_CWARPS + 1)          // the warp that copies short calls' h rows into the down stages
+#define TRX_FU_THREADS (32 * (TRX_FU_CWARPS + 2)) // + the producer warp and that one
 #define TRX_FU_MAXST 8                            // most stages of either kind
 #define TRX_FU_LOCAL_PREP 8                       // tokens up to which every CTA prepares the inputs itself
 
@@ -82,13 +83,32 @@ __device__ __forceinline__ bool trx_spin(const uint32_t *p, uint32_t target, boo
     }
 }
 
-// A CTA's walk over its range [v, end) of a virtual row space of n_active experts x per rows, in chunks of at most
-// `most` rows that stay inside one expert (and, when aligned, inside one `most`-row block). When `most` divides
-// `per` the CTAs share whole chunks. int32: the spaces hold at most 64 x 2048 rows.
+// A CTA's walk over its share of a virtual row space of n_active experts x per rows, in chunks of at most `most`
+// rows that stay inside one expert.
+//  slot-major (longer calls): the CTA's range [v, end) of the space, chunks aligned to `most`-row blocks when asked;
+//           when `most` divides `per` the CTAs share whole chunks. Each expert's rows are done by a few CTAs.
+//  expert-major (short calls): the CTA's rows [ra, rb) of EVERY expert (a multiple of `gran` rows), experts in
+//           order; the experts are then finished one after another across the grid, and a CTA holds every expert's
+//           contribution to its rows. v counts the CTA's rows from 0.
+// int32: the spaces hold at most 64 x 2048 rows.
 struct TrxWalk {
-    int v, end, slot, r, per, most;
-    bool aligned;
-    __device__ void init(int V, int per_, int most_, bool aligned_) {
+    int v, end, slot, r, per, most, ra, rb;
+    bool aligned, em;
+    __device__ void init(int V, int per_, int most_, bool aligned_, bool em_ = false, int gran = 1) {
+        per = per_;
+        most = most_;
+        aligned = aligned_;
+        em = em_;
+        if (em) {
+            const int64_t units = per / gran;
+            ra = (int)(units * blockIdx.x / gridDim.x) * gran;
+            rb = blockIdx.x + 1 == gridDim.x ? per : (int)(units * (blockIdx.x + 1) / gridDim.x) * gran;
+            slot = 0;
+            r = ra;
+            v = 0;
+            end = (V / per) * (rb - ra);
+            return;
+        }
         int64_t a, b;
         if (per_ % most_ == 0) { // whole chunks: the CTAs' shares differ by one chunk at most, none is partial
             trx_cta_range(V / most_, a, b);
@@ -99,20 +119,24 @@ struct TrxWalk {
         }
         v = (int)a;
         end = (int)b;
-        per = per_;
-        most = most_;
-        aligned = aligned_;
+        ra = 0;
+        rb = per;
         slot = v / per;
         r = v - slot * per;
     }
     __device__ bool more() const { return v < end; }
-    __device__ int n() const { return min(min(aligned ? most - r % most : most, end - v), per - r); }
+    __device__ int n() const {
+        if (em) return min(most, rb - r);
+        return min(min(aligned ? most - r % most : most, end - v), per - r);
+    }
+    // whether the current chunk is the CTA's last of its expert
+    __device__ bool seg_end() const { return r + n() == rb || v + n() == end; }
     __device__ void next() {
         const int k = n();
         v += k;
         r += k;
-        if (r == per) {
-            r = 0;
+        if (r == rb) {
+            r = ra;
             slot++;
         }
     }
@@ -127,10 +151,21 @@ struct TrxFusedSmem {
 
 #define TRX_FU_SEG_MAX 4 // tokens up to which a CTA keeps its h values in shared memory and publishes once an expert
 
-// the most gate/up rows one CTA of `grid` takes (whole chunks)
+// the most gate/up rows one CTA of `grid` takes (whole chunks, or its rows of every expert)
 __host__ __device__ inline int trx_fu_rows_g(int E, int k, int T, int F, int grid) {
     const int act = E < T * k ? E : T * k, units = act * F / TRX_GU_CHUNK;
-    return (units + grid - 1) / grid * TRX_GU_CHUNK;
+    const int whole = (units + grid - 1) / grid * TRX_GU_CHUNK, em = act * ((F + grid - 1) / grid + 1);
+    return whole > em ? whole : em;
+}
+
+// short calls: the row granularity of the expert-major down walk (its chunks' Q6_K d values are whole 16-byte
+// pieces), and the most down rows a CTA takes of one expert
+__host__ __device__ inline int trx_fu_dn_gran(int down_type, int F) {
+    return down_type == TRX_Q6_K && F / 256 < 8 ? 8 / (F / 256) : 1;
+}
+__host__ __device__ inline int trx_fu_rows_d(int down_type, int H, int F, int grid) {
+    const int g = trx_fu_dn_gran(down_type, F);
+    return (H / g + grid - 1) / grid * g + g;
 }
 
 
@@ -144,14 +179,19 @@ __host__ __device__ inline TrxFusedSmem trx_fused_layout(int gate_type, int down
     l.gu_stage = (size_t)2 * TRX_GU_CHUNK * rbg;
     // Q6_K: the rows' f16 d values (stored after all rows of the matrix) come with them, the 16-row block's
     l.dn_stage = (size_t)TRX_DN_CHUNK * rbd + (down_type == TRX_Q6_K ? (size_t)TRX_DN_CHUNK * (F / 256) * 2 : 0);
+    // short calls: the h rows of the chunk's expert come with its weights (not for the Q4_K down, which reads its
+    // prepared inputs from L2)
+    if (T <= TRX_FU_SEG_MAX && down_type != TRX_Q4_K) l.dn_stage += (size_t)T * F * 4;
     size_t stages = sg * l.gu_stage + sd * l.dn_stage;
     const size_t router = (size_t)(1 + (T < TRX_TOK_STAGE ? T : TRX_TOK_STAGE)) * H * 4;
     if (router > stages) stages = router;
     l.bars = trx_align128(stages);
     l.meta = trx_align128(l.bars + 8 * 4 * TRX_FU_MAXST);
     l.seg = trx_align128(l.meta + (size_t)T * k * 16);
-    const size_t seg_bytes =
-        T <= TRX_FU_SEG_MAX ? ((size_t)2 * trx_fu_rows_g(E, k, T, F, grid) + (size_t)sd * TRX_DN_CHUNK) * T * 4 : 0;
+    // short calls: (g, u) of the CTA's gate/up rows, then h3 of its down rows for every grouped row
+    const size_t seg_bytes = T <= TRX_FU_SEG_MAX ? (size_t)2 * trx_fu_rows_g(E, k, T, F, grid) * T * 4 +
+                                                       (size_t)T * k * trx_fu_rows_d(down_type, H, F, grid) * 4
+                                                 : 0;
     l.tok = trx_align128(l.seg + seg_bytes);
     l.tok_bytes = gate_type == TRX_Q4_K ? trx_align128((size_t)H * 4 + (size_t)(H / 32 + H / 256) * 8) : (size_t)H * 4;
     l.total = l.tok + (size_t)T * l.tok_bytes;
@@ -170,7 +210,8 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ int s_active[TRX_MAX_EXPERTS], s_off[TRX_MAX_EXPERTS + 1], s_nact, s_flag;
     __shared__ int s_pact[TRX_MAX_EXPERTS]; // the producer's copy of the active experts
-    __shared__ __align__(16) float sp[TRX_FU_CWARPS + 1][96]; // per-warp scratch (16-byte aligned rows)
+    __shared__ __align__(16) float sp[TRX_FU_CWARPS + 2][96]; // per-warp scratch (16-byte aligned rows)
+    __shared__ int s_armed; // down chunks whose stage the producer has armed (read by the h-copy warp)
     __shared__ int scnt[64];
     __shared__ uint32_t s_gcnt[TRX_FU_MAXST], s_dcnt[TRX_FU_MAXST];
     constexpr int CHG = TRX_GU_CHUNK, CHD = TRX_DN_CHUNK;
@@ -200,6 +241,7 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
     int *s_selid = s_place + R;
     uint8_t *s_tok = smem + lay.tok;
     if (tid < TRX_FU_MAXST) s_gcnt[tid] = s_dcnt[tid] = 0u;
+    if (tid == 0) s_armed = 0;
     const int nsb_g = H / 256;
     if (tid == 0) { // the pipelines' barriers (their region is not scratch for the routing phase)
         for (int s = 0; s < SG; s++) {
@@ -213,12 +255,24 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
         trx_fence_barrier_init();
     }
     if (warp == 1) trx_expf_prefetch(lane); // the softmax's table, before the routing needs it
-    // The producer warp mixes 16-row block blockIdx.x (below); for short calls its residual values are read now,
-    // so that the read (from host memory, in the host-pointer road) is over long before the mix
-    const bool xpre_ok = T * CHD <= 32 && (int)blockIdx.x < H / CHD;
-    float xpre = 0.0f;
-    if (xpre_ok && warp == TRX_FU_CWARPS && lane < T * CHD)
-        xpre = x_io[(int64_t)(lane / CHD) * H + (int64_t)blockIdx.x * CHD + lane % CHD];
+    // Short calls: the producer warp mixes this CTA's down rows [mra, mrb) of every token (below); their residual
+    // values are read now, so that the read (from host memory, in the host-pointer road) is over long before the mix
+    const bool seg = T <= TRX_FU_SEG_MAX;
+    const int dgran = trx_fu_dn_gran(DT, F), nrmax = trx_fu_rows_d(DT, H, F, gridDim.x);
+    int mra, mrb;
+    {
+        TrxWalk mw;
+        mw.init(H, H, CHD, true, true, dgran);
+        mra = mw.ra;
+        mrb = mw.rb;
+    }
+    float xpre[2] = {0.0f, 0.0f};
+    if (seg && warp == TRX_FU_CWARPS)
+#pragma unroll
+        for (int q = 0; q < 2; q++) {
+            const int i = lane + 32 * q, nr = mrb - mra;
+            if (i < nr * T) xpre[q] = x_io[(int64_t)(i / nr) * H + mra + i % nr];
+        }
 
     {
         // ---------------- phase A: CTAs 0..E-1 the logits of one expert each; the tokens' prepared inputs either
@@ -243,7 +297,7 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
         }
         if (lprep && warp >= w0) {
             if (GT == TRX_Q4_K) {
-                for (int q = warp - w0; q < T * nsb_g; q += TRX_FU_CWARPS + 1 - w0) {
+                for (int q = warp - w0; q < T * nsb_g; q += TRX_FU_CWARPS + 2 - w0) {
                     const int t = q / nsb_g, s4 = q % nsb_g;
                     uint8_t *tok = s_tok + t * lay.tok_bytes;
                     double *bfd = reinterpret_cast<double *>(tok + (size_t)H * 4);
@@ -299,7 +353,7 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
         __syncthreads();
         TRX_CYC(54);
         const long long c1 = clock64();
-        for (int t = warp; t < T; t += TRX_FU_CWARPS + 1)
+        for (int t = warp; t < T; t += TRX_FU_CWARPS + 2)
             trx_route_token<true>(slog + t * E, E, k, S.norm_topk, lane, sp[warp], s_selid + t * k, s_selw + t * k);
         if (w.trace != nullptr && tid == 0) w.trace[(size_t)blockIdx.x * 64 + 7] = (uint64_t)(clock64() - c1);
         trx_fence_proxy_async(); // the routing's writes to the stage area, before the copies that land there
@@ -329,7 +383,7 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
         if (m0 >> lane & 1u) s_pact[__popc(m0 & lt)] = lane;
         if (m1 >> lane & 1u) s_pact[__popc(m0) + __popc(m1 & lt)] = lane + 32;
         __syncwarp();
-    } else {
+    } else if (warp < TRX_FU_CWARPS) {
         const int ctid = tid; // 0..255
         if (warp == 0) {
             const bool out = blockIdx.x == 0;
@@ -367,7 +421,7 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
             }
         }
         asm volatile("bar.sync 1, %0;" ::"n"(32 * TRX_FU_CWARPS) : "memory");        // the consumers: sorted
-        asm volatile("bar.arrive 2, %0;" ::"n"(32 * (TRX_FU_CWARPS + 1)) : "memory"); // tell the producer
+        asm volatile("bar.arrive 2, %0;" ::"n"(TRX_FU_THREADS) : "memory");          // tell the producer
         n_act = s_nact;
         TRX_TRACE(2);
         TRX_CYC(58);
@@ -379,10 +433,14 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
     // chunk h = silu(g) u, one row a lane, written out, and one device-scope fence and count per expert segment of
     // this CTA; per down chunk h3 written out, one fence and count, and the mix of a 16-row block when its count
     // completes. Longer calls: the consumers finish and publish themselves, chunk by chunk.
-    const bool seg = T <= TRX_FU_SEG_MAX;
-    float2 *sgu = reinterpret_cast<float2 *>(smem + lay.seg); // [row of the CTA's gate/up range][token]: (g, u)
-    float *sh3 = reinterpret_cast<float *>(sgu + (size_t)trx_fu_rows_g(E, k, T, F, gridDim.x) * T); // [stage][row][token]
-    // the mix of a completed 16-row block (one warp): every token's k outputs in increasing expert id, then the residual
+    float2 *sgu = reinterpret_cast<float2 *>(smem + lay.seg); // [row of the CTA's gate/up rows][token]: (g, u)
+    float *sh3 = reinterpret_cast<float *>(sgu + (size_t)trx_fu_rows_g(E, k, T, F, gridDim.x) * T); // [grouped row][row]
+    // short calls, Q8_0 / Q6_K down: the chunk's h rows come into the stage (after the weights and d values)
+    const bool hcopy = seg && DT != TRX_Q4_K;
+    const int hoff = TRX_DN_CHUNK * rbd + (DT == TRX_Q6_K ? TRX_DN_CHUNK * nsb_d * 2 : 0);
+    const uint32_t need = (uint32_t)F + (DT == TRX_Q4_K ? 1u : 0u); // an expert's count once its h is complete
+    // longer calls: the mix of a completed 16-row block (one warp): every token's k outputs in increasing expert id,
+    // then the residual
     auto combine = [&](int blk) {
         __threadfence();
         for (int i = lane; i < T * CHD; i += 32) {
@@ -393,8 +451,7 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
                 out = __fadd_rn(out, __fmul_rn(s_selw[jj], __ldcg(w.h3 + (int64_t)s_place[jj] * H + dd)));
             }
             if (ffn_out) ffn_out[(int64_t)t * H + dd] = out;
-            const float xv = xpre_ok && blk == (int)blockIdx.x ? xpre : x_io[(int64_t)t * H + dd];
-            x_io[(int64_t)t * H + dd] = __fadd_rn(xv, out);
+            x_io[(int64_t)t * H + dd] = __fadd_rn(x_io[(int64_t)t * H + dd], out);
         }
         if (lane == 0) w.comb_cnt[blk] = 0u;
     };
@@ -403,8 +460,8 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
         // ---------------- the producer: every chunk of this CTA, in consumption order (the copies by lane 0; the
         // publication by the whole warp)
         TrxWalk gw, dw; // the next chunk to copy
-        gw.init(n_act * F, F, CHG, false);
-        dw.init(n_act * H, H, CHD, true);
+        gw.init(n_act * F, F, CHG, false, seg);
+        dw.init(n_act * H, H, CHD, true, seg, dgran);
         auto issue_g = [&](int s) {
             if (lane == 0) {
                 const int e = s_pact[gw.slot], n = gw.n();
@@ -414,31 +471,35 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
                 trx_bulk_g2s(dst + gu_half, L.up + e * L.up_mb + (int64_t)gw.r * rbg, n * rbg, &full_g[s]);
             }
         };
+        // a down chunk's weights and Q6_K d values (those of its rows: the expert-major chunks start and end on
+        // whole 16-byte pieces of them; else those of its 16-row block); with hcopy the stage also waits for the
+        // expert's h rows, copied by the h-copy warp once the expert is complete
         auto issue_d = [&](int s) {
             if (lane == 0) {
-                const int e = s_pact[dw.slot], n = dw.n();
-                const int dbytes = DT == TRX_Q6_K ? CHD * nsb_d * 2 : 0; // 16-byte multiple, 16-byte aligned
-                trx_mbar_expect_tx(&full_d[s], (uint32_t)(n * rbd + dbytes));
+                const int e = s_active[dw.slot], n = dw.n();
+                const int drow = seg ? dw.r : dw.r / CHD * CHD, dbytes = DT == TRX_Q6_K ? (seg ? n : CHD) * nsb_d * 2 : 0;
+                const int hbytes = hcopy ? (s_off[e + 1] - s_off[e]) * F * 4 : 0;
+                trx_mbar_expect_tx(&full_d[s], (uint32_t)(n * rbd + dbytes + hbytes));
                 trx_bulk_g2s(dn_buf + s * lay.dn_stage, L.down + e * L.down_mb + (int64_t)dw.r * rbd, n * rbd, &full_d[s]);
                 if (DT == TRX_Q6_K)
                     trx_bulk_g2s(dn_buf + s * lay.dn_stage + CHD * rbd,
-                                 L.down + e * L.down_mb + (int64_t)H * rbd + (int64_t)(dw.r / CHD) * CHD * nsb_d * 2, dbytes,
-                                 &full_d[s]);
+                                 L.down + e * L.down_mb + (int64_t)H * rbd + (int64_t)drow * nsb_d * 2, dbytes, &full_d[s]);
             }
         };
         auto wait_all = [&](uint64_t *bar, int parity) {
             return __all_sync(0xffffffffu, trx_mbar_wait(bar, parity, TRX_WAIT_NS));
         };
         for (; issued_g < SG && gw.more(); issued_g++, gw.next()) issue_g(issued_g);
-        asm volatile("bar.sync 2, %0;" ::"n"(32 * (TRX_FU_CWARPS + 1)) : "memory"); // the routing is sorted
+        asm volatile("bar.sync 2, %0;" ::"n"(TRX_FU_THREADS) : "memory"); // the routing is sorted
         // the down weights only after this CTA's first gate/up stages have landed: every CTA's gate/up data then
         // comes first out of HBM, and the down data streams while the gate/up rows are multiplied
         for (int q = 0; q < issued_g && !failed; q++)
             if (!wait_all(&full_g[q], 0)) failed = true;
         for (; !failed && issued_d < SD && dw.more(); issued_d++, dw.next()) issue_d(issued_d);
+        if (lane == 0) *(volatile int *)&s_armed = issued_d;
         // gate/up chunks in order: wait for the consumers, publish (seg), refill the stage
         TrxWalk pw;
-        pw.init(n_act * F, F, CHG, false);
+        pw.init(n_act * F, F, CHG, false, seg);
         const int gv0 = pw.v;
         int seg_v0 = pw.v, seg_slot = pw.slot;
         for (int j = 0; !failed && pw.more(); j++, pw.next()) {
@@ -459,7 +520,7 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
                     w.h[(int64_t)(p0 + pp) * F + (DT != TRX_Q4_K ? trx_lc_pos(r) : r)] = trx_silu_mul(gu.x, gu.y);
                 }
             }
-            if (seg && (pw.r + n == F || pw.v + n == pw.end)) { // this chunk ends the CTA's segment of the expert
+            if (seg && pw.seg_end()) { // this chunk ends the CTA's segment of the expert
                 const int e = s_active[slot], p0 = s_off[e], np = s_off[e + 1] - p0, rows = pw.v + n - seg_v0;
                 __syncwarp();
                 uint32_t old = 0;
@@ -491,47 +552,90 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
             }
         }
         if (w.trace != nullptr && lane == 0) w.trace[(size_t)blockIdx.x * 64 + 59] = trx_globaltimer(); // h published
-        // down chunks in order: wait for the consumers, publish and mix (seg), refill the stage
+        // down chunks in order: their h rows copied (short calls), wait for the consumers, refill the stage
         TrxWalk pd;
-        pd.init(n_act * H, H, CHD, true);
+        pd.init(n_act * H, H, CHD, true, seg, dgran);
         int n_mix = 0; // the blocks this CTA mixed (for the timeline)
         for (int j = 0; !failed && pd.more(); j++, pd.next()) {
-            const int s = j % SD, n = pd.n(), d0 = pd.r;
+            const int s = j % SD;
             if (!wait_all(&empty_d[s], (j / SD) & 1)) {
                 failed = true;
                 break;
-            }
-            if (seg) {
-                const int e = s_active[pd.slot], p0 = s_off[e], np = s_off[e + 1] - p0;
-                for (int i = lane; i < n * np; i += 32)
-                    w.h3[(int64_t)(p0 + i % np) * H + d0 + i / np] = sh3[((size_t)s * CHD + i / np) * T + i % np];
-                __syncwarp();
-                if (lane == 0) {
-                    __threadfence();
-                    atomicAdd(&w.comb_cnt[d0 / CHD], (uint32_t)n);
-                }
             }
             if (dw.more()) {
                 issue_d(s);
                 issued_d++;
                 dw.next();
+                if (lane == 0) *(volatile int *)&s_armed = issued_d;
             }
         }
-        // the mixes: 16-row block b is mixed by CTA b mod grid once all its rows are counted (the mixing spread over
-        // the CTAs, none of them waiting for a block before its own rows are out)
-        for (int blk = blockIdx.x; !failed && blk < H / CHD; blk += gridDim.x) {
-            bool ok = true;
-            if (lane == 0) ok = trx_spin(&w.comb_cnt[blk], (uint32_t)(n_act * CHD), false);
-            if (!__shfl_sync(0xffffffffu, ok, 0)) {
-                failed = true;
-                break;
+        if (seg) {
+            // the mix of this CTA's rows [mra, mrb) of every token: it holds every expert's outputs for them (the
+            // empties above: every chunk's h3 is in shared memory); the k outputs in increasing expert id, then the
+            // residual (read at the kernel's start)
+            const int nr = mrb - mra;
+            for (int i = lane; !failed && i < nr * T; i += 32) {
+                const int t = i / nr, d = mra + i % nr;
+                float out = 0.0f;
+                for (int sl = 0; sl < k; sl++) {
+                    const int jj = t * k + sl;
+                    out = __fadd_rn(out, __fmul_rn(s_selw[jj], sh3[(size_t)s_place[jj] * nrmax + (d - mra)]));
+                }
+                if (ffn_out) ffn_out[(int64_t)t * H + d] = out;
+                const float xv = i < 32 ? xpre[0] : i < 64 ? xpre[1] : x_io[(int64_t)t * H + d];
+                x_io[(int64_t)t * H + d] = __fadd_rn(xv, out);
             }
-            combine(blk);
-            n_mix++;
+            n_mix = 1;
+        } else {
+            // the mixes: 16-row block b is mixed by CTA b mod grid once all its rows are counted (the mixing spread
+            // over the CTAs, none of them waiting for a block before its own rows are out)
+            for (int blk = blockIdx.x; !failed && blk < H / CHD; blk += gridDim.x) {
+                bool ok = true;
+                if (lane == 0) ok = trx_spin(&w.comb_cnt[blk], (uint32_t)(n_act * CHD), false);
+                if (!__shfl_sync(0xffffffffu, ok, 0)) {
+                    failed = true;
+                    break;
+                }
+                combine(blk);
+                n_mix++;
+            }
         }
         if (w.trace != nullptr && lane == 0) {
             w.trace[(size_t)blockIdx.x * 64 + 50] = trx_globaltimer(); // the producer's publication done
             w.trace[(size_t)blockIdx.x * 64 + 51] = (uint64_t)n_mix;
+        }
+    } else if (warp == TRX_FU_HWARP) {
+        // ---------------- short calls (Q8_0 / Q6_K down): the h rows of each down chunk's expert into its stage, once
+        // the producer has armed the stage for the chunk and the expert is complete (chunks in order; the experts
+        // complete in that order too)
+        asm volatile("bar.sync 2, %0;" ::"n"(TRX_FU_THREADS) : "memory"); // the routing is sorted
+        n_act = s_nact;
+        if (hcopy) {
+            TrxWalk hw;
+            hw.init(n_act * H, H, CHD, true, seg, dgran);
+            for (int j = 0; !failed && hw.more(); j++, hw.next()) {
+                bool ok = true;
+                if (lane == 0) {
+                    uint64_t t0 = 0;
+                    for (int it = 0; *(volatile int *)&s_armed <= j; it++) {
+                        if (it == 0) t0 = trx_globaltimer();
+                        else if (trx_globaltimer() - t0 > TRX_SPIN_NS) {
+                            ok = false;
+                            break;
+                        }
+                        __nanosleep(32);
+                    }
+                    if (ok) ok = trx_spin(&sync->gu_done[hw.slot], need, false);
+                    if (ok) {
+                        const int e = s_active[hw.slot], p0 = s_off[e], s = j % SD;
+                        // the h the count made visible (generic writes of other CTAs), before the bulk copy reads it
+                        asm volatile("fence.proxy.async.global;" ::: "memory");
+                        trx_bulk_g2s(dn_buf + s * lay.dn_stage + hoff, w.h + (int64_t)p0 * F, (s_off[e + 1] - p0) * F * 4,
+                                     &full_d[s]);
+                    }
+                }
+                if (!__shfl_sync(0xffffffffu, ok, 0)) failed = true;
+            }
         }
     } else {
         // ---------------- a consumer warp. The consumers form two groups of TRX_FU_GW warps that take the chunks in
@@ -542,7 +646,7 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
         TrxQ4X X;
         int jg = 0;
         TrxWalk gw;
-        gw.init(n_act * F, F, CHG, false);
+        gw.init(n_act * F, F, CHG, false, seg);
         const int gv0 = gw.v;
         // gate / up / SwiGLU: rows wl and wl + TRX_FU_GW of the group's chunks
         for (; gw.more(); jg++, gw.next()) {
@@ -632,16 +736,15 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
 
         // ---------------- down: half-warp hw = 2 wl + lane / 16 of the group takes rows hw and hw + 8 of its chunks
         cur = -1;
-        const uint32_t need = (uint32_t)F + (DT == TRX_Q4_K ? 1u : 0u);
         int jd = 0, ready = -1; // ready: the last slot whose gate/up rows this warp saw complete
         TrxWalk dw;
-        dw.init(n_act * H, H, CHD, true);
+        dw.init(n_act * H, H, CHD, true, seg, dgran);
         for (; dw.more() && !failed; jd++, dw.next()) {
             if ((jd & 1) != grp) continue;
             const int slot = dw.slot, e = s_active[slot], d0 = dw.r, n = dw.n();
             const int p0 = s_off[e], p1 = s_off[e + 1];
             const int s = jd % SD;
-            if (slot != ready) {
+            if (slot != ready && !hcopy) { // (with hcopy the stage's barrier includes the expert's h rows)
                 bool ok = true;
                 if (lane == 0) ok = trx_spin(&sync->gu_done[slot], need, false);
                 if (!__shfl_sync(0xffffffffu, ok, 0)) {
@@ -661,8 +764,8 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
             const int rac = ra < n ? ra : 0, rbc = rb < n ? rb : 0; // a row past the chunk computes row 0, unstored
             if (2 * wl < n) {
                 const uint8_t *sta = dn_buf + s * lay.dn_stage + rac * rbd, *stb = dn_buf + s * lay.dn_stage + rbc * rbd;
-                const uint8_t *dps = dn_buf + s * lay.dn_stage + CHD * rbd; // the block's Q6_K d values
-                const int da = (d0 + rac) % CHD, db = (d0 + rbc) % CHD;
+                const uint8_t *dps = dn_buf + s * lay.dn_stage + CHD * rbd; // the rows' (or block's) Q6_K d values
+                const int dbase = seg ? 0 : d0 % CHD, da = dbase + rac, db = dbase + rbc;
                 for (int p = p0; p < p1; p++) {
                     float va, vb;
                     if (DT == TRX_Q4_K) {
@@ -675,20 +778,22 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
                         va = trx_q4k_row4<true>(sta, X, lane);
                         vb = trx_q4k_row4<true>(stb, X, lane);
                     } else { // one 256-block an iteration, h through L1 (after the acquire above)
-                        const float2 v = DT == TRX_Q8_0
-                                             ? trx_q8l_dot2(sta, stb, w.h + (int64_t)p * F, nsb_d, lane & 15)
-                                             : trx_q6l_dot2(sta, stb, dps + da * nsb_d * 2, dps + db * nsb_d * 2,
-                                                            w.h + (int64_t)p * F, nsb_d, lane & 15);
+                        const float *hx = hcopy ? reinterpret_cast<const float *>(dn_buf + s * lay.dn_stage + hoff) +
+                                                      (int64_t)(p - p0) * F
+                                                : w.h + (int64_t)p * F;
+                        const float2 v = DT == TRX_Q8_0 ? trx_q8l_dot2(sta, stb, hx, nsb_d, lane & 15)
+                                                        : trx_q6l_dot2(sta, stb, dps + da * nsb_d * 2, dps + db * nsb_d * 2,
+                                                                       hx, nsb_d, lane & 15);
                         va = v.x;
                         vb = v.y;
                     }
                     if ((lane & 15) == 0) {
                         if (ra < n) {
-                            if (seg) sh3[((size_t)s * CHD + ra) * T + (p - p0)] = va;
+                            if (seg) sh3[(size_t)p * nrmax + (d0 - dw.ra) + ra] = va;
                             else w.h3[(int64_t)p * H + d0 + ra] = va;
                         }
                         if (rb < n) {
-                            if (seg) sh3[((size_t)s * CHD + rb) * T + (p - p0)] = vb;
+                            if (seg) sh3[(size_t)p * nrmax + (d0 - dw.ra) + rb] = vb;
                             else w.h3[(int64_t)p * H + d0 + rb] = vb;
                         }
                     }
