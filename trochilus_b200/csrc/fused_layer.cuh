@@ -99,8 +99,8 @@ struct TrxWalk {
         most = most_;
         aligned = aligned_;
         em = em_;
-        if (em) {
-            const int64_t units = per / gran;
+        if (em) { // 32-bit arithmetic: per x grid stays far below 2^32
+            const uint32_t units = (uint32_t)(per / gran);
             ra = (int)(units * blockIdx.x / gridDim.x) * gran;
             rb = blockIdx.x + 1 == gridDim.x ? per : (int)(units * (blockIdx.x + 1) / gridDim.x) * gran;
             slot = 0;
@@ -109,13 +109,13 @@ struct TrxWalk {
             end = (V / per) * (rb - ra);
             return;
         }
-        int64_t a, b;
+        uint32_t a, b; // 32-bit: V x grid stays below 2^32 (V <= 64 x 2048)
+        const uint32_t units = per_ % most_ == 0 ? (uint32_t)(V / most_) : (uint32_t)V; // whole chunks, or rows
+        a = units * blockIdx.x / gridDim.x;
+        b = units * (blockIdx.x + 1) / gridDim.x;
         if (per_ % most_ == 0) { // whole chunks: the CTAs' shares differ by one chunk at most, none is partial
-            trx_cta_range(V / most_, a, b);
             a *= most_;
             b *= most_;
-        } else {
-            trx_cta_range(V, a, b);
         }
         v = (int)a;
         end = (int)b;
@@ -223,11 +223,6 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
     do {                                                                                                               \
         if (w.trace != nullptr && threadIdx.x == 0) w.trace[(size_t)blockIdx.x * 64 + (slot)] = clock64() - ck0;      \
     } while (0)
-    if (w.trace != nullptr && tid == 0) {
-        uint32_t smid;
-        asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
-        w.trace[(size_t)blockIdx.x * 64 + 49] = smid; // the SM this CTA runs on (not a time)
-    }
     const int rbg = GT == TRX_Q4_K ? H / 256 * 144 : H / 32 * 34;
     const int rbd = DT == TRX_Q4_K ? nsb_d * 144 : DT == TRX_Q6_K ? nsb_d * 208 : F / 32 * 34;
     const TrxFusedSmem lay = trx_fused_layout(GT, DT, H, F, T, k, SG, SD, E, gridDim.x);
@@ -367,6 +362,7 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
     const bool lprep = T <= TRX_FU_LOCAL_PREP;
     int n_act;
     if (warp == TRX_FU_CWARPS) {
+        if (w.trace != nullptr && lane == 0) w.trace[(size_t)blockIdx.x * 64 + 49] = trx_globaltimer(); // producer on
         uint32_t m0 = 0, m1 = 0; // the selected experts as a 64-bit set
         for (int j = lane; j < R; j += 32) {
             const int e = s_selid[j];
@@ -383,6 +379,7 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
         if (m0 >> lane & 1u) s_pact[__popc(m0 & lt)] = lane;
         if (m1 >> lane & 1u) s_pact[__popc(m0) + __popc(m1 & lt)] = lane + 32;
         __syncwarp();
+        if (w.trace != nullptr && lane == 0) w.trace[(size_t)blockIdx.x * 64 + 61] = trx_globaltimer(); // mask done
     } else if (warp < TRX_FU_CWARPS) {
         const int ctid = tid; // 0..255
         if (warp == 0) {
@@ -489,7 +486,9 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
         auto wait_all = [&](uint64_t *bar, int parity) {
             return __all_sync(0xffffffffu, trx_mbar_wait(bar, parity, TRX_WAIT_NS));
         };
+        if (w.trace != nullptr && lane == 0) w.trace[(size_t)blockIdx.x * 64 + 51] = trx_globaltimer(); // walks set
         for (; issued_g < SG && gw.more(); issued_g++, gw.next()) issue_g(issued_g);
+        if (w.trace != nullptr && lane == 0) w.trace[(size_t)blockIdx.x * 64 + 3] = trx_globaltimer(); // copies out
         asm volatile("bar.sync 2, %0;" ::"n"(TRX_FU_THREADS) : "memory"); // the routing is sorted
         // the down weights only after this CTA's first gate/up stages have landed: every CTA's gate/up data then
         // comes first out of HBM, and the down data streams while the gate/up rows are multiplied
@@ -602,7 +601,6 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
         }
         if (w.trace != nullptr && lane == 0) {
             w.trace[(size_t)blockIdx.x * 64 + 50] = trx_globaltimer(); // the producer's publication done
-            w.trace[(size_t)blockIdx.x * 64 + 51] = (uint64_t)n_mix;
         }
     } else if (warp == TRX_FU_HWARP) {
         // ---------------- short calls (Q8_0 / Q6_K down): the h rows of each down chunk's expert into its stage, once

@@ -24,8 +24,9 @@ def summarize(tr: np.ndarray) -> dict:
         u = (v.astype(np.float64) - float(t0)) / 1000.0
         return {"min": round(float(u.min()), 2), "median": round(float(np.median(u)), 2), "max": round(float(u.max()), 2)}
 
-    names = (("start", 0), ("router_prep_work_done", 62), ("h_published", 59), ("route_done", 60), ("down_expert_ready_w0", 61),
-             ("phase_a_done", 1), ("sorted_w0", 48), ("routing_seen", 2), ("inputs_staged", 3), ("gate_up_done_w0", 4),
+    names = (("start", 0), ("router_prep_work_done", 62), ("h_published", 59), ("route_done", 60), ("producer_mask_done", 61), ("producer_on", 49),
+             ("producer_walks_set", 51), ("producer_first_copies_out", 3),
+             ("phase_a_done", 1), ("sorted_w0", 48), ("routing_seen", 2), ("gate_up_done_w0", 4),
              ("down_first_ready_w0", 5), ("down_done_w0", 6), ("end", 52))
     out = {"ctas": int(tr.shape[0]), **{n: stat(tr[:, slot]) for n, slot in names}}
     med = lambda slot: (stat(tr[:, slot]) or {}).get("median")
