@@ -89,6 +89,22 @@ TRMOE_API int tr_gpu_moe_set_layer(tr_gpu_moe *m, int64_t layer, const void *rou
 TRMOE_API int tr_gpu_moe_layer(tr_gpu_moe *m, int64_t layer, const float *normed, int64_t n_tok, float *x_inout,
                      int64_t *sel_id_out, float *sel_w_out);
 
+/* ffn_norm moved into the hook (the rank-1 next step beyond the MoE block): the FFN sub-block of forward_layer
+ * from its ffn_norm to the mix (src/models/olmoe.c:1834-1933), so that the engine passes the residual stream and
+ * no normed rows cross the host link.
+ * tr_gpu_moe_set_ffn_norm replaces the layer's ffn_norm tensor view (olmoe.c:1836, layer->ffn_norm: n_embd floats)
+ * and the model's epsilon (olmoe.c:556, olmoe.attention.layer_norm_rms_epsilon). 0, or -1 with a message. */
+TRMOE_API int tr_gpu_moe_set_ffn_norm(tr_gpu_moe *m, int64_t layer, const float *weight, float eps, char *err,
+                                      size_t err_len);
+
+/* Replaces: olmoe.c:1834-1933 (norm_body's tr_rmsnorm per token, src/kernels/kernels.c:1351-1360, then the MoE
+ * block as tr_gpu_moe_layer). x_inout: the residual stream, n_tok rows of n_embd, normalised into the layer's
+ * input and then given the layer's output. normed_out (optional): the n_tok normalised rows. Host memory, as
+ * tr_gpu_moe_layer (pinned x: the same in-place road). 0, or -1 with a message (also when the layer has no
+ * ffn_norm weight). */
+TRMOE_API int tr_gpu_moe_ffn(tr_gpu_moe *m, int64_t layer, int64_t n_tok, float *x_inout, float *normed_out,
+                             int64_t *sel_id_out, float *sel_w_out);
+
 /* Optional device outputs of tr_gpu_moe_layer_dev (any field NULL: not written) */
 typedef struct {
     float *logits;      /* [n_tok][n_expert] router logits (after the bias) */
@@ -135,6 +151,12 @@ TRMOE_API int tr_gpu_moe_set_prefill(tr_gpu_moe *m, int64_t min_tokens);
  * stream) and returning without waiting. d_normed and d_x_inout are device pointers. 0, or -1. */
 TRMOE_API int tr_gpu_moe_layer_dev(tr_gpu_moe *m, int64_t layer, const float *d_normed, int64_t n_tok, float *d_x_inout,
                          const tr_gpu_moe_outputs *out, void *stream);
+
+/* tr_gpu_moe_ffn on device pointers, enqueued on `stream` (NULL: the context's own), not waited for: d_x_inout
+ * normalised and given the layer's output; d_normed_out (optional) receives the normalised rows; out as
+ * tr_gpu_moe_layer_dev. */
+TRMOE_API int tr_gpu_moe_ffn_dev(tr_gpu_moe *m, int64_t layer, int64_t n_tok, float *d_x_inout, float *d_normed_out,
+                                 const tr_gpu_moe_outputs *out, void *stream);
 
 /* One part of tr_gpu_moe_layer_dev: 0 route (router, top-k, dispatch, input preparation), 1 gate/up and
  * SwiGLU, 2 the down input's Q4_K preparation (nothing for another down type), 3 down, combine and residual

@@ -252,6 +252,24 @@ void orc_swiglu(float *x, const float *y, int64_t n) {
     }
 }
 
+/* ---- ffn_norm: RMSNorm of one row in place (src/kernels/kernels.c:1351-1360, called per token by norm_body,
+ * src/models/olmoe.c:1360-1366, for the MoE block's input at olmoe.c:1834-1840). The sum of squares is the f32
+ * dot of the row with itself under the lane contract (kernels.c:19-23: each product rounded, then added to lane
+ * k mod 16, the lanes joined by the tree); mean = sumsq / n; inv = 1 / sqrtf(mean + eps) (each step one IEEE
+ * rounding); x[i] = (x[i] * inv) * w[i]. ---- */
+
+void orc_rmsnorm(float *x, const float *w, int64_t n, float eps) {
+    float lane[LANES] = {0};
+    for (int64_t k = 0; k < n; k++) lane[k % LANES] += x[k] * x[k];
+    const float sumsq = lane_tree(lane);
+    const float mean = sumsq / (float)n;
+    const float inv = 1.0f / sqrtf(mean + eps);
+    for (int64_t i = 0; i < n; i++) {
+        const float t = x[i] * inv;
+        x[i] = t * w[i];
+    }
+}
+
 /* ---- routing and dispatch (src/models/olmoe.c:1455-1502, 1850-1861) ---- */
 
 /* probs: T rows of E router logits, softmaxed in place; then k repeated argmaxes (strict >, ties to

@@ -71,6 +71,18 @@ class _Common:
         self._dot_row = f("dot_row")
         self._dot_row.restype = C.c_float
         self._dot_row.argtypes = [C.c_int, C.c_void_p, C.c_void_p, C.c_int64]
+        self._rmsnorm = f("rmsnorm")
+        self._rmsnorm.argtypes = [C.c_void_p, C.c_void_p, C.c_int64, C.c_float]
+
+    def rmsnorm(self, x: np.ndarray, w: np.ndarray, eps: float) -> np.ndarray:
+        """ffn_norm: each row of x (T x n, or one row) normalised by its RMS and scaled by w
+        (src/kernels/kernels.c:1351-1360 per token, as norm_body applies it, src/models/olmoe.c:1360-1366)"""
+        y = np.array(x, dtype=np.float32, copy=True)
+        w = np.ascontiguousarray(w, dtype=np.float32)
+        rows = y.reshape(-1, y.shape[-1])
+        for r in rows:  # a view of y's memory: normalised in place
+            self._rmsnorm(r.ctypes.data, _ptr(w), r.size, eps)
+        return y
 
     def expf(self, x: np.ndarray) -> np.ndarray:
         x = np.ascontiguousarray(x, dtype=np.float32)

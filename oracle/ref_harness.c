@@ -64,6 +64,11 @@ void ref_softmax(float *x, int64_t n) {
     tr_kernels_init();
     tr_softmax(x, n);
 }
+/* the reference's own RMSNorm of one row (src/kernels/kernels.c:1351-1360), as norm_body applies it per token */
+void ref_rmsnorm(float *x, const float *w, int64_t n, float eps) {
+    tr_kernels_init();
+    tr_rmsnorm(x, w, n, eps);
+}
 void ref_swiglu(float *x, const float *y, int64_t n) {
     tr_kernels_init();
     tr_swiglu(NULL, x, y, n);

@@ -128,6 +128,34 @@ def test_softmax_swiglu_pinned(oracle, reflib):
     assert same_bits(oracle.swiglu(x, y), reflib.swiglu(x, y))
 
 
+@pytest.mark.parametrize("tier", ["scalar", "avx2", "avx512"])
+def test_rmsnorm_pinned(oracle, reflib, tier):
+    """ffn_norm (src/kernels/kernels.c:1351-1360): the restatement against the reference's every tier, on rows of
+    several widths and scales, and rows holding zeros, subnormals, huge values, infinities and NaNs"""
+    try:
+        reflib.set_tier(tier)
+    except RuntimeError:
+        pytest.skip(f"tier {tier} not on this CPU")
+    try:
+        rng = np.random.default_rng(9)
+        for n in (16, 64, 100, 2048):
+            for scale in (1e-20, 1e-3, 1.0, 40.0, 1e18):
+                x = (rng.normal(size=(3, n)) * scale).astype(np.float32)
+                w = rng.normal(size=n).astype(np.float32)
+                for eps in (1e-5, 1e-6, 0.0):
+                    assert same_bits(oracle.rmsnorm(x, w, eps), reflib.rmsnorm(x, w, eps)), (n, scale, eps)
+        x = rng.normal(size=(6, 2048)).astype(np.float32)
+        w = rng.normal(size=2048).astype(np.float32)
+        x[0] = 0.0
+        x[1, :64] = np.resize(_special_floats(), 64)
+        x[2, 5] = np.inf
+        x[3, 7] = np.nan
+        x[4] *= 1e-41  # subnormal squares
+        assert same_bits(oracle.rmsnorm(x, w, 1e-5), reflib.rmsnorm(x, w, 1e-5))
+    finally:
+        reflib.set_tier(None)
+
+
 @pytest.mark.parametrize("t", [gb.Q8_0, gb.Q4_K, gb.Q6_K])
 def test_encoders_decode_close(reflib, t):
     """this project's encoders give blocks the reference decodes back to the inputs (within the format's step)"""

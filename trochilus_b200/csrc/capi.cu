@@ -27,6 +27,7 @@
 #include "fused_layer.cuh"
 #include "prefill.cuh"
 #include "ep.cuh"
+#include "ffn_norm.cuh"
 
 namespace {
 
@@ -171,6 +172,10 @@ struct tr_gpu_moe {
     uint32_t epoch = 0;
     // the host-pointer road's completion word: mapped pinned host memory the fused kernel writes its epoch to
     uint32_t *h_done = nullptr, *d_done = nullptr;
+    // ffn_norm (tr_gpu_moe_set_ffn_norm): per layer n_embd weights on the device, the epsilon, whether set
+    float *norm_w = nullptr;
+    std::vector<float> norm_eps;
+    std::vector<int> norm_set;
     bool fused_ok = false;
     float *d_normed = nullptr, *d_x = nullptr;
     int64_t *d_sel_id = nullptr;
@@ -517,6 +522,7 @@ extern "C" void tr_gpu_moe_free(tr_gpu_moe *m) {
     if (m->ep_tab) cudaFree(m->ep_tab);
     if (m->ep_buf) cudaFree(m->ep_buf);
     if (m->h_done) cudaFreeHost(m->h_done);
+    if (m->norm_w) cudaFree(m->norm_w);
     for (auto &es : m->evs)
         for (cudaEvent_t e : es.ev) cudaEventDestroy(e);
     if (m->stream) cudaStreamDestroy(m->stream);
@@ -879,33 +885,44 @@ extern "C" int tr_gpu_moe_layer_part(tr_gpu_moe *m, int64_t layer, int part, con
     return launch_layer(m, layer, d_normed, n_tok, d_x_inout, out, st, part, part);
 }
 
-extern "C" int tr_gpu_moe_layer(tr_gpu_moe *m, int64_t layer, const float *normed, int64_t n_tok, float *x_inout,
-                                int64_t *sel_id_out, float *sel_w_out) {
-    g_err.clear();
-    if (m == nullptr || normed == nullptr || x_inout == nullptr) {
-        set_err("bad arguments to tr_gpu_moe_layer");
+// normed = ffn_norm(x) of layer `layer` for n_tok rows (x: device memory, or pinned host memory mapped in)
+static int launch_ffn_norm(tr_gpu_moe *m, int64_t layer, const float *x, int64_t n_tok, float *normed, cudaStream_t st) {
+    if (layer < 0 || layer >= m->cfg.n_layers || m->norm_w == nullptr || !m->norm_set[(size_t)layer]) {
+        set_err("layer %lld has no ffn_norm weight (tr_gpu_moe_set_ffn_norm)", (long long)layer);
         return -1;
     }
+    const int H = (int)m->cfg.n_embd;
+    trx_k_ffn_norm<<<(unsigned)n_tok, 128, (size_t)H * 4, st>>>(x, m->norm_w + layer * H, m->norm_eps[(size_t)layer], H,
+                                                                normed);
+    return ck(cudaGetLastError(), "ffn_norm launch") ? 0 : -1;
+}
+
+// The host-pointer calls. normed == NULL: the layer's ffn_norm of x first (tr_gpu_moe_ffn).
+static int host_layer(tr_gpu_moe *m, int64_t layer, const float *normed, int64_t n_tok, float *x_inout,
+                      float *normed_out, int64_t *sel_id_out, float *sel_w_out) {
     if (n_tok < 1 || n_tok > m->cfg.max_tokens) {
         set_err("bad token count %lld (max %lld)", (long long)n_tok, (long long)m->cfg.max_tokens);
         return -1;
     }
     if (!ck(cudaSetDevice(m->device), "cudaSetDevice")) return -1;
+    const bool norm = normed == nullptr;
     const size_t xb = (size_t)(n_tok * m->cfg.n_embd) * 4;
     const int64_t R = n_tok * m->cfg.n_used;
     cudaStream_t st = m->stream;
-    // Short calls on pinned x (page-locked, mapped: cudaHostAlloc, cudaHostRegister, torch pin_memory): the fused
-    // kernel reads and writes x in place through its device mapping and posts its epoch to a pinned word once
-    // every output is out; the host polls that word instead of copying x back and synchronising the stream.
+    // Short calls on pinned x (page-locked, mapped: cudaHostAlloc, cudaHostRegister, torch pin_memory): the kernels
+    // read (and the layer writes) x in place through its device mapping, and the layer posts its epoch to a pinned
+    // word once every output is out; the host polls that word instead of copying x back and synchronising the stream.
     cudaPointerAttributes pa{};
-    if (m->h_done && sel_id_out == nullptr && sel_w_out == nullptr && n_tok <= TRX_HOST_ZC_MAX &&
-        takes_fused(m, (int)n_tok) && cudaPointerGetAttributes(&pa, x_inout) == cudaSuccess &&
+    if (m->h_done && sel_id_out == nullptr && sel_w_out == nullptr && normed_out == nullptr &&
+        n_tok <= TRX_HOST_ZC_MAX && takes_fused(m, (int)n_tok) && cudaPointerGetAttributes(&pa, x_inout) == cudaSuccess &&
         pa.type == cudaMemoryTypeHost && pa.devicePointer != nullptr) {
         uint32_t epoch = 0;
-        if (!ck(cudaMemcpyAsync(m->d_normed, normed, xb, cudaMemcpyHostToDevice, st), "copy normed") ||
-            launch_layer(m, layer, m->d_normed, n_tok, (float *)pa.devicePointer, nullptr, st, 0, 3, m->d_done,
-                         &epoch) != 0)
-            return -1;
+        float *xd = (float *)pa.devicePointer;
+        // the ffn_norm reads x from a device copy: one copy-engine transfer beats the kernel's reads over the link
+        const bool in = norm ? ck(cudaMemcpyAsync(m->d_x, x_inout, xb, cudaMemcpyHostToDevice, st), "copy x") &&
+                                   launch_ffn_norm(m, layer, m->d_x, n_tok, m->d_normed, st) == 0
+                             : ck(cudaMemcpyAsync(m->d_normed, normed, xb, cudaMemcpyHostToDevice, st), "copy normed");
+        if (!in || launch_layer(m, layer, m->d_normed, n_tok, xd, nullptr, st, 0, 3, m->d_done, &epoch) != 0) return -1;
         const volatile uint32_t *word = m->h_done;
         const auto t0 = std::chrono::steady_clock::now();
         for (unsigned spins = 1;; spins++) {
@@ -941,10 +958,13 @@ extern "C" int tr_gpu_moe_layer(tr_gpu_moe *m, int64_t layer, const float *norme
         out.sel_id = m->d_sel_id;
         out.sel_w = m->d_sel_w;
     }
-    bool ok = ck(cudaMemcpyAsync(m->d_normed, normed, xb, cudaMemcpyHostToDevice, st), "copy normed") &&
-              ck(cudaMemcpyAsync(m->d_x, x_inout, xb, cudaMemcpyHostToDevice, st), "copy x") &&
+    bool ok = ck(cudaMemcpyAsync(m->d_x, x_inout, xb, cudaMemcpyHostToDevice, st), "copy x") &&
+              (norm ? launch_ffn_norm(m, layer, m->d_x, n_tok, m->d_normed, st) == 0
+                    : ck(cudaMemcpyAsync(m->d_normed, normed, xb, cudaMemcpyHostToDevice, st), "copy normed")) &&
               launch_layer(m, layer, m->d_normed, n_tok, m->d_x, sel ? &out : nullptr, st) == 0 &&
               ck(cudaMemcpyAsync(x_inout, m->d_x, xb, cudaMemcpyDeviceToHost, st), "copy x back");
+    if (ok && normed_out)
+        ok = ck(cudaMemcpyAsync(normed_out, m->d_normed, xb, cudaMemcpyDeviceToHost, st), "copy normed out");
     if (ok && sel_id_out)
         ok = ck(cudaMemcpyAsync(sel_id_out, m->d_sel_id, (size_t)R * 8, cudaMemcpyDeviceToHost, st), "copy sel_id");
     if (ok && sel_w_out)
@@ -958,6 +978,76 @@ extern "C" int tr_gpu_moe_layer(tr_gpu_moe *m, int64_t layer, const float *norme
         ok = false;
     }
     return ok ? 0 : -1;
+}
+
+extern "C" int tr_gpu_moe_layer(tr_gpu_moe *m, int64_t layer, const float *normed, int64_t n_tok, float *x_inout,
+                                int64_t *sel_id_out, float *sel_w_out) {
+    g_err.clear();
+    if (m == nullptr || normed == nullptr || x_inout == nullptr) {
+        set_err("bad arguments to tr_gpu_moe_layer");
+        return -1;
+    }
+    return host_layer(m, layer, normed, n_tok, x_inout, nullptr, sel_id_out, sel_w_out);
+}
+
+// ---------------------------------------------------------------------------------------------
+// ffn_norm fused into the hook (ffn_norm.cuh)
+
+extern "C" int tr_gpu_moe_set_ffn_norm(tr_gpu_moe *m, int64_t layer, const float *weight, float eps, char *err,
+                                       size_t err_len) {
+    g_err.clear();
+    if (m == nullptr || layer < 0 || layer >= m->cfg.n_layers || weight == nullptr || !(eps >= 0.0f)) {
+        set_err("bad arguments to tr_gpu_moe_set_ffn_norm");
+        put_err(err, err_len);
+        return -1;
+    }
+    const int64_t H = m->cfg.n_embd;
+    bool ok = ck(cudaSetDevice(m->device), "cudaSetDevice");
+    if (ok && m->norm_w == nullptr) {
+        ok = ck(cudaMalloc(&m->norm_w, (size_t)(m->cfg.n_layers * H) * 4), "cudaMalloc(ffn_norm)");
+        if (ok) {
+            m->norm_eps.assign((size_t)m->cfg.n_layers, 0.0f);
+            m->norm_set.assign((size_t)m->cfg.n_layers, 0);
+        }
+    }
+    if (ok) ok = ck(cudaMemcpyAsync(m->norm_w + layer * H, weight, (size_t)H * 4, cudaMemcpyHostToDevice, m->stream),
+                    "copy ffn_norm") &&
+                 stream_wait(m->stream);
+    if (!ok) {
+        put_err(err, err_len);
+        return -1;
+    }
+    m->norm_eps[(size_t)layer] = eps;
+    m->norm_set[(size_t)layer] = 1;
+    return 0;
+}
+
+extern "C" int tr_gpu_moe_ffn(tr_gpu_moe *m, int64_t layer, int64_t n_tok, float *x_inout, float *normed_out,
+                              int64_t *sel_id_out, float *sel_w_out) {
+    g_err.clear();
+    if (m == nullptr || x_inout == nullptr) {
+        set_err("bad arguments to tr_gpu_moe_ffn");
+        return -1;
+    }
+    return host_layer(m, layer, nullptr, n_tok, x_inout, normed_out, sel_id_out, sel_w_out);
+}
+
+extern "C" int tr_gpu_moe_ffn_dev(tr_gpu_moe *m, int64_t layer, int64_t n_tok, float *d_x_inout, float *d_normed_out,
+                                  const tr_gpu_moe_outputs *out, void *stream) {
+    g_err.clear();
+    if (m == nullptr || d_x_inout == nullptr) {
+        set_err("bad arguments to tr_gpu_moe_ffn_dev");
+        return -1;
+    }
+    if (n_tok < 1 || n_tok > m->cfg.max_tokens) {
+        set_err("bad token count %lld (max %lld)", (long long)n_tok, (long long)m->cfg.max_tokens);
+        return -1;
+    }
+    if (!ck(cudaSetDevice(m->device), "cudaSetDevice")) return -1;
+    cudaStream_t st = stream ? (cudaStream_t)stream : m->stream;
+    float *nb = d_normed_out ? d_normed_out : m->d_normed;
+    if (launch_ffn_norm(m, layer, d_x_inout, n_tok, nb, st) != 0) return -1;
+    return launch_layer(m, layer, nb, n_tok, d_x_inout, out, st);
 }
 
 // ---------------------------------------------------------------------------------------------

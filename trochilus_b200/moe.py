@@ -26,7 +26,8 @@ EXPORTS = ["tr_gpu_moe_create", "tr_gpu_moe_free", "tr_gpu_moe_bytes", "tr_gpu_m
            "tr_gpu_moe_check", "tr_gpu_moe_layer_part", "tr_gpu_moe_trace",
            "tr_gpu_moe_trace_read", "trmoe_last_error", "tr_matmul", "tr_matmul_grouped",
            "tr_matmul_grouped_s", "tr_softmax", "tr_swiglu", "trmoe_kernel_cache_clear", "tr_matmul_q4k_noalloc",
-           "tr_gpu_moe_set_prefill", "tr_gpu_moe_ep_pack", "tr_gpu_moe_experts_dev", "tr_gpu_moe_ep_combine"]
+           "tr_gpu_moe_set_prefill", "tr_gpu_moe_ep_pack", "tr_gpu_moe_experts_dev", "tr_gpu_moe_ep_combine",
+           "tr_gpu_moe_set_ffn_norm", "tr_gpu_moe_ffn", "tr_gpu_moe_ffn_dev"]
 
 
 class Config(C.Structure):
@@ -66,6 +67,10 @@ def lib():
     L.tr_gpu_moe_layer_dev.argtypes = [C.c_void_p, C.c_int64, C.c_void_p, C.c_int64, C.c_void_p,
                                        C.POINTER(Outputs), C.c_void_p]
     L.tr_gpu_moe_launches.argtypes = [C.c_void_p, C.c_int64]
+    L.tr_gpu_moe_set_ffn_norm.argtypes = [C.c_void_p, C.c_int64, C.c_void_p, C.c_float, C.c_char_p, C.c_size_t]
+    L.tr_gpu_moe_ffn.argtypes = [C.c_void_p, C.c_int64, C.c_int64, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]
+    L.tr_gpu_moe_ffn_dev.argtypes = [C.c_void_p, C.c_int64, C.c_int64, C.c_void_p, C.c_void_p, C.POINTER(Outputs),
+                                     C.c_void_p]
     L.tr_gpu_moe_set_prefill.argtypes = [C.c_void_p, C.c_int64]
     L.tr_gpu_moe_ep_pack.argtypes = [C.c_void_p, C.c_void_p, C.c_int64, C.c_int32, C.c_int64, C.c_void_p, C.c_void_p,
                                      C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]
@@ -145,6 +150,41 @@ class GpuMoe:
         if rc != 0:
             raise RuntimeError(f"tr_gpu_moe_layer: {last_error()}")
         return (sid, sw) if want_sel else None
+
+    def set_ffn_norm(self, layer: int, weight: np.ndarray, eps: float):
+        """tr_gpu_moe_set_ffn_norm: the layer's ffn_norm weight (n_embd floats) and the model's RMS epsilon."""
+        weight = np.ascontiguousarray(weight, dtype=np.float32)
+        assert weight.size == self.cfg.n_embd
+        err = C.create_string_buffer(512)
+        if lib().tr_gpu_moe_set_ffn_norm(self.h, layer, _p(weight), eps, err, 512) != 0:
+            raise RuntimeError(f"tr_gpu_moe_set_ffn_norm: {err.value.decode()}")
+
+    def ffn(self, layer: int, x: np.ndarray, want_normed: bool = False, want_sel: bool = False):
+        """tr_gpu_moe_ffn on host arrays: x (T x n_embd, float32, C order) normalised by the layer's ffn_norm and
+        given the layer's output in place; returns (normed or None, sel_id or None, sel_w or None)."""
+        assert x.dtype == np.float32 and x.flags.c_contiguous
+        T = x.shape[0]
+        nrm = np.zeros_like(x) if want_normed else None
+        sid = np.zeros((T, self.cfg.n_used), np.int64) if want_sel else None
+        sw = np.zeros((T, self.cfg.n_used), np.float32) if want_sel else None
+        if lib().tr_gpu_moe_ffn(self.h, layer, T, _p(x), _p(nrm), _p(sid), _p(sw)) != 0:
+            raise RuntimeError(f"tr_gpu_moe_ffn: {last_error()}")
+        return nrm, sid, sw
+
+    def ffn_ptrs(self, layer: int, n_tok: int, x_ptr: int, host: bool, normed_ptr: int | None = None,
+                 outs: dict | None = None, stream: int = 0):
+        """Raw-pointer forms: host=True tr_gpu_moe_ffn (host memory, e.g. pinned), else tr_gpu_moe_ffn_dev (device
+        pointers, enqueued on `stream`)."""
+        if host:
+            rc = lib().tr_gpu_moe_ffn(self.h, layer, n_tok, x_ptr, normed_ptr, None, None)
+        else:
+            o = None
+            if outs:
+                o = Outputs(*(outs.get(k) for k in ("logits", "sel_id", "sel_w", "offsets", "place", "ffn_out")))
+            rc = lib().tr_gpu_moe_ffn_dev(self.h, layer, n_tok, x_ptr, normed_ptr, C.byref(o) if o else None,
+                                          stream or None)
+        if rc != 0:
+            raise RuntimeError(f"tr_gpu_moe_ffn: {last_error()}")
 
     def layer_ptrs(self, layer: int, normed_ptr: int, n_tok: int, x_ptr: int, host: bool):
         """Raw-pointer form of layer() for pinned host buffers (host=True) or device buffers (host=False, on the
