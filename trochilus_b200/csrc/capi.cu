@@ -747,11 +747,17 @@ static bool takes_fused(const tr_gpu_moe *m, int T) {
            (int)m->cfg.n_expert + T <= m->grid_fused && fused_stages(m, T, &sg, &sd);
 }
 
+static int launch_ffn_norm(tr_gpu_moe *m, int64_t layer, const float *x, int64_t n_tok, float *normed, cudaStream_t st);
+
 // done: when the fused kernel takes the call, the device address of the word it writes its epoch to when every
-// output is out (*epoch_out: that epoch)
+// output is out (*epoch_out: that epoch).
+// norm_src (the ffn_norm in the hook): the call's input rows are these residual rows (device memory), normalised
+// first: inside the fused kernel for short calls, else by trx_k_ffn_norm into d_normed; normed_out (optional)
+// receives the normalised rows.
 static int launch_layer(tr_gpu_moe *m, int64_t layer, const float *d_normed, int64_t n_tok, float *d_x,
                         const tr_gpu_moe_outputs *out, cudaStream_t st, int first = 0, int last = 3,
-                        uint32_t *done = nullptr, uint32_t *epoch_out = nullptr) {
+                        uint32_t *done = nullptr, uint32_t *epoch_out = nullptr, const float *norm_src = nullptr,
+                        float *normed_out = nullptr) {
     const tr_gpu_moe_config &c = m->cfg;
     if (layer < 0 || layer >= c.n_layers || !m->layer_set[(size_t)layer]) {
         set_err("layer %lld is not set", (long long)layer);
@@ -765,8 +771,16 @@ static int launch_layer(tr_gpu_moe *m, int64_t layer, const float *d_normed, int
         set_err("bad part range %d..%d", first, last);
         return -1;
     }
-    const TrxLayer &L = m->layers[(size_t)layer];
-    TrxShape S{(int)c.n_expert, (int)c.n_used, (int)c.n_embd, (int)c.n_ff, (int)c.norm_topk};
+    TrxLayer L = m->layers[(size_t)layer];
+    TrxShape S{(int)c.n_expert, (int)c.n_used, (int)c.n_embd, (int)c.n_ff, (int)c.norm_topk, 0};
+    if (norm_src) {
+        if (m->norm_w == nullptr || !m->norm_set[(size_t)layer]) {
+            set_err("layer %lld has no ffn_norm weight (tr_gpu_moe_set_ffn_norm)", (long long)layer);
+            return -1;
+        }
+        L.norm_w = m->norm_w + layer * c.n_embd;
+        L.norm_eps = m->norm_eps[(size_t)layer];
+    }
     TrxWork w = m->work;
     w.trace = m->trace;
     if (out) {
@@ -791,11 +805,28 @@ static int launch_layer(tr_gpu_moe *m, int64_t layer, const float *d_normed, int
         for (int z = 0; z < TRMOE_ZONES; z++) es->used[z] = true;
         es->used[2] = c.down_type == TRX_Q4_K;
     }
+    int sg = 0, sd = 0;
+    const bool fused = first == 0 && last == 3 && !(m->pf_ok && m->pf_min > 0 && T >= m->pf_min) && m->fused_ok &&
+                       T <= TRX_ROUTE_FUSED_MAX && E + T <= m->grid_fused && !es && fused_stages(m, T, &sg, &sd);
+    if (norm_src) {
+        // short fused calls normalise inside the kernel when the rows fit the stage area beside the router's staging
+        const bool inside =
+            fused && T <= TRX_FU_LOCAL_PREP && ((uintptr_t)norm_src & 15) == 0 &&
+            trx_fu_norm_off(T, S.H, E) + (size_t)T * S.H * 4 <=
+                trx_fused_layout(c.gate_type, c.down_type, S.H, S.F, T, S.k, sg, sd, E, m->grid_fused).bars;
+        if (inside) {
+            S.norm_in = 1;
+            d_normed = norm_src;
+            w.out_normed = normed_out;
+        } else {
+            float *nb = normed_out ? normed_out : m->d_normed;
+            if (launch_ffn_norm(m, layer, norm_src, n_tok, nb, st) != 0) return -1;
+            d_normed = nb;
+        }
+    }
     if (first == 0 && last == 3 && m->pf_ok && m->pf_min > 0 && T >= m->pf_min && !es)
         return launch_prefill(m, L, S, w, d_normed, T, d_x, out ? out->ffn_out : nullptr, st);
-    int sg = 0, sd = 0;
-    if (first == 0 && last == 3 && m->fused_ok && T <= TRX_ROUTE_FUSED_MAX && E + T <= m->grid_fused && !es &&
-        fused_stages(m, T, &sg, &sd)) {
+    if (fused) {
         float *ffn = out ? out->ffn_out : nullptr;
         uint32_t epoch = ++m->epoch & 0x7fffffffu;
         if (epoch == 0) epoch = ++m->epoch & 0x7fffffffu; // 0 is the completion word's initial value
@@ -919,10 +950,12 @@ static int host_layer(tr_gpu_moe *m, int64_t layer, const float *normed, int64_t
         uint32_t epoch = 0;
         float *xd = (float *)pa.devicePointer;
         // the ffn_norm reads x from a device copy: one copy-engine transfer beats the kernel's reads over the link
-        const bool in = norm ? ck(cudaMemcpyAsync(m->d_x, x_inout, xb, cudaMemcpyHostToDevice, st), "copy x") &&
-                                   launch_ffn_norm(m, layer, m->d_x, n_tok, m->d_normed, st) == 0
+        // with the ffn_norm, the norm reads a device copy of x (one copy-engine transfer beats reads over the link)
+        const bool in = norm ? ck(cudaMemcpyAsync(m->d_x, x_inout, xb, cudaMemcpyHostToDevice, st), "copy x")
                              : ck(cudaMemcpyAsync(m->d_normed, normed, xb, cudaMemcpyHostToDevice, st), "copy normed");
-        if (!in || launch_layer(m, layer, m->d_normed, n_tok, xd, nullptr, st, 0, 3, m->d_done, &epoch) != 0) return -1;
+        if (!in || launch_layer(m, layer, m->d_normed, n_tok, xd, nullptr, st, 0, 3, m->d_done, &epoch,
+                                norm ? m->d_x : nullptr) != 0)
+            return -1;
         const volatile uint32_t *word = m->h_done;
         const auto t0 = std::chrono::steady_clock::now();
         for (unsigned spins = 1;; spins++) {
@@ -958,10 +991,12 @@ static int host_layer(tr_gpu_moe *m, int64_t layer, const float *normed, int64_t
         out.sel_id = m->d_sel_id;
         out.sel_w = m->d_sel_w;
     }
+    // (with the ffn_norm the normalised rows go to a buffer of their own: the layer updates d_x while reading them)
+    float *nb = normed_out ? m->d_normed : nullptr;
     bool ok = ck(cudaMemcpyAsync(m->d_x, x_inout, xb, cudaMemcpyHostToDevice, st), "copy x") &&
-              (norm ? launch_ffn_norm(m, layer, m->d_x, n_tok, m->d_normed, st) == 0
-                    : ck(cudaMemcpyAsync(m->d_normed, normed, xb, cudaMemcpyHostToDevice, st), "copy normed")) &&
-              launch_layer(m, layer, m->d_normed, n_tok, m->d_x, sel ? &out : nullptr, st) == 0 &&
+              (norm || ck(cudaMemcpyAsync(m->d_normed, normed, xb, cudaMemcpyHostToDevice, st), "copy normed")) &&
+              launch_layer(m, layer, m->d_normed, n_tok, m->d_x, sel ? &out : nullptr, st, 0, 3, nullptr, nullptr,
+                           norm ? m->d_x : nullptr, nb) == 0 &&
               ck(cudaMemcpyAsync(x_inout, m->d_x, xb, cudaMemcpyDeviceToHost, st), "copy x back");
     if (ok && normed_out)
         ok = ck(cudaMemcpyAsync(normed_out, m->d_normed, xb, cudaMemcpyDeviceToHost, st), "copy normed out");
@@ -1045,9 +1080,8 @@ extern "C" int tr_gpu_moe_ffn_dev(tr_gpu_moe *m, int64_t layer, int64_t n_tok, f
     }
     if (!ck(cudaSetDevice(m->device), "cudaSetDevice")) return -1;
     cudaStream_t st = stream ? (cudaStream_t)stream : m->stream;
-    float *nb = d_normed_out ? d_normed_out : m->d_normed;
-    if (launch_ffn_norm(m, layer, d_x_inout, n_tok, nb, st) != 0) return -1;
-    return launch_layer(m, layer, nb, n_tok, d_x_inout, out, st);
+    return launch_layer(m, layer, m->d_normed, n_tok, d_x_inout, out, st, 0, 3, nullptr, nullptr, d_x_inout,
+                        d_normed_out);
 }
 
 // ---------------------------------------------------------------------------------------------

@@ -198,6 +198,14 @@ __host__ __device__ inline TrxFusedSmem trx_fused_layout(int gate_type, int down
     return l;
 }
 
+// The routing phase's use of the stage area (free until the barriers): the router's staging ((1 + min(T, 16))
+// rows of H floats), the logits' slot, then the routing warm-up's 4 KB of scratch, then (norm_in) the call's
+// normalised rows. The offset of those rows; the fused norm needs them to end before the barriers.
+__host__ __device__ inline size_t trx_fu_norm_off(int T, int H, int E) {
+    const size_t wscr = trx_align128((size_t)(1 + (T < TRX_TOK_STAGE ? T : TRX_TOK_STAGE)) * H * 4 + (size_t)T * E * 4);
+    return trx_align128(wscr + 4096);
+}
+
 #define TRX_TRACE(slot)                                                                                                \
     do {                                                                                                               \
         if (w.trace != nullptr && threadIdx.x == 0) w.trace[(size_t)blockIdx.x * 64 + (slot)] = trx_globaltimer();     \
@@ -273,6 +281,60 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
         // ---------------- phase A: CTAs 0..E-1 the logits of one expert each; the tokens' prepared inputs either
         // by every CTA for itself into shared memory (T <= TRX_FU_LOCAL_PREP: from normed, while the logits are
         // computed elsewhere) or by CTAs E..E+T-1 into global memory; every CTA that wrote counts itself in (release)
+        // norm_in (short calls, the ffn_norm in the hook): every CTA first normalises the call's residual rows into
+        // its shared memory, warp t token t: the row in, lanes 0-15 the lane contract's sum of squares (tree-joined),
+        // inv = 1 / sqrtf(sumsq / H + eps), then normed = (x inv) w in place (Trochilus's tr_rmsnorm,
+        // src/kernels/kernels.c:1351-1360); CTA 0 also writes them out when asked. The routing phase reads them there.
+        const float *nin = normed;
+        if (S.norm_in) {
+            float *sn = reinterpret_cast<float *>(smem + trx_fu_norm_off(T, H, E));
+            for (int t = warp; t < T; t += TRX_FU_CWARPS + 2) {
+                const float *xr = normed + (int64_t)t * H;
+                float *row = sn + (size_t)t * H;
+                for (int base = 0; base < H; base += 32 * 4 * 8) { // 8 loads a lane in flight
+                    float4 v[8];
+#pragma unroll
+                    for (int j = 0; j < 8; j++) {
+                        const int i = base + (j * 32 + lane) * 4;
+                        v[j] = i < H ? __ldcg(reinterpret_cast<const float4 *>(xr + i)) : make_float4(0.f, 0.f, 0.f, 0.f);
+                    }
+#pragma unroll
+                    for (int j = 0; j < 8; j++) {
+                        const int i = base + (j * 32 + lane) * 4;
+                        if (i < H) *reinterpret_cast<float4 *>(row + i) = v[j];
+                    }
+                }
+                __syncwarp();
+                float acc = 0.0f;
+                if (lane < 16)
+                    for (int kk = lane; kk < H; kk += 16) acc = __fadd_rn(acc, __fmul_rn(row[kk], row[kk]));
+                acc = trx_lane_tree16(acc); // lanes 16-31 join with zeros; lane 0 holds the sum
+                const float inv =
+                    __shfl_sync(0xffffffffu, __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(acc, (float)H), L.norm_eps))), 0);
+                for (int base = 0; base < H; base += 32 * 4 * 8) {
+                    float4 wv[8];
+#pragma unroll
+                    for (int j = 0; j < 8; j++) {
+                        const int i = base + (j * 32 + lane) * 4;
+                        wv[j] = i < H ? __ldg(reinterpret_cast<const float4 *>(L.norm_w + i)) : make_float4(0.f, 0.f, 0.f, 0.f);
+                    }
+#pragma unroll
+                    for (int j = 0; j < 8; j++) {
+                        const int i = base + (j * 32 + lane) * 4;
+                        if (i < H) {
+                            float4 *p = reinterpret_cast<float4 *>(row + i);
+                            const float4 xv = *p;
+                            *p = make_float4(__fmul_rn(__fmul_rn(xv.x, inv), wv[j].x), __fmul_rn(__fmul_rn(xv.y, inv), wv[j].y),
+                                             __fmul_rn(__fmul_rn(xv.z, inv), wv[j].z), __fmul_rn(__fmul_rn(xv.w, inv), wv[j].w));
+                        }
+                    }
+                }
+            }
+            __syncthreads();
+            if (blockIdx.x == 0 && w.out_normed)
+                for (int i = tid; i < T * H; i += blockDim.x) w.out_normed[i] = sn[i];
+            nin = sn;
+        }
         const bool lprep = T <= TRX_FU_LOCAL_PREP;
         const int writers = E + (lprep ? 0 : T);
         // short calls: the router CTAs compute the logits with warps 0-3 only, while the others prepare the inputs
@@ -280,8 +342,8 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
         const int rthr = lprep ? 128 : 0, w0 = (int)blockIdx.x < E && rthr ? rthr / 32 : 0;
         if ((int)blockIdx.x < writers && (rthr == 0 || tid < rthr)) {
             if ((int)blockIdx.x < E)
-                trx_router_block(L, S, normed, blockIdx.x, 0, T, w, reinterpret_cast<float *>(smem), rthr);
-            else trx_prep_token(L, S, normed, blockIdx.x - E, w);
+                trx_router_block(L, S, nin, blockIdx.x, 0, T, w, reinterpret_cast<float *>(smem), rthr);
+            else trx_prep_token(L, S, normed, blockIdx.x - E, w); // (norm_in is for short calls only)
             if (rthr) asm volatile("bar.sync 3, %0;" ::"r"(rthr) : "memory");
             else __syncthreads();
             TRX_TRACE(62);
@@ -296,13 +358,13 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
                     const int t = q / nsb_g, s4 = q % nsb_g;
                     uint8_t *tok = s_tok + t * lay.tok_bytes;
                     double *bfd = reinterpret_cast<double *>(tok + (size_t)H * 4);
-                    trx_prep_q4x_block(normed + (int64_t)t * H + 256 * s4, reinterpret_cast<uint32_t *>(tok), s4, nsb_g,
+                    trx_prep_q4x_block(nin + (int64_t)t * H + 256 * s4, reinterpret_cast<uint32_t *>(tok), s4, nsb_g,
                                        bfd + 8 * s4, bfd + H / 32 + s4, lane);
                 }
             } else {
                 for (int i = tid - 32 * w0; i < T * H / 4; i += blockDim.x - 32 * w0) {
                     const int t = (4 * i) / H, kk = (4 * i) % H;
-                    const float4 v = *reinterpret_cast<const float4 *>(normed + (int64_t)t * H + kk);
+                    const float4 v = *reinterpret_cast<const float4 *>(nin + (int64_t)t * H + kk);
                     float *dst = reinterpret_cast<float *>(s_tok + t * lay.tok_bytes);
                     dst[trx_lc_pos(kk)] = v.x;
                     dst[trx_lc_pos(kk + 1)] = v.y;

@@ -44,10 +44,13 @@ struct TrxLayer {
     const float *router_bias;        // NULL: none
     const uint8_t *gate, *up, *down; // n_expert matrices each
     int64_t gate_mb, up_mb, down_mb; // bytes per expert matrix
+    const float *norm_w;             // ffn_norm weight (n_embd floats), NULL until set
+    float norm_eps;
 };
 
 struct TrxShape {
     int E, k, H, F, norm_topk;
+    int norm_in; // the fused kernel: the input rows are the residual stream, normalised with L.norm_w first
 };
 
 struct TrxWork {
@@ -77,6 +80,7 @@ struct TrxWork {
     int64_t *out_place;
     float *out_logits;
     uint64_t *trace;     // NULL, or 64 %globaltimer slots per CTA of the fused kernel (tr_gpu_moe_trace)
+    float *out_normed;   // NULL, or where the fused kernel (norm_in) writes the normalised rows
     uint32_t *host_done; // NULL, or a word of mapped pinned host memory: the fused kernel writes its epoch there
                          // once every output is visible to the host (bit 31 set: it gave up)
 };
