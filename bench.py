@@ -272,10 +272,10 @@ def run_prefill(args, dev, cpu_seconds):
     return out
 
 
-def ep_launches(gate, down):
-    """our kernels a step of the expert-parallel layer: route 1; pack 2; experts: sort, gather, gate and up 2 each,
-    SwiGLU, down 2, scatter; combine 1"""
-    return 1 + 2 + (2 + 2 + 2 + 1 + 2 + 2) + 1
+def ep_launches(gate, down, rows):
+    """our kernels a step of the expert-parallel layer: route 1; pack 2; experts: the fused kernel for up to 64
+    received rows, else sort, gather, gate and up 2 each, SwiGLU, down 2, scatter; combine 1"""
+    return 1 + 2 + (1 if rows <= 64 else 2 + 2 + 2 + 1 + 2 + 2) + 1
 
 
 def run_ep(args, rank, world, dist):
@@ -287,7 +287,8 @@ def run_ep(args, rank, world, dist):
     torch.cuda.set_device(dev)
     gate, down = TYPES[args.gate], TYPES[args.down]
     T, NL = args.tokens, args.layers
-    m = GpuMoe(NL, E, K_USED, H, F, gb.BF16, gate, down, max_tokens=T * world, device=dev)
+    # max_tokens: every row a rank can receive in the padded exchange (world x T k), so its experts take one kernel
+    m = GpuMoe(NL, E, K_USED, H, F, gb.BF16, gate, down, max_tokens=T * world * K_USED, device=dev)
     lays, routers = host_layers(gate, down, n_host=2, n_routers=NL)
     for l in range(NL):
         lay = dict(lays[l % len(lays)])
@@ -388,7 +389,7 @@ def run_ep(args, rank, world, dist):
             "cpu_baseline": None,
             "e2e": {"value": world * T * e2e_steps / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": T * H * 4,
                     "d2h_bytes_per_step": T * H * 4, "steps": e2e_steps},
-            "gpu_launches": ep_launches(gate, down) * steps, "clocks": clk.summary(),
+            "gpu_launches": ep_launches(gate, down, world * T * K_USED) * steps, "clocks": clk.summary(),
             "timing": f"CUDA graph of {NL} expert-parallel layer calls (kernels + NCCL) replayed {reps} times; CUDA "
                       f"events, max over ranks"}
     print(json.dumps(line), flush=True)

@@ -127,7 +127,9 @@ typedef struct {
  *   3. the caller exchanges counts, rows and ids (NCCL all-to-all);
  *   4. tr_gpu_moe_experts_dev computes the expert FFN (gate/up, SwiGLU, down; the exact definitions) of n_rows rows
  *      that arrived in any order with their expert ids, into d_out (n_rows x n_embd), in arrival order (a row whose id
- *      is out of range, the padding, is skipped and its output row left as it was);
+ *      is out of range, the padding, gets no expert: its output row is left as it was or zeroed). Calls of up to 64
+ *      rows and at most the context's max_tokens run as one fused kernel, so create a rank's context with
+ *      max_tokens >= the most rows it receives (n_ranks x cap in the padded exchange);
  *   5. the caller sends the outputs back;
  *   6. tr_gpu_moe_ep_combine: x[t] += sum over slots in expert-id order of sel_w[t][slot] * d_back[place[t k + slot]]
  *      (and ffn_out, if not NULL).
@@ -139,6 +141,31 @@ TRMOE_API int tr_gpu_moe_experts_dev(tr_gpu_moe *m, int64_t layer, const float *
                                      int64_t n_rows, float *d_out, void *stream);
 TRMOE_API int tr_gpu_moe_ep_combine(tr_gpu_moe *m, const float *d_sel_w, const int32_t *d_place, const float *d_back,
                                     int64_t n_tok, float *d_x, float *d_ffn_out, void *stream);
+
+/* Expert parallelism over peer memory (NVLink stores between the ranks' GPUs, no NCCL on the data path; a B200
+ * replacement for the all-to-alls above, same plan and the same bit-for-bit result). Each rank's context owns an
+ * exchange region for n_ranks sources of cap rows each (cap >= n_tok x n_used of every call). Set-up, once:
+ * tr_gpu_moe_ep_peer_region makes the region and writes its CUDA IPC handle (TRMOE_IPC_HANDLE_BYTES) to
+ * ipc_handle_out; the caller gathers every rank's handle in rank order (e.g. torch.distributed.all_gather_object)
+ * and passes them to tr_gpu_moe_ep_peer_open. Per layer call, every rank in step, all enqueued on `stream`
+ * (no host synchronisation; a CUDA graph can hold them):
+ *   1. tr_gpu_moe_layer_part(part 0) routes the rank's tokens (sel_id, sel_w outputs);
+ *   2. tr_gpu_moe_ep_dispatch writes each (token, slot) row and its expert id straight into its owner's region
+ *      (unused slots: id -1), then the owner's arrival flag; d_place[j] = where row j's output comes back;
+ *   3. tr_gpu_moe_ep_experts waits for every source's rows, computes them (one fused kernel: the context's
+ *      max_tokens must be >= n_ranks x cap, and n_ranks x cap <= 64), writes each output row straight back into
+ *      its source's region, then the source's return flag;
+ *   4. tr_gpu_moe_ep_peer_combine waits for every owner's rows, then x[t] += the id-ordered mix (and ffn_out).
+ * Every wait on another rank is bounded (10 s); a rank that gives up sets the error flag tr_gpu_moe_check
+ * reports. 0 or -1. */
+#define TRMOE_IPC_HANDLE_BYTES 64
+TRMOE_API int tr_gpu_moe_ep_peer_region(tr_gpu_moe *m, int32_t n_ranks, int32_t rank, int64_t cap, void *ipc_handle_out);
+TRMOE_API int tr_gpu_moe_ep_peer_open(tr_gpu_moe *m, const void *ipc_handles);
+TRMOE_API int tr_gpu_moe_ep_dispatch(tr_gpu_moe *m, const int64_t *d_sel_id, int64_t n_tok, const float *d_normed,
+                                     int32_t *d_place, void *stream);
+TRMOE_API int tr_gpu_moe_ep_experts(tr_gpu_moe *m, int64_t layer, void *stream);
+TRMOE_API int tr_gpu_moe_ep_peer_combine(tr_gpu_moe *m, const float *d_sel_w, const int32_t *d_place, int64_t n_tok,
+                                         float *d_x, float *d_ffn_out, void *stream);
 
 /* No counterpart in the reference (its long passes run the same scalar definition): calls of at least min_tokens
  * tokens take the tensor-core road of a context with Q8_0 gate/up and down weights (router, top-k and dispatch

@@ -190,6 +190,13 @@ struct tr_gpu_moe {
     const uint8_t **ep_tab = nullptr;
     uint8_t *ep_buf = nullptr;
     int64_t ep_cap = 0;
+    // expert parallelism over peer memory (tr_gpu_moe_ep_peer_*): this rank's exchange region, the other ranks'
+    // regions as opened here, and their device table
+    uint8_t *epp_region = nullptr;
+    int epp_n = 0, epp_rank = 0;
+    int64_t epp_cap = 0;
+    std::vector<uint8_t *> epp_opened;
+    TrxEpPeers *epp_dev = nullptr;
     // zone timing (tr_gpu_moe_profile): one set of events per profiled call, read when asked, so that
     // profiling never makes a call wait for the one before it
     struct EvSet {
@@ -285,9 +292,9 @@ static bool plan_fused(tr_gpu_moe *m) {
 
 // the stages of a fused call of T tokens: as many as this CTA's share of the routed rows can use, within the
 // shared memory; false when even two of each do not fit (the multi-kernel road then takes the call)
-static bool fused_stages(const tr_gpu_moe *m, int T, int *sg, int *sd) {
+static bool fused_stages(const tr_gpu_moe *m, int T, int *sg, int *sd, int k_override = 0) {
     const tr_gpu_moe_config &c = m->cfg;
-    const int H = (int)c.n_embd, F = (int)c.n_ff, k = (int)c.n_used;
+    const int H = (int)c.n_embd, F = (int)c.n_ff, k = k_override ? k_override : (int)c.n_used;
     const int64_t act = std::min<int64_t>(c.n_expert, (int64_t)T * k);
     const int64_t rows_g = (act * F + m->grid_fused - 1) / m->grid_fused, rows_d = (act * H + m->grid_fused - 1) / m->grid_fused;
     int g = (int)std::min<int64_t>(TRX_FU_MAXST, std::max<int64_t>(2, (rows_g + TRX_GU_CHUNK - 1) / TRX_GU_CHUNK + 1));
@@ -522,6 +529,10 @@ extern "C" void tr_gpu_moe_free(tr_gpu_moe *m) {
     if (m->ep_tab) cudaFree(m->ep_tab);
     if (m->ep_buf) cudaFree(m->ep_buf);
     if (m->h_done) cudaFreeHost(m->h_done);
+    for (uint8_t *p : m->epp_opened)
+        if (p) cudaIpcCloseMemHandle(p);
+    if (m->epp_dev) cudaFree(m->epp_dev);
+    if (m->epp_region) cudaFree(m->epp_region);
     if (m->norm_w) cudaFree(m->norm_w);
     for (auto &es : m->evs)
         for (cudaEvent_t e : es.ev) cudaEventDestroy(e);
@@ -1127,6 +1138,34 @@ extern "C" int tr_gpu_moe_experts_dev(tr_gpu_moe *m, int64_t layer, const float 
     cudaStream_t st = stream ? (cudaStream_t)stream : m->stream;
     const tr_gpu_moe_config &c = m->cfg;
     const int64_t E = c.n_expert, H = c.n_embd, F = c.n_ff, n = n_rows, mx = std::max(H, F);
+    // Up to TRX_ROUTE_FUSED_MAX rows, and no more than the context's max_tokens (its per-row work buffers): the fused
+    // decode kernel with the routing given (row t to expert ids[t] alone, weight 1: its mix is the expert's row),
+    // one launch
+    int sg = 0, sd = 0;
+    if (m->fused_ok && n <= TRX_ROUTE_FUSED_MAX && n <= c.max_tokens && n <= m->grid_fused &&
+        fused_stages(m, (int)n, &sg, &sd, 1)) {
+        const TrxLayer &L = m->layers[(size_t)layer];
+        const TrxShape S{(int)E, 1, (int)H, (int)F, 0, 0, 1};
+        TrxWork w = m->work;
+        w.ext_ids = d_ids;
+        const uint32_t epoch = (++m->epoch & 0x7fffffffu) | 1u;
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)m->grid_fused);
+        cfg.blockDim = dim3(TRX_FU_THREADS);
+        cfg.dynamicSmemBytes = trx_fused_layout(c.gate_type, c.down_type, (int)H, (int)F, (int)n, 1, sg, sd, (int)E,
+                                                m->grid_fused).total;
+        cfg.stream = st;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeCooperative;
+        attr[0].val.cooperative = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        return ck(cudaLaunchKernelEx(&cfg, layer_fn(c.gate_type, c.down_type), L, S, d_rows, (int)n, w, m->sync,
+                                     (float *)nullptr, d_out, epoch, sg, sd),
+                  "fused experts launch")
+                   ? 0
+                   : -1;
+    }
     // scratch: sort (offsets, place, xmap), grouped rows, gate and up outputs, down output, prepared inputs
     const int64_t so = align_up((E + 8 + 2 * n) * 4, 256), xb = align_up(n * H * 4, 256), gb = align_up(n * F * 4, 256),
                   qb = align_up(n * mx * 4, 256), bfb = align_up(n * (mx / 32) * 8, 256), scb = align_up(n * (mx / 256) * 8, 256),
@@ -1175,6 +1214,140 @@ extern "C" int tr_gpu_moe_ep_combine(tr_gpu_moe *m, const float *d_sel_w, const 
     const int64_t total = n_tok * m->cfg.n_embd;
     trx_k_pf_combine<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(d_sel_w, d_place, d_back, (int)n_tok,
                                                                      (int)m->cfg.n_used, (int)m->cfg.n_embd, d_x, d_ffn_out);
+    return ck(cudaGetLastError(), "ep combine launch") ? 0 : -1;
+}
+
+// ---------------------------------------------------------------------------------------------
+// expert parallelism over peer memory (ep.cuh): the exchange region, the peers' regions, dispatch / experts / combine
+
+extern "C" int tr_gpu_moe_ep_peer_region(tr_gpu_moe *m, int32_t n_ranks, int32_t rank, int64_t cap, void *ipc_handle_out) {
+    g_err.clear();
+    if (m == nullptr || n_ranks < 1 || n_ranks > TRX_EP_MAX_RANKS || rank < 0 || rank >= n_ranks || cap < 1 ||
+        cap > 256 || ipc_handle_out == nullptr || m->cfg.n_expert % n_ranks != 0 || m->epp_region != nullptr) {
+        set_err("bad arguments to tr_gpu_moe_ep_peer_region (or the region exists)");
+        return -1;
+    }
+    if (!ck(cudaSetDevice(m->device), "cudaSetDevice")) return -1;
+    size_t ids, rows, back, total;
+    trx_ep_layout(n_ranks, (int)cap, (int)m->cfg.n_embd, ids, rows, back, total);
+    cudaIpcMemHandle_t h;
+    if (!ck(cudaMalloc(&m->epp_region, total), "cudaMalloc(exchange region)") ||
+        !ck(cudaMemset(m->epp_region, 0, total), "cudaMemset(exchange region)") ||
+        !ck(cudaIpcGetMemHandle(&h, m->epp_region), "cudaIpcGetMemHandle")) {
+        if (m->epp_region) cudaFree(m->epp_region);
+        m->epp_region = nullptr;
+        return -1;
+    }
+    memcpy(ipc_handle_out, &h, sizeof h);
+    m->epp_n = n_ranks;
+    m->epp_rank = rank;
+    m->epp_cap = cap;
+    return 0;
+}
+
+extern "C" int tr_gpu_moe_ep_peer_open(tr_gpu_moe *m, const void *ipc_handles) {
+    g_err.clear();
+    if (m == nullptr || m->epp_region == nullptr || ipc_handles == nullptr || m->epp_dev != nullptr) {
+        set_err("bad arguments to tr_gpu_moe_ep_peer_open (no region, or already open)");
+        return -1;
+    }
+    if (!ck(cudaSetDevice(m->device), "cudaSetDevice")) return -1;
+    TrxEpPeers P{};
+    P.n = m->epp_n;
+    P.rank = m->epp_rank;
+    P.cap = (int)m->epp_cap;
+    P.H = (int)m->cfg.n_embd;
+    size_t total;
+    trx_ep_layout(P.n, P.cap, P.H, P.off_ids, P.off_rows, P.off_back, total);
+    m->epp_opened.assign((size_t)P.n, nullptr);
+    for (int r = 0; r < P.n; r++) {
+        if (r == P.rank) {
+            P.base[r] = m->epp_region;
+            continue;
+        }
+        cudaIpcMemHandle_t h;
+        memcpy(&h, (const uint8_t *)ipc_handles + (size_t)r * sizeof h, sizeof h);
+        void *p = nullptr;
+        if (!ck(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle")) return -1;
+        m->epp_opened[(size_t)r] = (uint8_t *)p;
+        P.base[r] = (uint8_t *)p;
+    }
+    if (!ck(cudaMalloc(&m->epp_dev, sizeof P), "cudaMalloc(peer table)") ||
+        !ck(cudaMemcpy(m->epp_dev, &P, sizeof P, cudaMemcpyHostToDevice), "copy peer table"))
+        return -1;
+    return 0;
+}
+
+extern "C" int tr_gpu_moe_ep_dispatch(tr_gpu_moe *m, const int64_t *d_sel_id, int64_t n_tok, const float *d_normed,
+                                      int32_t *d_place, void *stream) {
+    g_err.clear();
+    if (m == nullptr || m->epp_dev == nullptr || d_sel_id == nullptr || d_normed == nullptr || d_place == nullptr ||
+        n_tok < 1 || n_tok * m->cfg.n_used > m->epp_cap || n_tok * m->cfg.n_used > 256) {
+        set_err("bad arguments to tr_gpu_moe_ep_dispatch (no open exchange, or n_tok x n_used above its cap)");
+        return -1;
+    }
+    if (!ck(cudaSetDevice(m->device), "cudaSetDevice")) return -1;
+    cudaStream_t st = stream ? (cudaStream_t)stream : m->stream;
+    trx_k_ep_dispatch<<<1, 256, 0, st>>>(d_sel_id, (int)n_tok, (int)m->cfg.n_used, (int)(m->cfg.n_expert / m->epp_n),
+                                        d_normed, m->epp_dev, d_place);
+    return ck(cudaGetLastError(), "ep dispatch launch") ? 0 : -1;
+}
+
+extern "C" int tr_gpu_moe_ep_experts(tr_gpu_moe *m, int64_t layer, void *stream) {
+    g_err.clear();
+    if (m == nullptr || m->epp_dev == nullptr || layer < 0 || layer >= m->cfg.n_layers || !m->layer_set[(size_t)layer]) {
+        set_err("bad arguments to tr_gpu_moe_ep_experts (no open exchange, or the layer is not set)");
+        return -1;
+    }
+    if (!ck(cudaSetDevice(m->device), "cudaSetDevice")) return -1;
+    cudaStream_t st = stream ? (cudaStream_t)stream : m->stream;
+    const tr_gpu_moe_config &c = m->cfg;
+    const int64_t n = (int64_t)m->epp_n * m->epp_cap, E = c.n_expert, H = c.n_embd, F = c.n_ff;
+    int sg = 0, sd = 0;
+    if (!(m->fused_ok && n <= TRX_ROUTE_FUSED_MAX && n <= c.max_tokens && n <= m->grid_fused &&
+          fused_stages(m, (int)n, &sg, &sd, 1))) {
+        set_err("tr_gpu_moe_ep_experts: n_ranks x cap = %lld rows do not fit the fused kernel (at most %d, and the "
+                "context's max_tokens)", (long long)n, TRX_ROUTE_FUSED_MAX);
+        return -1;
+    }
+    size_t ids, rows, back, total;
+    trx_ep_layout(m->epp_n, (int)m->epp_cap, (int)H, ids, rows, back, total);
+    const TrxLayer &L = m->layers[(size_t)layer];
+    const TrxShape S{(int)E, 1, (int)H, (int)F, 0, 0, 1};
+    TrxWork w = m->work;
+    w.ext_ids = (const int32_t *)(m->epp_region + ids);
+    w.ep = m->epp_dev;
+    const uint32_t epoch = (++m->epoch & 0x7fffffffu) | 1u;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)m->grid_fused);
+    cfg.blockDim = dim3(TRX_FU_THREADS);
+    cfg.dynamicSmemBytes = trx_fused_layout(c.gate_type, c.down_type, (int)H, (int)F, (int)n, 1, sg, sd, (int)E,
+                                            m->grid_fused).total;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return ck(cudaLaunchKernelEx(&cfg, layer_fn(c.gate_type, c.down_type), L, S, (const float *)(m->epp_region + rows),
+                                 (int)n, w, m->sync, (float *)nullptr, (float *)nullptr, epoch, sg, sd),
+              "ep experts launch")
+               ? 0
+               : -1;
+}
+
+extern "C" int tr_gpu_moe_ep_peer_combine(tr_gpu_moe *m, const float *d_sel_w, const int32_t *d_place, int64_t n_tok,
+                                          float *d_x, float *d_ffn_out, void *stream) {
+    g_err.clear();
+    if (m == nullptr || m->epp_dev == nullptr || d_sel_w == nullptr || d_place == nullptr || d_x == nullptr || n_tok < 1) {
+        set_err("bad arguments to tr_gpu_moe_ep_peer_combine");
+        return -1;
+    }
+    if (!ck(cudaSetDevice(m->device), "cudaSetDevice")) return -1;
+    cudaStream_t st = stream ? (cudaStream_t)stream : m->stream;
+    const int64_t total = n_tok * m->cfg.n_embd;
+    trx_k_ep_peer_combine<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(d_sel_w, d_place, m->epp_dev, (int)n_tok,
+                                                                          (int)m->cfg.n_used, d_x, d_ffn_out, m->work.err);
     return ck(cudaGetLastError(), "ep combine launch") ? 0 : -1;
 }
 

@@ -34,6 +34,7 @@
 #include <cstdint>
 #include "bulk.cuh"
 #include "moe_kernels.cuh"
+#include "ep.cuh"
 
 #define TRX_SPIN_NS 1000000000ull
 #define TRX_FU_CWARPS 8                           // consumer warps
@@ -194,7 +195,9 @@ __host__ __device__ inline TrxFusedSmem trx_fused_layout(int gate_type, int down
                                                  : 0;
     l.tok = trx_align128(l.seg + seg_bytes);
     l.tok_bytes = gate_type == TRX_Q4_K ? trx_align128((size_t)H * 4 + (size_t)(H / 32 + H / 256) * 8) : (size_t)H * 4;
-    l.total = l.tok + (size_t)T * l.tok_bytes;
+    // the tokens' prepared inputs stay in shared memory for short calls (prepared there); longer ones read them from
+    // L2, where the prep CTAs wrote them
+    l.total = l.tok + (T <= TRX_FU_LOCAL_PREP ? (size_t)T * l.tok_bytes : 0);
     return l;
 }
 
@@ -270,7 +273,7 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
         mrb = mw.rb;
     }
     float xpre[2] = {0.0f, 0.0f};
-    if (seg && warp == TRX_FU_CWARPS)
+    if (seg && warp == TRX_FU_CWARPS && !S.ext)
 #pragma unroll
         for (int q = 0; q < 2; q++) {
             const int i = lane + 32 * q, nr = mrb - mra;
@@ -285,6 +288,19 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
         // its shared memory, warp t token t: the row in, lanes 0-15 the lane contract's sum of squares (tree-joined),
         // inv = 1 / sqrtf(sumsq / H + eps), then normed = (x inv) w in place (Trochilus's tr_rmsnorm,
         // src/kernels/kernels.c:1351-1360); CTA 0 also writes them out when asked. The routing phase reads them there.
+        // ext over peer memory: every source rank's rows of this step must have arrived (its flag holds the epoch)
+        if (w.ep) {
+            int why = 0;
+            if (tid == 0) {
+                const TrxEpHdr *own = reinterpret_cast<const TrxEpHdr *>(w.ep->base[w.ep->rank]);
+                s_flag = trx_ep_wait_flags(own->recv_flag, w.ep->n, own->epoch, TRX_EP_WAIT_NS, &why);
+            }
+            __syncthreads();
+            if (!s_flag) {
+                if (tid == 0) atomicCAS(w.err, 0, 7 | why); // the first error stays
+                return;
+            }
+        }
         const float *nin = normed;
         if (S.norm_in) {
             float *sn = reinterpret_cast<float *>(smem + trx_fu_norm_off(T, H, E));
@@ -336,14 +352,15 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
             nin = sn;
         }
         const bool lprep = T <= TRX_FU_LOCAL_PREP;
-        const int writers = E + (lprep ? 0 : T);
+        const int nrc = S.ext ? 0 : E; // router CTAs (none when the rows come routed)
+        const int writers = nrc + (lprep ? 0 : T);
         // short calls: the router CTAs compute the logits with warps 0-3 only, while the others prepare the inputs
         // and warm up the routing code (below)
-        const int rthr = lprep ? 128 : 0, w0 = (int)blockIdx.x < E && rthr ? rthr / 32 : 0;
+        const int rthr = lprep ? 128 : 0, w0 = (int)blockIdx.x < nrc && rthr ? rthr / 32 : 0;
         if ((int)blockIdx.x < writers && (rthr == 0 || tid < rthr)) {
-            if ((int)blockIdx.x < E)
+            if ((int)blockIdx.x < nrc)
                 trx_router_block(L, S, nin, blockIdx.x, 0, T, w, reinterpret_cast<float *>(smem), rthr);
-            else trx_prep_token(L, S, normed, blockIdx.x - E, w); // (norm_in is for short calls only)
+            else trx_prep_token(L, S, normed, blockIdx.x - nrc, w); // (norm_in is for short calls only)
             if (rthr) asm volatile("bar.sync 3, %0;" ::"r"(rthr) : "memory");
             else __syncthreads();
             TRX_TRACE(62);
@@ -378,7 +395,7 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
         // would otherwise be fetched cold from L2 line by line)
         // the routing warm-up's scratch: past the router's staging (in use meanwhile) and the logits' slot
         const size_t wscr = trx_align128((size_t)(1 + (T < TRX_TOK_STAGE ? T : TRX_TOK_STAGE)) * H * 4 + (size_t)T * E * 4);
-        if (warp == 4 && wscr + 4096 <= lay.bars) {
+        if (warp == 4 && !S.ext && wscr + 4096 <= lay.bars) {
             float *dl = reinterpret_cast<float *>(smem + wscr);
             int32_t *di = reinterpret_cast<int32_t *>(dl + 64);
             float *dw = dl + 128;
@@ -406,11 +423,18 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
         TRX_TRACE(1);
         TRX_CYC(53);
         float *slog = reinterpret_cast<float *>(smem); // T x E logits (the stage buffers are free until the barriers)
-        for (int j = tid; j < T * E; j += blockDim.x) slog[j] = __ldcg(w.logits + j);
+        if (S.ext) { // routed elsewhere: row t to expert ext_ids[t] alone, weight 1
+            for (int j = tid; j < T; j += blockDim.x) {
+                s_selid[j] = __ldcg(w.ext_ids + j);
+                s_selw[j] = 1.0f;
+            }
+        } else {
+            for (int j = tid; j < T * E; j += blockDim.x) slog[j] = __ldcg(w.logits + j);
+        }
         __syncthreads();
         TRX_CYC(54);
         const long long c1 = clock64();
-        for (int t = warp; t < T; t += TRX_FU_CWARPS + 2)
+        for (int t = warp; !S.ext && t < T; t += TRX_FU_CWARPS + 2)
             trx_route_token<true>(slog + t * E, E, k, S.norm_topk, lane, sp[warp], s_selid + t * k, s_selw + t * k);
         if (w.trace != nullptr && tid == 0) w.trace[(size_t)blockIdx.x * 64 + 7] = (uint64_t)(clock64() - c1);
         trx_fence_proxy_async(); // the routing's writes to the stage area, before the copies that land there
@@ -428,6 +452,7 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
         uint32_t m0 = 0, m1 = 0; // the selected experts as a 64-bit set
         for (int j = lane; j < R; j += 32) {
             const int e = s_selid[j];
+            if (e < 0) continue; // (a row routed nowhere)
             if (e < 32) m0 |= 1u << e;
             else m1 |= 1u << (e - 32);
         }
@@ -450,7 +475,7 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
                                 out ? w.out_place : nullptr};
             TRX_CYC(56);
             const long long c0 = clock64();
-            if (T == 1) {
+            if (T == 1 && !S.ext) {
                 trx_sort_single(s_selid, E, k, so, lane);
             } else {
                 trx_warp_counting_sort(s_selid, R, E, k, so, scnt, lane);
@@ -462,21 +487,6 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
             for (int j = ctid - 32; j < R; j += 32 * (TRX_FU_CWARPS - 1)) {
                 w.out_sel_id[j] = s_selid[j];
                 w.out_sel_w[j] = s_selw[j];
-            }
-        }
-        for (int t = 0; t < (lprep ? 0 : T); t++) {
-            uint8_t *dst = s_tok + t * lay.tok_bytes;
-            if (GT == TRX_Q4_K) {
-                for (int i = ctid; i < H / 4; i += 32 * TRX_FU_CWARPS)
-                    reinterpret_cast<uint4 *>(dst)[i] = __ldcg(reinterpret_cast<const uint4 *>(w.xq + (int64_t)t * H) + i);
-                double *bfd = reinterpret_cast<double *>(dst + (size_t)H * 4);
-                for (int i = ctid; i < H / 32; i += 32 * TRX_FU_CWARPS) bfd[i] = __ldcg(w.xq_bf + (int64_t)t * (H / 32) + i);
-                for (int i = ctid; i < H / 256; i += 32 * TRX_FU_CWARPS)
-                    bfd[H / 32 + i] = __ldcg(w.xq_sc + (int64_t)t * (H / 256) + i);
-            } else {
-                for (int i = ctid; i < H / 4; i += 32 * TRX_FU_CWARPS)
-                    reinterpret_cast<float4 *>(dst)[i] =
-                        __ldcg(reinterpret_cast<const float4 *>(w.x_lc + (int64_t)t * H) + i);
             }
         }
         asm volatile("bar.sync 1, %0;" ::"n"(32 * TRX_FU_CWARPS) : "memory");        // the consumers: sorted
@@ -498,6 +508,14 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
     const bool hcopy = seg && DT != TRX_Q4_K;
     const int hoff = TRX_DN_CHUNK * rbd + (DT == TRX_Q6_K ? TRX_DN_CHUNK * nsb_d * 2 : 0);
     const uint32_t need = (uint32_t)F + (DT == TRX_Q4_K ? 1u : 0u); // an expert's count once its h is complete
+    // where token t's output row goes: ffn_out, or (ext over peer memory) its source rank's region, at [this rank]
+    // [its slot]; NULL: nowhere (no ffn_out, or a padding row)
+    auto out_row = [&](int t) -> float * {
+        if (w.ep == nullptr) return ffn_out ? ffn_out + (int64_t)t * H : nullptr;
+        if (s_selid[t] < 0) return nullptr;
+        const TrxEpPeers *P = w.ep;
+        return reinterpret_cast<float *>(P->base[t / P->cap] + P->off_back) + ((size_t)P->rank * P->cap + t % P->cap) * H;
+    };
     // longer calls: the mix of a completed 16-row block (one warp): every token's k outputs in increasing expert id,
     // then the residual
     auto combine = [&](int blk) {
@@ -507,10 +525,11 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
             float out = 0.0f;
             for (int sl = 0; sl < k; sl++) {
                 const int jj = t * k + sl;
+                if (s_selid[jj] < 0) continue; // (a row routed nowhere)
                 out = __fadd_rn(out, __fmul_rn(s_selw[jj], __ldcg(w.h3 + (int64_t)s_place[jj] * H + dd)));
             }
-            if (ffn_out) ffn_out[(int64_t)t * H + dd] = out;
-            x_io[(int64_t)t * H + dd] = __fadd_rn(x_io[(int64_t)t * H + dd], out);
+            if (float *o = out_row(t)) o[dd] = out;
+            if (!S.ext) x_io[(int64_t)t * H + dd] = __fadd_rn(x_io[(int64_t)t * H + dd], out);
         }
         if (lane == 0) w.comb_cnt[blk] = 0u;
     };
@@ -640,11 +659,14 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
                 float out = 0.0f;
                 for (int sl = 0; sl < k; sl++) {
                     const int jj = t * k + sl;
+                    if (s_selid[jj] < 0) continue; // (a row routed nowhere)
                     out = __fadd_rn(out, __fmul_rn(s_selw[jj], sh3[(size_t)s_place[jj] * nrmax + (d - mra)]));
                 }
-                if (ffn_out) ffn_out[(int64_t)t * H + d] = out;
-                const float xv = i < 32 ? xpre[0] : i < 64 ? xpre[1] : x_io[(int64_t)t * H + d];
-                x_io[(int64_t)t * H + d] = __fadd_rn(xv, out);
+                if (float *o = out_row(t)) o[d] = out;
+                if (!S.ext) {
+                    const float xv = i < 32 ? xpre[0] : i < 64 ? xpre[1] : x_io[(int64_t)t * H + d];
+                    x_io[(int64_t)t * H + d] = __fadd_rn(xv, out);
+                }
             }
             n_mix = 1;
         } else {
@@ -728,17 +750,25 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
                     float y[4]; // gate a, up a, gate b, up b
                     if (GT == TRX_Q4_K) {
                         if (t != cur) {
-                            const double *bfd = reinterpret_cast<const double *>(tok + (size_t)H * 4);
-                            trx_q4x_load(reinterpret_cast<const uint32_t *>(tok), 32, lane, bfd + 8 * (lane >> 2),
-                                         bfd + H / 32 + (lane >> 2), X);
+                            if (lprep) {
+                                const double *bfd = reinterpret_cast<const double *>(tok + (size_t)H * 4);
+                                trx_q4x_load(reinterpret_cast<const uint32_t *>(tok), 32, lane, bfd + 8 * (lane >> 2),
+                                             bfd + H / 32 + (lane >> 2), X);
+                            } else { // (the prep CTAs' rows in L2)
+                                trx_q4x_load<true>(w.xq + (int64_t)t * H, 32, lane,
+                                                   w.xq_bf + (int64_t)t * (H / 32) + 8 * (lane >> 2),
+                                                   w.xq_sc + (int64_t)t * (H / 256) + (lane >> 2), X);
+                            }
                             cur = t;
                         }
                         const uint8_t *const rows[4] = {ga, ga + gu_half, gb, gb + gu_half};
                         trx_q4k_row8xn<true, 4>(rows, X, lane, y);
                     } else { // half 0 the gate rows, half 1 the up rows
-                        const float *xt = reinterpret_cast<const float *>(tok);
-                        const float va = trx_q8l_dot<true, false>(lane < 16 ? ga : ga + gu_half, xt, H / 256, lane & 15);
-                        const float vb = trx_q8l_dot<true, false>(lane < 16 ? gb : gb + gu_half, xt, H / 256, lane & 15);
+                        const float *xt = lprep ? reinterpret_cast<const float *>(tok) : w.x_lc + (int64_t)t * H;
+                        const float va = lprep ? trx_q8l_dot<true, false>(lane < 16 ? ga : ga + gu_half, xt, H / 256, lane & 15)
+                                               : trx_q8l_dot<true, true>(lane < 16 ? ga : ga + gu_half, xt, H / 256, lane & 15);
+                        const float vb = lprep ? trx_q8l_dot<true, false>(lane < 16 ? gb : gb + gu_half, xt, H / 256, lane & 15)
+                                               : trx_q8l_dot<true, true>(lane < 16 ? gb : gb + gu_half, xt, H / 256, lane & 15);
                         y[0] = va;
                         y[1] = __shfl_sync(0xffffffffu, va, 16);
                         y[2] = vb;
@@ -880,7 +910,7 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
     // ---------------- end
     if (__syncthreads_or(failed)) {
         if (warp == TRX_FU_CWARPS && lane == 0) {
-            atomicExch(w.err, 3);
+            atomicCAS(w.err, 0, 3 | (w.ep ? 0x100 : 0)); // the first error stays
             // every copy still in flight lands before the CTA's shared memory goes away
             for (int q = 0; q < issued_g; q++) trx_mbar_wait(&full_g[q % SG], (q / SG) & 1, TRX_WAIT_NS);
             for (int q = 0; q < issued_d; q++) trx_mbar_wait(&full_d[q % SD], (q / SD) & 1, TRX_WAIT_NS);
@@ -892,7 +922,7 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
     TRX_TRACE(52);
     if (tid == 0) {
         // the CTA's outputs (x may be host memory: system scope) before its count
-        if (w.host_done) __threadfence_system();
+        if (w.host_done || w.ep) __threadfence_system();
         else __threadfence();
         if (atomicAdd(&sync->finish, 1u) == gridDim.x - 1) { // every CTA is past its waits
             __threadfence();
@@ -901,6 +931,13 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
             sync->finish = 0u;
             __threadfence();
             if (w.host_done) trx_post_done(w.host_done, epoch); // every CTA's outputs are out
+            if (w.ep) { // every output row is in its source's region: the sources' return flags
+                const TrxEpPeers *P = w.ep;
+                const uint32_t ep_epoch = reinterpret_cast<const TrxEpHdr *>(P->base[P->rank])->epoch;
+                __threadfence_system();
+                for (int s = 0; s < P->n; s++)
+                    trx_st_release_sys(&reinterpret_cast<TrxEpHdr *>(P->base[s])->back_flag[P->rank], ep_epoch);
+            }
         }
     }
 }

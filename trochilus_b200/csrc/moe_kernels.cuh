@@ -51,6 +51,8 @@ struct TrxLayer {
 struct TrxShape {
     int E, k, H, F, norm_topk;
     int norm_in; // the fused kernel: the input rows are the residual stream, normalised with L.norm_w first
+    int ext;     // the fused kernel: rows routed elsewhere (expert parallelism): row t goes to expert w.ext_ids[t]
+                 // alone (k = 1, weight 1; -1: none), the output is the expert's row (ffn_out), no residual
 };
 
 struct TrxWork {
@@ -81,6 +83,9 @@ struct TrxWork {
     float *out_logits;
     uint64_t *trace;     // NULL, or 64 %globaltimer slots per CTA of the fused kernel (tr_gpu_moe_trace)
     float *out_normed;   // NULL, or where the fused kernel (norm_in) writes the normalised rows
+    const int32_t *ext_ids; // the fused kernel's external routing (ext): each row's expert, -1 for none
+    const struct TrxEpPeers *ep; // ext over peer memory: rows and ids from this rank's exchange region, each output
+                                 // row back into its source rank's region, then the sources' return flags
     uint32_t *host_done; // NULL, or a word of mapped pinned host memory: the fused kernel writes its epoch there
                          // once every output is visible to the host (bit 31 set: it gave up)
 };
@@ -264,7 +269,7 @@ __device__ void trx_warp_counting_sort(const int32_t *__restrict__ sel_id, int R
             i1 += b;
         }
     }
-    const int total0 = __shfl_sync(0xffffffffu, i0, 31);
+    const int total0 = __shfl_sync(0xffffffffu, i0, 31), total = total0 + __shfl_sync(0xffffffffu, i1, 31);
     const int off0 = i0 - c0, off1 = total0 + i1 - c1;
     if (lane < E) {
         w.offsets[lane] = off0;
@@ -274,9 +279,9 @@ __device__ void trx_warp_counting_sort(const int32_t *__restrict__ sel_id, int R
         w.offsets[lane + 32] = off1;
         if (w.out_offsets) w.out_offsets[lane + 32] = off1;
     }
-    if (lane == 0) {
-        w.offsets[E] = R;
-        if (w.out_offsets) w.out_offsets[E] = R;
+    if (lane == 0) { // the rows with an expert (rows with none, id -1, are left out)
+        w.offsets[E] = total;
+        if (w.out_offsets) w.out_offsets[E] = total;
     }
     const unsigned a0 = __ballot_sync(0xffffffffu, c0 > 0), a1 = __ballot_sync(0xffffffffu, c1 > 0);
     const unsigned lt = (1u << lane) - 1u;

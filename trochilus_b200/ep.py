@@ -153,3 +153,40 @@ class GpuEpBackend:
         with torch.cuda.stream(self.stream):
             self.m.ep_combine(sel_w.data_ptr(), place.data_ptr(), back.data_ptr(), x.shape[0], x.data_ptr(),
                               None if ffn_out is None else ffn_out.data_ptr(), stream=self._s())
+
+
+class PeerEp:
+    """The expert-parallel layer over peer memory (libtrmoe.so's tr_gpu_moe_ep_peer_* / _dispatch / _experts /
+    _peer_combine): rows go straight into their owner's exchange region over NVLink and come back the same way; no
+    collective on the data path, so a CUDA graph can hold whole layer calls. Set up collectively (the IPC handles are
+    gathered once with torch.distributed); every rank then calls layer() in step. m: a GpuMoe holding this rank's
+    experts, with max_tokens >= world x cap; cap >= the most (token, slot) rows a rank sends in one call."""
+
+    def __init__(self, dist, m, cap: int, stream: torch.cuda.Stream | None = None):
+        self.m, self.cap = m, cap
+        self.stream = stream or torch.cuda.current_stream()
+        world, rank = dist.get_world_size(), dist.get_rank()
+        c = m.cfg
+        self.k, self.H = c.n_used, c.n_embd
+        handle = m.ep_peer_region(world, rank, cap)
+        handles = [None] * world
+        dist.all_gather_object(handles, handle)
+        m.ep_peer_open(handles)
+        self.dev = torch.device("cuda", torch.cuda.current_device())
+
+    def layer(self, layer: int, normed: torch.Tensor, x: torch.Tensor, ffn_out: torch.Tensor | None = None):
+        """x (T x H) += the layer's output for this rank's tokens; returns (sel_id, sel_w)"""
+        T = normed.shape[0]
+        sel_id = torch.empty((T * self.k,), dtype=torch.int64, device=self.dev)
+        sel_w = torch.empty((T * self.k,), dtype=torch.float32, device=self.dev)
+        place = torch.empty((T * self.k,), dtype=torch.int32, device=self.dev)
+        sp = self.stream.cuda_stream
+        with torch.cuda.stream(self.stream):
+            self.m.layer_part(layer, 0, normed.data_ptr(), T, x.data_ptr(),
+                              {"sel_id": sel_id.data_ptr(), "sel_w": sel_w.data_ptr()}, stream=sp)
+            self.m.ep_dispatch(sel_id.data_ptr(), T, normed.data_ptr(), place.data_ptr(), stream=sp)
+            self.m.ep_experts(layer, stream=sp)
+            self.m.ep_peer_combine(sel_w.data_ptr(), place.data_ptr(), T, x.data_ptr(),
+                                   None if ffn_out is None else ffn_out.data_ptr(), stream=sp)
+        return sel_id, sel_w
+

@@ -27,7 +27,8 @@ EXPORTS = ["tr_gpu_moe_create", "tr_gpu_moe_free", "tr_gpu_moe_bytes", "tr_gpu_m
            "tr_gpu_moe_trace_read", "trmoe_last_error", "tr_matmul", "tr_matmul_grouped",
            "tr_matmul_grouped_s", "tr_softmax", "tr_swiglu", "trmoe_kernel_cache_clear", "tr_matmul_q4k_noalloc",
            "tr_gpu_moe_set_prefill", "tr_gpu_moe_ep_pack", "tr_gpu_moe_experts_dev", "tr_gpu_moe_ep_combine",
-           "tr_gpu_moe_set_ffn_norm", "tr_gpu_moe_ffn", "tr_gpu_moe_ffn_dev"]
+           "tr_gpu_moe_set_ffn_norm", "tr_gpu_moe_ffn", "tr_gpu_moe_ffn_dev", "tr_gpu_moe_ep_peer_region",
+           "tr_gpu_moe_ep_peer_open", "tr_gpu_moe_ep_dispatch", "tr_gpu_moe_ep_experts", "tr_gpu_moe_ep_peer_combine"]
 
 
 class Config(C.Structure):
@@ -67,6 +68,12 @@ def lib():
     L.tr_gpu_moe_layer_dev.argtypes = [C.c_void_p, C.c_int64, C.c_void_p, C.c_int64, C.c_void_p,
                                        C.POINTER(Outputs), C.c_void_p]
     L.tr_gpu_moe_launches.argtypes = [C.c_void_p, C.c_int64]
+    L.tr_gpu_moe_ep_peer_region.argtypes = [C.c_void_p, C.c_int32, C.c_int32, C.c_int64, C.c_void_p]
+    L.tr_gpu_moe_ep_peer_open.argtypes = [C.c_void_p, C.c_void_p]
+    L.tr_gpu_moe_ep_dispatch.argtypes = [C.c_void_p, C.c_void_p, C.c_int64, C.c_void_p, C.c_void_p, C.c_void_p]
+    L.tr_gpu_moe_ep_experts.argtypes = [C.c_void_p, C.c_int64, C.c_void_p]
+    L.tr_gpu_moe_ep_peer_combine.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_void_p, C.c_void_p,
+                                             C.c_void_p]
     L.tr_gpu_moe_set_ffn_norm.argtypes = [C.c_void_p, C.c_int64, C.c_void_p, C.c_float, C.c_char_p, C.c_size_t]
     L.tr_gpu_moe_ffn.argtypes = [C.c_void_p, C.c_int64, C.c_int64, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]
     L.tr_gpu_moe_ffn_dev.argtypes = [C.c_void_p, C.c_int64, C.c_int64, C.c_void_p, C.c_void_p, C.POINTER(Outputs),
@@ -258,6 +265,31 @@ class GpuMoe:
         if lib().tr_gpu_moe_ep_pack(self.h, sel_id_ptr, n_tok, n_ranks, cap, normed_ptr, send_rows_ptr, send_ids_ptr,
                                     send_counts_ptr, place_ptr, scratch_ptr, stream or None) != 0:
             raise RuntimeError(f"tr_gpu_moe_ep_pack: {last_error()}")
+
+    def ep_peer_region(self, n_ranks: int, rank: int, cap: int) -> bytes:
+        """tr_gpu_moe_ep_peer_region: this rank's exchange region; returns its IPC handle (64 bytes)"""
+        h = C.create_string_buffer(64)
+        if lib().tr_gpu_moe_ep_peer_region(self.h, n_ranks, rank, cap, h) != 0:
+            raise RuntimeError(f"tr_gpu_moe_ep_peer_region: {last_error()}")
+        return h.raw
+
+    def ep_peer_open(self, handles: list):
+        """tr_gpu_moe_ep_peer_open: every rank's handle, in rank order"""
+        buf = C.create_string_buffer(b"".join(handles), 64 * len(handles))
+        if lib().tr_gpu_moe_ep_peer_open(self.h, buf) != 0:
+            raise RuntimeError(f"tr_gpu_moe_ep_peer_open: {last_error()}")
+
+    def ep_dispatch(self, sel_id_ptr, n_tok, normed_ptr, place_ptr, stream=0):
+        if lib().tr_gpu_moe_ep_dispatch(self.h, sel_id_ptr, n_tok, normed_ptr, place_ptr, stream or None) != 0:
+            raise RuntimeError(f"tr_gpu_moe_ep_dispatch: {last_error()}")
+
+    def ep_experts(self, layer, stream=0):
+        if lib().tr_gpu_moe_ep_experts(self.h, layer, stream or None) != 0:
+            raise RuntimeError(f"tr_gpu_moe_ep_experts: {last_error()}")
+
+    def ep_peer_combine(self, sel_w_ptr, place_ptr, n_tok, x_ptr, ffn_ptr=None, stream=0):
+        if lib().tr_gpu_moe_ep_peer_combine(self.h, sel_w_ptr, place_ptr, n_tok, x_ptr, ffn_ptr, stream or None) != 0:
+            raise RuntimeError(f"tr_gpu_moe_ep_peer_combine: {last_error()}")
 
     def experts_dev(self, layer, rows_ptr, ids_ptr, n_rows, out_ptr, stream=0):
         """tr_gpu_moe_experts_dev (device pointers)."""
