@@ -143,9 +143,11 @@ __host__ __device__ inline void trx_ep_layout(int n, int cap, int H, size_t &ids
     total = back + (size_t)n * cap * H * 4;
 }
 
+// a flag another GPU writes: read by an atomic (or 0) with acquire semantics at system scope, which the memory's own
+// L2 carries out, rather than a load
 __device__ __forceinline__ uint32_t trx_ld_acquire_sys(const uint32_t *p) {
     uint32_t v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    asm volatile("atom.acquire.sys.global.or.b32 %0, [%1], 0;" : "=r"(v) : "l"(p) : "memory");
     return v;
 }
 
