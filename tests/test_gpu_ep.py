@@ -171,7 +171,7 @@ def _peer_worker(rank, world, port, out_dir):
         d, keep = make_desc(lay, H, F, K, 0, rt, gt, dt)
         orc = Oracle()
         rng = np.random.default_rng(rank + 10)
-        # the oracle's answers first: the ranks then reach the exchange together (its waits are bounded at 1 s)
+        # the oracle's answers first: the ranks then reach the exchange together (its waits are bounded at 10 s)
         cases = []
         for call in range(3):
             T = 1 + (rank + call) % 2
@@ -222,9 +222,10 @@ def _peer_worker(rank, world, port, out_dir):
         dist.destroy_process_group()
 
 
-@pytest.mark.skip(reason="experimental, not used by bench.py: on 2 GPUs the first two calls match the oracle bit for "
-                         "bit, but from the third call one rank's flag written over NVLink is not seen by its owner "
-                         "(the bounded wait gives up: error flag 6/7 with source 1, value 2, epoch 3)")
+@pytest.mark.skipif(os.environ.get("TRX_PEER_EP_TEST") != "1",
+                    reason="experimental, not used by bench.py; set TRX_PEER_EP_TEST=1 to run it. Its last GPU run "
+                           "failed at the third call because the flag wait gave up at its first miss whenever an "
+                           "earlier flag was already set (its clock never started); fixed since, not yet re-run")
 def test_ep_peer_memory_matches_oracle(cuda, tmp_path):
     torch = cuda
     n = torch.cuda.device_count()

@@ -143,11 +143,9 @@ __host__ __device__ inline void trx_ep_layout(int n, int cap, int H, size_t &ids
     total = back + (size_t)n * cap * H * 4;
 }
 
-// a flag another GPU writes: read by an atomic (or 0) with acquire semantics at system scope, which the memory's own
-// L2 carries out, rather than a load
 __device__ __forceinline__ uint32_t trx_ld_acquire_sys(const uint32_t *p) {
     uint32_t v;
-    asm volatile("atom.acquire.sys.global.or.b32 %0, [%1], 0;" : "=r"(v) : "l"(p) : "memory");
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
 }
 
@@ -159,11 +157,13 @@ __device__ __forceinline__ void trx_st_release_sys(uint32_t *p, uint32_t v) {
     (void)old;
 }
 
-// Waits until flags[0..n) all hold `epoch` (one thread); false when it gave up (limit_ns), with *why = the source it
-// waited for, the value it last saw and the epoch it wanted, packed for the error flag
+// Waits until flags[0..n) all hold `epoch` (one thread); false when it gave up (limit_ns after the first flag it
+// found unset), with *why = the source it waited for, the value it last saw and the epoch it wanted, packed for the
+// error flag
 __device__ inline bool trx_ep_wait_flags(const uint32_t *flags, int n, uint32_t epoch, uint64_t limit_ns, int *why) {
     uint64_t t0 = 0;
-    for (int s = 0, it = 0; s < n; it++) {
+    bool timing = false; // the clock starts at the first miss, whichever flag it is on
+    for (int s = 0; s < n;) {
         const uint32_t v = trx_ld_acquire_sys(flags + s);
         if (v == epoch) {
             s++;
@@ -171,8 +171,10 @@ __device__ inline bool trx_ep_wait_flags(const uint32_t *flags, int n, uint32_t 
         }
         uint64_t now;
         asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(now));
-        if (it == 0) t0 = now;
-        else if (now - t0 > limit_ns) {
+        if (!timing) {
+            t0 = now;
+            timing = true;
+        } else if (now - t0 > limit_ns) {
             *why = (s & 15) << 4 | (int)(v & 0xfffu) << 8 | (int)(epoch & 0x7ffu) << 20;
             return false;
         }
