@@ -151,10 +151,11 @@ __device__ __forceinline__ uint32_t trx_ld_acquire_sys(const uint32_t *p) {
 
 // a flag in another GPU's memory: a system-scope atomic exchange with release semantics, performed at the memory's
 // own GPU (a plain store to a peer can stay in flight; the atomic is carried out where the flag lives)
-__device__ __forceinline__ void trx_st_release_sys(uint32_t *p, uint32_t v) {
+// (returns the flag's previous value)
+__device__ __forceinline__ uint32_t trx_st_release_sys(uint32_t *p, uint32_t v) {
     uint32_t old;
     asm volatile("atom.release.sys.global.exch.b32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
-    (void)old;
+    return old;
 }
 
 // Waits until flags[0..n) all hold `epoch` (one thread); false when it gave up (limit_ns after the first flag it
