@@ -250,6 +250,41 @@ TRMOE_API void tr_matmul_grouped_s(tr_pool *pool, const tr_mat *w, const int64_t
 TRMOE_API void tr_softmax(float *x, int64_t n);
 /* Replaces: tr_swiglu (src/kernels/kernels.h:345): x[i] = silu(x[i]) * y[i]. */
 TRMOE_API void tr_swiglu(tr_pool *pool, float *x, const float *y, int64_t n);
+/* Replaces: tr_matmul_s (src/kernels/kernels.h:279): tr_matmul's result; the scratch argument is ignored. */
+TRMOE_API void tr_matmul_s(tr_pool *pool, const tr_mat *w, const float *x, int64_t n_tokens, float *y, const void *s);
+
+/* Q4_K's prepared road (src/kernels/kernels.h:280-300, 346-350). The engine prepares a pass's input rows once into
+ * its own buffer, one slot of tr_q4x_bytes(cols) bytes a row, and every Q4_K matmul of the pass reads them, a
+ * group's input row p from slot map[p]. In this library a slot holds the row's floats at its start; the GPU prepares
+ * the integer digits inside each matmul from those floats, so every output is the reference road's (which equals
+ * tr_matmul_grouped_s's bit for bit, kernels.h:286-292). The slots' format is the library's own: the engine must take
+ * these six functions together (tr_q4x_road, tr_q4x_prepare, tr_matmul_q4x_prepared, tr_matmul_q4x_prepared_n,
+ * tr_swiglu_prepare and tr_matmul_s), never mix them with the CPU's. Pool and scratch are not consulted. */
+/* Replaces: tr_q4x_bytes (src/kernels/kernels.h:90): the bytes of one slot, the reference's formula. */
+TRMOE_API size_t tr_q4x_bytes(int64_t n);
+/* Replaces: tr_q4x_road (src/kernels/kernels.h:289): 1 when w[0] is Q4_K, its rows a multiple of 16 and its
+ * columns a positive multiple of 256 (the calls the library's Q4_K road takes), else 0. */
+TRMOE_API int tr_q4x_road(tr_pool *pool, const tr_mat *w, const int64_t *offsets, int64_t n_groups, const void *s);
+/* Replaces: tr_q4x_prepare (src/kernels/kernels.h:288): rows 0..n-1 of x (cols floats each) into xq, row r's
+ * floats at byte r * tr_q4x_bytes(cols). A host copy: the GPU is not involved. */
+TRMOE_API void tr_q4x_prepare(tr_pool *pool, const float *x, int64_t n, int64_t cols, void *xq);
+/* Replaces: tr_matmul_q4x_prepared (src/kernels/kernels.h:290-291): y[p*rows + r] = row r of w[g(p)] . the row in
+ * slot map[p] of xq (map NULL: slot p). 1 when done (an empty call included); 0, y untouched, when tr_q4x_road
+ * refuses w. A GPU failure prints `trmoe: tr_matmul_q4x_prepared failed: <reason>` and returns 1 (y unspecified). */
+TRMOE_API int tr_matmul_q4x_prepared(tr_pool *pool, const tr_mat *w, const int64_t *offsets, int64_t n_groups,
+                                     const void *xq, const int64_t *map, float *y, const void *s);
+/* Replaces: tr_matmul_q4x_prepared_n (src/kernels/kernels.h:298-299): the same for n_w (1..TRMOE_Q4X_MATS) weights of
+ * one shape on the same groups and slots, y[m] from w[m]; the rows go to the GPU and are prepared once for all of
+ * them. 0, every y untouched, when n_w is out of range, a weight is refused or the shapes differ. */
+#define TRMOE_Q4X_MATS 3
+TRMOE_API int tr_matmul_q4x_prepared_n(tr_pool *pool, const tr_mat *const *w, int n_w, const int64_t *offsets,
+                                       int64_t n_groups, const void *xq, const int64_t *map, float *const *y,
+                                       const void *s);
+/* Replaces: tr_q4x_fused_calls (src/kernels/kernels.h:300): tr_matmul_q4x_prepared_n's calls of n_w > 1 so far. */
+TRMOE_API uint64_t tr_q4x_fused_calls(void);
+/* Replaces: tr_swiglu_prepare (src/kernels/kernels.h:350): tr_swiglu over n_rows rows of n, then row r's floats into
+ * xq at byte r * tr_q4x_bytes(n) (the down's slots). */
+TRMOE_API void tr_swiglu_prepare(tr_pool *pool, float *x, const float *y, int64_t n_rows, int64_t n, void *xq);
 
 /* No counterpart in the reference (it has no GPU matmul API). y[t*rows + r] = row r of a Q4_K matrix . x[t*cols ..],
  * bit for bit tr_matmul's result, for callers that cannot allocate device memory: a process whose HBM is all held

@@ -53,3 +53,41 @@ def test_bytes_and_config_checks_without_gpu():
         moe.GpuMoe(1, 65, 8, 2048, 1024, moe.F32, moe.Q4_K, moe.Q6_K, 1)
     with pytest.raises(RuntimeError, match="n_embd 2048"):
         moe.GpuMoe(1, 64, 8, 1024, 1024, moe.F32, moe.Q4_K, moe.Q6_K, 1)
+
+
+def test_prepared_road_host_logic_without_gpu():
+    """Q4_K's prepared road (tr_q4x_road, tr_q4x_bytes, tr_q4x_prepare, and the refusals of
+    tr_matmul_q4x_prepared(_n)) answers on the host: which weights it takes, the slot size (the reference's
+    tr_q4x_bytes, src/kernels/kernels.c:489-492), where a prepared row's floats go, and a refused call leaves y
+    untouched and returns 0 (an empty call returns 1)."""
+    import numpy as np
+    from trochilus_b200 import moe
+    L = moe.lib()
+    assert [moe.q4x_bytes(n) for n in (256, 512, 1024, 2048)] == [1152, 2304, 4544, 9024]
+    assert moe.q4x_road(moe.Q4_K, 1024, 2048) == 1 and moe.q4x_road(moe.Q4_K, 2048, 1024) == 1
+    assert moe.q4x_road(moe.Q8_0, 1024, 2048) == 0 and moe.q4x_road(moe.Q6_K, 2048, 1024) == 0
+    assert moe.q4x_road(moe.Q4_K, 1000, 2048) == 0 and moe.q4x_road(moe.Q4_K, 1024, 2000) == 0
+    x = np.random.default_rng(0).normal(size=(3, 512)).astype(np.float32)
+    xq = moe.q4x_prepare(x)
+    sl = moe.q4x_bytes(512)
+    assert xq.size == 3 * sl
+    for r in range(3):
+        assert np.array_equal(xq[r * sl:r * sl + 2048].view(np.float32), x[r])
+        assert not xq[r * sl + 2048:(r + 1) * sl].any()  # the rest of a slot is not written
+    off = np.array([0, 2, 3], dtype=np.int64)
+    w = np.zeros((16, 34 * 16), dtype=np.uint8)
+    q8 = (moe.TrMat * 2)(moe.TrMat(moe.Q8_0, 16, 512, w.ctypes.data), moe.TrMat(moe.Q8_0, 16, 512, w.ctypes.data))
+    y = np.full((3, 16), np.nan, dtype=np.float32)
+    assert L.tr_matmul_q4x_prepared(None, q8, off.ctypes.data, 2, xq.ctypes.data, None, y.ctypes.data, None) == 0
+    assert np.isnan(y).all()
+    empty = np.array([0, 0, 0], dtype=np.int64)
+    assert L.tr_matmul_q4x_prepared(None, q8, empty.ctypes.data, 2, xq.ctypes.data, None, y.ctypes.data, None) == 1
+    w4 = np.zeros((16, 144 * 2), dtype=np.uint8)
+    a = (moe.TrMat * 2)(*[moe.TrMat(moe.Q4_K, 16, 512, w4.ctypes.data)] * 2)
+    b = (moe.TrMat * 2)(*[moe.TrMat(moe.Q4_K, 32, 512, w4.ctypes.data)] * 2)
+    wp = (C.c_void_p * 4)(C.cast(a, C.c_void_p), C.cast(b, C.c_void_p), C.cast(a, C.c_void_p), C.cast(a, C.c_void_p))
+    yp = (C.c_void_p * 4)(*[y.ctypes.data] * 4)
+    before = moe.q4x_fused_calls()
+    for n_w in (0, 2, 4):  # out of range, shapes that differ, out of range
+        assert L.tr_matmul_q4x_prepared_n(None, wp, n_w, off.ctypes.data, 2, xq.ctypes.data, None, yp, None) == 0
+    assert np.isnan(y).all() and moe.q4x_fused_calls() == before

@@ -1,5 +1,6 @@
 """The CPU oracle (oracle/moe_oracle.c) pinned against Trochilus's own code (oracle/_ref) and against the
 golden vectors that code produced (tests/golden). CPU only."""
+import ctypes as C
 import os
 
 import numpy as np
@@ -166,3 +167,69 @@ def test_encoders_decode_close(reflib, t):
         back = reflib.dequant_row(t, q[r], 512)
         tol = {gb.Q8_0: 0.02 * 4 / 127, gb.Q4_K: 0.02 * 8 / 15 * 1.2, gb.Q6_K: 0.02 * 4 / 31}[t]
         assert np.max(np.abs(back - w[r])) < tol
+
+
+class _PmScratch(C.Structure):
+    """Trochilus's tr_pm_scratch (src/kernels/kernels.h:250-262)"""
+    _fields_ = [("xil", C.c_void_p), ("max_x", C.c_int64), ("xq", C.c_void_p), ("xq_bytes", C.c_int64),
+                ("work", C.c_void_p), ("max_cols", C.c_int64), ("n_workers", C.c_int), ("plan", C.c_void_p),
+                ("max_groups", C.c_int64), ("max_tokens", C.c_int64)]
+
+
+def _aligned(nbytes, align=64):
+    buf = np.zeros(nbytes + align, dtype=np.uint8)
+    off = (-buf.ctypes.data) % align
+    return buf[off:off + nbytes]
+
+
+@pytest.mark.parametrize("rows,cols", [(64, 512), (1024, 2048), (2048, 1024)])
+def test_reference_prepared_road_equals_float_road(oracle, reflib, rows, cols):
+    """The premise of the library's prepared road: the reference's Q4_K road on rows prepared once
+    (tr_q4x_prepare + tr_matmul_q4x_prepared(_n), src/kernels/kernels.c:1157-1228), a group's row read through a map,
+    gives the float road's outputs (the oracle's grouped matmul on the gathered floats) bit for bit, so a library
+    whose prepared rows are the floats themselves returns the same y."""
+    L = reflib.lib
+    L.tr_pm_scratch_init.argtypes = [C.c_void_p, C.c_int, C.c_int64, C.c_int64, C.c_int64, C.c_int64]
+    L.tr_pm_scratch_free.argtypes = [C.c_void_p]
+    L.tr_q4x_bytes.restype = C.c_size_t
+    L.tr_q4x_bytes.argtypes = [C.c_int64]
+    L.tr_q4x_prepare.argtypes = [C.c_void_p, C.c_void_p, C.c_int64, C.c_int64, C.c_void_p]
+    L.tr_matmul_q4x_prepared.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_void_p, C.c_void_p,
+                                         C.c_void_p, C.c_void_p]
+    L.tr_matmul_q4x_prepared_n.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_int64, C.c_void_p,
+                                           C.c_void_p, C.c_void_p, C.c_void_p]
+
+    class Mat(C.Structure):
+        _fields_ = [("type", C.c_int32), ("rows", C.c_int64), ("cols", C.c_int64), ("data", C.c_void_p)]
+
+    rng = np.random.default_rng(rows + cols)
+    G, T, k = 6, 5, 4
+    R = T * k
+    sel = np.stack([rng.choice(G, size=k, replace=False) for _ in range(T)]).ravel()
+    order = np.argsort(sel, kind="stable")  # the counting sort's rows: by group, then by (token, slot)
+    offsets = np.concatenate([[0], np.cumsum(np.bincount(sel, minlength=G))]).astype(np.int64)
+    xmap = (order // k).astype(np.int64)
+    x = rng.normal(size=(T, cols)).astype(np.float32)
+    x[1, :7] = [0.0, -0.0, 1e-40, -3e38, 3e38, 1.0, -1.0]
+    mats = [[np.ascontiguousarray(gb.random_blocks(gb.Q4_K, rows, cols, rng)) for _ in range(G)] for _ in range(2)]
+    want = [oracle.matmul_grouped(gb.Q4_K, rows, cols, m, offsets, x[xmap]) for m in mats]
+    pool = reflib.pool(4)
+    s = _PmScratch()
+    assert L.tr_pm_scratch_init(C.byref(s), 4, G, R, cols, R * cols) == 0
+    try:
+        xq = _aligned(T * int(L.tr_q4x_bytes(cols)))
+        L.tr_q4x_prepare(pool, x.ctypes.data, T, cols, xq.ctypes.data)
+        ws = [(Mat * G)(*[Mat(gb.Q4_K, rows, cols, mm.ctypes.data) for mm in m]) for m in mats]
+        y = np.full((R, rows), np.nan, dtype=np.float32)
+        assert L.tr_matmul_q4x_prepared(pool, C.cast(ws[0], C.c_void_p), offsets.ctypes.data, G, xq.ctypes.data,
+                                        xmap.ctypes.data, y.ctypes.data, C.byref(s)) == 1
+        assert same_bits(y, want[0])
+        ys = [np.full((R, rows), np.nan, dtype=np.float32) for _ in range(2)]
+        wp = (C.c_void_p * 2)(*[C.cast(w, C.c_void_p) for w in ws])
+        yp = (C.c_void_p * 2)(*[v.ctypes.data for v in ys])
+        assert L.tr_matmul_q4x_prepared_n(pool, wp, 2, offsets.ctypes.data, G, xq.ctypes.data, xmap.ctypes.data, yp,
+                                          C.byref(s)) == 1
+        assert same_bits(ys[0], want[0]) and same_bits(ys[1], want[1])
+    finally:
+        L.tr_pm_scratch_free(C.byref(s))
+        reflib.lib.ref_pool_destroy(pool)

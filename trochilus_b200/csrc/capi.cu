@@ -7,6 +7,7 @@
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 
+#include <atomic>
 #include <chrono>
 #include <cstdarg>
 #include <cstdlib>
@@ -1479,6 +1480,106 @@ bool kgrouped(const tr_mat *w, const int64_t *offsets, int64_t n_groups, const f
 
 void kfail(const char *fn) { fprintf(stderr, "trmoe: %s failed: %s\n", fn, g_err.c_str()); }
 
+// Q4_K's prepared road (tr_q4x_road, tr_q4x_prepare, tr_matmul_q4x_prepared(_n), tr_swiglu_prepare). The engine keeps
+// a pass's prepared input rows in its own buffer, one slot of tr_q4x_bytes(cols) bytes a row; here a slot holds the
+// row's floats at its start, and the GPU prepares the digits inside each matmul from them (the same floats give the
+// same digits, so every output is the reference road's).
+
+// the bytes of one slot: Trochilus's tr_q4x_bytes (src/kernels/kernels.c:489-492)
+int64_t q4x_slot(int64_t n) {
+    const int64_t b = 4 * n + n / 8 + n / 4 + n / 32;
+    return (b + 63) / 64 * 64;
+}
+
+// the weights the library's Q4_K road takes (its kernels' shape limits); the reference's q4x_road
+// (src/kernels/kernels.c:1122-1128) tests w[0] alone too, the other groups being of its type and shape by contract
+bool q4x_takes(const tr_mat *w) {
+    return w != nullptr && w[0].type == TRX_Q4_K && w[0].rows > 0 && w[0].rows % 16 == 0 && w[0].cols > 0 &&
+           w[0].cols % 256 == 0 && w[0].rows <= INT32_MAX / 2 && w[0].cols <= INT32_MAX / 2;
+}
+
+std::atomic<uint64_t> g_q4x_fused{0}; // tr_matmul_q4x_prepared_n's calls of more than one weight
+
+// y_m[p rows + r] = row r of ws[m][g(p)] . input row p, for m < n_w (Q4_K weights of one shape, the same groups);
+// input row p = the floats at the start of slot map[p] (map NULL: slot p) of xq. The slots the call reads go up in
+// one strided copy, the rows are gathered on the GPU, prepared once, and every weight reads them.
+bool kprepared(const tr_mat *const *ws, int n_w, const int64_t *offsets, int64_t n_groups, const uint8_t *xq,
+               const int64_t *map, float *const *ys) {
+    const int64_t rows = ws[0][0].rows, cols = ws[0][0].cols, n_in = offsets[n_groups], slot = q4x_slot(cols);
+    for (int m = 0; m < n_w; m++)
+        for (int64_t g = 0; g < n_groups; g++)
+            if (ws[m][g].type != TRX_Q4_K || ws[m][g].rows != rows || ws[m][g].cols != cols) {
+                set_err("weight %d group %lld has type %d %lldx%lld, not Q4_K %lldx%lld", m, (long long)g,
+                        (int)ws[m][g].type, (long long)ws[m][g].rows, (long long)ws[m][g].cols, (long long)rows,
+                        (long long)cols);
+                return false;
+            }
+    int64_t n_src = n_in;
+    if (map) {
+        n_src = 0;
+        for (int64_t p = 0; p < n_in; p++) {
+            if (map[p] < 0 || map[p] >= INT32_MAX / 2) {
+                set_err("map[%lld] = %lld is not a prepared row", (long long)p, (long long)map[p]);
+                return false;
+            }
+            n_src = std::max(n_src, map[p] + 1);
+        }
+    }
+    if (n_in > INT32_MAX / 2 || n_groups > 65535) { // (the groups are the grid's second dimension)
+        set_err("too large: %lld input rows in %lld groups", (long long)n_in, (long long)n_groups);
+        return false;
+    }
+    KCtx &c = kctx();
+    std::lock_guard<std::mutex> lock(c.mu);
+    if (!kinit(c) || !ck(cudaSetDevice(c.device), "cudaSetDevice")) return false;
+    std::vector<const uint8_t *> ptrs((size_t)(n_w * n_groups), nullptr);
+    for (int m = 0; m < n_w; m++)
+        for (int64_t g = 0; g < n_groups; g++)
+            if (offsets[g + 1] > offsets[g]) {
+                ptrs[(size_t)(m * n_groups + g)] = kmat(c, ws[m][g]);
+                if (ptrs[(size_t)(m * n_groups + g)] == nullptr) return false;
+            }
+    // device buffer: the slots' floats, the gathered rows (map given), the prepared rows (planes, sub-block sums,
+    // scales), the map, the offsets, then per weight its group table and output
+    const int64_t sb = align_up(n_src * cols * 4, 256), xb = map ? align_up(n_in * cols * 4, 256) : 0,
+                  pb = align_up(n_in * cols * 4, 256), bfb = align_up(n_in * (cols / 32) * 8, 256),
+                  scb = align_up(n_in * (cols / 256 + 1) * 8, 256), mb = map ? align_up(n_in * 4, 256) : 0,
+                  ob = align_up((n_groups + 1) * 4, 256), gb = align_up(n_groups * 8, 256),
+                  yb = align_up(n_in * rows * 4, 256);
+    if (!kreserve(&c.buf, &c.buf_bytes, sb + xb + pb + bfb + scb + mb + ob + n_w * (gb + yb))) return false;
+    uint8_t *b = c.buf;
+    float *dsrc = (float *)b;
+    float *dx = map ? (float *)(b + sb) : dsrc;
+    uint32_t *dq = (uint32_t *)(b + sb + xb);
+    double *dbf = (double *)(b + sb + xb + pb);
+    double *dsc = (double *)(b + sb + xb + pb + bfb);
+    int32_t *dmap = (int32_t *)(b + sb + xb + pb + bfb + scb);
+    int32_t *doff = (int32_t *)(b + sb + xb + pb + bfb + scb + mb);
+    uint8_t *per = b + sb + xb + pb + bfb + scb + mb + ob; // weight m: table at per + m (gb + yb), output after it
+    std::vector<int32_t> off32((size_t)n_groups + 1), map32(map ? (size_t)n_in : 0);
+    for (int64_t g = 0; g <= n_groups; g++) off32[(size_t)g] = (int32_t)offsets[g];
+    for (size_t p = 0; p < map32.size(); p++) map32[p] = (int32_t)map[p];
+    bool ok = ck(cudaMemcpy2DAsync(dsrc, (size_t)cols * 4, xq, (size_t)slot, (size_t)cols * 4, (size_t)n_src,
+                                   cudaMemcpyHostToDevice, c.st),
+                 "copy prepared rows") &&
+              ck(cudaMemcpyAsync(doff, off32.data(), off32.size() * 4, cudaMemcpyHostToDevice, c.st), "copy offsets");
+    if (ok && map) {
+        ok = ck(cudaMemcpyAsync(dmap, map32.data(), map32.size() * 4, cudaMemcpyHostToDevice, c.st), "copy map");
+        if (ok) trx_kapi_gather_k<<<(unsigned)n_in, 256, 0, c.st>>>(dsrc, dmap, (int)cols, dx);
+    }
+    for (int m = 0; ok && m < n_w; m++) {
+        const uint8_t **dg = (const uint8_t **)(per + m * (gb + yb));
+        float *dy = (float *)(per + m * (gb + yb) + gb);
+        ok = ck(cudaMemcpyAsync(dg, ptrs.data() + m * n_groups, (size_t)n_groups * 8, cudaMemcpyHostToDevice, c.st),
+                "copy table") &&
+             trx_kapi_grouped(TRX_Q4_K, rows, cols, dg, doff, (int)n_groups, (int)n_in, dx, dq, dbf, dsc, dy, c.st,
+                              m == 0) &&
+             ck(cudaGetLastError(), "grouped kernel") &&
+             ck(cudaMemcpyAsync(ys[m], dy, (size_t)(n_in * rows * 4), cudaMemcpyDeviceToHost, c.st), "copy y");
+    }
+    return ok && stream_wait(c.st);
+}
+
 } // namespace
 
 extern "C" void tr_matmul_grouped(tr_pool *pool, const tr_mat *w, const int64_t *offsets, int64_t n_groups,
@@ -1531,6 +1632,82 @@ extern "C" void tr_swiglu(tr_pool *pool, float *x, const float *y, int64_t n) {
              ck(cudaMemcpyAsync(x, dx, (size_t)n * 4, cudaMemcpyDeviceToHost, c.st), "copy back") && stream_wait(c.st);
     }
     if (!ok) kfail("tr_swiglu");
+}
+
+extern "C" void tr_matmul_s(tr_pool *pool, const tr_mat *w, const float *x, int64_t n_tokens, float *y, const void *s) {
+    (void)pool;
+    (void)s;
+    g_err.clear();
+    const int64_t offsets[2] = {0, n_tokens};
+    if (!kgrouped(w, offsets, 1, x, y)) kfail("tr_matmul_s");
+}
+
+extern "C" size_t tr_q4x_bytes(int64_t n) { return (size_t)q4x_slot(n); }
+
+extern "C" int tr_q4x_road(tr_pool *pool, const tr_mat *w, const int64_t *offsets, int64_t n_groups, const void *s) {
+    (void)pool;
+    (void)offsets;
+    (void)n_groups;
+    (void)s;
+    return q4x_takes(w) ? 1 : 0;
+}
+
+extern "C" void tr_q4x_prepare(tr_pool *pool, const float *x, int64_t n, int64_t cols, void *xq) {
+    (void)pool;
+    if (n <= 0 || cols <= 0) return;
+    const int64_t slot = q4x_slot(cols);
+    for (int64_t r = 0; r < n; r++) memcpy((uint8_t *)xq + r * slot, x + r * cols, (size_t)cols * 4);
+}
+
+extern "C" int tr_matmul_q4x_prepared(tr_pool *pool, const tr_mat *w, const int64_t *offsets, int64_t n_groups,
+                                      const void *xq, const int64_t *map, float *y, const void *s) {
+    (void)pool;
+    (void)s;
+    g_err.clear();
+    if (n_groups <= 0 || offsets[n_groups] <= 0 || w[0].rows <= 0) return 1;
+    if (!q4x_takes(w)) return 0;
+    float *const ys[1] = {y};
+    if (!kprepared(&w, 1, offsets, n_groups, (const uint8_t *)xq, map, ys)) kfail("tr_matmul_q4x_prepared");
+    return 1;
+}
+
+extern "C" int tr_matmul_q4x_prepared_n(tr_pool *pool, const tr_mat *const *w, int n_w, const int64_t *offsets,
+                                        int64_t n_groups, const void *xq, const int64_t *map, float *const *y,
+                                        const void *s) {
+    if (n_w < 1 || n_w > TRMOE_Q4X_MATS) return 0;
+    if (n_w == 1) return tr_matmul_q4x_prepared(pool, w[0], offsets, n_groups, xq, map, y[0], s);
+    g_err.clear();
+    if (n_groups <= 0 || offsets[n_groups] <= 0 || w[0][0].rows <= 0) return 1;
+    for (int m = 0; m < n_w; m++)
+        if (!q4x_takes(w[m]) || w[m][0].rows != w[0][0].rows || w[m][0].cols != w[0][0].cols) return 0;
+    g_q4x_fused.fetch_add(1, std::memory_order_relaxed);
+    if (!kprepared(w, n_w, offsets, n_groups, (const uint8_t *)xq, map, y)) kfail("tr_matmul_q4x_prepared_n");
+    return 1;
+}
+
+extern "C" uint64_t tr_q4x_fused_calls(void) { return g_q4x_fused.load(std::memory_order_relaxed); }
+
+extern "C" void tr_swiglu_prepare(tr_pool *pool, float *x, const float *y, int64_t n_rows, int64_t n, void *xq) {
+    (void)pool;
+    g_err.clear();
+    if (n_rows <= 0 || n <= 0) return;
+    const int64_t total = n_rows * n, slot = q4x_slot(n);
+    KCtx &c = kctx();
+    std::lock_guard<std::mutex> lock(c.mu);
+    bool ok = kinit(c) && ck(cudaSetDevice(c.device), "cudaSetDevice") &&
+              kreserve(&c.buf, &c.buf_bytes, 2 * align_up(total * 4, 256));
+    if (ok) {
+        float *dx = (float *)c.buf, *dy = (float *)(c.buf + align_up(total * 4, 256));
+        ok = ck(cudaMemcpyAsync(dx, x, (size_t)total * 4, cudaMemcpyHostToDevice, c.st), "copy x") &&
+             ck(cudaMemcpyAsync(dy, y, (size_t)total * 4, cudaMemcpyHostToDevice, c.st), "copy y") &&
+             trx_kapi_swiglu(dx, dy, total, c.st) && ck(cudaGetLastError(), "swiglu kernel") &&
+             ck(cudaMemcpyAsync(x, dx, (size_t)total * 4, cudaMemcpyDeviceToHost, c.st), "copy back") &&
+             ck(cudaMemcpy2DAsync(xq, (size_t)slot, dx, (size_t)n * 4, (size_t)n * 4, (size_t)n_rows,
+                                  cudaMemcpyDeviceToHost, c.st),
+                "copy prepared rows") &&
+             stream_wait(c.st);
+    }
+    if (!ok) kfail("tr_swiglu_prepare");
 }
 
 extern "C" void trmoe_kernel_cache_clear(void) {

@@ -96,12 +96,13 @@ __global__ void __launch_bounds__(256) trx_kapi_grouped_k(const uint8_t *const *
     }
 }
 
+// prep false (Q4_K): dq, dbf, dsc already hold dx's prepared rows (an earlier call on the same inputs wrote them)
 inline bool trx_kapi_grouped(int type, int64_t rows, int64_t cols, const uint8_t *const *dg, const int32_t *doff,
                              int n_groups, int n_in, const float *dx, uint32_t *dq, double *dbf, double *dsc, float *dy,
-                             cudaStream_t st) {
+                             cudaStream_t st, bool prep = true) {
     if (type == TRX_Q4_K) {
         const int64_t warps = (int64_t)n_in * (cols / 256);
-        trx_kapi_prep_q4x<<<(unsigned)((warps + 7) / 8), 256, 0, st>>>(dx, n_in, (int)cols, dq, dbf, dsc);
+        if (prep) trx_kapi_prep_q4x<<<(unsigned)((warps + 7) / 8), 256, 0, st>>>(dx, n_in, (int)cols, dq, dbf, dsc);
         dim3 grid((unsigned)((rows + 7) / 8), (unsigned)n_groups);
         trx_kapi_grouped_k<TRX_Q4_K><<<grid, 256, 0, st>>>(dg, doff, (int)rows, (int)cols, dx, dq, dbf, dsc, dy);
         return true;
@@ -124,6 +125,15 @@ inline bool trx_kapi_grouped(int type, int64_t rows, int64_t cols, const uint8_t
     else
         trx_kapi_grouped_k<TRX_F16><<<grid, 256, 0, st>>>(dg, doff, (int)rows, (int)cols, dx, dq, dbf, dsc, dy);
     return true;
+}
+
+// dst row p = src row map[p] (cols floats, a multiple of 4; 16-byte aligned rows), a block a row
+__global__ void __launch_bounds__(256) trx_kapi_gather_k(const float *__restrict__ src, const int32_t *__restrict__ map,
+                                                         int cols, float *__restrict__ dst) {
+    const int64_t p = blockIdx.x;
+    const float4 *s = reinterpret_cast<const float4 *>(src + (int64_t)map[p] * cols);
+    float4 *d = reinterpret_cast<float4 *>(dst + p * cols);
+    for (int i = threadIdx.x; i < cols / 4; i += blockDim.x) d[i] = s[i];
 }
 
 // tr_softmax over n values, one block: the max as the reference's serial scan from x[0], the exp of each

@@ -7,6 +7,7 @@ kernels would. It raises when the library is missing: there is no fallback of an
                   (src/models/olmoe.c:1845-1933) on the GPU, weights resident in HBM
   matmul_grouped  tr_matmul_grouped (src/kernels/kernels.h:244-245) on host arrays
   matmul, softmax, swiglu   tr_matmul, tr_softmax, tr_swiglu
+  q4x_road, q4x_prepare, matmul_q4x_prepared, swiglu_prepare   Q4_K's prepared road (kernels.h:280-300, 350)
 """
 from __future__ import annotations
 
@@ -28,7 +29,9 @@ EXPORTS = ["tr_gpu_moe_create", "tr_gpu_moe_free", "tr_gpu_moe_bytes", "tr_gpu_m
            "tr_matmul_grouped_s", "tr_softmax", "tr_swiglu", "trmoe_kernel_cache_clear", "tr_matmul_q4k_noalloc",
            "tr_gpu_moe_set_prefill", "tr_gpu_moe_ep_pack", "tr_gpu_moe_experts_dev", "tr_gpu_moe_ep_combine",
            "tr_gpu_moe_set_ffn_norm", "tr_gpu_moe_ffn", "tr_gpu_moe_ffn_dev", "tr_gpu_moe_ep_peer_region",
-           "tr_gpu_moe_ep_peer_open", "tr_gpu_moe_ep_dispatch", "tr_gpu_moe_ep_experts", "tr_gpu_moe_ep_peer_combine"]
+           "tr_gpu_moe_ep_peer_open", "tr_gpu_moe_ep_dispatch", "tr_gpu_moe_ep_experts", "tr_gpu_moe_ep_peer_combine",
+           "tr_matmul_s", "tr_q4x_bytes", "tr_q4x_road", "tr_q4x_prepare", "tr_matmul_q4x_prepared",
+           "tr_matmul_q4x_prepared_n", "tr_q4x_fused_calls", "tr_swiglu_prepare"]
 
 
 class Config(C.Structure):
@@ -101,6 +104,17 @@ def lib():
     L.tr_swiglu.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64]
     L.tr_matmul_q4k_noalloc.argtypes = [C.c_void_p, C.c_int64, C.c_int64, C.c_void_p, C.c_int64, C.c_void_p,
                                         C.c_void_p]
+    L.tr_matmul_s.argtypes = [C.c_void_p, C.POINTER(TrMat), C.c_void_p, C.c_int64, C.c_void_p, C.c_void_p]
+    L.tr_q4x_bytes.argtypes = [C.c_int64]
+    L.tr_q4x_bytes.restype = C.c_size_t
+    L.tr_q4x_road.argtypes = [C.c_void_p, C.POINTER(TrMat), C.c_void_p, C.c_int64, C.c_void_p]
+    L.tr_q4x_prepare.argtypes = [C.c_void_p, C.c_void_p, C.c_int64, C.c_int64, C.c_void_p]
+    L.tr_matmul_q4x_prepared.argtypes = [C.c_void_p, C.POINTER(TrMat), C.c_void_p, C.c_int64, C.c_void_p, C.c_void_p,
+                                         C.c_void_p, C.c_void_p]
+    L.tr_matmul_q4x_prepared_n.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_int64, C.c_void_p,
+                                           C.c_void_p, C.c_void_p, C.c_void_p]
+    L.tr_q4x_fused_calls.restype = C.c_uint64
+    L.tr_swiglu_prepare.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_int64, C.c_void_p]
     _lib = L
     return L
 
@@ -345,6 +359,76 @@ def matmul(type_: int, rows: int, cols: int, w: np.ndarray, x: np.ndarray):
     if err:
         raise RuntimeError(f"tr_matmul: {err}")
     return y
+
+
+def matmul_s(type_: int, rows: int, cols: int, w: np.ndarray, x: np.ndarray):
+    """tr_matmul_s on host arrays (tr_matmul's result; no scratch)."""
+    m = TrMat(type_, rows, cols, w.ctypes.data)
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    y = np.full((x.shape[0], rows), np.nan, dtype=np.float32)
+    lib().tr_matmul_s(None, C.byref(m), _p(x), x.shape[0], _p(y), None)
+    err = last_error()
+    if err:
+        raise RuntimeError(f"tr_matmul_s: {err}")
+    return y
+
+
+def q4x_bytes(cols: int) -> int:
+    """tr_q4x_bytes: the bytes of one prepared row's slot"""
+    return int(lib().tr_q4x_bytes(cols))
+
+
+def q4x_road(type_: int, rows: int, cols: int) -> int:
+    """tr_q4x_road for weights of this type and shape (the groups and scratch are not consulted)"""
+    m = TrMat(type_, rows, cols, None)
+    return int(lib().tr_q4x_road(None, C.byref(m), None, 1, None))
+
+
+def q4x_prepare(x: np.ndarray, xq: np.ndarray | None = None) -> np.ndarray:
+    """tr_q4x_prepare: x (n x cols) into slots of tr_q4x_bytes(cols) bytes (a uint8 buffer, made when None)"""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    n, cols = x.shape
+    if xq is None:
+        xq = np.zeros(n * q4x_bytes(cols), dtype=np.uint8)
+    lib().tr_q4x_prepare(None, _p(x), n, cols, _p(xq))
+    return xq
+
+
+def matmul_q4x_prepared(rows: int, cols: int, mats_list, offsets, xq: np.ndarray, map_=None):
+    """tr_matmul_q4x_prepared (one weight) or tr_matmul_q4x_prepared_n (several) on host arrays: mats_list[m][g] =
+    weight m's group g (rows x row_bytes uint8, Q4_K); returns (the call's return value, [y_m])."""
+    n_w, n = len(mats_list), len(mats_list[0])
+    ws = [(TrMat * n)(*[TrMat(Q4_K, rows, cols, mm.ctypes.data) for mm in mats]) for mats in mats_list]
+    off = np.ascontiguousarray(offsets, dtype=np.int64)
+    mp = None if map_ is None else np.ascontiguousarray(map_, dtype=np.int64)
+    ys = [np.full((int(off[-1]), rows), np.nan, dtype=np.float32) for _ in range(n_w)]
+    if n_w == 1:
+        rc = lib().tr_matmul_q4x_prepared(None, ws[0], _p(off), n, _p(xq), _p(mp), _p(ys[0]), None)
+    else:
+        wp = (C.c_void_p * n_w)(*[C.cast(w, C.c_void_p) for w in ws])
+        yp = (C.c_void_p * n_w)(*[y.ctypes.data for y in ys])
+        rc = lib().tr_matmul_q4x_prepared_n(None, wp, n_w, _p(off), n, _p(xq), _p(mp), yp, None)
+    err = last_error()
+    if err:
+        raise RuntimeError(f"tr_matmul_q4x_prepared: {err}")
+    return rc, ys
+
+
+def q4x_fused_calls() -> int:
+    return int(lib().tr_q4x_fused_calls())
+
+
+def swiglu_prepare(x: np.ndarray, y: np.ndarray):
+    """tr_swiglu_prepare on host arrays (n_rows x n): returns (x after, the slots)"""
+    out = np.array(x, dtype=np.float32, copy=True)
+    y = np.ascontiguousarray(y, dtype=np.float32)
+    n_rows, n = out.shape
+    xq = np.zeros(n_rows * q4x_bytes(n), dtype=np.uint8)
+    lib().tr_swiglu_prepare(None, _p(out), _p(y), n_rows, n, _p(xq))
+    err = last_error()
+    if err:
+        raise RuntimeError(f"tr_swiglu_prepare: {err}")
+    return out, xq
 
 
 def kernel_cache_clear():
