@@ -759,6 +759,29 @@ static bool takes_fused(const tr_gpu_moe *m, int T) {
            (int)m->cfg.n_expert + T <= m->grid_fused && fused_stages(m, T, &sg, &sd);
 }
 
+// the fused decode kernel (fused_layer.cuh) over T rows of S's shape: one cooperative launch, a CTA an SM, with sg / sd
+// stages (fused_stages) and the shared memory their layout takes
+static int launch_fused(tr_gpu_moe *m, const TrxLayer &L, const TrxShape &S, const float *normed, int T, const TrxWork &w,
+                        float *x_io, float *ffn_out, uint32_t epoch, int sg, int sd, cudaStream_t st, const char *what) {
+    const tr_gpu_moe_config &c = m->cfg;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)m->grid_fused);
+    cfg.blockDim = dim3(TRX_FU_THREADS);
+    cfg.dynamicSmemBytes =
+        trx_fused_layout(c.gate_type, c.down_type, S.H, S.F, T, S.k, sg, sd, S.E, m->grid_fused).total;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return ck(cudaLaunchKernelEx(&cfg, layer_fn(c.gate_type, c.down_type), L, S, normed, T, w, m->sync, x_io, ffn_out,
+                                 epoch, sg, sd),
+              what)
+               ? 0
+               : -1;
+}
+
 static int launch_ffn_norm(tr_gpu_moe *m, int64_t layer, const float *x, int64_t n_tok, float *normed, cudaStream_t st);
 
 // done: when the fused kernel takes the call, the device address of the word it writes its epoch to when every
@@ -844,21 +867,7 @@ static int launch_layer(tr_gpu_moe *m, int64_t layer, const float *d_normed, int
         if (epoch == 0) epoch = ++m->epoch & 0x7fffffffu; // 0 is the completion word's initial value
         w.host_done = done;
         if (epoch_out) *epoch_out = epoch;
-        cudaLaunchConfig_t cfg = {};
-        cfg.gridDim = dim3((unsigned)m->grid_fused);
-        cfg.blockDim = dim3(TRX_FU_THREADS);
-        cfg.dynamicSmemBytes = trx_fused_layout(c.gate_type, c.down_type, S.H, S.F, T, S.k, sg, sd, E, m->grid_fused).total;
-        cfg.stream = st;
-        cudaLaunchAttribute attr[1];
-        attr[0].id = cudaLaunchAttributeCooperative;
-        attr[0].val.cooperative = 1;
-        cfg.attrs = attr;
-        cfg.numAttrs = 1;
-        return ck(cudaLaunchKernelEx(&cfg, layer_fn(c.gate_type, c.down_type), L, S, d_normed, T, w, m->sync, d_x, ffn,
-                                     epoch, sg, sd),
-                  "fused layer launch")
-                   ? 0
-                   : -1;
+        return launch_fused(m, L, S, d_normed, T, w, d_x, ffn, epoch, sg, sd, st, "fused layer launch");
     }
     mark(0);
     if (first <= 0 && 0 <= last) {
@@ -1150,22 +1159,7 @@ extern "C" int tr_gpu_moe_experts_dev(tr_gpu_moe *m, int64_t layer, const float 
         TrxWork w = m->work;
         w.ext_ids = d_ids;
         const uint32_t epoch = (++m->epoch & 0x7fffffffu) | 1u;
-        cudaLaunchConfig_t cfg = {};
-        cfg.gridDim = dim3((unsigned)m->grid_fused);
-        cfg.blockDim = dim3(TRX_FU_THREADS);
-        cfg.dynamicSmemBytes = trx_fused_layout(c.gate_type, c.down_type, (int)H, (int)F, (int)n, 1, sg, sd, (int)E,
-                                                m->grid_fused).total;
-        cfg.stream = st;
-        cudaLaunchAttribute attr[1];
-        attr[0].id = cudaLaunchAttributeCooperative;
-        attr[0].val.cooperative = 1;
-        cfg.attrs = attr;
-        cfg.numAttrs = 1;
-        return ck(cudaLaunchKernelEx(&cfg, layer_fn(c.gate_type, c.down_type), L, S, d_rows, (int)n, w, m->sync,
-                                     (float *)nullptr, d_out, epoch, sg, sd),
-                  "fused experts launch")
-                   ? 0
-                   : -1;
+        return launch_fused(m, L, S, d_rows, (int)n, w, nullptr, d_out, epoch, sg, sd, st, "fused experts launch");
     }
     // scratch: sort (offsets, place, xmap), grouped rows, gate and up outputs, down output, prepared inputs
     const int64_t so = align_up((E + 8 + 2 * n) * 4, 256), xb = align_up(n * H * 4, 256), gb = align_up(n * F * 4, 256),
@@ -1319,22 +1313,8 @@ extern "C" int tr_gpu_moe_ep_experts(tr_gpu_moe *m, int64_t layer, void *stream)
     w.ext_ids = (const int32_t *)(m->epp_region + ids);
     w.ep = m->epp_dev;
     const uint32_t epoch = (++m->epoch & 0x7fffffffu) | 1u;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)m->grid_fused);
-    cfg.blockDim = dim3(TRX_FU_THREADS);
-    cfg.dynamicSmemBytes = trx_fused_layout(c.gate_type, c.down_type, (int)H, (int)F, (int)n, 1, sg, sd, (int)E,
-                                            m->grid_fused).total;
-    cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeCooperative;
-    attr[0].val.cooperative = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    return ck(cudaLaunchKernelEx(&cfg, layer_fn(c.gate_type, c.down_type), L, S, (const float *)(m->epp_region + rows),
-                                 (int)n, w, m->sync, (float *)nullptr, (float *)nullptr, epoch, sg, sd),
-              "ep experts launch")
-               ? 0
-               : -1;
+    return launch_fused(m, L, S, (const float *)(m->epp_region + rows), (int)n, w, nullptr, nullptr, epoch, sg, sd, st,
+                        "ep experts launch");
 }
 
 extern "C" int tr_gpu_moe_ep_peer_combine(tr_gpu_moe *m, const float *d_sel_w, const int32_t *d_place, int64_t n_tok,
