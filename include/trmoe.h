@@ -77,6 +77,23 @@ TRMOE_API int tr_gpu_moe_set_layer(tr_gpu_moe *m, int64_t layer, const void *rou
                          const void *const *gate, const void *const *up, const void *const *down, char *err,
                          size_t err_len);
 
+/* The model loader (the rank-4 next step beyond the MoE block): an OLMoE GGUF file (versions 2 and 3) straight into
+ * the context's resident layout, in place of the reference's load (src/models/olmoe.c:541-641, 895-925) and its
+ * expert store (src/memory/experts.h): every layer's experts live in HBM, none on the host.
+ * tr_gpu_moe_config_from_gguf fills cfg's n_layers, n_expert, n_used, n_embd, n_ff, norm_topk and the three types
+ * from the file's olmoe.* metadata and its ffn_gate_inp / ffn_*_exps tensors (max_tokens is left as the caller set
+ * it), and *rms_eps (optional) from olmoe.attention.layer_norm_rms_epsilon. router_type is BF16 when every router is
+ * BF16 or an F32 whose values are all bfloat16 (the reference keeps those as BF16, olmoe.c:391), else F32. A file
+ * whose layers use different expert types is refused (a context takes one gate/up type and one down type). Every
+ * count, length and offset is checked against the file's size. Host only. 0, or -1 with a message. */
+TRMOE_API int tr_gpu_moe_config_from_gguf(const char *path, tr_gpu_moe_config *cfg, float *rms_eps, char *err,
+                                          size_t err_len);
+/* Sets every layer of m from the file: tr_gpu_moe_set_layer with the router (narrowed to BF16 or widened to F32 as
+ * the context's type asks) and the 64 experts' slices of each stacked tensor, and tr_gpu_moe_set_ffn_norm with the
+ * layer's ffn_norm and the file's epsilon. The file must give m's configuration (tr_gpu_moe_config_from_gguf's).
+ * The file is mapped read-only while the call runs. 0, or -1 with a message. */
+TRMOE_API int tr_gpu_moe_load_gguf(tr_gpu_moe *m, const char *path, char *err, size_t err_len);
+
 /* Replaces: forward_layer's MoE block from the router to the mix (src/models/olmoe.c:1845-1933), the
  * hook sitting where tr_gpu_attn_decode sits for the attention (olmoe.c:1790-1797).
  * normed: n_tok rows of n_embd (the ffn_norm output); x_inout: the residual stream, n_tok rows of

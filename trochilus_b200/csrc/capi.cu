@@ -26,6 +26,7 @@
 #include "moe_kernels.cuh"
 #include "kernel_api.cuh"
 #include "fused_layer.cuh"
+#include "gguf_file.h"
 #include "prefill.cuh"
 #include "ep.cuh"
 #include "ffn_norm.cuh"
@@ -1103,6 +1104,217 @@ extern "C" int tr_gpu_moe_ffn_dev(tr_gpu_moe *m, int64_t layer, int64_t n_tok, f
     cudaStream_t st = stream ? (cudaStream_t)stream : m->stream;
     return launch_layer(m, layer, m->d_normed, n_tok, d_x_inout, out, st, 0, 3, nullptr, nullptr, d_x_inout,
                         d_normed_out);
+}
+
+// ---------------------------------------------------------------------------------------------
+// the model loader: an OLMoE GGUF file straight into the context's resident layout (no expert store)
+
+namespace {
+
+// the MoE block's tensors of one layer (src/models/olmoe.c:605-641, 901-906)
+struct GgufLayer {
+    const TrxGgufTensor *router, *norm, *gate, *up, *down;
+};
+
+// a tensor of the given ggml dimensions (olmoe.c's check_shape / find_experts): NULL with the reason in err
+const TrxGgufTensor *gguf_need(const TrxGguf &g, const std::string &name, uint32_t n_dims, uint64_t ne0, uint64_t ne1,
+                               uint64_t ne2, std::string &err) {
+    const TrxGgufTensor *t = g.tensor(name);
+    if (t == nullptr) {
+        err = "missing tensor '" + name + "'";
+        return nullptr;
+    }
+    const uint64_t want[3] = {ne0, ne1, ne2};
+    bool ok = t->n_dims == n_dims;
+    for (uint32_t d = 0; ok && d < n_dims; d++) ok = t->ne[d] == want[d];
+    if (!ok) {
+        err = "tensor '" + name + "' has shape [";
+        for (uint32_t d = 0; d < t->n_dims; d++) err += (d ? ", " : "") + std::to_string(t->ne[d]);
+        err += "], expected [";
+        for (uint32_t d = 0; d < n_dims; d++) err += (d ? ", " : "") + std::to_string(want[d]);
+        err += "]";
+        return nullptr;
+    }
+    return t;
+}
+
+// every value of an F32 tensor a bfloat16 (its low 16 bits zero), as Trochilus's tr_f32_to_bf16_exact asks
+// (src/kernels/kernels.h:82-85) before it keeps an F32 router as BF16
+bool gguf_bf16_exact(const TrxGgufTensor &t, const uint8_t *p) {
+    for (uint64_t i = 0; i < t.n_bytes / 4; i++) {
+        uint32_t v;
+        memcpy(&v, p + 4 * i, 4);
+        if (v & 0xffffu) return false;
+    }
+    return true;
+}
+
+// The file's MoE configuration (olmoe.c:541-575's metadata, the router, ffn_norm and expert tensors of every layer),
+// with *eps its RMSNorm epsilon and layers[L] each layer's tensors. The context takes one gate/up type and one down
+// type: a file whose layers differ is refused. The router type is BF16 when every layer's router is BF16 or an F32
+// whose values are all bfloat16 (the reference keeps those as BF16, olmoe.c:391), else F32.
+bool gguf_config(const TrxGguf &g, tr_gpu_moe_config &cfg, float &eps, std::vector<GgufLayer> &layers, std::string &err) {
+    std::string arch;
+    if (g.get_str("general.architecture", arch) && arch != "olmoe") {
+        err = "general.architecture is '" + arch + "', not 'olmoe'";
+        return false;
+    }
+    uint32_t nl = 0, H = 0, F = 0, E = 0, k = 0;
+    const char *need[5] = {"olmoe.block_count", "olmoe.embedding_length", "olmoe.feed_forward_length",
+                           "olmoe.expert_count", "olmoe.expert_used_count"};
+    uint32_t *dst[5] = {&nl, &H, &F, &E, &k};
+    for (int i = 0; i < 5; i++)
+        if (!g.get_u32(need[i], *dst[i])) {
+            err = std::string("missing metadata key '") + need[i] + "'";
+            return false;
+        }
+    if (!g.get_f32("olmoe.attention.layer_norm_rms_epsilon", eps)) {
+        err = "missing metadata key 'olmoe.attention.layer_norm_rms_epsilon'";
+        return false;
+    }
+    bool norm_topk = false;
+    g.get_bool("olmoe.expert_weights_norm", norm_topk);
+    if (nl == 0 || H == 0 || F == 0 || E == 0 || k == 0) {
+        err = "invalid (zero) hyperparameter in metadata";
+        return false;
+    }
+    if (k > E) {
+        err = "olmoe.expert_used_count exceeds olmoe.expert_count";
+        return false;
+    }
+    layers.assign(nl, GgufLayer{});
+    bool all_bf16 = true;
+    for (uint32_t L = 0; L < nl; L++) {
+        const std::string b = "blk." + std::to_string(L) + ".";
+        GgufLayer &y = layers[L];
+        if (!(y.router = gguf_need(g, b + "ffn_gate_inp.weight", 2, H, E, 0, err)) ||
+            !(y.norm = gguf_need(g, b + "ffn_norm.weight", 1, H, 0, 0, err)) ||
+            !(y.gate = gguf_need(g, b + "ffn_gate_exps.weight", 3, H, F, E, err)) ||
+            !(y.up = gguf_need(g, b + "ffn_up_exps.weight", 3, H, F, E, err)) ||
+            !(y.down = gguf_need(g, b + "ffn_down_exps.weight", 3, F, H, E, err)))
+            return false;
+        if (y.router->type != TRX_F32 && y.router->type != TRX_BF16) {
+            err = b + "ffn_gate_inp.weight has type " + std::to_string(y.router->type) + " (F32 or BF16 taken)";
+            return false;
+        }
+        if (y.norm->type != TRX_F32) {
+            err = b + "ffn_norm.weight is not F32";
+            return false;
+        }
+        if (y.up->type != y.gate->type || y.gate->type != layers[0].gate->type || y.down->type != layers[0].down->type) {
+            err = "layer " + std::to_string(L) + "'s expert types differ from layer 0's (gate/up " +
+                  std::to_string(layers[0].gate->type) + ", down " + std::to_string(layers[0].down->type) +
+                  "): a context takes one gate/up type and one down type";
+            return false;
+        }
+        if (y.router->type == TRX_F32 && all_bf16) all_bf16 = gguf_bf16_exact(*y.router, g.bytes(*y.router));
+    }
+    cfg.n_layers = nl;
+    cfg.n_expert = E;
+    cfg.n_used = k;
+    cfg.n_embd = H;
+    cfg.n_ff = F;
+    cfg.norm_topk = norm_topk ? 1 : 0;
+    cfg.router_type = all_bf16 ? TRX_BF16 : TRX_F32;
+    cfg.gate_type = (int32_t)layers[0].gate->type;
+    cfg.down_type = (int32_t)layers[0].down->type;
+    return true;
+}
+
+} // namespace
+
+extern "C" int tr_gpu_moe_config_from_gguf(const char *path, tr_gpu_moe_config *cfg, float *rms_eps, char *err,
+                                           size_t err_len) {
+    g_err.clear();
+    if (path == nullptr || cfg == nullptr) {
+        set_err("bad arguments to tr_gpu_moe_config_from_gguf");
+        put_err(err, err_len);
+        return -1;
+    }
+    TrxGguf g;
+    std::string e;
+    tr_gpu_moe_config c = *cfg;
+    float eps = 0.0f;
+    std::vector<GgufLayer> layers;
+    if (!g.open(path, e) || !gguf_config(g, c, eps, layers, e)) {
+        set_err("%s", e.c_str());
+        put_err(err, err_len);
+        return -1;
+    }
+    *cfg = c;
+    if (rms_eps) *rms_eps = eps;
+    return 0;
+}
+
+extern "C" int tr_gpu_moe_load_gguf(tr_gpu_moe *m, const char *path, char *err, size_t err_len) {
+    g_err.clear();
+    if (m == nullptr || path == nullptr) {
+        set_err("bad arguments to tr_gpu_moe_load_gguf");
+        put_err(err, err_len);
+        return -1;
+    }
+    TrxGguf g;
+    std::string e;
+    tr_gpu_moe_config f = m->cfg;
+    float eps = 0.0f;
+    std::vector<GgufLayer> layers;
+    if (!g.open(path, e) || !gguf_config(g, f, eps, layers, e)) {
+        set_err("%s", e.c_str());
+        put_err(err, err_len);
+        return -1;
+    }
+    const tr_gpu_moe_config &c = m->cfg;
+    if (f.n_layers != c.n_layers || f.n_expert != c.n_expert || f.n_used != c.n_used || f.n_embd != c.n_embd ||
+        f.n_ff != c.n_ff || f.norm_topk != c.norm_topk || f.gate_type != c.gate_type || f.down_type != c.down_type ||
+        (f.router_type == TRX_F32 && c.router_type == TRX_BF16)) {
+        set_err("the file's MoE configuration (layers %lld, experts %lld of %lld, %lldx%lld, norm_topk %d, router %d, "
+                "gate/up %d, down %d) is not the context's (tr_gpu_moe_config_from_gguf gives it)",
+                (long long)f.n_layers, (long long)f.n_used, (long long)f.n_expert, (long long)f.n_embd,
+                (long long)f.n_ff, f.norm_topk, f.router_type, f.gate_type, f.down_type);
+        put_err(err, err_len);
+        return -1;
+    }
+    const int64_t E = c.n_expert, H = c.n_embd, F = c.n_ff;
+    const int64_t gate_bytes = trx_row_bytes(c.gate_type, H) * F, down_bytes = trx_row_bytes(c.down_type, F) * H;
+    std::vector<const void *> gp((size_t)E), up((size_t)E), dp((size_t)E);
+    std::vector<uint16_t> r16;
+    std::vector<float> r32;
+    for (int64_t L = 0; L < c.n_layers; L++) {
+        const GgufLayer &y = layers[(size_t)L];
+        // the router in the context's type: as stored, narrowed (bfloat16-exact F32) or widened (BF16 into F32)
+        const void *router = g.bytes(*y.router);
+        const int64_t nr = E * H;
+        if (y.router->type == TRX_F32 && c.router_type == TRX_BF16) {
+            r16.resize((size_t)nr);
+            for (int64_t i = 0; i < nr; i++) {
+                uint32_t v;
+                memcpy(&v, (const uint8_t *)router + 4 * i, 4);
+                r16[(size_t)i] = (uint16_t)(v >> 16);
+            }
+            router = r16.data();
+        } else if (y.router->type == TRX_BF16 && c.router_type == TRX_F32) {
+            r32.resize((size_t)nr);
+            for (int64_t i = 0; i < nr; i++) {
+                uint16_t v;
+                memcpy(&v, (const uint8_t *)router + 2 * i, 2);
+                const uint32_t w = (uint32_t)v << 16;
+                memcpy(&r32[(size_t)i], &w, 4);
+            }
+            router = r32.data();
+        }
+        // expert e of a stacked tensor at byte e out row_bytes(in) (olmoe.c:466-472)
+        for (int64_t x = 0; x < E; x++) {
+            gp[(size_t)x] = g.bytes(*y.gate) + x * gate_bytes;
+            up[(size_t)x] = g.bytes(*y.up) + x * gate_bytes;
+            dp[(size_t)x] = g.bytes(*y.down) + x * down_bytes;
+        }
+        if (tr_gpu_moe_set_layer(m, L, router, nullptr, gp.data(), up.data(), dp.data(), err, err_len) != 0)
+            return -1;
+        float norm_host[8192];
+        memcpy(norm_host, g.bytes(*y.norm), (size_t)H * 4); // (the mapping's bytes may be unaligned for floats)
+        if (tr_gpu_moe_set_ffn_norm(m, L, norm_host, eps, err, err_len) != 0) return -1;
+    }
+    return 0;
 }
 
 // ---------------------------------------------------------------------------------------------

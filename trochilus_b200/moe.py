@@ -31,7 +31,8 @@ EXPORTS = ["tr_gpu_moe_create", "tr_gpu_moe_free", "tr_gpu_moe_bytes", "tr_gpu_m
            "tr_gpu_moe_set_ffn_norm", "tr_gpu_moe_ffn", "tr_gpu_moe_ffn_dev", "tr_gpu_moe_ep_peer_region",
            "tr_gpu_moe_ep_peer_open", "tr_gpu_moe_ep_dispatch", "tr_gpu_moe_ep_experts", "tr_gpu_moe_ep_peer_combine",
            "tr_matmul_s", "tr_q4x_bytes", "tr_q4x_road", "tr_q4x_prepare", "tr_matmul_q4x_prepared",
-           "tr_matmul_q4x_prepared_n", "tr_q4x_fused_calls", "tr_swiglu_prepare"]
+           "tr_matmul_q4x_prepared_n", "tr_q4x_fused_calls", "tr_swiglu_prepare", "tr_gpu_moe_config_from_gguf",
+           "tr_gpu_moe_load_gguf"]
 
 
 class Config(C.Structure):
@@ -115,6 +116,9 @@ def lib():
                                            C.c_void_p, C.c_void_p, C.c_void_p]
     L.tr_q4x_fused_calls.restype = C.c_uint64
     L.tr_swiglu_prepare.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_int64, C.c_void_p]
+    L.tr_gpu_moe_config_from_gguf.argtypes = [C.c_char_p, C.POINTER(Config), C.POINTER(C.c_float), C.c_char_p,
+                                              C.c_size_t]
+    L.tr_gpu_moe_load_gguf.argtypes = [C.c_void_p, C.c_char_p, C.c_char_p, C.c_size_t]
     _lib = L
     return L
 
@@ -179,6 +183,21 @@ class GpuMoe:
         err = C.create_string_buffer(512)
         if lib().tr_gpu_moe_set_ffn_norm(self.h, layer, _p(weight), eps, err, 512) != 0:
             raise RuntimeError(f"tr_gpu_moe_set_ffn_norm: {err.value.decode()}")
+
+    def load_gguf(self, path: str):
+        """tr_gpu_moe_load_gguf: every layer's router, experts and ffn_norm from an OLMoE GGUF file"""
+        err = C.create_string_buffer(512)
+        if lib().tr_gpu_moe_load_gguf(self.h, os.fsencode(path), err, 512) != 0:
+            raise RuntimeError(f"tr_gpu_moe_load_gguf: {err.value.decode()}")
+
+    @classmethod
+    def from_gguf(cls, path: str, max_tokens: int, device: int = 0) -> "GpuMoe":
+        """a context made from the file's configuration (tr_gpu_moe_config_from_gguf) and loaded from it"""
+        cfg, _ = config_from_gguf(path, max_tokens)
+        m = cls(cfg.n_layers, cfg.n_expert, cfg.n_used, cfg.n_embd, cfg.n_ff, cfg.router_type, cfg.gate_type,
+                cfg.down_type, max_tokens, norm_topk=cfg.norm_topk, device=device)
+        m.load_gguf(path)
+        return m
 
     def ffn(self, layer: int, x: np.ndarray, want_normed: bool = False, want_sel: bool = False):
         """tr_gpu_moe_ffn on host arrays: x (T x n_embd, float32, C order) normalised by the layer's ffn_norm and
@@ -331,6 +350,16 @@ class GpuMoe:
             self.close()
         except Exception:
             pass
+
+
+def config_from_gguf(path: str, max_tokens: int = 1) -> tuple[Config, float]:
+    """tr_gpu_moe_config_from_gguf: the context configuration an OLMoE GGUF file gives, and its RMSNorm epsilon"""
+    cfg = Config(0, 0, 0, 0, 0, 0, 0, 0, 0, max_tokens)
+    eps = C.c_float(0.0)
+    err = C.create_string_buffer(512)
+    if lib().tr_gpu_moe_config_from_gguf(os.fsencode(path), C.byref(cfg), C.byref(eps), err, 512) != 0:
+        raise RuntimeError(f"tr_gpu_moe_config_from_gguf: {err.value.decode()}")
+    return cfg, float(eps.value)
 
 
 def matmul_grouped(type_: int, rows: int, cols: int, mats, offsets, x: np.ndarray, use_s: bool = False):
