@@ -95,9 +95,23 @@ void orc_expf_many(const float *x, float *y, int64_t n) {
     for (int64_t i = 0; i < n; i++) y[i] = orc_expf(x[i]);
 }
 
+/* ---- planted mistakes: tests/test_oracle.py sets one at a time to show that the bit comparisons the GPU tests
+ * rely on see a wrong step (the reference's "a test never seen red proves nothing", tools/mutate_gpu.sh:2-10).
+ * 0, the default, plants nothing; every mistake changes one step of the definition:
+ *  1 the lanes joined in sequence instead of by the tree    2 the mix adds the slots in decreasing order
+ *  3 argmax ties go to the higher id                         4 Q4_K's super-block values summed in float
+ *  5 SwiGLU as v (1 / (1 + e))                               6 RMSNorm as x (inv w) ---- */
+static int g_mutation = 0;
+void orc_set_mutation(int m) { g_mutation = m; }
+
 /* ---- the lane contract ---- */
 
 static float lane_tree(const float l[LANES]) {
+    if (g_mutation == 1) {
+        float s = l[0];
+        for (int i = 1; i < LANES; i++) s = s + l[i];
+        return s;
+    }
     const float a = (l[0] + l[1]) + (l[2] + l[3]), b = (l[4] + l[5]) + (l[6] + l[7]);
     const float c = (l[8] + l[9]) + (l[10] + l[11]), d = (l[12] + l[13]) + (l[14] + l[15]);
     return (a + b) + (c + d);
@@ -208,8 +222,13 @@ float orc_dot_row(int type, const void *row_, const float *x, int64_t n) {
     const unsigned char *row = (const unsigned char *)row_;
     if (type == ORC_Q4_K) {
         double y = 0.0;
-        for (int64_t s = 0; s < n / 256; s++) y = y + q4k_block(row + 144 * s, x + 256 * s);
-        return (float)y;
+        float yf = 0.0f;
+        for (int64_t s = 0; s < n / 256; s++) {
+            const double v = q4k_block(row + 144 * s, x + 256 * s);
+            y = y + v;
+            yf = yf + (float)v;
+        }
+        return g_mutation == 4 ? yf : (float)y;
     }
     float *w = (float *)malloc((size_t)n * sizeof(float));
     dequant_lane_row(type, row, n, w);
@@ -247,7 +266,7 @@ void orc_softmax(float *x, int64_t n) {
 void orc_swiglu(float *x, const float *y, int64_t n) {
     for (int64_t i = 0; i < n; i++) {
         const float e = orc_expf(-x[i]);
-        const float silu = x[i] / (1.0f + e);
+        const float silu = g_mutation == 5 ? x[i] * (1.0f / (1.0f + e)) : x[i] / (1.0f + e);
         x[i] = silu * y[i];
     }
 }
@@ -265,6 +284,10 @@ void orc_rmsnorm(float *x, const float *w, int64_t n, float eps) {
     const float mean = sumsq / (float)n;
     const float inv = 1.0f / sqrtf(mean + eps);
     for (int64_t i = 0; i < n; i++) {
+        if (g_mutation == 6) {
+            x[i] = x[i] * (inv * w[i]);
+            continue;
+        }
         const float t = x[i] * inv;
         x[i] = t * w[i];
     }
@@ -286,7 +309,7 @@ void orc_route(float *probs, int64_t T, int64_t E, int64_t k, int norm_topk, int
             int64_t best = -1;
             float bv = 0.0f;
             for (int64_t e = 0; e < E; e++)
-                if (!taken[e] && (best < 0 || r[e] > bv)) {
+                if (!taken[e] && (best < 0 || r[e] > bv || (g_mutation == 3 && r[e] == bv))) {
                     best = e;
                     bv = r[e];
                 }
@@ -373,8 +396,8 @@ int orc_moe_layer(const orc_moe_desc *d, const float *normed, int64_t T, float *
     orc_matmul_grouped(d->down_type, H, F, d->down, offsets, E, h1, h3);
     for (int64_t t = 0; t < T; t++) {
         for (int64_t c = 0; c < H; c++) out[c] = 0.0f;
-        for (int64_t s = 0; s < k; s++) {
-            const int64_t j = t * k + s;
+        for (int64_t i = 0; i < k; i++) {
+            const int64_t s = g_mutation == 2 ? k - 1 - i : i, j = t * k + s;
             const float w = sel_w[j], *row = h3 + place[j] * H;
             for (int64_t c = 0; c < H; c++) out[c] = out[c] + w * row[c];
         }

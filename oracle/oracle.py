@@ -117,6 +117,12 @@ class Oracle(_Common):
         L.orc_moe_layer.argtypes = [C.POINTER(Desc), C.c_void_p, C.c_int64, C.c_void_p] + [C.c_void_p] * 8
         L.orc_row_bytes.restype = C.c_size_t
         L.orc_row_bytes.argtypes = [C.c_int, C.c_int64]
+        L.orc_set_mutation.argtypes = [C.c_int]
+
+    def set_mutation(self, m: int):
+        """plants mistake m in the restatement (moe_oracle.c lists them; 0: none). Tests only, to show that a
+        comparison sees a wrong step; every caller sets it back to 0."""
+        self.lib.orc_set_mutation(m)
 
     def matmul_grouped(self, type_, rows, cols, mats, offsets, x):
         offsets = np.ascontiguousarray(offsets, dtype=np.int64)

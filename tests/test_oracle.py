@@ -233,3 +233,47 @@ def test_reference_prepared_road_equals_float_road(oracle, reflib, rows, cols):
     finally:
         L.tr_pm_scratch_free(C.byref(s))
         reflib.lib.ref_pool_destroy(pool)
+
+
+@pytest.mark.parametrize("m,what", [(1, "lanes joined in sequence"), (2, "mix in decreasing slot order"),
+                                    (3, "ties to the higher id"), (4, "Q4_K blocks summed in float"),
+                                    (5, "SwiGLU by a reciprocal"), (6, "RMSNorm associated the other way")])
+def test_planted_mistakes_are_seen(oracle, reflib, m, what):
+    """Each mistake planted in the restatement (one step of the definition changed) makes its result differ from
+    the reference's in the bits the GPU tests compare, so those comparisons are not blind (the restatement without
+    it matches the reference in the tests above; Trochilus's mutation tests, tools/mutate_gpu.sh:2-10)."""
+    rng = np.random.default_rng(60 + m)
+    pool = reflib.pool(0)
+
+    def layer(lay, E, k, H, F, rt, gt, dt, T):
+        d, keep = make_desc(lay, H, F, k, 0, rt, gt, dt, None)
+        normed = rng.normal(size=(T, H)).astype(np.float32)
+        x = rng.normal(size=(T, H)).astype(np.float32)
+        return oracle.moe_layer(d, normed, x), reflib.moe_layer(d, normed, x, pool=pool)
+
+    try:
+        oracle.set_mutation(m)
+        if m in (1, 2, 4):
+            gt = gb.Q4_K if m == 4 else gb.Q8_0
+            lay = gb.make_layer(70 + m, 16, 512, 256, gt, gt, gb.F32, mode="random")
+            a, b = layer(lay, 16, 4, 512, 256, gb.F32, gt, gt, 3)
+            key = "logits" if m == 1 else "x"
+            seen = not same_bits(a[key], b[key])
+        elif m == 3:  # a zero router: every probability ties
+            lay = gb.make_layer(73, 16, 512, 256, gb.Q8_0, gb.Q8_0, gb.F32, mode="random")
+            lay["router"] = np.zeros_like(lay["router"])
+            a, b = layer(lay, 16, 4, 512, 256, gb.F32, gb.Q8_0, gb.Q8_0, 2)
+            assert (b["sel_id"] == np.arange(4)).all()  # the reference: ties to the lower id
+            seen = not same_bits(a["sel_id"], b["sel_id"])
+        elif m == 5:
+            x = (rng.normal(size=4096) * 4).astype(np.float32)
+            y = rng.normal(size=4096).astype(np.float32)
+            seen = not same_bits(oracle.swiglu(x, y), reflib.swiglu(x, y))
+        else:
+            x = (rng.normal(size=(4, 2048)) * 3).astype(np.float32)
+            w = (1.0 + 0.1 * rng.normal(size=2048)).astype(np.float32)
+            seen = not same_bits(oracle.rmsnorm(x, w, 1e-5), reflib.rmsnorm(x, w, 1e-5))
+        assert seen, what
+    finally:
+        oracle.set_mutation(0)
+        reflib.pool_destroy(pool)
