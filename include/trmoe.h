@@ -240,6 +240,50 @@ TRMOE_API int tr_gpu_moe_launches(const tr_gpu_moe *m, int64_t n_tok);
 TRMOE_API const char *trmoe_last_error(void);
 
 /* ---------------------------------------------------------------------------------------------
+ * Decode attention (the rank-3 next step beyond the MoE block): Trochilus's GPU attention backend
+ * (src/backend/gpu_attn.h:29-78) on the B200, with the same names, arguments and conventions, so the engine links
+ * it in place of src/backend/gpu_attn.c. A session keeps its keys and values in HBM ([layer][head][pos][head_dim]
+ * f32); a decode token sends q, k and v and reads back its output, for every head the bits tr_attention_group
+ * gives a single query (tr_attention_head, src/kernels/kernels.c:1521-1528). head_dim 128 and one KV head per
+ * query head, as the reference supports. */
+typedef struct tr_gpu tr_gpu;           /* the device */
+typedef struct tr_gpu_attn tr_gpu_attn; /* one session's cache in HBM and its buffers */
+#define TRMOE_GPU_WARM_MAX_NS 200000000 /* the longest tr_gpu_attn_warm */
+#define TRMOE_GPU_VRAM_RESERVE ((uint64_t)512 << 20) /* HBM a cache must leave free */
+
+/* Replaces: tr_gpu_open (gpu_attn.h:37): the first device of compute capability 10.0 (the library's kernels are
+ * built for sm_100a). NULL with a message when there is no driver or no such device. */
+TRMOE_API tr_gpu *tr_gpu_open(char *err, size_t err_len);
+/* Replaces: tr_gpu_close (gpu_attn.h:38). NULL: nothing. Every session of the device is freed first. */
+TRMOE_API void tr_gpu_close(tr_gpu *g);
+/* Replaces: tr_gpu_name (gpu_attn.h:40). */
+TRMOE_API const char *tr_gpu_name(const tr_gpu *g);
+/* Replaces: tr_gpu_attn_create (gpu_attn.h:46-47): a cache of n_ctx positions for every layer and head. NULL with a
+ * message when the shape is not supported (head_dim 128) or HBM would keep less than TRMOE_GPU_VRAM_RESERVE free.
+ * One session, one thread at a time (the calls make the device current on the calling thread). */
+TRMOE_API tr_gpu_attn *tr_gpu_attn_create(tr_gpu *g, int64_t n_layers, int64_t n_head, int64_t head_dim,
+                                          int64_t n_ctx, char *err, size_t err_len);
+/* Replaces: tr_gpu_attn_free (gpu_attn.h:48). NULL: nothing. */
+TRMOE_API void tr_gpu_attn_free(tr_gpu_attn *a);
+/* Replaces: tr_gpu_attn_bytes (gpu_attn.h:50): HBM a session of that shape takes. */
+TRMOE_API uint64_t tr_gpu_attn_bytes(int64_t n_layers, int64_t n_head, int64_t head_dim, int64_t n_ctx);
+/* Replaces: tr_gpu_attn_write (gpu_attn.h:57): positions pos0 .. pos0 + n_tok - 1 of one layer, k and v
+ * [n_tok][n_head * head_dim] host rows. Returns when the GPU holds them. 0, or -1 (a range outside the cache). */
+TRMOE_API int tr_gpu_attn_write(tr_gpu_attn *a, int64_t layer, int64_t pos0, int64_t n_tok, const float *k,
+                                const float *v);
+/* Replaces: tr_gpu_attn_decode (gpu_attn.h:65-66): one decode token of one layer at position pos: stores k and v at
+ * pos, attends to positions 0 .. pos and writes out [n_head * head_dim], head h the bits
+ * tr_attention_head(q + h * head_dim, keys, values, n_head * head_dim, h * head_dim, pos + 1, head_dim, scale, ...)
+ * writes. Host rows (pinned or not). 0, or -1 on a CUDA error, a give-up of a bounded wait, or pos outside the
+ * cache: the caller then stays on the CPU, whose own cache is whole. */
+TRMOE_API int tr_gpu_attn_decode(tr_gpu_attn *a, int64_t layer, int64_t pos, const float *q, const float *k,
+                                 const float *v, float scale, float *out);
+/* Replaces: tr_gpu_attn_warm (gpu_attn.h:74): keeps one warp of the GPU busy for ns nanoseconds (at most
+ * TRMOE_GPU_WARM_MAX_NS) or until the next decode call starts, so that clocks a long idle lowered are up again. 0,
+ * or -1. */
+TRMOE_API int tr_gpu_attn_warm(tr_gpu_attn *a, uint64_t ns);
+
+/* ---------------------------------------------------------------------------------------------
  * 2. The kernel level (Trochilus src/kernels/kernels.h) */
 
 typedef struct tr_pool tr_pool; /* the reference's thread pool: accepted and ignored */

@@ -293,6 +293,28 @@ void orc_rmsnorm(float *x, const float *w, int64_t n, float eps) {
     }
 }
 
+/* ---- one decode token's attention for one head (tr_attention_head, src/kernels/kernels.c:1521-1528, which
+ * tr_attention_group takes for a single query, kernels.c:1564-1567): scores[t] = dot(q, key t) * scale, the dot
+ * under the lane contract (kernels.c:19-23) and the scale one more rounding; tr_softmax over the n_pos scores; then
+ * out = +0 and, position by position in increasing t, out[d] = out[d] + scores[t] * value t[d] (k_axpy_f32,
+ * kernels.c:34-36), every product and sum rounded. keys and values: row t at t * stride + offset. ---- */
+
+void orc_attention_head(const float *q, const float *keys, const float *values, int64_t stride, int64_t offset,
+                        int64_t n_pos, int64_t head_dim, float scale, float *scores, float *out) {
+    for (int64_t t = 0; t < n_pos; t++) {
+        const float *kt = keys + t * stride + offset;
+        float lane[LANES] = {0};
+        for (int64_t d = 0; d < head_dim; d++) lane[d % LANES] += q[d] * kt[d];
+        scores[t] = lane_tree(lane) * scale;
+    }
+    orc_softmax(scores, n_pos);
+    for (int64_t d = 0; d < head_dim; d++) out[d] = 0.0f;
+    for (int64_t t = 0; t < n_pos; t++) {
+        const float *vt = values + t * stride + offset;
+        for (int64_t d = 0; d < head_dim; d++) out[d] = out[d] + scores[t] * vt[d];
+    }
+}
+
 /* ---- routing and dispatch (src/models/olmoe.c:1455-1502, 1850-1861) ---- */
 
 /* probs: T rows of E router logits, softmaxed in place; then k repeated argmaxes (strict >, ties to

@@ -118,6 +118,22 @@ class Oracle(_Common):
         L.orc_row_bytes.restype = C.c_size_t
         L.orc_row_bytes.argtypes = [C.c_int, C.c_int64]
         L.orc_set_mutation.argtypes = [C.c_int]
+        L.orc_attention_head.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_int64, C.c_int64,
+                                         C.c_int64, C.c_float, C.c_void_p, C.c_void_p]
+
+    def attention(self, q, keys, values, scale):
+        """one decode token's attention, head by head: q [n_head][hd], keys / values [n_pos][n_head][hd] (the
+        engine's cache rows); returns out [n_head][hd] (tr_attention_head per head at its offset)"""
+        q = np.ascontiguousarray(q, dtype=np.float32)
+        keys = np.ascontiguousarray(keys, dtype=np.float32)
+        values = np.ascontiguousarray(values, dtype=np.float32)
+        n_pos, n_head, hd = keys.shape
+        out = np.zeros((n_head, hd), dtype=np.float32)
+        scores = np.zeros(max(n_pos, 1), dtype=np.float32)
+        for h in range(n_head):
+            self.lib.orc_attention_head(q[h].ctypes.data, _ptr(keys), _ptr(values), n_head * hd, h * hd, n_pos, hd,
+                                        scale, _ptr(scores), out[h].ctypes.data)
+        return out
 
     def set_mutation(self, m: int):
         """plants mistake m in the restatement (moe_oracle.c lists them; 0: none). Tests only, to show that a

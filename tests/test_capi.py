@@ -91,3 +91,24 @@ def test_prepared_road_host_logic_without_gpu():
     for n_w in (0, 2, 4):  # out of range, shapes that differ, out of range
         assert L.tr_matmul_q4x_prepared_n(None, wp, n_w, off.ctypes.data, 2, xq.ctypes.data, None, yp, None) == 0
     assert np.isnan(y).all() and moe.q4x_fused_calls() == before
+
+
+def test_attention_host_logic_without_gpu():
+    """the GPU attention backend's host side (src/backend/gpu_attn.h's conventions): no device is an error with a
+    message, a shape the kernels do not take is refused before any device call, a missing session is an error,
+    and the bytes a session takes"""
+    import ctypes as C
+    from trochilus_b200 import moe
+    L = moe.lib()
+    err = C.create_string_buffer(256)
+    assert not L.tr_gpu_open(err, 256) and b"device" in err.value  # this container has no GPU
+    assert not L.tr_gpu_attn_create(None, 2, 4, 64, 16, err, 256) and b"head_dim 64 not supported" in err.value
+    assert not L.tr_gpu_attn_create(None, 2, 4, 128, 0, err, 256) and b"bad shape" in err.value
+    assert not L.tr_gpu_attn_create(None, 2, 4, 128, 16, err, 256) and b"no device" in err.value
+    assert L.tr_gpu_attn_decode(None, 0, 0, None, None, None, 1.0, None) == -1 and "bad arguments" in moe.last_error()
+    assert L.tr_gpu_attn_write(None, 0, 0, 1, None, None) == -1
+    cache = 2 * 16 * 16 * 4096 * 128 * 4
+    assert cache < L.tr_gpu_attn_bytes(16, 16, 128, 4096) < cache + (8 << 20)
+    assert L.tr_gpu_attn_bytes(0, 16, 128, 4096) == 0
+    L.tr_gpu_close(None)
+    L.tr_gpu_attn_free(None)

@@ -277,3 +277,38 @@ def test_planted_mistakes_are_seen(oracle, reflib, m, what):
     finally:
         oracle.set_mutation(0)
         reflib.pool_destroy(pool)
+
+
+@pytest.mark.parametrize("tier", ["scalar", "avx2", "avx512"])
+def test_attention_head_pinned(oracle, reflib, tier):
+    """one decode token's attention (tr_attention_head, src/kernels/kernels.c:1521-1528; the GPU attention's
+    contract, src/backend/gpu_attn.h:1-9): the restatement against the reference's every tier, head by head at its
+    offset in the cache rows, for contexts from one position to past 2048, with huge scores, a NaN and an
+    infinity"""
+    try:
+        reflib.set_tier(tier)
+    except RuntimeError:
+        pytest.skip(f"tier {tier} not on this CPU")
+    L = reflib.lib
+    L.tr_attention_head.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_int64, C.c_int64, C.c_int64,
+                                    C.c_float, C.c_void_p, C.c_void_p]
+    rng = np.random.default_rng(11)
+    n_head, hd = 4, 128
+    scale = np.float32(1.0 / np.sqrt(hd))
+    try:
+        for n_pos in (1, 2, 7, 100, 2049):
+            q = rng.normal(size=(n_head, hd)).astype(np.float32)
+            keys = rng.normal(size=(n_pos, n_head, hd)).astype(np.float32)
+            values = rng.normal(size=(n_pos, n_head, hd)).astype(np.float32)
+            q[1] *= 40.0  # scores far apart: probabilities underflow to 0
+            if n_pos > 5:
+                values[3, 2, 9] = np.nan
+                keys[4, 3, 0] = np.inf
+            want = np.zeros((n_head, hd), dtype=np.float32)
+            scores = np.zeros(n_pos, dtype=np.float32)
+            for h in range(n_head):
+                L.tr_attention_head(q[h].ctypes.data, keys.ctypes.data, values.ctypes.data, n_head * hd, h * hd, n_pos,
+                                    hd, scale, scores.ctypes.data, want[h].ctypes.data)
+            assert same_bits(oracle.attention(q, keys, values, scale), want), n_pos
+    finally:
+        reflib.set_tier(None)

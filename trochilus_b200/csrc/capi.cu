@@ -27,6 +27,7 @@
 #include "kernel_api.cuh"
 #include "fused_layer.cuh"
 #include "gguf_file.h"
+#include "attention.cuh"
 #include "prefill.cuh"
 #include "ep.cuh"
 #include "ffn_norm.cuh"
@@ -1542,6 +1543,239 @@ extern "C" int tr_gpu_moe_ep_peer_combine(tr_gpu_moe *m, const float *d_sel_w, c
     trx_k_ep_peer_combine<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(d_sel_w, d_place, m->epp_dev, (int)n_tok,
                                                                           (int)m->cfg.n_used, d_x, d_ffn_out, m->work.err);
     return ck(cudaGetLastError(), "ep combine launch") ? 0 : -1;
+}
+
+// ---------------------------------------------------------------------------------------------
+// decode attention (attention.cuh): Trochilus's GPU attention backend (src/backend/gpu_attn.h) on the B200
+
+struct tr_gpu {
+    int device = 0;
+    char name[256] = {0};
+};
+
+struct tr_gpu_attn {
+    tr_gpu *g = nullptr;
+    int64_t n_layers = 0, n_head = 0, n_ctx = 0, s_stride = 0;
+    float *keys = nullptr, *values = nullptr; // [layer][head][pos][128]
+    float *scores = nullptr;                  // [head][s_stride]
+    float *io = nullptr;                      // a call's rows: q, k, v of a decode, or a write's chunk; then out
+    int32_t *err = nullptr;
+    cudaStream_t st = nullptr, warm_st = nullptr;
+    uint32_t *h_stop = nullptr, *d_stop = nullptr; // the warm-up kernel's stop word (mapped pinned)
+};
+
+namespace {
+
+constexpr int64_t kAttnWriteChunk = 256; // tokens a write moves per copy
+constexpr uint64_t kAttnReserve = (uint64_t)512 << 20;
+constexpr uint64_t kAttnWarmMaxNs = 200000000;
+
+int64_t attn_s_stride(int64_t n_ctx) { return (n_ctx + TRX_ATTN_CHUNK - 1) / TRX_ATTN_CHUNK * TRX_ATTN_CHUNK; }
+
+// a failed call's stream and error word: whatever was in flight finishes, the word goes back to 0
+bool attn_fail(tr_gpu_attn *a, const char *what) {
+    cudaStreamSynchronize(a->st);
+    cudaMemsetAsync(a->err, 0, 4, a->st);
+    cudaStreamSynchronize(a->st);
+    set_err("%s", what);
+    return false;
+}
+
+} // namespace
+
+extern "C" tr_gpu *tr_gpu_open(char *err, size_t err_len) {
+    g_err.clear();
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) {
+        cudaGetLastError();
+        set_err("no CUDA device (or no driver)");
+        put_err(err, err_len);
+        return nullptr;
+    }
+    for (int d = 0; d < n; d++) {
+        cudaDeviceProp p;
+        if (cudaGetDeviceProperties(&p, d) != cudaSuccess || p.major != 10 || p.minor != 0) continue;
+        tr_gpu *g = new tr_gpu;
+        g->device = d;
+        snprintf(g->name, sizeof g->name, "%s", p.name);
+        return g;
+    }
+    set_err("no device of compute capability 10.0 (the library's kernels are built for sm_100a)");
+    put_err(err, err_len);
+    return nullptr;
+}
+
+extern "C" void tr_gpu_close(tr_gpu *g) { delete g; }
+
+extern "C" const char *tr_gpu_name(const tr_gpu *g) { return g ? g->name : ""; }
+
+extern "C" uint64_t tr_gpu_attn_bytes(int64_t n_layers, int64_t n_head, int64_t head_dim, int64_t n_ctx) {
+    if (n_layers < 1 || n_head < 1 || head_dim < 1 || n_ctx < 1) return 0;
+    const uint64_t cache = 2ull * (uint64_t)n_layers * (uint64_t)n_head * (uint64_t)n_ctx * (uint64_t)head_dim * 4;
+    const uint64_t scores = (uint64_t)n_head * (uint64_t)attn_s_stride(n_ctx) * 4;
+    const uint64_t io = (uint64_t)std::max<int64_t>(4, 2 * kAttnWriteChunk) * (uint64_t)(n_head * head_dim) * 4;
+    return cache + scores + io + 256;
+}
+
+extern "C" void tr_gpu_attn_free(tr_gpu_attn *a) {
+    if (a == nullptr) return;
+    cudaSetDevice(a->g->device);
+    if (a->h_stop) *(volatile uint32_t *)a->h_stop = 1u; // a warm-up still running stops
+    if (a->warm_st) cudaStreamSynchronize(a->warm_st);
+    if (a->st) cudaStreamSynchronize(a->st);
+    cudaFree(a->keys);
+    cudaFree(a->values);
+    cudaFree(a->scores);
+    cudaFree(a->io);
+    cudaFree(a->err);
+    if (a->h_stop) cudaFreeHost(a->h_stop);
+    if (a->st) cudaStreamDestroy(a->st);
+    if (a->warm_st) cudaStreamDestroy(a->warm_st);
+    delete a;
+}
+
+extern "C" tr_gpu_attn *tr_gpu_attn_create(tr_gpu *g, int64_t n_layers, int64_t n_head, int64_t head_dim,
+                                           int64_t n_ctx, char *err, size_t err_len) {
+    g_err.clear();
+    if (head_dim != TRX_ATTN_HD) {
+        set_err("head_dim %lld not supported (128)", (long long)head_dim);
+        put_err(err, err_len);
+        return nullptr;
+    }
+    if (n_layers < 1 || n_head < 1 || n_head > 65535 || n_ctx < 1 || n_ctx > (1 << 24)) {
+        set_err("bad shape (layers %lld, heads %lld, context %lld)", (long long)n_layers, (long long)n_head,
+                (long long)n_ctx);
+        put_err(err, err_len);
+        return nullptr;
+    }
+    if (g == nullptr) {
+        set_err("no device (tr_gpu_open)");
+        put_err(err, err_len);
+        return nullptr;
+    }
+    if (!ck(cudaSetDevice(g->device), "cudaSetDevice")) {
+        put_err(err, err_len);
+        return nullptr;
+    }
+    size_t free_b = 0, total_b = 0;
+    const uint64_t need = tr_gpu_attn_bytes(n_layers, n_head, head_dim, n_ctx);
+    if (!ck(cudaMemGetInfo(&free_b, &total_b), "cudaMemGetInfo")) {
+        put_err(err, err_len);
+        return nullptr;
+    }
+    if ((uint64_t)free_b < need + kAttnReserve) {
+        set_err("the cache needs %llu bytes and %llu must stay free; %llu are", (unsigned long long)need,
+                (unsigned long long)kAttnReserve, (unsigned long long)free_b);
+        put_err(err, err_len);
+        return nullptr;
+    }
+    tr_gpu_attn *a = new tr_gpu_attn;
+    a->g = g;
+    a->n_layers = n_layers;
+    a->n_head = n_head;
+    a->n_ctx = n_ctx;
+    a->s_stride = attn_s_stride(n_ctx);
+    const size_t cache = (size_t)n_layers * n_head * n_ctx * TRX_ATTN_HD * 4;
+    const size_t io = (size_t)std::max<int64_t>(4, 2 * kAttnWriteChunk) * n_head * TRX_ATTN_HD * 4;
+    bool ok = ck(cudaMalloc(&a->keys, cache), "cudaMalloc(keys)") &&
+              ck(cudaMalloc(&a->values, cache), "cudaMalloc(values)") &&
+              ck(cudaMalloc(&a->scores, (size_t)n_head * a->s_stride * 4), "cudaMalloc(scores)") &&
+              ck(cudaMalloc(&a->io, io), "cudaMalloc(io)") && ck(cudaMalloc(&a->err, 4), "cudaMalloc(err)") &&
+              ck(cudaMemset(a->err, 0, 4), "cudaMemset(err)") &&
+              ck(cudaMemset(a->scores, 0, (size_t)n_head * a->s_stride * 4), "cudaMemset(scores)") &&
+              ck(cudaStreamCreateWithFlags(&a->st, cudaStreamNonBlocking), "cudaStreamCreate") &&
+              ck(cudaStreamCreateWithFlags(&a->warm_st, cudaStreamNonBlocking), "cudaStreamCreate") &&
+              ck(cudaHostAlloc((void **)&a->h_stop, 4, cudaHostAllocMapped), "cudaHostAlloc(stop)") &&
+              ck(cudaHostGetDevicePointer((void **)&a->d_stop, a->h_stop, 0), "cudaHostGetDevicePointer(stop)") &&
+              ck(cudaFuncSetAttribute(trx_attn_values, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      TRX_ATTN_STAGES * TRX_ATTN_STAGE_BYTES),
+                 "values kernel shared memory");
+    if (!ok) {
+        put_err(err, err_len);
+        tr_gpu_attn_free(a);
+        return nullptr;
+    }
+    *a->h_stop = 1u;
+    return a;
+}
+
+extern "C" int tr_gpu_attn_write(tr_gpu_attn *a, int64_t layer, int64_t pos0, int64_t n_tok, const float *k,
+                                 const float *v) {
+    g_err.clear();
+    if (a == nullptr || layer < 0 || layer >= a->n_layers || pos0 < 0 || n_tok < 0 || pos0 + n_tok > a->n_ctx ||
+        (n_tok > 0 && (k == nullptr || v == nullptr))) {
+        set_err("bad arguments to tr_gpu_attn_write (a range outside the cache)");
+        return -1;
+    }
+    if (!ck(cudaSetDevice(a->g->device), "cudaSetDevice")) return -1;
+    const int64_t row = a->n_head * TRX_ATTN_HD, lay = a->n_head * a->n_ctx * TRX_ATTN_HD;
+    bool ok = true;
+    for (int64_t i = 0; ok && i < n_tok; i += kAttnWriteChunk) {
+        const int64_t n = std::min(kAttnWriteChunk, n_tok - i);
+        float *sk = a->io, *sv = a->io + kAttnWriteChunk * row;
+        const unsigned blocks = (unsigned)((n * a->n_head + 7) / 8);
+        ok = ck(cudaMemcpyAsync(sk, k + i * row, (size_t)(n * row) * 4, cudaMemcpyHostToDevice, a->st), "copy k") &&
+             ck(cudaMemcpyAsync(sv, v + i * row, (size_t)(n * row) * 4, cudaMemcpyHostToDevice, a->st), "copy v");
+        if (ok) {
+            trx_attn_store<<<blocks, 256, 0, a->st>>>(sk, (int)n, (int)a->n_head, pos0 + i, a->n_ctx, a->keys + layer * lay);
+            trx_attn_store<<<blocks, 256, 0, a->st>>>(sv, (int)n, (int)a->n_head, pos0 + i, a->n_ctx,
+                                                      a->values + layer * lay);
+            ok = ck(cudaGetLastError(), "store kernel") && stream_wait(a->st); // (the staging is reused)
+        }
+    }
+    return ok ? 0 : -1;
+}
+
+extern "C" int tr_gpu_attn_decode(tr_gpu_attn *a, int64_t layer, int64_t pos, const float *q, const float *k,
+                                  const float *v, float scale, float *out) {
+    g_err.clear();
+    if (a == nullptr || layer < 0 || layer >= a->n_layers || pos < 0 || pos >= a->n_ctx || q == nullptr ||
+        k == nullptr || v == nullptr || out == nullptr) {
+        set_err("bad arguments to tr_gpu_attn_decode (pos outside the cache)");
+        return -1;
+    }
+    *(volatile uint32_t *)a->h_stop = 1u; // a warm-up still running ends
+    if (!ck(cudaSetDevice(a->g->device), "cudaSetDevice")) return -1;
+    const int64_t row = a->n_head * TRX_ATTN_HD, lay = a->n_head * a->n_ctx * TRX_ATTN_HD, n_pos = pos + 1;
+    float *dq = a->io, *dk = a->io + row, *dv = a->io + 2 * row, *dout = a->io + 3 * row;
+    float *K = a->keys + layer * lay, *V = a->values + layer * lay;
+    bool ok = ck(cudaMemcpyAsync(dq, q, (size_t)row * 4, cudaMemcpyHostToDevice, a->st), "copy q") &&
+              ck(cudaMemcpyAsync(dk, k, (size_t)row * 4, cudaMemcpyHostToDevice, a->st), "copy k") &&
+              ck(cudaMemcpyAsync(dv, v, (size_t)row * 4, cudaMemcpyHostToDevice, a->st), "copy v");
+    if (!ok) return -1;
+    const unsigned sb = (unsigned)((a->n_head + 7) / 8);
+    trx_attn_store<<<sb, 256, 0, a->st>>>(dk, 1, (int)a->n_head, pos, a->n_ctx, K);
+    trx_attn_store<<<sb, 256, 0, a->st>>>(dv, 1, (int)a->n_head, pos, a->n_ctx, V);
+    trx_attn_scores<<<dim3((unsigned)((n_pos + 15) / 16), (unsigned)a->n_head), 256, 0, a->st>>>(
+        dq, K, (int)n_pos, a->n_ctx, scale, a->scores, a->s_stride);
+    trx_softmax_rows_k<<<(unsigned)a->n_head, 256, 0, a->st>>>(a->scores, n_pos, a->s_stride);
+    trx_attn_values<<<(unsigned)a->n_head, 160, TRX_ATTN_STAGES * TRX_ATTN_STAGE_BYTES, a->st>>>(
+        a->scores, a->s_stride, V, (int)n_pos, a->n_ctx, dout, a->err);
+    int32_t e = 0;
+    ok = ck(cudaGetLastError(), "attention kernels") &&
+         ck(cudaMemcpyAsync(out, dout, (size_t)row * 4, cudaMemcpyDeviceToHost, a->st), "copy out") &&
+         ck(cudaMemcpyAsync(&e, a->err, 4, cudaMemcpyDeviceToHost, a->st), "copy error word") && stream_wait(a->st);
+    if (!ok) return -1;
+    if (e != 0) {
+        attn_fail(a, "the attention kernel gave up on a bounded wait");
+        return -1;
+    }
+    return 0;
+}
+
+extern "C" int tr_gpu_attn_warm(tr_gpu_attn *a, uint64_t ns) {
+    g_err.clear();
+    if (a == nullptr) {
+        set_err("bad arguments to tr_gpu_attn_warm");
+        return -1;
+    }
+    if (!ck(cudaSetDevice(a->g->device), "cudaSetDevice")) return -1;
+    // the one before has ended (its stop word was set, or its time ran out), then the stop word is cleared
+    *(volatile uint32_t *)a->h_stop = 1u;
+    if (!ck(cudaStreamSynchronize(a->warm_st), "warm stream")) return -1;
+    *(volatile uint32_t *)a->h_stop = 0u;
+    trx_attn_warm<<<1, 1, 0, a->warm_st>>>(a->d_stop, std::min<uint64_t>(ns, kAttnWarmMaxNs));
+    return ck(cudaGetLastError(), "warm kernel") ? 0 : -1;
 }
 
 // ---------------------------------------------------------------------------------------------

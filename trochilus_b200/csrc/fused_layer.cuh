@@ -911,9 +911,13 @@ __global__ void __launch_bounds__(TRX_FU_THREADS, 1)
     if (__syncthreads_or(failed)) {
         if (warp == TRX_FU_CWARPS && lane == 0) {
             atomicCAS(w.err, 0, 3 | (w.ep ? 0x100 : 0)); // the first error stays
-            // every copy still in flight lands before the CTA's shared memory goes away
-            for (int q = 0; q < issued_g; q++) trx_mbar_wait(&full_g[q % SG], (q / SG) & 1, TRX_WAIT_NS);
-            for (int q = 0; q < issued_d; q++) trx_mbar_wait(&full_d[q % SD], (q / SD) & 1, TRX_WAIT_NS);
+            // every copy still in flight lands before the CTA's shared memory goes away: only a stage's latest copy
+            // can be (a stage is refilled after its consumers saw the one before land), and only its phase parity
+            // is unambiguous
+            for (int q = max(0, issued_g - SG); q < issued_g; q++)
+                trx_mbar_wait(&full_g[q % SG], (q / SG) & 1, TRX_WAIT_NS);
+            for (int q = max(0, issued_d - SD); q < issued_d; q++)
+                trx_mbar_wait(&full_d[q % SD], (q / SD) & 1, TRX_WAIT_NS);
             if (w.host_done) trx_post_done(w.host_done, epoch | 0x80000000u);
         }
         __syncthreads();

@@ -136,9 +136,9 @@ __global__ void __launch_bounds__(256) trx_kapi_gather_k(const float *__restrict
     for (int i = threadIdx.x; i < cols / 4; i += blockDim.x) d[i] = s[i];
 }
 
-// tr_softmax over n values, one block: the max as the reference's serial scan from x[0], the exp of each
-// difference, the 16-lane sum (lane l adds elements l, l + 16, ... in order), the divisions
-__global__ void __launch_bounds__(256) trx_kapi_softmax_k(float *__restrict__ x, int64_t n) {
+// tr_softmax over n values by one block of 256 threads: the max as the reference's serial scan from x[0], the exp
+// of each difference, the 16-lane sum (lane l adds elements l, l + 16, ... in order), the divisions
+__device__ __forceinline__ void trx_softmax_block(float *__restrict__ x, int64_t n) {
     __shared__ float red[8];
     __shared__ float s_m, s_sum;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -167,6 +167,13 @@ __global__ void __launch_bounds__(256) trx_kapi_softmax_k(float *__restrict__ x,
     __syncthreads();
     const float sum = s_sum;
     for (int64_t i = tid; i < n; i += blockDim.x) x[i] = __fdiv_rn(x[i], sum);
+}
+
+__global__ void __launch_bounds__(256) trx_kapi_softmax_k(float *__restrict__ x, int64_t n) { trx_softmax_block(x, n); }
+
+// tr_softmax over each of gridDim.x rows of n values, stride floats apart, a block a row
+__global__ void __launch_bounds__(256) trx_softmax_rows_k(float *__restrict__ x, int64_t n, int64_t stride) {
+    trx_softmax_block(x + (int64_t)blockIdx.x * stride, n);
 }
 
 inline bool trx_kapi_softmax(float *d, int64_t n, cudaStream_t st) {

@@ -32,7 +32,8 @@ EXPORTS = ["tr_gpu_moe_create", "tr_gpu_moe_free", "tr_gpu_moe_bytes", "tr_gpu_m
            "tr_gpu_moe_ep_peer_open", "tr_gpu_moe_ep_dispatch", "tr_gpu_moe_ep_experts", "tr_gpu_moe_ep_peer_combine",
            "tr_matmul_s", "tr_q4x_bytes", "tr_q4x_road", "tr_q4x_prepare", "tr_matmul_q4x_prepared",
            "tr_matmul_q4x_prepared_n", "tr_q4x_fused_calls", "tr_swiglu_prepare", "tr_gpu_moe_config_from_gguf",
-           "tr_gpu_moe_load_gguf"]
+           "tr_gpu_moe_load_gguf", "tr_gpu_open", "tr_gpu_close", "tr_gpu_name", "tr_gpu_attn_create",
+           "tr_gpu_attn_free", "tr_gpu_attn_bytes", "tr_gpu_attn_write", "tr_gpu_attn_decode", "tr_gpu_attn_warm"]
 
 
 class Config(C.Structure):
@@ -119,6 +120,20 @@ def lib():
     L.tr_gpu_moe_config_from_gguf.argtypes = [C.c_char_p, C.POINTER(Config), C.POINTER(C.c_float), C.c_char_p,
                                               C.c_size_t]
     L.tr_gpu_moe_load_gguf.argtypes = [C.c_void_p, C.c_char_p, C.c_char_p, C.c_size_t]
+    L.tr_gpu_open.restype = C.c_void_p
+    L.tr_gpu_open.argtypes = [C.c_char_p, C.c_size_t]
+    L.tr_gpu_close.argtypes = [C.c_void_p]
+    L.tr_gpu_name.restype = C.c_char_p
+    L.tr_gpu_name.argtypes = [C.c_void_p]
+    L.tr_gpu_attn_create.restype = C.c_void_p
+    L.tr_gpu_attn_create.argtypes = [C.c_void_p, C.c_int64, C.c_int64, C.c_int64, C.c_int64, C.c_char_p, C.c_size_t]
+    L.tr_gpu_attn_free.argtypes = [C.c_void_p]
+    L.tr_gpu_attn_bytes.restype = C.c_uint64
+    L.tr_gpu_attn_bytes.argtypes = [C.c_int64] * 4
+    L.tr_gpu_attn_write.argtypes = [C.c_void_p, C.c_int64, C.c_int64, C.c_int64, C.c_void_p, C.c_void_p]
+    L.tr_gpu_attn_decode.argtypes = [C.c_void_p, C.c_int64, C.c_int64, C.c_void_p, C.c_void_p, C.c_void_p,
+                                     C.c_float, C.c_void_p]
+    L.tr_gpu_attn_warm.argtypes = [C.c_void_p, C.c_uint64]
     _lib = L
     return L
 
@@ -344,6 +359,60 @@ class GpuMoe:
         if self.h:
             lib().tr_gpu_moe_free(self.h)
             self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class GpuAttn:
+    """A tr_gpu_attn session (Trochilus's GPU attention backend, src/backend/gpu_attn.h) on host arrays: the device
+    (tr_gpu_open) and one session's cache of n_ctx positions for n_layers layers of n_head heads of 128."""
+
+    def __init__(self, n_layers: int, n_head: int, n_ctx: int, head_dim: int = 128):
+        L = lib()
+        err = C.create_string_buffer(512)
+        self.g = L.tr_gpu_open(err, 512)
+        if not self.g:
+            raise RuntimeError(f"tr_gpu_open: {err.value.decode()}")
+        self.a = L.tr_gpu_attn_create(self.g, n_layers, n_head, head_dim, n_ctx, err, 512)
+        if not self.a:
+            L.tr_gpu_close(self.g)
+            self.g = None
+            raise RuntimeError(f"tr_gpu_attn_create: {err.value.decode()}")
+        self.n_head, self.hd = n_head, head_dim
+
+    def name(self) -> str:
+        return lib().tr_gpu_name(self.g).decode()
+
+    def write(self, layer: int, pos0: int, k: np.ndarray, v: np.ndarray):
+        """tr_gpu_attn_write: k, v [n_tok][n_head * head_dim]"""
+        k = np.ascontiguousarray(k, dtype=np.float32).reshape(-1, self.n_head * self.hd)
+        v = np.ascontiguousarray(v, dtype=np.float32).reshape(-1, self.n_head * self.hd)
+        if lib().tr_gpu_attn_write(self.a, layer, pos0, k.shape[0], _p(k), _p(v)) != 0:
+            raise RuntimeError(f"tr_gpu_attn_write: {last_error()}")
+
+    def decode(self, layer: int, pos: int, q, k, v, scale: float) -> np.ndarray:
+        """tr_gpu_attn_decode: q, k, v [n_head * head_dim]; returns out [n_head][head_dim]"""
+        q, k, v = (np.ascontiguousarray(a, dtype=np.float32).ravel() for a in (q, k, v))
+        out = np.full((self.n_head, self.hd), np.nan, dtype=np.float32)
+        if lib().tr_gpu_attn_decode(self.a, layer, pos, _p(q), _p(k), _p(v), scale, _p(out)) != 0:
+            raise RuntimeError(f"tr_gpu_attn_decode: {last_error()}")
+        return out
+
+    def warm(self, ns: int):
+        if lib().tr_gpu_attn_warm(self.a, ns) != 0:
+            raise RuntimeError(f"tr_gpu_attn_warm: {last_error()}")
+
+    def close(self):
+        if getattr(self, "a", None):
+            lib().tr_gpu_attn_free(self.a)
+            self.a = None
+        if getattr(self, "g", None):
+            lib().tr_gpu_close(self.g)
+            self.g = None
 
     def __del__(self):
         try:
