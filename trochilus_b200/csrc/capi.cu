@@ -972,7 +972,6 @@ static int host_layer(tr_gpu_moe *m, int64_t layer, const float *normed, int64_t
         pa.type == cudaMemoryTypeHost && pa.devicePointer != nullptr) {
         uint32_t epoch = 0;
         float *xd = (float *)pa.devicePointer;
-        // the ffn_norm reads x from a device copy: one copy-engine transfer beats the kernel's reads over the link
         // with the ffn_norm, the norm reads a device copy of x (one copy-engine transfer beats reads over the link)
         const bool in = norm ? ck(cudaMemcpyAsync(m->d_x, x_inout, xb, cudaMemcpyHostToDevice, st), "copy x")
                              : ck(cudaMemcpyAsync(m->d_normed, normed, xb, cudaMemcpyHostToDevice, st), "copy normed");
