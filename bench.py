@@ -18,6 +18,9 @@ Arms:
              `prefill` = configs[2]'s layer (2048 tokens, Q8_0) on the tensor-core road, same keys, its roofline
              the useful TFLOP/s over the dense TF32 peak (--prefill-tokens 0 skips it; --only-prefill prints it alone).
   reference  Trochilus's own CPU code on this box's host cores, same config (rank 0 only under torchrun).
+--only-attention P prints only the decode attention backend's line (tr_gpu_attn_decode, Trochilus's gpu_attn.h on the
+B200): one layer of OLMoE's 16 heads of 128 at a context of P positions, wall time per call through the host API,
+its K and V bytes against the HBM peak, and Trochilus's own tr_attention_head on one host core beside it.
 N > 1: one process per GPU (torchrun), expert parallel (trochilus_b200/ep.py): rank r holds experts
 [64 r / N, 64 (r + 1) / N) and owns T tokens a step (weak scaling); each step routes them, sends their rows to the
 experts' ranks and back with NCCL all-to-alls (padded blocks: no host sync), and combines. time = max over ranks,
@@ -62,6 +65,8 @@ def args_parse():
                    help="tokens of the prefill measurement added to the line (configs[2]'s layer); 0: skip it")
     p.add_argument("--prefill-steps", type=int, default=20)
     p.add_argument("--only-prefill", action="store_true", help="run and print only the prefill measurement")
+    p.add_argument("--only-attention", type=int, default=0, metavar="P",
+                   help="run and print only the decode attention measurement at a context of P positions")
     return p.parse_args()
 
 
@@ -567,6 +572,66 @@ def run_ours(args, rank, world, dist):
     print(json.dumps(line), flush=True)
 
 
+def run_attention(args):
+    """decode attention through the host API: one layer, 16 heads of 128, P positions in the cache, a decode token
+    at position P (its k and v stored, positions 0..P attended); the reference's tr_attention_head on one host core
+    for the same shape"""
+    from trochilus_b200.moe import GpuAttn
+    n_head, hd, P = 16, 128, args.only_attention
+    rng = np.random.default_rng(3)
+    kv = rng.normal(size=(P + 1, n_head * hd)).astype(np.float32)
+    q = rng.normal(size=n_head * hd).astype(np.float32)
+    scale = float(np.float32(1.0 / np.sqrt(hd)))
+    a = GpuAttn(1, n_head, P + 1)
+    a.write(0, 0, kv[:P], kv[:P])
+    for _ in range(max(args.warmup, 3)):
+        a.decode(0, P, q, kv[P], kv[P], scale)
+    steps = max(min(args.steps, 2000), 10)
+    with Clocks(0) as clk:
+        clk.wait_first()
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            out = a.decode(0, P, q, kv[P], kv[P], scale)
+        sec = (time.perf_counter() - t0) / steps
+    a.close()
+    cache_bytes = 2 * n_head * (P + 1) * hd * 4
+    peak, peak_kind = peaks()
+    achieved = cache_bytes / sec / 1e9
+    cpu = None
+    try:
+        import ctypes as C
+        from oracle.oracle import RefLib
+        L = RefLib().lib
+        L.tr_attention_head.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_int64, C.c_int64,
+                                        C.c_int64, C.c_float, C.c_void_p, C.c_void_p]
+        keys = np.ascontiguousarray(kv)
+        scores = np.zeros(P + 1, dtype=np.float32)
+        ref = np.zeros((n_head, hd), dtype=np.float32)
+        reps, c0 = 0, time.perf_counter()
+        while time.perf_counter() - c0 < min(args.cpu_seconds, 5.0) or reps == 0:
+            for h in range(n_head):
+                L.tr_attention_head(q[h * hd:].ctypes.data, keys.ctypes.data, keys.ctypes.data, n_head * hd, h * hd,
+                                    P + 1, hd, scale, scores.ctypes.data, ref[h].ctypes.data)
+            reps += 1
+        cpu_us = (time.perf_counter() - c0) / reps * 1e6
+        same = bool(np.array_equal(ref.view(np.uint32), out.view(np.uint32)))
+        cpu = {"value": cpu_us, "unit": "us", "cores": 1, "kind": "reference",
+               "sample": f"{reps} calls of tr_attention_head x {n_head} heads, best tier, one thread",
+               "same_bits_as_gpu": same}
+    except Exception as exc:  # the reference library is a checker: its absence leaves the baseline out
+        cpu = {"value": None, "sample": f"unavailable: {exc}"}
+    line = {"metric": f"decode attention, us per layer call (16 heads x 128, {P} cached positions)",
+            "value": sec * 1e6, "unit": "us", "n_gpus": 1, "steps": steps, "warmup": args.warmup,
+            "higher_is_better": False, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "tr_gpu_attn_decode through the host API (q, k, v in, out back)",
+                       "context": P, "n_head": n_head, "head_dim": hd},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "peak_kind": peak_kind, "algorithmic_bytes": cache_bytes,
+                         "note": "wall time per host call (copies, five launches, synchronisation) over K and V bytes"},
+            "cpu_baseline": cpu, "clocks": clk.summary(), "vs_baseline": None}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = args_parse()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -580,7 +645,11 @@ def main():
         torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
         dist_.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
         dist = dist_
-    if args.only_prefill:
+    if args.only_attention > 0:
+        import torch
+        torch.cuda.set_device(0)
+        run_attention(args)
+    elif args.only_prefill:
         import torch
         torch.cuda.set_device(0)
         print(json.dumps(run_prefill(args, 0, 0 if args.no_cpu_baseline else args.cpu_seconds)), flush=True)
