@@ -34,11 +34,19 @@ __global__ void __launch_bounds__(256) trx_attn_store(const float *__restrict__ 
     reinterpret_cast<float4 *>(cache + ((int64_t)h * n_ctx + pos0 + i) * TRX_ATTN_HD)[lane] = v;
 }
 
-// scores[h * s_stride + t] for t < n_pos: 16 positions a block of 256 threads, blockIdx.y the head
+// scores[h * s_stride + t] for t < n_pos: 16 positions a block of 256 threads, blockIdx.y the head. The block also
+// asks L2 for the same positions' value rows (a bulk prefetch, no data moved to the SM), so that the value kernel's
+// few CTAs stream them from L2 rather than HBM.
 __global__ void __launch_bounds__(256) trx_attn_scores(const float *__restrict__ q, const float *__restrict__ keys,
-                                                       int n_pos, int64_t n_ctx, float scale, float *__restrict__ scores,
-                                                       int64_t s_stride) {
+                                                       const float *__restrict__ values, int n_pos, int64_t n_ctx,
+                                                       float scale, float *__restrict__ scores, int64_t s_stride) {
     const int h = blockIdx.y, l = threadIdx.x & 15;
+    if (threadIdx.x == 0) {
+        const int first = blockIdx.x * 16, rows = min(16, n_pos - first);
+        const float *v = values + ((int64_t)h * n_ctx + first) * TRX_ATTN_HD;
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(v), "r"((uint32_t)rows * TRX_ATTN_HD * 4)
+                     : "memory");
+    }
     const int t0 = blockIdx.x * 16 + (threadIdx.x >> 4);
     const int t = t0 < n_pos ? t0 : n_pos - 1; // every lane takes part in the tree
     const float *qh = q + (int64_t)h * TRX_ATTN_HD;

@@ -1746,7 +1746,7 @@ extern "C" int tr_gpu_attn_decode(tr_gpu_attn *a, int64_t layer, int64_t pos, co
     trx_attn_store<<<sb, 256, 0, a->st>>>(dk, 1, (int)a->n_head, pos, a->n_ctx, K);
     trx_attn_store<<<sb, 256, 0, a->st>>>(dv, 1, (int)a->n_head, pos, a->n_ctx, V);
     trx_attn_scores<<<dim3((unsigned)((n_pos + 15) / 16), (unsigned)a->n_head), 256, 0, a->st>>>(
-        dq, K, (int)n_pos, a->n_ctx, scale, a->scores, a->s_stride);
+        dq, K, V, (int)n_pos, a->n_ctx, scale, a->scores, a->s_stride);
     trx_softmax_rows_k<<<(unsigned)a->n_head, 256, 0, a->st>>>(a->scores, n_pos, a->s_stride);
     trx_attn_values<<<(unsigned)a->n_head, 160, TRX_ATTN_STAGES * TRX_ATTN_STAGE_BYTES, a->st>>>(
         a->scores, a->s_stride, V, (int)n_pos, a->n_ctx, dout, a->err);
