@@ -122,7 +122,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-@pytest.mark.parametrize("world,padded", [(2, False), (2, True), (4, False), (4, True)])
+@pytest.mark.parametrize("world,padded", [(2, False), (2, True), (4, False), (4, True), (8, True)])
 def test_ep_exchange_on_gloo_ranks_matches_one_process(world, padded):
     import torch.multiprocessing as mp
     mp.spawn(_worker, args=(world, _free_port(), gb.F32, gb.Q8_0, gb.Q6_K, padded), nprocs=world, join=True)
