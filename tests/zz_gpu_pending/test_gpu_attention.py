@@ -12,8 +12,8 @@ from tests.golden.cases import same_bits
 
 pytestmark = [pytest.mark.gpu,
               pytest.mark.skipif(os.environ.get("TRX_ATTN_GPU_TEST") != "1",
-                                 reason="written after the GPU time of its round ran out and not yet run on a B200; "
-                                        "set TRX_ATTN_GPU_TEST=1 to run it")]
+                                 reason="written without GPU time and not yet run on a B200; set TRX_ATTN_GPU_TEST=1 "
+                                        "to run it")]
 
 
 def test_decode_attention_matches_oracle(cuda, oracle):
