@@ -1106,1110 +1106,10 @@ extern "C" int tr_gpu_moe_ffn_dev(tr_gpu_moe *m, int64_t layer, int64_t n_tok, f
                         d_normed_out);
 }
 
-// ---------------------------------------------------------------------------------------------
-// the model loader: an OLMoE GGUF file straight into the context's resident layout (no expert store)
+#include "capi_loader.inc"
 
-namespace {
+#include "capi_ep.inc"
 
-// the MoE block's tensors of one layer (src/models/olmoe.c:605-641, 901-906)
-struct GgufLayer {
-    const TrxGgufTensor *router, *norm, *gate, *up, *down;
-};
+#include "capi_attention.inc"
 
-// a tensor of the given ggml dimensions (olmoe.c's check_shape / find_experts): NULL with the reason in err
-const TrxGgufTensor *gguf_need(const TrxGguf &g, const std::string &name, uint32_t n_dims, uint64_t ne0, uint64_t ne1,
-                               uint64_t ne2, std::string &err) {
-    const TrxGgufTensor *t = g.tensor(name);
-    if (t == nullptr) {
-        err = "missing tensor '" + name + "'";
-        return nullptr;
-    }
-    const uint64_t want[3] = {ne0, ne1, ne2};
-    bool ok = t->n_dims == n_dims;
-    for (uint32_t d = 0; ok && d < n_dims; d++) ok = t->ne[d] == want[d];
-    if (!ok) {
-        err = "tensor '" + name + "' has shape [";
-        for (uint32_t d = 0; d < t->n_dims; d++) err += (d ? ", " : "") + std::to_string(t->ne[d]);
-        err += "], expected [";
-        for (uint32_t d = 0; d < n_dims; d++) err += (d ? ", " : "") + std::to_string(want[d]);
-        err += "]";
-        return nullptr;
-    }
-    return t;
-}
-
-// every value of an F32 tensor a bfloat16 (its low 16 bits zero), as Trochilus's tr_f32_to_bf16_exact asks
-// (src/kernels/kernels.h:82-85) before it keeps an F32 router as BF16
-bool gguf_bf16_exact(const TrxGgufTensor &t, const uint8_t *p) {
-    for (uint64_t i = 0; i < t.n_bytes / 4; i++) {
-        uint32_t v;
-        memcpy(&v, p + 4 * i, 4);
-        if (v & 0xffffu) return false;
-    }
-    return true;
-}
-
-// The file's MoE configuration (olmoe.c:541-575's metadata, the router, ffn_norm and expert tensors of every layer),
-// with *eps its RMSNorm epsilon and layers[L] each layer's tensors. The context takes one gate/up type and one down
-// type: a file whose layers differ is refused. The router type is BF16 when every layer's router is BF16 or an F32
-// whose values are all bfloat16 (the reference keeps those as BF16, olmoe.c:391), else F32.
-bool gguf_config(const TrxGguf &g, tr_gpu_moe_config &cfg, float &eps, std::vector<GgufLayer> &layers, std::string &err) {
-    std::string arch;
-    if (g.get_str("general.architecture", arch) && arch != "olmoe") {
-        err = "general.architecture is '" + arch + "', not 'olmoe'";
-        return false;
-    }
-    uint32_t nl = 0, H = 0, F = 0, E = 0, k = 0;
-    const char *need[5] = {"olmoe.block_count", "olmoe.embedding_length", "olmoe.feed_forward_length",
-                           "olmoe.expert_count", "olmoe.expert_used_count"};
-    uint32_t *dst[5] = {&nl, &H, &F, &E, &k};
-    for (int i = 0; i < 5; i++)
-        if (!g.get_u32(need[i], *dst[i])) {
-            err = std::string("missing metadata key '") + need[i] + "'";
-            return false;
-        }
-    if (!g.get_f32("olmoe.attention.layer_norm_rms_epsilon", eps)) {
-        err = "missing metadata key 'olmoe.attention.layer_norm_rms_epsilon'";
-        return false;
-    }
-    bool norm_topk = false;
-    g.get_bool("olmoe.expert_weights_norm", norm_topk);
-    if (nl == 0 || H == 0 || F == 0 || E == 0 || k == 0) {
-        err = "invalid (zero) hyperparameter in metadata";
-        return false;
-    }
-    if (k > E) {
-        err = "olmoe.expert_used_count exceeds olmoe.expert_count";
-        return false;
-    }
-    layers.assign(nl, GgufLayer{});
-    bool all_bf16 = true;
-    for (uint32_t L = 0; L < nl; L++) {
-        const std::string b = "blk." + std::to_string(L) + ".";
-        GgufLayer &y = layers[L];
-        if (!(y.router = gguf_need(g, b + "ffn_gate_inp.weight", 2, H, E, 0, err)) ||
-            !(y.norm = gguf_need(g, b + "ffn_norm.weight", 1, H, 0, 0, err)) ||
-            !(y.gate = gguf_need(g, b + "ffn_gate_exps.weight", 3, H, F, E, err)) ||
-            !(y.up = gguf_need(g, b + "ffn_up_exps.weight", 3, H, F, E, err)) ||
-            !(y.down = gguf_need(g, b + "ffn_down_exps.weight", 3, F, H, E, err)))
-            return false;
-        if (y.router->type != TRX_F32 && y.router->type != TRX_BF16) {
-            err = b + "ffn_gate_inp.weight has type " + std::to_string(y.router->type) + " (F32 or BF16 taken)";
-            return false;
-        }
-        if (y.norm->type != TRX_F32) {
-            err = b + "ffn_norm.weight is not F32";
-            return false;
-        }
-        if (y.up->type != y.gate->type || y.gate->type != layers[0].gate->type || y.down->type != layers[0].down->type) {
-            err = "layer " + std::to_string(L) + "'s expert types differ from layer 0's (gate/up " +
-                  std::to_string(layers[0].gate->type) + ", down " + std::to_string(layers[0].down->type) +
-                  "): a context takes one gate/up type and one down type";
-            return false;
-        }
-        if (y.router->type == TRX_F32 && all_bf16) all_bf16 = gguf_bf16_exact(*y.router, g.bytes(*y.router));
-    }
-    cfg.n_layers = nl;
-    cfg.n_expert = E;
-    cfg.n_used = k;
-    cfg.n_embd = H;
-    cfg.n_ff = F;
-    cfg.norm_topk = norm_topk ? 1 : 0;
-    cfg.router_type = all_bf16 ? TRX_BF16 : TRX_F32;
-    cfg.gate_type = (int32_t)layers[0].gate->type;
-    cfg.down_type = (int32_t)layers[0].down->type;
-    return true;
-}
-
-} // namespace
-
-extern "C" int tr_gpu_moe_config_from_gguf(const char *path, tr_gpu_moe_config *cfg, float *rms_eps, char *err,
-                                           size_t err_len) {
-    g_err.clear();
-    if (path == nullptr || cfg == nullptr) {
-        set_err("bad arguments to tr_gpu_moe_config_from_gguf");
-        put_err(err, err_len);
-        return -1;
-    }
-    TrxGguf g;
-    std::string e;
-    tr_gpu_moe_config c = *cfg;
-    float eps = 0.0f;
-    std::vector<GgufLayer> layers;
-    if (!g.open(path, e) || !gguf_config(g, c, eps, layers, e)) {
-        set_err("%s", e.c_str());
-        put_err(err, err_len);
-        return -1;
-    }
-    *cfg = c;
-    if (rms_eps) *rms_eps = eps;
-    return 0;
-}
-
-extern "C" int tr_gpu_moe_load_gguf(tr_gpu_moe *m, const char *path, char *err, size_t err_len) {
-    g_err.clear();
-    if (m == nullptr || path == nullptr) {
-        set_err("bad arguments to tr_gpu_moe_load_gguf");
-        put_err(err, err_len);
-        return -1;
-    }
-    TrxGguf g;
-    std::string e;
-    tr_gpu_moe_config f = m->cfg;
-    float eps = 0.0f;
-    std::vector<GgufLayer> layers;
-    if (!g.open(path, e) || !gguf_config(g, f, eps, layers, e)) {
-        set_err("%s", e.c_str());
-        put_err(err, err_len);
-        return -1;
-    }
-    const tr_gpu_moe_config &c = m->cfg;
-    if (f.n_layers != c.n_layers || f.n_expert != c.n_expert || f.n_used != c.n_used || f.n_embd != c.n_embd ||
-        f.n_ff != c.n_ff || f.norm_topk != c.norm_topk || f.gate_type != c.gate_type || f.down_type != c.down_type ||
-        (f.router_type == TRX_F32 && c.router_type == TRX_BF16)) {
-        set_err("the file's MoE configuration (layers %lld, experts %lld of %lld, %lldx%lld, norm_topk %d, router %d, "
-                "gate/up %d, down %d) is not the context's (tr_gpu_moe_config_from_gguf gives it)",
-                (long long)f.n_layers, (long long)f.n_used, (long long)f.n_expert, (long long)f.n_embd,
-                (long long)f.n_ff, f.norm_topk, f.router_type, f.gate_type, f.down_type);
-        put_err(err, err_len);
-        return -1;
-    }
-    const int64_t E = c.n_expert, H = c.n_embd, F = c.n_ff;
-    const int64_t gate_bytes = trx_row_bytes(c.gate_type, H) * F, down_bytes = trx_row_bytes(c.down_type, F) * H;
-    std::vector<const void *> gp((size_t)E), up((size_t)E), dp((size_t)E);
-    std::vector<uint16_t> r16;
-    std::vector<float> r32;
-    for (int64_t L = 0; L < c.n_layers; L++) {
-        const GgufLayer &y = layers[(size_t)L];
-        // the router in the context's type: as stored, narrowed (bfloat16-exact F32) or widened (BF16 into F32)
-        const void *router = g.bytes(*y.router);
-        const int64_t nr = E * H;
-        if (y.router->type == TRX_F32 && c.router_type == TRX_BF16) {
-            r16.resize((size_t)nr);
-            for (int64_t i = 0; i < nr; i++) {
-                uint32_t v;
-                memcpy(&v, (const uint8_t *)router + 4 * i, 4);
-                r16[(size_t)i] = (uint16_t)(v >> 16);
-            }
-            router = r16.data();
-        } else if (y.router->type == TRX_BF16 && c.router_type == TRX_F32) {
-            r32.resize((size_t)nr);
-            for (int64_t i = 0; i < nr; i++) {
-                uint16_t v;
-                memcpy(&v, (const uint8_t *)router + 2 * i, 2);
-                const uint32_t w = (uint32_t)v << 16;
-                memcpy(&r32[(size_t)i], &w, 4);
-            }
-            router = r32.data();
-        }
-        // expert e of a stacked tensor at byte e out row_bytes(in) (olmoe.c:466-472)
-        for (int64_t x = 0; x < E; x++) {
-            gp[(size_t)x] = g.bytes(*y.gate) + x * gate_bytes;
-            up[(size_t)x] = g.bytes(*y.up) + x * gate_bytes;
-            dp[(size_t)x] = g.bytes(*y.down) + x * down_bytes;
-        }
-        if (tr_gpu_moe_set_layer(m, L, router, nullptr, gp.data(), up.data(), dp.data(), err, err_len) != 0)
-            return -1;
-        float norm_host[8192];
-        memcpy(norm_host, g.bytes(*y.norm), (size_t)H * 4); // (the mapping's bytes may be unaligned for floats)
-        if (tr_gpu_moe_set_ffn_norm(m, L, norm_host, eps, err, err_len) != 0) return -1;
-    }
-    return 0;
-}
-
-// ---------------------------------------------------------------------------------------------
-// expert parallelism (ep.cuh): pack, the experts of arriving rows, combine
-
-extern "C" int tr_gpu_moe_ep_pack(tr_gpu_moe *m, const int64_t *d_sel_id, int64_t n_tok, int32_t n_ranks, int64_t cap,
-                                  const float *d_normed, float *d_send_rows, int32_t *d_send_ids, int32_t *d_send_counts,
-                                  int32_t *d_place, int32_t *d_scratch, void *stream) {
-    g_err.clear();
-    const int64_t R = n_tok * (m ? m->cfg.n_used : 0);
-    if (m == nullptr || d_sel_id == nullptr || d_normed == nullptr || d_send_rows == nullptr || d_send_ids == nullptr ||
-        d_send_counts == nullptr || d_place == nullptr || d_scratch == nullptr || n_tok < 1 || n_ranks < 1 ||
-        n_ranks > 64 || m->cfg.n_expert % n_ranks != 0 || (cap != 0 && cap < R) || R > (1 << 24)) {
-        set_err("bad arguments to tr_gpu_moe_ep_pack (ranks must divide the experts; cap 0 or at least n_tok x n_used)");
-        return -1;
-    }
-    if (!ck(cudaSetDevice(m->device), "cudaSetDevice")) return -1;
-    cudaStream_t st = stream ? (cudaStream_t)stream : m->stream;
-    const int H = (int)m->cfg.n_embd;
-    const int64_t div = m->cfg.n_expert / n_ranks;
-    int32_t *offsets = d_scratch, *xmap = d_scratch + 72; // scratch: 72 + R int32
-    if (cap > 0 && !ck(cudaMemsetAsync(d_send_ids, 0xff, (size_t)(n_ranks * cap) * 4, st), "clear ids")) return -1;
-    trx_k_stable_sort<<<1, 1024, 0, st>>>(d_sel_id, nullptr, div, (int)R, n_ranks, offsets, d_place, xmap, d_send_counts);
-    trx_k_gather_rows<<<(unsigned)R, 256, 0, st>>>(d_normed, xmap, offsets + n_ranks, (int)m->cfg.n_used, H, d_send_rows,
-                                                   d_sel_id, d_send_ids, offsets, (int)cap, div, d_place);
-    return ck(cudaGetLastError(), "ep pack launch") ? 0 : -1;
-}
-
-extern "C" int tr_gpu_moe_experts_dev(tr_gpu_moe *m, int64_t layer, const float *d_rows, const int32_t *d_ids,
-                                      int64_t n_rows, float *d_out, void *stream) {
-    g_err.clear();
-    if (m == nullptr || layer < 0 || layer >= m->cfg.n_layers || !m->layer_set[(size_t)layer] || n_rows < 0 ||
-        (n_rows > 0 && (d_rows == nullptr || d_ids == nullptr || d_out == nullptr))) {
-        set_err("bad arguments to tr_gpu_moe_experts_dev (or the layer is not set)");
-        return -1;
-    }
-    if (n_rows == 0) return 0;
-    if (n_rows > (1 << 24)) {
-        set_err("tr_gpu_moe_experts_dev: %lld rows is more than it takes", (long long)n_rows);
-        return -1;
-    }
-    if (!ck(cudaSetDevice(m->device), "cudaSetDevice")) return -1;
-    cudaStream_t st = stream ? (cudaStream_t)stream : m->stream;
-    const tr_gpu_moe_config &c = m->cfg;
-    const int64_t E = c.n_expert, H = c.n_embd, F = c.n_ff, n = n_rows, mx = std::max(H, F);
-    // Up to TRX_ROUTE_FUSED_MAX rows, and no more than the context's max_tokens (its per-row work buffers): the fused
-    // decode kernel with the routing given (row t to expert ids[t] alone, weight 1: its mix is the expert's row),
-    // one launch
-    int sg = 0, sd = 0;
-    if (m->fused_ok && n <= TRX_ROUTE_FUSED_MAX && n <= c.max_tokens && n <= m->grid_fused &&
-        fused_stages(m, (int)n, &sg, &sd, 1)) {
-        const TrxLayer &L = m->layers[(size_t)layer];
-        const TrxShape S{(int)E, 1, (int)H, (int)F, 0, 0, 1};
-        TrxWork w = m->work;
-        w.ext_ids = d_ids;
-        const uint32_t epoch = (++m->epoch & 0x7fffffffu) | 1u;
-        return launch_fused(m, L, S, d_rows, (int)n, w, nullptr, d_out, epoch, sg, sd, st, "fused experts launch");
-    }
-    // scratch: sort (offsets, place, xmap), grouped rows, gate and up outputs, down output, prepared inputs
-    const int64_t so = align_up((E + 8 + 2 * n) * 4, 256), xb = align_up(n * H * 4, 256), gb = align_up(n * F * 4, 256),
-                  qb = align_up(n * mx * 4, 256), bfb = align_up(n * (mx / 32) * 8, 256), scb = align_up(n * (mx / 256) * 8, 256),
-                  need = so + 2 * xb + 2 * gb + qb + bfb + scb;
-    if (need > m->ep_cap) {
-        if (m->ep_buf) {
-            if (!stream_wait(st)) return -1;
-            cudaFree(m->ep_buf);
-            m->ep_buf = nullptr;
-            m->ep_cap = 0;
-        }
-        if (!ck(cudaMalloc(&m->ep_buf, (size_t)need), "cudaMalloc(expert scratch)")) return -1;
-        m->ep_cap = need;
-    }
-    uint8_t *b = m->ep_buf;
-    int32_t *offsets = (int32_t *)b, *place = offsets + E + 8, *xmap = place + n;
-    float *xg = (float *)(b + so), *y = (float *)(b + so + xb), *g = (float *)(b + so + 2 * xb),
-          *u = (float *)(b + so + 2 * xb + gb);
-    uint32_t *dq = (uint32_t *)(b + so + 2 * xb + 2 * gb);
-    double *dbf = (double *)(b + so + 2 * xb + 2 * gb + qb), *dsc = (double *)(b + so + 2 * xb + 2 * gb + qb + bfb);
-    const uint8_t *const *tab = m->ep_tab + (size_t)layer * 3 * E;
-    trx_k_stable_sort<<<1, 1024, 0, st>>>(nullptr, d_ids, 1, (int)n, (int)E, offsets, place, xmap, nullptr);
-    trx_k_gather_rows<<<(unsigned)n, 256, 0, st>>>(d_rows, xmap, offsets + E, 1, (int)H, xg, nullptr, nullptr, nullptr,
-                                                   0, 1, nullptr);
-    bool ok = trx_kapi_grouped(c.gate_type, F, H, tab, offsets, (int)E, (int)n, xg, dq, dbf, dsc, g, st) &&
-              trx_kapi_grouped(c.gate_type, F, H, tab + E, offsets, (int)E, (int)n, xg, dq, dbf, dsc, u, st) &&
-              trx_kapi_swiglu(g, u, n * F, st) &&
-              trx_kapi_grouped(c.down_type, H, F, tab + 2 * E, offsets, (int)E, (int)n, g, dq, dbf, dsc, y, st);
-    if (!ok) {
-        set_err("tr_gpu_moe_experts_dev: launch failed");
-        return -1;
-    }
-    trx_k_scatter_rows<<<(unsigned)n, 256, 0, st>>>(y, xmap, offsets + E, (int)H, d_out);
-    return ck(cudaGetLastError(), "experts launch") ? 0 : -1;
-}
-
-extern "C" int tr_gpu_moe_ep_combine(tr_gpu_moe *m, const float *d_sel_w, const int32_t *d_place, const float *d_back,
-                                     int64_t n_tok, float *d_x, float *d_ffn_out, void *stream) {
-    g_err.clear();
-    if (m == nullptr || d_sel_w == nullptr || d_place == nullptr || d_back == nullptr || d_x == nullptr || n_tok < 1) {
-        set_err("bad arguments to tr_gpu_moe_ep_combine");
-        return -1;
-    }
-    if (!ck(cudaSetDevice(m->device), "cudaSetDevice")) return -1;
-    cudaStream_t st = stream ? (cudaStream_t)stream : m->stream;
-    const int64_t total = n_tok * m->cfg.n_embd;
-    trx_k_pf_combine<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(d_sel_w, d_place, d_back, (int)n_tok,
-                                                                     (int)m->cfg.n_used, (int)m->cfg.n_embd, d_x, d_ffn_out);
-    return ck(cudaGetLastError(), "ep combine launch") ? 0 : -1;
-}
-
-// ---------------------------------------------------------------------------------------------
-// expert parallelism over peer memory (ep.cuh): the exchange region, the peers' regions, dispatch / experts / combine
-
-extern "C" int tr_gpu_moe_ep_peer_region(tr_gpu_moe *m, int32_t n_ranks, int32_t rank, int64_t cap, void *ipc_handle_out) {
-    g_err.clear();
-    if (m == nullptr || n_ranks < 1 || n_ranks > TRX_EP_MAX_RANKS || rank < 0 || rank >= n_ranks || cap < 1 ||
-        cap > 256 || ipc_handle_out == nullptr || m->cfg.n_expert % n_ranks != 0 || m->epp_region != nullptr) {
-        set_err("bad arguments to tr_gpu_moe_ep_peer_region (or the region exists)");
-        return -1;
-    }
-    if (!ck(cudaSetDevice(m->device), "cudaSetDevice")) return -1;
-    size_t ids, rows, back, total;
-    trx_ep_layout(n_ranks, (int)cap, (int)m->cfg.n_embd, ids, rows, back, total);
-    cudaIpcMemHandle_t h;
-    if (!ck(cudaMalloc(&m->epp_region, total), "cudaMalloc(exchange region)") ||
-        !ck(cudaMemset(m->epp_region, 0, total), "cudaMemset(exchange region)") ||
-        !ck(cudaIpcGetMemHandle(&h, m->epp_region), "cudaIpcGetMemHandle")) {
-        if (m->epp_region) cudaFree(m->epp_region);
-        m->epp_region = nullptr;
-        return -1;
-    }
-    memcpy(ipc_handle_out, &h, sizeof h);
-    m->epp_n = n_ranks;
-    m->epp_rank = rank;
-    m->epp_cap = cap;
-    return 0;
-}
-
-extern "C" int tr_gpu_moe_ep_peer_open(tr_gpu_moe *m, const void *ipc_handles) {
-    g_err.clear();
-    if (m == nullptr || m->epp_region == nullptr || ipc_handles == nullptr || m->epp_dev != nullptr) {
-        set_err("bad arguments to tr_gpu_moe_ep_peer_open (no region, or already open)");
-        return -1;
-    }
-    if (!ck(cudaSetDevice(m->device), "cudaSetDevice")) return -1;
-    TrxEpPeers P{};
-    P.n = m->epp_n;
-    P.rank = m->epp_rank;
-    P.cap = (int)m->epp_cap;
-    P.H = (int)m->cfg.n_embd;
-    size_t total;
-    trx_ep_layout(P.n, P.cap, P.H, P.off_ids, P.off_rows, P.off_back, total);
-    m->epp_opened.assign((size_t)P.n, nullptr);
-    for (int r = 0; r < P.n; r++) {
-        if (r == P.rank) {
-            P.base[r] = m->epp_region;
-            continue;
-        }
-        cudaIpcMemHandle_t h;
-        memcpy(&h, (const uint8_t *)ipc_handles + (size_t)r * sizeof h, sizeof h);
-        void *p = nullptr;
-        if (!ck(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle")) return -1;
-        m->epp_opened[(size_t)r] = (uint8_t *)p;
-        P.base[r] = (uint8_t *)p;
-    }
-    if (!ck(cudaMalloc(&m->epp_dev, sizeof P), "cudaMalloc(peer table)") ||
-        !ck(cudaMemcpy(m->epp_dev, &P, sizeof P, cudaMemcpyHostToDevice), "copy peer table"))
-        return -1;
-    return 0;
-}
-
-extern "C" int tr_gpu_moe_ep_dispatch(tr_gpu_moe *m, const int64_t *d_sel_id, int64_t n_tok, const float *d_normed,
-                                      int32_t *d_place, void *stream) {
-    g_err.clear();
-    if (m == nullptr || m->epp_dev == nullptr || d_sel_id == nullptr || d_normed == nullptr || d_place == nullptr ||
-        n_tok < 1 || n_tok * m->cfg.n_used > m->epp_cap || n_tok * m->cfg.n_used > 256) {
-        set_err("bad arguments to tr_gpu_moe_ep_dispatch (no open exchange, or n_tok x n_used above its cap)");
-        return -1;
-    }
-    if (!ck(cudaSetDevice(m->device), "cudaSetDevice")) return -1;
-    cudaStream_t st = stream ? (cudaStream_t)stream : m->stream;
-    trx_k_ep_dispatch<<<1, 256, 0, st>>>(d_sel_id, (int)n_tok, (int)m->cfg.n_used, (int)(m->cfg.n_expert / m->epp_n),
-                                        d_normed, m->epp_dev, d_place);
-    return ck(cudaGetLastError(), "ep dispatch launch") ? 0 : -1;
-}
-
-extern "C" int tr_gpu_moe_ep_experts(tr_gpu_moe *m, int64_t layer, void *stream) {
-    g_err.clear();
-    if (m == nullptr || m->epp_dev == nullptr || layer < 0 || layer >= m->cfg.n_layers || !m->layer_set[(size_t)layer]) {
-        set_err("bad arguments to tr_gpu_moe_ep_experts (no open exchange, or the layer is not set)");
-        return -1;
-    }
-    if (!ck(cudaSetDevice(m->device), "cudaSetDevice")) return -1;
-    cudaStream_t st = stream ? (cudaStream_t)stream : m->stream;
-    const tr_gpu_moe_config &c = m->cfg;
-    const int64_t n = (int64_t)m->epp_n * m->epp_cap, E = c.n_expert, H = c.n_embd, F = c.n_ff;
-    int sg = 0, sd = 0;
-    if (!(m->fused_ok && n <= TRX_ROUTE_FUSED_MAX && n <= c.max_tokens && n <= m->grid_fused &&
-          fused_stages(m, (int)n, &sg, &sd, 1))) {
-        set_err("tr_gpu_moe_ep_experts: n_ranks x cap = %lld rows do not fit the fused kernel (at most %d, and the "
-                "context's max_tokens)", (long long)n, TRX_ROUTE_FUSED_MAX);
-        return -1;
-    }
-    size_t ids, rows, back, total;
-    trx_ep_layout(m->epp_n, (int)m->epp_cap, (int)H, ids, rows, back, total);
-    const TrxLayer &L = m->layers[(size_t)layer];
-    const TrxShape S{(int)E, 1, (int)H, (int)F, 0, 0, 1};
-    TrxWork w = m->work;
-    w.ext_ids = (const int32_t *)(m->epp_region + ids);
-    w.ep = m->epp_dev;
-    const uint32_t epoch = (++m->epoch & 0x7fffffffu) | 1u;
-    return launch_fused(m, L, S, (const float *)(m->epp_region + rows), (int)n, w, nullptr, nullptr, epoch, sg, sd, st,
-                        "ep experts launch");
-}
-
-extern "C" int tr_gpu_moe_ep_peer_combine(tr_gpu_moe *m, const float *d_sel_w, const int32_t *d_place, int64_t n_tok,
-                                          float *d_x, float *d_ffn_out, void *stream) {
-    g_err.clear();
-    if (m == nullptr || m->epp_dev == nullptr || d_sel_w == nullptr || d_place == nullptr || d_x == nullptr || n_tok < 1) {
-        set_err("bad arguments to tr_gpu_moe_ep_peer_combine");
-        return -1;
-    }
-    if (!ck(cudaSetDevice(m->device), "cudaSetDevice")) return -1;
-    cudaStream_t st = stream ? (cudaStream_t)stream : m->stream;
-    const int64_t total = n_tok * m->cfg.n_embd;
-    trx_k_ep_peer_combine<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(d_sel_w, d_place, m->epp_dev, (int)n_tok,
-                                                                          (int)m->cfg.n_used, d_x, d_ffn_out, m->work.err);
-    return ck(cudaGetLastError(), "ep combine launch") ? 0 : -1;
-}
-
-// ---------------------------------------------------------------------------------------------
-// decode attention (attention.cuh): Trochilus's GPU attention backend (src/backend/gpu_attn.h) on the B200
-
-struct tr_gpu {
-    int device = 0;
-    char name[256] = {0};
-};
-
-struct tr_gpu_attn {
-    tr_gpu *g = nullptr;
-    int64_t n_layers = 0, n_head = 0, n_ctx = 0, s_stride = 0;
-    float *keys = nullptr, *values = nullptr; // [layer][head][pos][128]
-    float *scores = nullptr;                  // [head][s_stride]
-    float *io = nullptr;                      // a call's rows: q, k, v of a decode, or a write's chunk; then out
-    int32_t *err = nullptr;
-    cudaStream_t st = nullptr, warm_st = nullptr;
-    uint32_t *h_stop = nullptr, *d_stop = nullptr; // the warm-up kernel's stop word (mapped pinned)
-};
-
-namespace {
-
-constexpr int64_t kAttnWriteChunk = 256; // tokens a write moves per copy
-constexpr uint64_t kAttnReserve = (uint64_t)512 << 20;
-constexpr uint64_t kAttnWarmMaxNs = 200000000;
-
-int64_t attn_s_stride(int64_t n_ctx) { return (n_ctx + TRX_ATTN_CHUNK - 1) / TRX_ATTN_CHUNK * TRX_ATTN_CHUNK; }
-
-// a failed call's stream and error word: whatever was in flight finishes, the word goes back to 0
-bool attn_fail(tr_gpu_attn *a, const char *what) {
-    cudaStreamSynchronize(a->st);
-    cudaMemsetAsync(a->err, 0, 4, a->st);
-    cudaStreamSynchronize(a->st);
-    set_err("%s", what);
-    return false;
-}
-
-} // namespace
-
-extern "C" tr_gpu *tr_gpu_open(char *err, size_t err_len) {
-    g_err.clear();
-    int n = 0;
-    if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) {
-        cudaGetLastError();
-        set_err("no CUDA device (or no driver)");
-        put_err(err, err_len);
-        return nullptr;
-    }
-    for (int d = 0; d < n; d++) {
-        cudaDeviceProp p;
-        if (cudaGetDeviceProperties(&p, d) != cudaSuccess || p.major != 10 || p.minor != 0) continue;
-        tr_gpu *g = new tr_gpu;
-        g->device = d;
-        snprintf(g->name, sizeof g->name, "%s", p.name);
-        return g;
-    }
-    set_err("no device of compute capability 10.0 (the library's kernels are built for sm_100a)");
-    put_err(err, err_len);
-    return nullptr;
-}
-
-extern "C" void tr_gpu_close(tr_gpu *g) { delete g; }
-
-extern "C" const char *tr_gpu_name(const tr_gpu *g) { return g ? g->name : ""; }
-
-extern "C" uint64_t tr_gpu_attn_bytes(int64_t n_layers, int64_t n_head, int64_t head_dim, int64_t n_ctx) {
-    if (n_layers < 1 || n_head < 1 || head_dim < 1 || n_ctx < 1) return 0;
-    const uint64_t cache = 2ull * (uint64_t)n_layers * (uint64_t)n_head * (uint64_t)n_ctx * (uint64_t)head_dim * 4;
-    const uint64_t scores = (uint64_t)n_head * (uint64_t)attn_s_stride(n_ctx) * 4;
-    const uint64_t io = (uint64_t)std::max<int64_t>(4, 2 * kAttnWriteChunk) * (uint64_t)(n_head * head_dim) * 4;
-    return cache + scores + io + 256;
-}
-
-extern "C" void tr_gpu_attn_free(tr_gpu_attn *a) {
-    if (a == nullptr) return;
-    cudaSetDevice(a->g->device);
-    if (a->h_stop) *(volatile uint32_t *)a->h_stop = 1u; // a warm-up still running stops
-    if (a->warm_st) cudaStreamSynchronize(a->warm_st);
-    if (a->st) cudaStreamSynchronize(a->st);
-    cudaFree(a->keys);
-    cudaFree(a->values);
-    cudaFree(a->scores);
-    cudaFree(a->io);
-    cudaFree(a->err);
-    if (a->h_stop) cudaFreeHost(a->h_stop);
-    if (a->st) cudaStreamDestroy(a->st);
-    if (a->warm_st) cudaStreamDestroy(a->warm_st);
-    delete a;
-}
-
-extern "C" tr_gpu_attn *tr_gpu_attn_create(tr_gpu *g, int64_t n_layers, int64_t n_head, int64_t head_dim,
-                                           int64_t n_ctx, char *err, size_t err_len) {
-    g_err.clear();
-    if (head_dim != TRX_ATTN_HD) {
-        set_err("head_dim %lld not supported (128)", (long long)head_dim);
-        put_err(err, err_len);
-        return nullptr;
-    }
-    if (n_layers < 1 || n_head < 1 || n_head > 65535 || n_ctx < 1 || n_ctx > (1 << 24)) {
-        set_err("bad shape (layers %lld, heads %lld, context %lld)", (long long)n_layers, (long long)n_head,
-                (long long)n_ctx);
-        put_err(err, err_len);
-        return nullptr;
-    }
-    if (g == nullptr) {
-        set_err("no device (tr_gpu_open)");
-        put_err(err, err_len);
-        return nullptr;
-    }
-    if (!ck(cudaSetDevice(g->device), "cudaSetDevice")) {
-        put_err(err, err_len);
-        return nullptr;
-    }
-    size_t free_b = 0, total_b = 0;
-    const uint64_t need = tr_gpu_attn_bytes(n_layers, n_head, head_dim, n_ctx);
-    if (!ck(cudaMemGetInfo(&free_b, &total_b), "cudaMemGetInfo")) {
-        put_err(err, err_len);
-        return nullptr;
-    }
-    if ((uint64_t)free_b < need + kAttnReserve) {
-        set_err("the cache needs %llu bytes and %llu must stay free; %llu are", (unsigned long long)need,
-                (unsigned long long)kAttnReserve, (unsigned long long)free_b);
-        put_err(err, err_len);
-        return nullptr;
-    }
-    tr_gpu_attn *a = new tr_gpu_attn;
-    a->g = g;
-    a->n_layers = n_layers;
-    a->n_head = n_head;
-    a->n_ctx = n_ctx;
-    a->s_stride = attn_s_stride(n_ctx);
-    const size_t cache = (size_t)n_layers * n_head * n_ctx * TRX_ATTN_HD * 4;
-    const size_t io = (size_t)std::max<int64_t>(4, 2 * kAttnWriteChunk) * n_head * TRX_ATTN_HD * 4;
-    bool ok = ck(cudaMalloc(&a->keys, cache), "cudaMalloc(keys)") &&
-              ck(cudaMalloc(&a->values, cache), "cudaMalloc(values)") &&
-              ck(cudaMalloc(&a->scores, (size_t)n_head * a->s_stride * 4), "cudaMalloc(scores)") &&
-              ck(cudaMalloc(&a->io, io), "cudaMalloc(io)") && ck(cudaMalloc(&a->err, 4), "cudaMalloc(err)") &&
-              ck(cudaMemset(a->err, 0, 4), "cudaMemset(err)") &&
-              ck(cudaMemset(a->scores, 0, (size_t)n_head * a->s_stride * 4), "cudaMemset(scores)") &&
-              ck(cudaStreamCreateWithFlags(&a->st, cudaStreamNonBlocking), "cudaStreamCreate") &&
-              ck(cudaStreamCreateWithFlags(&a->warm_st, cudaStreamNonBlocking), "cudaStreamCreate") &&
-              ck(cudaHostAlloc((void **)&a->h_stop, 4, cudaHostAllocMapped), "cudaHostAlloc(stop)") &&
-              ck(cudaHostGetDevicePointer((void **)&a->d_stop, a->h_stop, 0), "cudaHostGetDevicePointer(stop)") &&
-              ck(cudaFuncSetAttribute(trx_attn_values, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      TRX_ATTN_STAGES * TRX_ATTN_STAGE_BYTES),
-                 "values kernel shared memory");
-    if (!ok) {
-        put_err(err, err_len);
-        tr_gpu_attn_free(a);
-        return nullptr;
-    }
-    *a->h_stop = 1u;
-    return a;
-}
-
-extern "C" int tr_gpu_attn_write(tr_gpu_attn *a, int64_t layer, int64_t pos0, int64_t n_tok, const float *k,
-                                 const float *v) {
-    g_err.clear();
-    if (a == nullptr || layer < 0 || layer >= a->n_layers || pos0 < 0 || n_tok < 0 || pos0 + n_tok > a->n_ctx ||
-        (n_tok > 0 && (k == nullptr || v == nullptr))) {
-        set_err("bad arguments to tr_gpu_attn_write (a range outside the cache)");
-        return -1;
-    }
-    if (!ck(cudaSetDevice(a->g->device), "cudaSetDevice")) return -1;
-    const int64_t row = a->n_head * TRX_ATTN_HD, lay = a->n_head * a->n_ctx * TRX_ATTN_HD;
-    bool ok = true;
-    for (int64_t i = 0; ok && i < n_tok; i += kAttnWriteChunk) {
-        const int64_t n = std::min(kAttnWriteChunk, n_tok - i);
-        float *sk = a->io, *sv = a->io + kAttnWriteChunk * row;
-        const unsigned blocks = (unsigned)((n * a->n_head + 7) / 8);
-        ok = ck(cudaMemcpyAsync(sk, k + i * row, (size_t)(n * row) * 4, cudaMemcpyHostToDevice, a->st), "copy k") &&
-             ck(cudaMemcpyAsync(sv, v + i * row, (size_t)(n * row) * 4, cudaMemcpyHostToDevice, a->st), "copy v");
-        if (ok) {
-            trx_attn_store<<<blocks, 256, 0, a->st>>>(sk, (int)n, (int)a->n_head, pos0 + i, a->n_ctx, a->keys + layer * lay);
-            trx_attn_store<<<blocks, 256, 0, a->st>>>(sv, (int)n, (int)a->n_head, pos0 + i, a->n_ctx,
-                                                      a->values + layer * lay);
-            ok = ck(cudaGetLastError(), "store kernel") && stream_wait(a->st); // (the staging is reused)
-        }
-    }
-    return ok ? 0 : -1;
-}
-
-extern "C" int tr_gpu_attn_decode(tr_gpu_attn *a, int64_t layer, int64_t pos, const float *q, const float *k,
-                                  const float *v, float scale, float *out) {
-    g_err.clear();
-    if (a == nullptr || layer < 0 || layer >= a->n_layers || pos < 0 || pos >= a->n_ctx || q == nullptr ||
-        k == nullptr || v == nullptr || out == nullptr) {
-        set_err("bad arguments to tr_gpu_attn_decode (pos outside the cache)");
-        return -1;
-    }
-    *(volatile uint32_t *)a->h_stop = 1u; // a warm-up still running ends
-    if (!ck(cudaSetDevice(a->g->device), "cudaSetDevice")) return -1;
-    const int64_t row = a->n_head * TRX_ATTN_HD, lay = a->n_head * a->n_ctx * TRX_ATTN_HD, n_pos = pos + 1;
-    float *dq = a->io, *dk = a->io + row, *dv = a->io + 2 * row, *dout = a->io + 3 * row;
-    float *K = a->keys + layer * lay, *V = a->values + layer * lay;
-    bool ok = ck(cudaMemcpyAsync(dq, q, (size_t)row * 4, cudaMemcpyHostToDevice, a->st), "copy q") &&
-              ck(cudaMemcpyAsync(dk, k, (size_t)row * 4, cudaMemcpyHostToDevice, a->st), "copy k") &&
-              ck(cudaMemcpyAsync(dv, v, (size_t)row * 4, cudaMemcpyHostToDevice, a->st), "copy v");
-    if (!ok) return -1;
-    const unsigned sb = (unsigned)((a->n_head + 7) / 8);
-    trx_attn_store<<<sb, 256, 0, a->st>>>(dk, 1, (int)a->n_head, pos, a->n_ctx, K);
-    trx_attn_store<<<sb, 256, 0, a->st>>>(dv, 1, (int)a->n_head, pos, a->n_ctx, V);
-    trx_attn_scores<<<dim3((unsigned)((n_pos + 15) / 16), (unsigned)a->n_head), 256, 0, a->st>>>(
-        dq, K, V, (int)n_pos, a->n_ctx, scale, a->scores, a->s_stride);
-    trx_softmax_rows_k<<<(unsigned)a->n_head, 256, 0, a->st>>>(a->scores, n_pos, a->s_stride);
-    trx_attn_values<<<(unsigned)a->n_head, 160, TRX_ATTN_STAGES * TRX_ATTN_STAGE_BYTES, a->st>>>(
-        a->scores, a->s_stride, V, (int)n_pos, a->n_ctx, dout, a->err);
-    int32_t e = 0;
-    ok = ck(cudaGetLastError(), "attention kernels") &&
-         ck(cudaMemcpyAsync(out, dout, (size_t)row * 4, cudaMemcpyDeviceToHost, a->st), "copy out") &&
-         ck(cudaMemcpyAsync(&e, a->err, 4, cudaMemcpyDeviceToHost, a->st), "copy error word") && stream_wait(a->st);
-    if (!ok) return -1;
-    if (e != 0) {
-        attn_fail(a, "the attention kernel gave up on a bounded wait");
-        return -1;
-    }
-    return 0;
-}
-
-extern "C" int tr_gpu_attn_warm(tr_gpu_attn *a, uint64_t ns) {
-    g_err.clear();
-    if (a == nullptr) {
-        set_err("bad arguments to tr_gpu_attn_warm");
-        return -1;
-    }
-    if (!ck(cudaSetDevice(a->g->device), "cudaSetDevice")) return -1;
-    // the one before has ended (its stop word was set, or its time ran out), then the stop word is cleared
-    *(volatile uint32_t *)a->h_stop = 1u;
-    if (!ck(cudaStreamSynchronize(a->warm_st), "warm stream")) return -1;
-    *(volatile uint32_t *)a->h_stop = 0u;
-    trx_attn_warm<<<1, 1, 0, a->warm_st>>>(a->d_stop, std::min<uint64_t>(ns, kAttnWarmMaxNs));
-    return ck(cudaGetLastError(), "warm kernel") ? 0 : -1;
-}
-
-// ---------------------------------------------------------------------------------------------
-// the kernel level
-
-namespace {
-
-struct KMat {
-    uint8_t *dev;
-    int64_t bytes;
-};
-
-struct KCtx {
-    std::mutex mu;
-    bool init = false;
-    int device = 0;
-    cudaStream_t st = nullptr;
-    std::unordered_map<std::string, KMat> mats;
-    uint8_t *buf = nullptr; // x, prepared x, y
-    int64_t buf_bytes = 0;
-    uint8_t *tmp = nullptr;
-    int64_t tmp_bytes = 0;
-};
-
-KCtx &kctx() {
-    static KCtx c;
-    return c;
-}
-
-bool kinit(KCtx &c) {
-    if (c.init) return true;
-    if (!ck(cudaGetDevice(&c.device), "cudaGetDevice") ||
-        !ck(cudaStreamCreateWithFlags(&c.st, cudaStreamNonBlocking), "cudaStreamCreate"))
-        return false;
-    c.init = true;
-    return true;
-}
-
-bool kreserve(uint8_t **p, int64_t *have, int64_t need) {
-    if (*have >= need) return true;
-    if (*p) cudaFree(*p);
-    *p = nullptr;
-    *have = 0;
-    if (!ck(cudaMalloc(p, (size_t)need), "cudaMalloc")) return false;
-    *have = need;
-    return true;
-}
-
-// the device copy of a host matrix, uploaded on first sight
-uint8_t *kmat(KCtx &c, const tr_mat &w) {
-    char key[96];
-    snprintf(key, sizeof key, "%p/%d/%lld/%lld", w.data, (int)w.type, (long long)w.rows, (long long)w.cols);
-    auto it = c.mats.find(key);
-    if (it != c.mats.end()) return it->second.dev;
-    const int64_t bytes = trx_row_bytes(w.type, w.cols) * w.rows;
-    uint8_t *d = nullptr;
-    if (!ck(cudaMalloc(&d, (size_t)align_up(bytes, 256)), "cudaMalloc(weight)")) return nullptr;
-    if (!kreserve(&c.tmp, &c.tmp_bytes, bytes) || !upload_matrix(w.type, w.rows, w.cols, w.data, d, c.tmp, c.st)) {
-        cudaFree(d);
-        return nullptr;
-    }
-    c.mats[key] = KMat{d, bytes};
-    return d;
-}
-
-bool ktype_ok(const tr_mat &w) {
-    switch (w.type) {
-    case TRX_F32:
-    case TRX_F16:
-    case TRX_BF16: return w.cols % 16 == 0;
-    case TRX_Q8_0:
-    case TRX_Q6_K:
-    case TRX_Q4_K: return w.cols % 256 == 0;
-    default: return false;
-    }
-}
-
-bool kgrouped(const tr_mat *w, const int64_t *offsets, int64_t n_groups, const float *x, float *y) {
-    if (n_groups <= 0 || offsets[n_groups] <= 0 || w[0].rows <= 0) return true;
-    const int type = w[0].type;
-    const int64_t rows = w[0].rows, cols = w[0].cols, n_in = offsets[n_groups];
-    for (int64_t g = 0; g < n_groups; g++)
-        if (w[g].type != type || w[g].rows != rows || w[g].cols != cols || !ktype_ok(w[g])) {
-            set_err("tr_matmul_grouped: group %lld has type %d %lldx%lld, not supported or not the first's", (long long)g,
-                    (int)w[g].type, (long long)w[g].rows, (long long)w[g].cols);
-            return false;
-        }
-    if (n_in > INT32_MAX / 2 || rows > INT32_MAX / 2) {
-        set_err("tr_matmul_grouped: too large");
-        return false;
-    }
-    KCtx &c = kctx();
-    std::lock_guard<std::mutex> lock(c.mu);
-    if (!kinit(c) || !ck(cudaSetDevice(c.device), "cudaSetDevice")) return false;
-    std::vector<const uint8_t *> ptrs((size_t)n_groups, nullptr);
-    for (int64_t g = 0; g < n_groups; g++)
-        if (offsets[g + 1] > offsets[g]) {
-            ptrs[(size_t)g] = kmat(c, w[g]);
-            if (ptrs[(size_t)g] == nullptr) return false;
-        }
-    // device buffer: x, prepared x (planes + bf + scale), y, group table, offsets
-    const int64_t xb = align_up(n_in * cols * 4, 256), pb = align_up(n_in * cols * 4, 256),
-                  bfb = align_up(n_in * (cols / 32) * 8, 256), scb = align_up(n_in * (cols / 256 + 1) * 8, 256),
-                  yb = align_up(n_in * rows * 4, 256), gb = align_up(n_groups * 8, 256),
-                  ob = align_up((n_groups + 1) * 4, 256);
-    if (!kreserve(&c.buf, &c.buf_bytes, xb + pb + bfb + scb + yb + gb + ob)) return false;
-    uint8_t *b = c.buf;
-    float *dx = (float *)b;
-    uint32_t *dq = (uint32_t *)(b + xb);
-    double *dbf = (double *)(b + xb + pb);
-    double *dsc = (double *)(b + xb + pb + bfb);
-    float *dy = (float *)(b + xb + pb + bfb + scb);
-    const uint8_t **dg = (const uint8_t **)(b + xb + pb + bfb + scb + yb);
-    int32_t *doff = (int32_t *)(b + xb + pb + bfb + scb + yb + gb);
-    std::vector<int32_t> off32((size_t)n_groups + 1);
-    for (int64_t g = 0; g <= n_groups; g++) off32[(size_t)g] = (int32_t)offsets[g];
-    bool ok = ck(cudaMemcpyAsync(dx, x, (size_t)(n_in * cols * 4), cudaMemcpyHostToDevice, c.st), "copy x") &&
-              ck(cudaMemcpyAsync(dg, ptrs.data(), (size_t)n_groups * 8, cudaMemcpyHostToDevice, c.st), "copy table") &&
-              ck(cudaMemcpyAsync(doff, off32.data(), (size_t)(n_groups + 1) * 4, cudaMemcpyHostToDevice, c.st),
-                 "copy offsets");
-    if (!ok) return false;
-    ok = trx_kapi_grouped(type, rows, cols, dg, doff, (int)n_groups, (int)n_in, dx, dq, dbf, dsc, dy, c.st) &&
-         ck(cudaGetLastError(), "grouped kernel") &&
-         ck(cudaMemcpyAsync(y, dy, (size_t)(n_in * rows * 4), cudaMemcpyDeviceToHost, c.st), "copy y") &&
-         stream_wait(c.st);
-    return ok;
-}
-
-void kfail(const char *fn) { fprintf(stderr, "trmoe: %s failed: %s\n", fn, g_err.c_str()); }
-
-// Q4_K's prepared road (tr_q4x_road, tr_q4x_prepare, tr_matmul_q4x_prepared(_n), tr_swiglu_prepare). The engine keeps
-// a pass's prepared input rows in its own buffer, one slot of tr_q4x_bytes(cols) bytes a row; here a slot holds the
-// row's floats at its start, and the GPU prepares the digits inside each matmul from them (the same floats give the
-// same digits, so every output is the reference road's).
-
-// the bytes of one slot: Trochilus's tr_q4x_bytes (src/kernels/kernels.c:489-492)
-int64_t q4x_slot(int64_t n) {
-    const int64_t b = 4 * n + n / 8 + n / 4 + n / 32;
-    return (b + 63) / 64 * 64;
-}
-
-// the weights the library's Q4_K road takes (its kernels' shape limits); the reference's q4x_road
-// (src/kernels/kernels.c:1122-1128) tests w[0] alone too, the other groups being of its type and shape by contract
-bool q4x_takes(const tr_mat *w) {
-    return w != nullptr && w[0].type == TRX_Q4_K && w[0].rows > 0 && w[0].rows % 16 == 0 && w[0].cols > 0 &&
-           w[0].cols % 256 == 0 && w[0].rows <= INT32_MAX / 2 && w[0].cols <= INT32_MAX / 2;
-}
-
-std::atomic<uint64_t> g_q4x_fused{0}; // tr_matmul_q4x_prepared_n's calls of more than one weight
-
-// y_m[p rows + r] = row r of ws[m][g(p)] . input row p, for m < n_w (Q4_K weights of one shape, the same groups);
-// input row p = the floats at the start of slot map[p] (map NULL: slot p) of xq. The slots the call reads go up in
-// one strided copy, the rows are gathered on the GPU, prepared once, and every weight reads them.
-bool kprepared(const tr_mat *const *ws, int n_w, const int64_t *offsets, int64_t n_groups, const uint8_t *xq,
-               const int64_t *map, float *const *ys) {
-    const int64_t rows = ws[0][0].rows, cols = ws[0][0].cols, n_in = offsets[n_groups], slot = q4x_slot(cols);
-    for (int m = 0; m < n_w; m++)
-        for (int64_t g = 0; g < n_groups; g++)
-            if (ws[m][g].type != TRX_Q4_K || ws[m][g].rows != rows || ws[m][g].cols != cols) {
-                set_err("weight %d group %lld has type %d %lldx%lld, not Q4_K %lldx%lld", m, (long long)g,
-                        (int)ws[m][g].type, (long long)ws[m][g].rows, (long long)ws[m][g].cols, (long long)rows,
-                        (long long)cols);
-                return false;
-            }
-    int64_t n_src = n_in;
-    if (map) {
-        n_src = 0;
-        for (int64_t p = 0; p < n_in; p++) {
-            if (map[p] < 0 || map[p] >= INT32_MAX / 2) {
-                set_err("map[%lld] = %lld is not a prepared row", (long long)p, (long long)map[p]);
-                return false;
-            }
-            n_src = std::max(n_src, map[p] + 1);
-        }
-    }
-    if (n_in > INT32_MAX / 2 || n_groups > 65535) { // (the groups are the grid's second dimension)
-        set_err("too large: %lld input rows in %lld groups", (long long)n_in, (long long)n_groups);
-        return false;
-    }
-    KCtx &c = kctx();
-    std::lock_guard<std::mutex> lock(c.mu);
-    if (!kinit(c) || !ck(cudaSetDevice(c.device), "cudaSetDevice")) return false;
-    std::vector<const uint8_t *> ptrs((size_t)(n_w * n_groups), nullptr);
-    for (int m = 0; m < n_w; m++)
-        for (int64_t g = 0; g < n_groups; g++)
-            if (offsets[g + 1] > offsets[g]) {
-                ptrs[(size_t)(m * n_groups + g)] = kmat(c, ws[m][g]);
-                if (ptrs[(size_t)(m * n_groups + g)] == nullptr) return false;
-            }
-    // device buffer: the slots' floats, the gathered rows (map given), the prepared rows (planes, sub-block sums,
-    // scales), the map, the offsets, then per weight its group table and output
-    const int64_t sb = align_up(n_src * cols * 4, 256), xb = map ? align_up(n_in * cols * 4, 256) : 0,
-                  pb = align_up(n_in * cols * 4, 256), bfb = align_up(n_in * (cols / 32) * 8, 256),
-                  scb = align_up(n_in * (cols / 256 + 1) * 8, 256), mb = map ? align_up(n_in * 4, 256) : 0,
-                  ob = align_up((n_groups + 1) * 4, 256), gb = align_up(n_groups * 8, 256),
-                  yb = align_up(n_in * rows * 4, 256);
-    if (!kreserve(&c.buf, &c.buf_bytes, sb + xb + pb + bfb + scb + mb + ob + n_w * (gb + yb))) return false;
-    uint8_t *b = c.buf;
-    float *dsrc = (float *)b;
-    float *dx = map ? (float *)(b + sb) : dsrc;
-    uint32_t *dq = (uint32_t *)(b + sb + xb);
-    double *dbf = (double *)(b + sb + xb + pb);
-    double *dsc = (double *)(b + sb + xb + pb + bfb);
-    int32_t *dmap = (int32_t *)(b + sb + xb + pb + bfb + scb);
-    int32_t *doff = (int32_t *)(b + sb + xb + pb + bfb + scb + mb);
-    uint8_t *per = b + sb + xb + pb + bfb + scb + mb + ob; // weight m: table at per + m (gb + yb), output after it
-    std::vector<int32_t> off32((size_t)n_groups + 1), map32(map ? (size_t)n_in : 0);
-    for (int64_t g = 0; g <= n_groups; g++) off32[(size_t)g] = (int32_t)offsets[g];
-    for (size_t p = 0; p < map32.size(); p++) map32[p] = (int32_t)map[p];
-    bool ok = ck(cudaMemcpy2DAsync(dsrc, (size_t)cols * 4, xq, (size_t)slot, (size_t)cols * 4, (size_t)n_src,
-                                   cudaMemcpyHostToDevice, c.st),
-                 "copy prepared rows") &&
-              ck(cudaMemcpyAsync(doff, off32.data(), off32.size() * 4, cudaMemcpyHostToDevice, c.st), "copy offsets");
-    if (ok && map) {
-        ok = ck(cudaMemcpyAsync(dmap, map32.data(), map32.size() * 4, cudaMemcpyHostToDevice, c.st), "copy map");
-        if (ok) trx_kapi_gather_k<<<(unsigned)n_in, 256, 0, c.st>>>(dsrc, dmap, (int)cols, dx);
-    }
-    for (int m = 0; ok && m < n_w; m++) {
-        const uint8_t **dg = (const uint8_t **)(per + m * (gb + yb));
-        float *dy = (float *)(per + m * (gb + yb) + gb);
-        ok = ck(cudaMemcpyAsync(dg, ptrs.data() + m * n_groups, (size_t)n_groups * 8, cudaMemcpyHostToDevice, c.st),
-                "copy table") &&
-             trx_kapi_grouped(TRX_Q4_K, rows, cols, dg, doff, (int)n_groups, (int)n_in, dx, dq, dbf, dsc, dy, c.st,
-                              m == 0) &&
-             ck(cudaGetLastError(), "grouped kernel") &&
-             ck(cudaMemcpyAsync(ys[m], dy, (size_t)(n_in * rows * 4), cudaMemcpyDeviceToHost, c.st), "copy y");
-    }
-    return ok && stream_wait(c.st);
-}
-
-} // namespace
-
-extern "C" void tr_matmul_grouped(tr_pool *pool, const tr_mat *w, const int64_t *offsets, int64_t n_groups,
-                                  const float *x, float *y) {
-    (void)pool;
-    g_err.clear();
-    if (!kgrouped(w, offsets, n_groups, x, y)) kfail("tr_matmul_grouped");
-}
-
-extern "C" void tr_matmul_grouped_s(tr_pool *pool, const tr_mat *w, const int64_t *offsets, int64_t n_groups,
-                                    const float *x, float *y, const void *s) {
-    (void)s;
-    tr_matmul_grouped(pool, w, offsets, n_groups, x, y);
-}
-
-extern "C" void tr_matmul(tr_pool *pool, const tr_mat *w, const float *x, int64_t n_tokens, float *y) {
-    const int64_t offsets[2] = {0, n_tokens};
-    tr_matmul_grouped(pool, w, offsets, 1, x, y);
-}
-
-extern "C" void tr_softmax(float *x, int64_t n) {
-    g_err.clear();
-    if (n <= 0) return;
-    KCtx &c = kctx();
-    std::lock_guard<std::mutex> lock(c.mu);
-    bool ok = kinit(c) && ck(cudaSetDevice(c.device), "cudaSetDevice") &&
-              kreserve(&c.buf, &c.buf_bytes, align_up(n * 4, 256));
-    if (ok) {
-        float *d = (float *)c.buf;
-        ok = ck(cudaMemcpyAsync(d, x, (size_t)n * 4, cudaMemcpyHostToDevice, c.st), "copy") &&
-             trx_kapi_softmax(d, n, c.st) && ck(cudaGetLastError(), "softmax kernel") &&
-             ck(cudaMemcpyAsync(x, d, (size_t)n * 4, cudaMemcpyDeviceToHost, c.st), "copy back") && stream_wait(c.st);
-    }
-    if (!ok) kfail("tr_softmax");
-}
-
-extern "C" void tr_swiglu(tr_pool *pool, float *x, const float *y, int64_t n) {
-    (void)pool;
-    g_err.clear();
-    if (n <= 0) return;
-    KCtx &c = kctx();
-    std::lock_guard<std::mutex> lock(c.mu);
-    bool ok = kinit(c) && ck(cudaSetDevice(c.device), "cudaSetDevice") &&
-              kreserve(&c.buf, &c.buf_bytes, 2 * align_up(n * 4, 256));
-    if (ok) {
-        float *dx = (float *)c.buf, *dy = (float *)(c.buf + align_up(n * 4, 256));
-        ok = ck(cudaMemcpyAsync(dx, x, (size_t)n * 4, cudaMemcpyHostToDevice, c.st), "copy x") &&
-             ck(cudaMemcpyAsync(dy, y, (size_t)n * 4, cudaMemcpyHostToDevice, c.st), "copy y") &&
-             trx_kapi_swiglu(dx, dy, n, c.st) && ck(cudaGetLastError(), "swiglu kernel") &&
-             ck(cudaMemcpyAsync(x, dx, (size_t)n * 4, cudaMemcpyDeviceToHost, c.st), "copy back") && stream_wait(c.st);
-    }
-    if (!ok) kfail("tr_swiglu");
-}
-
-extern "C" void tr_matmul_s(tr_pool *pool, const tr_mat *w, const float *x, int64_t n_tokens, float *y, const void *s) {
-    (void)pool;
-    (void)s;
-    g_err.clear();
-    const int64_t offsets[2] = {0, n_tokens};
-    if (!kgrouped(w, offsets, 1, x, y)) kfail("tr_matmul_s");
-}
-
-extern "C" size_t tr_q4x_bytes(int64_t n) { return (size_t)q4x_slot(n); }
-
-extern "C" int tr_q4x_road(tr_pool *pool, const tr_mat *w, const int64_t *offsets, int64_t n_groups, const void *s) {
-    (void)pool;
-    (void)offsets;
-    (void)n_groups;
-    (void)s;
-    return q4x_takes(w) ? 1 : 0;
-}
-
-extern "C" void tr_q4x_prepare(tr_pool *pool, const float *x, int64_t n, int64_t cols, void *xq) {
-    (void)pool;
-    if (n <= 0 || cols <= 0) return;
-    const int64_t slot = q4x_slot(cols);
-    for (int64_t r = 0; r < n; r++) memcpy((uint8_t *)xq + r * slot, x + r * cols, (size_t)cols * 4);
-}
-
-extern "C" int tr_matmul_q4x_prepared(tr_pool *pool, const tr_mat *w, const int64_t *offsets, int64_t n_groups,
-                                      const void *xq, const int64_t *map, float *y, const void *s) {
-    (void)pool;
-    (void)s;
-    g_err.clear();
-    if (n_groups <= 0 || offsets[n_groups] <= 0 || w[0].rows <= 0) return 1;
-    if (!q4x_takes(w)) return 0;
-    float *const ys[1] = {y};
-    if (!kprepared(&w, 1, offsets, n_groups, (const uint8_t *)xq, map, ys)) kfail("tr_matmul_q4x_prepared");
-    return 1;
-}
-
-extern "C" int tr_matmul_q4x_prepared_n(tr_pool *pool, const tr_mat *const *w, int n_w, const int64_t *offsets,
-                                        int64_t n_groups, const void *xq, const int64_t *map, float *const *y,
-                                        const void *s) {
-    if (n_w < 1 || n_w > TRMOE_Q4X_MATS) return 0;
-    if (n_w == 1) return tr_matmul_q4x_prepared(pool, w[0], offsets, n_groups, xq, map, y[0], s);
-    g_err.clear();
-    if (n_groups <= 0 || offsets[n_groups] <= 0 || w[0][0].rows <= 0) return 1;
-    for (int m = 0; m < n_w; m++)
-        if (!q4x_takes(w[m]) || w[m][0].rows != w[0][0].rows || w[m][0].cols != w[0][0].cols) return 0;
-    g_q4x_fused.fetch_add(1, std::memory_order_relaxed);
-    if (!kprepared(w, n_w, offsets, n_groups, (const uint8_t *)xq, map, y)) kfail("tr_matmul_q4x_prepared_n");
-    return 1;
-}
-
-extern "C" uint64_t tr_q4x_fused_calls(void) { return g_q4x_fused.load(std::memory_order_relaxed); }
-
-extern "C" void tr_swiglu_prepare(tr_pool *pool, float *x, const float *y, int64_t n_rows, int64_t n, void *xq) {
-    (void)pool;
-    g_err.clear();
-    if (n_rows <= 0 || n <= 0) return;
-    const int64_t total = n_rows * n, slot = q4x_slot(n);
-    KCtx &c = kctx();
-    std::lock_guard<std::mutex> lock(c.mu);
-    bool ok = kinit(c) && ck(cudaSetDevice(c.device), "cudaSetDevice") &&
-              kreserve(&c.buf, &c.buf_bytes, 2 * align_up(total * 4, 256));
-    if (ok) {
-        float *dx = (float *)c.buf, *dy = (float *)(c.buf + align_up(total * 4, 256));
-        ok = ck(cudaMemcpyAsync(dx, x, (size_t)total * 4, cudaMemcpyHostToDevice, c.st), "copy x") &&
-             ck(cudaMemcpyAsync(dy, y, (size_t)total * 4, cudaMemcpyHostToDevice, c.st), "copy y") &&
-             trx_kapi_swiglu(dx, dy, total, c.st) && ck(cudaGetLastError(), "swiglu kernel") &&
-             ck(cudaMemcpyAsync(x, dx, (size_t)total * 4, cudaMemcpyDeviceToHost, c.st), "copy back") &&
-             ck(cudaMemcpy2DAsync(xq, (size_t)slot, dx, (size_t)n * 4, (size_t)n * 4, (size_t)n_rows,
-                                  cudaMemcpyDeviceToHost, c.st),
-                "copy prepared rows") &&
-             stream_wait(c.st);
-    }
-    if (!ok) kfail("tr_swiglu_prepare");
-}
-
-extern "C" void trmoe_kernel_cache_clear(void) {
-    KCtx &c = kctx();
-    std::lock_guard<std::mutex> lock(c.mu);
-    for (auto &kv : c.mats) cudaFree(kv.second.dev);
-    c.mats.clear();
-}
-
-// ---------------------------------------------------------------------------------------------
-// tr_matmul_q4k_noalloc: the Q4_K kernel-level product on caller-owned device memory, allocating nothing
-
-// Its scratch, one per GPU that loads the library: bytes 0..7 the group table's one matrix pointer, 8..15 the
-// group offsets {0, n_tokens}, then from byte 256 the tokens' prepared rows (planes, sub-block sums, scales).
-// Host code never dereferences this name: on the host it only stands for the symbol, whose device address
-// cudaGetSymbolAddress gives.
-static __device__ __align__(256) uint8_t g_noalloc_scratch[TRMOE_NOALLOC_SCRATCH_BYTES];
-
-namespace {
-
-constexpr int kNoallocDevices = 64;
-std::mutex g_noalloc_mu;
-uint8_t *g_noalloc_ptr[kNoallocDevices]; // per device: the scratch's device address, found on its first call
-
-// the scratch's address on the current device `dev`, looked up once with that device current
-uint8_t *noalloc_scratch(int dev) {
-    std::lock_guard<std::mutex> lock(g_noalloc_mu);
-    if (g_noalloc_ptr[dev] == nullptr) {
-        void *p = nullptr;
-        if (!ck(cudaGetSymbolAddress(&p, g_noalloc_scratch), "cudaGetSymbolAddress")) return nullptr;
-        g_noalloc_ptr[dev] = static_cast<uint8_t *>(p);
-    }
-    return g_noalloc_ptr[dev];
-}
-
-// writes the scratch's group table: one group of n_tok rows multiplied by w
-__global__ void trx_noalloc_table(uint8_t *scratch, const uint8_t *w, int32_t n_tok) {
-    *reinterpret_cast<const uint8_t **>(scratch) = w;
-    reinterpret_cast<int32_t *>(scratch + 8)[0] = 0;
-    reinterpret_cast<int32_t *>(scratch + 8)[1] = n_tok;
-}
-
-} // namespace
-
-extern "C" int tr_matmul_q4k_noalloc(const void *d_w, int64_t rows, int64_t cols, const float *d_x, int64_t n_tokens,
-                                     float *d_y, void *stream) {
-    g_err.clear();
-    if (d_w == nullptr || d_x == nullptr || d_y == nullptr || rows < 1 || rows > (1 << 24) || cols < 256 ||
-        cols % 256 != 0 || cols > (1 << 20) || n_tokens < 1 || ((uintptr_t)d_w & 15u) != 0 || ((uintptr_t)d_x & 15u) != 0) {
-        set_err("tr_matmul_q4k_noalloc: bad arguments (rows %lld, cols %lld: a multiple of 256, n_tokens %lld, "
-                "d_w and d_x 16-byte aligned)",
-                (long long)rows, (long long)cols, (long long)n_tokens);
-        return -1;
-    }
-    // the scratch's parts, each rounded up to 256 bytes: table, planes, sub-block sums, scales
-    const int64_t pb = align_up(n_tokens * cols * 4, 256), bfb = align_up(n_tokens * (cols / 32) * 8, 256),
-                  scb = align_up(n_tokens * (cols / 256) * 8, 256), need = 256 + pb + bfb + scb;
-    if (need > (int64_t)TRMOE_NOALLOC_SCRATCH_BYTES) {
-        set_err("tr_matmul_q4k_noalloc: %lld tokens of %lld columns need %lld bytes of scratch, more than its %lld",
-                (long long)n_tokens, (long long)cols, (long long)need, (long long)TRMOE_NOALLOC_SCRATCH_BYTES);
-        return -1;
-    }
-    int dev = 0;
-    if (!ck(cudaGetDevice(&dev), "cudaGetDevice")) return -1;
-    if (dev < 0 || dev >= kNoallocDevices) {
-        set_err("tr_matmul_q4k_noalloc: device %d is beyond the %d it serves", dev, kNoallocDevices);
-        return -1;
-    }
-    uint8_t *scratch = noalloc_scratch(dev);
-    if (scratch == nullptr) return -1;
-    cudaStream_t st = (cudaStream_t)stream;
-    // nothing in the scratch has to start at zero: this call writes the table and every prepared row it reads
-    trx_noalloc_table<<<1, 1, 0, st>>>(scratch, static_cast<const uint8_t *>(d_w), (int32_t)n_tokens);
-    uint32_t *dq = reinterpret_cast<uint32_t *>(scratch + 256);
-    double *dbf = reinterpret_cast<double *>(scratch + 256 + pb);
-    double *dsc = reinterpret_cast<double *>(scratch + 256 + pb + bfb);
-    trx_kapi_grouped(TRX_Q4_K, rows, cols, reinterpret_cast<const uint8_t *const *>(scratch),
-                     reinterpret_cast<const int32_t *>(scratch + 8), 1, (int)n_tokens, d_x, dq, dbf, dsc, d_y, st);
-    return ck(cudaGetLastError(), "tr_matmul_q4k_noalloc launch") ? 0 : -1;
-}
+#include "capi_kernel_level.inc"
