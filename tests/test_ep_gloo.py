@@ -135,3 +135,50 @@ def test_expert_range_and_local_layer():
     lay = {"router": None, "gate": list(range(8)), "up": list(range(8)), "down": list(range(8))}
     loc = ep.local_layer(lay, 8, 1, 2)
     assert loc["gate"] == [None] * 4 + [4, 5, 6, 7]
+
+
+def _leaver(rank, world, port, out_dir):
+    """rank 1 leaves between two layer calls (an exception on the host, none of its collectives in flight); rank 0's
+    next exchange must end in an error within the process group's short timeout, not wait for good"""
+    import datetime
+
+    import torch.distributed as dist
+    from oracle.oracle import Oracle
+    os.environ["MASTER_ADDR"], os.environ["MASTER_PORT"] = "127.0.0.1", str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
+    oracle = Oracle()
+    lay = gb.make_layer(555, E, H, F, gb.Q8_0, gb.Q6_K, gb.F32, mode="random")
+    be = OracleEpBackend(oracle, lay, None, rank, world, gb.F32, gb.Q8_0, gb.Q6_K)
+    normed, x = _case(rank)
+    cap = (3 + 2 * (world - 1)) * K
+    ep.ep_layer(dist, be, 0, torch.from_numpy(normed), torch.from_numpy(x.copy()), cap=cap)
+    if rank == 1:
+        try:
+            raise RuntimeError("rank 1 fails between steps")
+        except RuntimeError:
+            os._exit(0)  # leaves without a word to the others
+    import time
+    t0 = time.monotonic()
+    try:
+        ep.ep_layer(dist, be, 0, torch.from_numpy(normed), torch.from_numpy(x.copy()), cap=cap)
+        result = "no error"
+    except Exception as exc:  # gloo: the peer's closed connection or the timeout
+        result = f"error after {time.monotonic() - t0:.1f} s: {type(exc).__name__}"
+    with open(os.path.join(out_dir, "rank0"), "w") as f:
+        f.write(result)
+    os._exit(0)  # (the group cannot be torn down collectively any more)
+
+
+def test_ep_rank_leaving_ends_in_an_error_not_a_hang(tmp_path):
+    import torch.multiprocessing as mp
+    import time
+    ctx = mp.spawn(_leaver, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=False)
+    t0 = time.monotonic()
+    while not ctx.join(timeout=5) and time.monotonic() - t0 < 120:  # (returns each time one rank ends)
+        pass
+    for p in ctx.processes:
+        if p.is_alive():
+            p.kill()
+    text = (tmp_path / "rank0").read_text()
+    assert text.startswith("error after"), text
+    assert float(text.split()[2]) < 60.0, text
