@@ -312,3 +312,18 @@ def test_attention_head_pinned(oracle, reflib, tier):
             assert same_bits(oracle.attention(q, keys, values, scale), want), n_pos
     finally:
         reflib.set_tier(None)
+
+
+@pytest.mark.parametrize("t", [gb.Q8_0, gb.Q4_K, gb.Q6_K])
+def test_block_formats_match_gguf_py(reflib, t):
+    """the GGUF block formats as the reference decodes them equal gguf-py's dequantisation bit for bit (Trochilus's
+    tools/check_dequant.py check), on random blocks with special scales (zero, subnormal, negative, large): the
+    weights every parity test feeds the GPU are read as the file format defines them"""
+    import gguf
+    from gguf import quants
+    rng = np.random.default_rng(40 + t)
+    for special in (False, True):
+        blk = gb.random_blocks(t, 6, 1024, rng, special=special)
+        ref = np.stack([reflib.dequant_row(t, blk[i], 1024) for i in range(6)])
+        want = quants.dequantize(blk, gguf.GGMLQuantizationType(t)).astype(np.float32)
+        assert same_bits(ref, want), (t, special)
