@@ -20,8 +20,9 @@
  * Conventions kept from gpu_attn.h: int results are 0 on success and -1 on failure; creation returns
  * NULL with a message in (err, err_len); one context, one thread at a time. There is no CPU fallback:
  * a failure is an error. The void kernel-level calls have no return code in the reference; on a
- * failure they print the reason to stderr, leave the output untouched and record the message that
- * trmoe_last_error() returns. */
+ * failure they print the reason to stderr, record the message that trmoe_last_error() returns and set
+ * every output float the call owns to a quiet NaN, so that nothing computed from it passes for a result.
+ * With TRMOE_ABORT_ON_ERROR=1 in the environment they abort() the process instead. */
 #ifndef TRMOE_H
 #define TRMOE_H
 
@@ -239,6 +240,11 @@ TRMOE_API int tr_gpu_moe_launches(const tr_gpu_moe *m, int64_t n_tok);
 /* The message of this thread's last failure ("" if none). */
 TRMOE_API const char *trmoe_last_error(void);
 
+/* The architecture the library's device code was built for, as the CUDA runtime reports it for the fused decode
+ * kernel on the current device (cudaFuncGetAttributes' binaryVersion: 100 for sm_100a), or -1 with
+ * trmoe_last_error() set when there is no device or the code cannot run on it. No counterpart in the reference. */
+TRMOE_API int trmoe_kernel_arch(void);
+
 /* ---------------------------------------------------------------------------------------------
  * Decode attention (the rank-3 next step beyond the MoE block): Trochilus's GPU attention backend
  * (src/backend/gpu_attn.h:29-78) on the B200, with the same names, arguments and conventions, so the engine links
@@ -331,7 +337,7 @@ TRMOE_API int tr_q4x_road(tr_pool *pool, const tr_mat *w, const int64_t *offsets
 TRMOE_API void tr_q4x_prepare(tr_pool *pool, const float *x, int64_t n, int64_t cols, void *xq);
 /* Replaces: tr_matmul_q4x_prepared (src/kernels/kernels.h:290-291): y[p*rows + r] = row r of w[g(p)] . the row in
  * slot map[p] of xq (map NULL: slot p). 1 when done (an empty call included); 0, y untouched, when tr_q4x_road
- * refuses w. A GPU failure prints `trmoe: tr_matmul_q4x_prepared failed: <reason>` and returns 1 (y unspecified). */
+ * refuses w. A GPU failure prints `trmoe: tr_matmul_q4x_prepared failed: <reason>`, fills y with NaN and returns 1. */
 TRMOE_API int tr_matmul_q4x_prepared(tr_pool *pool, const tr_mat *w, const int64_t *offsets, int64_t n_groups,
                                      const void *xq, const int64_t *map, float *y, const void *s);
 /* Replaces: tr_matmul_q4x_prepared_n (src/kernels/kernels.h:298-299): the same for n_w (1..TRMOE_Q4X_MATS) weights of
@@ -358,7 +364,9 @@ TRMOE_API void tr_swiglu_prepare(tr_pool *pool, float *x, const float *y, int64_
  * it plus, per token, cols * 4 + cols / 4 + cols / 32 bytes (each part rounded up to 256), so 2048 columns fit
  * 478 tokens; a larger call is rejected with an error. A successful call allocates nothing, host or device.
  * The first call on a device looks up the scratch's device address (cudaGetSymbolAddress) and keeps it: make
- * that first call before any stream capture. Every call shares the one scratch array and leaves its contents
+ * that first call before any stream capture. Under lazy module loading (CUDA_MODULE_LOADING=LAZY, the default of
+ * recent CUDA runtimes) that first call, or the first launch of a kernel, may also load the library's device code,
+ * which the driver may back with device memory of its own; the calls after it allocate nothing. Every call shares the one scratch array and leaves its contents
  * there: calls that may overlap on the GPU (different streams, or different host threads on one device) race,
  * and the caller must serialise them. Asynchronous on `stream` (NULL: the default stream); returns 0, or -1 with
  * trmoe_last_error() set. */

@@ -1,6 +1,6 @@
 """libtrmoe.so from C: tests/c/abi_test.c, compiled as strict C11 against include/trmoe.h together with a table of
 every declared function's address (so a declaration the library does not export fails to link), run without a GPU
-(the conventions: NULL contexts with messages, host-only answers). tests/zz_gpu_pending/test_gpu_c_abi.py runs the
+(the conventions: NULL contexts with messages, host-only answers). tests/test_gpu_c_abi.py runs the
 same program's GPU part."""
 import os
 import subprocess

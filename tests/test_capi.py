@@ -35,10 +35,40 @@ def test_library_builds_and_exports_every_declared_symbol():
         getattr(lib, n)
 
 
-def test_library_is_sm100a():
+def test_library_is_built_for_sm100a_only():
+    """the build names sm_100a alone (no PTX for a JIT to fall back on); on a device the runtime's own report of the
+    fused kernel's binary version is checked (test_gpu_layer.py::test_kernel_binary_is_sm100); without one the query
+    is an error with a message, not a crash"""
+    from trochilus_b200 import build, moe
+    assert build.ARCH == ["-gencode", "arch=compute_100a,code=sm_100a"]
+    assert moe.lib().trmoe_kernel_arch() == -1 and moe.last_error()
+
+
+def test_failed_void_calls_poison_their_outputs():
+    """the reference's kernel API is void, so a failure cannot be returned: every output float is set to NaN (a
+    refused type here, and with no device here every call fails at its first CUDA call) and TRMOE_ABORT_ON_ERROR=1
+    ends the process instead"""
+    import numpy as np
     from trochilus_b200 import moe
-    out = subprocess.check_output(["/usr/local/cuda/bin/cuobjdump", "--list-elf", moe.LIB_PATH], text=True)
-    assert "sm_100a" in out
+    L = moe.lib()
+    w = np.zeros((16, 34 * 16), dtype=np.uint8)
+    x = np.ones((3, 512), dtype=np.float32)
+    for typ in (99, moe.Q8_0):  # a type the library does not take; a good call that finds no device
+        y = np.zeros((3, 16), dtype=np.float32)
+        L.tr_matmul(None, C.byref(moe.TrMat(typ, 16, 512, w.ctypes.data)), x.ctypes.data, 3, y.ctypes.data)
+        assert np.isnan(y).all(), typ
+        assert moe.last_error()
+    v = np.ones(64, dtype=np.float32)
+    L.tr_softmax(v.ctypes.data, 64)
+    assert np.isnan(v).all()
+    v = np.ones(64, dtype=np.float32)
+    L.tr_swiglu(None, v.ctypes.data, np.ones(64, dtype=np.float32).ctypes.data, 64)
+    assert np.isnan(v).all()
+    code = ("import ctypes as C, numpy as np\nfrom trochilus_b200 import moe\n"
+            "v = np.ones(8, dtype=np.float32)\nmoe.lib().tr_softmax(v.ctypes.data, 8)\nprint('survived')\n")
+    r = subprocess.run([__import__("sys").executable, "-c", code], cwd=ROOT, capture_output=True, text=True,
+                       env={**os.environ, "TRMOE_ABORT_ON_ERROR": "1"})
+    assert r.returncode != 0 and "survived" not in r.stdout and "aborting" in r.stderr
 
 
 def test_bytes_and_config_checks_without_gpu():

@@ -3,17 +3,12 @@ src/backend/gpu_attn.h on the B200) bit for bit against the CPU oracle's tr_atte
 tier of the reference in test_oracle.py), as the reference's tests/test_gpu_attn.c checks its own backend: a
 prompt written into the cache, then decode tokens at contexts that cross the value kernel's 64-position stages,
 several layers and heads, a NaN and an infinity in the cache."""
-import os
-
 import numpy as np
 import pytest
 
 from tests.golden.cases import same_bits
 
-pytestmark = [pytest.mark.gpu,
-              pytest.mark.skipif(os.environ.get("TRX_ATTN_GPU_TEST") != "1",
-                                 reason="written without GPU time and not yet run on a B200; set TRX_ATTN_GPU_TEST=1 "
-                                        "to run it")]
+pytestmark = pytest.mark.gpu
 
 
 def test_decode_attention_matches_oracle(cuda, oracle):

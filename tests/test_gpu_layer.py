@@ -203,3 +203,9 @@ def test_host_call_on_pinned_x(cuda, oracle, gt, dt, rt):
     m.check()
     m.close()
 
+
+
+def test_kernel_binary_is_sm100(cuda):
+    """the runtime's own report for the fused decode kernel: native sm_100 code (binaryVersion 100), no JIT"""
+    from trochilus_b200 import moe
+    assert moe.lib().trmoe_kernel_arch() == 100, moe.last_error()

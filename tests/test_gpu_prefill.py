@@ -1,7 +1,11 @@
 """The tensor-core road for long passes (prefill.cuh: 3xTF32 tcgen05 GEMMs) against the exact definition: the routing
 (logits, top-k ids and weights, the dispatch permutation) bit for bit, the layer output within the north-star bound
-of 1e-5 relative error. The bound is normwise per token: max_d |got - want| <= 1e-5 * max_d |want| over the token's
-output row (a single element of a sum with cancellation has no meaningful relative error of its own)."""
+of 1e-5 relative error.
+
+The bound held is normwise per token: max_d |got - want| <= 1e-5 * max_d |want| over the token's output row. The
+element-wise figure max_d |got - want| / |want| is printed beside it, over the elements whose magnitude is at least
+1 % of their row's largest (an element of a sum with cancellation, near zero, has no meaningful relative error of its
+own: there the normwise bound is the one that says something)."""
 import numpy as np
 import pytest
 
@@ -42,13 +46,22 @@ def _rel_err(got, want):
     return num / den
 
 
+def _elem_err(got, want, floor=1e-2):
+    """element-wise max |got - want| / |want| over the elements with |want| >= floor * their row's max |want|"""
+    g, w = got.astype(np.float64), want.astype(np.float64)
+    big = np.abs(w) >= floor * np.max(np.abs(w), axis=1, keepdims=True)
+    big &= np.abs(w) > 0
+    return float(np.max(np.abs(g - w)[big] / np.abs(w)[big])) if big.any() else 0.0
+
+
 def _check(got, want, tag):
     for key in ("logits", "sel_id", "sel_w", "offsets", "place"):
         assert same_bits(got[key], want[key]), (tag, key)
     for key in ("ffn_out", "x"):
         assert np.all(np.isfinite(got[key])), (tag, key)
         err = _rel_err(got[key], want[key])
-        print(f"{tag} {key}: max normwise relative error {err.max():.3e} (bound {REL:.0e})")
+        print(f"{tag} {key}: max normwise relative error {err.max():.3e} (bound {REL:.0e}); "
+              f"element-wise {_elem_err(got[key], want[key]):.3e} (elements >= 1% of the row's max)")
         assert err.max() <= REL, (tag, key, float(err.max()), int(err.argmax()))
 
 
@@ -74,10 +87,11 @@ def test_prefill_small_shape_against_oracle(cuda, oracle):
     m.close()
 
 
-@pytest.mark.parametrize("T", [256, 1000])
+@pytest.mark.parametrize("T", [256, 1000, 2048])
 def test_prefill_olmoe_shape_against_exact_road(cuda, T):
     """OLMoE shape with Zipf-skewed routing (experts from one row to several 128-row tiles); the reference result is
-    the exact road on the GPU, itself bit for bit the oracle's (test_gpu_layer)."""
+    the exact road on the GPU, itself bit for bit the oracle's (test_gpu_layer). T = 2048 is the benched prefill
+    call (configs[2]'s layer: Q8_0 gate/up and down, BF16 router)."""
     from trochilus_b200.moe import GpuMoe
     E, k, H, F = 64, 8, 2048, 1024
     lay = gb.make_layer(77 + T, E, H, F, gb.Q8_0, gb.Q8_0, gb.BF16, mode="random")

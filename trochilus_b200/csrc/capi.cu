@@ -351,6 +351,15 @@ static bool plan_kernels(tr_gpu_moe *m) {
 
 extern "C" const char *trmoe_last_error(void) { return g_err.c_str(); }
 
+extern "C" int trmoe_kernel_arch(void) {
+    g_err.clear();
+    int dev = 0;
+    if (!ck(cudaGetDevice(&dev), "cudaGetDevice")) return -1;
+    cudaFuncAttributes a{};
+    if (!ck(cudaFuncGetAttributes(&a, trx_k_layer<TRX_Q4_K, TRX_Q6_K>), "cudaFuncGetAttributes")) return -1;
+    return a.binaryVersion;
+}
+
 extern "C" uint64_t tr_gpu_moe_bytes(const tr_gpu_moe_config *cfg) {
     if (cfg == nullptr) return 0;
     return (uint64_t)(layer_bytes(*cfg) * cfg->n_layers + work_layout(*cfg).total);

@@ -33,7 +33,8 @@ EXPORTS = ["tr_gpu_moe_create", "tr_gpu_moe_free", "tr_gpu_moe_bytes", "tr_gpu_m
            "tr_matmul_s", "tr_q4x_bytes", "tr_q4x_road", "tr_q4x_prepare", "tr_matmul_q4x_prepared",
            "tr_matmul_q4x_prepared_n", "tr_q4x_fused_calls", "tr_swiglu_prepare", "tr_gpu_moe_config_from_gguf",
            "tr_gpu_moe_load_gguf", "tr_gpu_open", "tr_gpu_close", "tr_gpu_name", "tr_gpu_attn_create",
-           "tr_gpu_attn_free", "tr_gpu_attn_bytes", "tr_gpu_attn_write", "tr_gpu_attn_decode", "tr_gpu_attn_warm"]
+           "tr_gpu_attn_free", "tr_gpu_attn_bytes", "tr_gpu_attn_write", "tr_gpu_attn_decode", "tr_gpu_attn_warm",
+           "trmoe_kernel_arch"]
 
 
 class Config(C.Structure):
