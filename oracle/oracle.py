@@ -21,9 +21,13 @@ REF_SO = os.path.join(HERE, "_ref", "libtrref_moe.so")
 F32, F16, Q8_0, Q4_K, Q6_K, BF16 = 0, 1, 8, 12, 14, 30
 
 
-def build():
-    """make -C oracle (the restatement always; the reference harness when the reference tree exists)."""
-    subprocess.check_call(["make", "-s", "-C", HERE, "all"])
+def build(ref_tree: str | None = None):
+    """make -C oracle: the restatement always; with ref_tree (the reference's source tree, when it exists) also the
+    reference's kernels with the harness and its whole engine, plain and relinked onto libtrmoe.so."""
+    args = ["make", "-s", "-C", HERE, "all"]
+    if ref_tree and os.path.exists(os.path.join(ref_tree, "src", "kernels", "kernels.c")):
+        args.append(f"REF={ref_tree}")
+    subprocess.check_call(args)
 
 
 class Desc(C.Structure):
