@@ -32,6 +32,29 @@ __device__ __forceinline__ void trx_bulk_g2s(void *dst, const void *src, uint32_
                  : "memory");
 }
 
+// An L2 policy for data a call reads once (the expert weights): its lines are the first the L2 evicts, so the
+// stream of a layer's weights does not push out what every call reuses (the kernels' code, the routing arrays, the
+// activations, the routers).
+__device__ __forceinline__ uint64_t trx_policy_evict_first() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+
+// trx_bulk_g2s with an L2 cache policy (trx_policy_evict_first)
+__device__ __forceinline__ void trx_bulk_g2s_hint(void *dst, const void *src, uint32_t bytes, uint64_t *bar,
+                                                  uint64_t policy) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], "
+                 "%4;" ::"r"(trx_smem(dst)),
+                 "l"(src), "r"(bytes), "r"(trx_smem(bar)), "l"(policy)
+                 : "memory");
+}
+
+// Bring [src, src + bytes) into L2 without waiting for it (src and bytes multiples of 16)
+__device__ __forceinline__ void trx_bulk_prefetch_l2(const void *src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 __device__ __forceinline__ bool trx_mbar_try_wait(uint64_t *bar, uint32_t parity) {
     uint32_t ok;
     asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
@@ -40,6 +63,11 @@ __device__ __forceinline__ bool trx_mbar_try_wait(uint64_t *bar, uint32_t parity
                  : "memory");
     return ok != 0;
 }
+
+// Programmatic dependent launch: let the next kernel of the stream be scheduled (it still waits for this grid's end
+// in its own trx_griddep_wait), and wait for the previous kernel's end and memory (a no-op without one)
+__device__ __forceinline__ void trx_griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void trx_griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 __device__ __forceinline__ uint64_t trx_globaltimer() {
     uint64_t t;

@@ -26,6 +26,7 @@
 #include "moe_kernels.cuh"
 #include "kernel_api.cuh"
 #include "fused_layer.cuh"
+#include "decode.cuh"
 #include "gguf_file.h"
 #include "attention.cuh"
 #include "prefill.cuh"
@@ -99,7 +100,7 @@ bool upload_matrix(int type, int64_t rows, int64_t cols, const void *host, uint8
 }
 
 struct WorkLayout {
-    int64_t off[26];
+    int64_t off[28];
     int64_t total;
 };
 
@@ -137,10 +138,12 @@ WorkLayout work_layout(const tr_gpu_moe_config &c) {
         (int64_t)sizeof(TrxSync), // 23 the fused kernel's counters
         pf ? R * H * 4 : 0, // 24 the tensor-core road: the grouped inputs' hi plane
         pf ? R * H * 4 : 0, // 25 and lo plane
+        TRX_DC_GRID_MAX * E * 8, // 26 the one-token kernel's tagged logits (a row for each CTA)
+        TRX_DC_KMAX * F * 8, // 27 and its tagged h values
     };
     WorkLayout w{};
     int64_t o = 0;
-    for (int i = 0; i < 26; i++) {
+    for (int i = 0; i < 28; i++) {
         w.off[i] = o;
         o += align_up(sizes[i], 256);
     }
@@ -180,6 +183,9 @@ struct tr_gpu_moe {
     std::vector<float> norm_eps;
     std::vector<int> norm_set;
     bool fused_ok = false;
+    bool dec1_ok = false;  // the one-token decode kernel (decode.cuh) fits and may be launched
+    bool dec1_pdl = true;  // and is launched with programmatic dependent launch (off if the driver refuses it)
+    int64_t tag_bytes = 0; // its tagged exchange words (work regions 26 and 27), cleared with the counters
     float *d_normed = nullptr, *d_x = nullptr;
     int64_t *d_sel_id = nullptr;
     float *d_sel_w = nullptr;
@@ -290,6 +296,24 @@ static bool plan_fused(tr_gpu_moe *m) {
         return false;
     m->grid_fused = m->sm_count; // one CTA per SM (occupancy is at least one: checked)
     m->fused_ok = occ >= 1;
+    // the one-token kernel: its plan's shared memory, a CTA an SM
+    if (m->fused_ok && trx_dec1_takes(c.gate_type, c.down_type, c.router_type, (int)c.n_embd, (int)c.n_ff,
+                                      (int)c.n_expert, (int)c.n_used, 1, m->grid_fused, false)) {
+        const TrxDecPlan P = trx_dec_plan((int)c.n_embd, (int)c.n_ff, (int)c.n_used, m->grid_fused);
+        bool ok1 = true;
+        for (auto fn : {trx_k_dec1<TRX_F32>, trx_k_dec1<TRX_BF16>}) {
+            int occ1 = 0;
+            cudaFuncAttributes fa1{};
+            if (!ck(cudaFuncGetAttributes(&fa1, fn), "cudaFuncGetAttributes") ||
+                fa1.sharedSizeBytes + P.total + 1024 > limit ||
+                !ck(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)P.total), "smem dec1") ||
+                !ck(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ1, fn, TRX_DC_THREADS, P.total), "occupancy"))
+                ok1 = false;
+            else ok1 = ok1 && occ1 >= 1;
+        }
+        g_err.clear();
+        m->dec1_ok = ok1;
+    }
     return true;
 }
 
@@ -517,6 +541,9 @@ extern "C" tr_gpu_moe *tr_gpu_moe_create(const tr_gpu_moe_config *cfg, int devic
     m->d_sel_id = (int64_t *)(b + wl.off[21]);
     m->d_sel_w = (float *)(b + wl.off[22]);
     m->sync = (TrxSync *)(b + wl.off[23]);
+    w.tag_logits = (unsigned long long *)(b + wl.off[26]);
+    w.tag_h = (unsigned long long *)(b + wl.off[27]);
+    m->tag_bytes = wl.off[27] + align_up(TRX_DC_KMAX * cfg->n_ff * 8, 256) - wl.off[26];
     if (prefill_capable(*cfg)) {
         m->pf_xhi = (float *)(b + wl.off[24]);
         m->pf_xlo = (float *)(b + wl.off[25]);
@@ -683,6 +710,8 @@ static void reset_counters(tr_gpu_moe *m, cudaStream_t st) {
     cudaMemsetAsync(m->work.route_cnt, 0, 4, st);
     cudaMemsetAsync(m->work.comb_cnt, 0, (size_t)(m->cfg.n_embd / TRX_DN_CHUNK) * 4, st);
     cudaMemsetAsync(m->sync, 0, sizeof(TrxSync), st);
+    // the one-token kernel's tagged words: a word a failed call left could carry the next call's tag
+    if (m->tag_bytes > 0) cudaMemsetAsync(m->work.tag_logits, 0, (size_t)m->tag_bytes, st);
     m->epoch = 0;
     stream_wait(st);
 }
@@ -793,6 +822,35 @@ static int launch_fused(tr_gpu_moe *m, const TrxLayer &L, const TrxShape &S, con
                : -1;
 }
 
+// the one-token decode kernel (decode.cuh): one cooperative launch, a CTA an SM
+static int launch_dec1(tr_gpu_moe *m, const TrxLayer &L, const TrxShape &S, const float *normed, const TrxWork &w,
+                       float *x_io, float *ffn_out, uint32_t epoch, cudaStream_t st) {
+    const TrxDecPlan P = trx_dec_plan(S.H, S.F, S.k, m->grid_fused);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)m->grid_fused);
+    cfg.blockDim = dim3(TRX_DC_THREADS);
+    cfg.dynamicSmemBytes = P.total;
+    cfg.stream = st;
+    // cooperative (every CTA resident at once: they wait on one another) and, where the driver takes both,
+    // programmatic dependent launch (the kernel's set-up overlaps the previous kernel's tail)
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = m->dec1_pdl ? 2 : 1;
+    auto fn = L.router_type == TRX_BF16 ? trx_k_dec1<TRX_BF16> : trx_k_dec1<TRX_F32>;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, fn, L, S, normed, w, m->sync, x_io, ffn_out, epoch, P);
+    if (e != cudaSuccess && m->dec1_pdl) { // not taken together: cooperative alone from now on
+        (void)cudaGetLastError();
+        m->dec1_pdl = false;
+        cfg.numAttrs = 1;
+        e = cudaLaunchKernelEx(&cfg, fn, L, S, normed, w, m->sync, x_io, ffn_out, epoch, P);
+    }
+    return ck(e, "decode layer launch") ? 0 : -1;
+}
+
 static int launch_ffn_norm(tr_gpu_moe *m, int64_t layer, const float *x, int64_t n_tok, float *normed, cudaStream_t st);
 
 // done: when the fused kernel takes the call, the device address of the word it writes its epoch to when every
@@ -854,12 +912,15 @@ static int launch_layer(tr_gpu_moe *m, int64_t layer, const float *d_normed, int
     int sg = 0, sd = 0;
     const bool fused = first == 0 && last == 3 && !(m->pf_ok && m->pf_min > 0 && T >= m->pf_min) && m->fused_ok &&
                        T <= TRX_ROUTE_FUSED_MAX && E + T <= m->grid_fused && !es && fused_stages(m, T, &sg, &sd);
+    // one token on the one-token kernel's shapes: decode.cuh
+    const bool dec1 = fused && m->dec1_ok && !S.ext &&
+                      trx_dec1_takes(c.gate_type, c.down_type, c.router_type, S.H, S.F, S.E, S.k, T, m->grid_fused, false);
     if (norm_src) {
         // short fused calls normalise inside the kernel when the rows fit the stage area beside the router's staging
-        const bool inside =
-            fused && T <= TRX_FU_LOCAL_PREP && ((uintptr_t)norm_src & 15) == 0 &&
-            trx_fu_norm_off(T, S.H, E) + (size_t)T * S.H * 4 <=
-                trx_fused_layout(c.gate_type, c.down_type, S.H, S.F, T, S.k, sg, sd, E, m->grid_fused).bars;
+        const bool inside = (dec1 && ((uintptr_t)norm_src & 15) == 0) ||
+                            (fused && T <= TRX_FU_LOCAL_PREP && ((uintptr_t)norm_src & 15) == 0 &&
+                             trx_fu_norm_off(T, S.H, E) + (size_t)T * S.H * 4 <=
+                                 trx_fused_layout(c.gate_type, c.down_type, S.H, S.F, T, S.k, sg, sd, E, m->grid_fused).bars);
         if (inside) {
             S.norm_in = 1;
             d_normed = norm_src;
@@ -878,6 +939,8 @@ static int launch_layer(tr_gpu_moe *m, int64_t layer, const float *d_normed, int
         if (epoch == 0) epoch = ++m->epoch & 0x7fffffffu; // 0 is the completion word's initial value
         w.host_done = done;
         if (epoch_out) *epoch_out = epoch;
+        if (dec1 && (!S.norm_in || ((uintptr_t)d_normed & 15) == 0))
+            return launch_dec1(m, L, S, d_normed, w, d_x, ffn, epoch, st);
         return launch_fused(m, L, S, d_normed, T, w, d_x, ffn, epoch, sg, sd, st, "fused layer launch");
     }
     mark(0);

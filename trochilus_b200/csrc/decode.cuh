@@ -1,0 +1,489 @@
+// decode.cuh: a one-token MoE layer call, the decode road's common case, as one compact persistent kernel.
+//
+// The same arithmetic as the general fused kernel (fused_layer.cuh), the same routing code and row dots, laid out
+// for one token so that its code stays small and no warp waits on another warp's stages.
+//
+// Exchange between CTAs without fences or counters: every word one CTA publishes for the others (a logit, an h
+// value) is a 64-bit store of the value and the call's tag (TrxSync::seq + 1) together, which a reader sees whole or
+// not at all; a reader polls until the words it needs carry this call's tag. CTA 0 advances seq as it ends: it can
+// end only after it holds h values from every CTA, each stored with a tag derived from that CTA's read of seq, so
+// every CTA has read seq by then. (A device-scope fence after a store measured about 1200 cycles on the B200, and a
+// fence and a counter at the end of every CTA about 1.3 us a call.) A logit is pushed to every CTA's own row of E
+// words, so that each CTA polls lines no other CTA polls: 148 CTAs polling the same 64 words took 3.3 us.
+//
+// Launched with programmatic dependent launch: the barriers, the expf table and the router row (static weights) are
+// set up before trx_griddep_wait, under the previous kernel's tail.
+//
+//  prologue  a helper warp initialises the barriers; in CTAs 0..E-1 warp 0 loads router row e into registers at
+//            once, warps 0-3 stage the token's row in shared memory meanwhile (or, with the ffn_norm in the hook,
+//            every CTA normalises the residual row there first), warp 0 forms logit e (the 16-lane contract) and
+//            publishes it tagged; warps 4-11 prepare the row for Q4_K's integer definition (all CTAs).
+//  routing   every CTA, once it holds all E tagged logits, routes the token (softmax, top-k, ids sorted) and its
+//            trivial sort in shared memory.
+//  experts   a CTA owns rows [ga, gb) of every selected expert's gate and up matrices and rows [da, db) of every
+//            selected expert's down matrix. Each of 14 consumer warps streams its own units through a ring of
+//            TRX_DC_NS shared-memory slots with 1-D TMA bulk copies (no multicast), one mbarrier a slot, so it waits
+//            only for its own bytes: four gate/up units (one row of gate and the same row of up), then two down
+//            steps (a half-warp the same row of two experts, trx_q6l_dot_pair_il). A unit's two row values go to
+//            warp 14, which forms h = silu(g) u for a whole step's units at once (lane l: unit l) and publishes them
+//            tagged, so that the exponential's latency is paid once a step, off the consumers' path. The down weights
+//            do not depend on h, so they load while the gate/up rows are multiplied; a step's h rows come from the
+//            helper warp, which gathers expert i's tagged h values into shared memory, experts in order, the rows of
+//            experts 2q and 2q + 1 interleaved (the pairs the down step multiplies together).
+//  mix       each CTA adds, for its rows [da, db), the k expert outputs in increasing expert id and the sum to the
+//            residual (Trochilus's mix_body); CTA 0 advances seq (the host-pointer road: the last CTA, which also
+//            posts the host word).
+//
+// Limits (checked on the host, trx_dec1_takes): one token, no external routing, gate/up Q4_K of 2048 columns, down
+// Q6_K of 256, 512 or 1024 columns, k even and at most 8, and a grid whose shares fit the ring (at most 7 gate/up rows
+// and 14 down rows of an expert a CTA for k = 8). Every wait is bounded; a warp that gives up sets the error flag,
+// waits (bounded) for its own copies in flight and leaves.
+//
+// Trochilus references: forward_layer's MoE block src/models/olmoe.c:1845-1933 (route_token :1455-1502, the
+// counting sort :1850-1861, expert_stages :1642-1689, mix_body :1432-1446); tr_rmsnorm src/kernels/kernels.c:1351-1360.
+#pragma once
+#include <cstdint>
+#include "fused_layer.cuh"
+
+#define TRX_DC_CWARPS 14  // consumer warps
+#define TRX_DC_SILU 14    // the warp that forms h = silu(g) u for the consumers' gate/up units
+#define TRX_DC_HELPER 15  // the helper warp (barriers, h gathering)
+#define TRX_DC_THREADS 512
+#define TRX_DC_NS 3       // slots a consumer warp has in flight
+#define TRX_DC_SLOT 3456  // bytes a slot: a gate/up unit (2 x 1152) or a down step (2 x (2 x 832 + 2 x 16))
+#define TRX_DC_GU 4       // gate/up units a warp
+#define TRX_DC_DN 2       // down steps a warp
+#define TRX_DC_KMAX 8
+#define TRX_DC_GRID_MAX 256 // CTAs (the tagged logits: a row of E words for each)
+
+struct TrxDecPlan {
+    uint32_t off_h, off_xq, total; // shared memory: h rows (k x F floats), the prepared token row, the whole
+    int ng_max, nd_max;            // the most gate/up and down rows of an expert a CTA takes
+};
+
+__host__ __device__ inline uint32_t trx_dc_align(uint32_t v) { return (v + 127u) / 128u * 128u; }
+
+__host__ inline TrxDecPlan trx_dec_plan(int H, int F, int k, int grid) {
+    TrxDecPlan P{};
+    P.off_h = trx_dc_align(TRX_DC_CWARPS * TRX_DC_NS * TRX_DC_SLOT);
+    P.off_xq = trx_dc_align(P.off_h + (uint32_t)(k * F * 4 > H * 4 ? k * F * 4 : H * 4));
+    P.total = trx_dc_align(P.off_xq + (uint32_t)(H * 4 + (H / 32) * 8 + (H / 256) * 8));
+    P.ng_max = (F + grid - 1) / grid;
+    P.nd_max = ((H / 2 + grid - 1) / grid) * 2;
+    return P;
+}
+
+// whether a call takes trx_k_dec1 (the host's part of the limits above)
+__host__ inline bool trx_dec1_takes(int gate_type, int down_type, int router_type, int H, int F, int E, int k, int T,
+                                    int grid, bool ext) {
+    if (T != 1 || ext || gate_type != TRX_Q4_K || down_type != TRX_Q6_K) return false;
+    if (router_type != TRX_F32 && router_type != TRX_BF16) return false;
+    // (1, 2 or 4 blocks a down row: a row's d values never straddle a 16-byte piece)
+    if (H != 2048 || (F != 256 && F != 512 && F != 1024) || E > TRX_MAX_EXPERTS || k < 2 || k % 2 || k > TRX_DC_KMAX)
+        return false;
+    const TrxDecPlan P = trx_dec_plan(H, F, k, grid);
+    return k * P.ng_max <= TRX_DC_CWARPS * TRX_DC_GU && (k / 2) * P.nd_max <= 2 * TRX_DC_CWARPS * TRX_DC_DN &&
+           P.nd_max <= 16 && P.ng_max <= 32 && grid <= TRX_DC_GRID_MAX && F >= grid;
+}
+
+// a value and its tag in one 64-bit word (relaxed, device scope; an aligned 64-bit access is never torn)
+__device__ __forceinline__ void trx_st_tagged(unsigned long long *p, uint32_t tag, float v) {
+    const unsigned long long x = ((unsigned long long)tag << 32) | __float_as_uint(v);
+    asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(x) : "memory");
+}
+__device__ __forceinline__ unsigned long long trx_ld_tagged(const unsigned long long *p) {
+    unsigned long long x;
+    asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(x) : "l"(p) : "memory");
+    return x;
+}
+__device__ __forceinline__ ulonglong2 trx_ld_tagged2(const unsigned long long *p) {
+    ulonglong2 x;
+    asm volatile("ld.relaxed.gpu.global.v2.b64 {%0, %1}, [%2];" : "=l"(x.x), "=l"(x.y) : "l"(p) : "memory");
+    return x;
+}
+
+template <int RT>
+__global__ void __launch_bounds__(TRX_DC_THREADS, 1)
+    trx_k_dec1(TrxLayer L, TrxShape S, const float *__restrict__ normed, TrxWork w, TrxSync *sync,
+               float *__restrict__ x_io, float *__restrict__ ffn_out, uint32_t epoch, const TrxDecPlan P) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ __align__(8) uint64_t s_full[TRX_DC_CWARPS][TRX_DC_NS];
+    __shared__ __align__(8) uint64_t s_hbar[TRX_DC_KMAX];
+    __shared__ __align__(8) uint64_t s_gubar[TRX_DC_GU];          // step j's gate/up values are in s_gu
+    __shared__ __align__(8) float2 s_gu[TRX_DC_GU * TRX_DC_CWARPS]; // unit u's (gate, up) row values
+    __shared__ __align__(16) float sp[96];
+    __shared__ __align__(16) float s_q6sc[2 * TRX_DC_CWARPS][32 * TRX_Q6L_SS_BLOCKS];
+    __shared__ __align__(16) float s_h3[TRX_DC_KMAX][16];
+    __shared__ float s_logit[TRX_MAX_EXPERTS], s_selw[TRX_DC_KMAX], s_inv;
+    __shared__ int32_t s_selid[TRX_DC_KMAX], s_off[TRX_MAX_EXPERTS + 1], s_act[TRX_MAX_EXPERTS], s_nact;
+    __shared__ int32_t s_place[TRX_DC_KMAX], s_xmap[TRX_DC_KMAX];
+    __shared__ int s_flag;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int E = S.E, H = S.H, F = S.F, k = S.k, nsb = F / 256, G = gridDim.x, c = blockIdx.x;
+    TRX_TRACE(0);
+    trx_griddep_launch();
+    float *hbuf = reinterpret_cast<float *>(smem + P.off_h); // h rows; before the routing, the token's row
+    uint32_t *xq = reinterpret_cast<uint32_t *>(smem + P.off_xq);
+    double *xbf = reinterpret_cast<double *>(smem + P.off_xq + H * 4), *xsc = xbf + H / 32;
+    // this CTA's rows: [ga, ga + ng) of every gate/up matrix, [da, da + nd) of every down matrix (whole row pairs)
+    const int ga = F * c / G, ng = F * (c + 1) / G - ga;
+    const int da = (H / 2) * c / G * 2, nd = (H / 2) * (c + 1) / G * 2 - da;
+    if (warp == TRX_DC_HELPER && lane == 0) {
+        for (int i = 0; i < TRX_DC_CWARPS * TRX_DC_NS; i++) trx_mbar_init(&s_full[0][0] + i, 1);
+        for (int i = 0; i < k; i++) trx_mbar_init(&s_hbar[i], 32); // every helper lane arrives
+        for (int j = 0; j < TRX_DC_GU; j++) { // a consumer with a unit in step j arrives
+            const int n = k * ng - TRX_DC_CWARPS * j;
+            trx_mbar_init(&s_gubar[j], (uint32_t)(n < 0 ? 0 : n > TRX_DC_CWARPS ? TRX_DC_CWARPS : n) + (n <= 0));
+        }
+        trx_fence_barrier_init();
+    }
+    if (warp == 1) trx_expf_prefetch(lane);
+
+    // ---------------- prologue
+    const bool router = c < E;
+    constexpr int EB = RT == TRX_BF16 ? 2 : 4;
+    constexpr int GB = RT == TRX_BF16 ? 8 : 4; // router blocks a group: 16 loads of 16 bytes a lane in flight
+    uint4 rr[16];
+    const uint8_t *rrow = L.router + (int64_t)c * H * EB;
+    const int l16 = lane & 15;
+    if (router && warp == 0) { // the row's first group straight into registers, in flight while the input is staged
+#pragma unroll
+        for (int j = 0; j < 16; j++)
+            rr[j] = __ldg(reinterpret_cast<const uint4 *>(rrow + ((size_t)256 * (j / (16 / GB)) + 16 * l16) * EB) + j % (16 / GB));
+    }
+    trx_griddep_wait(); // what the previous kernels wrote (the input row, x, seq) from here on
+    const uint32_t tag = __ldcg(&sync->seq) + 1u; // this call's tag (never 0: a cleared word never matches)
+    // residual values of this CTA's output rows, read now (from host memory on the host-pointer road)
+    float xres = 0.0f;
+    if (tid < nd) xres = x_io[da + tid];
+    const float *xrow = normed; // the token's (normalised) row for the preparation: global, or hbuf
+    if (S.norm_in) {
+        // the ffn_norm: the residual row into hbuf, the 16-lane sum of squares, inv = 1 / sqrtf(sumsq / H + eps),
+        // then normed = (x inv) w (Trochilus's tr_rmsnorm)
+        for (int i = tid; i < H / 4; i += TRX_DC_THREADS)
+            *reinterpret_cast<float4 *>(hbuf + 4 * i) = __ldcg(reinterpret_cast<const float4 *>(normed) + i);
+        __syncthreads();
+        if (warp == 0) {
+            float acc = 0.0f;
+            if (lane < 16)
+                for (int kk = lane; kk < H; kk += 16) acc = __fadd_rn(acc, __fmul_rn(hbuf[kk], hbuf[kk]));
+            acc = trx_lane_tree16(acc);
+            if (lane == 0) s_inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(acc, (float)H), L.norm_eps)));
+        }
+        __syncthreads();
+        const float inv = s_inv;
+        for (int i = tid; i < H; i += TRX_DC_THREADS) hbuf[i] = __fmul_rn(__fmul_rn(hbuf[i], inv), __ldg(L.norm_w + i));
+        __syncthreads();
+        if (c == 0 && w.out_normed)
+            for (int i = tid; i < H; i += TRX_DC_THREADS) w.out_normed[i] = hbuf[i];
+        xrow = hbuf;
+    } else if (router && warp < 4) {
+        for (int i = tid; i < H / 4; i += 128)
+            *reinterpret_cast<float4 *>(hbuf + 4 * i) = __ldg(reinterpret_cast<const float4 *>(normed) + i);
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+    }
+    if (router && warp == 0) {
+        // logit c: lane l adds fl(w x) for k = l + 16 m in increasing k from +0, then the tree (src/kernels/kernels.c:
+        // 73-75, 101-109); both half-warps run the same row (the tree needs the whole warp)
+        float acc = 0.0f;
+        for (int i0 = 0; i0 < H / 256; i0 += GB) {
+            if (i0 > 0) {
+#pragma unroll
+                for (int j = 0; j < 16; j++)
+                    rr[j] = __ldg(reinterpret_cast<const uint4 *>(rrow + ((size_t)256 * (i0 + j / (16 / GB)) + 16 * l16) * EB) +
+                                  j % (16 / GB));
+            }
+#pragma unroll
+            for (int g = 0; g < GB; g++) {
+                float wv[16];
+#pragma unroll
+                for (int q = 0; q < 16 / GB; q++) {
+                    const uint4 v = rr[g * (16 / GB) + q];
+                    const uint32_t ws[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                    for (int cc = 0; cc < 4; cc++) {
+                        if (RT == TRX_BF16) {
+                            wv[8 * q + 2 * cc] = __uint_as_float(ws[cc] << 16);
+                            wv[8 * q + 2 * cc + 1] = __uint_as_float(ws[cc] & 0xffff0000u);
+                        } else {
+                            wv[4 * q + cc] = __uint_as_float(ws[cc]);
+                        }
+                    }
+                }
+                const float *xb = hbuf + 256 * (i0 + g) + l16; // (staged, or normalised, in hbuf)
+#pragma unroll
+                for (int m = 0; m < 16; m++) acc = __fadd_rn(acc, __fmul_rn(wv[m], xb[16 * m]));
+            }
+        }
+        acc = trx_lane_tree16(acc); // (in every lane: both half-warps ran the row)
+        const float v = L.router_bias ? __fadd_rn(acc, L.router_bias[c]) : acc;
+        for (int j = lane; j < G; j += 32) trx_st_tagged(w.tag_logits + (int64_t)j * E + c, tag, v); // every CTA's row
+        if (lane == 0 && w.out_logits) w.out_logits[c] = v;
+        TRX_TRACE(62);
+    }
+    // the token's row prepared for Q4_K's integer definition: warp 4 + s takes 256-block s
+    if (warp >= 4 && warp < 4 + H / 256)
+        trx_prep_q4x_block(xrow + 256 * (warp - 4), xq, warp - 4, H / 256, xbf + 8 * (warp - 4), xsc + (warp - 4), lane);
+
+    // ---------------- routing: once it holds every tagged logit, every CTA routes the token itself
+    if (warp == 0) {
+        bool got0 = lane >= E, got1 = lane + 32 >= E, ok = true;
+        uint64_t t0 = 0;
+        for (;;) {
+            if (!got0) {
+                const unsigned long long x = trx_ld_tagged(w.tag_logits + (int64_t)c * E + lane);
+                if ((uint32_t)(x >> 32) == tag) {
+                    s_logit[lane] = __uint_as_float((uint32_t)x);
+                    got0 = true;
+                }
+            }
+            if (!got1) {
+                const unsigned long long x = trx_ld_tagged(w.tag_logits + (int64_t)c * E + lane + 32);
+                if ((uint32_t)(x >> 32) == tag) {
+                    s_logit[lane + 32] = __uint_as_float((uint32_t)x);
+                    got1 = true;
+                }
+            }
+            if (__all_sync(0xffffffffu, got0 && got1)) break;
+            const uint64_t now = trx_globaltimer();
+            if (t0 == 0) t0 = now;
+            else if (now - t0 > TRX_SPIN_NS) {
+                ok = false;
+                break;
+            }
+            __nanosleep(20);
+        }
+        const bool all_ok = __all_sync(0xffffffffu, ok);
+        if (lane == 0) s_flag = all_ok ? 1 : 0;
+    }
+    __syncthreads();
+    if (!s_flag) {
+        if (tid == 0) {
+            atomicExch(w.err, 2);
+            if (w.host_done) trx_post_done(w.host_done, epoch | 0x80000000u);
+        }
+        return;
+    }
+    TRX_TRACE(1);
+    if (warp == 0) {
+        trx_route_token<true>(s_logit, E, k, S.norm_topk, lane, sp, s_selid, s_selw);
+        __syncwarp();
+        const bool out = c == 0;
+        trx_sort_single(s_selid, E, k,
+                        TrxSortOut{s_off, s_act, &s_nact, s_place, s_xmap, out ? w.out_offsets : nullptr,
+                                   out ? w.out_place : nullptr},
+                        lane);
+        if (out && w.out_sel_id && lane < k) {
+            w.out_sel_id[lane] = s_selid[lane];
+            w.out_sel_w[lane] = s_selw[lane];
+        }
+    }
+    __syncthreads();
+    TRX_TRACE(60);
+
+    const uint64_t pol = trx_policy_evict_first(); // the weights are read once a call
+    if (warp == TRX_DC_CWARPS) {
+        // the CTA's share of every selected expert into L2 at once (gate rows, up rows, down rows, the down rows' d
+        // values: lane 4 i + part), so that HBM streams the whole call's weights while the rings start; the rings'
+        // copies then read L2
+        const int i = lane >> 2, part = lane & 3, rbg = H / 256 * 144, rbd = nsb * 208;
+        if (i < k) {
+            const int e = s_selid[i];
+            if (part < 2) {
+                const uint8_t *mat = part == 0 ? L.gate + e * L.gate_mb : L.up + e * L.up_mb;
+                if (ng > 0) trx_bulk_prefetch_l2(mat + (int64_t)ga * rbg, (uint32_t)(ng * rbg));
+            } else if (nd > 0) {
+                const uint8_t *mat = L.down + e * L.down_mb;
+                if (part == 2) {
+                    trx_bulk_prefetch_l2(mat + (int64_t)da * rbd, (uint32_t)(nd * rbd));
+                } else { // the d values of rows [da, da + nd), widened to 16-byte bounds
+                    const int64_t lo = (int64_t)H * rbd + (((int64_t)da * nsb * 2) & ~15ll);
+                    const int64_t hi = (int64_t)H * rbd + (((int64_t)(da + nd) * nsb * 2 + 15) & ~15ll);
+                    trx_bulk_prefetch_l2(mat + lo, (uint32_t)(hi - lo));
+                }
+            }
+        }
+    }
+    bool failed = false;
+    if (warp < TRX_DC_CWARPS) {
+        // ---------------- a consumer warp: TRX_DC_GU gate/up units, then TRX_DC_DN down steps, through its slots
+        uint8_t *slots = smem + (size_t)warp * TRX_DC_NS * TRX_DC_SLOT;
+        const int ngu = k * ng, ndn = (k / 2) * nd; // gate/up units (expert-major), down units (expert pairs)
+        const int rbg = H / 256 * 144, rbd = nsb * 208;
+        // lane 0 arms step j in its slot (a step with nothing to load completes at once: zero bytes expected)
+        auto issue = [&](int j) {
+            if (lane != 0) return;
+            uint8_t *dst = slots + (j % TRX_DC_NS) * TRX_DC_SLOT;
+            uint64_t *bar = &s_full[warp][j % TRX_DC_NS];
+            trx_fence_proxy_async(); // this warp's reads of the slot's last step before the copy rewrites it
+            if (j < TRX_DC_GU) {
+                const int u = warp + TRX_DC_CWARPS * j;
+                if (u >= ngu) {
+                    trx_mbar_expect_tx(bar, 0u);
+                    return;
+                }
+                const int i = u / ng, r = ga + u % ng, e = s_selid[i];
+                trx_mbar_expect_tx(bar, 2u * rbg);
+                trx_bulk_g2s_hint(dst, L.gate + e * L.gate_mb + (int64_t)r * rbg, rbg, bar, pol);
+                trx_bulk_g2s_hint(dst + rbg, L.up + e * L.up_mb + (int64_t)r * rbg, rbg, bar, pol);
+            } else {
+                uint32_t bytes = 0;
+                for (int hh = 0; hh < 2; hh++)
+                    if (2 * warp + hh + 2 * TRX_DC_CWARPS * (j - TRX_DC_GU) < ndn) bytes += 2u * rbd + 32u;
+                trx_mbar_expect_tx(bar, bytes);
+                for (int hh = 0; hh < 2; hh++) {
+                    const int v = 2 * warp + hh + 2 * TRX_DC_CWARPS * (j - TRX_DC_GU);
+                    if (v >= ndn) continue;
+                    const int q = v / nd, r = da + v % nd;
+                    uint8_t *d0 = dst + hh * (2 * rbd + 32);
+                    for (int ab = 0; ab < 2; ab++) {
+                        const uint8_t *mat = L.down + s_selid[2 * q + ab] * L.down_mb;
+                        trx_bulk_g2s_hint(d0 + ab * rbd, mat + (int64_t)r * rbd, rbd, bar, pol);
+                        // the row's d values: the 16-byte piece that holds them
+                        trx_bulk_g2s_hint(d0 + 2 * rbd + 16 * ab, mat + (int64_t)H * rbd + ((int64_t)r * nsb * 2 & ~15ll),
+                                          16u, bar, pol);
+                    }
+                }
+            }
+        };
+        int issued = 0;
+        for (; issued < TRX_DC_NS; issued++) issue(issued);
+        TrxQ4X X;
+        trx_q4x_load(xq, 32, lane, xbf + 8 * (lane >> 2), xsc + (lane >> 2), X);
+        float *ss = s_q6sc[2 * warp + (lane >> 4)];
+        for (int j = 0; j < TRX_DC_GU + TRX_DC_DN && !failed; j++) {
+            const uint8_t *src = slots + (j % TRX_DC_NS) * TRX_DC_SLOT;
+            if (!__all_sync(0xffffffffu, trx_mbar_wait(&s_full[warp][j % TRX_DC_NS], (j / TRX_DC_NS) & 1, TRX_WAIT_NS))) {
+                failed = true;
+                break;
+            }
+            if (warp == 0) TRX_TRACE(8 + j); // (the timeline: warp 0's step j has its weights)
+            if (j < TRX_DC_GU) {
+                const int u = warp + TRX_DC_CWARPS * j;
+                if (u < ngu) {
+                    const uint8_t *const rows2[2] = {src, src + rbg};
+                    float y2[2];
+                    trx_q4k_row8xn<true, 2>(rows2, X, lane, y2);
+                    if (lane == 0) { // to the silu warp
+                        s_gu[u] = make_float2(y2[0], y2[1]);
+                        trx_mbar_arrive(&s_gubar[j]);
+                    }
+                }
+            } else {
+                const int v = 2 * warp + (lane >> 4) + 2 * TRX_DC_CWARPS * (j - TRX_DC_GU);
+                const int v0 = 2 * warp + 2 * TRX_DC_CWARPS * (j - TRX_DC_GU);
+                if (v0 < ndn) { // (the warp's first unit exists; a second one past the end computes unstored)
+                    const bool valid = v < ndn;
+                    const int q = valid ? v / nd : 0, rl = valid ? v % nd : 0, r = da + rl;
+                    const bool ok =
+                        trx_mbar_wait(&s_hbar[2 * q], 0, TRX_WAIT_NS) && trx_mbar_wait(&s_hbar[2 * q + 1], 0, TRX_WAIT_NS);
+                    if (!__all_sync(0xffffffffu, ok)) {
+                        failed = true;
+                        break;
+                    }
+                    if (warp == 0) TRX_TRACE(24 + j); // its h rows
+                    const uint8_t *d0 = src + (valid ? (lane >> 4) : 0) * (2 * rbd + 32);
+                    const int dh = (r * nsb * 2) & 15; // the row's d values inside their 16-byte piece
+                    const float2 val = trx_q6l_dot_pair_il(d0, d0 + 2 * rbd + dh, d0 + rbd, d0 + 2 * rbd + 16 + dh,
+                                                           hbuf + (size_t)q * 2 * F, nsb, lane & 15, ss);
+                    if (valid && (lane & 15) == 0) {
+                        s_h3[2 * q][rl] = val.x;
+                        s_h3[2 * q + 1][rl] = val.y;
+                    }
+                }
+            }
+            __syncwarp();
+            if (warp == 0) TRX_TRACE(16 + j); // computed
+            if (issued < TRX_DC_GU + TRX_DC_DN) issue(issued++);
+        }
+        if (failed && lane == 0) { // every copy this warp armed lands before the CTA can leave
+            for (int j = 0; j < issued; j++)
+                trx_mbar_wait(&s_full[warp][j % TRX_DC_NS], (j / TRX_DC_NS) & 1, TRX_WAIT_NS);
+        }
+    } else if (warp == TRX_DC_SILU) {
+        // ---------------- h = silu(g) u of a step's gate/up units at once (lane l: unit 14 j + l), published tagged;
+        // the consumers go on to their next rows meanwhile
+        const int ngu = k * ng;
+        for (int j = 0; j < TRX_DC_GU && TRX_DC_CWARPS * j < ngu && !failed; j++) {
+            if (!__all_sync(0xffffffffu, trx_mbar_wait(&s_gubar[j], 0, TRX_WAIT_NS))) {
+                failed = true;
+                break;
+            }
+            const int u = TRX_DC_CWARPS * j + lane;
+            if (lane < TRX_DC_CWARPS && u < ngu) {
+                const float2 gu = s_gu[u];
+                trx_st_tagged(w.tag_h + (int64_t)(u / ng) * F + trx_lc_pos(ga + u % ng), tag, trx_silu_mul(gu.x, gu.y));
+            }
+        }
+    } else if (warp == TRX_DC_HELPER) {
+        // ---------------- the helper: expert i's h into shared memory, experts in order, each value once it carries
+        // this call's tag. Lane l takes value pairs l + 32 m (m < F / 64): every load of a poll is issued before the
+        // first is looked at, 512 contiguous bytes a warp-wide load; the lane arrives once it holds all its pairs.
+        const int npair = F / 64; // 4, 8 or 16
+        for (int i = 0; i < k && !failed; i++) {
+            const unsigned long long *src = w.tag_h + (int64_t)i * F;
+            float *dst = hbuf + (size_t)(i >> 1) * 2 * F + (i & 1); // expert pairs' rows interleaved
+            uint32_t want = (1u << npair) - 1u; // the pairs still missing
+            uint64_t t0 = 0;
+            for (;;) {
+                ulonglong2 v[16];
+#pragma unroll
+                for (int m = 0; m < 16; m++)
+                    if (want >> m & 1u) v[m] = trx_ld_tagged2(src + 2 * (lane + 32 * m));
+#pragma unroll
+                for (int m = 0; m < 16; m++) {
+                    if ((want >> m & 1u) && (uint32_t)(v[m].x >> 32) == tag && (uint32_t)(v[m].y >> 32) == tag) {
+                        dst[4 * (lane + 32 * m)] = __uint_as_float((uint32_t)v[m].x);
+                        dst[4 * (lane + 32 * m) + 2] = __uint_as_float((uint32_t)v[m].y);
+                        want &= ~(1u << m);
+                    }
+                }
+                if (want == 0u) break;
+                const uint64_t now = trx_globaltimer();
+                if (t0 == 0) t0 = now;
+                else if (now - t0 > TRX_SPIN_NS) {
+                    failed = true;
+                    break;
+                }
+                __nanosleep(100);
+            }
+            if (__any_sync(0xffffffffu, failed)) {
+                failed = true;
+                break;
+            }
+            if (w.trace != nullptr && lane == 0) w.trace[(size_t)blockIdx.x * 64 + 32 + i] = trx_globaltimer();
+            trx_mbar_arrive(&s_hbar[i]); // (each lane its own values: the barrier orders them before the readers)
+        }
+    }
+    TRX_TRACE(6);
+
+    // ---------------- mix and end
+    if (__syncthreads_or(failed)) {
+        if (tid == 0) {
+            atomicCAS(w.err, 0, 3);
+            if (w.host_done) trx_post_done(w.host_done, epoch | 0x80000000u);
+        }
+        return;
+    }
+    if (tid < nd) { // output row da + tid: the k outputs in increasing expert id, then the residual
+        float out = 0.0f;
+        for (int i = 0; i < k; i++) out = __fadd_rn(out, __fmul_rn(s_selw[i], s_h3[i][tid]));
+        if (ffn_out) ffn_out[da + tid] = out;
+        x_io[da + tid] = __fadd_rn(xres, out);
+    }
+    __syncthreads();
+    TRX_TRACE(52);
+    if (w.host_done == nullptr) {
+        if (c == 0 && tid == 0) sync->seq = tag; // the next call's tag: tag + 1 (the next kernel sees it at our end)
+        return;
+    }
+    if (tid == 0) { // the host-pointer road: the host learns the end from a word the last CTA posts
+        __threadfence_system(); // the outputs (x may be host memory) before the count
+        if (atomicAdd(&sync->finish, 1u) == (uint32_t)G - 1) { // every CTA is past its waits
+            sync->seq = tag;
+            sync->finish = 0u;
+            __threadfence();
+            trx_post_done(w.host_done, epoch);
+        }
+    }
+}

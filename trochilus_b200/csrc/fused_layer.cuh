@@ -46,7 +46,7 @@
 
 struct TrxSync {
     uint32_t route_cnt;                // router and prep CTAs done in this call
-    uint32_t routed;                   // unused (kept for the layout)
+    uint32_t seq;                      // the one-token kernel's call count: its exchanged words carry seq + 1
     uint32_t finish;                   // CTAs done in this call
     uint32_t pad;
     uint32_t gu_done[TRX_MAX_EXPERTS]; // gate/up rows done per active slot (+1 once Q4_K's down inputs are ready)

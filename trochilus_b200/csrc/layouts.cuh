@@ -16,10 +16,13 @@
 //  Q8L   from Q8_0 (34 B per 32 weights): per 256 weights (8 blocks), 16 B of the 8 f16 scales, then
 //        256 B where byte 16 l + m is q[l + 16 m] (lane l's m-th weight of the chunk). A 16-byte
 //        load of a thread of the 16-lane contract is then 16 consecutive terms of its own lane.
-//  Q6L   from Q6_K (210 B per 256 weights): per row, for each block s: 128 B low nibbles
-//        (lane l: 8 bytes, weight m in nibble m & 1 of byte m >> 1), then 64 B high bit-pairs
-//        (lane l: 4 bytes, weight m in bits 2 (m & 3) of byte m >> 2), then the 16 int8 scales;
-//        the f16 d of every (row, block) after all the rows of the matrix.
+//  Q6L   from Q6_K (210 B per 256 weights): per row, for each block s: 128 B low nibbles, then 64 B
+//        high bit-pairs, then the 16 int8 scales; the f16 d of every (row, block) after all the rows of
+//        the matrix. Lane l's 16 weights m (element l + 16 m) are ordered so that four 6-bit quants come
+//        out as the four bytes of a word in two or three logic operations: its 8 low-nibble bytes hold,
+//        in byte b < 4, weights b (low nibble) and b + 4 (high nibble), in byte 4 + b weights 8 + b and
+//        12 + b; its 4 high-bit bytes hold in byte b the pairs of weights b, b + 4, b + 8, b + 12 at bits
+//        0, 2, 4 and 6.
 //  F32, BF16 (router): as in the file.
 // The lane-contract dots (Q8_0, Q6_K, F32, BF16) take their input row in the "LC order": inside
 // every 256 floats, x[l + 16 m] sits at 64 (m >> 2) + 4 l + (m & 3), so that a thread's four
@@ -83,29 +86,26 @@ __global__ void trx_repack_q6l(const uint8_t *__restrict__ src, uint8_t *__restr
     uint8_t *dd = dst + rows * nsb * 208 + r * nsb * 2;
     for (int64_t s = 0; s < nsb; s++) {
         const uint8_t *blk = srow + s * 210;
-        // lane l, pair b: low nibbles of weights m = 2b, 2b + 1 (element l + 16 m)
+        // the low nibble and the high bit-pair of weight m of lane l (element i = l + 16 m of the block)
+        auto lo4 = [&](int l, int m) -> unsigned {
+            const int i = l + 16 * m, hh = i >> 7, c = (i >> 5) & 3, ll = i & 31;
+            const unsigned v = blk[64 * hh + 32 * (c & 1) + ll];
+            return (c & 2) ? v >> 4 : v & 15u;
+        };
+        auto hi2 = [&](int l, int m) -> unsigned {
+            const int i = l + 16 * m, hh = i >> 7, c = (i >> 5) & 3, ll = i & 31;
+            return (blk[128 + 32 * hh + ll] >> (2 * c)) & 3u;
+        };
+        // lane l's byte t (0..7): weights mb (low nibble) and mb + 4 (high nibble), mb = t < 4 ? t : t + 4
         for (int t = threadIdx.x; t < 128; t += blockDim.x) {
-            const int l = t >> 3, b = t & 7;
-            uint8_t v = 0;
-            for (int h = 0; h < 2; h++) {
-                const int i = l + 16 * (2 * b + h); // element in the block
-                const int hh = i >> 7, c = (i >> 5) & 3, ll = i & 31;
-                unsigned lo = blk[64 * hh + 32 * (c & 1) + ll];
-                lo = (c & 2) ? lo >> 4 : lo & 15u;
-                v |= (uint8_t)(lo << (4 * h));
-            }
-            drow[s * 128 + t] = v;
+            const int l = t >> 3, b = t & 7, mb = b < 4 ? b : b + 4;
+            drow[s * 128 + t] = (uint8_t)(lo4(l, mb) | lo4(l, mb + 4) << 4);
         }
+        // lane l's byte b (0..3): the pairs of weights b, b + 4, b + 8, b + 12 at bits 0, 2, 4, 6
         for (int t = threadIdx.x; t < 64; t += blockDim.x) {
             const int l = t >> 2, b = t & 3;
-            uint8_t v = 0;
-            for (int u = 0; u < 4; u++) {
-                const int i = l + 16 * (4 * b + u);
-                const int hh = i >> 7, c = (i >> 5) & 3, ll = i & 31;
-                const unsigned hi = (blk[128 + 32 * hh + ll] >> (2 * c)) & 3u;
-                v |= (uint8_t)(hi << (2 * u));
-            }
-            drow[nsb * 128 + s * 64 + t] = v;
+            drow[nsb * 128 + s * 64 + t] =
+                (uint8_t)(hi2(l, b) | hi2(l, b + 4) << 2 | hi2(l, b + 8) << 4 | hi2(l, b + 12) << 6);
         }
         for (int t = threadIdx.x; t < 16; t += blockDim.x) drow[nsb * 192 + s * 16 + t] = blk[192 + t];
         if (threadIdx.x == 0) {
@@ -143,10 +143,14 @@ __host__ __device__ inline int trx_q4x_lanes(int s, int nsb) {
     return 4 * (nb < 8 ? nb : 8);
 }
 
+// 2^n as a double from its bits, for the exponents the preparation takes (|n| < 1022): the same value as
+// ldexp(1.0, n), without its library call
+__device__ __forceinline__ double trx_pow2d(int n) { return __longlong_as_double((long long)(1023 + n) << 52); }
+
 // One warp per 256-block; lane L takes elements 8 L .. 8 L + 7. CG: read x through L2 only (a row another CTA of
 // the same kernel wrote). planes_row, bf_blk, sc_blk: the row's planes, the block's sums and scale.
 template <bool CG = false>
-__device__ __forceinline__ void trx_prep_q4x_block(const float *__restrict__ x, uint32_t *__restrict__ planes_row, int s,
+__device__ __noinline__ void trx_prep_q4x_block(const float *__restrict__ x, uint32_t *__restrict__ planes_row, int s,
                                                    int nsb, double *__restrict__ bf_blk, double *__restrict__ sc_blk,
                                                    int lane) {
     float v[8];
@@ -173,9 +177,9 @@ __device__ __forceinline__ void trx_prep_q4x_block(const float *__restrict__ x, 
         const int e = field ? field - 126 : (32 - __clz((int)(mb & 0x7fffffu))) - 149;
         sh = 31 - e;
         // m 2^sh is exact in double (a power of two times a float)
-        if (__dmul_rn((double)m, ldexp(1.0, sh)) > 2085998640.0) sh--;
+        if (__dmul_rn((double)m, trx_pow2d(sh)) > 2085998640.0) sh--;
     }
-    const double f = bad ? 0.0 : ldexp(1.0, sh);
+    const double f = bad ? 0.0 : trx_pow2d(sh);
     int32_t X[8];
 #pragma unroll
     for (int i = 0; i < 8; i++) {
@@ -189,7 +193,7 @@ __device__ __forceinline__ void trx_prep_q4x_block(const float *__restrict__ x, 
     sum += trx_shfl_xor64(sum, 1);
     sum += trx_shfl_xor64(sum, 2);
     if ((lane & 3) == 0) bf_blk[lane >> 2] = (double)sum;
-    if (lane == 0) sc_blk[0] = bad ? __longlong_as_double(0x7ff8000000000000ll) : ldexp(1.0, -sh);
+    if (lane == 0) sc_blk[0] = bad ? __longlong_as_double(0x7ff8000000000000ll) : trx_pow2d(-sh);
     // this lane's 8 elements: chunk c = lane / 8, groups g, g + 1 (g = 2 (lane % 8)) of consumer lane 4 (s % 8) + c
     const int c = lane >> 3, g = 2 * (lane & 7), NL = trx_q4x_lanes(s, nsb), L = 4 * (s & 7) + c;
     uint32_t *pass = planes_row + 2048 * (s >> 3);
@@ -325,27 +329,57 @@ __device__ __forceinline__ float trx_q8l_block(float acc, uint4 sc, uint4 q, con
     return acc;
 }
 
-// Q6L: ql = the thread's 16 low nibbles (element m: bits 4 (m % 8) of word m / 8), qh = its 16 high bit pairs
-// (bits 2 m), scv = the block's 16 int8 sub-block scales (element m has scale m), d = the block's f16 d
-__device__ __forceinline__ float trx_q6l_block(float acc, uint2 ql, uint32_t qh, uint4 scv, float d, const float (&xv)[16]) {
+// Q6L: the thread's 16 six-bit quants as four words of four bytes (word j: weights 4 j .. 4 j + 3), from its 8
+// low-nibble bytes ql and its 4 high-bit bytes qh (the layout above)
+__device__ __forceinline__ void trx_q6l_quants(uint2 ql, uint32_t qh, uint32_t (&q4)[4]) {
+    q4[0] = (ql.x & 0x0f0f0f0fu) | ((qh << 4) & 0x30303030u);
+    q4[1] = ((ql.x >> 4) & 0x0f0f0f0fu) | ((qh << 2) & 0x30303030u);
+    q4[2] = (ql.y & 0x0f0f0f0fu) | (qh & 0x30303030u);
+    q4[3] = ((ql.y >> 4) & 0x0f0f0f0fu) | ((qh >> 2) & 0x30303030u);
+}
+
+// One 256-block of a Q6L row for thread l of the half-warp, with the block's 16 sub-block scales fl(d sc_m) given
+// (element m has scale m): w = scale (q - 32), exact (d has 11 significant bits, sc 8, q - 32 6); the products
+// w x rounded one by one, added in order of m.
+__device__ __forceinline__ float trx_q6l_block_sc(float acc, uint2 ql, uint32_t qh, const float (&scale)[16],
+                                                  const float (&xv)[16]) {
+    uint32_t q4[4];
+    trx_q6l_quants(ql, qh, q4);
+    const trx_f2 bias6 = trx_pack2(8388640.0f, 8388640.0f); // 2^23 + 32
+#pragma unroll
+    for (int m = 0; m < 16; m += 2) {
+        // 2^23 + q as float bits (byte m & 3 of word m / 4 under the exponent of 2^23), less 2^23 + 32: q - 32
+        const trx_f2 qv = trx_sub2(trx_pack2(__uint_as_float(__byte_perm(q4[m >> 2], 0x4b000000u, 0x7440u | (m & 3))),
+                                             __uint_as_float(__byte_perm(q4[m >> 2], 0x4b000000u, 0x7440u | ((m + 1) & 3)))),
+                                   bias6);
+        const trx_f2 p = trx_mul2(trx_mul2(trx_pack2(scale[m], scale[m + 1]), qv), trx_pack2(xv[m], xv[m + 1]));
+        acc = __fadd_rn(acc, trx_lo(p));
+        acc = __fadd_rn(acc, trx_hi(p));
+    }
+    return acc;
+}
+
+// the block's 16 scales fl(d sc_m) from its int8 scales scv (sc_m in byte m) and its f16 d
+__device__ __forceinline__ void trx_q6l_scales(uint4 scv, float d, float (&scale)[16]) {
     const uint32_t scw[4] = {scv.x ^ 0x80808080u, scv.y ^ 0x80808080u, scv.z ^ 0x80808080u, scv.w ^ 0x80808080u};
-    const uint32_t qlw[2] = {ql.x, ql.y};
-    const trx_f2 d2 = trx_pack2(d, d), bias8 = trx_pack2(8388736.0f, 8388736.0f), bias6 = trx_pack2(8388640.0f, 8388640.0f);
-    auto qbits = [&](int m) { // 2^23 + the 6-bit quant, as float bits
-        return 0x4b000000u | ((qlw[m >> 3] >> (4 * (m & 7))) & 15u) | (((qh >> (2 * m)) & 3u) << 4);
-    };
+    const trx_f2 d2 = trx_pack2(d, d), bias8 = trx_pack2(8388736.0f, 8388736.0f); // 2^23 + 128
 #pragma unroll
     for (int m = 0; m < 16; m += 2) {
         const trx_f2 scf = trx_sub2(trx_pack2(__uint_as_float(__byte_perm(scw[m >> 2], 0x4b000000u, 0x7440u | (m & 3))),
                                               __uint_as_float(__byte_perm(scw[m >> 2], 0x4b000000u, 0x7440u | ((m + 1) & 3)))),
                                     bias8);
-        const trx_f2 scale = trx_mul2(d2, scf);                                                  // d * sc
-        const trx_f2 qv = trx_sub2(trx_pack2(__uint_as_float(qbits(m)), __uint_as_float(qbits(m + 1))), bias6); // q - 32
-        const trx_f2 p = trx_mul2(trx_mul2(scale, qv), trx_pack2(xv[m], xv[m + 1]));
-        acc = __fadd_rn(acc, trx_lo(p));
-        acc = __fadd_rn(acc, trx_hi(p));
+        const trx_f2 sc = trx_mul2(d2, scf); // exact
+        scale[m] = trx_lo(sc);
+        scale[m + 1] = trx_hi(sc);
     }
-    return acc;
+}
+
+// Q6L: ql, qh = the thread's low nibbles and high bit pairs, scv = the block's 16 int8 sub-block scales (element m
+// has scale m), d = the block's f16 d
+__device__ __forceinline__ float trx_q6l_block(float acc, uint2 ql, uint32_t qh, uint4 scv, float d, const float (&xv)[16]) {
+    float scale[16];
+    trx_q6l_scales(scv, d, scale);
+    return trx_q6l_block_sc(acc, ql, qh, scale, xv);
 }
 
 // the thread's 16 inputs of block i of an LC-ordered row
@@ -389,6 +423,115 @@ __device__ __forceinline__ float trx_q6l_dot(const uint8_t *__restrict__ row, co
                                          : __ldg(reinterpret_cast<const uint16_t *>(dptr) + s)), xv);
     }
     return trx_lane_tree16(acc);
+}
+
+// Two Q6L rows a and b (in shared memory, each with its own LC-ordered input row xa, xb and d values da, db), thread l
+// of a half-warp: the products of the two rows' element m are formed together by paired operations (each half rounded
+// on its own), and each row's chain adds them with scalar additions, so each row's products and sums are exactly the
+// single-row road's, in the same order. (A paired addition in the chains gave other bits on sm_100: measured, 239 of
+// 256 random row pairs differed from the scalar chain; the chains therefore stay scalar.) The rows' scales are
+// computed once into the half-warp's scratch ss (32 nsb floats: row a's, then row b's). Both half-warps of the warp
+// call it together (it synchronises the warp). nsb <= TRX_Q6L_SS_BLOCKS.
+#define TRX_Q6L_SS_BLOCKS 4
+__device__ __noinline__ float2 trx_q6l_dot_pair(const uint8_t *__restrict__ ra, const uint8_t *__restrict__ da,
+                                                const float *__restrict__ xa, const uint8_t *__restrict__ rb,
+                                                const uint8_t *__restrict__ db, const float *__restrict__ xb, int nsb,
+                                                int l, float *__restrict__ ss) {
+    float *ssb = ss + 16 * TRX_Q6L_SS_BLOCKS;
+    for (int s = 0; s < nsb; s++) {
+        const float sca = (float)reinterpret_cast<const int8_t *>(ra + 192 * nsb + 16 * s)[l]; // exact
+        const float scb = (float)reinterpret_cast<const int8_t *>(rb + 192 * nsb + 16 * s)[l];
+        ss[16 * s + l] = __fmul_rn(trx_half(reinterpret_cast<const uint16_t *>(da)[s]), sca); // exact
+        ssb[16 * s + l] = __fmul_rn(trx_half(reinterpret_cast<const uint16_t *>(db)[s]), scb);
+    }
+    __syncwarp();
+    float aa = 0.0f, ab = 0.0f;
+    const trx_f2 bias6 = trx_pack2(8388640.0f, 8388640.0f); // 2^23 + 32
+#pragma unroll 1
+    for (int s = 0; s < nsb; s++) {
+        float xva[16], xvb[16], sa[16], sb[16];
+        trx_lc_block<false>(xa, s, l, xva);
+        trx_lc_block<false>(xb, s, l, xvb);
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            const float4 u = *reinterpret_cast<const float4 *>(ss + 16 * s + 4 * q);
+            const float4 v = *reinterpret_cast<const float4 *>(ssb + 16 * s + 4 * q);
+            sa[4 * q] = u.x; sa[4 * q + 1] = u.y; sa[4 * q + 2] = u.z; sa[4 * q + 3] = u.w;
+            sb[4 * q] = v.x; sb[4 * q + 1] = v.y; sb[4 * q + 2] = v.z; sb[4 * q + 3] = v.w;
+        }
+        uint32_t qa[4], qb[4];
+        trx_q6l_quants(*reinterpret_cast<const uint2 *>(ra + 128 * s + 8 * l),
+                       *reinterpret_cast<const uint32_t *>(ra + 128 * nsb + 64 * s + 4 * l), qa);
+        trx_q6l_quants(*reinterpret_cast<const uint2 *>(rb + 128 * s + 8 * l),
+                       *reinterpret_cast<const uint32_t *>(rb + 128 * nsb + 64 * s + 4 * l), qb);
+#pragma unroll
+        for (int m = 0; m < 16; m++) {
+            const uint32_t sel = 0x7440u | (m & 3);
+            const trx_f2 qv = trx_sub2(trx_pack2(__uint_as_float(__byte_perm(qa[m >> 2], 0x4b000000u, sel)),
+                                                 __uint_as_float(__byte_perm(qb[m >> 2], 0x4b000000u, sel))),
+                                       bias6); // (q_a - 32, q_b - 32)
+            const trx_f2 p = trx_mul2(trx_mul2(trx_pack2(sa[m], sb[m]), qv), trx_pack2(xva[m], xvb[m]));
+            aa = __fadd_rn(aa, trx_lo(p));
+            ab = __fadd_rn(ab, trx_hi(p));
+        }
+    }
+    __syncwarp(); // the scratch is free for the warp's next rows
+    return make_float2(trx_lane_tree16(aa), trx_lane_tree16(ab));
+}
+
+// trx_q6l_dot_pair with both operands laid out for the paired operations: xab holds the two LC-ordered input rows
+// interleaved (position p: xab[2 p] row a's input, xab[2 p + 1] row b's), and the scratch ss receives the scales as
+// pairs (sa_m, sb_m), so every 16-byte load yields two ready pairs and no value is moved to form one. Same products,
+// same order of additions, same bits.
+__device__ __noinline__ float2 trx_q6l_dot_pair_il(const uint8_t *__restrict__ ra, const uint8_t *__restrict__ da,
+                                                   const uint8_t *__restrict__ rb, const uint8_t *__restrict__ db,
+                                                   const float *__restrict__ xab, int nsb, int l, float *__restrict__ ss) {
+    for (int s = 0; s < nsb; s++) {
+        const float sca = (float)reinterpret_cast<const int8_t *>(ra + 192 * nsb + 16 * s)[l]; // exact
+        const float scb = (float)reinterpret_cast<const int8_t *>(rb + 192 * nsb + 16 * s)[l];
+        *reinterpret_cast<float2 *>(ss + 2 * (16 * s + l)) =
+            make_float2(__fmul_rn(trx_half(reinterpret_cast<const uint16_t *>(da)[s]), sca),
+                        __fmul_rn(trx_half(reinterpret_cast<const uint16_t *>(db)[s]), scb)); // exact
+    }
+    __syncwarp();
+    float aa = 0.0f, ab = 0.0f;
+    const trx_f2 bias6 = trx_pack2(8388640.0f, 8388640.0f); // 2^23 + 32
+#pragma unroll 1
+    for (int s = 0; s < nsb; s++) {
+        trx_f2 xv[16], sv[16];
+#pragma unroll
+        for (int q = 0; q < 4; q++) { // element 4 q + j: position 256 s + 64 q + 4 l + j
+            const ulonglong2 u = *reinterpret_cast<const ulonglong2 *>(xab + 2 * (256 * s + 64 * q + 4 * l));
+            const ulonglong2 v = *reinterpret_cast<const ulonglong2 *>(xab + 2 * (256 * s + 64 * q + 4 * l) + 4);
+            xv[4 * q] = u.x;
+            xv[4 * q + 1] = u.y;
+            xv[4 * q + 2] = v.x;
+            xv[4 * q + 3] = v.y;
+        }
+#pragma unroll
+        for (int q = 0; q < 8; q++) {
+            const ulonglong2 u = *reinterpret_cast<const ulonglong2 *>(ss + 2 * (16 * s + 2 * q));
+            sv[2 * q] = u.x;
+            sv[2 * q + 1] = u.y;
+        }
+        uint32_t qa[4], qb[4];
+        trx_q6l_quants(*reinterpret_cast<const uint2 *>(ra + 128 * s + 8 * l),
+                       *reinterpret_cast<const uint32_t *>(ra + 128 * nsb + 64 * s + 4 * l), qa);
+        trx_q6l_quants(*reinterpret_cast<const uint2 *>(rb + 128 * s + 8 * l),
+                       *reinterpret_cast<const uint32_t *>(rb + 128 * nsb + 64 * s + 4 * l), qb);
+#pragma unroll
+        for (int m = 0; m < 16; m++) {
+            const uint32_t sel = 0x7440u | (m & 3);
+            const trx_f2 qv = trx_sub2(trx_pack2(__uint_as_float(__byte_perm(qa[m >> 2], 0x4b000000u, sel)),
+                                                 __uint_as_float(__byte_perm(qb[m >> 2], 0x4b000000u, sel))),
+                                       bias6); // (q_a - 32, q_b - 32)
+            const trx_f2 p = trx_mul2(trx_mul2(sv[m], qv), xv[m]);
+            aa = __fadd_rn(aa, trx_lo(p));
+            ab = __fadd_rn(ab, trx_hi(p));
+        }
+    }
+    __syncwarp(); // the scratch is free for the warp's next rows
+    return make_float2(trx_lane_tree16(aa), trx_lane_tree16(ab));
 }
 
 // Two rows (a, b in shared memory) of the same width against one LC-ordered input row read through L1 (each

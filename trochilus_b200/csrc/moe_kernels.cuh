@@ -88,6 +88,8 @@ struct TrxWork {
                                  // row back into its source rank's region, then the sources' return flags
     uint32_t *host_done; // NULL, or a word of mapped pinned host memory: the fused kernel writes its epoch there
                          // once every output is visible to the host (bit 31 set: it gave up)
+    unsigned long long *tag_logits; // the one-token kernel (decode.cuh): [E] logits, each with the call's tag
+    unsigned long long *tag_h;      // and [k][F] h values (LC order), each with the call's tag
 };
 
 // ---------------------------------------------------------------------------------------------
@@ -131,15 +133,17 @@ __device__ __noinline__ void trx_route_token(const float *__restrict__ logits, i
         // to the lower id): probabilities are in [0, 1], so their bits order them as unsigned integers; key = bits
         // + 1 for a present element, 0 for an absent one (E < 64), which no present element follows
         const uint32_t q0 = ok0 ? __float_as_uint(p0) + 1u : 0u, q1 = ok1 ? __float_as_uint(p1) + 1u : 0u;
-        int c0 = 0, c1 = 0;
-#pragma unroll 4
+        // the 64 keys come by shuffles, all issued independently (the loop fully unrolled, four partial counts a
+        // key), so that their latencies overlap
+        int c0[4] = {0, 0, 0, 0}, c1[4] = {0, 0, 0, 0};
+#pragma unroll
         for (int j = 0; j < 32; j++) {
             const uint32_t a = __shfl_sync(0xffffffffu, q0, j), b = __shfl_sync(0xffffffffu, q1, j); // ids j, j + 32
-            c0 += (a > q0 || (a == q0 && j < lane)) + (b > q0);
-            c1 += (a >= q1) + (b > q1 || (b == q1 && j < lane));
+            c0[j & 3] += (a > q0 || (a == q0 && j < lane)) + (b > q0);
+            c1[j & 3] += (a >= q1) + (b > q1 || (b == q1 && j < lane));
         }
-        r0 = c0;
-        r1 = c1;
+        r0 = (c0[0] + c0[1]) + (c0[2] + c0[3]);
+        r1 = (c1[0] + c1[1]) + (c1[2] + c1[3]);
     }
     const bool s0 = ok0 && r0 < k, s1 = ok1 && r1 < k;
     float w0 = p0, w1 = p1;
@@ -557,7 +561,7 @@ __global__ void __launch_bounds__(256) trx_k_prep_tokens(TrxLayer L, TrxShape S,
 // ---------------------------------------------------------------------------------------------
 // gate / up / SwiGLU
 
-__device__ __forceinline__ float trx_silu_mul(float g, float u) {
+__device__ __noinline__ float trx_silu_mul(float g, float u) {
     const float e = trx_expf(-g);
     const float silu = __fdiv_rn(g, __fadd_rn(1.0f, e));
     return __fmul_rn(silu, u);
