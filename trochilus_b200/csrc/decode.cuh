@@ -384,8 +384,11 @@ __global__ void __launch_bounds__(TRX_DC_THREADS, 1)
                     if (warp == 0) TRX_TRACE(24 + j); // its h rows
                     const uint8_t *d0 = src + (valid ? (lane >> 4) : 0) * (2 * rbd + 32);
                     const int dh = (r * nsb * 2) & 15; // the row's d values inside their 16-byte piece
-                    const float2 val = trx_q6l_dot_pair_il(d0, d0 + 2 * rbd + dh, d0 + rbd, d0 + 2 * rbd + 16 + dh,
-                                                           hbuf + (size_t)q * 2 * F, nsb, lane & 15, ss);
+                    const uint8_t *rb = d0 + rbd, *dA = d0 + 2 * rbd + dh, *dB = d0 + 2 * rbd + 16 + dh;
+                    const float *xab = hbuf + (size_t)q * 2 * F;
+                    const float2 val = nsb == 4   ? trx_q6l_dot_pair_il<4>(d0, dA, rb, dB, xab, lane & 15, ss)
+                                       : nsb == 2 ? trx_q6l_dot_pair_il<2>(d0, dA, rb, dB, xab, lane & 15, ss)
+                                                  : trx_q6l_dot_pair_il<1>(d0, dA, rb, dB, xab, lane & 15, ss);
                     if (valid && (lane & 15) == 0) {
                         s_h3[2 * q][rl] = val.x;
                         s_h3[2 * q + 1][rl] = val.y;
@@ -422,7 +425,7 @@ __global__ void __launch_bounds__(TRX_DC_THREADS, 1)
         const int npair = F / 64; // 4, 8 or 16
         for (int i = 0; i < k && !failed; i++) {
             const unsigned long long *src = w.tag_h + (int64_t)i * F;
-            float *dst = hbuf + (size_t)(i >> 1) * 2 * F + (i & 1); // expert pairs' rows interleaved
+            float *dst = hbuf + (size_t)(i >> 1) * 2 * F + (i & 1); // expert pairs' rows interleaved (trx_il_off)
             uint32_t want = (1u << npair) - 1u; // the pairs still missing
             uint64_t t0 = 0;
             for (;;) {
@@ -433,8 +436,9 @@ __global__ void __launch_bounds__(TRX_DC_THREADS, 1)
 #pragma unroll
                 for (int m = 0; m < 16; m++) {
                     if ((want >> m & 1u) && (uint32_t)(v[m].x >> 32) == tag && (uint32_t)(v[m].y >> 32) == tag) {
-                        dst[4 * (lane + 32 * m)] = __uint_as_float((uint32_t)v[m].x);
-                        dst[4 * (lane + 32 * m) + 2] = __uint_as_float((uint32_t)v[m].y);
+                        const int pos = 2 * (lane + 32 * m); // (even: pos and pos + 1 are 2 apart in the layout)
+                        dst[trx_il_off(pos)] = __uint_as_float((uint32_t)v[m].x);
+                        dst[trx_il_off(pos) + 2] = __uint_as_float((uint32_t)v[m].y);
                         want &= ~(1u << m);
                     }
                 }

@@ -479,16 +479,26 @@ __device__ __noinline__ float2 trx_q6l_dot_pair(const uint8_t *__restrict__ ra, 
     return make_float2(trx_lane_tree16(aa), trx_lane_tree16(ab));
 }
 
-// trx_q6l_dot_pair with both operands laid out for the paired operations: xab holds the two LC-ordered input rows
-// interleaved (position p: xab[2 p] row a's input, xab[2 p + 1] row b's), and the scratch ss receives the scales as
-// pairs (sa_m, sb_m), so every 16-byte load yields two ready pairs and no value is moved to form one. Same products,
-// same order of additions, same bits.
+// The interleaved layout of two LC-ordered input rows a, b (trx_q6l_dot_pair_il): within each 64-position group g,
+// thread l's positions 4l, 4l+1 as (a, b, a, b) at float offset 128 g + 4 l and 4l+2, 4l+3 at 128 g + 64 + 4 l, so
+// that each 16-byte load of a half-warp reads 256 contiguous bytes and yields two ready pairs.
+__host__ __device__ inline int trx_il_off(int p) {
+    return 128 * (p >> 6) + 64 * ((p & 3) >> 1) + 4 * ((p >> 2) & 15) + 2 * (p & 1);
+}
+
+// trx_q6l_dot_pair with both operands laid out for the paired operations: xab holds the rows' inputs interleaved
+// (trx_il_off; row a's at even offsets, row b's at odd ones) and the scratch ss receives the scales as pairs
+// (sa_m, sb_m), so no value is moved to form a pair; NSB (1, 2 or 4 blocks) unrolled. Same products, same order of
+// additions, same bits. (The chains stay scalar: ptxas fuses a paired multiply feeding a paired addition into a
+// paired fma, explicit rounding notwithstanding; measured.)
+template <int NSB>
 __device__ __noinline__ float2 trx_q6l_dot_pair_il(const uint8_t *__restrict__ ra, const uint8_t *__restrict__ da,
                                                    const uint8_t *__restrict__ rb, const uint8_t *__restrict__ db,
-                                                   const float *__restrict__ xab, int nsb, int l, float *__restrict__ ss) {
-    for (int s = 0; s < nsb; s++) {
-        const float sca = (float)reinterpret_cast<const int8_t *>(ra + 192 * nsb + 16 * s)[l]; // exact
-        const float scb = (float)reinterpret_cast<const int8_t *>(rb + 192 * nsb + 16 * s)[l];
+                                                   const float *__restrict__ xab, int l, float *__restrict__ ss) {
+#pragma unroll
+    for (int s = 0; s < NSB; s++) {
+        const float sca = (float)reinterpret_cast<const int8_t *>(ra + 192 * NSB + 16 * s)[l]; // exact
+        const float scb = (float)reinterpret_cast<const int8_t *>(rb + 192 * NSB + 16 * s)[l];
         *reinterpret_cast<float2 *>(ss + 2 * (16 * s + l)) =
             make_float2(__fmul_rn(trx_half(reinterpret_cast<const uint16_t *>(da)[s]), sca),
                         __fmul_rn(trx_half(reinterpret_cast<const uint16_t *>(db)[s]), scb)); // exact
@@ -496,13 +506,13 @@ __device__ __noinline__ float2 trx_q6l_dot_pair_il(const uint8_t *__restrict__ r
     __syncwarp();
     float aa = 0.0f, ab = 0.0f;
     const trx_f2 bias6 = trx_pack2(8388640.0f, 8388640.0f); // 2^23 + 32
-#pragma unroll 1
-    for (int s = 0; s < nsb; s++) {
+#pragma unroll
+    for (int s = 0; s < NSB; s++) {
         trx_f2 xv[16], sv[16];
 #pragma unroll
         for (int q = 0; q < 4; q++) { // element 4 q + j: position 256 s + 64 q + 4 l + j
-            const ulonglong2 u = *reinterpret_cast<const ulonglong2 *>(xab + 2 * (256 * s + 64 * q + 4 * l));
-            const ulonglong2 v = *reinterpret_cast<const ulonglong2 *>(xab + 2 * (256 * s + 64 * q + 4 * l) + 4);
+            const ulonglong2 u = *reinterpret_cast<const ulonglong2 *>(xab + 128 * (4 * s + q) + 4 * l);
+            const ulonglong2 v = *reinterpret_cast<const ulonglong2 *>(xab + 128 * (4 * s + q) + 64 + 4 * l);
             xv[4 * q] = u.x;
             xv[4 * q + 1] = u.y;
             xv[4 * q + 2] = v.x;
@@ -516,9 +526,9 @@ __device__ __noinline__ float2 trx_q6l_dot_pair_il(const uint8_t *__restrict__ r
         }
         uint32_t qa[4], qb[4];
         trx_q6l_quants(*reinterpret_cast<const uint2 *>(ra + 128 * s + 8 * l),
-                       *reinterpret_cast<const uint32_t *>(ra + 128 * nsb + 64 * s + 4 * l), qa);
+                       *reinterpret_cast<const uint32_t *>(ra + 128 * NSB + 64 * s + 4 * l), qa);
         trx_q6l_quants(*reinterpret_cast<const uint2 *>(rb + 128 * s + 8 * l),
-                       *reinterpret_cast<const uint32_t *>(rb + 128 * nsb + 64 * s + 4 * l), qb);
+                       *reinterpret_cast<const uint32_t *>(rb + 128 * NSB + 64 * s + 4 * l), qb);
 #pragma unroll
         for (int m = 0; m < 16; m++) {
             const uint32_t sel = 0x7440u | (m & 3);
