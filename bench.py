@@ -506,8 +506,8 @@ def run_ours(args, rank, world, dist):
                   "act_prep": 2 * T * K_USED * F * 4, "down": down_bytes}
     peak, peak_kind = peaks()
     launches = m.launches(T)
-    if launches == 1:  # one fused kernel per call: it is the dominant (only) kernel, its bytes the layer's
-        dom = "trx_k_layer (fused MoE layer)"
+    if launches == 1:  # one kernel per call: it is the dominant (only) kernel, its bytes the layer's
+        dom = m.kernel_name(T)
         zone_bytes[dom] = layer_bytes
         zone_ms[dom] = ms_step
     else:

@@ -229,13 +229,19 @@ TRMOE_API int tr_gpu_moe_check(tr_gpu_moe *m);
 /* Timeline of the fused kernel (the counterpart of Trochilus's TR_POOL_TRACE, src/base/threads.h:98-108): when
  * on, every CTA of the fused kernel writes %globaltimer (ns) at its events into 64 slots: 0 start, 1 router or
  * preparation work done, 2 routing seen, 3 copies armed, 4+j gate/up chunk j done (j < 16), 20+j down chunk j's
- * inputs ready, 36+j down chunk j done, 52 end (0: no such event). tr_gpu_moe_trace_read waits for the stream and
+ * inputs ready, 36+j down chunk j done, 52 end (0: no such event). The one-token kernel: 0 start, 62 logit
+ * published, 1 logits held, 60 routed, 8+j warp 0's step j weights in, 24+j its h rows in, 16+j step done, 32+i
+ * expert i's h gathered, 6 experts done, 52 end. tr_gpu_moe_trace_read waits for the stream and
  * copies the last call's slots (ctas * 64 values, at most n) to host memory; returns the number of CTAs, or -1. */
 TRMOE_API int tr_gpu_moe_trace(tr_gpu_moe *m, int on);
 TRMOE_API int tr_gpu_moe_trace_read(tr_gpu_moe *m, uint64_t *slots, int64_t n);
 
 /* How many kernels one tr_gpu_moe_layer_dev call launches for n_tok tokens. */
 TRMOE_API int tr_gpu_moe_launches(const tr_gpu_moe *m, int64_t n_tok);
+
+/* The kernel one tr_gpu_moe_layer_dev call of n_tok tokens runs when it is a single kernel: "trx_k_dec1" (the
+ * one-token decode kernel), "trx_k_layer" (the fused layer kernel); "" when the call takes several kernels. */
+TRMOE_API const char *tr_gpu_moe_kernel_name(const tr_gpu_moe *m, int64_t n_tok);
 
 /* The message of this thread's last failure ("" if none). */
 TRMOE_API const char *trmoe_last_error(void);

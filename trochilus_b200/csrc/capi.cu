@@ -726,6 +726,15 @@ extern "C" int tr_gpu_moe_launches(const tr_gpu_moe *m, int64_t n_tok) {
     return (n_tok <= TRX_ROUTE_FUSED_MAX ? 1 : 4) + 2 + (m->cfg.down_type == TRX_Q4_K ? 1 : 0);
 }
 
+extern "C" const char *tr_gpu_moe_kernel_name(const tr_gpu_moe *m, int64_t n_tok) {
+    if (m == nullptr || tr_gpu_moe_launches(m, n_tok) != 1) return "";
+    const tr_gpu_moe_config &c = m->cfg;
+    if (m->dec1_ok && trx_dec1_takes(c.gate_type, c.down_type, c.router_type, (int)c.n_embd, (int)c.n_ff,
+                                     (int)c.n_expert, (int)c.n_used, (int)n_tok, m->grid_fused, false))
+        return "trx_k_dec1";
+    return "trx_k_layer";
+}
+
 extern "C" int tr_gpu_moe_check(tr_gpu_moe *m) {
     g_err.clear();
     if (m == nullptr || !ck(cudaSetDevice(m->device), "cudaSetDevice") || !stream_wait(m->stream)) return -1;

@@ -23,8 +23,8 @@ F32, F16, Q8_0, Q4_K, Q6_K, BF16 = 0, 1, 8, 12, 14, 30
 
 # every function include/trmoe.h declares
 EXPORTS = ["tr_gpu_moe_create", "tr_gpu_moe_free", "tr_gpu_moe_bytes", "tr_gpu_moe_set_layer", "tr_gpu_moe_layer",
-           "tr_gpu_moe_layer_dev", "tr_gpu_moe_launches", "tr_gpu_moe_profile", "tr_gpu_moe_profile_read",
-           "tr_gpu_moe_check", "tr_gpu_moe_layer_part", "tr_gpu_moe_trace",
+           "tr_gpu_moe_layer_dev", "tr_gpu_moe_launches", "tr_gpu_moe_kernel_name", "tr_gpu_moe_profile",
+           "tr_gpu_moe_profile_read", "tr_gpu_moe_check", "tr_gpu_moe_layer_part", "tr_gpu_moe_trace",
            "tr_gpu_moe_trace_read", "trmoe_last_error", "tr_matmul", "tr_matmul_grouped",
            "tr_matmul_grouped_s", "tr_softmax", "tr_swiglu", "trmoe_kernel_cache_clear", "tr_matmul_q4k_noalloc",
            "tr_gpu_moe_set_prefill", "tr_gpu_moe_ep_pack", "tr_gpu_moe_experts_dev", "tr_gpu_moe_ep_combine",
@@ -74,6 +74,8 @@ def lib():
     L.tr_gpu_moe_layer_dev.argtypes = [C.c_void_p, C.c_int64, C.c_void_p, C.c_int64, C.c_void_p,
                                        C.POINTER(Outputs), C.c_void_p]
     L.tr_gpu_moe_launches.argtypes = [C.c_void_p, C.c_int64]
+    L.tr_gpu_moe_kernel_name.argtypes = [C.c_void_p, C.c_int64]
+    L.tr_gpu_moe_kernel_name.restype = C.c_char_p
     L.tr_gpu_moe_ep_peer_region.argtypes = [C.c_void_p, C.c_int32, C.c_int32, C.c_int64, C.c_void_p]
     L.tr_gpu_moe_ep_peer_open.argtypes = [C.c_void_p, C.c_void_p]
     L.tr_gpu_moe_ep_dispatch.argtypes = [C.c_void_p, C.c_void_p, C.c_int64, C.c_void_p, C.c_void_p, C.c_void_p]
@@ -307,6 +309,10 @@ class GpuMoe:
 
     def launches(self, n_tok: int) -> int:
         return int(lib().tr_gpu_moe_launches(self.h, n_tok))
+
+    def kernel_name(self, n_tok: int) -> str:
+        """the kernel a call of n_tok tokens runs when it is one kernel ("" otherwise)"""
+        return lib().tr_gpu_moe_kernel_name(self.h, n_tok).decode()
 
     def ep_pack(self, sel_id_ptr, n_tok, n_ranks, cap, normed_ptr, send_rows_ptr, send_ids_ptr, send_counts_ptr,
                 place_ptr, scratch_ptr, stream=0):
