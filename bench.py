@@ -64,6 +64,8 @@ def args_parse():
     p.add_argument("--prefill-tokens", type=int, default=2048,
                    help="tokens of the prefill measurement added to the line (configs[2]'s layer); 0: skip it")
     p.add_argument("--prefill-steps", type=int, default=20)
+    p.add_argument("--ep-tokens", default="1,64",
+                   help="N > 1: tokens a rank for the expert-parallel measurements reported under \"ep\" (\"\": none)")
     p.add_argument("--only-prefill", action="store_true", help="run and print only the prefill measurement")
     p.add_argument("--only-attention", type=int, default=0, metavar="P",
                    help="run and print only the decode attention measurement at a context of P positions")
@@ -283,7 +285,7 @@ def ep_launches(gate, down, rows):
     return 1 + 2 + (1 if rows <= 64 else 2 + 2 + 2 + 1 + 2 + 2) + 1
 
 
-def run_ep(args, rank, world, dist):
+def run_ep(args, rank, world, dist, T=None, steps=None):
     import torch
     from trochilus_b200 import ep
     from trochilus_b200.moe import GpuMoe
@@ -291,7 +293,8 @@ def run_ep(args, rank, world, dist):
     dev = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(dev)
     gate, down = TYPES[args.gate], TYPES[args.down]
-    T, NL = args.tokens, args.layers
+    T = args.tokens if T is None else T
+    NL = args.layers
     # max_tokens: every row a rank can receive in the padded exchange (world x T k), so its experts take one kernel
     m = GpuMoe(NL, E, K_USED, H, F, gb.BF16, gate, down, max_tokens=T * world * K_USED, device=dev)
     lays, routers = host_layers(gate, down, n_host=2, n_routers=NL)
@@ -312,7 +315,7 @@ def run_ep(args, rank, world, dist):
             ep.ep_layer(dist, be, i % NL, normed[i % NL], x, cap=cap)
     torch.cuda.synchronize()
     dist.barrier()
-    steps = args.steps
+    steps = args.steps if steps is None else steps
     reps = max(steps // NL, 1)
     steps = reps * NL
     # a CUDA graph of NL layer calls (kernels and NCCL all-to-alls; the padded exchange has no host sync)
@@ -377,8 +380,9 @@ def run_ep(args, rank, world, dist):
     e2e_s = float(te.item())
     m.close()
     if rank != 0:
-        return
+        return None
     cfg = workload_config(args)
+    cfg["tokens_per_step"] = T
     cfg["parallelism"] = f"ep{world}"
     cfg["experts_per_gpu"] = E // world
     line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": steps,
@@ -397,7 +401,7 @@ def run_ep(args, rank, world, dist):
             "gpu_launches": ep_launches(gate, down, world * T * K_USED) * steps, "clocks": clk.summary(),
             "timing": f"CUDA graph of {NL} expert-parallel layer calls (kernels + NCCL) replayed {reps} times; CUDA "
                       f"events, max over ranks"}
-    print(json.dumps(line), flush=True)
+    return line
 
 
 def run_ours(args, rank, world, dist):
@@ -552,11 +556,16 @@ def run_ours(args, rank, world, dist):
             cpu = {"value": None, "unit": "tokens/s", "cores": 0, "kind": "reference", "sample": f"unavailable: {exc}"}
     m.close()
     if rank != 0:
-        return
+        return None
+    cfg = workload_config(args)
+    if world > 1:
+        cfg["parallelism"] = f"dp{world}"
+        cfg["replicas"] = ("each GPU holds every expert of the 16 layers (4.2 GB of its 180 GB) and serves its own "
+                           "token stream: no data-path collective")
     line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": steps,
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "int32/int64+f64 (Q4_K), f32 (Q6_K/Q8_0 lane contract)",
-            "data": "synthetic", "config": workload_config(args),
+            "data": "synthetic", "config": cfg,
             "roofline": {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_kind": peak_kind, "traffic": traffic,
                          "algorithmic_bytes": zone_bytes[dom], "avg_ms": zone_ms[dom]},
@@ -569,7 +578,7 @@ def run_ours(args, rank, world, dist):
             "prefill": prefill,
             "timing": f"CUDA graphs of {NL} layer calls replayed (+ a graph of the last {tail_n}); zones from graphs "
                       f"of parts 0..z"}
-    print(json.dumps(line), flush=True)
+    return line
 
 
 def run_attention(args):
@@ -655,10 +664,23 @@ def main():
         print(json.dumps(run_prefill(args, 0, 0 if args.no_cpu_baseline else args.cpu_seconds)), flush=True)
     elif args.impl == "reference":
         run_reference(args, rank, world)
-    elif world > 1:
-        run_ep(args, rank, world, dist)
     else:
-        run_ours(args, rank, world, dist)
+        # N = 1: the decode layer call on one GPU. N > 1: the same call on N data-parallel replicas (the headline:
+        # one-token decode streams are independent), then the north star's expert-parallel layer (64/N experts a
+        # GPU, NCCL all-to-all dispatch and combine) at one token a rank and at a throughput batch, under "ep"
+        line = run_ours(args, rank, world, dist)
+        if world > 1 and args.ep_tokens:
+            ep_lines = {}
+            for t_ep in [int(v) for v in args.ep_tokens.split(",") if v]:
+                r = run_ep(args, rank, world, dist, T=t_ep, steps=min(args.steps, 2048 if t_ep == 1 else 256))
+                if r is not None:
+                    ep_lines[f"T{t_ep}"] = {k: r[k] for k in ("value", "unit", "ms_per_step", "steps", "roofline",
+                                                              "e2e", "gpu_launches", "timing")}
+                    ep_lines[f"T{t_ep}"]["tokens_per_rank"] = t_ep
+            if line is not None:
+                line["ep"] = ep_lines
+        if line is not None:
+            print(json.dumps(line), flush=True)
     if dist:
         dist.destroy_process_group()
 

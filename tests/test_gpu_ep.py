@@ -222,10 +222,6 @@ def _peer_worker(rank, world, port, out_dir):
         dist.destroy_process_group()
 
 
-@pytest.mark.skipif(os.environ.get("TRX_PEER_EP_TEST") != "1",
-                    reason="experimental, not used by bench.py; set TRX_PEER_EP_TEST=1 to run it. Its last GPU run "
-                           "failed at the third call because the flag wait gave up at its first miss whenever an "
-                           "earlier flag was already set (its clock never started); fixed since, not yet re-run")
 def test_ep_peer_memory_matches_oracle(cuda, tmp_path):
     torch = cuda
     n = torch.cuda.device_count()
