@@ -64,6 +64,8 @@ def args_parse():
     p.add_argument("--prefill-tokens", type=int, default=2048,
                    help="tokens of the prefill measurement added to the line (configs[2]'s layer); 0: skip it")
     p.add_argument("--prefill-steps", type=int, default=20)
+    p.add_argument("--no-extra", action="store_true", help="skip the other configurations (\"configs\" key)")
+    p.add_argument("--extra-cpu-seconds", type=float, default=2.0)
     p.add_argument("--ep-tokens", default="1,64",
                    help="N > 1: tokens a rank for the expert-parallel measurements reported under \"ep\" (\"\": none)")
     p.add_argument("--only-prefill", action="store_true", help="run and print only the prefill measurement")
@@ -134,20 +136,24 @@ class Clocks:
                 "reasons": reasons, "samples": len(self.rows)}
 
 
-def cpu_reference(args, gate, down, seconds, steps=None, warmup=0):
+def cpu_reference(args, gate, down, seconds, steps=None, warmup=0, tokens=None, bias=None, names=None, lay=None):
     """Trochilus's own code (oracle/_ref) on all host cores: tokens/s of one MoE layer on T tokens. Either a
-    bounded time (seconds) or exactly `steps` layer calls after `warmup`."""
+    bounded time (seconds) or exactly `steps` layer calls after `warmup`. tokens, bias (the router's per-expert
+    bias), names (gate, down) and lay (host layer) default to the bench's own workload."""
     from oracle.oracle import RefLib, make_desc
+    T = args.tokens if tokens is None else tokens
+    gname, dname = (args.gate, args.down) if names is None else names
     ref = RefLib()
-    lays, routers = host_layers(gate, down, n_host=1, n_routers=1)
-    lay = dict(lays[0])
-    lay["router"] = routers[0]
-    d, keep = make_desc(lay, H, F, K_USED, 0, gb.BF16, gate, down)
+    if lay is None:
+        lays, routers = host_layers(gate, down, n_host=1, n_routers=1)
+        lay = dict(lays[0])
+        lay["router"] = routers[0]
+    d, keep = make_desc(lay, H, F, K_USED, 0, gb.BF16, gate, down, bias)
     pool = ref.pool(0)
-    st = ref.state(pool, d, args.tokens)
+    st = ref.state(pool, d, T)
     rng = np.random.default_rng(5)
-    xs = [rng.normal(size=(args.tokens, H)).astype(np.float32) for _ in range(16)]
-    res = np.zeros((args.tokens, H), np.float32)
+    xs = [rng.normal(size=(T, H)).astype(np.float32) for _ in range(16)]
+    res = np.zeros((T, H), np.float32)
     for i in range(warmup):
         ref.moe_layer(d, xs[i % 16], res, pool=pool, state=st)
     n, t0 = 0, time.perf_counter()
@@ -161,9 +167,10 @@ def cpu_reference(args, gate, down, seconds, steps=None, warmup=0):
     tier = ref.tier()
     ref.state_free(st)
     ref.pool_destroy(pool)
-    return {"value": args.tokens * n / el, "unit": "tokens/s", "cores": cores, "kind": "reference",
-            "sample": f"{n} MoE-layer calls of {args.tokens} token(s), {args.gate}/{args.down}, BF16 router, "
-                      f"{el:.1f} s, Trochilus tier {tier}, tr_pool of {cores} threads"}
+    return {"value": T * n / el, "unit": "tokens/s", "cores": cores, "kind": "reference",
+            "sample": f"{n} MoE-layer calls of {T} token(s), {gname}/{dname}, BF16 router"
+                      f"{', Zipf router bias' if bias is not None else ''}, {el:.1f} s, Trochilus tier {tier}, "
+                      f"tr_pool of {cores} threads"}
 
 
 def run_reference(args, rank, world):
@@ -247,6 +254,12 @@ def run_prefill(args, dev, cpu_seconds):
     flops = 2.0 * T * K_USED * 3 * H * F + 2.0 * T * E * H
     tflops = flops / (ms / 1000.0) / 1e12
     peak, peak_kind = tf32_peak()
+    traffic = None
+    try:
+        with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
+            traffic = json.load(f).get(f"q8_0/q8_0/T{T}/trx_k_pf_gemm (gate/up + down)")
+    except (OSError, ValueError):
+        pass
     # e2e through the host-pointer call: normed and x in, x out, per call
     hn = torch.randn((T, H)).pin_memory()
     hx = torch.randn((T, H)).pin_memory()
@@ -265,7 +278,8 @@ def run_prefill(args, dev, cpu_seconds):
                         "peak": peak, "unit": "TFLOP/s", "frac": tflops / peak, "peak_kind": peak_kind,
                         "flops": flops, "issued_frac": 3.0 * tflops / peak,
                         "note": "useful flops of the whole layer call over its time; the tensor pipe issues 3x these "
-                                "(hi.hi, hi.lo, lo.hi): issued_frac", "traffic": None},
+                                "(hi.hi, hi.lo, lo.hi): issued_frac", "traffic": traffic,
+                        "traffic_note": "dram read+write of the call's two GEMM launches (ncu, profiles/traffic.json)"},
            "e2e": {"value": T / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": 2 * T * H * 4,
                    "d2h_bytes_per_step": T * H * 4},
            "clocks": clk.summary()}
@@ -402,6 +416,102 @@ def run_ep(args, rank, world, dist, T=None, steps=None):
             "timing": f"CUDA graph of {NL} expert-parallel layer calls (kernels + NCCL) replayed {reps} times; CUDA "
                       f"events, max over ranks"}
     return line
+
+
+# The rest of the metric's configurations (BASELINE.json configs[1] at more tokens, the Q8_0 decode, configs[3]'s
+# Zipf-routed passes): key, gate, down, tokens a call, Zipf router bias
+EXTRA = (("q8_0_T1", "q8_0", "q8_0", 1, False), ("q8_0_T8", "q8_0", "q8_0", 8, False),
+         ("q8_0_T64", "q8_0", "q8_0", 64, False), ("q4km_T8", "q4_k", "q6_k", 8, False),
+         ("q4km_T64", "q4_k", "q6_k", 64, False), ("zipf_q4k_T512", "q4_k", "q4_k", 512, True),
+         ("zipf_q4k_T4096", "q4_k", "q4_k", 4096, True), ("zipf_q8_0_T512", "q8_0", "q8_0", 512, True),
+         ("zipf_q8_0_T4096", "q8_0", "q8_0", 4096, True))
+
+
+def run_extra(args, dev, cpu_seconds):
+    """Each EXTRA configuration on one GPU: CUDA graphs of 4 resident layer calls (two distinct weight sets, each
+    larger than L2), the layer's algorithmic bytes and useful flops over its time, and Trochilus's CPU code on the
+    same configuration for cpu_seconds."""
+    import torch
+    from trochilus_b200.moe import GpuMoe
+    peak, peak_kind = peaks()
+    out, host = {}, {}
+    NLX = 4
+    for key, gname, dname, T, zipf in EXTRA:
+        gate, down = TYPES[gname], TYPES[dname]
+        if (gate, down) not in host:  # one set of host layers per type pair
+            host.clear()
+            host[(gate, down)] = host_layers(gate, down, n_host=2, n_routers=NLX)
+        lays, routers = host[(gate, down)]
+        bias = gb.zipf_bias(6, E) if zipf else None
+        m = GpuMoe(NLX, E, K_USED, H, F, gb.BF16, gate, down, max_tokens=T, device=dev)
+        for l in range(NLX):
+            lay = dict(lays[l % 2])
+            lay["router"] = routers[l]
+            m.set_layer(l, lay, bias)
+        g = torch.Generator(device="cuda")
+        g.manual_seed(4321 + T)
+        normed = torch.randn((NLX, T, H), device="cuda", generator=g)
+        x = torch.randn((T, H), device="cuda", generator=g)
+        sp = torch.cuda.Stream()
+        for i in range(3):
+            m.layer_dev(i % NLX, normed[i % NLX].data_ptr(), T, x.data_ptr(), None, stream=sp.cuda_stream)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=sp):
+            for l in range(NLX):
+                m.layer_dev(l, normed[l].data_ptr(), T, x.data_ptr(), None,
+                            stream=torch.cuda.current_stream().cuda_stream)
+        for _ in range(3):
+            graph.replay()
+        torch.cuda.synchronize()
+        cur = torch.cuda.current_stream()  # the stream the replays run on
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(cur)
+        graph.replay()
+        e1.record(cur)
+        torch.cuda.synchronize()
+        reps = max(3, min(400, int(300.0 / max(e0.elapsed_time(e1), 1e-3))))  # about 0.3 s timed
+        with Clocks(dev) as clk:
+            clk.wait_first()
+            torch.cuda.synchronize()
+            e0.record(cur)
+            for _ in range(reps):
+                graph.replay()
+            e1.record(cur)
+            torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / (reps * NLX)
+        del graph
+        sel = torch.zeros((NLX, T * K_USED), dtype=torch.int64, device="cuda")
+        sel_w = torch.zeros((T * K_USED,), device="cuda")
+        for l in range(NLX):
+            m.layer_dev(l, normed[l].data_ptr(), T, x.data_ptr(), {"sel_id": sel[l].data_ptr(), "sel_w": sel_w.data_ptr()},
+                        stream=torch.cuda.current_stream().cuda_stream)
+        torch.cuda.synchronize()
+        m.check()
+        U = float(np.mean([len(np.unique(r)) for r in sel.cpu().numpy()]))
+        nbytes = U * bytes_per_expert(gate, down) + E * gb.row_bytes(gb.BF16, H) + 2 * T * H * 4
+        flops = 2.0 * T * K_USED * 3 * H * F + 2.0 * T * E * H
+        kname, nl = m.kernel_name(T), m.launches(T)
+        m.close()
+        entry = {"value": T / (ms / 1000.0), "unit": "tokens/s", "tokens_per_step": T, "ms_per_step": ms,
+                 "steps": reps * NLX, "warmup": 3 * NLX + 3, "gate": gname, "down": dname, "zipf_router_bias": zipf,
+                 "kernel": kname or f"{nl} kernels a call", "gpu_launches_per_step": nl,
+                 "roofline": {"bound": "hbm", "achieved": nbytes / (ms / 1000.0) / 1e9, "peak": peak, "unit": "GB/s",
+                              "frac": nbytes / (ms / 1000.0) / 1e9 / peak, "peak_kind": peak_kind,
+                              "algorithmic_bytes": nbytes, "distinct_experts": U, "traffic": None,
+                              "useful_tflops": flops / (ms / 1000.0) / 1e12},
+                 "clocks": clk.summary()}
+        if cpu_seconds > 0:
+            try:
+                lay = dict(lays[0])
+                lay["router"] = routers[0]
+                entry["cpu_baseline"] = cpu_reference(args, gate, down, cpu_seconds, tokens=T, bias=bias,
+                                                      names=(gname, dname), lay=lay)
+            except Exception as exc:  # the prebuilt reference is missing on this box
+                entry["cpu_baseline"] = {"value": None, "unit": "tokens/s", "cores": 0, "kind": "reference",
+                                         "sample": f"unavailable: {exc}"}
+        out[key] = entry
+    return out
 
 
 def run_ours(args, rank, world, dist):
@@ -548,6 +658,9 @@ def run_ours(args, rank, world, dist):
     prefill = None
     if world == 1 and args.prefill_tokens > 0:
         prefill = run_prefill(args, dev, 0 if args.no_cpu_baseline else args.cpu_seconds)
+    extra = None
+    if world == 1 and not args.no_extra:
+        extra = run_extra(args, dev, 0 if args.no_cpu_baseline else args.extra_cpu_seconds)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
@@ -575,7 +688,7 @@ def run_ours(args, rank, world, dist):
                                "multikernel_zone_ms": {z: zone_ms[z] for z in ("router", "gate_up", "act_prep", "down")},
                                "multikernel_ms": layer_ms},
             "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches * steps, "clocks": clk.summary(),
-            "prefill": prefill,
+            "prefill": prefill, "configs": extra,
             "timing": f"CUDA graphs of {NL} layer calls replayed (+ a graph of the last {tail_n}); zones from graphs "
                       f"of parts 0..z"}
     return line
