@@ -65,15 +65,17 @@ def _check(got, want, tag):
         assert err.max() <= REL, (tag, key, float(err.max()), int(err.argmax()))
 
 
-def test_prefill_small_shape_against_oracle(cuda, oracle):
+@pytest.mark.parametrize("dt", [gb.Q8_0, gb.Q6_K])
+def test_prefill_small_shape_against_oracle(cuda, oracle, dt):
+    """a small shape against the oracle, Q8_0 gate/up with a Q8_0 or a Q6_K down (the Q6L converter)"""
     from trochilus_b200.moe import GpuMoe
     E, k, H, F, T = 16, 4, 512, 256, 300
-    lay = gb.make_layer(4242, E, H, F, gb.Q8_0, gb.Q8_0, gb.F32, mode="random")
+    lay = gb.make_layer(4242, E, H, F, gb.Q8_0, dt, gb.F32, mode="random")
     bias = gb.zipf_bias(5, E)
-    d, keep = make_desc(lay, H, F, k, 0, gb.F32, gb.Q8_0, gb.Q8_0, bias)
-    m = GpuMoe(1, E, k, H, F, gb.F32, gb.Q8_0, gb.Q8_0, max_tokens=T)
+    d, keep = make_desc(lay, H, F, k, 0, gb.F32, gb.Q8_0, dt, bias)
+    m = GpuMoe(1, E, k, H, F, gb.F32, gb.Q8_0, dt, max_tokens=T)
     m.set_layer(0, lay, bias)
-    assert m.launches(T) == 7  # the tensor-core road is the default for long Q8_0 passes
+    assert m.launches(T) == 7  # the tensor-core road is the default for long passes
     rng = np.random.default_rng(7)
     normed = rng.normal(size=(T, H)).astype(np.float32)
     x = rng.normal(size=(T, H)).astype(np.float32)
@@ -87,16 +89,18 @@ def test_prefill_small_shape_against_oracle(cuda, oracle):
     m.close()
 
 
-@pytest.mark.parametrize("T", [256, 1000, 2048])
-def test_prefill_olmoe_shape_against_exact_road(cuda, T):
+@pytest.mark.parametrize("gt,dt,T", [(gb.Q8_0, gb.Q8_0, 256), (gb.Q8_0, gb.Q8_0, 1000), (gb.Q8_0, gb.Q8_0, 2048),
+                                     (gb.Q4_K, gb.Q6_K, 256), (gb.Q4_K, gb.Q6_K, 512), (gb.Q4_K, gb.Q4_K, 512)])
+def test_prefill_olmoe_shape_against_exact_road(cuda, gt, dt, T):
     """OLMoE shape with Zipf-skewed routing (experts from one row to several 128-row tiles); the reference result is
-    the exact road on the GPU, itself bit for bit the oracle's (test_gpu_layer). T = 2048 is the benched prefill
-    call (configs[2]'s layer: Q8_0 gate/up and down, BF16 router)."""
+    the exact road on the GPU, itself bit for bit the oracle's (test_gpu_layer). T = 2048 Q8_0 is the benched
+    prefill call (configs[2]'s layer: Q8_0 gate/up and down, BF16 router); Q4_K / Q6_K is configs[1]'s Q4_K_M
+    prompt pass, Q4_K / Q4_K configs[3]'s all-Q4_K pass."""
     from trochilus_b200.moe import GpuMoe
     E, k, H, F = 64, 8, 2048, 1024
-    lay = gb.make_layer(77 + T, E, H, F, gb.Q8_0, gb.Q8_0, gb.BF16, mode="random")
+    lay = gb.make_layer(77 + T + gt + dt, E, H, F, gt, dt, gb.BF16, mode="random")
     bias = gb.zipf_bias(9, E)
-    m = GpuMoe(1, E, k, H, F, gb.BF16, gb.Q8_0, gb.Q8_0, max_tokens=T)
+    m = GpuMoe(1, E, k, H, F, gb.BF16, gt, dt, max_tokens=T)
     m.set_layer(0, lay, bias)
     rng = np.random.default_rng(T)
     normed = rng.normal(size=(T, H)).astype(np.float32)
@@ -111,10 +115,14 @@ def test_prefill_olmoe_shape_against_exact_road(cuda, T):
     m.close()
 
 
-def test_set_prefill_refused_without_q8_weights(cuda):
+def test_set_prefill_on_a_q4_k_m_context(cuda):
+    """Q4_K_M contexts have the tensor-core road too: the threshold moves it, a negative one is refused"""
     from trochilus_b200.moe import GpuMoe
-    m = GpuMoe(1, 64, 8, 2048, 1024, gb.BF16, gb.Q4_K, gb.Q6_K, max_tokens=4)
+    m = GpuMoe(1, 64, 8, 2048, 1024, gb.BF16, gb.Q4_K, gb.Q6_K, max_tokens=512)
     m.set_prefill(0)
-    with pytest.raises(RuntimeError, match="tensor-core road"):
-        m.set_prefill(256)
+    assert m.launches(512) != 7
+    m.set_prefill(256)
+    assert m.launches(512) == 7 and m.launches(255) != 7
+    with pytest.raises(RuntimeError):
+        m.set_prefill(-1)
     m.close()

@@ -105,8 +105,11 @@ struct WorkLayout {
 };
 
 // carve the workspace of one context (every piece 256-byte aligned)
-// whether a context can take the tensor-core road for long passes (Q8_0 gate/up and down)
-bool prefill_capable(const tr_gpu_moe_config &c) { return c.gate_type == TRX_Q8_0 && c.down_type == TRX_Q8_0; }
+// whether a context can take the tensor-core road for long passes: its converters dequantise Q8_0, Q4_K and Q6_K
+bool prefill_capable(const tr_gpu_moe_config &c) {
+    auto ok = [](int t) { return t == TRX_Q8_0 || t == TRX_Q4_K || t == TRX_Q6_K; };
+    return ok(c.gate_type) && ok(c.down_type);
+}
 
 WorkLayout work_layout(const tr_gpu_moe_config &c) {
     const int64_t T = c.max_tokens, E = c.n_expert, k = c.n_used, H = c.n_embd, F = c.n_ff, R = T * k;
@@ -453,14 +456,26 @@ static bool encode_map(CUtensorMap *map, float *base, int64_t rows, int64_t cols
     return true;
 }
 
+// the tensor-core GEMM for gate/up or down over weights of the given type
+typedef void (*PfGemmFn)(const CUtensorMap, const CUtensorMap, TrxPfArgs);
+static PfGemmFn pf_gemm_fn(bool gateup, int type) {
+    if (gateup)
+        return type == TRX_Q4_K ? trx_k_pf_gemm<true, TRX_Q4_K>
+               : type == TRX_Q6_K ? trx_k_pf_gemm<true, TRX_Q6_K>
+                                  : trx_k_pf_gemm<true, TRX_Q8_0>;
+    return type == TRX_Q4_K ? trx_k_pf_gemm<false, TRX_Q4_K>
+           : type == TRX_Q6_K ? trx_k_pf_gemm<false, TRX_Q6_K>
+                              : trx_k_pf_gemm<false, TRX_Q8_0>;
+}
+
 // the tensor-core road: its kernels' shared memory and the A operands' tensor maps (the h planes reuse the h and
 // hq regions, which the Q8_0 roads of the other kernels leave free during a prefill call)
 static bool plan_prefill(tr_gpu_moe *m) {
     const tr_gpu_moe_config &c = m->cfg;
     const int64_t R = c.max_tokens * c.n_used;
-    if (!ck(cudaFuncSetAttribute(trx_k_pf_gemm<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, TRX_PF_SMEM),
+    if (!ck(cudaFuncSetAttribute(pf_gemm_fn(true, c.gate_type), cudaFuncAttributeMaxDynamicSharedMemorySize, TRX_PF_SMEM),
             "smem prefill") ||
-        !ck(cudaFuncSetAttribute(trx_k_pf_gemm<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, TRX_PF_SMEM),
+        !ck(cudaFuncSetAttribute(pf_gemm_fn(false, c.down_type), cudaFuncAttributeMaxDynamicSharedMemorySize, TRX_PF_SMEM),
             "smem prefill"))
         return false;
     if (!encode_map(&m->pf_map_x[0], m->pf_xhi, R, c.n_embd) || !encode_map(&m->pf_map_x[1], m->pf_xlo, R, c.n_embd) ||
@@ -780,8 +795,8 @@ static int launch_prefill(tr_gpu_moe *m, const TrxLayer &L, const TrxShape &S, c
     a.N = F;
     a.out_hi = w.h;
     a.out_lo = reinterpret_cast<float *>(w.hq);
-    trx_k_pf_gemm<true><<<dim3((unsigned)(F / 128), mtiles), TRX_PF_THREADS, TRX_PF_SMEM, st>>>(m->pf_map_x[0],
-                                                                                               m->pf_map_x[1], a);
+    pf_gemm_fn(true, L.gate_type)<<<dim3((unsigned)(F / 128), mtiles), TRX_PF_THREADS, TRX_PF_SMEM, st>>>(
+        m->pf_map_x[0], m->pf_map_x[1], a);
     a.wa = L.down;
     a.wb = nullptr;
     a.wa_mb = L.down_mb;
@@ -790,8 +805,8 @@ static int launch_prefill(tr_gpu_moe *m, const TrxLayer &L, const TrxShape &S, c
     a.N = H;
     a.out_hi = w.h3;
     a.out_lo = nullptr;
-    trx_k_pf_gemm<false><<<dim3((unsigned)(H / TRX_PF_BN), mtiles), TRX_PF_THREADS, TRX_PF_SMEM, st>>>(m->pf_map_h[0],
-                                                                                                      m->pf_map_h[1], a);
+    pf_gemm_fn(false, L.down_type)<<<dim3((unsigned)(H / TRX_PF_BN), mtiles), TRX_PF_THREADS, TRX_PF_SMEM, st>>>(
+        m->pf_map_h[0], m->pf_map_h[1], a);
     const int64_t n = (int64_t)T * H;
     trx_k_pf_combine<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(w.sel_w, w.place, w.h3, T, S.k, H, d_x, ffn_out);
     return ck(cudaGetLastError(), "prefill launch") ? 0 : -1;
@@ -989,7 +1004,7 @@ extern "C" int tr_gpu_moe_set_prefill(tr_gpu_moe *m, int64_t min_tokens) {
     }
     if (!m->pf_ok) {
         if (min_tokens == 0) return 0;
-        set_err("this context has no tensor-core road (it needs Q8_0 gate/up and down weights)");
+        set_err("this context has no tensor-core road (its weight types have no converter)");
         return -1;
     }
     m->pf_min = min_tokens;

@@ -213,7 +213,7 @@ __device__ __forceinline__ bool trx_pf_tile(const int32_t *offsets, const int32_
 }
 
 // ---- the grouped GEMM: grid (N / tile outputs, m-tiles upper bound) ----
-template <bool GATEUP>
+template <bool GATEUP, int WT>
 __global__ void __launch_bounds__(TRX_PF_THREADS, 1)
     trx_k_pf_gemm(const __grid_constant__ CUtensorMap map_hi, const __grid_constant__ CUtensorMap map_lo, TrxPfArgs a) {
     extern __shared__ __align__(1024) uint8_t pf_smem_raw[];
@@ -311,38 +311,93 @@ __global__ void __launch_bounds__(TRX_PF_THREADS, 1)
     } else {
         // ---- converters: this thread's B row r = tid (gate/up: r < 128 the gate row of output 128 n + r, r >= 128
         // the up row of output 128 n + r - 128; down: row 256 n + r), dequantised k-step by k-step into the swizzled
-        // hi/lo tiles
-        const int64_t rb = (int64_t)(K / 256) * 272;
+        // hi/lo tiles. K-step j of a 256-block holds Q8L positions 32 j .. 32 j + 31: position 16 l + m is column
+        // l + 16 m, the column of lane l's element m in the 16-lane contract (the Q8L and Q6L storage order).
+        const int nsb = K / 256;
+        const int64_t rb = (int64_t)nsb * (WT == TRX_Q8_0 ? 272 : WT == TRX_Q4_K ? 144 : 208);
         const int r = tid;
-        const uint8_t *rp = GATEUP ? (r < 128 ? a.wa + e * a.wa_mb : a.wb + e * a.wb_mb) + trx_q8l_col(128 * n + (r & 127)) * rb
-                                   : a.wa + e * a.wa_mb + (int64_t)(256 * n + r) * rb;
-        float d[8];
-        uint4 qa, qb; // this k-step's 32 quants
+        const uint8_t *mat = GATEUP && r >= 128 ? a.wb + e * a.wb_mb : a.wa + e * a.wa_mb;
+        const int row = GATEUP ? trx_q8l_col(128 * n + (r & 127)) : 256 * n + r;
+        const uint8_t *rp = mat + (int64_t)row * rb;
+        // the block's scales: Q8_0 the 8 f16 d of its 32-column groups; Q4_K fl(d sc_j) (0..7) and fl(dmin m_j)
+        // (8..15) of its 8 sub-blocks; Q6_K fl(d sc_m) of its 16 sub-blocks (all exact)
+        float sc[16];
+        uint4 qa, qb; // this k-step's quant bytes
         auto load_q = [&](int ks) {
-            const int64_t o = (int64_t)(ks >> 3) * 272 + 16 + 32 * (ks & 7);
-            qa = __ldg(reinterpret_cast<const uint4 *>(rp + o));
-            qb = __ldg(reinterpret_cast<const uint4 *>(rp + o + 16));
-        };
-        auto load_d = [&](int chunk) {
-            const uint4 u = __ldg(reinterpret_cast<const uint4 *>(rp + (int64_t)chunk * 272));
-            const uint32_t wd[4] = {u.x, u.y, u.z, u.w};
+            const int j = ks & 7, blk = ks >> 3;
+            if (WT == TRX_Q8_0) {
+                const int64_t o = (int64_t)blk * 272 + 16 + 32 * j;
+                qa = __ldg(reinterpret_cast<const uint4 *>(rp + o));
+                qb = __ldg(reinterpret_cast<const uint4 *>(rp + o + 16));
+            } else if (WT == TRX_Q4_K) {
+                // columns 2 j + t + 16 m (t = 0, 1): byte 32 (m >> 2) + 16 (m & 1) + 2 j + t of the block's quants,
+                // the high nibble when (m >> 1) & 1; halfword w = 2 (m >> 2) + (m & 1) holds both t
+                const uint8_t *q = rp + (int64_t)blk * 144 + 16 + 2 * j;
+                uint32_t hw[8];
 #pragma unroll
-            for (int b = 0; b < 8; b++) d[b] = trx_half((uint16_t)(wd[b >> 1] >> (16 * (b & 1))));
+                for (int w2 = 0; w2 < 8; w2++) hw[w2] = __ldg(reinterpret_cast<const uint16_t *>(q + 32 * (w2 >> 1) + 16 * (w2 & 1)));
+                qa = make_uint4(hw[0] | hw[1] << 16, hw[2] | hw[3] << 16, hw[4] | hw[5] << 16, hw[6] | hw[7] << 16);
+            } else { // Q6L: lanes 2 j and 2 j + 1's low nibbles (8 bytes each) and high bit pairs (4 bytes each)
+                qa = __ldg(reinterpret_cast<const uint4 *>(rp + 128 * blk + 16 * j));
+                const uint2 h = __ldg(reinterpret_cast<const uint2 *>(rp + 128 * nsb + 64 * blk + 8 * j));
+                qb = make_uint4(h.x, h.y, 0u, 0u);
+            }
         };
-        // the row's 32 weights into tile row r: position b of the k-step has scale (b % 16) / 2
+        auto load_d = [&](int blk) {
+            if (WT == TRX_Q8_0) {
+                const uint4 u = __ldg(reinterpret_cast<const uint4 *>(rp + (int64_t)blk * 272));
+                const uint32_t wd[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+                for (int b = 0; b < 8; b++) sc[b] = trx_half((uint16_t)(wd[b >> 1] >> (16 * (b & 1))));
+            } else if (WT == TRX_Q4_K) {
+                const uint4 hdr = __ldg(reinterpret_cast<const uint4 *>(rp + (int64_t)blk * 144));
+                const float d = trx_half((uint16_t)(hdr.x & 0xffffu)), dmin = trx_half((uint16_t)(hdr.x >> 16));
+                const uint32_t sw[3] = {hdr.y, hdr.z, hdr.w}; // the 12 packed scale bytes
+                auto byte = [&](int i) { return (sw[i >> 2] >> (8 * (i & 3))) & 255u; };
+#pragma unroll
+                for (int jj = 0; jj < 8; jj++) { // Q4_K's 6-bit scale and min of sub-block jj
+                    const uint32_t scj = jj < 4 ? byte(jj) & 63u : (byte(jj + 4) & 15u) | ((byte(jj - 4) >> 6) << 4);
+                    const uint32_t mj = jj < 4 ? byte(jj + 4) & 63u : (byte(jj + 4) >> 4) | ((byte(jj) >> 6) << 4);
+                    sc[jj] = __fmul_rn(d, (float)scj);
+                    sc[8 + jj] = __fmul_rn(dmin, (float)mj);
+                }
+            } else {
+                const float d = trx_half(__ldg(reinterpret_cast<const uint16_t *>(mat + (int64_t)a.N * rb) +
+                                               (int64_t)row * nsb + blk)); // (the d values follow the N rows)
+                const uint4 u = __ldg(reinterpret_cast<const uint4 *>(rp + 192 * nsb + 16 * blk));
+                const uint32_t sw[4] = {u.x ^ 0x80808080u, u.y ^ 0x80808080u, u.z ^ 0x80808080u, u.w ^ 0x80808080u};
+#pragma unroll
+                for (int m = 0; m < 16; m++) sc[m] = __fmul_rn(d, trx_s8_to_f32(sw[m >> 2], m & 3));
+            }
+        };
+        // the weight at position i of the k-step (exact, but Q4_K's d sc q - dmin m, rounded once)
+        auto weight = [&](const uint4 ca, const uint4 cb, int i) -> float {
+            const uint32_t wa[4] = {ca.x, ca.y, ca.z, ca.w};
+            if (WT == TRX_Q8_0) {
+                const uint32_t qw = i < 16 ? wa[i >> 2] : (i < 24 ? (i < 20 ? cb.x : cb.y) : (i < 28 ? cb.z : cb.w));
+                return __fmul_rn(sc[(i & 15) >> 1], trx_s8_to_f32(qw ^ 0x80808080u, i & 3)); // 19 bits at most
+            } else if (WT == TRX_Q4_K) {
+                const int t = i >> 4, m = i & 15, w2 = 2 * (m >> 2) + (m & 1);
+                const uint32_t q = (wa[w2 >> 1] >> (16 * (w2 & 1) + 8 * t + 4 * ((m >> 1) & 1))) & 15u;
+                const float qf = __fsub_rn(__uint_as_float(0x4b000000u | q), 8388608.0f); // exact
+                return __fsub_rn(__fmul_rn(sc[m >> 1], qf), sc[8 + (m >> 1)]);
+            } else {
+                const int lh = i >> 4, m = i & 15;
+                uint32_t q4[4];
+                trx_q6l_quants(make_uint2(wa[2 * lh], wa[2 * lh + 1]), lh ? cb.y : cb.x, q4);
+                const uint32_t q = (q4[m >> 2] >> (8 * (m & 3))) & 255u;
+                const float qf = __fsub_rn(__uint_as_float(0x4b000000u | q), 8388640.0f); // q - 32, exact
+                return __fmul_rn(sc[m], qf); // exact
+            }
+        };
+        // the row's 32 weights into tile row r
         auto put_row = [&](int s, uint4 ca, uint4 cb) {
-            const uint32_t qw[8] = {ca.x ^ 0x80808080u, ca.y ^ 0x80808080u, ca.z ^ 0x80808080u, ca.w ^ 0x80808080u,
-                                    cb.x ^ 0x80808080u, cb.y ^ 0x80808080u, cb.z ^ 0x80808080u, cb.w ^ 0x80808080u};
             uint8_t *th = b_hi(s) + (r >> 3) * 1024 + (r & 7) * 128, *tlo = b_lo(s) + (r >> 3) * 1024 + (r & 7) * 128;
 #pragma unroll
             for (int c = 0; c < 8; c++) { // 16-byte chunk c holds positions 4 c .. 4 c + 3
                 float hv[4], lv[4];
 #pragma unroll
-                for (int i = 0; i < 4; i++) {
-                    const int b = 4 * c + i;
-                    const float wv = __fmul_rn(d[(b & 15) >> 1], trx_s8_to_f32(qw[c], i)); // exact: 19 bits at most
-                    trx_split(wv, hv[i], lv[i]);
-                }
+                for (int i = 0; i < 4; i++) trx_split(weight(ca, cb, 4 * c + i), hv[i], lv[i]);
                 const int sw = (c ^ (r & 7)) << 4;
                 *reinterpret_cast<float4 *>(th + sw) = make_float4(hv[0], hv[1], hv[2], hv[3]);
                 *reinterpret_cast<float4 *>(tlo + sw) = make_float4(lv[0], lv[1], lv[2], lv[3]);
