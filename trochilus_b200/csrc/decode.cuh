@@ -18,8 +18,8 @@
 //            once, warps 0-3 stage the token's row in shared memory meanwhile (or, with the ffn_norm in the hook,
 //            every CTA normalises the residual row there first), warp 0 forms logit e (the 16-lane contract) and
 //            publishes it tagged; warps 4-11 prepare the row for Q4_K's integer definition (all CTAs).
-//  routing   every CTA, once it holds all E tagged logits, routes the token (softmax, top-k, ids sorted) and its
-//            trivial sort in shared memory.
+//  routing   every CTA, once it holds all E tagged logits, routes the token (softmax, top-k, ids sorted) in shared
+//            memory; CTA 0's warp 14 forms the dispatch permutation when the caller asks for it.
 //  experts   a CTA owns rows [ga, gb) of every selected expert's gate and up matrices and rows [da, db) of every
 //            selected expert's down matrix. Each of 14 consumer warps streams its own units through a ring of
 //            TRX_DC_NS shared-memory slots with 1-D TMA bulk copies (no multicast), one mbarrier a slot, so it waits
@@ -269,10 +269,6 @@ __global__ void __launch_bounds__(TRX_DC_THREADS, 1)
         trx_route_token<true>(s_logit, E, k, S.norm_topk, lane, sp, s_selid, s_selw);
         __syncwarp();
         const bool out = c == 0;
-        trx_sort_single(s_selid, E, k,
-                        TrxSortOut{s_off, s_act, &s_nact, s_place, s_xmap, out ? w.out_offsets : nullptr,
-                                   out ? w.out_place : nullptr},
-                        lane);
         if (out && w.out_sel_id && lane < k) {
             w.out_sel_id[lane] = s_selid[lane];
             w.out_sel_w[lane] = s_selw[lane];
@@ -282,6 +278,12 @@ __global__ void __launch_bounds__(TRX_DC_THREADS, 1)
     TRX_TRACE(60);
 
     const uint64_t pol = trx_policy_evict_first(); // the weights are read once a call
+    if (warp == TRX_DC_CWARPS && c == 0 && (w.out_offsets || w.out_place)) {
+        // the dispatch permutation, when asked for: the ids are sorted already, so only CTA 0 forms it, off the
+        // experts' path (the trivial sort, Trochilus's counting sort for one token)
+        trx_sort_single(s_selid, E, k, TrxSortOut{s_off, s_act, &s_nact, s_place, s_xmap, w.out_offsets, w.out_place},
+                        lane);
+    }
     if (warp == TRX_DC_CWARPS) {
         // the CTA's share of every selected expert into L2 at once (gate rows, up rows, down rows, the down rows' d
         // values: lane 4 i + part), so that HBM streams the whole call's weights while the rings start; the rings'

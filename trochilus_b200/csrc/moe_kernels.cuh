@@ -117,8 +117,8 @@ __device__ __noinline__ void trx_route_token(const float *__restrict__ logits, i
     for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
     const float x0 = __shfl_sync(0xffffffffu, v0, 0);
     if (x0 != x0) m = x0;
-    const float e0 = ok0 ? trx_expf(__fsub_rn(v0, m)) : 0.0f;
-    const float e1 = ok1 ? trx_expf(__fsub_rn(v1, m)) : 0.0f;
+    const float2 ee = trx_expf2(ok0 ? __fsub_rn(v0, m) : -1.0f, ok1 ? __fsub_rn(v1, m) : -1.0f);
+    const float e0 = ok0 ? ee.x : 0.0f, e1 = ok1 ? ee.y : 0.0f;
     // 16-lane sum: lane l (< 16) adds elements l, l+16, l+32, l+48 in order from +0 (absent ones are +0)
     const float b = __shfl_sync(0xffffffffu, e0, (lane & 15) + 16);
     const float d = __shfl_sync(0xffffffffu, e1, (lane & 15) + 16);
