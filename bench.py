@@ -178,7 +178,7 @@ def run_reference(args, rank, world):
     if rank != 0:
         return
     steps = max(args.steps // 20, 20)
-    warm = max(args.warmup, 3)
+    warm = max(args.warmup, 50)  # the reference's caches and thread pool settled (a call is well under a ms)
     r = cpu_reference(args, gate, down, None, steps=steps, warmup=warm)
     line = {"impl": "reference", "metric": METRIC, "value": r["value"], "unit": "tokens/s", "n_gpus": world,
             "steps": steps, "warmup": warm, "ms_per_step": 1000.0 * args.tokens / r["value"],

@@ -236,11 +236,12 @@ TRMOE_API int tr_gpu_moe_check(tr_gpu_moe *m);
 TRMOE_API int tr_gpu_moe_trace(tr_gpu_moe *m, int on);
 TRMOE_API int tr_gpu_moe_trace_read(tr_gpu_moe *m, uint64_t *slots, int64_t n);
 
-/* How many kernels one tr_gpu_moe_layer_dev call launches for n_tok tokens. */
+/* How many kernels one tr_gpu_moe_layer_dev call launches for n_tok tokens (without dispatch outputs). */
 TRMOE_API int tr_gpu_moe_launches(const tr_gpu_moe *m, int64_t n_tok);
 
 /* The kernel one tr_gpu_moe_layer_dev call of n_tok tokens runs when it is a single kernel: "trx_k_dec1" (the
- * one-token decode kernel), "trx_k_layer" (the fused layer kernel); "" when the call takes several kernels. */
+ * one-token decode kernel; also for calls of up to 32 tokens on its shapes, which launch it once a token),
+ * "trx_k_layer" (the fused layer kernel); "" when the call takes several different kernels. */
 TRMOE_API const char *tr_gpu_moe_kernel_name(const tr_gpu_moe *m, int64_t n_tok);
 
 /* The message of this thread's last failure ("" if none). */

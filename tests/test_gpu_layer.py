@@ -80,6 +80,50 @@ def test_layer_matches_oracle_fresh_seeds(cuda, oracle, gt, dt, rt):
     m.close()
 
 
+@pytest.mark.parametrize("T", [2, 8, 32])
+def test_short_calls_one_launch_a_token(cuda, oracle, T):
+    """Q4_K_M calls of 2..32 tokens without the dispatch permutation run the one-token kernel once a token: every
+    output bit for bit the oracle's on the device road, the host road with copies and (up to 16 tokens) the
+    zero-copy host road"""
+    torch = cuda
+    from trochilus_b200.moe import GpuMoe
+    lay = gb.make_layer(31 + T, 64, 2048, 1024, gb.Q4_K, gb.Q6_K, gb.BF16, mode="random")
+    bias = gb.zipf_bias(4, 64)
+    d, keep = make_desc(lay, 2048, 1024, 8, 0, gb.BF16, gb.Q4_K, gb.Q6_K, bias)
+    m = GpuMoe(1, 64, 8, 2048, 1024, gb.BF16, gb.Q4_K, gb.Q6_K, max_tokens=T)
+    m.set_layer(0, lay, bias)
+    assert m.launches(T) == T and m.kernel_name(T) == "trx_k_dec1"
+    rng = np.random.default_rng(T)
+    normed = rng.normal(size=(T, 2048)).astype(np.float32)
+    x = rng.normal(size=(T, 2048)).astype(np.float32)
+    want = oracle.moe_layer(d, normed, x)
+    for rep in range(2):
+        dn = torch.from_numpy(normed).cuda()
+        dx = torch.from_numpy(x.copy()).cuda()
+        o = {"logits": torch.full((T, 64), float("nan"), device="cuda"),
+             "sel_id": torch.full((T * 8,), -1, dtype=torch.int64, device="cuda"),
+             "sel_w": torch.full((T * 8,), float("nan"), device="cuda"),
+             "ffn_out": torch.full((T, 2048), float("nan"), device="cuda")}
+        m.layer_dev(0, dn.data_ptr(), T, dx.data_ptr(), {kk: v.data_ptr() for kk, v in o.items()},
+                    stream=torch.cuda.current_stream().cuda_stream)
+        torch.cuda.synchronize()
+        m.check()
+        got = {kk: v.cpu().numpy() for kk, v in o.items()}
+        assert same_bits(got["logits"], want["logits"]), rep
+        assert same_bits(got["sel_id"].reshape(T, 8), want["sel_id"]), rep
+        assert same_bits(got["sel_w"].reshape(T, 8), want["sel_w"]), rep
+        assert same_bits(got["ffn_out"], want["ffn_out"]), rep
+        assert same_bits(dx.cpu().numpy(), want["x"]), rep
+    xo = x.copy()
+    sid, sw = m.layer(0, normed, xo)
+    assert same_bits(xo, want["x"]) and same_bits(sid, want["sel_id"]) and same_bits(sw, want["sel_w"])
+    hn = torch.from_numpy(normed.copy()).pin_memory()
+    hx = torch.from_numpy(x.copy()).pin_memory()
+    m.layer_ptrs(0, hn.data_ptr(), T, hx.data_ptr(), host=True)
+    assert same_bits(hx.numpy(), want["x"])
+    m.close()
+
+
 def test_many_layers_one_context(cuda, oracle):
     """layers set independently, called in any order, each its own weights"""
     c = dict(E=64, k=8, H=2048, F=1024, router=gb.BF16, gate=gb.Q4_K, down=gb.Q6_K, norm_topk=0, T=3)

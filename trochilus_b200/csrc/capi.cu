@@ -731,18 +731,29 @@ static void reset_counters(tr_gpu_moe *m, cudaStream_t st) {
     stream_wait(st);
 }
 
+// whether a plain call of n_tok tokens (no dispatch outputs) runs the one-token kernel once a token
+static bool takes_dec1seq(const tr_gpu_moe *m, int64_t n_tok) {
+    const tr_gpu_moe_config &c = m->cfg;
+    return n_tok > 1 && n_tok <= TRX_DC_SEQ_MAX && m->dec1_ok &&
+           trx_dec1_takes(c.gate_type, c.down_type, c.router_type, (int)c.n_embd, (int)c.n_ff, (int)c.n_expert,
+                          (int)c.n_used, 1, m->grid_fused, false);
+}
+
 extern "C" int tr_gpu_moe_launches(const tr_gpu_moe *m, int64_t n_tok) {
     if (m == nullptr) return 0;
     if (m->pf_ok && m->pf_min > 0 && n_tok >= m->pf_min && !m->prof) return 7; // route 3, gather, 2 GEMMs, combine
     int sg, sd;
     if (m->fused_ok && n_tok <= TRX_ROUTE_FUSED_MAX && m->cfg.n_expert + n_tok <= m->grid_fused && !m->prof &&
         fused_stages(m, (int)n_tok, &sg, &sd))
-        return 1;
+        return takes_dec1seq(m, n_tok) ? (int)n_tok : 1;
     return (n_tok <= TRX_ROUTE_FUSED_MAX ? 1 : 4) + 2 + (m->cfg.down_type == TRX_Q4_K ? 1 : 0);
 }
 
 extern "C" const char *tr_gpu_moe_kernel_name(const tr_gpu_moe *m, int64_t n_tok) {
-    if (m == nullptr || tr_gpu_moe_launches(m, n_tok) != 1) return "";
+    if (m == nullptr) return "";
+    const int nl = tr_gpu_moe_launches(m, n_tok);
+    if (nl == n_tok && n_tok > 1 && takes_dec1seq(m, n_tok)) return "trx_k_dec1";
+    if (nl != 1) return "";
     const tr_gpu_moe_config &c = m->cfg;
     if (m->dec1_ok && trx_dec1_takes(c.gate_type, c.down_type, c.router_type, (int)c.n_embd, (int)c.n_ff,
                                      (int)c.n_expert, (int)c.n_used, (int)n_tok, m->grid_fused, false))
@@ -939,9 +950,16 @@ static int launch_layer(tr_gpu_moe *m, int64_t layer, const float *d_normed, int
     // one token on the one-token kernel's shapes: decode.cuh
     const bool dec1 = fused && m->dec1_ok && !S.ext &&
                       trx_dec1_takes(c.gate_type, c.down_type, c.router_type, S.H, S.F, S.E, S.k, T, m->grid_fused, false);
+    // a few tokens on those shapes: one launch of it a token. Each token's arithmetic is the one-token call's, so
+    // the outputs are the same bits; the fused kernel costs about 40 us a token at T = 8 against its 24. Not when
+    // the call's dispatch permutation (offsets, place over every token) is asked for.
+    const bool dec1seq = fused && T > 1 && T <= TRX_DC_SEQ_MAX && m->dec1_ok && !S.ext && w.out_offsets == nullptr &&
+                         w.out_place == nullptr &&
+                         trx_dec1_takes(c.gate_type, c.down_type, c.router_type, S.H, S.F, S.E, S.k, 1, m->grid_fused,
+                                        false);
     if (norm_src) {
         // short fused calls normalise inside the kernel when the rows fit the stage area beside the router's staging
-        const bool inside = (dec1 && ((uintptr_t)norm_src & 15) == 0) ||
+        const bool inside = ((dec1 || dec1seq) && ((uintptr_t)norm_src & 15) == 0) ||
                             (fused && T <= TRX_FU_LOCAL_PREP && ((uintptr_t)norm_src & 15) == 0 &&
                              trx_fu_norm_off(T, S.H, E) + (size_t)T * S.H * 4 <=
                                  trx_fused_layout(c.gate_type, c.down_type, S.H, S.F, T, S.k, sg, sd, E, m->grid_fused).bars);
@@ -965,6 +983,22 @@ static int launch_layer(tr_gpu_moe *m, int64_t layer, const float *d_normed, int
         if (epoch_out) *epoch_out = epoch;
         if (dec1 && (!S.norm_in || ((uintptr_t)d_normed & 15) == 0))
             return launch_dec1(m, L, S, d_normed, w, d_x, ffn, epoch, st);
+        if (dec1seq && (!S.norm_in || ((uintptr_t)d_normed & 15) == 0)) {
+            const int64_t H = S.H;
+            for (int t = 0; t < T; t++) {
+                TrxWork wt = w;
+                wt.host_done = t == T - 1 ? done : nullptr; // the last launch posts the call's epoch
+                if (wt.out_logits) wt.out_logits += (int64_t)t * E;
+                if (wt.out_sel_id) {
+                    wt.out_sel_id += (int64_t)t * S.k;
+                    wt.out_sel_w += (int64_t)t * S.k;
+                }
+                if (wt.out_normed) wt.out_normed += t * H;
+                if (launch_dec1(m, L, S, d_normed + t * H, wt, d_x + t * H, ffn ? ffn + t * H : nullptr, epoch, st) != 0)
+                    return -1;
+            }
+            return 0;
+        }
         return launch_fused(m, L, S, d_normed, T, w, d_x, ffn, epoch, sg, sd, st, "fused layer launch");
     }
     mark(0);

@@ -55,6 +55,7 @@
 #define TRX_DC_DN 2       // down steps a warp
 #define TRX_DC_KMAX 8
 #define TRX_DC_GRID_MAX 256 // CTAs (the tagged logits: a row of E words for each)
+#define TRX_DC_SEQ_MAX 32   // calls of up to this many tokens run one launch a token (faster than the fused kernel)
 
 struct TrxDecPlan {
     uint32_t off_h, off_xq, total; // shared memory: h rows (k x F floats), the prepared token row, the whole
@@ -489,7 +490,8 @@ __global__ void __launch_bounds__(TRX_DC_THREADS, 1)
             sync->seq = tag;
             sync->finish = 0u;
             __threadfence();
-            trx_post_done(w.host_done, epoch);
+            // (a call of several tokens runs one launch a token and only the last posts: it reports any give-up)
+            trx_post_done(w.host_done, *(volatile int32_t *)w.err ? (epoch | 0x80000000u) : epoch);
         }
     }
 }
