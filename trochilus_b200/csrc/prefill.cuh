@@ -153,6 +153,12 @@ __device__ __forceinline__ void trx_split(float v, float &hi, float &lo) {
     lo = trx_tf32(__fsub_rn(v, hi));
 }
 
+// h = silu(g) u on the tensor road, which holds a 1e-5 bound rather than the reference's bits: the fast exponential
+// and division intrinsics (a few ulp) instead of the correctly rounded trx_expf and an IEEE division
+__device__ __forceinline__ float trx_pf_silu_mul(float g, float u) {
+    return __fmul_rn(__fdividef(g, __fadd_rn(1.0f, __expf(-g))), u);
+}
+
 // the Q8L position of column k within its 256-block, and back
 __host__ __device__ __forceinline__ int trx_q8l_pos(int k) { return (k & ~255) + 16 * (k & 15) + ((k >> 4) & 15); }
 __host__ __device__ __forceinline__ int trx_q8l_col(int pos) { return (pos & ~255) + ((pos >> 4) & 15) + 16 * (pos & 15); }
@@ -485,7 +491,7 @@ __global__ void __launch_bounds__(TRX_PF_THREADS, 1)
                         for (int i = 0; i < 32; i += 4) {
                             float hv[4], lv[4];
 #pragma unroll
-                            for (int j = 0; j < 4; j++) trx_split(trx_silu_mul(g[i + j], u[i + j]), hv[j], lv[j]);
+                            for (int j = 0; j < 4; j++) trx_split(trx_pf_silu_mul(g[i + j], u[i + j]), hv[j], lv[j]);
                             *reinterpret_cast<float4 *>(oh + i) = make_float4(hv[0], hv[1], hv[2], hv[3]);
                             *reinterpret_cast<float4 *>(ol + i) = make_float4(lv[0], lv[1], lv[2], lv[3]);
                         }
