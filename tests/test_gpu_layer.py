@@ -80,17 +80,19 @@ def test_layer_matches_oracle_fresh_seeds(cuda, oracle, gt, dt, rt):
     m.close()
 
 
-@pytest.mark.parametrize("T", [2, 8, 32])
-def test_short_calls_one_launch_a_token(cuda, oracle, T):
-    """Q4_K_M calls of 2..32 tokens without the dispatch permutation run the one-token kernel once a token: every
-    output bit for bit the oracle's on the device road, the host road with copies and (up to 16 tokens) the
+@pytest.mark.parametrize("gt,dt,rt,T", [(gb.Q4_K, gb.Q6_K, gb.BF16, 2), (gb.Q4_K, gb.Q6_K, gb.BF16, 8),
+                                        (gb.Q4_K, gb.Q6_K, gb.BF16, 32), (gb.Q8_0, gb.Q8_0, gb.F32, 1),
+                                        (gb.Q8_0, gb.Q8_0, gb.BF16, 8), (gb.Q8_0, gb.Q8_0, gb.F32, 32)])
+def test_short_calls_one_launch_a_token(cuda, oracle, gt, dt, rt, T):
+    """Q4_K_M and Q8_0 calls of 1..32 tokens without the dispatch permutation run the one-token kernel once a token:
+    every output bit for bit the oracle's on the device road, the host road with copies and (up to 16 tokens) the
     zero-copy host road"""
     torch = cuda
     from trochilus_b200.moe import GpuMoe
-    lay = gb.make_layer(31 + T, 64, 2048, 1024, gb.Q4_K, gb.Q6_K, gb.BF16, mode="random")
+    lay = gb.make_layer(31 + T + gt, 64, 2048, 1024, gt, dt, rt, mode="random")
     bias = gb.zipf_bias(4, 64)
-    d, keep = make_desc(lay, 2048, 1024, 8, 0, gb.BF16, gb.Q4_K, gb.Q6_K, bias)
-    m = GpuMoe(1, 64, 8, 2048, 1024, gb.BF16, gb.Q4_K, gb.Q6_K, max_tokens=T)
+    d, keep = make_desc(lay, 2048, 1024, 8, 0, rt, gt, dt, bias)
+    m = GpuMoe(1, 64, 8, 2048, 1024, rt, gt, dt, max_tokens=T)
     m.set_layer(0, lay, bias)
     assert m.launches(T) == T and m.kernel_name(T) == "trx_k_dec1"
     rng = np.random.default_rng(T)

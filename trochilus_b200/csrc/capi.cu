@@ -283,6 +283,14 @@ static LayerFn layer_fn(int gate_type, int down_type) {
 }
 
 // the fused kernel: the most shared memory a CTA may take, and a cooperative grid of one CTA per SM
+// the one-token kernel for a router type and a gate/up type (Q4_K: Q4_K_M's road, Q8_0: all Q8_0)
+typedef void (*Dec1Fn)(TrxLayer, TrxShape, const float *, TrxWork, TrxSync *, float *, float *, uint32_t, TrxDecPlan);
+static Dec1Fn dec1_fn(int router_type, int gate_type) {
+    if (gate_type == TRX_Q8_0)
+        return router_type == TRX_BF16 ? trx_k_dec1<TRX_BF16, TRX_Q8_0> : trx_k_dec1<TRX_F32, TRX_Q8_0>;
+    return router_type == TRX_BF16 ? trx_k_dec1<TRX_BF16, TRX_Q4_K> : trx_k_dec1<TRX_F32, TRX_Q4_K>;
+}
+
 static bool plan_fused(tr_gpu_moe *m) {
     const tr_gpu_moe_config &c = m->cfg;
     int coop = 0, occ = 0;
@@ -302,9 +310,9 @@ static bool plan_fused(tr_gpu_moe *m) {
     // the one-token kernel: its plan's shared memory, a CTA an SM
     if (m->fused_ok && trx_dec1_takes(c.gate_type, c.down_type, c.router_type, (int)c.n_embd, (int)c.n_ff,
                                       (int)c.n_expert, (int)c.n_used, 1, m->grid_fused, false)) {
-        const TrxDecPlan P = trx_dec_plan((int)c.n_embd, (int)c.n_ff, (int)c.n_used, m->grid_fused);
+        const TrxDecPlan P = trx_dec_plan(c.gate_type, (int)c.n_embd, (int)c.n_ff, (int)c.n_used, m->grid_fused);
         bool ok1 = true;
-        for (auto fn : {trx_k_dec1<TRX_F32>, trx_k_dec1<TRX_BF16>}) {
+        for (auto fn : {dec1_fn(TRX_F32, c.gate_type), dec1_fn(TRX_BF16, c.gate_type)}) {
             int occ1 = 0;
             cudaFuncAttributes fa1{};
             if (!ck(cudaFuncGetAttributes(&fa1, fn), "cudaFuncGetAttributes") ||
@@ -860,7 +868,7 @@ static int launch_fused(tr_gpu_moe *m, const TrxLayer &L, const TrxShape &S, con
 // the one-token decode kernel (decode.cuh): one cooperative launch, a CTA an SM
 static int launch_dec1(tr_gpu_moe *m, const TrxLayer &L, const TrxShape &S, const float *normed, const TrxWork &w,
                        float *x_io, float *ffn_out, uint32_t epoch, cudaStream_t st) {
-    const TrxDecPlan P = trx_dec_plan(S.H, S.F, S.k, m->grid_fused);
+    const TrxDecPlan P = trx_dec_plan(L.gate_type, S.H, S.F, S.k, m->grid_fused);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)m->grid_fused);
     cfg.blockDim = dim3(TRX_DC_THREADS);
@@ -875,7 +883,7 @@ static int launch_dec1(tr_gpu_moe *m, const TrxLayer &L, const TrxShape &S, cons
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = m->dec1_pdl ? 2 : 1;
-    auto fn = L.router_type == TRX_BF16 ? trx_k_dec1<TRX_BF16> : trx_k_dec1<TRX_F32>;
+    auto fn = dec1_fn(L.router_type, L.gate_type);
     cudaError_t e = cudaLaunchKernelEx(&cfg, fn, L, S, normed, w, m->sync, x_io, ffn_out, epoch, P);
     if (e != cudaSuccess && m->dec1_pdl) { // not taken together: cooperative alone from now on
         (void)cudaGetLastError();

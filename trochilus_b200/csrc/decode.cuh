@@ -17,14 +17,16 @@
 //  prologue  a helper warp initialises the barriers; in CTAs 0..E-1 warp 0 loads router row e into registers at
 //            once, warps 0-3 stage the token's row in shared memory meanwhile (or, with the ffn_norm in the hook,
 //            every CTA normalises the residual row there first), warp 0 forms logit e (the 16-lane contract) and
-//            publishes it tagged; warps 4-11 prepare the row for Q4_K's integer definition (all CTAs).
+//            publishes it tagged; warps 4-11 prepare the row for the gate/up dots (all CTAs): Q4_K's integer
+//            definition, or Q8_0's inputs in LC order.
 //  routing   every CTA, once it holds all E tagged logits, routes the token (softmax, top-k, ids sorted) in shared
 //            memory; CTA 0's warp 14 forms the dispatch permutation when the caller asks for it.
 //  experts   a CTA owns rows [ga, gb) of every selected expert's gate and up matrices and rows [da, db) of every
 //            selected expert's down matrix. Each of 14 consumer warps streams its own units through a ring of
-//            TRX_DC_NS shared-memory slots with 1-D TMA bulk copies (no multicast), one mbarrier a slot, so it waits
+//            shared-memory slots with 1-D TMA bulk copies (no multicast), one mbarrier a slot, so it waits
 //            only for its own bytes: four gate/up units (one row of gate and the same row of up), then two down
-//            steps (a half-warp the same row of two experts, trx_q6l_dot_pair_il). A unit's two row values go to
+//            steps (a half-warp the same row of two experts, trx_q6l_dot_pair_il or trx_q8l_dot_pair_il). Q4_K_M
+//            takes three slots of 3456 bytes a warp, Q8_0 two of 4352. A unit's two row values go to
 //            warp 14, which forms h = silu(g) u for a whole step's units at once (lane l: unit l) and publishes them
 //            tagged, so that the exponential's latency is paid once a step, off the consumers' path. The down weights
 //            do not depend on h, so they load while the gate/up rows are multiplied; a step's h rows come from the
@@ -34,8 +36,8 @@
 //            residual (Trochilus's mix_body); CTA 0 advances seq (the host-pointer road: the last CTA, which also
 //            posts the host word).
 //
-// Limits (checked on the host, trx_dec1_takes): one token, no external routing, gate/up Q4_K of 2048 columns, down
-// Q6_K of 256, 512 or 1024 columns, k even and at most 8, and a grid whose shares fit the ring (at most 7 gate/up rows
+// Limits (checked on the host, trx_dec1_takes): one token, no external routing, 2048 columns of gate/up and 256,
+// 512 or 1024 of down, Q4_K gate/up with a Q6_K down or Q8_0 throughout, k even and at most 8, and a grid whose shares fit the ring (at most 7 gate/up rows
 // and 14 down rows of an expert a CTA for k = 8). Every wait is bounded; a warp that gives up sets the error flag,
 // waits (bounded) for its own copies in flight and leaves.
 //
@@ -49,8 +51,10 @@
 #define TRX_DC_SILU 14    // the warp that forms h = silu(g) u for the consumers' gate/up units
 #define TRX_DC_HELPER 15  // the helper warp (barriers, h gathering)
 #define TRX_DC_THREADS 512
-#define TRX_DC_NS 3       // slots a consumer warp has in flight
-#define TRX_DC_SLOT 3456  // bytes a slot: a gate/up unit (2 x 1152) or a down step (2 x (2 x 832 + 2 x 16))
+#define TRX_DC_NS 3       // slots a consumer warp has in flight (Q4_K_M; Q8_0 weights take 2 larger ones)
+#define TRX_DC_SLOT 3456  // Q4_K_M bytes a slot: a gate/up unit (2 x 1152) or a down step (2 x (2 x 832 + 2 x 16))
+#define TRX_DC_NS8 2      // Q8_0: slots a consumer warp has in flight
+#define TRX_DC_SLOT8 4352 // Q8_0 bytes a slot: a gate/up unit (2 x 2176) or a down step of up to 1024 columns
 #define TRX_DC_GU 4       // gate/up units a warp
 #define TRX_DC_DN 2       // down steps a warp
 #define TRX_DC_KMAX 8
@@ -59,16 +63,24 @@
 
 struct TrxDecPlan {
     uint32_t off_h, off_xq, total; // shared memory: h rows (k x F floats), the prepared token row, the whole
+    uint32_t slot;                 // bytes a slot
+    int ns;                        // slots a consumer warp has in flight
     int ng_max, nd_max;            // the most gate/up and down rows of an expert a CTA takes
 };
 
 __host__ __device__ inline uint32_t trx_dc_align(uint32_t v) { return (v + 127u) / 128u * 128u; }
 
-__host__ inline TrxDecPlan trx_dec_plan(int H, int F, int k, int grid) {
+// gate_type Q4_K (with a Q6_K down) or Q8_0 (with a Q8_0 down)
+__host__ inline TrxDecPlan trx_dec_plan(int gate_type, int H, int F, int k, int grid) {
     TrxDecPlan P{};
-    P.off_h = trx_dc_align(TRX_DC_CWARPS * TRX_DC_NS * TRX_DC_SLOT);
+    const bool q8 = gate_type == TRX_Q8_0;
+    // Q8_0: a gate/up unit is 2 rows of H / 256 272-byte blocks, a down step 2 x 2 rows of F / 256 (no larger for F <= H)
+    P.slot = q8 ? TRX_DC_SLOT8 : TRX_DC_SLOT; // (H = 2048)
+    P.ns = q8 ? TRX_DC_NS8 : TRX_DC_NS;
+    P.off_h = trx_dc_align(TRX_DC_CWARPS * P.ns * P.slot);
     P.off_xq = trx_dc_align(P.off_h + (uint32_t)(k * F * 4 > H * 4 ? k * F * 4 : H * 4));
-    P.total = trx_dc_align(P.off_xq + (uint32_t)(H * 4 + (H / 32) * 8 + (H / 256) * 8));
+    // the token's row: Q4_K's prepared planes, sums and scales; Q8_0's inputs in LC order
+    P.total = trx_dc_align(P.off_xq + (uint32_t)(q8 ? H * 4 : H * 4 + (H / 32) * 8 + (H / 256) * 8));
     P.ng_max = (F + grid - 1) / grid;
     P.nd_max = ((H / 2 + grid - 1) / grid) * 2;
     return P;
@@ -77,13 +89,15 @@ __host__ inline TrxDecPlan trx_dec_plan(int H, int F, int k, int grid) {
 // whether a call takes trx_k_dec1 (the host's part of the limits above)
 __host__ inline bool trx_dec1_takes(int gate_type, int down_type, int router_type, int H, int F, int E, int k, int T,
                                     int grid, bool ext) {
-    if (T != 1 || ext || gate_type != TRX_Q4_K || down_type != TRX_Q6_K) return false;
+    if (T != 1 || ext) return false;
+    if (!(gate_type == TRX_Q4_K && down_type == TRX_Q6_K) && !(gate_type == TRX_Q8_0 && down_type == TRX_Q8_0))
+        return false;
     if (router_type != TRX_F32 && router_type != TRX_BF16) return false;
     // (1, 2 or 4 blocks a down row: a row's d values never straddle a 16-byte piece)
     if (H != 2048 || (F != 256 && F != 512 && F != 1024) || E > TRX_MAX_EXPERTS || k < 2 || k % 2 || k > TRX_DC_KMAX)
         return false;
-    const TrxDecPlan P = trx_dec_plan(H, F, k, grid);
-    return k * P.ng_max <= TRX_DC_CWARPS * TRX_DC_GU && (k / 2) * P.nd_max <= 2 * TRX_DC_CWARPS * TRX_DC_DN &&
+    const TrxDecPlan P = trx_dec_plan(gate_type, H, F, k, grid);
+    return P.total <= 200 * 1024 && k * P.ng_max <= TRX_DC_CWARPS * TRX_DC_GU && (k / 2) * P.nd_max <= 2 * TRX_DC_CWARPS * TRX_DC_DN &&
            P.nd_max <= 16 && P.ng_max <= 32 && grid <= TRX_DC_GRID_MAX && F >= grid;
 }
 
@@ -103,7 +117,7 @@ __device__ __forceinline__ ulonglong2 trx_ld_tagged2(const unsigned long long *p
     return x;
 }
 
-template <int RT>
+template <int RT, int GT>
 __global__ void __launch_bounds__(TRX_DC_THREADS, 1)
     trx_k_dec1(TrxLayer L, TrxShape S, const float *__restrict__ normed, TrxWork w, TrxSync *sync,
                float *__restrict__ x_io, float *__restrict__ ffn_out, uint32_t epoch, const TrxDecPlan P) {
@@ -222,9 +236,20 @@ __global__ void __launch_bounds__(TRX_DC_THREADS, 1)
         if (lane == 0 && w.out_logits) w.out_logits[c] = v;
         TRX_TRACE(62);
     }
-    // the token's row prepared for Q4_K's integer definition: warp 4 + s takes 256-block s
-    if (warp >= 4 && warp < 4 + H / 256)
-        trx_prep_q4x_block(xrow + 256 * (warp - 4), xq, warp - 4, H / 256, xbf + 8 * (warp - 4), xsc + (warp - 4), lane);
+    constexpr bool Q8 = GT == TRX_Q8_0;
+    constexpr int NS = Q8 ? TRX_DC_NS8 : TRX_DC_NS;           // (the plan's ns and slot, as constants)
+    constexpr uint32_t SLOT = Q8 ? TRX_DC_SLOT8 : TRX_DC_SLOT;
+    float *xlc = reinterpret_cast<float *>(xq); // (Q8_0: the token's row in LC order)
+    // the token's row prepared for the gate/up dots, warp 4 + s taking 256-block s: Q4_K's integer definition, or
+    // Q8_0's inputs in LC order
+    if (warp >= 4 && warp < 4 + H / 256) {
+        const int sb = warp - 4;
+        if (Q8) {
+            for (int i = lane; i < 256; i += 32) xlc[256 * sb + trx_lc_pos(i)] = xrow[256 * sb + i];
+        } else {
+            trx_prep_q4x_block(xrow + 256 * sb, xq, sb, H / 256, xbf + 8 * sb, xsc + sb, lane);
+        }
+    }
 
     // ---------------- routing: once it holds every tagged logit, every CTA routes the token itself
     if (warp == 0) {
@@ -289,7 +314,7 @@ __global__ void __launch_bounds__(TRX_DC_THREADS, 1)
         // the CTA's share of every selected expert into L2 at once (gate rows, up rows, down rows, the down rows' d
         // values: lane 4 i + part), so that HBM streams the whole call's weights while the rings start; the rings'
         // copies then read L2
-        const int i = lane >> 2, part = lane & 3, rbg = H / 256 * 144, rbd = nsb * 208;
+        const int i = lane >> 2, part = lane & 3, rbg = H / 256 * (Q8 ? 272 : 144), rbd = nsb * (Q8 ? 272 : 208);
         if (i < k) {
             const int e = s_selid[i];
             if (part < 2) {
@@ -299,7 +324,7 @@ __global__ void __launch_bounds__(TRX_DC_THREADS, 1)
                 const uint8_t *mat = L.down + e * L.down_mb;
                 if (part == 2) {
                     trx_bulk_prefetch_l2(mat + (int64_t)da * rbd, (uint32_t)(nd * rbd));
-                } else { // the d values of rows [da, da + nd), widened to 16-byte bounds
+                } else if (!Q8) { // the Q6L d values of rows [da, da + nd), widened to 16-byte bounds
                     const int64_t lo = (int64_t)H * rbd + (((int64_t)da * nsb * 2) & ~15ll);
                     const int64_t hi = (int64_t)H * rbd + (((int64_t)(da + nd) * nsb * 2 + 15) & ~15ll);
                     trx_bulk_prefetch_l2(mat + lo, (uint32_t)(hi - lo));
@@ -310,14 +335,15 @@ __global__ void __launch_bounds__(TRX_DC_THREADS, 1)
     bool failed = false;
     if (warp < TRX_DC_CWARPS) {
         // ---------------- a consumer warp: TRX_DC_GU gate/up units, then TRX_DC_DN down steps, through its slots
-        uint8_t *slots = smem + (size_t)warp * TRX_DC_NS * TRX_DC_SLOT;
+        uint8_t *slots = smem + (size_t)warp * NS * SLOT;
         const int ngu = k * ng, ndn = (k / 2) * nd; // gate/up units (expert-major), down units (expert pairs)
-        const int rbg = H / 256 * 144, rbd = nsb * 208;
+        // row bytes (Q8L: 272 a block; Q6L: 208 a block, the d values apart) and a half-warp's share of a down step
+        const int rbg = H / 256 * (Q8 ? 272 : 144), rbd = nsb * (Q8 ? 272 : 208), rhalf = Q8 ? 2 * rbd : 2 * rbd + 32;
         // lane 0 arms step j in its slot (a step with nothing to load completes at once: zero bytes expected)
         auto issue = [&](int j) {
             if (lane != 0) return;
-            uint8_t *dst = slots + (j % TRX_DC_NS) * TRX_DC_SLOT;
-            uint64_t *bar = &s_full[warp][j % TRX_DC_NS];
+            uint8_t *dst = slots + (j % NS) * SLOT;
+            uint64_t *bar = &s_full[warp][j % NS];
             trx_fence_proxy_async(); // this warp's reads of the slot's last step before the copy rewrites it
             if (j < TRX_DC_GU) {
                 const int u = warp + TRX_DC_CWARPS * j;
@@ -332,31 +358,32 @@ __global__ void __launch_bounds__(TRX_DC_THREADS, 1)
             } else {
                 uint32_t bytes = 0;
                 for (int hh = 0; hh < 2; hh++)
-                    if (2 * warp + hh + 2 * TRX_DC_CWARPS * (j - TRX_DC_GU) < ndn) bytes += 2u * rbd + 32u;
+                    if (2 * warp + hh + 2 * TRX_DC_CWARPS * (j - TRX_DC_GU) < ndn) bytes += (uint32_t)rhalf;
                 trx_mbar_expect_tx(bar, bytes);
                 for (int hh = 0; hh < 2; hh++) {
                     const int v = 2 * warp + hh + 2 * TRX_DC_CWARPS * (j - TRX_DC_GU);
                     if (v >= ndn) continue;
                     const int q = v / nd, r = da + v % nd;
-                    uint8_t *d0 = dst + hh * (2 * rbd + 32);
+                    uint8_t *d0 = dst + hh * rhalf;
                     for (int ab = 0; ab < 2; ab++) {
                         const uint8_t *mat = L.down + s_selid[2 * q + ab] * L.down_mb;
                         trx_bulk_g2s_hint(d0 + ab * rbd, mat + (int64_t)r * rbd, rbd, bar, pol);
-                        // the row's d values: the 16-byte piece that holds them
-                        trx_bulk_g2s_hint(d0 + 2 * rbd + 16 * ab, mat + (int64_t)H * rbd + ((int64_t)r * nsb * 2 & ~15ll),
-                                          16u, bar, pol);
+                        // Q6L: the row's d values, the 16-byte piece that holds them
+                        if (!Q8)
+                            trx_bulk_g2s_hint(d0 + 2 * rbd + 16 * ab,
+                                              mat + (int64_t)H * rbd + ((int64_t)r * nsb * 2 & ~15ll), 16u, bar, pol);
                     }
                 }
             }
         };
         int issued = 0;
-        for (; issued < TRX_DC_NS; issued++) issue(issued);
+        for (; issued < NS; issued++) issue(issued);
         TrxQ4X X;
-        trx_q4x_load(xq, 32, lane, xbf + 8 * (lane >> 2), xsc + (lane >> 2), X);
+        if (!Q8) trx_q4x_load(xq, 32, lane, xbf + 8 * (lane >> 2), xsc + (lane >> 2), X);
         float *ss = s_q6sc[2 * warp + (lane >> 4)];
         for (int j = 0; j < TRX_DC_GU + TRX_DC_DN && !failed; j++) {
-            const uint8_t *src = slots + (j % TRX_DC_NS) * TRX_DC_SLOT;
-            if (!__all_sync(0xffffffffu, trx_mbar_wait(&s_full[warp][j % TRX_DC_NS], (j / TRX_DC_NS) & 1, TRX_WAIT_NS))) {
+            const uint8_t *src = slots + (j % NS) * SLOT;
+            if (!__all_sync(0xffffffffu, trx_mbar_wait(&s_full[warp][j % NS], (j / NS) & 1, TRX_WAIT_NS))) {
                 failed = true;
                 break;
             }
@@ -364,9 +391,15 @@ __global__ void __launch_bounds__(TRX_DC_THREADS, 1)
             if (j < TRX_DC_GU) {
                 const int u = warp + TRX_DC_CWARPS * j;
                 if (u < ngu) {
-                    const uint8_t *const rows2[2] = {src, src + rbg};
                     float y2[2];
-                    trx_q4k_row8xn<true, 2>(rows2, X, lane, y2);
+                    if (Q8) { // the gate row by half-warp 0, the up row by half-warp 1 (16-lane contract each)
+                        const float y = trx_q8l_dot<true>(src + (lane >> 4) * rbg, xlc, H / 256, lane & 15);
+                        y2[0] = y;
+                        y2[1] = __shfl_sync(0xffffffffu, y, 16);
+                    } else {
+                        const uint8_t *const rows2[2] = {src, src + rbg};
+                        trx_q4k_row8xn<true, 2>(rows2, X, lane, y2);
+                    }
                     if (lane == 0) { // to the silu warp
                         s_gu[u] = make_float2(y2[0], y2[1]);
                         trx_mbar_arrive(&s_gubar[j]);
@@ -385,13 +418,21 @@ __global__ void __launch_bounds__(TRX_DC_THREADS, 1)
                         break;
                     }
                     if (warp == 0) TRX_TRACE(24 + j); // its h rows
-                    const uint8_t *d0 = src + (valid ? (lane >> 4) : 0) * (2 * rbd + 32);
-                    const int dh = (r * nsb * 2) & 15; // the row's d values inside their 16-byte piece
-                    const uint8_t *rb = d0 + rbd, *dA = d0 + 2 * rbd + dh, *dB = d0 + 2 * rbd + 16 + dh;
+                    const uint8_t *d0 = src + (valid ? (lane >> 4) : 0) * rhalf;
+                    const uint8_t *rb = d0 + rbd;
                     const float *xab = hbuf + (size_t)q * 2 * F;
-                    const float2 val = nsb == 4   ? trx_q6l_dot_pair_il<4>(d0, dA, rb, dB, xab, lane & 15, ss)
-                                       : nsb == 2 ? trx_q6l_dot_pair_il<2>(d0, dA, rb, dB, xab, lane & 15, ss)
-                                                  : trx_q6l_dot_pair_il<1>(d0, dA, rb, dB, xab, lane & 15, ss);
+                    float2 val;
+                    if (Q8) {
+                        val = nsb == 4   ? trx_q8l_dot_pair_il<4>(d0, rb, xab, lane & 15)
+                              : nsb == 2 ? trx_q8l_dot_pair_il<2>(d0, rb, xab, lane & 15)
+                                         : trx_q8l_dot_pair_il<1>(d0, rb, xab, lane & 15);
+                    } else {
+                        const int dh = (r * nsb * 2) & 15; // the row's d values inside their 16-byte piece
+                        const uint8_t *dA = d0 + 2 * rbd + dh, *dB = d0 + 2 * rbd + 16 + dh;
+                        val = nsb == 4   ? trx_q6l_dot_pair_il<4>(d0, dA, rb, dB, xab, lane & 15, ss)
+                              : nsb == 2 ? trx_q6l_dot_pair_il<2>(d0, dA, rb, dB, xab, lane & 15, ss)
+                                         : trx_q6l_dot_pair_il<1>(d0, dA, rb, dB, xab, lane & 15, ss);
+                    }
                     if (valid && (lane & 15) == 0) {
                         s_h3[2 * q][rl] = val.x;
                         s_h3[2 * q + 1][rl] = val.y;
@@ -404,7 +445,7 @@ __global__ void __launch_bounds__(TRX_DC_THREADS, 1)
         }
         if (failed && lane == 0) { // every copy this warp armed lands before the CTA can leave
             for (int j = 0; j < issued; j++)
-                trx_mbar_wait(&s_full[warp][j % TRX_DC_NS], (j / TRX_DC_NS) & 1, TRX_WAIT_NS);
+                trx_mbar_wait(&s_full[warp][j % NS], (j / NS) & 1, TRX_WAIT_NS);
         }
     } else if (warp == TRX_DC_SILU) {
         // ---------------- h = silu(g) u of a step's gate/up units at once (lane l: unit 14 j + l), published tagged;

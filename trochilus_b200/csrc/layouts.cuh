@@ -544,6 +544,50 @@ __device__ __noinline__ float2 trx_q6l_dot_pair_il(const uint8_t *__restrict__ r
     return make_float2(trx_lane_tree16(aa), trx_lane_tree16(ab));
 }
 
+// The Q8L counterpart of trx_q6l_dot_pair_il: rows a and b in the Q8L layout (272 bytes a 256-block: the block's
+// 8 f16 scales, then its quants in position order, thread l's 16 at bytes 16 l ..), the inputs interleaved
+// (trx_il_off). Element m of thread l has scale m / 2; w = fl(d q) (exact), the product fl(w x) rounded, added in
+// order of m: trx_q8l_block's arithmetic for each row. NSB: 1, 2 or 4 blocks.
+template <int NSB>
+__device__ __noinline__ float2 trx_q8l_dot_pair_il(const uint8_t *__restrict__ ra, const uint8_t *__restrict__ rb,
+                                                   const float *__restrict__ xab, int l) {
+    float aa = 0.0f, ab = 0.0f;
+    const trx_f2 bias = trx_pack2(8388736.0f, 8388736.0f); // 2^23 + 128
+#pragma unroll
+    for (int s = 0; s < NSB; s++) {
+        trx_f2 xv[16], dv[8];
+#pragma unroll
+        for (int q = 0; q < 4; q++) { // element 4 q + j: position 256 s + 64 q + 4 l + j
+            const ulonglong2 u = *reinterpret_cast<const ulonglong2 *>(xab + 128 * (4 * s + q) + 4 * l);
+            const ulonglong2 v = *reinterpret_cast<const ulonglong2 *>(xab + 128 * (4 * s + q) + 64 + 4 * l);
+            xv[4 * q] = u.x;
+            xv[4 * q + 1] = u.y;
+            xv[4 * q + 2] = v.x;
+            xv[4 * q + 3] = v.y;
+        }
+        const uint4 ha = *reinterpret_cast<const uint4 *>(ra + 272 * s), hb = *reinterpret_cast<const uint4 *>(rb + 272 * s);
+        const uint32_t wa[4] = {ha.x, ha.y, ha.z, ha.w}, wb[4] = {hb.x, hb.y, hb.z, hb.w};
+#pragma unroll
+        for (int i = 0; i < 8; i++) // (d_a, d_b) of scale i
+            dv[i] = trx_pack2(trx_half((uint16_t)(wa[i >> 1] >> (16 * (i & 1)))), trx_half((uint16_t)(wb[i >> 1] >> (16 * (i & 1)))));
+        const uint4 qa4 = *reinterpret_cast<const uint4 *>(ra + 272 * s + 16 + 16 * l);
+        const uint4 qb4 = *reinterpret_cast<const uint4 *>(rb + 272 * s + 16 + 16 * l);
+        const uint32_t qa[4] = {qa4.x ^ 0x80808080u, qa4.y ^ 0x80808080u, qa4.z ^ 0x80808080u, qa4.w ^ 0x80808080u};
+        const uint32_t qb[4] = {qb4.x ^ 0x80808080u, qb4.y ^ 0x80808080u, qb4.z ^ 0x80808080u, qb4.w ^ 0x80808080u};
+#pragma unroll
+        for (int m = 0; m < 16; m++) {
+            const uint32_t sel = 0x7440u | (m & 3);
+            const trx_f2 qv = trx_sub2(trx_pack2(__uint_as_float(__byte_perm(qa[m >> 2], 0x4b000000u, sel)),
+                                                 __uint_as_float(__byte_perm(qb[m >> 2], 0x4b000000u, sel))),
+                                       bias); // (q_a, q_b), exact
+            const trx_f2 p = trx_mul2(trx_mul2(dv[m >> 1], qv), xv[m]);
+            aa = __fadd_rn(aa, trx_lo(p));
+            ab = __fadd_rn(ab, trx_hi(p));
+        }
+    }
+    return make_float2(trx_lane_tree16(aa), trx_lane_tree16(ab));
+}
+
 // Two rows (a, b in shared memory) of the same width against one LC-ordered input row read through L1 (each
 // 256-block's inputs loaded once for both rows), one 256-block an iteration (a small loop body). Q6L: da, db the
 // rows' f16 d values in shared memory. Returns both tree sums (the same in all 16 threads of the half-warp).
