@@ -240,7 +240,7 @@ TRMOE_API int tr_gpu_moe_trace_read(tr_gpu_moe *m, uint64_t *slots, int64_t n);
 TRMOE_API int tr_gpu_moe_launches(const tr_gpu_moe *m, int64_t n_tok);
 
 /* The kernel one tr_gpu_moe_layer_dev call of n_tok tokens runs when it is a single kernel: "trx_k_dec1" (the
- * one-token decode kernel; also for calls of up to 32 tokens on its shapes, which launch it once a token),
+ * one-token decode kernel; also for calls of up to 64 tokens on its shapes, which launch it once a token),
  * "trx_k_layer" (the fused layer kernel); "" when the call takes several different kernels. */
 TRMOE_API const char *tr_gpu_moe_kernel_name(const tr_gpu_moe *m, int64_t n_tok);
 

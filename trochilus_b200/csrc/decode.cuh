@@ -59,7 +59,7 @@
 #define TRX_DC_DN 2       // down steps a warp
 #define TRX_DC_KMAX 8
 #define TRX_DC_GRID_MAX 256 // CTAs (the tagged logits: a row of E words for each)
-#define TRX_DC_SEQ_MAX 32   // calls of up to this many tokens run one launch a token (faster than the fused kernel)
+#define TRX_DC_SEQ_MAX 64   // calls of up to this many tokens run one launch a token (faster than the fused kernel)
 
 struct TrxDecPlan {
     uint32_t off_h, off_xq, total; // shared memory: h rows (k x F floats), the prepared token row, the whole
