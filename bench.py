@@ -418,13 +418,13 @@ def run_ep(args, rank, world, dist, T=None, steps=None):
     return line
 
 
-# The rest of the metric's configurations (BASELINE.json configs[1] at more tokens, the Q8_0 decode, configs[3]'s
-# Zipf-routed passes): key, gate, down, tokens a call, Zipf router bias
-EXTRA = (("q8_0_T1", "q8_0", "q8_0", 1, False), ("q8_0_T8", "q8_0", "q8_0", 8, False),
-         ("q8_0_T64", "q8_0", "q8_0", 64, False), ("q4km_T8", "q4_k", "q6_k", 8, False),
-         ("q4km_T64", "q4_k", "q6_k", 64, False), ("zipf_q4k_T512", "q4_k", "q4_k", 512, True),
-         ("zipf_q4k_T4096", "q4_k", "q4_k", 4096, True), ("zipf_q8_0_T512", "q8_0", "q8_0", 512, True),
-         ("zipf_q8_0_T4096", "q8_0", "q8_0", 4096, True))
+# The rest of the metric's configurations: BASELINE.json configs[3] (the isolated layer, all-Q4_K and all-Q8_0, Zipf
+# router bias, T in {1, 8, 64, 512, 4096, 16384}), configs[1]'s Q4_K_M layer at more tokens, and configs[4]'s MoE
+# step (64 sequences x 4 verify rows = 256 tokens, Q8_0): key, gate, down, tokens a call, Zipf router bias
+EXTRA = tuple((f"{n}_zipf_T{t}", g, g, t, True) for n, g in (("q4k", "q4_k"), ("q8_0", "q8_0"))
+              for t in (1, 8, 64, 512, 4096, 16384)) + \
+        (("q4km_T8", "q4_k", "q6_k", 8, False), ("q4km_T64", "q4_k", "q6_k", 64, False),
+         ("q8_0_T256_cfg4", "q8_0", "q8_0", 256, False))
 
 
 def run_extra(args, dev, cpu_seconds):

@@ -186,10 +186,10 @@ TRMOE_API int tr_gpu_moe_ep_peer_combine(tr_gpu_moe *m, const float *d_sel_w, co
                                          float *d_x, float *d_ffn_out, void *stream);
 
 /* No counterpart in the reference (its long passes run the same scalar definition): calls of at least min_tokens
- * tokens take the tensor-core road of a context with Q8_0 gate/up and down weights (router, top-k and dispatch
- * exact as always; expert products as 3xTF32 tcgen05 GEMMs, within 1e-5 relative of the exact result; combine
- * exact). 0 keeps every call on the exact road. Default 256. Returns 0, or -1 (a non-zero min_tokens on a context
- * without the road). */
+ * tokens take the tensor-core road (weights Q8_0, Q4_K or Q6_K; router, top-k and dispatch exact as always; expert
+ * products as 3xTF32 tcgen05 GEMMs, within 1e-5 relative of the exact result; combine exact). 0 keeps every call on
+ * the exact road. Default 256, or 32 when the down weights are Q4_K (their exact road costs about 74 us a token).
+ * Returns 0, or -1 (a non-zero min_tokens on a context without the road). */
 TRMOE_API int tr_gpu_moe_set_prefill(tr_gpu_moe *m, int64_t min_tokens);
 
 /* tr_gpu_moe_layer on device memory, enqueued on `stream` (a cudaStream_t; NULL: the context's own

@@ -212,6 +212,7 @@ def test_q4k_long_pass_multikernel(cuda, oracle):
     from trochilus_b200.moe import GpuMoe
     m = GpuMoe(1, 64, 8, 2048, 1024, gb.BF16, gb.Q4_K, gb.Q4_K, max_tokens=T)
     m.set_layer(0, lay)
+    m.set_prefill(0)  # the exact road (a Q4_K down takes the tensor road from 32 tokens by default)
     rng = np.random.default_rng(5)
     normed = rng.normal(size=(T, 2048)).astype(np.float32)
     x = rng.normal(size=(T, 2048)).astype(np.float32)

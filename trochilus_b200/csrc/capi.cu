@@ -491,7 +491,9 @@ static bool plan_prefill(tr_gpu_moe *m) {
         !encode_map(&m->pf_map_h[1], reinterpret_cast<float *>(m->work.hq), R, c.n_ff))
         return false;
     m->pf_ok = true;
-    m->pf_min = 256;
+    // calls this long take the road by default: 256 tokens, or 32 when the down weights are Q4_K, whose exact road
+    // (the Q4_K input preparation of every h row) costs about 74 us a token against the road's flat ~1 ms (measured)
+    m->pf_min = c.down_type == TRX_Q4_K ? 32 : 256;
     return true;
 }
 
