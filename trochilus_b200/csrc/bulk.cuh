@@ -50,6 +50,17 @@ __device__ __forceinline__ void trx_bulk_g2s_hint(void *dst, const void *src, ui
                  : "memory");
 }
 
+// A 3-D tiled TMA load (no multicast) with an L2 cache policy: the box at element (x, y, z) of the tensor map (a
+// CUtensorMap in kernel parameter, constant or global memory) into shared memory (128-byte aligned), completing on
+// bar. x times the element size must be a multiple of 16 bytes.
+__device__ __forceinline__ void trx_tma_load_3d_hint(void *dst, const void *map, int x, int y, int z, uint64_t *bar,
+                                                     uint64_t policy) {
+    asm volatile("cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint "
+                 "[%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(trx_smem(dst)),
+                 "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(trx_smem(bar)), "l"(policy)
+                 : "memory");
+}
+
 // Bring [src, src + bytes) into L2 without waiting for it (src and bytes multiples of 16)
 __device__ __forceinline__ void trx_bulk_prefetch_l2(const void *src, uint32_t bytes) {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");

@@ -57,9 +57,11 @@ bool ck(cudaError_t e, const char *what) {
 }
 
 // waits for the stream, polling; a GPU that does not finish within timeout_s is an error, not a hang
+// Polls the stream: busy for the first 2 ms (a decode call's work takes tens of microseconds, and a sleep, however
+// short it asks to be, lasts about 60 us on Linux), then with 20 us sleeps between the polls.
 bool stream_wait(cudaStream_t s, double timeout_s = 60.0) {
     const auto t0 = std::chrono::steady_clock::now();
-    for (unsigned spins = 0;; spins++) {
+    for (;;) {
         const cudaError_t e = cudaStreamQuery(s);
         if (e == cudaSuccess) return true;
         if (e != cudaErrorNotReady) return ck(e, "cudaStreamQuery");
@@ -68,7 +70,7 @@ bool stream_wait(cudaStream_t s, double timeout_s = 60.0) {
             set_err("the GPU did not finish within %.0f s", timeout_s);
             return false;
         }
-        if (spins > 64) std::this_thread::sleep_for(std::chrono::microseconds(20));
+        if (dt > 0.002) std::this_thread::sleep_for(std::chrono::microseconds(20));
     }
 }
 
@@ -188,6 +190,8 @@ struct tr_gpu_moe {
     bool fused_ok = false;
     bool dec1_ok = false;  // the one-token decode kernel (decode.cuh) fits and may be launched
     bool dec1_pdl = true;  // and is launched with programmatic dependent launch (off if the driver refuses it)
+    // Q4_K: per layer the one-token kernel's tensor maps over the gate and up matrices (trx_dec1_map)
+    std::vector<CUtensorMap> dc_maps;
     int64_t tag_bytes = 0; // its tagged exchange words (work regions 26 and 27), cleared with the counters
     float *d_normed = nullptr, *d_x = nullptr;
     int64_t *d_sel_id = nullptr;
@@ -284,7 +288,8 @@ static LayerFn layer_fn(int gate_type, int down_type) {
 
 // the fused kernel: the most shared memory a CTA may take, and a cooperative grid of one CTA per SM
 // the one-token kernel for a router type and a gate/up type (Q4_K: Q4_K_M's road, Q8_0: all Q8_0)
-typedef void (*Dec1Fn)(TrxLayer, TrxShape, const float *, TrxWork, TrxSync *, float *, float *, uint32_t, TrxDecPlan);
+typedef void (*Dec1Fn)(TrxLayer, TrxShape, const float *, TrxWork, TrxSync *, float *, float *, uint32_t, TrxDecPlan,
+                       const CUtensorMap, const CUtensorMap);
 static Dec1Fn dec1_fn(int router_type, int gate_type) {
     if (gate_type == TRX_Q8_0)
         return router_type == TRX_BF16 ? trx_k_dec1<TRX_BF16, TRX_Q8_0> : trx_k_dec1<TRX_F32, TRX_Q8_0>;
@@ -439,8 +444,7 @@ static bool check_config(const tr_gpu_moe_config *c) {
     return true;
 }
 
-// a 2-D fp32 tensor map over rows x cols (row-major), boxes of 32 columns x 128 rows, 128-byte swizzle
-static bool encode_map(CUtensorMap *map, float *base, int64_t rows, int64_t cols) {
+static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
     static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
     if (encode == nullptr) {
         cudaDriverEntryPointQueryResult q{};
@@ -448,10 +452,36 @@ static bool encode_map(CUtensorMap *map, float *base, int64_t rows, int64_t cols
         if (!ck(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q), "driver entry point") ||
             q != cudaDriverEntryPointSuccess || fn == nullptr) {
             if (g_err.empty()) set_err("cuTensorMapEncodeTiled is not available");
-            return false;
+            return nullptr;
         }
         encode = (PFN_cuTensorMapEncodeTiled_v12000)fn;
     }
+    return encode;
+}
+
+// The one-token kernel's map over a layer's Q4_K gate (or up) matrices: bytes x rows x experts (row bytes, n_ff
+// rows, expert stride), boxes of one 256-block (144 bytes) of 8 rows of one expert; rows past n_ff read as zeros
+static bool trx_dec1_map(CUtensorMap *map, const uint8_t *base, int64_t row_bytes, int64_t rows, int64_t experts,
+                         int64_t expert_bytes) {
+    PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
+    if (encode == nullptr) return false;
+    const cuuint64_t dims[3] = {(cuuint64_t)row_bytes, (cuuint64_t)rows, (cuuint64_t)experts};
+    const cuuint64_t strides[2] = {(cuuint64_t)row_bytes, (cuuint64_t)expert_bytes};
+    const cuuint32_t box[3] = {144, 8, 1}, es[3] = {1, 1, 1};
+    const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, (void *)base, dims, strides, box, es,
+                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        set_err("cuTensorMapEncodeTiled failed (%d)", (int)r);
+        return false;
+    }
+    return true;
+}
+
+// a 2-D fp32 tensor map over rows x cols (row-major), boxes of 32 columns x 128 rows, 128-byte swizzle
+static bool encode_map(CUtensorMap *map, float *base, int64_t rows, int64_t cols) {
+    PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
+    if (encode == nullptr) return false;
     const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows}, strides[1] = {(cuuint64_t)cols * 4};
     const cuuint32_t box[2] = {TRX_PF_BK, TRX_PF_BM}, es[2] = {1, 1};
     const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, base, dims, strides, box, es,
@@ -521,6 +551,7 @@ extern "C" tr_gpu_moe *tr_gpu_moe_create(const tr_gpu_moe_config *cfg, int devic
         m->layer_mem.assign((size_t)cfg->n_layers, nullptr);
         m->layers.assign((size_t)cfg->n_layers, TrxLayer{});
         m->layer_set.assign((size_t)cfg->n_layers, 0);
+        m->dc_maps.assign((size_t)(2 * cfg->n_layers), CUtensorMap{});
         for (int64_t l = 0; l < cfg->n_layers && ok; l++)
             ok = ck(cudaMalloc(&m->layer_mem[(size_t)l], (size_t)lb), "cudaMalloc(layer)");
     }
@@ -673,6 +704,14 @@ extern "C" int tr_gpu_moe_set_layer(tr_gpu_moe *m, int64_t layer, const void *ro
     if (!ok) {
         put_err(err, err_len);
         return -1;
+    }
+    // the one-token kernel's maps over the Q4_K gate and up matrices; without them (no driver entry point) every
+    // call takes the fused kernel instead
+    if (c.gate_type == TRX_Q4_K && m->dec1_ok &&
+        !(trx_dec1_map(&m->dc_maps[(size_t)(2 * layer)], L.gate, trx_row_bytes(c.gate_type, H), F, E, L.gate_mb) &&
+          trx_dec1_map(&m->dc_maps[(size_t)(2 * layer + 1)], L.up, trx_row_bytes(c.gate_type, H), F, E, L.up_mb))) {
+        m->dec1_ok = false;
+        g_err.clear();
     }
     m->layers[(size_t)layer] = L;
     m->layer_set[(size_t)layer] = 1;
@@ -868,8 +907,8 @@ static int launch_fused(tr_gpu_moe *m, const TrxLayer &L, const TrxShape &S, con
 }
 
 // the one-token decode kernel (decode.cuh): one cooperative launch, a CTA an SM
-static int launch_dec1(tr_gpu_moe *m, const TrxLayer &L, const TrxShape &S, const float *normed, const TrxWork &w,
-                       float *x_io, float *ffn_out, uint32_t epoch, cudaStream_t st) {
+static int launch_dec1(tr_gpu_moe *m, int64_t layer, const TrxLayer &L, const TrxShape &S, const float *normed,
+                       const TrxWork &w, float *x_io, float *ffn_out, uint32_t epoch, cudaStream_t st) {
     const TrxDecPlan P = trx_dec_plan(L.gate_type, S.H, S.F, S.k, m->grid_fused);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)m->grid_fused);
@@ -886,12 +925,18 @@ static int launch_dec1(tr_gpu_moe *m, const TrxLayer &L, const TrxShape &S, cons
     cfg.attrs = attr;
     cfg.numAttrs = m->dec1_pdl ? 2 : 1;
     auto fn = dec1_fn(L.router_type, L.gate_type);
-    cudaError_t e = cudaLaunchKernelEx(&cfg, fn, L, S, normed, w, m->sync, x_io, ffn_out, epoch, P);
+    // (Q4_K: the layer's maps; Q8_0 takes none, and gets zeroed ones)
+    CUtensorMap mg{}, mu{};
+    if (L.gate_type == TRX_Q4_K) {
+        mg = m->dc_maps[(size_t)(2 * layer)];
+        mu = m->dc_maps[(size_t)(2 * layer + 1)];
+    }
+    cudaError_t e = cudaLaunchKernelEx(&cfg, fn, L, S, normed, w, m->sync, x_io, ffn_out, epoch, P, mg, mu);
     if (e != cudaSuccess && m->dec1_pdl) { // not taken together: cooperative alone from now on
         (void)cudaGetLastError();
         m->dec1_pdl = false;
         cfg.numAttrs = 1;
-        e = cudaLaunchKernelEx(&cfg, fn, L, S, normed, w, m->sync, x_io, ffn_out, epoch, P);
+        e = cudaLaunchKernelEx(&cfg, fn, L, S, normed, w, m->sync, x_io, ffn_out, epoch, P, mg, mu);
     }
     return ck(e, "decode layer launch") ? 0 : -1;
 }
@@ -992,7 +1037,7 @@ static int launch_layer(tr_gpu_moe *m, int64_t layer, const float *d_normed, int
         w.host_done = done;
         if (epoch_out) *epoch_out = epoch;
         if (dec1 && (!S.norm_in || ((uintptr_t)d_normed & 15) == 0))
-            return launch_dec1(m, L, S, d_normed, w, d_x, ffn, epoch, st);
+            return launch_dec1(m, layer, L, S, d_normed, w, d_x, ffn, epoch, st);
         if (dec1seq && (!S.norm_in || ((uintptr_t)d_normed & 15) == 0)) {
             const int64_t H = S.H;
             for (int t = 0; t < T; t++) {
@@ -1004,7 +1049,8 @@ static int launch_layer(tr_gpu_moe *m, int64_t layer, const float *d_normed, int
                     wt.out_sel_w += (int64_t)t * S.k;
                 }
                 if (wt.out_normed) wt.out_normed += t * H;
-                if (launch_dec1(m, L, S, d_normed + t * H, wt, d_x + t * H, ffn ? ffn + t * H : nullptr, epoch, st) != 0)
+                if (launch_dec1(m, layer, L, S, d_normed + t * H, wt, d_x + t * H, ffn ? ffn + t * H : nullptr, epoch,
+                                st) != 0)
                     return -1;
             }
             return 0;

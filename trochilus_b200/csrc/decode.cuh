@@ -45,6 +45,7 @@
 // counting sort :1850-1861, expert_stages :1642-1689, mix_body :1432-1446); tr_rmsnorm src/kernels/kernels.c:1351-1360.
 #pragma once
 #include <cstdint>
+#include <cuda.h>
 #include "fused_layer.cuh"
 
 #define TRX_DC_CWARPS 14  // consumer warps
@@ -55,7 +56,8 @@
 #define TRX_DC_SLOT 3456  // Q4_K_M bytes a slot: a gate/up unit (2 x 1152) or a down step (2 x (2 x 832 + 2 x 16))
 #define TRX_DC_NS8 2      // Q8_0: slots a consumer warp has in flight
 #define TRX_DC_SLOT8 4352 // Q8_0 bytes a slot: a gate/up unit (2 x 2176) or a down step of up to 1024 columns
-#define TRX_DC_GU 4       // gate/up units a warp
+#define TRX_DC_GU 4       // gate/up units a warp (Q8_0: a gate row and its up row each)
+#define TRX_DC_GU4 5      // Q4_K: gate/up units a warp (a 256-block of 8 gate rows and 8 up rows each, on the tensor cores)
 #define TRX_DC_DN 2       // down steps a warp
 #define TRX_DC_KMAX 8
 #define TRX_DC_GRID_MAX 256 // CTAs (the tagged logits: a row of E words for each)
@@ -63,6 +65,7 @@
 
 struct TrxDecPlan {
     uint32_t off_h, off_xq, total; // shared memory: h rows (k x F floats), the prepared token row, the whole
+    uint32_t off_v;                // Q4_K: the gate/up units' block values (k x H / 256 x 16 doubles)
     uint32_t slot;                 // bytes a slot
     int ns;                        // slots a consumer warp has in flight
     int ng_max, nd_max;            // the most gate/up and down rows of an expert a CTA takes
@@ -79,8 +82,9 @@ __host__ inline TrxDecPlan trx_dec_plan(int gate_type, int H, int F, int k, int 
     P.ns = q8 ? TRX_DC_NS8 : TRX_DC_NS;
     P.off_h = trx_dc_align(TRX_DC_CWARPS * P.ns * P.slot);
     P.off_xq = trx_dc_align(P.off_h + (uint32_t)(k * F * 4 > H * 4 ? k * F * 4 : H * 4));
-    // the token's row: Q4_K's prepared planes, sums and scales; Q8_0's inputs in LC order
-    P.total = trx_dc_align(P.off_xq + (uint32_t)(q8 ? H * 4 : H * 4 + (H / 32) * 8 + (H / 256) * 8));
+    // the token's row: Q4_K's digits, sums and scales (trx_prep_q4m_block); Q8_0's inputs in LC order
+    P.off_v = trx_dc_align(P.off_xq + (uint32_t)(q8 ? H * 4 : H * 4 + (H / 32) * 8 + (H / 256) * 8));
+    P.total = q8 ? P.off_v : trx_dc_align(P.off_v + (uint32_t)(k * (H / 256) * 16 * 8));
     P.ng_max = (F + grid - 1) / grid;
     P.nd_max = ((H / 2 + grid - 1) / grid) * 2;
     return P;
@@ -97,7 +101,10 @@ __host__ inline bool trx_dec1_takes(int gate_type, int down_type, int router_typ
     if (H != 2048 || (F != 256 && F != 512 && F != 1024) || E > TRX_MAX_EXPERTS || k < 2 || k % 2 || k > TRX_DC_KMAX)
         return false;
     const TrxDecPlan P = trx_dec_plan(gate_type, H, F, k, grid);
-    return P.total <= 200 * 1024 && k * P.ng_max <= TRX_DC_CWARPS * TRX_DC_GU && (k / 2) * P.nd_max <= 2 * TRX_DC_CWARPS * TRX_DC_DN &&
+    // (Q8_0: a unit a gate/up row pair; Q4_K: a unit a 256-block of the CTA's rows, at most 8 of them)
+    const bool gu_fits = gate_type == TRX_Q8_0 ? k * P.ng_max <= TRX_DC_CWARPS * TRX_DC_GU
+                                               : P.ng_max <= 8 && k * (H / 256) <= TRX_DC_CWARPS * TRX_DC_GU4;
+    return P.total <= 200 * 1024 && gu_fits && (k / 2) * P.nd_max <= 2 * TRX_DC_CWARPS * TRX_DC_DN &&
            P.nd_max <= 16 && P.ng_max <= 32 && grid <= TRX_DC_GRID_MAX && F >= grid;
 }
 
@@ -117,14 +124,20 @@ __device__ __forceinline__ ulonglong2 trx_ld_tagged2(const unsigned long long *p
     return x;
 }
 
+// map_gate, map_up (Q4_K): 3-D tensor maps over the layer's gate and up matrices (row bytes, rows, experts), boxes of
+// one 256-block of 8 rows (trx_dec1_map); unused for Q8_0
 template <int RT, int GT>
 __global__ void __launch_bounds__(TRX_DC_THREADS, 1)
     trx_k_dec1(TrxLayer L, TrxShape S, const float *__restrict__ normed, TrxWork w, TrxSync *sync,
-               float *__restrict__ x_io, float *__restrict__ ffn_out, uint32_t epoch, const TrxDecPlan P) {
+               float *__restrict__ x_io, float *__restrict__ ffn_out, uint32_t epoch, const TrxDecPlan P,
+               const __grid_constant__ CUtensorMap map_gate, const __grid_constant__ CUtensorMap map_up) {
     extern __shared__ __align__(128) uint8_t smem[];
+    constexpr bool Q8 = GT == TRX_Q8_0;
+    constexpr int GU = Q8 ? TRX_DC_GU : TRX_DC_GU4; // gate/up steps a warp
     __shared__ __align__(8) uint64_t s_full[TRX_DC_CWARPS][TRX_DC_NS];
     __shared__ __align__(8) uint64_t s_hbar[TRX_DC_KMAX];
-    __shared__ __align__(8) uint64_t s_gubar[TRX_DC_GU];          // step j's gate/up values are in s_gu
+    __shared__ __align__(8) uint64_t s_gubar[TRX_DC_KMAX]; // Q8_0: step j's gate/up values are in s_gu; Q4_K:
+                                                            // expert i's block values are in the v rows
     __shared__ __align__(8) float2 s_gu[TRX_DC_GU * TRX_DC_CWARPS]; // unit u's (gate, up) row values
     __shared__ __align__(16) float sp[96];
     __shared__ __align__(16) float s_q6sc[2 * TRX_DC_CWARPS][32 * TRX_Q6L_SS_BLOCKS];
@@ -134,9 +147,16 @@ __global__ void __launch_bounds__(TRX_DC_THREADS, 1)
     __shared__ int32_t s_place[TRX_DC_KMAX], s_xmap[TRX_DC_KMAX];
     __shared__ int s_flag;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int E = S.E, H = S.H, F = S.F, k = S.k, nsb = F / 256, G = gridDim.x, c = blockIdx.x;
+    const int E = S.E, H = S.H, F = S.F, k = S.k, nsb = F / 256, G = gridDim.x, c = blockIdx.x, NB = H / 256;
     TRX_TRACE(0);
     trx_griddep_launch();
+    if (!Q8 && (trx_smem(smem) & 127u) != 0u) { // (the tensor copies need 128-byte aligned slots: report, touch nothing)
+        if (threadIdx.x == 0) {
+            atomicExch(w.err, 4);
+            if (w.host_done) trx_post_done(w.host_done, epoch | 0x80000000u);
+        }
+        return;
+    }
     float *hbuf = reinterpret_cast<float *>(smem + P.off_h); // h rows; before the routing, the token's row
     uint32_t *xq = reinterpret_cast<uint32_t *>(smem + P.off_xq);
     double *xbf = reinterpret_cast<double *>(smem + P.off_xq + H * 4), *xsc = xbf + H / 32;
@@ -146,9 +166,13 @@ __global__ void __launch_bounds__(TRX_DC_THREADS, 1)
     if (warp == TRX_DC_HELPER && lane == 0) {
         for (int i = 0; i < TRX_DC_CWARPS * TRX_DC_NS; i++) trx_mbar_init(&s_full[0][0] + i, 1);
         for (int i = 0; i < k; i++) trx_mbar_init(&s_hbar[i], 32); // every helper lane arrives
-        for (int j = 0; j < TRX_DC_GU; j++) { // a consumer with a unit in step j arrives
-            const int n = k * ng - TRX_DC_CWARPS * j;
-            trx_mbar_init(&s_gubar[j], (uint32_t)(n < 0 ? 0 : n > TRX_DC_CWARPS ? TRX_DC_CWARPS : n) + (n <= 0));
+        if (Q8) {
+            for (int j = 0; j < TRX_DC_GU; j++) { // a consumer with a unit in step j arrives
+                const int n = k * ng - TRX_DC_CWARPS * j;
+                trx_mbar_init(&s_gubar[j], (uint32_t)(n < 0 ? 0 : n > TRX_DC_CWARPS ? TRX_DC_CWARPS : n) + (n <= 0));
+            }
+        } else {
+            for (int i = 0; i < k; i++) trx_mbar_init(&s_gubar[i], (uint32_t)(32 * NB)); // every lane of its units
         }
         trx_fence_barrier_init();
     }
@@ -236,18 +260,19 @@ __global__ void __launch_bounds__(TRX_DC_THREADS, 1)
         if (lane == 0 && w.out_logits) w.out_logits[c] = v;
         TRX_TRACE(62);
     }
-    constexpr bool Q8 = GT == TRX_Q8_0;
     constexpr int NS = Q8 ? TRX_DC_NS8 : TRX_DC_NS;           // (the plan's ns and slot, as constants)
     constexpr uint32_t SLOT = Q8 ? TRX_DC_SLOT8 : TRX_DC_SLOT;
     float *xlc = reinterpret_cast<float *>(xq); // (Q8_0: the token's row in LC order)
-    // the token's row prepared for the gate/up dots, warp 4 + s taking 256-block s: Q4_K's integer definition, or
-    // Q8_0's inputs in LC order
+    uint8_t *xdig = reinterpret_cast<uint8_t *>(xq); // (Q4_K: the token's digits, 1024 bytes a 256-block)
+    double *sv = reinterpret_cast<double *>(smem + P.off_v); // (Q4_K: unit (i, b)'s 16 row values at 16 (i NB + b))
+    // the token's row prepared for the gate/up dots, warp 4 + s taking 256-block s: Q4_K's integer definition as
+    // the tensor cores take it, or Q8_0's inputs in LC order
     if (warp >= 4 && warp < 4 + H / 256) {
         const int sb = warp - 4;
         if (Q8) {
             for (int i = lane; i < 256; i += 32) xlc[256 * sb + trx_lc_pos(i)] = xrow[256 * sb + i];
         } else {
-            trx_prep_q4x_block(xrow + 256 * sb, xq, sb, H / 256, xbf + 8 * sb, xsc + sb, lane);
+            trx_prep_q4m_block(xrow + 256 * sb, xdig + 1024 * sb, xbf + 8 * sb, xsc + sb, lane);
         }
     }
 
@@ -334,9 +359,10 @@ __global__ void __launch_bounds__(TRX_DC_THREADS, 1)
     }
     bool failed = false;
     if (warp < TRX_DC_CWARPS) {
-        // ---------------- a consumer warp: TRX_DC_GU gate/up units, then TRX_DC_DN down steps, through its slots
+        // ---------------- a consumer warp: GU gate/up units, then TRX_DC_DN down steps, through its slots
         uint8_t *slots = smem + (size_t)warp * NS * SLOT;
-        const int ngu = k * ng, ndn = (k / 2) * nd; // gate/up units (expert-major), down units (expert pairs)
+        // gate/up units (expert-major; Q4_K: an expert's NB blocks), down units (expert pairs)
+        const int ngu = Q8 ? k * ng : k * NB, ndn = (k / 2) * nd;
         // row bytes (Q8L: 272 a block; Q6L: 208 a block, the d values apart) and a half-warp's share of a down step
         const int rbg = H / 256 * (Q8 ? 272 : 144), rbd = nsb * (Q8 ? 272 : 208), rhalf = Q8 ? 2 * rbd : 2 * rbd + 32;
         // lane 0 arms step j in its slot (a step with nothing to load completes at once: zero bytes expected)
@@ -345,23 +371,30 @@ __global__ void __launch_bounds__(TRX_DC_THREADS, 1)
             uint8_t *dst = slots + (j % NS) * SLOT;
             uint64_t *bar = &s_full[warp][j % NS];
             trx_fence_proxy_async(); // this warp's reads of the slot's last step before the copy rewrites it
-            if (j < TRX_DC_GU) {
+            if (j < GU) {
                 const int u = warp + TRX_DC_CWARPS * j;
                 if (u >= ngu) {
                     trx_mbar_expect_tx(bar, 0u);
                     return;
                 }
-                const int i = u / ng, r = ga + u % ng, e = s_selid[i];
-                trx_mbar_expect_tx(bar, 2u * rbg);
-                trx_bulk_g2s_hint(dst, L.gate + e * L.gate_mb + (int64_t)r * rbg, rbg, bar, pol);
-                trx_bulk_g2s_hint(dst + rbg, L.up + e * L.up_mb + (int64_t)r * rbg, rbg, bar, pol);
+                if (Q8) {
+                    const int i = u / ng, r = ga + u % ng, e = s_selid[i];
+                    trx_mbar_expect_tx(bar, 2u * rbg);
+                    trx_bulk_g2s_hint(dst, L.gate + e * L.gate_mb + (int64_t)r * rbg, rbg, bar, pol);
+                    trx_bulk_g2s_hint(dst + rbg, L.up + e * L.up_mb + (int64_t)r * rbg, rbg, bar, pol);
+                } else { // 256-block b of rows ga .. ga + 7 of expert e's gate and up (rows past F read as zeros)
+                    const int i = u / NB, b = u % NB, e = s_selid[i];
+                    trx_mbar_expect_tx(bar, 2u * 8u * 144u);
+                    trx_tma_load_3d_hint(dst, &map_gate, 144 * b, ga, e, bar, pol);
+                    trx_tma_load_3d_hint(dst + 8 * 144, &map_up, 144 * b, ga, e, bar, pol);
+                }
             } else {
                 uint32_t bytes = 0;
                 for (int hh = 0; hh < 2; hh++)
-                    if (2 * warp + hh + 2 * TRX_DC_CWARPS * (j - TRX_DC_GU) < ndn) bytes += (uint32_t)rhalf;
+                    if (2 * warp + hh + 2 * TRX_DC_CWARPS * (j - GU) < ndn) bytes += (uint32_t)rhalf;
                 trx_mbar_expect_tx(bar, bytes);
                 for (int hh = 0; hh < 2; hh++) {
-                    const int v = 2 * warp + hh + 2 * TRX_DC_CWARPS * (j - TRX_DC_GU);
+                    const int v = 2 * warp + hh + 2 * TRX_DC_CWARPS * (j - GU);
                     if (v >= ndn) continue;
                     const int q = v / nd, r = da + v % nd;
                     uint8_t *d0 = dst + hh * rhalf;
@@ -378,36 +411,36 @@ __global__ void __launch_bounds__(TRX_DC_THREADS, 1)
         };
         int issued = 0;
         for (; issued < NS; issued++) issue(issued);
-        TrxQ4X X;
-        if (!Q8) trx_q4x_load(xq, 32, lane, xbf + 8 * (lane >> 2), xsc + (lane >> 2), X);
         float *ss = s_q6sc[2 * warp + (lane >> 4)];
-        for (int j = 0; j < TRX_DC_GU + TRX_DC_DN && !failed; j++) {
+        for (int j = 0; j < GU + TRX_DC_DN && !failed; j++) {
             const uint8_t *src = slots + (j % NS) * SLOT;
             if (!__all_sync(0xffffffffu, trx_mbar_wait(&s_full[warp][j % NS], (j / NS) & 1, TRX_WAIT_NS))) {
                 failed = true;
                 break;
             }
             if (warp == 0) TRX_TRACE(8 + j); // (the timeline: warp 0's step j has its weights)
-            if (j < TRX_DC_GU) {
+            if (j < GU) {
                 const int u = warp + TRX_DC_CWARPS * j;
-                if (u < ngu) {
-                    float y2[2];
-                    if (Q8) { // the gate row by half-warp 0, the up row by half-warp 1 (16-lane contract each)
-                        const float y = trx_q8l_dot<true>(src + (lane >> 4) * rbg, xlc, H / 256, lane & 15);
-                        y2[0] = y;
-                        y2[1] = __shfl_sync(0xffffffffu, y, 16);
-                    } else {
-                        const uint8_t *const rows2[2] = {src, src + rbg};
-                        trx_q4k_row8xn<true, 2>(rows2, X, lane, y2);
-                    }
+                if (u < ngu && Q8) { // the gate row by half-warp 0, the up row by half-warp 1 (16-lane contract each)
+                    const float y = trx_q8l_dot<true>(src + (lane >> 4) * rbg, xlc, H / 256, lane & 15);
+                    const float yu = __shfl_sync(0xffffffffu, y, 16);
                     if (lane == 0) { // to the silu warp
-                        s_gu[u] = make_float2(y2[0], y2[1]);
+                        s_gu[u] = make_float2(y, yu);
                         trx_mbar_arrive(&s_gubar[j]);
                     }
+                } else if (u < ngu) { // block b of the 8 gate and 8 up rows: lane 4 g holds row g's block values
+                    const int i = u / NB, b = u % NB;
+                    double vg, vu;
+                    trx_q4k_blk_mma(src, src + 8 * 144, xdig + 1024 * b, xbf + 8 * b, xsc[b], lane, vg, vu);
+                    if ((lane & 3) == 0 && (lane >> 2) < ng) {
+                        sv[16 * (i * NB + b) + (lane >> 2)] = vg;
+                        sv[16 * (i * NB + b) + 8 + (lane >> 2)] = vu;
+                    }
+                    trx_mbar_arrive(&s_gubar[i]); // (every lane: its own stores before the silu warp's reads)
                 }
             } else {
-                const int v = 2 * warp + (lane >> 4) + 2 * TRX_DC_CWARPS * (j - TRX_DC_GU);
-                const int v0 = 2 * warp + 2 * TRX_DC_CWARPS * (j - TRX_DC_GU);
+                const int v = 2 * warp + (lane >> 4) + 2 * TRX_DC_CWARPS * (j - GU);
+                const int v0 = 2 * warp + 2 * TRX_DC_CWARPS * (j - GU);
                 if (v0 < ndn) { // (the warp's first unit exists; a second one past the end computes unstored)
                     const bool valid = v < ndn;
                     const int q = valid ? v / nd : 0, rl = valid ? v % nd : 0, r = da + rl;
@@ -441,7 +474,7 @@ __global__ void __launch_bounds__(TRX_DC_THREADS, 1)
             }
             __syncwarp();
             if (warp == 0) TRX_TRACE(16 + j); // computed
-            if (issued < TRX_DC_GU + TRX_DC_DN) issue(issued++);
+            if (issued < GU + TRX_DC_DN) issue(issued++);
         }
         if (failed && lane == 0) { // every copy this warp armed lands before the CTA can leave
             for (int j = 0; j < issued; j++)
@@ -451,7 +484,7 @@ __global__ void __launch_bounds__(TRX_DC_THREADS, 1)
         // ---------------- h = silu(g) u of a step's gate/up units at once (lane l: unit 14 j + l), published tagged;
         // the consumers go on to their next rows meanwhile
         const int ngu = k * ng;
-        for (int j = 0; j < TRX_DC_GU && TRX_DC_CWARPS * j < ngu && !failed; j++) {
+        for (int j = 0; Q8 && j < TRX_DC_GU && TRX_DC_CWARPS * j < ngu && !failed; j++) {
             if (!__all_sync(0xffffffffu, trx_mbar_wait(&s_gubar[j], 0, TRX_WAIT_NS))) {
                 failed = true;
                 break;
@@ -460,6 +493,23 @@ __global__ void __launch_bounds__(TRX_DC_THREADS, 1)
             if (lane < TRX_DC_CWARPS && u < ngu) {
                 const float2 gu = s_gu[u];
                 trx_st_tagged(w.tag_h + (int64_t)(u / ng) * F + trx_lc_pos(ga + u % ng), tag, trx_silu_mul(gu.x, gu.y));
+            }
+        }
+        // Q4_K: expert i's rows once its NB units are in, lane l taking row ga + l: the block values added in order
+        // from +0 (f64), rounded to float once (Trochilus's Q4_K row value), then h = silu(g) u
+        for (int i = 0; !Q8 && i < k && !failed; i++) {
+            if (!__all_sync(0xffffffffu, trx_mbar_wait(&s_gubar[i], 0, TRX_WAIT_NS))) {
+                failed = true;
+                break;
+            }
+            if (lane < ng) {
+                double ag = 0.0, au = 0.0;
+                for (int b = 0; b < NB; b++) {
+                    ag = __dadd_rn(ag, sv[16 * (i * NB + b) + lane]);
+                    au = __dadd_rn(au, sv[16 * (i * NB + b) + 8 + lane]);
+                }
+                trx_st_tagged(w.tag_h + (int64_t)i * F + trx_lc_pos(ga + lane), tag,
+                              trx_silu_mul(__double2float_rn(ag), __double2float_rn(au)));
             }
         }
     } else if (warp == TRX_DC_HELPER) {

@@ -147,18 +147,13 @@ __host__ __device__ inline int trx_q4x_lanes(int s, int nsb) {
 // ldexp(1.0, n), without its library call
 __device__ __forceinline__ double trx_pow2d(int n) { return __longlong_as_double((long long)(1023 + n) << 52); }
 
-// One warp per 256-block; lane L takes elements 8 L .. 8 L + 7. CG: read x through L2 only (a row another CTA of
-// the same kernel wrote). planes_row, bf_blk, sc_blk: the row's planes, the block's sums and scale.
-template <bool CG = false>
-__device__ __noinline__ void trx_prep_q4x_block(const float *__restrict__ x, uint32_t *__restrict__ planes_row, int s,
-                                                   int nsb, double *__restrict__ bf_blk, double *__restrict__ sc_blk,
-                                                   int lane) {
-    float v[8];
-    const float4 a = trx_ldx<CG>(x + 8 * lane);
-    const float4 b = trx_ldx<CG>(x + 8 * lane + 4);
-    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+// The integer form of a 256-block of x, by one warp: lane L holds elements 8 L .. 8 L + 7 in v and gets their
+// X = nearest-even(x 2^sh) (0 in a block holding a NaN or an infinity, which sets bad), the block's shift sh chosen
+// from max|x| so that every |X| stays at most 2085998640 (Trochilus tr_q4x_shift, src/kernels/kernels_internal.h:
+// 150-166, and k_q4x_prep, src/kernels/kernels.c:200-239).
+__device__ __forceinline__ void trx_q4x_digitise(const float (&v)[8], int32_t (&X)[8], int &sh, int &bad) {
     float m = 0.0f;
-    int bad = 0;
+    bad = 0;
 #pragma unroll
     for (int i = 0; i < 8; i++) {
         const float av = fabsf(v[i]);
@@ -170,7 +165,7 @@ __device__ __noinline__ void trx_prep_q4x_block(const float *__restrict__ x, uin
         m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
         bad |= __shfl_xor_sync(0xffffffffu, bad, o);
     }
-    int sh = 0;
+    sh = 0;
     if (!bad && m != 0.0f) {
         const uint32_t mb = __float_as_uint(m);
         const int field = (int)((mb >> 23) & 255u);
@@ -180,12 +175,26 @@ __device__ __noinline__ void trx_prep_q4x_block(const float *__restrict__ x, uin
         if (__dmul_rn((double)m, trx_pow2d(sh)) > 2085998640.0) sh--;
     }
     const double f = bad ? 0.0 : trx_pow2d(sh);
-    int32_t X[8];
 #pragma unroll
     for (int i = 0; i < 8; i++) {
         const double t = __dmul_rn((double)v[i], f); // exact
         X[i] = bad ? 0 : (int32_t)__double2ll_rn(t);   // nearest, ties to even
     }
+}
+
+// One warp per 256-block; lane L takes elements 8 L .. 8 L + 7. CG: read x through L2 only (a row another CTA of
+// the same kernel wrote). planes_row, bf_blk, sc_blk: the row's planes, the block's sums and scale.
+template <bool CG = false>
+__device__ __noinline__ void trx_prep_q4x_block(const float *__restrict__ x, uint32_t *__restrict__ planes_row, int s,
+                                                   int nsb, double *__restrict__ bf_blk, double *__restrict__ sc_blk,
+                                                   int lane) {
+    float v[8];
+    const float4 a = trx_ldx<CG>(x + 8 * lane);
+    const float4 b = trx_ldx<CG>(x + 8 * lane + 4);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+    int32_t X[8];
+    int sh, bad;
+    trx_q4x_digitise(v, X, sh, bad);
     // sub-block sums: sub-block j holds lanes 4 j .. 4 j + 3
     int64_t sum = 0;
 #pragma unroll
@@ -304,6 +313,135 @@ __device__ __forceinline__ double trx_q4k_value(uint4 hdr, int64_t T, int64_t M,
     const double dmin = trx_half_d((uint16_t)(hdr.x >> 16));
     const double val = __dsub_rn(__dmul_rn(d, trx_i2d(T)), __dmul_rn(dmin, trx_i2d(M)));
     return __dmul_rn(val, sc);
+}
+
+// ---- Q4_K on the integer tensor cores (one-token decode) ----
+//
+// T = sum_j sc_j sum_{k in j} q_k X_k is an exact integer, so it may be formed in any order and by any exact
+// means: here by mma.sync m16n8k32 (u8 quants x s8 digits, s32 sums), the 32 elements of a sub-block being one
+// product's K. X is split into four balanced base-256 digits, X = D0 + 256 D1 + 65536 D2 + 2^24 D3 with every
+// D_p in [-128, 127] (|X| <= 2085998640 keeps D3 within 125), which are the four columns of B (the other four are
+// zero). The rows of A are 8 gate rows and the same 8 up rows of one 256-block; a high-nibble sub-block enters as
+// 16 q (the byte masked in place), its sum then shifted back right by 4, exactly.
+//
+// The digits' layout, made for the B fragments: product K index k' of thread (g, t) (g = lane / 4, t = lane % 4)
+// holds element 8 t + k' (k' < 4) or 8 t + 4 + (k' - 16) (k' >= 16) of the sub-block, the A fragments taking the
+// same elements of a quant row. So thread (p, t), p < 4, reads digit plane p's elements 8 t .. 8 t + 7 of every
+// sub-block: 64 bytes per block, in four 16-byte chunks (chunk q: sub-blocks 2 q and 2 q + 1), chunk q of lane
+// L = 4 p + t stored at 16 (4 L + (q ^ ((L >> 1) & 3))) so that eight lanes' loads of a phase hit distinct banks.
+__device__ __forceinline__ int trx_q4m_chunk_off(int L, int q) { return 16 * (4 * L + (q ^ ((L >> 1) & 3))); }
+
+// One warp per 256-block, lane L taking elements 8 L .. 8 L + 7 (the same X as trx_prep_q4x_block): the block's
+// digits (1024 bytes at dig), sub-block sums (bf_blk[0..7]) and scale (*sc_blk; NaN for a NaN or an infinity).
+__device__ __noinline__ void trx_prep_q4m_block(const float *__restrict__ x, uint8_t *__restrict__ dig,
+                                                double *__restrict__ bf_blk, double *__restrict__ sc_blk, int lane) {
+    float v[8];
+    const float4 a = *reinterpret_cast<const float4 *>(x + 8 * lane);
+    const float4 b = *reinterpret_cast<const float4 *>(x + 8 * lane + 4);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+    int32_t X[8];
+    int sh, bad;
+    trx_q4x_digitise(v, X, sh, bad);
+    int64_t sum = 0;
+#pragma unroll
+    for (int i = 0; i < 8; i++) sum += X[i];
+    sum += trx_shfl_xor64(sum, 1);
+    sum += trx_shfl_xor64(sum, 2);
+    if ((lane & 3) == 0) bf_blk[lane >> 2] = (double)sum;
+    if (lane == 0) sc_blk[0] = bad ? __longlong_as_double(0x7ff8000000000000ll) : trx_pow2d(-sh);
+    // balanced digits: D = ((r + 128) mod 256) - 128, r = (r - D) / 256 (exact: r - D is a multiple of 256)
+    uint32_t pw[4][2] = {{0, 0}, {0, 0}, {0, 0}, {0, 0}};
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        int32_t r = X[i];
+#pragma unroll
+        for (int p = 0; p < 4; p++) {
+            const int32_t d = p < 3 ? ((r + 128) & 255) - 128 : r;
+            r = (r - d) >> 8;
+            pw[p][i >> 2] |= ((uint32_t)d & 255u) << (8 * (i & 3));
+        }
+    }
+    // elements 8 L .. 8 L + 7 are sub-block s = L / 4, part t = L % 4: consumer lane 4 p + t, chunk s / 2, half s % 2
+    const int sb = lane >> 2, t = lane & 3;
+#pragma unroll
+    for (int p = 0; p < 4; p++)
+        *reinterpret_cast<uint2 *>(dig + trx_q4m_chunk_off(4 * p + t, sb >> 1) + 8 * (sb & 1)) =
+            make_uint2(pw[p][0], pw[p][1]);
+}
+
+// d = A (16 x 32 u8, row) x B (32 x 8 s8, col), s32, from zero
+__device__ __forceinline__ void trx_mma_u8s8(int32_t (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                             uint32_t b0, uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%10, %10, %10, %10};"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+}
+
+// byte i (0..3) of w, as an int
+__device__ __forceinline__ int trx_byte(uint32_t w, int i) { return (int)((w >> (8 * i)) & 255u); }
+
+// One Q4_K block (256 columns) of 8 gate rows and the same 8 up rows against the token's digits, by one warp:
+// gate, up: the rows' blocks in shared memory, 144 bytes apart (row g at 144 g); dig, bf, sc: the token's block
+// (trx_prep_q4m_block). Lane 4 g gets the block's value v = (d T - dmin M) 2^-sh (f64, Trochilus's definition,
+// src/kernels/kernels.c:196-253) of gate row g in vg and of up row g in vu.
+__device__ __forceinline__ void trx_q4k_blk_mma(const uint8_t *__restrict__ gate, const uint8_t *__restrict__ up,
+                                                const uint8_t *__restrict__ dig, const double *__restrict__ bf,
+                                                double sc, int lane, double &vg, double &vu) {
+    const int g = lane >> 2, t = lane & 3;
+    const uint8_t *rg = gate + 144 * g, *ru = up + 144 * g;
+    const uint4 hg = *reinterpret_cast<const uint4 *>(rg), hu = *reinterpret_cast<const uint4 *>(ru);
+    uint4 B[4];
+#pragma unroll
+    for (int q = 0; q < 4; q++)
+        B[q] = g < 4 ? *reinterpret_cast<const uint4 *>(dig + trx_q4m_chunk_off(lane, q)) : make_uint4(0, 0, 0, 0);
+    // the 6-bit scales of sub-blocks 0..3 and 4..7 and the mins, packed a byte each (Q4_K's 12 scale bytes: j < 4:
+    // sc = byte j & 63, m = byte j + 4 & 63; j >= 4: the low (sc) or high (m) nibble of byte j + 4 and the top two
+    // bits of byte j - 4 (sc) or byte j (m))
+    const uint32_t sg03 = hg.y & 0x3f3f3f3fu, sg47 = (hg.w & 0x0f0f0f0fu) | ((hg.y >> 2) & 0x30303030u);
+    const uint32_t su03 = hu.y & 0x3f3f3f3fu, su47 = (hu.w & 0x0f0f0f0fu) | ((hu.y >> 2) & 0x30303030u);
+    int32_t lo[4] = {0, 0, 0, 0}, hi[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int j = 0; j < 4; j++) { // sub-blocks 2 j (low nibbles) and 2 j + 1 (high nibbles) of bytes 32 j .. 32 j + 31
+        const uint2 wg = *reinterpret_cast<const uint2 *>(rg + 16 + 32 * j + 8 * t);
+        const uint2 wu = *reinterpret_cast<const uint2 *>(ru + 16 + 32 * j + 8 * t);
+        const uint32_t pg = j < 2 ? sg03 : sg47, pu = j < 2 ? su03 : su47;
+        const int sgl = trx_byte(pg, (2 * j) & 3), sgh = trx_byte(pg, (2 * j + 1) & 3);
+        const int sul = trx_byte(pu, (2 * j) & 3), suh = trx_byte(pu, (2 * j + 1) & 3);
+        const uint4 bq = B[j]; // chunk j: sub-block 2 j in x, y; 2 j + 1 in z, w
+        int32_t c[4];
+        trx_mma_u8s8(c, wg.x & 0x0f0f0f0fu, wu.x & 0x0f0f0f0fu, wg.y & 0x0f0f0f0fu, wu.y & 0x0f0f0f0fu, bq.x, bq.y);
+        lo[0] += sgl * c[0];
+        lo[1] += sgl * c[1];
+        lo[2] += sul * c[2];
+        lo[3] += sul * c[3];
+        trx_mma_u8s8(c, wg.x & 0xf0f0f0f0u, wu.x & 0xf0f0f0f0u, wg.y & 0xf0f0f0f0u, wu.y & 0xf0f0f0f0u, bq.z, bq.w);
+        hi[0] += sgh * c[0];
+        hi[1] += sgh * c[1];
+        hi[2] += suh * c[2];
+        hi[3] += suh * c[3];
+    }
+    // planes 2 t and 2 t + 1 (t < 2; lanes t >= 2 hold the zero columns): the gate row's and the up row's parts
+    const int64_t ag = (int64_t)(lo[0] + (hi[0] >> 4)) + 256ll * (int64_t)(lo[1] + (hi[1] >> 4));
+    const int64_t au = (int64_t)(lo[2] + (hi[2] >> 4)) + 256ll * (int64_t)(lo[3] + (hi[3] >> 4));
+    // (in lane t = 0: its planes 0, 1 and lane t = 1's planes 2, 3)
+    const int64_t Tg = ag + 65536ll * trx_shfl_xor64(ag, 1), Tu = au + 65536ll * trx_shfl_xor64(au, 1);
+    // M = sum_j m_j S_j, S_j the sub-block sums of X: lane t takes sub-blocks 2 t and 2 t + 1 (exact in f64), whose
+    // mins are bytes 2 t, 2 t + 1 (mod 4) of the packed mins of sub-blocks 0..3 or 4..7
+    const uint32_t mgp = t < 2 ? (hg.z & 0x3f3f3f3fu) : (((hg.w >> 4) & 0x0f0f0f0fu) | ((hg.z >> 2) & 0x30303030u));
+    const uint32_t mup = t < 2 ? (hu.z & 0x3f3f3f3fu) : (((hu.w >> 4) & 0x0f0f0f0fu) | ((hu.z >> 2) & 0x30303030u));
+    const int i0 = (2 * t) & 3;
+    const double S0 = bf[2 * t], S1 = bf[2 * t + 1];
+    double Mg = __dadd_rn(__dmul_rn((double)trx_byte(mgp, i0), S0), __dmul_rn((double)trx_byte(mgp, i0 + 1), S1));
+    double Mu = __dadd_rn(__dmul_rn((double)trx_byte(mup, i0), S0), __dmul_rn((double)trx_byte(mup, i0 + 1), S1));
+    Mg = __dadd_rn(Mg, __shfl_xor_sync(0xffffffffu, Mg, 1));
+    Mu = __dadd_rn(Mu, __shfl_xor_sync(0xffffffffu, Mu, 1));
+    Mg = __dadd_rn(Mg, __shfl_xor_sync(0xffffffffu, Mg, 2));
+    Mu = __dadd_rn(Mu, __shfl_xor_sync(0xffffffffu, Mu, 2));
+    const double dg = trx_half_d((uint16_t)(hg.x & 0xffffu)), dmg = trx_half_d((uint16_t)(hg.x >> 16));
+    const double du = trx_half_d((uint16_t)(hu.x & 0xffffu)), dmu = trx_half_d((uint16_t)(hu.x >> 16));
+    vg = __dmul_rn(__dsub_rn(__dmul_rn(dg, trx_i2d(Tg)), __dmul_rn(dmg, Mg)), sc);
+    vu = __dmul_rn(__dsub_rn(__dmul_rn(du, trx_i2d(Tu)), __dmul_rn(dmu, Mu)), sc);
 }
 
 // One 256-block of the lane contract for thread l of a half-warp: its 16 elements k = 256 i + l + 16 m, m = 0..15,
