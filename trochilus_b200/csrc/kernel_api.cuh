@@ -20,6 +20,20 @@ __global__ void trx_kapi_prep_q4x(const float *__restrict__ x, int n_in, int col
                        sc + (int64_t)p * nsb + s, threadIdx.x & 31);
 }
 
+// A small call's first kernel: its group table and offsets (tab_bytes, a multiple of 4) and its input rows (total
+// floats), from mapped pinned host memory (read over the host link) into device memory; lc: the rows go into LC
+// order (the Q8_0 and Q6_K dots' input layout), else as they are
+__global__ void trx_kapi_pull(const uint32_t *__restrict__ h_tab, int tab_bytes, uint32_t *__restrict__ d_tab,
+                              const float *__restrict__ h_x, int64_t total, int cols, float *__restrict__ d_x, int lc) {
+    const int64_t i0 = blockIdx.x * (int64_t)blockDim.x + threadIdx.x, n = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i = i0; i < tab_bytes / 4; i += n) d_tab[i] = h_tab[i];
+    for (int64_t i = i0; i < total; i += n) {
+        const int64_t p = i / cols;
+        const int k = (int)(i % cols);
+        d_x[lc ? p * cols + trx_lc_pos(k) : i] = h_x[i];
+    }
+}
+
 __global__ void trx_kapi_lc(const float *__restrict__ x, int64_t total, int cols, float *__restrict__ y) {
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
         const int64_t p = i / cols;
@@ -97,9 +111,10 @@ __global__ void __launch_bounds__(256) trx_kapi_grouped_k(const uint8_t *const *
 }
 
 // prep false (Q4_K): dq, dbf, dsc already hold dx's prepared rows (an earlier call on the same inputs wrote them)
+// lc_done: dq already holds dx's rows in LC order (Q8_0, Q6_K: trx_kapi_pull wrote them)
 inline bool trx_kapi_grouped(int type, int64_t rows, int64_t cols, const uint8_t *const *dg, const int32_t *doff,
                              int n_groups, int n_in, const float *dx, uint32_t *dq, double *dbf, double *dsc, float *dy,
-                             cudaStream_t st, bool prep = true) {
+                             cudaStream_t st, bool prep = true, bool lc_done = false) {
     if (type == TRX_Q4_K) {
         const int64_t warps = (int64_t)n_in * (cols / 256);
         if (prep) trx_kapi_prep_q4x<<<(unsigned)((warps + 7) / 8), 256, 0, st>>>(dx, n_in, (int)cols, dq, dbf, dsc);
@@ -110,8 +125,9 @@ inline bool trx_kapi_grouped(int type, int64_t rows, int64_t cols, const uint8_t
     dim3 grid((unsigned)((rows + 15) / 16), (unsigned)n_groups);
     if (type == TRX_Q8_0 || type == TRX_Q6_K) {
         const int64_t total = (int64_t)n_in * cols;
-        trx_kapi_lc<<<(unsigned)std::min<int64_t>((total + 255) / 256, 4096), 256, 0, st>>>(dx, total, (int)cols,
-                                                                                           reinterpret_cast<float *>(dq));
+        if (!lc_done)
+            trx_kapi_lc<<<(unsigned)std::min<int64_t>((total + 255) / 256, 4096), 256, 0, st>>>(
+                dx, total, (int)cols, reinterpret_cast<float *>(dq));
         if (type == TRX_Q8_0)
             trx_kapi_grouped_k<TRX_Q8_0><<<grid, 256, 0, st>>>(dg, doff, (int)rows, (int)cols, dx, dq, dbf, dsc, dy);
         else
