@@ -82,9 +82,11 @@ def test_layer_matches_oracle_fresh_seeds(cuda, oracle, gt, dt, rt):
 
 @pytest.mark.parametrize("gt,dt,rt,T", [(gb.Q4_K, gb.Q6_K, gb.BF16, 2), (gb.Q4_K, gb.Q6_K, gb.BF16, 8),
                                         (gb.Q4_K, gb.Q6_K, gb.BF16, 32), (gb.Q8_0, gb.Q8_0, gb.F32, 1),
-                                        (gb.Q8_0, gb.Q8_0, gb.BF16, 8), (gb.Q8_0, gb.Q8_0, gb.F32, 64)])
+                                        (gb.Q8_0, gb.Q8_0, gb.BF16, 8), (gb.Q8_0, gb.Q8_0, gb.F32, 64),
+                                        (gb.Q4_K, gb.Q4_K, gb.BF16, 1), (gb.Q4_K, gb.Q4_K, gb.F32, 12)])
 def test_short_calls_one_launch_a_token(cuda, oracle, gt, dt, rt, T):
-    """Q4_K_M and Q8_0 calls of 1..64 tokens without the dispatch permutation run the one-token kernel once a token:
+    """Q4_K_M, all-Q4_K and Q8_0 calls of 1..64 tokens (all-Q4_K: below the tensor road's 32) without the dispatch
+    permutation run the one-token kernel once a token:
     every output bit for bit the oracle's on the device road, the host road with copies and (up to 16 tokens) the
     zero-copy host road"""
     torch = cuda
@@ -228,7 +230,7 @@ def test_q4k_long_pass_multikernel(cuda, oracle):
 def test_host_call_on_pinned_x(cuda, oracle, gt, dt, rt):
     """tr_gpu_moe_layer with x in pinned host memory: short calls take the zero-copy road (x read and written in
     place through its mapping, completion posted to a pinned word), longer ones the copy road; both bit for bit the
-    oracle's, call after call on the same buffers"""
+    oracle's, call after call on the same buffers, normed pinned or pageable"""
     torch = cuda
     rng = np.random.default_rng(77 + gt)
     lay = gb.make_layer(int(rng.integers(1 << 30)), 64, 2048, 1024, gt, dt, rt, mode="random")
@@ -247,6 +249,10 @@ def test_host_call_on_pinned_x(cuda, oracle, gt, dt, rt):
                 assert same_bits(hx.numpy(), want["x"]), (T, rep)
         want2 = oracle.moe_layer(d, normed, want["x"])
         assert same_bits(hx.numpy(), want2["x"]), T
+        # normed in pageable memory (copied by the copy engine), x still pinned
+        hx.copy_(torch.from_numpy(x))
+        m.layer_ptrs(0, normed.ctypes.data, T, hx.data_ptr(), host=True)
+        assert same_bits(hx.numpy(), want["x"]), (T, "pageable normed")
     m.check()
     m.close()
 

@@ -190,7 +190,8 @@ struct tr_gpu_moe {
     bool fused_ok = false;
     bool dec1_ok = false;  // the one-token decode kernel (decode.cuh) fits and may be launched
     bool dec1_pdl = true;  // and is launched with programmatic dependent launch (off if the driver refuses it)
-    // Q4_K: per layer the one-token kernel's tensor maps over the gate and up matrices (trx_dec1_map)
+    // Q4_K: per layer the one-token kernel's tensor maps over the gate, up and (a Q4_K) down matrices
+    // (trx_dec1_map)
     std::vector<CUtensorMap> dc_maps;
     int64_t tag_bytes = 0; // its tagged exchange words (work regions 26 and 27), cleared with the counters
     float *d_normed = nullptr, *d_x = nullptr;
@@ -289,11 +290,14 @@ static LayerFn layer_fn(int gate_type, int down_type) {
 // the fused kernel: the most shared memory a CTA may take, and a cooperative grid of one CTA per SM
 // the one-token kernel for a router type and a gate/up type (Q4_K: Q4_K_M's road, Q8_0: all Q8_0)
 typedef void (*Dec1Fn)(TrxLayer, TrxShape, const float *, TrxWork, TrxSync *, float *, float *, uint32_t, TrxDecPlan,
-                       const CUtensorMap, const CUtensorMap);
-static Dec1Fn dec1_fn(int router_type, int gate_type) {
+                       const CUtensorMap, const CUtensorMap, const CUtensorMap);
+static Dec1Fn dec1_fn(int router_type, int gate_type, int down_type) {
+    const bool bf = router_type == TRX_BF16;
     if (gate_type == TRX_Q8_0)
-        return router_type == TRX_BF16 ? trx_k_dec1<TRX_BF16, TRX_Q8_0> : trx_k_dec1<TRX_F32, TRX_Q8_0>;
-    return router_type == TRX_BF16 ? trx_k_dec1<TRX_BF16, TRX_Q4_K> : trx_k_dec1<TRX_F32, TRX_Q4_K>;
+        return bf ? trx_k_dec1<TRX_BF16, TRX_Q8_0, TRX_Q8_0> : trx_k_dec1<TRX_F32, TRX_Q8_0, TRX_Q8_0>;
+    if (down_type == TRX_Q4_K)
+        return bf ? trx_k_dec1<TRX_BF16, TRX_Q4_K, TRX_Q4_K> : trx_k_dec1<TRX_F32, TRX_Q4_K, TRX_Q4_K>;
+    return bf ? trx_k_dec1<TRX_BF16, TRX_Q4_K, TRX_Q6_K> : trx_k_dec1<TRX_F32, TRX_Q4_K, TRX_Q6_K>;
 }
 
 static bool plan_fused(tr_gpu_moe *m) {
@@ -315,9 +319,10 @@ static bool plan_fused(tr_gpu_moe *m) {
     // the one-token kernel: its plan's shared memory, a CTA an SM
     if (m->fused_ok && trx_dec1_takes(c.gate_type, c.down_type, c.router_type, (int)c.n_embd, (int)c.n_ff,
                                       (int)c.n_expert, (int)c.n_used, 1, m->grid_fused, false)) {
-        const TrxDecPlan P = trx_dec_plan(c.gate_type, (int)c.n_embd, (int)c.n_ff, (int)c.n_used, m->grid_fused);
+        const TrxDecPlan P =
+            trx_dec_plan(c.gate_type, c.down_type, (int)c.n_embd, (int)c.n_ff, (int)c.n_used, m->grid_fused);
         bool ok1 = true;
-        for (auto fn : {dec1_fn(TRX_F32, c.gate_type), dec1_fn(TRX_BF16, c.gate_type)}) {
+        for (auto fn : {dec1_fn(TRX_F32, c.gate_type, c.down_type), dec1_fn(TRX_BF16, c.gate_type, c.down_type)}) {
             int occ1 = 0;
             cudaFuncAttributes fa1{};
             if (!ck(cudaFuncGetAttributes(&fa1, fn), "cudaFuncGetAttributes") ||
@@ -459,15 +464,15 @@ static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
     return encode;
 }
 
-// The one-token kernel's map over a layer's Q4_K gate (or up) matrices: bytes x rows x experts (row bytes, n_ff
-// rows, expert stride), boxes of one 256-block (144 bytes) of 8 rows of one expert; rows past n_ff read as zeros
+// The one-token kernel's map over a layer's Q4_K gate, up or down matrices: bytes x rows x experts (row bytes, rows,
+// expert stride), boxes of one 256-block (144 bytes) of box_rows rows of one expert; rows past the end read as zeros
 static bool trx_dec1_map(CUtensorMap *map, const uint8_t *base, int64_t row_bytes, int64_t rows, int64_t experts,
-                         int64_t expert_bytes) {
+                         int64_t expert_bytes, int box_rows) {
     PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
     if (encode == nullptr) return false;
     const cuuint64_t dims[3] = {(cuuint64_t)row_bytes, (cuuint64_t)rows, (cuuint64_t)experts};
     const cuuint64_t strides[2] = {(cuuint64_t)row_bytes, (cuuint64_t)expert_bytes};
-    const cuuint32_t box[3] = {144, 8, 1}, es[3] = {1, 1, 1};
+    const cuuint32_t box[3] = {144, (cuuint32_t)box_rows, 1}, es[3] = {1, 1, 1};
     const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, (void *)base, dims, strides, box, es,
                               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
                               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -551,7 +556,7 @@ extern "C" tr_gpu_moe *tr_gpu_moe_create(const tr_gpu_moe_config *cfg, int devic
         m->layer_mem.assign((size_t)cfg->n_layers, nullptr);
         m->layers.assign((size_t)cfg->n_layers, TrxLayer{});
         m->layer_set.assign((size_t)cfg->n_layers, 0);
-        m->dc_maps.assign((size_t)(2 * cfg->n_layers), CUtensorMap{});
+        m->dc_maps.assign((size_t)(3 * cfg->n_layers), CUtensorMap{});
         for (int64_t l = 0; l < cfg->n_layers && ok; l++)
             ok = ck(cudaMalloc(&m->layer_mem[(size_t)l], (size_t)lb), "cudaMalloc(layer)");
     }
@@ -708,8 +713,10 @@ extern "C" int tr_gpu_moe_set_layer(tr_gpu_moe *m, int64_t layer, const void *ro
     // the one-token kernel's maps over the Q4_K gate and up matrices; without them (no driver entry point) every
     // call takes the fused kernel instead
     if (c.gate_type == TRX_Q4_K && m->dec1_ok &&
-        !(trx_dec1_map(&m->dc_maps[(size_t)(2 * layer)], L.gate, trx_row_bytes(c.gate_type, H), F, E, L.gate_mb) &&
-          trx_dec1_map(&m->dc_maps[(size_t)(2 * layer + 1)], L.up, trx_row_bytes(c.gate_type, H), F, E, L.up_mb))) {
+        !(trx_dec1_map(&m->dc_maps[(size_t)(3 * layer)], L.gate, trx_row_bytes(c.gate_type, H), F, E, L.gate_mb, 8) &&
+          trx_dec1_map(&m->dc_maps[(size_t)(3 * layer + 1)], L.up, trx_row_bytes(c.gate_type, H), F, E, L.up_mb, 8) &&
+          (c.down_type != TRX_Q4_K || trx_dec1_map(&m->dc_maps[(size_t)(3 * layer + 2)], L.down,
+                                                   trx_row_bytes(c.down_type, F), H, E, L.down_mb, 16)))) {
         m->dec1_ok = false;
         g_err.clear();
     }
@@ -909,7 +916,7 @@ static int launch_fused(tr_gpu_moe *m, const TrxLayer &L, const TrxShape &S, con
 // the one-token decode kernel (decode.cuh): one cooperative launch, a CTA an SM
 static int launch_dec1(tr_gpu_moe *m, int64_t layer, const TrxLayer &L, const TrxShape &S, const float *normed,
                        const TrxWork &w, float *x_io, float *ffn_out, uint32_t epoch, cudaStream_t st) {
-    const TrxDecPlan P = trx_dec_plan(L.gate_type, S.H, S.F, S.k, m->grid_fused);
+    const TrxDecPlan P = trx_dec_plan(L.gate_type, L.down_type, S.H, S.F, S.k, m->grid_fused);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)m->grid_fused);
     cfg.blockDim = dim3(TRX_DC_THREADS);
@@ -924,19 +931,20 @@ static int launch_dec1(tr_gpu_moe *m, int64_t layer, const TrxLayer &L, const Tr
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = m->dec1_pdl ? 2 : 1;
-    auto fn = dec1_fn(L.router_type, L.gate_type);
-    // (Q4_K: the layer's maps; Q8_0 takes none, and gets zeroed ones)
-    CUtensorMap mg{}, mu{};
+    auto fn = dec1_fn(L.router_type, L.gate_type, L.down_type);
+    // (Q4_K: the layer's maps, and the down's for a Q4_K down; Q8_0 takes none, and gets zeroed ones)
+    CUtensorMap mg{}, mu{}, md{};
     if (L.gate_type == TRX_Q4_K) {
-        mg = m->dc_maps[(size_t)(2 * layer)];
-        mu = m->dc_maps[(size_t)(2 * layer + 1)];
+        mg = m->dc_maps[(size_t)(3 * layer)];
+        mu = m->dc_maps[(size_t)(3 * layer + 1)];
+        md = m->dc_maps[(size_t)(3 * layer + 2)];
     }
-    cudaError_t e = cudaLaunchKernelEx(&cfg, fn, L, S, normed, w, m->sync, x_io, ffn_out, epoch, P, mg, mu);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, fn, L, S, normed, w, m->sync, x_io, ffn_out, epoch, P, mg, mu, md);
     if (e != cudaSuccess && m->dec1_pdl) { // not taken together: cooperative alone from now on
         (void)cudaGetLastError();
         m->dec1_pdl = false;
         cfg.numAttrs = 1;
-        e = cudaLaunchKernelEx(&cfg, fn, L, S, normed, w, m->sync, x_io, ffn_out, epoch, P, mg, mu);
+        e = cudaLaunchKernelEx(&cfg, fn, L, S, normed, w, m->sync, x_io, ffn_out, epoch, P, mg, mu, md);
     }
     return ck(e, "decode layer launch") ? 0 : -1;
 }
@@ -1158,7 +1166,10 @@ static int host_layer(tr_gpu_moe *m, int64_t layer, const float *normed, int64_t
         pa.type == cudaMemoryTypeHost && pa.devicePointer != nullptr) {
         uint32_t epoch = 0;
         float *xd = (float *)pa.devicePointer;
-        // with the ffn_norm, the norm reads a device copy of x (one copy-engine transfer beats reads over the link)
+        // the input rows by one copy-engine transfer (with the ffn_norm, of x: the norm reads a device copy of x,
+        // which beats every CTA reading all of x over the link). (A variant in which the one-token kernel read a
+        // pinned normed itself, each CTA its share over the link, published to the others as tagged words, measured
+        // 46 us a call against 39.5: the gather of the whole row in every CTA costs more than the transfer.)
         const bool in = norm ? ck(cudaMemcpyAsync(m->d_x, x_inout, xb, cudaMemcpyHostToDevice, st), "copy x")
                              : ck(cudaMemcpyAsync(m->d_normed, normed, xb, cudaMemcpyHostToDevice, st), "copy normed");
         if (!in || launch_layer(m, layer, m->d_normed, n_tok, xd, nullptr, st, 0, 3, m->d_done, &epoch,

@@ -58,7 +58,8 @@
 #define TRX_DC_SLOT8 4352 // Q8_0 bytes a slot: a gate/up unit (2 x 2176) or a down step of up to 1024 columns
 #define TRX_DC_GU 4       // gate/up units a warp (Q8_0: a gate row and its up row each)
 #define TRX_DC_GU4 5      // Q4_K: gate/up units a warp (a 256-block of 8 gate rows and 8 up rows each, on the tensor cores)
-#define TRX_DC_DN 2       // down steps a warp
+#define TRX_DC_DN 2       // down steps a warp (Q6_K, Q8_0: two row pairs each)
+#define TRX_DC_DN4 3      // Q4_K down: down units a warp (a 256-block of the CTA's 16 rows of one expert each)
 #define TRX_DC_KMAX 8
 #define TRX_DC_GRID_MAX 256 // CTAs (the tagged logits: a row of E words for each)
 #define TRX_DC_SEQ_MAX 64   // calls of up to this many tokens run one launch a token (faster than the fused kernel)
@@ -66,6 +67,8 @@
 struct TrxDecPlan {
     uint32_t off_h, off_xq, total; // shared memory: h rows (k x F floats), the prepared token row, the whole
     uint32_t off_v;                // Q4_K: the gate/up units' block values (k x H / 256 x 16 doubles)
+    uint32_t off_d;                // Q4_K down: the down units' block values (k x F / 256 x 16 doubles), then the h
+                                   // rows' sub-block sums (k x F / 32) and scales (k x F / 256)
     uint32_t slot;                 // bytes a slot
     int ns;                        // slots a consumer warp has in flight
     int ng_max, nd_max;            // the most gate/up and down rows of an expert a CTA takes
@@ -73,8 +76,8 @@ struct TrxDecPlan {
 
 __host__ __device__ inline uint32_t trx_dc_align(uint32_t v) { return (v + 127u) / 128u * 128u; }
 
-// gate_type Q4_K (with a Q6_K down) or Q8_0 (with a Q8_0 down)
-__host__ inline TrxDecPlan trx_dec_plan(int gate_type, int H, int F, int k, int grid) {
+// gate_type Q4_K (with a Q6_K or Q4_K down) or Q8_0 (with a Q8_0 down)
+__host__ inline TrxDecPlan trx_dec_plan(int gate_type, int down_type, int H, int F, int k, int grid) {
     TrxDecPlan P{};
     const bool q8 = gate_type == TRX_Q8_0;
     // Q8_0: a gate/up unit is 2 rows of H / 256 272-byte blocks, a down step 2 x 2 rows of F / 256 (no larger for F <= H)
@@ -84,7 +87,10 @@ __host__ inline TrxDecPlan trx_dec_plan(int gate_type, int H, int F, int k, int 
     P.off_xq = trx_dc_align(P.off_h + (uint32_t)(k * F * 4 > H * 4 ? k * F * 4 : H * 4));
     // the token's row: Q4_K's digits, sums and scales (trx_prep_q4m_block); Q8_0's inputs in LC order
     P.off_v = trx_dc_align(P.off_xq + (uint32_t)(q8 ? H * 4 : H * 4 + (H / 32) * 8 + (H / 256) * 8));
-    P.total = q8 ? P.off_v : trx_dc_align(P.off_v + (uint32_t)(k * (H / 256) * 16 * 8));
+    P.off_d = q8 ? P.off_v : trx_dc_align(P.off_v + (uint32_t)(k * (H / 256) * 16 * 8));
+    P.total = down_type != TRX_Q4_K ? P.off_d
+                                    : trx_dc_align(P.off_d + (uint32_t)(k * (F / 256) * 16 * 8 + k * (F / 32) * 8 +
+                                                                        k * (F / 256) * 8));
     P.ng_max = (F + grid - 1) / grid;
     P.nd_max = ((H / 2 + grid - 1) / grid) * 2;
     return P;
@@ -94,18 +100,22 @@ __host__ inline TrxDecPlan trx_dec_plan(int gate_type, int H, int F, int k, int 
 __host__ inline bool trx_dec1_takes(int gate_type, int down_type, int router_type, int H, int F, int E, int k, int T,
                                     int grid, bool ext) {
     if (T != 1 || ext) return false;
-    if (!(gate_type == TRX_Q4_K && down_type == TRX_Q6_K) && !(gate_type == TRX_Q8_0 && down_type == TRX_Q8_0))
+    if (!(gate_type == TRX_Q4_K && (down_type == TRX_Q6_K || down_type == TRX_Q4_K)) &&
+        !(gate_type == TRX_Q8_0 && down_type == TRX_Q8_0))
         return false;
     if (router_type != TRX_F32 && router_type != TRX_BF16) return false;
     // (1, 2 or 4 blocks a down row: a row's d values never straddle a 16-byte piece)
     if (H != 2048 || (F != 256 && F != 512 && F != 1024) || E > TRX_MAX_EXPERTS || k < 2 || k % 2 || k > TRX_DC_KMAX)
         return false;
-    const TrxDecPlan P = trx_dec_plan(gate_type, H, F, k, grid);
+    const TrxDecPlan P = trx_dec_plan(gate_type, down_type, H, F, k, grid);
     // (Q8_0: a unit a gate/up row pair; Q4_K: a unit a 256-block of the CTA's rows, at most 8 of them)
     const bool gu_fits = gate_type == TRX_Q8_0 ? k * P.ng_max <= TRX_DC_CWARPS * TRX_DC_GU
                                                : P.ng_max <= 8 && k * (H / 256) <= TRX_DC_CWARPS * TRX_DC_GU4;
-    return P.total <= 200 * 1024 && gu_fits && (k / 2) * P.nd_max <= 2 * TRX_DC_CWARPS * TRX_DC_DN &&
-           P.nd_max <= 16 && P.ng_max <= 32 && grid <= TRX_DC_GRID_MAX && F >= grid;
+    // (Q4_K down: a unit a 256-block of the CTA's rows of one expert, at most 16 of them; else two row pairs)
+    const bool dn_fits = down_type == TRX_Q4_K ? k * (F / 256) <= TRX_DC_CWARPS * TRX_DC_DN4
+                                               : (k / 2) * P.nd_max <= 2 * TRX_DC_CWARPS * TRX_DC_DN;
+    return P.total <= 206 * 1024 && gu_fits && dn_fits && P.nd_max <= 16 && P.ng_max <= 32 &&
+           grid <= TRX_DC_GRID_MAX && F >= grid;
 }
 
 // a value and its tag in one 64-bit word (relaxed, device scope; an aligned 64-bit access is never torn)
@@ -125,15 +135,18 @@ __device__ __forceinline__ ulonglong2 trx_ld_tagged2(const unsigned long long *p
 }
 
 // map_gate, map_up (Q4_K): 3-D tensor maps over the layer's gate and up matrices (row bytes, rows, experts), boxes of
-// one 256-block of 8 rows (trx_dec1_map); unused for Q8_0
-template <int RT, int GT>
+// one 256-block of 8 rows (trx_dec1_map); map_down (Q4_K down): the same over the down matrices, boxes of 16 rows;
+// unused otherwise
+template <int RT, int GT, int DT>
 __global__ void __launch_bounds__(TRX_DC_THREADS, 1)
     trx_k_dec1(TrxLayer L, TrxShape S, const float *__restrict__ normed, TrxWork w, TrxSync *sync,
                float *__restrict__ x_io, float *__restrict__ ffn_out, uint32_t epoch, const TrxDecPlan P,
-               const __grid_constant__ CUtensorMap map_gate, const __grid_constant__ CUtensorMap map_up) {
+               const __grid_constant__ CUtensorMap map_gate, const __grid_constant__ CUtensorMap map_up,
+               const __grid_constant__ CUtensorMap map_down) {
     extern __shared__ __align__(128) uint8_t smem[];
-    constexpr bool Q8 = GT == TRX_Q8_0;
+    constexpr bool Q8 = GT == TRX_Q8_0, DQ4 = DT == TRX_Q4_K;
     constexpr int GU = Q8 ? TRX_DC_GU : TRX_DC_GU4; // gate/up steps a warp
+    constexpr int DN = DQ4 ? TRX_DC_DN4 : TRX_DC_DN; // down steps a warp
     __shared__ __align__(8) uint64_t s_full[TRX_DC_CWARPS][TRX_DC_NS];
     __shared__ __align__(8) uint64_t s_hbar[TRX_DC_KMAX];
     __shared__ __align__(8) uint64_t s_gubar[TRX_DC_KMAX]; // Q8_0: step j's gate/up values are in s_gu; Q4_K:
@@ -265,6 +278,8 @@ __global__ void __launch_bounds__(TRX_DC_THREADS, 1)
     float *xlc = reinterpret_cast<float *>(xq); // (Q8_0: the token's row in LC order)
     uint8_t *xdig = reinterpret_cast<uint8_t *>(xq); // (Q4_K: the token's digits, 1024 bytes a 256-block)
     double *sv = reinterpret_cast<double *>(smem + P.off_v); // (Q4_K: unit (i, b)'s 16 row values at 16 (i NB + b))
+    // (Q4_K down: unit (i, b)'s 16 row values at 16 (i nsb + b), then the h blocks' sub-block sums and scales)
+    double *dv = reinterpret_cast<double *>(smem + P.off_d), *dbf = dv + 16 * k * nsb, *dsc = dbf + 8 * k * nsb;
     // the token's row prepared for the gate/up dots, warp 4 + s taking 256-block s: Q4_K's integer definition as
     // the tensor cores take it, or Q8_0's inputs in LC order
     if (warp >= 4 && warp < 4 + H / 256) {
@@ -339,7 +354,8 @@ __global__ void __launch_bounds__(TRX_DC_THREADS, 1)
         // the CTA's share of every selected expert into L2 at once (gate rows, up rows, down rows, the down rows' d
         // values: lane 4 i + part), so that HBM streams the whole call's weights while the rings start; the rings'
         // copies then read L2
-        const int i = lane >> 2, part = lane & 3, rbg = H / 256 * (Q8 ? 272 : 144), rbd = nsb * (Q8 ? 272 : 208);
+        const int i = lane >> 2, part = lane & 3, rbg = H / 256 * (Q8 ? 272 : 144);
+        const int rbd = nsb * (Q8 ? 272 : DQ4 ? 144 : 208);
         if (i < k) {
             const int e = s_selid[i];
             if (part < 2) {
@@ -349,7 +365,7 @@ __global__ void __launch_bounds__(TRX_DC_THREADS, 1)
                 const uint8_t *mat = L.down + e * L.down_mb;
                 if (part == 2) {
                     trx_bulk_prefetch_l2(mat + (int64_t)da * rbd, (uint32_t)(nd * rbd));
-                } else if (!Q8) { // the Q6L d values of rows [da, da + nd), widened to 16-byte bounds
+                } else if (!Q8 && !DQ4) { // the Q6L d values of rows [da, da + nd), widened to 16-byte bounds
                     const int64_t lo = (int64_t)H * rbd + (((int64_t)da * nsb * 2) & ~15ll);
                     const int64_t hi = (int64_t)H * rbd + (((int64_t)(da + nd) * nsb * 2 + 15) & ~15ll);
                     trx_bulk_prefetch_l2(mat + lo, (uint32_t)(hi - lo));
@@ -359,10 +375,11 @@ __global__ void __launch_bounds__(TRX_DC_THREADS, 1)
     }
     bool failed = false;
     if (warp < TRX_DC_CWARPS) {
-        // ---------------- a consumer warp: GU gate/up units, then TRX_DC_DN down steps, through its slots
+        // ---------------- a consumer warp: GU gate/up units, then DN down steps, through its slots
         uint8_t *slots = smem + (size_t)warp * NS * SLOT;
-        // gate/up units (expert-major; Q4_K: an expert's NB blocks), down units (expert pairs)
-        const int ngu = Q8 ? k * ng : k * NB, ndn = (k / 2) * nd;
+        // gate/up units (expert-major; Q4_K: an expert's NB blocks), down units (expert pairs; Q4_K down: an
+        // expert's nsb blocks)
+        const int ngu = Q8 ? k * ng : k * NB, ndn = DQ4 ? k * nsb : (k / 2) * nd;
         // row bytes (Q8L: 272 a block; Q6L: 208 a block, the d values apart) and a half-warp's share of a down step
         const int rbg = H / 256 * (Q8 ? 272 : 144), rbd = nsb * (Q8 ? 272 : 208), rhalf = Q8 ? 2 * rbd : 2 * rbd + 32;
         // lane 0 arms step j in its slot (a step with nothing to load completes at once: zero bytes expected)
@@ -388,6 +405,15 @@ __global__ void __launch_bounds__(TRX_DC_THREADS, 1)
                     trx_tma_load_3d_hint(dst, &map_gate, 144 * b, ga, e, bar, pol);
                     trx_tma_load_3d_hint(dst + 8 * 144, &map_up, 144 * b, ga, e, bar, pol);
                 }
+            } else if (DQ4) { // 256-block b of rows da .. da + 15 of expert e's down (rows past H read as zeros)
+                const int v = warp + TRX_DC_CWARPS * (j - GU);
+                if (v >= ndn) {
+                    trx_mbar_expect_tx(bar, 0u);
+                    return;
+                }
+                const int i = v / nsb, b = v % nsb;
+                trx_mbar_expect_tx(bar, 16u * 144u);
+                trx_tma_load_3d_hint(dst, &map_down, 144 * b, da, s_selid[i], bar, pol);
             } else {
                 uint32_t bytes = 0;
                 for (int hh = 0; hh < 2; hh++)
@@ -412,7 +438,7 @@ __global__ void __launch_bounds__(TRX_DC_THREADS, 1)
         int issued = 0;
         for (; issued < NS; issued++) issue(issued);
         float *ss = s_q6sc[2 * warp + (lane >> 4)];
-        for (int j = 0; j < GU + TRX_DC_DN && !failed; j++) {
+        for (int j = 0; j < GU + DN && !failed; j++) {
             const uint8_t *src = slots + (j % NS) * SLOT;
             if (!__all_sync(0xffffffffu, trx_mbar_wait(&s_full[warp][j % NS], (j / NS) & 1, TRX_WAIT_NS))) {
                 failed = true;
@@ -437,6 +463,27 @@ __global__ void __launch_bounds__(TRX_DC_THREADS, 1)
                         sv[16 * (i * NB + b) + 8 + (lane >> 2)] = vu;
                     }
                     trx_mbar_arrive(&s_gubar[i]); // (every lane: its own stores before the silu warp's reads)
+                }
+            } else if (DQ4) {
+                // a Q4_K down unit: block b of the CTA's 16 rows of expert i against the expert's h, prepared here
+                // in place for Q4_K's integer definition (this unit is the block's only reader), on the tensor cores
+                const int v = warp + TRX_DC_CWARPS * (j - GU);
+                if (v < ndn) {
+                    const int i = v / nsb, b = v % nsb, ib = i * nsb + b;
+                    if (!__all_sync(0xffffffffu, trx_mbar_wait(&s_hbar[i], 0, TRX_WAIT_NS))) {
+                        failed = true;
+                        break;
+                    }
+                    uint8_t *hd = reinterpret_cast<uint8_t *>(hbuf + (size_t)i * F + 256 * b);
+                    trx_prep_q4m_block(reinterpret_cast<const float *>(hd), hd, dbf + 8 * ib, dsc + ib, lane);
+                    __syncwarp();
+                    double v0, v1; // (tile rows g and 8 + g)
+                    trx_q4k_blk_mma(src, src + 8 * 144, hd, dbf + 8 * ib, dsc[ib], lane, v0, v1);
+                    if ((lane & 3) == 0) {
+                        const int g = lane >> 2;
+                        if (g < nd) dv[16 * ib + g] = v0;
+                        if (8 + g < nd) dv[16 * ib + 8 + g] = v1;
+                    }
                 }
             } else {
                 const int v = 2 * warp + (lane >> 4) + 2 * TRX_DC_CWARPS * (j - GU);
@@ -474,7 +521,7 @@ __global__ void __launch_bounds__(TRX_DC_THREADS, 1)
             }
             __syncwarp();
             if (warp == 0) TRX_TRACE(16 + j); // computed
-            if (issued < GU + TRX_DC_DN) issue(issued++);
+            if (issued < GU + DN) issue(issued++);
         }
         if (failed && lane == 0) { // every copy this warp armed lands before the CTA can leave
             for (int j = 0; j < issued; j++)
@@ -517,7 +564,8 @@ __global__ void __launch_bounds__(TRX_DC_THREADS, 1)
                     ag = __dadd_rn(ag, sv[16 * (e * NB + b) + r]);
                     au = __dadd_rn(au, sv[16 * (e * NB + b) + 8 + r]);
                 }
-                trx_st_tagged(w.tag_h + (int64_t)e * F + trx_lc_pos(ga + r), tag,
+                // (LC order for a Q6_K down's lane contract; a Q4_K down takes the row in its natural order)
+                trx_st_tagged(w.tag_h + (int64_t)e * F + (DQ4 ? ga + r : trx_lc_pos(ga + r)), tag,
                               trx_silu_mul(__double2float_rn(ag), __double2float_rn(au)));
             }
             i += n;
@@ -529,7 +577,8 @@ __global__ void __launch_bounds__(TRX_DC_THREADS, 1)
         const int npair = F / 64; // 4, 8 or 16
         for (int i = 0; i < k && !failed; i++) {
             const unsigned long long *src = w.tag_h + (int64_t)i * F;
-            float *dst = hbuf + (size_t)(i >> 1) * 2 * F + (i & 1); // expert pairs' rows interleaved (trx_il_off)
+            // expert pairs' rows interleaved (trx_il_off); a Q4_K down takes each expert's row as it is
+            float *dst = DQ4 ? hbuf + (size_t)i * F : hbuf + (size_t)(i >> 1) * 2 * F + (i & 1);
             uint32_t want = (1u << npair) - 1u; // the pairs still missing
             uint64_t t0 = 0;
             for (;;) {
@@ -541,8 +590,13 @@ __global__ void __launch_bounds__(TRX_DC_THREADS, 1)
                 for (int m = 0; m < 16; m++) {
                     if ((want >> m & 1u) && (uint32_t)(v[m].x >> 32) == tag && (uint32_t)(v[m].y >> 32) == tag) {
                         const int pos = 2 * (lane + 32 * m); // (even: pos and pos + 1 are 2 apart in the layout)
-                        dst[trx_il_off(pos)] = __uint_as_float((uint32_t)v[m].x);
-                        dst[trx_il_off(pos) + 2] = __uint_as_float((uint32_t)v[m].y);
+                        if (DQ4) {
+                            dst[pos] = __uint_as_float((uint32_t)v[m].x);
+                            dst[pos + 1] = __uint_as_float((uint32_t)v[m].y);
+                        } else {
+                            dst[trx_il_off(pos)] = __uint_as_float((uint32_t)v[m].x);
+                            dst[trx_il_off(pos) + 2] = __uint_as_float((uint32_t)v[m].y);
+                        }
                         want &= ~(1u << m);
                     }
                 }
@@ -575,7 +629,17 @@ __global__ void __launch_bounds__(TRX_DC_THREADS, 1)
     }
     if (tid < nd) { // output row da + tid: the k outputs in increasing expert id, then the residual
         float out = 0.0f;
-        for (int i = 0; i < k; i++) out = __fadd_rn(out, __fmul_rn(s_selw[i], s_h3[i][tid]));
+        for (int i = 0; i < k; i++) {
+            float h3 = 0.0f;
+            if (DQ4) { // the row's block values added in order from +0 (f64), rounded once
+                double a = 0.0;
+                for (int b = 0; b < nsb; b++) a = __dadd_rn(a, dv[16 * (i * nsb + b) + tid]);
+                h3 = __double2float_rn(a);
+            } else {
+                h3 = s_h3[i][tid];
+            }
+            out = __fadd_rn(out, __fmul_rn(s_selw[i], h3));
+        }
         if (ffn_out) ffn_out[da + tid] = out;
         x_io[da + tid] = __fadd_rn(xres, out);
     }
