@@ -149,6 +149,24 @@ def test_many_layers_one_context(cuda, oracle):
     m.close()
 
 
+def test_misaligned_rows_are_refused(cuda):
+    """input rows that do not start on a 16-byte boundary (the kernels read them 16 bytes at a time) are refused with
+    an error before any launch, and the context keeps working"""
+    torch = cuda
+    c = dict(E=64, k=8, H=2048, F=1024, router=gb.BF16, gate=gb.Q4_K, down=gb.Q6_K, norm_topk=0, T=2)
+    m = _ctx(c)
+    m.set_layer(0, gb.make_layer(5, 64, 2048, 1024, gb.Q4_K, gb.Q6_K, gb.BF16, mode="random"))
+    dn = torch.zeros((2 * 2048 + 4,), device="cuda")
+    dx = torch.zeros((2048,), device="cuda")
+    st = torch.cuda.current_stream().cuda_stream
+    with pytest.raises(RuntimeError, match="16-byte boundary"):
+        m.layer_dev(0, dn.data_ptr() + 4, 1, dx.data_ptr(), None, stream=st)
+    m.layer_dev(0, dn.data_ptr(), 1, dx.data_ptr(), None, stream=st)  # aligned: runs
+    torch.cuda.synchronize()
+    m.check()
+    m.close()
+
+
 def test_unset_layer_is_an_error(cuda):
     c = dict(E=64, k=8, H=2048, F=1024, router=gb.F32, gate=gb.Q8_0, down=gb.Q8_0, norm_topk=0, T=1)
     m = _ctx(c, n_layers=2)

@@ -969,6 +969,11 @@ static int launch_layer(tr_gpu_moe *m, int64_t layer, const float *d_normed, int
         set_err("bad token count %lld (max %lld) or input", (long long)n_tok, (long long)c.max_tokens);
         return -1;
     }
+    // (the kernels read the input rows 16 bytes at a time, and x a float at a time)
+    if (((uintptr_t)d_normed & 15) != 0 || ((uintptr_t)d_x & 3) != 0) {
+        set_err("the input rows must start on a 16-byte boundary and x on a 4-byte one");
+        return -1;
+    }
     if (first < 0 || last > 3 || first > last) {
         set_err("bad part range %d..%d", first, last);
         return -1;
