@@ -536,12 +536,13 @@ def run_ours(args, rank, world, dist):
     side = torch.cuda.Stream()
 
     def capture(parts, n=NL):
-        """a CUDA graph of n layer calls (call l: layer l on input row l): whole calls (parts None, the road a
-        user's call takes: one fused kernel for a short pass) or the given parts of the multi-kernel road"""
+        """a CUDA graph of n layer calls (call i: layer i mod NL on input row i mod NL): whole calls (parts None, the
+        road a user's call takes: one fused kernel for a short pass) or the given parts of the multi-kernel road"""
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph, stream=side):
             sp = torch.cuda.current_stream().cuda_stream
-            for l in range(n):
+            for i in range(n):
+                l = i % NL
                 if parts is None:
                     m.layer_dev(l, normed[l].data_ptr(), T, x.data_ptr(), None, stream=sp)
                 else:
@@ -557,10 +558,17 @@ def run_ours(args, rank, world, dist):
     parts_of = {"route": [0], "gate_up": [0, 1], "act_prep": [0, 1, 2], "parts": [0, 1, 2, 3], "call": None}
     graphs = {k: capture(v) for k, v in parts_of.items()}
     steps = args.steps
-    reps, tail_n = steps // NL, steps % NL
+    # a short run (up to 4 NL steps) is one graph of exactly its K calls, so that the timed region holds one graph
+    # launch; a longer one replays the NL-call graph K // NL times and a graph of the rest. Every graph the timed
+    # region replays is replayed (uploaded) before it.
+    whole = capture(None, steps) if steps <= 4 * NL else None
+    reps, tail_n = (0, 0) if whole is not None else (steps // NL, steps % NL)
     tail = capture(None, tail_n) if tail_n else None
     for _ in range(max(args.warmup // NL, 3)):
         graphs["call"].replay()
+        for g_ in (whole, tail):
+            if g_ is not None:
+                g_.replay()
     torch.cuda.synchronize()
     if dist:
         dist.barrier()
@@ -570,6 +578,8 @@ def run_ours(args, rank, world, dist):
         clk.wait_first()
         torch.cuda.synchronize()
         start.record(stream)
+        if whole is not None:
+            whole.replay()
         for _ in range(reps):
             graphs["call"].replay()
         if tail is not None:
@@ -601,7 +611,7 @@ def run_ours(args, rank, world, dist):
         cum[k] = e0.elapsed_time(e1) / (max(reps, 1) * NL)
     zone_ms = {"router": cum["route"], "gate_up": cum["gate_up"] - cum["route"],
                "act_prep": cum["act_prep"] - cum["gate_up"], "down": cum["parts"] - cum["act_prep"]}
-    del graphs, tail
+    del graphs, tail, whole
     # distinct experts per call (computed from the routing each call makes)
     sel = torch.zeros((NL, T * K_USED), dtype=torch.int64, device="cuda")
     sel_w = torch.zeros((T * K_USED,), device="cuda")
@@ -639,10 +649,10 @@ def run_ours(args, rank, world, dist):
     n_in = 16
     hn = torch.randn((n_in, T, H), generator=torch.Generator().manual_seed(99)).pin_memory()
     hx = torch.randn((T, H)).pin_memory()
-    # (at least 200 calls, about 8 ms, so that a short run's e2e figure is not a handful of calls)
-    e2e_steps = max(min(args.steps, 4000), 200)
+    # (at least 2000 calls, about 80 ms: the host road's steady state, which a short run's handful of calls misses)
+    e2e_steps = max(min(args.steps, 4000), 2000)
     hptr, xptr = [hn[j].data_ptr() for j in range(n_in)], hx.data_ptr()  # (no tensor indexing inside the loop)
-    for i in range(5):
+    for i in range(max(args.warmup, 200)):  # untimed: the host road's first calls run slower (about 8 ms of them)
         m.layer_ptrs(i % NL, hptr[i % n_in], T, xptr, host=True)
     if dist:
         dist.barrier()
@@ -691,8 +701,9 @@ def run_ours(args, rank, world, dist):
                                "multikernel_ms": layer_ms},
             "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches * steps, "clocks": clk.summary(),
             "prefill": prefill, "configs": extra,
-            "timing": f"CUDA graphs of {NL} layer calls replayed (+ a graph of the last {tail_n}); zones from graphs "
-                      f"of parts 0..z"}
+            "timing": (f"one CUDA graph of the {steps} layer calls" if steps <= 4 * NL else
+                       f"CUDA graphs of {NL} layer calls replayed (+ a graph of the last {tail_n})") +
+                      "; zones from graphs of parts 0..z"}
     return line
 
 
