@@ -59,6 +59,13 @@ bool ck(cudaError_t e, const char *what) {
 // waits for the stream, polling; a GPU that does not finish within timeout_s is an error, not a hang
 // Polls the stream: busy for the first 2 ms (a decode call's work takes tens of microseconds, and a sleep, however
 // short it asks to be, lasts about 60 us on Linux), then with 20 us sleeps between the polls.
+// what a kernel's error flag (TrxWork::err) says: the one-token kernel's 16 is a set-up refusal, every other value
+// a bounded wait that gave up (the value tells which wait)
+const char *err_flag_what(int32_t flag) {
+    return flag == 16 ? "the one-token kernel's shared memory was not 128-byte aligned for its tensor copies"
+                      : "a kernel gave up on a bounded wait";
+}
+
 bool stream_wait(cudaStream_t s, double timeout_s = 60.0) {
     const auto t0 = std::chrono::steady_clock::now();
     for (;;) {
@@ -824,7 +831,7 @@ extern "C" int tr_gpu_moe_check(tr_gpu_moe *m) {
     if (!ck(cudaMemcpy(&flag, m->work.err, 4, cudaMemcpyDeviceToHost), "read error flag")) return -1;
     if (flag != 0) {
         reset_counters(m, m->stream);
-        set_err("a kernel gave up on a bounded wait (device error flag %d)", flag);
+        set_err("%s (device error flag %d)", err_flag_what(flag), flag);
         return -1;
     }
     return 0;
@@ -1205,7 +1212,7 @@ static int host_layer(tr_gpu_moe *m, int64_t layer, const float *normed, int64_t
         reset_counters(m, st);
         int32_t flag = 0;
         cudaMemcpy(&flag, m->work.err, 4, cudaMemcpyDeviceToHost);
-        set_err("a kernel gave up on a bounded wait (device error flag %d)", flag);
+        set_err("%s (device error flag %d)", err_flag_what(flag), flag);
         return -1;
     }
     cudaGetLastError(); // a pointer the runtime does not know (pageable memory) is not an error here
@@ -1233,7 +1240,7 @@ static int host_layer(tr_gpu_moe *m, int64_t layer, const float *normed, int64_t
     if (ok) ok = stream_wait(st);
     if (ok && flag != 0) {
         reset_counters(m, st);
-        set_err("a kernel gave up on a bounded wait (device error flag %d)", flag);
+        set_err("%s (device error flag %d)", err_flag_what(flag), flag);
         ok = false;
     }
     return ok ? 0 : -1;

@@ -165,7 +165,7 @@ __global__ void __launch_bounds__(TRX_DC_THREADS, 1)
     trx_griddep_launch();
     if (!Q8 && (trx_smem(smem) & 127u) != 0u) { // (the tensor copies need 128-byte aligned slots: report, touch nothing)
         if (threadIdx.x == 0) {
-            atomicExch(w.err, 4);
+            atomicExch(w.err, 16);
             if (w.host_done) trx_post_done(w.host_done, epoch | 0x80000000u);
         }
         return;
