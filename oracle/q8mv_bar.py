@@ -12,7 +12,7 @@ output.weight and token_embd.weight (tests/bench_gpu_q8.c:838-870), all Q8_0. Ra
 real checkpoint (the timing does not depend on the values). Test and measurement infrastructure: nothing in the
 package imports this.
 
-    python oracle/q8mv_bar.py [--runs 50] [--out gpurun_out/q8mv_bar.json]
+    python oracle/q8mv_bar.py [--runs 50] [--out results.json]
 """
 from __future__ import annotations
 
@@ -102,7 +102,7 @@ def time_ours(mats: dict, runs: int) -> dict:
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--runs", type=int, default=50)
-    ap.add_argument("--out", default=os.path.join(ROOT, "gpurun_out", "q8mv_bar.json"))
+    ap.add_argument("--out", default=None, help="also write the results as JSON here")
     a = ap.parse_args()
     exe = os.path.join(HERE, "_ref", "bench_gpu_q8")
     if not os.path.exists(exe):
@@ -118,9 +118,10 @@ def main():
         res["reference_q8_mv"] = {"rc": p.returncode, "stdout": p.stdout.splitlines(), "stderr": p.stderr[-2000:]}
         print(p.stdout)
         res["ours_tr_matmul"] = time_ours(mats, a.runs)
-    os.makedirs(os.path.dirname(a.out), exist_ok=True)
-    with open(a.out, "w") as f:
-        json.dump(res, f, indent=1)
+    if a.out:
+        os.makedirs(os.path.dirname(os.path.abspath(a.out)), exist_ok=True)
+        with open(a.out, "w") as f:
+            json.dump(res, f, indent=1)
     print(json.dumps(res["ours_tr_matmul"], indent=1))
     if res["reference_q8_mv"]["rc"] != 0:
         raise SystemExit(f"bench_gpu_q8 exited {res['reference_q8_mv']['rc']}")
