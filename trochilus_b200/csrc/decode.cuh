@@ -1,7 +1,8 @@
 // decode.cuh: a one-token MoE layer call, the decode road's common case, as one compact persistent kernel.
 //
-// The same arithmetic as the general fused kernel (fused_layer.cuh), the same routing code and row dots, laid out
-// for one token so that its code stays small and no warp waits on another warp's stages.
+// The same results as the general fused kernel (fused_layer.cuh), the same routing code, laid out for one token so
+// that its code stays small and no warp waits on another warp's stages; its Q4_K rows run on the integer tensor
+// cores (exact integer sums, so the bits are the same).
 //
 // Exchange between CTAs without fences or counters: every word one CTA publishes for the others (a logit, an h
 // value) is a 64-bit store of the value and the call's tag (TrxSync::seq + 1) together, which a reader sees whole or
@@ -18,28 +19,31 @@
 //            once, warps 0-3 stage the token's row in shared memory meanwhile (or, with the ffn_norm in the hook,
 //            every CTA normalises the residual row there first), warp 0 forms logit e (the 16-lane contract) and
 //            publishes it tagged; warps 4-11 prepare the row for the gate/up dots (all CTAs): Q4_K's integer
-//            definition, or Q8_0's inputs in LC order.
+//            definition as the tensor cores take it (trx_prep_q4m_block), or Q8_0's inputs in LC order.
 //  routing   every CTA, once it holds all E tagged logits, routes the token (softmax, top-k, ids sorted) in shared
 //            memory; CTA 0's warp 14 forms the dispatch permutation when the caller asks for it.
 //  experts   a CTA owns rows [ga, gb) of every selected expert's gate and up matrices and rows [da, db) of every
 //            selected expert's down matrix. Each of 14 consumer warps streams its own units through a ring of
-//            shared-memory slots with 1-D TMA bulk copies (no multicast), one mbarrier a slot, so it waits
-//            only for its own bytes: four gate/up units (one row of gate and the same row of up), then two down
-//            steps (a half-warp the same row of two experts, trx_q6l_dot_pair_il or trx_q8l_dot_pair_il). Q4_K_M
-//            takes three slots of 3456 bytes a warp, Q8_0 two of 4352. A unit's two row values go to
-//            warp 14, which forms h = silu(g) u for a whole step's units at once (lane l: unit l) and publishes them
-//            tagged, so that the exponential's latency is paid once a step, off the consumers' path. The down weights
-//            do not depend on h, so they load while the gate/up rows are multiplied; a step's h rows come from the
-//            helper warp, which gathers expert i's tagged h values into shared memory, experts in order, the rows of
-//            experts 2q and 2q + 1 interleaved (the pairs the down step multiplies together).
+//            shared-memory slots (TMA, no multicast), one mbarrier a slot, so it waits only for its own bytes.
+//            Q4_K gate/up: five units a warp, each one 256-block of the CTA's 8 gate rows and the same 8 up rows
+//            (two 3-D tile loads), multiplied on the integer tensor cores (trx_q4k_blk_mma); warp 14 adds an
+//            expert's block values per row once its units are in and publishes h = silu(g) u tagged. Q8_0
+//            gate/up: four units a warp (a gate row and its up row by 1-D bulk copies, the 16-lane contract), whose
+//            (g, u) warp 14 turns into h a whole step at once. Then the down: two steps a warp (a half-warp the same
+//            row of two experts, trx_q6l_dot_pair_il or trx_q8l_dot_pair_il), or for a Q4_K down three units a warp
+//            (a 256-block of the CTA's 16 down rows of one expert, the expert's h block prepared in place, the same
+//            tensor-core product). The down weights do not depend on h, so they load while the gate/up rows are
+//            multiplied; the h rows come from the helper warp, which gathers expert i's tagged h values into shared
+//            memory, experts in order (Q6_K, Q8_0: the rows of experts 2q and 2q + 1 interleaved, the pairs a down
+//            step multiplies together).
 //  mix       each CTA adds, for its rows [da, db), the k expert outputs in increasing expert id and the sum to the
 //            residual (Trochilus's mix_body); CTA 0 advances seq (the host-pointer road: the last CTA, which also
 //            posts the host word).
 //
 // Limits (checked on the host, trx_dec1_takes): one token, no external routing, 2048 columns of gate/up and 256,
-// 512 or 1024 of down, Q4_K gate/up with a Q6_K down or Q8_0 throughout, k even and at most 8, and a grid whose shares fit the ring (at most 7 gate/up rows
-// and 14 down rows of an expert a CTA for k = 8). Every wait is bounded; a warp that gives up sets the error flag,
-// waits (bounded) for its own copies in flight and leaves.
+// 512 or 1024 of down, Q4_K gate/up with a Q6_K or Q4_K down, or Q8_0 throughout, k even and at most 8, and a grid
+// whose shares fit the ring (for Q4_K at most 8 gate/up rows and 16 down rows of an expert a CTA). Every wait is
+// bounded; a warp that gives up sets the error flag, waits (bounded) for its own copies in flight and leaves.
 //
 // Trochilus references: forward_layer's MoE block src/models/olmoe.c:1845-1933 (route_token :1455-1502, the
 // counting sort :1850-1861, expert_stages :1642-1689, mix_body :1432-1446); tr_rmsnorm src/kernels/kernels.c:1351-1360.
